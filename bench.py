@@ -1,0 +1,457 @@
+"""Decode / prefill throughput of the clj-xla decoder path on B200.
+
+Workload (default): Gemma-3-4B bf16, random-init weights, batch 1, prompt 2048
+random token ids, KV cache of 2048+512 positions - the headline HBM-roofline
+configuration.  A *step* is one KV-cached decode step of the whole model
+(one token per sequence): the lowered StableHLO decode graph executed by
+libcljxla_b200.so through its PJRT C ABI.  ``value`` is decode tokens/s with
+each step's token / position buffers already on the device; ``e2e`` is the
+same loop driven the way clj-xla's host drives it (upload token and position
+from host memory, execute, read the f32 logits back, greedy argmax on the
+host).  Prefill tokens/s of the same model is reported in ``prefill``.
+
+With ``--gpus N`` (torchrun, one process per GPU) every rank runs an
+independent replica of the workload (data parallel, no collective on the data
+path; ``scaling: weak``); value = all ranks' tokens / max time over ranks.
+
+``--impl reference`` times the CPU restatement of the reference's execution
+path (oracle/interp.py running the same printed graph on the host cores).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _pkg():
+    import importlib.util
+    if "cljxla_b200" in sys.modules:
+        return sys.modules["cljxla_b200"]
+    pkg_dir = os.path.join(ROOT, "clj-xla_b200")
+    spec = importlib.util.spec_from_file_location(
+        "cljxla_b200", os.path.join(pkg_dir, "__init__.py"), submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["cljxla_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=32)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--config", default="gemma3-4b")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt", type=int, default=2048)
+    p.add_argument("--gen", type=int, default=512)
+    p.add_argument("--prefill-reps", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=16)
+    p.add_argument("--cpu-steps", type=int, default=1)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tiny", action="store_true", help="reduced model for quick checks (not a bench line)")
+    return p.parse_args()
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def model_setup(args):
+    from cljxla_b200.host import drivers as d
+    import dataclasses
+    cfg = d.CONFIGS[args.config]
+    if args.tiny:
+        cfg = dataclasses.replace(cfg, vocab=2048, d_model=256, layers=4, n_heads=4, n_kv_heads=2, head_dim=64,
+                                  mlp=1024, window=64)
+    B, S = args.batch, args.prompt
+    T = d.round_up(S + args.gen, 128)
+    return cfg, B, S, T
+
+
+def device_weights(cfg, seed, device):
+    """Seeded random-init weights in invar order, generated on the GPU, as host
+    arrays (bf16 bit patterns) ready for BufferFromHostBuffer."""
+    import torch
+    from cljxla_b200.host import drivers as d
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = []
+    for name, shp, kind in d.weight_specs(cfg):
+        if kind == "mat":
+            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02)
+        elif kind == "gemma_norm":
+            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02)
+        elif kind == "plain_norm":
+            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02).add_(1.0)
+        elif kind == "one":
+            w = torch.ones(shp, device=device)
+        else:
+            w = torch.zeros(shp, device=device)
+        if cfg.dtype == "bf16":
+            out.append(w.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16))
+        else:
+            out.append(w.cpu().numpy())
+        del w
+    return out
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    pkg = _pkg()
+    from cljxla_b200.host import core, drivers as d
+    from cljxla_b200.host import stablehlo as shlo
+    from cljxla_b200.host.pjrt import DTYPE_ENUM
+
+    torch.cuda.set_device(local_rank)
+    cfg, B, S, T = model_setup(args)
+    ctx = core.init_backend(pkg.LIB_PATH, {"device": local_rank})
+    api, client = ctx["api"], ctx["client"]
+    wdt = DTYPE_ENUM[cfg.dtype]
+
+    t0 = time.time()
+    host_w = device_weights(cfg, 1234 + rank, f"cuda:{local_rank}")
+    specs = d.weight_specs(cfg)
+    wbufs = [core.buffer_from_host_buffer(ctx, w, shp, wdt) for w, (_, shp, _) in zip(host_w, specs)]
+    if args.no_cpu_baseline or rank != 0:
+        del host_w
+        host_w = None
+    t_w = time.time() - t0
+
+    g_dec = d.build_graph(cfg, "decode", B, S, T)
+    g_pre = d.build_graph(cfg, "prefill", B, S, T, dynamic_prefill=True)
+    txt_dec, txt_pre = shlo.graph_to_mlir_text(g_dec), shlo.graph_to_mlir_text(g_pre)
+    t1 = time.time()
+    ex_dec = core.compile_mlir_text(ctx, txt_dec, g_dec)
+    ex_pre = core.compile_mlir_text(ctx, txt_pre, g_pre)
+    t_c = time.time() - t1
+
+    cache_np = d.zero_cache(cfg, B, T)
+    cshape = list(cache_np.shape)
+
+    def zero_kv():
+        return [core.buffer_from_host_buffer(ctx, cache_np, cshape, wdt) for _ in range(2 * cfg.layers)]
+
+    stream = torch.cuda.ExternalStream(core.client_stream(ctx), device=f"cuda:{local_rank}")
+    rng = np.random.Generator(np.random.PCG64(7 + rank))
+
+    # ---------------- prefill (dynamic-position prefill graph, one sequence batch)
+    toks = d.make_prompt(cfg, B, S, seed=1 + rank)
+    x_pre = core.buffer_from_host_buffer(ctx, toks, [B, S], 4)
+    p_pre = core.buffer_from_host_buffer(ctx, d.pos_inputs(cfg, "prefill", B, 0, S), [S], 4)
+    pre_times = []
+    kv = None
+    for rep in range(max(1, args.prefill_reps) + 1):
+        kv0 = zero_kv()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        outs = api.execute_executable(ex_pre["handle"], [x_pre, p_pre] + wbufs + kv0, len(g_pre["outvars"]), wait=False)
+        e1.record(stream)
+        e1.synchronize()
+        if rep > 0:
+            pre_times.append(e0.elapsed_time(e1) / 1e3)
+        for b in kv0:
+            api.destroy_buffer(b)
+        api.destroy_buffer(outs[0])
+        if kv is not None:
+            for b in kv:
+                api.destroy_buffer(b)
+        kv = outs[1:]
+    prefill_s = float(np.median(pre_times))
+
+    # ---------------- decode, device-resident inputs
+    n_total = args.warmup + args.steps
+    xs = [core.buffer_from_host_buffer(ctx, rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64).astype(np.int32),
+                                       [B, 1], 4) for _ in range(n_total)]
+    ps = [core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4) for i in range(n_total)]
+
+    def step(i, kv):
+        outs = api.execute_executable(ex_dec["handle"], [xs[i], ps[i]] + wbufs + kv, len(g_dec["outvars"]), wait=False)
+        api.destroy_buffer(outs[0])
+        for b in kv:
+            api.destroy_buffer(b)
+        return outs[1:]
+
+    for i in range(args.warmup):
+        kv = step(i, kv)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    launches0 = core.kernel_launches(ctx)
+    with ClockSampler(local_rank) as clk:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.warmup, n_total):
+            kv = step(i, kv)
+        e1.record(stream)
+        e1.synchronize()
+    dec_s = e0.elapsed_time(e1) / 1e3
+    launches = core.kernel_launches(ctx) - launches0
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+
+    # ---------------- decode end to end (host tokens in, logits out, host argmax)
+    logits_bytes = B * cfg.vocab * 4
+    tok = np.array([[int(toks[0, -1])]] * B, np.int32)
+    e2e_steps = max(1, args.e2e_steps)
+    torch.cuda.synchronize()
+    t_e0 = time.perf_counter()
+    for i in range(e2e_steps):
+        xb = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
+        pb = core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4)
+        outs = api.execute_executable(ex_dec["handle"], [xb, pb] + wbufs + kv, len(g_dec["outvars"]))
+        logits = api.buffer_to_host_floats(outs[0], B * cfg.vocab).reshape(B, cfg.vocab)
+        tok = np.array([[d.argmax_host(logits[b])] for b in range(B)], np.int32)
+        for b in [xb, pb, outs[0]] + kv:
+            api.destroy_buffer(b)
+        kv = outs[1:]
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t_e0
+
+    # ---------------- roofline of the dominant kernel (one profiled decode step)
+    core.profile_enable(ctx, True)
+    for i in range(2):
+        kv = step(i % n_total, kv)
+    torch.cuda.synchronize()
+    prof = core.profile_dump(ctx)
+    core.profile_enable(ctx, False)
+    by_kind = {}
+    for e in prof:
+        k = by_kind.setdefault(e["kind"], {"ms": 0.0, "bytes": 0, "flops": 0, "calls": 0})
+        k["ms"] += e["ms"]
+        k["bytes"] += e["bytes"]
+        k["flops"] += e["flops"]
+        k["calls"] += e["calls"]
+    total_ms = sum(k["ms"] for k in by_kind.values())
+    dom = max(by_kind.items(), key=lambda kv_: kv_[1]["ms"])
+    hbm_peak, tc_peak, peak_src = load_peaks()
+    achieved = dom[1]["bytes"] / (dom[1]["ms"] / 1e3) / 1e9 if dom[1]["ms"] else 0.0
+
+    # ---------------- CPU baseline (rank 0, N=1): oracle on the host cores, bounded sample
+    cpu = None
+    if rank == 0 and world == 1 and host_w is not None:
+        cpu = cpu_baseline(cfg, B, S, T, txt_dec, host_w, args.cpu_steps)
+
+    for b in kv + xs + ps + wbufs + [x_pre, p_pre]:
+        api.destroy_buffer(b)
+
+    tokens = B * args.steps
+    res = {
+        "rank": rank, "dec_s": dec_s, "tokens": tokens, "prefill_s": prefill_s, "e2e_s": e2e_s,
+        "e2e_tokens": B * e2e_steps, "launches": launches, "clocks": clk.summary(),
+        "by_kind": by_kind, "total_ms": total_ms, "dom": dom[0], "achieved": achieved,
+        "hbm_peak": hbm_peak, "peak_src": peak_src, "cpu": cpu, "t_weights": t_w, "t_compile": t_c,
+        "plan": core.plan_info(ctx, ex_dec), "logits_bytes": logits_bytes,
+    }
+    return cfg, B, S, T, res
+
+
+def cpu_baseline(cfg, B, S, T, txt_dec, host_w, steps):
+    """Times the numpy oracle on the same decode graph (all host threads)."""
+    try:
+        import psutil
+        need = sum(w.size for w in host_w) * 4 * 1.3
+        if psutil.virtual_memory().available < need:
+            return {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                    "sample": f"skipped: host RAM below {need / 1e9:.0f} GB needed for f32 weights"}
+    except Exception:
+        pass
+    sys.path.insert(0, ROOT)
+    from oracle import interp
+    from cljxla_b200.host import drivers as d
+    wf = [interp.bf16_bits_to_f32(w) if w.dtype == np.uint16 else w for w in host_w]
+    kv = [np.zeros(d.cache_shape(cfg, B, T), np.float32) for _ in range(2 * cfg.layers)]
+    it = interp.Interpreter(txt_dec)
+    x = np.zeros((B, 1), np.int32)
+    t0 = time.perf_counter()
+    for i in range(max(1, steps)):
+        it.run([x, np.array([S + i], np.int32)] + wf + kv)
+    dt = (time.perf_counter() - t0) / max(1, steps)
+    return {"value": B / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{max(1, steps)} decode step(s) of the same graph at position {S}, numpy oracle "
+                      f"(CPU restatement of the reference graph, not the reference binary), {dt:.2f} s/step"}
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    import torch
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    cfg, B, S, T, res = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        t = torch.tensor([res["dec_s"], res["e2e_s"], res["prefill_s"]], device=f"cuda:{local_rank}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dec_s, e2e_s, pre_s = [float(x) for x in t.tolist()]
+    else:
+        dec_s, e2e_s, pre_s = res["dec_s"], res["e2e_s"], res["prefill_s"]
+    if rank == 0:
+        value = world * res["tokens"] / dec_s
+        dk = res["by_kind"][res["dom"]]
+        line = {
+            "metric": "decode tokens/s (greedy KV-cached decode step, whole job)",
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dec_s / args.steps * 1e3, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": cfg.dtype,
+            "data": "synthetic (random-init weights N(0,0.02), random token ids)",
+            "config": {"workload": f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions"
+                                   + (" [tiny]" if args.tiny else ""),
+                       "model": args.config, "global_batch": B * world, "seq_len": S, "kv_len": T,
+                       "parallelism": f"dp{world} (independent replicas)",
+                       "l2": "weights stream >> 126 MB L2 every step (no flush needed)"},
+            "prefill": {"value": round(world * B * S / pre_s, 1), "unit": "tokens/s",
+                        "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill"},
+            "e2e": {"value": round(world * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": res["logits_bytes"],
+                    "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"},
+            "roofline": {"bound": "hbm", "kernel": res["dom"],
+                         "achieved": round(res["achieved"], 1), "peak": res["hbm_peak"], "unit": "GB/s",
+                         "frac": round(res["achieved"] / res["hbm_peak"], 4), "traffic": None,
+                         "peak_source": res["peak_src"],
+                         "share_of_step": round(dk["ms"] / res["total_ms"], 4) if res["total_ms"] else None},
+            "cpu_baseline": res["cpu"],
+            "clocks": res["clocks"],
+            "gpu_launches": res["launches"],
+            "kernel_time_by_kind_ms": {k: round(v["ms"] / 2, 4) for k, v in res["by_kind"].items()},
+            "plan": res["plan"],
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_reference(args, rank, world):
+    """CPU restatement of the reference path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    sys.path.insert(0, ROOT)
+    _pkg()
+    from oracle import interp
+    from cljxla_b200.host import drivers as d
+    from cljxla_b200.host import stablehlo as shlo
+    cfg, B, S, T = model_setup(args)
+    rng = np.random.Generator(np.random.PCG64(1234))
+    wf = []
+    for name, shp, kind in d.weight_specs(cfg):
+        if kind == "mat":
+            a = rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
+        elif kind == "plain_norm":
+            a = np.float32(1) + rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
+        elif kind == "gemma_norm":
+            a = rng.standard_normal(shp, dtype=np.float32) * np.float32(0.02)
+        elif kind == "one":
+            a = np.ones(shp, np.float32)
+        else:
+            a = np.zeros(shp, np.float32)
+        wf.append(interp.round_bf16(a) if cfg.dtype == "bf16" else a)
+    txt = shlo.graph_to_mlir_text(d.build_graph(cfg, "decode", B, S, T))
+    it = interp.Interpreter(txt)
+    kv = [np.zeros(d.cache_shape(cfg, B, T), np.float32) for _ in range(2 * cfg.layers)]
+    x = np.zeros((B, 1), np.int32)
+    for i in range(args.warmup):
+        it.run([x, np.array([S + i], np.int32)] + wf + kv)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        outs = it.run([x, np.array([S + i], np.int32)] + wf + kv)
+        kv = outs[1:]
+    dt = time.perf_counter() - t0
+    v = B * args.steps / dt
+    line = {"impl": "reference", "metric": "decode tokens/s (greedy KV-cached decode step, whole job)",
+            "value": round(v, 4), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
+            "config": {"workload": f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions",
+                       "model": args.config, "global_batch": B, "seq_len": S},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": "full decode steps of the printed graph on the numpy oracle (CPU "
+                                       "restatement; the reference's JVM + xla_cpu_pjrt path is not installable here)"},
+            "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,398 @@
+// Generic kernels: every printed op the fused fast paths do not claim runs
+// here on the GPU (there is no CPU fallback).  Fused elementwise regions run
+// through a small register-program interpreter; reductions, strided copies
+// (view materialisation, concatenate), gather and dynamic_update_slice have
+// their own kernels.  All read operands through strided views so reshape /
+// transpose / broadcast_in_dim / slice never copy unless a consumer needs a
+// dense layout.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+
+namespace cljxla {
+
+namespace {
+
+__device__ __forceinline__ uint32_t ld_elem(const char* base, int64_t i, int dt) {
+  switch (dt) {
+    case KDT_F32: return __float_as_uint(((const float*)base)[i]);
+    case KDT_BF16: return (uint32_t)((const uint16_t*)base)[i] << 16;
+    case KDT_F16: return __float_as_uint(__half2float(((const __half*)base)[i]));
+    case KDT_I32: case KDT_U32: return (uint32_t)((const int32_t*)base)[i];
+    case KDT_I8: return (uint32_t)(int32_t)((const int8_t*)base)[i];
+    case KDT_U8: return (uint32_t)((const uint8_t*)base)[i];
+    case KDT_I16: return (uint32_t)(int32_t)((const int16_t*)base)[i];
+    case KDT_I1: return ((const uint8_t*)base)[i] ? 1u : 0u;
+    case KDT_I64: return (uint32_t)(int32_t)((const int64_t*)base)[i];
+    case KDT_F64: return __float_as_uint((float)((const double*)base)[i]);
+  }
+  return 0;
+}
+
+__device__ __forceinline__ void st_elem(char* base, int64_t i, int dt, uint32_t v) {
+  switch (dt) {
+    case KDT_F32: ((float*)base)[i] = __uint_as_float(v); break;
+    case KDT_BF16: {
+      __nv_bfloat16 b = __float2bfloat16_rn(__uint_as_float(v));
+      ((__nv_bfloat16*)base)[i] = b;
+      break;
+    }
+    case KDT_F16: ((__half*)base)[i] = __float2half_rn(__uint_as_float(v)); break;
+    case KDT_I32: case KDT_U32: ((int32_t*)base)[i] = (int32_t)v; break;
+    case KDT_I8: ((int8_t*)base)[i] = (int8_t)(int32_t)v; break;
+    case KDT_U8: ((uint8_t*)base)[i] = (uint8_t)v; break;
+    case KDT_I16: ((int16_t*)base)[i] = (int16_t)(int32_t)v; break;
+    case KDT_I1: ((uint8_t*)base)[i] = v ? 1 : 0; break;
+    case KDT_I64: ((int64_t*)base)[i] = (int64_t)(int32_t)v; break;
+    case KDT_F64: ((double*)base)[i] = (double)__uint_as_float(v); break;
+  }
+}
+
+__device__ __forceinline__ bool is_float_dt(int dt) {
+  return dt == KDT_F32 || dt == KDT_BF16 || dt == KDT_F16 || dt == KDT_F64;
+}
+
+// round an f32 value to the value set of a floating element type
+__device__ __forceinline__ float rnd(float v, int dt) {
+  if (dt == KDT_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == KDT_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t fbits(float v, int dt) { return __float_as_uint(rnd(v, dt)); }
+
+__device__ uint32_t ew_convert(uint32_t v, int from, int to) {
+  bool ff = is_float_dt(from), tf = is_float_dt(to);
+  if (to == KDT_I1) return ff ? (__uint_as_float(v) != 0.0f) : (v != 0);
+  if (ff && tf) return fbits(__uint_as_float(v), to);
+  if (!ff && tf) {
+    float f = (from == KDT_U32) ? (float)v : (float)(int32_t)v;
+    return fbits(f, to);
+  }
+  if (ff && !tf) {
+    float f = __uint_as_float(v);
+    int32_t r;
+    if (f != f) r = 0;
+    else if (f >= 2147483647.0f) r = 2147483647;
+    else if (f <= -2147483648.0f) r = (int32_t)0x80000000;
+    else r = (int32_t)f;  // truncation toward zero
+    if (to == KDT_I8) r = (int8_t)r;
+    else if (to == KDT_U8) r = (uint8_t)r;
+    else if (to == KDT_I16) r = (int16_t)r;
+    return (uint32_t)r;
+  }
+  int32_t r = (int32_t)v;
+  if (to == KDT_I8) r = (int8_t)r;
+  else if (to == KDT_U8) r = (uint8_t)r;
+  else if (to == KDT_I16) r = (int16_t)r;
+  return (uint32_t)r;
+}
+
+__global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParams P,
+                                                 const uint64_t* __restrict__ argtab) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = tid; e < P.n; e += nthreads) {
+    int64_t idx[CLJXLA_MAXR];
+    int64_t rem = e;
+    for (int d = P.rank - 1; d >= 0; --d) {
+      int64_t dim = P.dims[d];
+      idx[d] = rem % dim;
+      rem /= dim;
+    }
+    uint32_t R[EW_NREG];
+    for (int pc = 0; pc < P.ncode; ++pc) {
+      const EwInstr& I = P.code[pc];
+      uint32_t r = 0;
+      const int dt = I.dt;
+      const bool fl = is_float_dt(dt);
+      switch (I.op) {
+        case EW_LOAD: {
+          const EwIn& in = P.in[I.aux];
+          int64_t off = 0;
+          for (int d = 0; d < P.rank; ++d) off += idx[d] * in.stride[d];
+          r = ld_elem(dres(in.p, argtab), off, in.dt);
+          break;
+        }
+        case EW_IMM: r = fl ? __float_as_uint(I.fimm) : (uint32_t)I.iimm; break;
+        case EW_IOTA: r = fl ? fbits((float)idx[I.aux], dt) : (uint32_t)idx[I.aux]; break;
+        case EW_ADD: case EW_SUB: case EW_MUL: case EW_DIV: case EW_MAX: case EW_MIN: {
+          uint32_t a = R[I.a], b = R[I.b];
+          if (fl) {
+            float x = __uint_as_float(a), y = __uint_as_float(b), z;
+            switch (I.op) {
+              case EW_ADD: z = x + y; break;
+              case EW_SUB: z = x - y; break;
+              case EW_MUL: z = x * y; break;
+              case EW_DIV: z = x / y; break;
+              case EW_MAX: z = (x != x || y != y) ? __int_as_float(0x7fc00000) : fmaxf(x, y); break;
+              default: z = (x != x || y != y) ? __int_as_float(0x7fc00000) : fminf(x, y); break;
+            }
+            r = fbits(z, dt);
+          } else {
+            int32_t x = (int32_t)a, y = (int32_t)b, z;
+            switch (I.op) {
+              case EW_ADD: z = x + y; break;
+              case EW_SUB: z = x - y; break;
+              case EW_MUL: z = x * y; break;
+              case EW_DIV: z = y == 0 ? -1 : x / y; break;
+              case EW_MAX: z = x > y ? x : y; break;
+              default: z = x < y ? x : y; break;
+            }
+            if (dt == KDT_I1) z = z ? 1 : 0;
+            r = (uint32_t)z;
+          }
+          break;
+        }
+        case EW_EXP: case EW_TANH: case EW_SQRT: case EW_RSQRT: case EW_SIN: case EW_COS:
+        case EW_LOGISTIC: case EW_NEG: case EW_ABS: {
+          if (fl) {
+            float x = __uint_as_float(R[I.a]), z;
+            switch (I.op) {
+              case EW_EXP: z = expf(x); break;
+              case EW_TANH: z = tanhf(x); break;
+              case EW_SQRT: z = sqrtf(x); break;
+              case EW_RSQRT: z = 1.0f / sqrtf(x); break;
+              case EW_SIN: z = sinf(x); break;
+              case EW_COS: z = cosf(x); break;
+              case EW_LOGISTIC: z = 1.0f / (1.0f + expf(-x)); break;
+              case EW_NEG: z = -x; break;
+              default: z = fabsf(x); break;
+            }
+            r = fbits(z, dt);
+          } else {
+            int32_t x = (int32_t)R[I.a];
+            r = (uint32_t)(I.op == EW_NEG ? -x : (I.op == EW_ABS ? (x < 0 ? -x : x) : x));
+          }
+          break;
+        }
+        case EW_CONVERT: r = ew_convert(R[I.a], I.aux, dt); break;
+        case EW_CMP: {
+          uint32_t a = R[I.a], b = R[I.b];
+          bool c;
+          if (is_float_dt(I.aux2)) {
+            float x = __uint_as_float(a), y = __uint_as_float(b);
+            switch (I.aux) {
+              case 0: c = x == y; break;
+              case 1: c = x != y; break;
+              case 2: c = x >= y; break;
+              case 3: c = x > y; break;
+              case 4: c = x <= y; break;
+              default: c = x < y; break;
+            }
+          } else {
+            int32_t x = (int32_t)a, y = (int32_t)b;
+            switch (I.aux) {
+              case 0: c = x == y; break;
+              case 1: c = x != y; break;
+              case 2: c = x >= y; break;
+              case 3: c = x > y; break;
+              case 4: c = x <= y; break;
+              default: c = x < y; break;
+            }
+          }
+          r = c ? 1u : 0u;
+          break;
+        }
+        case EW_SELECT: r = R[I.a] ? R[I.b] : R[I.c]; break;
+      }
+      R[I.dst] = r;
+    }
+    for (int o = 0; o < P.nout; ++o) st_elem(dres(P.out[o].p, argtab), e, P.out[o].dt, R[P.out[o].reg]);
+  }
+}
+
+__device__ __forceinline__ int64_t view_off(const TView& v, int64_t e) {
+  int64_t off = 0;
+  for (int d = v.rank - 1; d >= 0; --d) {
+    int64_t dim = v.shape[d];
+    off += (e % dim) * v.stride[d];
+    e /= dim;
+  }
+  return off;
+}
+
+__global__ void copy_kernel(const __grid_constant__ CopyParams P, const uint64_t* __restrict__ argtab) {
+  const char* src = dres(P.src.p, argtab);
+  char* dst = dres(P.dst.p, argtab);
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < P.n; e += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t v = ld_elem(src, view_off(P.src, e), P.src.dt);
+    if (P.src.dt != P.dst.dt) v = ew_convert(v, P.src.dt, P.dst.dt);
+    st_elem(dst, view_off(P.dst, e), P.dst.dt, v);
+  }
+}
+
+template <int BLOCK>
+__global__ void __launch_bounds__(BLOCK) reduce_kernel(const __grid_constant__ ReduceParams P,
+                                                       const uint64_t* __restrict__ argtab) {
+  const char* src = dres(P.in.p, argtab);
+  char* dst = dres(P.out, argtab);
+  const bool fl = is_float_dt(P.in.dt);
+  __shared__ float sf[BLOCK / 32];
+  __shared__ int si[BLOCK / 32];
+  for (int64_t o = blockIdx.x; o < P.n_out; o += gridDim.x) {
+    int64_t base = 0, rem = o;
+    for (int d = P.nkeep - 1; d >= 0; --d) {
+      base += (rem % P.keep_shape[d]) * P.keep_stride[d];
+      rem /= P.keep_shape[d];
+    }
+    float accf = P.kind == 0 ? 0.0f : -INFINITY;
+    int32_t acci = P.kind == 0 ? 0 : (int32_t)0x80000000;
+    for (int64_t r = threadIdx.x; r < P.n_red; r += BLOCK) {
+      int64_t off = base;
+      if (P.nred == 1) {
+        off += r * P.red_stride[0];
+      } else {
+        int64_t rr = r;
+        for (int d = P.nred - 1; d >= 0; --d) {
+          off += (rr % P.red_shape[d]) * P.red_stride[d];
+          rr /= P.red_shape[d];
+        }
+      }
+      uint32_t v = ld_elem(src, off, P.in.dt);
+      if (fl) {
+        float x = __uint_as_float(v);
+        accf = P.kind == 0 ? accf + x : fmaxf(accf, x);
+      } else {
+        int32_t x = (int32_t)v;
+        acci = P.kind == 0 ? acci + x : max(acci, x);
+      }
+    }
+    for (int sh = 16; sh > 0; sh >>= 1) {
+      float of = __shfl_xor_sync(0xffffffffu, accf, sh);
+      int32_t oi = __shfl_xor_sync(0xffffffffu, acci, sh);
+      accf = P.kind == 0 ? accf + of : fmaxf(accf, of);
+      acci = P.kind == 0 ? acci + oi : max(acci, oi);
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) { sf[w] = accf; si[w] = acci; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float tf = P.kind == 0 ? 0.0f : -INFINITY;
+      int32_t ti = P.kind == 0 ? 0 : (int32_t)0x80000000;
+      for (int k = 0; k < BLOCK / 32; ++k) {
+        tf = P.kind == 0 ? tf + sf[k] : fmaxf(tf, sf[k]);
+        ti = P.kind == 0 ? ti + si[k] : max(ti, si[k]);
+      }
+      uint32_t res;
+      if (fl) {
+        tf = P.kind == 0 ? tf + P.init : fmaxf(tf, P.init);
+        res = fbits(tf, P.out_dt);
+      } else {
+        int32_t iv = (int32_t)P.init;
+        ti = P.kind == 0 ? ti + iv : max(ti, iv);
+        res = (uint32_t)ti;
+      }
+      st_elem(dst, o, P.out_dt, res);
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void gather_kernel(const __grid_constant__ GatherParams P, const uint64_t* __restrict__ argtab) {
+  const char* table = dres(P.table, argtab);
+  const char* idxb = dres(P.idx.p, argtab);
+  char* out = dres(P.out, argtab);
+  const int64_t esz = P.table_dt == KDT_F32 ? 4 : 2;
+  for (int64_t r = blockIdx.x; r < P.n_rows; r += gridDim.x) {
+    int64_t row = (int32_t)ld_elem(idxb, view_off(P.idx, r), P.idx_dt);
+    row = row < 0 ? 0 : (row >= P.rows_table ? P.rows_table - 1 : row);  // clamp (StableHLO gather)
+    const char* src = table + row * P.table_row_stride * esz;
+    char* dst = out + r * P.row_len * esz;
+    const int64_t bytes = P.row_len * esz;
+    if ((bytes & 15) == 0 && (((uintptr_t)src | (uintptr_t)dst) & 15) == 0) {
+      for (int64_t b = threadIdx.x * 16; b < bytes; b += blockDim.x * 16)
+        *(uint4*)(dst + b) = *(const uint4*)(src + b);
+    } else {
+      for (int64_t b = threadIdx.x; b < bytes; b += blockDim.x) dst[b] = src[b];
+    }
+  }
+}
+
+__device__ __forceinline__ int64_t dus_start(const DusParams& P, int d, const uint64_t* argtab) {
+  int64_t s = P.start_imm[d];
+  if (P.start_is_ptr[d]) s = (int32_t)ld_elem(dres(P.start_ptr[d], argtab), 0, P.start_dt[d]);
+  int64_t hi = P.out_shape[d] - P.upd_shape[d];
+  return s < 0 ? 0 : (s > hi ? hi : s);  // clamp so the update fits (StableHLO semantics)
+}
+
+__global__ void dus_kernel(const __grid_constant__ DusParams P, const uint64_t* __restrict__ argtab) {
+  int64_t st[CLJXLA_MAXR];
+  for (int d = 0; d < P.rank; ++d) st[d] = dus_start(P, d, argtab);
+  const char* opnd = dres(P.operand.p, argtab);
+  const char* upd = dres(P.update.p, argtab);
+  char* out = dres(P.out, argtab);
+  if (P.in_place) {
+    int64_t nu = 1;
+    for (int d = 0; d < P.rank; ++d) nu *= P.upd_shape[d];
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nu; e += (int64_t)gridDim.x * blockDim.x) {
+      int64_t rem = e, oo = 0, ostride = 1;
+      for (int d = P.rank - 1; d >= 0; --d) {
+        int64_t i = rem % P.upd_shape[d];
+        rem /= P.upd_shape[d];
+        oo += (st[d] + i) * ostride;
+        ostride *= P.out_shape[d];
+      }
+      st_elem(out, oo, P.dt, ld_elem(upd, view_off(P.update, e), P.update.dt));
+    }
+    return;
+  }
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < P.n; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = e, uo = 0;
+    bool inside = true;
+    int64_t ui = 0, ustride = 1;
+    for (int d = P.rank - 1; d >= 0; --d) {
+      int64_t i = rem % P.out_shape[d];
+      rem /= P.out_shape[d];
+      int64_t k = i - st[d];
+      if (k < 0 || k >= P.upd_shape[d]) inside = false;
+      ui += k * ustride;
+      ustride *= P.upd_shape[d];
+    }
+    (void)uo;
+    uint32_t v = inside ? ld_elem(upd, view_off(P.update, ui), P.update.dt)
+                        : ld_elem(opnd, view_off(P.operand, e), P.operand.dt);
+    st_elem(out, e, P.dt, v);
+  }
+}
+
+inline int grid_for(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  if (g > 148 * 64) g = 148 * 64;
+  return (int)(g < 1 ? 1 : g);
+}
+
+}  // namespace
+
+void launch_ew(const EwParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.n == 0) return;
+  ew_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
+}
+void launch_copy(const CopyParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.n == 0) return;
+  copy_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
+}
+void launch_reduce(const ReduceParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.n_out == 0) return;
+  int64_t g = p.n_out < 148 * 32 ? p.n_out : 148 * 32;
+  if (p.n_red >= 2048) reduce_kernel<512><<<(int)g, 512, 0, s>>>(p, argtab);
+  else if (p.n_red >= 256) reduce_kernel<256><<<(int)g, 256, 0, s>>>(p, argtab);
+  else reduce_kernel<64><<<(int)g, 64, 0, s>>>(p, argtab);
+}
+void launch_gather(const GatherParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.n_rows == 0) return;
+  int64_t g = p.n_rows < 65535 ? p.n_rows : 65535;
+  gather_kernel<<<(int)g, 128, 0, s>>>(p, argtab);
+}
+void launch_dus(const DusParams& p, const uint64_t* argtab, cudaStream_t s) {
+  int64_t n = p.n;
+  if (p.in_place) {
+    n = 1;
+    for (int d = 0; d < p.rank; ++d) n *= p.upd_shape[d];
+  }
+  if (n == 0) return;
+  dus_kernel<<<grid_for(n, 256), 256, 0, s>>>(p, argtab);
+}
+
+}  // namespace cljxla

@@ -1,0 +1,981 @@
+// Graph -> launch plan.
+//
+// 1. Dead code is dropped (the printed graphs carry unused RoPE branches:
+//    gemma.clj:173,177 compute q- and k-rotations twice).
+// 2. Values are classified: splat constants become immediates; reshape /
+//    transpose / broadcast_in_dim / slice / identity converts become strided
+//    views (no kernel); elementwise ops are grouped into fused register
+//    programs; every other op is one kernel.
+// 3. Elementwise grouping is cycle safe: a node may join an operand's group
+//    only if all the group's external inputs are produced before the group's
+//    first member, so the group can run as one kernel.
+// 4. Kernel units are ordered topologically (Kahn, earliest member first);
+//    views that a consumer cannot read in place are materialised on demand.
+// 5. Scratch buffers get arena offsets by liveness over the launch order.
+//
+// Device pointers go through the argument table (see kernels.h):
+//   [params P][outputs O][constant blob 1][scratch buffers T].
+#include "planner.h"
+
+#include <algorithm>
+#include <cmath>
+#include <functional>
+#include <map>
+#include <queue>
+#include <set>
+
+
+namespace cljxla {
+
+const char* kernel_kind_name(int k) {
+  static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
+                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc"};
+  return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
+}
+
+namespace {
+
+template <class T>
+std::vector<uint8_t> blob_of(const T& p) {
+  std::vector<uint8_t> b(sizeof(T));
+  memcpy(b.data(), &p, sizeof(T));
+  return b;
+}
+
+bool is_view_op(const Node& n, const Graph& g) {
+  switch (n.op) {
+    case Op::Reshape: case Op::Transpose: case Op::Broadcast: case Op::Slice: return true;
+    case Op::Convert: return g.nodes[n.in[0]].dt == n.dt;
+    default: return false;
+  }
+}
+
+std::vector<int64_t> dense_strides(const std::vector<int64_t>& shape) {
+  std::vector<int64_t> s(shape.size());
+  int64_t acc = 1;
+  for (int i = (int)shape.size() - 1; i >= 0; --i) {
+    s[i] = acc;
+    acc *= shape[i];
+  }
+  return s;
+}
+
+// Strides for `nshape` over memory described by (oshape, ostr), or false if
+// the reshape cannot be expressed as a strided view.
+bool reshape_strides(const std::vector<int64_t>& oshape, const std::vector<int64_t>& ostr,
+                     const std::vector<int64_t>& nshape, std::vector<int64_t>& nstr) {
+  std::vector<int64_t> os, ost;
+  for (size_t i = 0; i < oshape.size(); ++i)
+    if (oshape[i] != 1) { os.push_back(oshape[i]); ost.push_back(ostr[i]); }
+  nstr.assign(nshape.size(), 0);
+  size_t oi = 0;
+  size_t ni = 0;
+  while (ni < nshape.size() || oi < os.size()) {
+    if (ni < nshape.size() && nshape[ni] == 1) { nstr[ni] = 0; ++ni; continue; }
+    if (oi >= os.size() || ni >= nshape.size()) return false;
+    // take a chunk of old dims and new dims with equal products
+    int64_t op = os[oi], np = nshape[ni];
+    size_t oj = oi + 1, nj = ni + 1;
+    while (op != np) {
+      if (op < np) {
+        if (oj >= os.size()) return false;
+        op *= os[oj++];
+      } else {
+        while (nj < nshape.size() && nshape[nj] == 1) nj++;
+        if (nj >= nshape.size()) return false;
+        np *= nshape[nj++];
+      }
+    }
+    // old dims [oi, oj) must be mutually contiguous
+    for (size_t k = oi; k + 1 < oj; ++k)
+      if (ost[k] != ost[k + 1] * os[k + 1]) return false;
+    int64_t stride = ost[oj - 1];
+    for (size_t k = nj; k-- > ni;) {
+      if (nshape[k] == 1) { nstr[k] = 0; continue; }
+      nstr[k] = stride;
+      stride *= nshape[k];
+    }
+    oi = oj;
+    ni = nj;
+  }
+  return true;
+}
+
+int kdt(DT t) { return (int)t; }
+
+// host evaluation of elementwise ops on splat constants (same semantics as the
+// device interpreter: f32 arithmetic rounded to the result type; int32 ints)
+double round_host(double v, DT dt) {
+  switch (dt) {
+    case DT::F32: return (double)(float)v;
+    case DT::BF16: return (double)bf16_to_f32(f32_to_bf16((float)v));
+    case DT::F16: return (double)f16_to_f32(f32_to_f16((float)v));
+    case DT::I1: return v != 0 ? 1 : 0;
+    default: return (double)(int32_t)(int64_t)v;
+  }
+}
+
+bool fold_splat(const Node& n, const std::vector<double>& a, const std::vector<DT>& adt, double& out) {
+  const bool fl = dt_is_float(n.dt);
+  float x = a.size() > 0 ? (float)a[0] : 0.f, y = a.size() > 1 ? (float)a[1] : 0.f;
+  double r;
+  switch (n.op) {
+    case Op::Add: r = fl ? (double)(x + y) : (double)((int32_t)a[0] + (int32_t)a[1]); break;
+    case Op::Sub: r = fl ? (double)(x - y) : (double)((int32_t)a[0] - (int32_t)a[1]); break;
+    case Op::Mul: r = fl ? (double)(x * y) : (double)((int32_t)a[0] * (int32_t)a[1]); break;
+    case Op::Div:
+      if (fl) r = (double)(x / y);
+      else if ((int32_t)a[1] == 0) return false;
+      else r = (double)((int32_t)a[0] / (int32_t)a[1]);
+      break;
+    case Op::Max: r = fl ? (double)fmaxf(x, y) : std::max(a[0], a[1]); break;
+    case Op::Min: r = fl ? (double)fminf(x, y) : std::min(a[0], a[1]); break;
+    case Op::Neg: r = fl ? (double)(-x) : -a[0]; break;
+    case Op::Sqrt: if (!fl) return false; r = (double)sqrtf(x); break;
+    case Op::Convert:
+      if (fl) r = dt_is_float(adt[0]) ? (double)(float)a[0] : (double)(float)a[0];
+      else if (n.dt == DT::I1) r = a[0] != 0;
+      else r = dt_is_float(adt[0]) ? std::trunc(a[0]) : a[0];
+      break;
+    case Op::Select: r = a[0] != 0 ? a[1] : a[2]; break;
+    case Op::Compare: {
+      bool c;
+      switch (n.i0) {
+        case CMP_EQ: c = a[0] == a[1]; break;
+        case CMP_NE: c = a[0] != a[1]; break;
+        case CMP_GE: c = a[0] >= a[1]; break;
+        case CMP_GT: c = a[0] > a[1]; break;
+        case CMP_LE: c = a[0] <= a[1]; break;
+        default: c = a[0] < a[1]; break;
+      }
+      r = c;
+      break;
+    }
+    default: return false;  // transcendental splats are left to the device
+  }
+  out = round_host(r, n.dt);
+  return true;
+}
+
+struct Loc {
+  enum Kind { NONE, SPLAT, BUF, VIEWOP, EW } kind = NONE;
+  double splat = 0;
+  int slot = -1;  // argtab slot of the node's buffer (BUF / materialised EW)
+};
+
+class Planner {
+ public:
+  Planner(const Graph& g, const PlanOptions& o, Plan& p) : g_(g), opt_(o), plan_(p) {}
+  void run();
+
+ private:
+  const Graph& g_;
+  PlanOptions opt_;
+  Plan& plan_;
+  int P_ = 0, O_ = 0;
+  std::vector<Loc> loc_;
+  std::vector<char> live_;
+  std::vector<std::vector<int>> users_;
+  std::vector<int> uf_;                       // union-find parent (EW nodes)
+  std::vector<int> gmin_, gext_, gsize_, gin_;
+  std::vector<int> out_claim_;                // node -> output index claimed, or -1
+  std::vector<int> mat_slot_;                 // view node -> scratch slot of its materialised copy
+  std::vector<int64_t> tmp_bytes_;            // scratch buffer sizes
+  std::vector<int> tmp_first_, tmp_last_;     // liveness (launch indices)
+
+  int find(int x) { while (uf_[x] != x) x = uf_[x] = uf_[uf_[x]]; return x; }
+  int tmp_slot(int b) const { return P_ + O_ + 1 + b; }
+  int new_tmp(int64_t bytes) {
+    tmp_bytes_.push_back(std::max<int64_t>(bytes, 1));
+    tmp_first_.push_back((int)plan_.launches.size());
+    tmp_last_.push_back((int)plan_.launches.size());
+    return tmp_slot((int)tmp_bytes_.size() - 1);
+  }
+  void touch(int slot) {
+    int b = slot - (P_ + O_ + 1);
+    if (b >= 0) tmp_last_[b] = std::max(tmp_last_[b], (int)plan_.launches.size());
+  }
+  int view_root(int n) const {
+    while (is_view_op(g_.nodes[n], g_)) n = g_.nodes[n].in[0];
+    return n;
+  }
+  bool is_splat(int n) const { return loc_[n].kind == Loc::SPLAT; }
+
+  void classify();
+  void group_elementwise();
+  void decide_materialisation();
+  void emit_all();
+  void emit_unit(int u);
+  void emit_ew_group(const std::vector<int>& members);
+  void emit_node_kernel(int n);
+  void emit_outputs();
+  void allocate_arena();
+
+ public:
+  // pointer/view helpers (used by fast paths too)
+  int ensure_buf(int n);
+  TView view_of(int n);
+  TView dense_view(int slot, DT dt, const std::vector<int64_t>& shape, int64_t eoff = 0);
+  TView materialize(const TView& v, const std::vector<int64_t>& shape, DT dt);
+  void push(int kind, std::vector<uint8_t> blob, const std::string& label, int64_t bytes = 0, int64_t flops = 0) {
+    Launch l;
+    l.kind = kind;
+    l.blob = std::move(blob);
+    l.label = label;
+    l.algo_bytes = bytes;
+    l.algo_flops = flops;
+    plan_.launches.push_back(std::move(l));
+  }
+  DPtr slot_ptr(int slot, int64_t off_bytes = 0) {
+    DPtr p;
+    p.slot = slot;
+    p.pad_ = 0;
+    p.off = off_bytes;
+    touch(slot);
+    return p;
+  }
+};
+
+void Planner::classify() {
+  const int N = (int)g_.nodes.size();
+  loc_.assign(N, Loc());
+  for (int i = 0; i < N; ++i) {
+    const Node& n = g_.nodes[i];
+    if (!live_[i]) continue;
+    if (n.dt == DT::I64 || n.dt == DT::F64)
+      fail(E_UNIMPLEMENTED, std::string("element type ") + dt_name(n.dt) + " is not supported on this device path");
+    if (n.rank() > CLJXLA_MAXR) fail(E_UNIMPLEMENTED, "rank > 8 is not supported");
+    Loc& L = loc_[i];
+    if (n.op == Op::Param) { L.kind = Loc::BUF; continue; }
+    if (n.op == Op::Constant) {
+      if (n.splat) { L.kind = Loc::SPLAT; L.splat = n.splat_val; continue; }
+      L.kind = Loc::BUF;
+      size_t off = (plan_.const_blob.size() + 255) & ~size_t(255);
+      plan_.const_blob.resize(off + n.data.size());
+      memcpy(plan_.const_blob.data() + off, n.data.data(), n.data.size());
+      L.slot = P_ + O_;  // const blob; offset recorded in splat field
+      L.splat = (double)off;
+      continue;
+    }
+    if (is_view_op(n, g_)) {
+      if (is_splat(n.in[0])) {
+        L.kind = Loc::SPLAT;
+        L.splat = loc_[n.in[0]].splat;
+      } else {
+        L.kind = Loc::VIEWOP;
+      }
+      continue;
+    }
+    if (op_is_elementwise(n.op)) {
+      bool all_splat = n.op != Op::Iota;
+      std::vector<double> a;
+      std::vector<DT> adt;
+      for (int x : n.in) {
+        all_splat &= is_splat(x);
+        a.push_back(loc_[x].splat);
+        adt.push_back(g_.nodes[x].dt);
+      }
+      double v;
+      if (all_splat && !n.in.empty() && fold_splat(n, a, adt, v)) {
+        L.kind = Loc::SPLAT;
+        L.splat = v;
+        continue;
+      }
+      L.kind = Loc::EW;
+      continue;
+    }
+    L.kind = Loc::BUF;  // produced by its own kernel
+  }
+}
+
+void Planner::group_elementwise() {
+  const int N = (int)g_.nodes.size();
+  uf_.resize(N);
+  gmin_.assign(N, 0);
+  gext_.assign(N, -1);
+  gsize_.assign(N, 1);
+  gin_.assign(N, 0);
+  for (int i = 0; i < N; ++i) uf_[i] = i;
+  auto ext_idx = [&](int o) -> int {  // index of the node an operand needs computed first
+    if (is_splat(o)) return -1;
+    int r = view_root(o);
+    const Node& rn = g_.nodes[r];
+    if (rn.op == Op::Param || rn.op == Op::Constant || is_splat(r)) return -1;
+    return r;
+  };
+  for (int i = 0; i < N; ++i) {
+    if (!live_[i] || loc_[i].kind != Loc::EW) continue;
+    const Node& n = g_.nodes[i];
+    std::vector<int> cands;
+    if (opt_.fuse)
+      for (int o : n.in)
+        if (loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape) cands.push_back(find(o));
+    std::sort(cands.begin(), cands.end());
+    cands.erase(std::unique(cands.begin(), cands.end()), cands.end());
+    std::set<int> merged;
+    auto eval = [&](const std::set<int>& set, int& tmin, int& text, int& tsize, int& tin) {
+      tmin = i;
+      text = -1;
+      tsize = 1;
+      tin = 0;
+      for (int G : set) {
+        tmin = std::min(tmin, gmin_[G]);
+        text = std::max(text, gext_[G]);
+        tsize += gsize_[G];
+        tin += gin_[G];
+      }
+      for (int o : n.in) {
+        if (is_splat(o)) continue;
+        bool inside = loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape && set.count(find(o));
+        if (!inside) { text = std::max(text, ext_idx(o)); tin++; }
+      }
+    };
+    for (int G : cands) {
+      std::set<int> trial = merged;
+      trial.insert(G);
+      int tmin, text, tsize, tin;
+      eval(trial, tmin, text, tsize, tin);
+      if (text < tmin && tsize <= 24 && tin <= EW_MAXIN - 2) merged = trial;
+    }
+    int tmin, text, tsize, tin;
+    eval(merged, tmin, text, tsize, tin);
+    for (int M : merged) uf_[M] = i;
+    gmin_[i] = tmin;
+    gext_[i] = text;
+    gsize_[i] = tsize;
+    gin_[i] = tin;
+  }
+}
+
+void Planner::decide_materialisation() {
+  const int N = (int)g_.nodes.size();
+  for (int i = 0; i < N; ++i) {
+    if (!live_[i] || loc_[i].kind != Loc::EW) continue;
+    bool need = out_claim_[i] >= 0;
+    for (int u : users_[i]) {
+      if (!live_[u]) continue;
+      bool same = loc_[u].kind == Loc::EW && find(u) == find(i) && g_.nodes[u].shape == g_.nodes[i].shape;
+      if (!same) need = true;
+    }
+    for (int o : g_.outputs) if (o == i) need = true;
+    if (need) ensure_buf(i);
+  }
+}
+
+int Planner::ensure_buf(int n) {
+  Loc& L = loc_[n];
+  if (L.slot >= 0) return L.slot;
+  const Node& nd = g_.nodes[n];
+  if (nd.op == Op::Param) {
+    for (int k = 0; k < P_; ++k)
+      if (g_.params[k] == n) return L.slot = k;
+  }
+  if (out_claim_[n] >= 0) return L.slot = P_ + out_claim_[n];
+  return L.slot = new_tmp(nd.numel() * (int64_t)dt_size(nd.dt));
+}
+
+TView Planner::dense_view(int slot, DT dt, const std::vector<int64_t>& shape, int64_t eoff) {
+  TView v{};
+  v.p = slot_ptr(slot, eoff * (int64_t)dt_size(dt));
+  v.dt = kdt(dt);
+  v.rank = (int)shape.size();
+  auto st = dense_strides(shape);
+  for (int i = 0; i < v.rank; ++i) { v.shape[i] = shape[i]; v.stride[i] = st[i]; }
+  return v;
+}
+
+TView Planner::materialize(const TView& src, const std::vector<int64_t>& shape, DT dt) {
+  int slot = new_tmp(numel(shape) * (int64_t)dt_size(dt));
+  CopyParams cp{};
+  cp.src = src;
+  cp.dst = dense_view(slot, dt, shape);
+  cp.n = numel(shape);
+  push(K_COPY, blob_of(cp), "materialize", 2 * cp.n * (int64_t)dt_size(dt));
+  return dense_view(slot, dt, shape);
+}
+
+TView Planner::view_of(int n) {
+  const Node& nd = g_.nodes[n];
+  Loc& L = loc_[n];
+  if (L.kind == Loc::SPLAT) fail(E_INTERNAL, "view_of on a splat constant");
+  if (L.kind == Loc::BUF && nd.op == Op::Constant) {
+    TView v = dense_view(L.slot, nd.dt, nd.shape);
+    v.p.off = (int64_t)L.splat;
+    return v;
+  }
+  if (L.kind == Loc::BUF || L.kind == Loc::EW) {
+    if (L.slot < 0 && nd.op == Op::Param) ensure_buf(n);
+    if (L.slot < 0) fail(E_INTERNAL, std::string("value %") + nd.name + " is not materialised");
+    return dense_view(L.slot, nd.dt, nd.shape);
+  }
+  // view ops
+  if (mat_slot_[n] >= 0) return dense_view(mat_slot_[n], nd.dt, nd.shape);
+  TView in = view_of(nd.in[0]);
+  TView v = in;
+  v.rank = nd.rank();
+  for (int i = 0; i < v.rank; ++i) v.shape[i] = nd.shape[i];
+  switch (nd.op) {
+    case Op::Convert:
+      v.dt = kdt(nd.dt);
+      break;
+    case Op::Transpose:
+      for (int i = 0; i < v.rank; ++i) v.stride[i] = in.stride[nd.ia[i]];
+      break;
+    case Op::Broadcast: {
+      for (int i = 0; i < v.rank; ++i) v.stride[i] = 0;
+      for (int i = 0; i < in.rank; ++i) {
+        int od = (int)nd.ia[i];
+        v.stride[od] = (in.shape[i] == nd.shape[od]) ? in.stride[i] : 0;
+      }
+      break;
+    }
+    case Op::Slice: {
+      int64_t eoff = 0;
+      for (int i = 0; i < in.rank; ++i) {
+        eoff += nd.ia[i] * in.stride[i];
+        v.stride[i] = in.stride[i] * nd.ic[i];
+      }
+      v.p.off += eoff * (int64_t)dt_size(nd.dt);
+      break;
+    }
+    case Op::Reshape: {
+      std::vector<int64_t> os(in.shape, in.shape + in.rank), ost(in.stride, in.stride + in.rank), ns;
+      if (reshape_strides(os, ost, nd.shape, ns)) {
+        for (int i = 0; i < v.rank; ++i) v.stride[i] = ns[i];
+      } else {
+        std::vector<int64_t> ishape(in.shape, in.shape + in.rank);
+        TView m = materialize(in, ishape, g_.nodes[nd.in[0]].dt);
+        mat_slot_[n] = m.p.slot;
+        return dense_view(m.p.slot, nd.dt, nd.shape);
+      }
+      break;
+    }
+    default: fail(E_INTERNAL, "bad view op");
+  }
+  return v;
+}
+
+void Planner::emit_ew_group(const std::vector<int>& members) {
+  EwParams P{};
+  const Node& first = g_.nodes[members[0]];
+  P.rank = first.rank();
+  P.n = first.numel();
+  for (int i = 0; i < P.rank; ++i) P.dims[i] = first.shape[i];
+  std::map<int, int> reg_of;  // node -> register
+  std::map<std::pair<int, int64_t>, int> imm_reg;
+  std::map<int, int> load_reg;
+  std::set<int> member_set(members.begin(), members.end());
+  // last in-group use of each member (for register reuse)
+  std::map<int, int> last_use;
+  for (size_t k = 0; k < members.size(); ++k)
+    for (int o : g_.nodes[members[k]].in)
+      if (member_set.count(o)) last_use[o] = (int)k;
+  std::vector<int> free_regs;
+  for (int r = EW_NREG - 1; r >= 0; --r) free_regs.push_back(r);
+  auto alloc_reg = [&]() {
+    if (free_regs.empty()) fail(E_INTERNAL, "fused elementwise program needs too many registers");
+    int r = free_regs.back();
+    free_regs.pop_back();
+    return r;
+  };
+  auto emit = [&](const EwInstr& I) {
+    if (P.ncode >= EW_MAXCODE) fail(E_INTERNAL, "fused elementwise program too long");
+    P.code[P.ncode++] = I;
+  };
+  std::vector<std::pair<int, int>> outs;  // (node, reg)
+  std::string label;
+  int64_t bytes = 0;
+  for (size_t k = 0; k < members.size(); ++k) {
+    int id = members[k];
+    const Node& n = g_.nodes[id];
+    std::vector<int> regs;
+    for (int o : n.in) {
+      if (member_set.count(o) && reg_of.count(o)) { regs.push_back(reg_of[o]); continue; }
+      const Node& on = g_.nodes[o];
+      if (is_splat(o)) {
+        double v = loc_[o].splat;
+        int64_t key;
+        memcpy(&key, &v, 8);
+        auto kk = std::make_pair((int)on.dt, key);
+        if (!imm_reg.count(kk)) {
+          EwInstr I{};
+          I.op = EW_IMM;
+          I.dt = (uint8_t)kdt(on.dt);
+          I.dst = (uint8_t)alloc_reg();
+          I.fimm = (float)v;
+          I.iimm = (int32_t)(int64_t)v;
+          emit(I);
+          imm_reg[kk] = I.dst;
+        }
+        regs.push_back(imm_reg[kk]);
+        continue;
+      }
+      if (!load_reg.count(o)) {
+        if (P.nin >= EW_MAXIN) fail(E_INTERNAL, "fused elementwise region has too many inputs");
+        TView v = view_of(o);
+        EwIn& in = P.in[P.nin];
+        in.p = v.p;
+        in.dt = v.dt;
+        for (int d = 0; d < P.rank; ++d) in.stride[d] = v.stride[d];
+        bytes += on.numel() * (int64_t)dt_size(on.dt);
+        EwInstr I{};
+        I.op = EW_LOAD;
+        I.dt = (uint8_t)v.dt;
+        I.dst = (uint8_t)alloc_reg();
+        I.aux = (uint8_t)P.nin;
+        emit(I);
+        load_reg[o] = I.dst;
+        P.nin++;
+      }
+      regs.push_back(load_reg[o]);
+    }
+    EwInstr I{};
+    I.dt = (uint8_t)kdt(n.dt);
+    switch (n.op) {
+      case Op::Add: I.op = EW_ADD; break;
+      case Op::Sub: I.op = EW_SUB; break;
+      case Op::Mul: I.op = EW_MUL; break;
+      case Op::Div: I.op = EW_DIV; break;
+      case Op::Max: I.op = EW_MAX; break;
+      case Op::Min: I.op = EW_MIN; break;
+      case Op::Exp: I.op = EW_EXP; break;
+      case Op::Tanh: I.op = EW_TANH; break;
+      case Op::Sqrt: I.op = EW_SQRT; break;
+      case Op::Rsqrt: I.op = EW_RSQRT; break;
+      case Op::Sin: I.op = EW_SIN; break;
+      case Op::Cos: I.op = EW_COS; break;
+      case Op::Logistic: I.op = EW_LOGISTIC; break;
+      case Op::Neg: I.op = EW_NEG; break;
+      case Op::Abs: I.op = EW_ABS; break;
+      case Op::Convert: I.op = EW_CONVERT; I.aux = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
+      case Op::Compare: I.op = EW_CMP; I.aux = (uint8_t)n.i0; I.aux2 = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
+      case Op::Select: I.op = EW_SELECT; break;
+      case Op::Iota: I.op = EW_IOTA; I.aux = (uint8_t)n.i0; break;
+      default: fail(E_INTERNAL, "not an elementwise op");
+    }
+    if (regs.size() > 0) I.a = (uint8_t)regs[0];
+    if (regs.size() > 1) I.b = (uint8_t)regs[1];
+    if (regs.size() > 2) I.c = (uint8_t)regs[2];
+    // free operand registers whose last use is this instruction (members only)
+    for (int o : n.in)
+      if (member_set.count(o) && last_use[o] == (int)k && reg_of.count(o) && loc_[o].slot < 0) {
+        free_regs.push_back(reg_of[o]);
+        reg_of.erase(o);
+      }
+    I.dst = (uint8_t)alloc_reg();
+    emit(I);
+    reg_of[id] = I.dst;
+    if (loc_[id].slot >= 0) outs.emplace_back(id, I.dst);
+    if (!label.empty()) label += ",";
+    if (label.size() < 80) label += n.name;
+  }
+  // outputs, at most EW_MAXOUT per launch (re-run the program for extra chunks)
+  for (size_t s = 0; s < outs.size(); s += EW_MAXOUT) {
+    EwParams Q = P;
+    Q.nout = 0;
+    int64_t ob = 0;
+    for (size_t k = s; k < outs.size() && Q.nout < EW_MAXOUT; ++k) {
+      int id = outs[k].first;
+      const Node& n = g_.nodes[id];
+      Q.out[Q.nout].p = slot_ptr(loc_[id].slot);
+      Q.out[Q.nout].dt = kdt(n.dt);
+      Q.out[Q.nout].reg = outs[k].second;
+      ob += n.numel() * (int64_t)dt_size(n.dt);
+      Q.nout++;
+    }
+    push(K_EW, blob_of(Q), label, bytes + ob);
+  }
+}
+
+void Planner::emit_node_kernel(int id) {
+  const Node& n = g_.nodes[id];
+  int oslot = ensure_buf(id);
+  switch (n.op) {
+    case Op::Reduce: {
+      const Node& in = g_.nodes[n.in[0]];
+      if (!is_splat(n.in[1])) fail(E_UNIMPLEMENTED, "reduce with a non-constant init value");
+      TView v = view_of(n.in[0]);
+      ReduceParams R{};
+      R.in = v;
+      R.out = slot_ptr(oslot);
+      R.out_dt = kdt(n.dt);
+      R.kind = (int)n.i0;
+      R.init = (float)loc_[n.in[1]].splat;
+      std::set<int> red(n.ia.begin(), n.ia.end());
+      R.n_out = 1;
+      R.n_red = 1;
+      for (int d = 0; d < in.rank(); ++d) {
+        if (red.count(d)) {
+          R.red_shape[R.nred] = in.shape[d];
+          R.red_stride[R.nred] = v.stride[d];
+          R.nred++;
+          R.n_red *= in.shape[d];
+        } else {
+          R.keep_shape[R.nkeep] = in.shape[d];
+          R.keep_stride[R.nkeep] = v.stride[d];
+          R.nkeep++;
+          R.n_out *= in.shape[d];
+        }
+      }
+      if (R.nred == 0) { R.red_shape[0] = 1; R.red_stride[0] = 0; R.nred = 1; }
+      push(K_REDUCE, blob_of(R), n.name,
+           in.numel() * (int64_t)dt_size(in.dt) + n.numel() * (int64_t)dt_size(n.dt));
+      break;
+    }
+    case Op::Gather: {
+      const Node& tab = g_.nodes[n.in[0]];
+      const Node& idx = g_.nodes[n.in[1]];
+      bool ok = tab.rank() == 2 && n.ib == std::vector<int64_t>{0} && n.ic == std::vector<int64_t>{0} &&
+                n.id.size() == 2 && n.id[0] == 1 && n.id[1] == tab.shape[1] && idx.rank() >= 1 &&
+                n.i0 == idx.rank() - 1 && idx.shape.back() == 1 && n.ia == std::vector<int64_t>{idx.rank() - 1} &&
+                (tab.dt == DT::F32 || tab.dt == DT::BF16 || tab.dt == DT::F16);
+      if (!ok) fail(E_UNIMPLEMENTED, "gather form not supported (only row gathers of a 2-D table)");
+      TView tv = view_of(n.in[0]);
+      if (tv.stride[1] != 1) tv = materialize(tv, tab.shape, tab.dt);
+      GatherParams G{};
+      G.table = tv.p;
+      G.table_dt = tv.dt;
+      G.rows_table = tab.shape[0];
+      G.row_len = tab.shape[1];
+      G.table_row_stride = tv.stride[0];
+      TView iv = view_of(n.in[1]);
+      G.idx = iv;
+      G.idx_dt = iv.dt;
+      G.out = slot_ptr(oslot);
+      G.n_rows = idx.numel();
+      push(K_GATHER, blob_of(G), n.name, 2 * n.numel() * (int64_t)dt_size(n.dt));
+      break;
+    }
+    case Op::DUS: {
+      DusParams D{};
+      D.rank = n.rank();
+      D.dt = kdt(n.dt);
+      D.operand = view_of(n.in[0]);
+      D.update = view_of(n.in[1]);
+      const Node& up = g_.nodes[n.in[1]];
+      for (int d = 0; d < D.rank; ++d) {
+        D.out_shape[d] = n.shape[d];
+        D.upd_shape[d] = up.shape[d];
+        int s = n.in[2 + d];
+        if (is_splat(s)) {
+          D.start_imm[d] = (int64_t)loc_[s].splat;
+        } else {
+          TView sv = view_of(s);
+          D.start_ptr[d] = sv.p;
+          D.start_dt[d] = sv.dt;
+          D.start_is_ptr[d] = 1;
+        }
+      }
+      D.out = slot_ptr(oslot);
+      D.n = n.numel();
+      int64_t ub = up.numel() * (int64_t)dt_size(n.dt);
+      push(K_DUS, blob_of(D), n.name, 2 * n.numel() * (int64_t)dt_size(n.dt) + ub);
+      break;
+    }
+    case Op::Concat: {
+      int64_t off = 0;
+      int dim = (int)n.i0;
+      TView ov = dense_view(oslot, n.dt, n.shape);
+      for (int x : n.in) {
+        const Node& xn = g_.nodes[x];
+        CopyParams C{};
+        C.dst = ov;
+        for (int d = 0; d < C.dst.rank; ++d) C.dst.shape[d] = xn.shape[d];
+        C.dst.p.off += off * ov.stride[dim] * (int64_t)dt_size(n.dt);
+        if (is_splat(x)) {
+          // broadcast a splat into the slice through a one-instruction program
+          EwParams E{};
+          E.rank = xn.rank();
+          E.n = xn.numel();
+          for (int d = 0; d < E.rank; ++d) E.dims[d] = xn.shape[d];
+          EwInstr I{};
+          I.op = EW_IMM;
+          I.dt = (uint8_t)kdt(xn.dt);
+          I.fimm = (float)loc_[x].splat;
+          I.iimm = (int32_t)(int64_t)loc_[x].splat;
+          E.code[0] = I;
+          E.ncode = 1;
+          // write through a strided copy afterwards is overkill; store densely into a scratch then copy
+          int slot = new_tmp(xn.numel() * (int64_t)dt_size(xn.dt));
+          E.out[0].p = slot_ptr(slot);
+          E.out[0].dt = kdt(xn.dt);
+          E.out[0].reg = 0;
+          E.nout = 1;
+          push(K_EW, blob_of(E), n.name + ".splat");
+          C.src = dense_view(slot, xn.dt, xn.shape);
+        } else {
+          C.src = view_of(x);
+        }
+        C.n = xn.numel();
+        push(K_COPY, blob_of(C), n.name, 2 * C.n * (int64_t)dt_size(n.dt));
+        off += xn.shape[dim];
+      }
+      break;
+    }
+    case Op::Dot: {
+      const Node& a = g_.nodes[n.in[0]];
+      const Node& b = g_.nodes[n.in[1]];
+      std::vector<int64_t> lb = n.ia, rb = n.ib, lc = n.ic, rc = n.id, lf, rf;
+      for (int d = 0; d < a.rank(); ++d)
+        if (std::find(lb.begin(), lb.end(), d) == lb.end() && std::find(lc.begin(), lc.end(), d) == lc.end())
+          lf.push_back(d);
+      for (int d = 0; d < b.rank(); ++d)
+        if (std::find(rb.begin(), rb.end(), d) == rb.end() && std::find(rc.begin(), rc.end(), d) == rc.end())
+          rf.push_back(d);
+      auto collapse = [](const TView& v, const std::vector<int64_t>& dims, int64_t& size, int64_t& stride) {
+        size = 1;
+        stride = 0;
+        int64_t prev_stride = -1, prev_size = 1;
+        bool first = true;
+        for (int64_t d : dims) {
+          int64_t s = v.shape[d];
+          size *= s;
+          if (s == 1) continue;
+          if (!first && prev_stride != v.stride[d] * s) return false;
+          prev_stride = v.stride[d];
+          prev_size = s;
+          first = false;
+        }
+        (void)prev_size;
+        stride = first ? 0 : prev_stride;
+        return true;
+      };
+      auto canon = [&](int x, const std::vector<int64_t>& g1, const std::vector<int64_t>& g2,
+                       const std::vector<int64_t>& g3, int64_t s[3], int64_t z[3]) {
+        TView v = view_of(x);
+        const Node& xn = g_.nodes[x];
+        bool ok = collapse(v, g1, z[0], s[0]) && collapse(v, g2, z[1], s[1]) && collapse(v, g3, z[2], s[2]);
+        if (!ok) {
+          // permuted dense copy in (g1, g2, g3) order
+          std::vector<int64_t> perm;
+          for (auto d : g1) perm.push_back(d);
+          for (auto d : g2) perm.push_back(d);
+          for (auto d : g3) perm.push_back(d);
+          TView pv = v;
+          std::vector<int64_t> pshape;
+          for (size_t i = 0; i < perm.size(); ++i) {
+            pv.shape[i] = v.shape[perm[i]];
+            pv.stride[i] = v.stride[perm[i]];
+            pshape.push_back(v.shape[perm[i]]);
+          }
+          TView m = materialize(pv, pshape, xn.dt);
+          std::vector<int64_t> q1, q2, q3;
+          int k = 0;
+          for (size_t i = 0; i < g1.size(); ++i) q1.push_back(k++);
+          for (size_t i = 0; i < g2.size(); ++i) q2.push_back(k++);
+          for (size_t i = 0; i < g3.size(); ++i) q3.push_back(k++);
+          collapse(m, q1, z[0], s[0]);
+          collapse(m, q2, z[1], s[1]);
+          collapse(m, q3, z[2], s[2]);
+          return m;
+        }
+        return v;
+      };
+      int64_t as[3], az[3], bs[3], bz[3];
+      TView av = canon(n.in[0], lb, lf, lc, as, az);  // batch, M, K
+      TView bv = canon(n.in[1], rb, rc, rf, bs, bz);  // batch, K, N
+      if (az[0] != bz[0] || az[2] != bz[1]) fail(E_INVALID, "dot_general dimension mismatch in %" + n.name);
+      GemmParams G{};
+      G.a = av.p;
+      G.b = bv.p;
+      G.c = slot_ptr(oslot);
+      G.a_dt = av.dt;
+      G.b_dt = bv.dt;
+      G.c_dt = kdt(n.dt);
+      G.batch = az[0];
+      G.M = az[1];
+      G.K = az[2];
+      G.N = bz[2];
+      G.a_sb = as[0]; G.a_sm = as[1]; G.a_sk = as[2];
+      G.b_sb = bs[0]; G.b_sk = bs[1]; G.b_sn = bs[2];
+      G.c_sb = G.M * G.N;
+      if (!(G.a_dt == KDT_F32 || G.a_dt == KDT_BF16 || G.a_dt == KDT_F16) ||
+          !(G.b_dt == KDT_F32 || G.b_dt == KDT_BF16 || G.b_dt == KDT_F16) ||
+          !(G.c_dt == KDT_F32 || G.c_dt == KDT_BF16 || G.c_dt == KDT_F16))
+        fail(E_UNIMPLEMENTED, "dot_general on integer operands");
+      int64_t bytes = a.numel() * (int64_t)dt_size(a.dt) + b.numel() * (int64_t)dt_size(b.dt) +
+                      n.numel() * (int64_t)dt_size(n.dt);
+      int64_t flops = 2 * G.batch * G.M * G.N * G.K;
+      push(K_GEMM, blob_of(G), n.name, bytes, flops);
+      break;
+    }
+    default:
+      fail(E_UNIMPLEMENTED, std::string("no kernel for op ") + op_name(n.op));
+  }
+}
+
+void Planner::emit_outputs() {
+  std::vector<char> claimed_done(g_.nodes.size(), 0);
+  for (int k = 0; k < O_; ++k) {
+    int n = g_.outputs[k];
+    const Node& nd = g_.nodes[n];
+    int oslot = P_ + k;
+    if (out_claim_[n] == k) continue;  // written in place by its producer
+    TView dst = dense_view(oslot, nd.dt, nd.shape);
+    if (is_splat(n)) {
+      EwParams E{};
+      E.rank = nd.rank();
+      E.n = nd.numel();
+      for (int d = 0; d < E.rank; ++d) E.dims[d] = nd.shape[d];
+      EwInstr I{};
+      I.op = EW_IMM;
+      I.dt = (uint8_t)kdt(nd.dt);
+      I.fimm = (float)loc_[n].splat;
+      I.iimm = (int32_t)(int64_t)loc_[n].splat;
+      E.code[0] = I;
+      E.ncode = 1;
+      E.out[0].p = dst.p;
+      E.out[0].dt = kdt(nd.dt);
+      E.out[0].reg = 0;
+      E.nout = 1;
+      push(K_EW, blob_of(E), "out." + nd.name, nd.numel() * (int64_t)dt_size(nd.dt));
+      continue;
+    }
+    CopyParams C{};
+    C.src = view_of(n);
+    C.dst = dst;
+    C.n = nd.numel();
+    push(K_COPY, blob_of(C), "out." + nd.name, 2 * C.n * (int64_t)dt_size(nd.dt));
+  }
+}
+
+void Planner::emit_unit(int u) {
+  const Node& n = g_.nodes[u];
+  if (loc_[u].kind == Loc::EW) {
+    std::vector<int> members;
+    for (size_t i = 0; i < g_.nodes.size(); ++i)
+      if (live_[i] && loc_[i].kind == Loc::EW && find((int)i) == u) members.push_back((int)i);
+    std::sort(members.begin(), members.end());
+    emit_ew_group(members);
+    plan_.n_fused_groups++;
+    return;
+  }
+  (void)n;
+  emit_node_kernel(u);
+}
+
+void Planner::emit_all() {
+  const int N = (int)g_.nodes.size();
+  // unit of every kernel-producing node
+  std::vector<int> unit(N, -1);
+  for (int i = 0; i < N; ++i) {
+    if (!live_[i]) continue;
+    if (loc_[i].kind == Loc::EW) unit[i] = find(i);
+    else if (loc_[i].kind == Loc::BUF && g_.nodes[i].op != Op::Param && g_.nodes[i].op != Op::Constant) unit[i] = i;
+  }
+  std::map<int, std::set<int>> deps, rdeps;
+  std::set<int> units;
+  for (int i = 0; i < N; ++i) {
+    if (unit[i] < 0) continue;
+    units.insert(unit[i]);
+    for (int o : g_.nodes[i].in) {
+      if (is_splat(o)) continue;
+      int r = view_root(o);
+      if (unit[r] >= 0 && unit[r] != unit[i]) {
+        deps[unit[i]].insert(unit[r]);
+        rdeps[unit[r]].insert(unit[i]);
+      }
+    }
+  }
+  std::map<int, int> indeg;
+  std::map<int, int> umin;
+  for (int i = 0; i < N; ++i)
+    if (unit[i] >= 0 && !umin.count(unit[i])) umin[unit[i]] = i;
+  std::priority_queue<std::pair<int, int>, std::vector<std::pair<int, int>>, std::greater<>> q;
+  for (int u : units) {
+    indeg[u] = (int)deps[u].size();
+    if (indeg[u] == 0) q.push({umin[u], u});
+  }
+  size_t done = 0;
+  while (!q.empty()) {
+    int u = q.top().second;
+    q.pop();
+    emit_unit(u);
+    done++;
+    for (int v : rdeps[u])
+      if (--indeg[v] == 0) q.push({umin[v], v});
+  }
+  if (done != units.size()) fail(E_INTERNAL, "planner produced a cyclic schedule");
+}
+
+void Planner::allocate_arena() {
+  // greedy interval allocation, first fit over active blocks sorted by offset
+  const int T = (int)tmp_bytes_.size();
+  std::vector<int> order(T);
+  for (int i = 0; i < T; ++i) order[i] = i;
+  std::sort(order.begin(), order.end(), [&](int a, int b) {
+    return tmp_first_[a] != tmp_first_[b] ? tmp_first_[a] < tmp_first_[b] : a < b;
+  });
+  std::vector<int64_t> off(T, 0);
+  std::multimap<int64_t, int> active;  // offset -> buffer
+  int64_t peak = 0;
+  for (int b : order) {
+    for (auto it = active.begin(); it != active.end();) {
+      if (tmp_last_[it->second] < tmp_first_[b]) it = active.erase(it);
+      else ++it;
+    }
+    int64_t sz = (tmp_bytes_[b] + 255) & ~int64_t(255);
+    int64_t cand = 0;
+    for (auto& kv : active) {
+      int64_t s = kv.first, e = kv.first + ((tmp_bytes_[kv.second] + 255) & ~int64_t(255));
+      if (cand + sz <= s) break;
+      cand = std::max(cand, e);
+    }
+    off[b] = cand;
+    active.insert({cand, b});
+    peak = std::max(peak, cand + sz);
+  }
+  plan_.arena_bytes = peak;
+  plan_.tmp_offsets = off;
+}
+
+void Planner::run() {
+  const int N = (int)g_.nodes.size();
+  P_ = (int)g_.params.size();
+  O_ = (int)g_.outputs.size();
+  plan_.name = g_.name;
+  plan_.n_nodes = N;
+  for (int p : g_.params) plan_.params.push_back({g_.nodes[p].dt, g_.nodes[p].shape});
+  for (int o : g_.outputs) plan_.outs.push_back({g_.nodes[o].dt, g_.nodes[o].shape});
+  plan_.out_alias_param.assign(O_, -1);
+  users_.assign(N, {});
+  for (int i = 0; i < N; ++i)
+    for (int x : g_.nodes[i].in) users_[x].push_back(i);
+  live_.assign(N, 0);
+  std::vector<int> stack(g_.outputs.begin(), g_.outputs.end());
+  while (!stack.empty()) {
+    int x = stack.back();
+    stack.pop_back();
+    if (live_[x]) continue;
+    live_[x] = 1;
+    for (int y : g_.nodes[x].in) stack.push_back(y);
+  }
+  for (int i = 0; i < N; ++i) plan_.n_live += live_[i];
+  mat_slot_.assign(N, -1);
+  out_claim_.assign(N, -1);
+  classify();
+  // outputs produced by a kernel are written straight into the result buffer
+  for (int k = 0; k < O_; ++k) {
+    int n = g_.outputs[k];
+    if (out_claim_[n] >= 0) continue;
+    if ((loc_[n].kind == Loc::BUF && g_.nodes[n].op != Op::Param && g_.nodes[n].op != Op::Constant) ||
+        loc_[n].kind == Loc::EW)
+      out_claim_[n] = k;
+  }
+  group_elementwise();
+  decide_materialisation();
+  emit_all();
+  emit_outputs();
+  allocate_arena();
+}
+
+}  // namespace
+
+std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt) {
+  auto plan = std::make_unique<Plan>();
+  Planner p(g, opt, *plan);
+  p.run();
+  return plan;
+}
+
+}  // namespace cljxla

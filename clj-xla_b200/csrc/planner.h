@@ -1,0 +1,62 @@
+// Compiles a parsed graph into a launch plan for the B200.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "ir.h"
+#include "kernels.h"
+
+namespace cljxla {
+
+enum KernelKind : int {
+  K_EW = 0, K_REDUCE, K_COPY, K_GATHER, K_DUS, K_GEMM,
+  K_GEMV, K_ATTN_DECODE, K_ATTN_COMBINE, K_ROWNORM, K_GEMM_TC,
+  K_NUM_KINDS
+};
+const char* kernel_kind_name(int k);
+
+struct Launch {
+  int kind = 0;
+  std::vector<uint8_t> blob;  // the kernel's POD parameter block
+  std::string label;          // for profiling: which graph values it produces
+  int64_t algo_bytes = 0;     // algorithmic HBM bytes (roofline accounting)
+  int64_t algo_flops = 0;
+};
+
+struct TensorSpec {
+  DT dt;
+  std::vector<int64_t> shape;
+  int64_t bytes() const { return numel(shape) * (int64_t)dt_size(dt); }
+};
+
+struct PlanOptions {
+  bool fuse = true;          // elementwise fusion (off: one kernel per op, for debugging)
+  bool fast_kernels = true;  // specialised GEMV / attention / tcgen05 paths
+  bool kv_in_place = false;  // dynamic_update_slice results alias their operand storage
+};
+
+struct Plan {
+  std::string name;
+  std::vector<TensorSpec> params, outs;
+  std::vector<Launch> launches;
+  int64_t arena_bytes = 0;
+  std::vector<uint8_t> const_blob;  // uploaded once; DPtr slot = const_slot()
+  // outs[i] may alias param alias_param[i] (in-place dynamic_update_slice), else -1
+  std::vector<int> out_alias_param;
+  int n_nodes = 0, n_live = 0, n_fused_groups = 0;
+  std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
+  // argument table layout: [params][outputs][constant blob][scratch buffers]
+  int const_slot() const { return (int)(params.size() + outs.size()); }
+  int tmp_slot0() const { return const_slot() + 1; }
+  int argtab_size() const { return tmp_slot0() + (int)tmp_offsets.size(); }
+};
+
+std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
+
+// Dispatches one launch record (argtab: device pointer of the argument table).
+void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);
+void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);
+
+}  // namespace cljxla

@@ -1,0 +1,72 @@
+/*
+ * cljxla_b200.h - C ABI of libcljxla_b200.so, the B200 (sm_100a) executor
+ * that clj-xla loads in place of its PJRT CPU plugin.
+ *
+ * The boundary is the PJRT C API.  clj-xla's host binds exactly one symbol,
+ * GetPjrtApi (src/clj_xla/pjrt.clj:201-206 looks it up, :207 reads 984 bytes
+ * of the returned table), and then calls these table slots: Error_Destroy /
+ * Error_Message (pjrt.clj:63-82), Plugin_Initialize (:211-215),
+ * Plugin_Attributes (:116-146), Event_Await / Event_Destroy (:420-433,
+ * :508-522, :548-562), Client_Create (:261-275), Client_PlatformName
+ * (:277-291), Client_AddressableDevices (:293-308), Client_Compile with format
+ * "mlir" (:310-340), Client_BufferFromHostBuffer (:342-434),
+ * LoadedExecutable_Execute (:454-525), Buffer_Destroy (:436-452) and
+ * Buffer_ToHostBuffer (:527-611).  Struct layouts: pjrt_abi.h.
+ *
+ * The cljxla_b200_* functions are additions with no counterpart in the
+ * reference; they expose counters and profiling for tests and benchmarks.
+ */
+#ifndef CLJXLA_B200_H_
+#define CLJXLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "pjrt_abi.h"
+
+#if defined(__GNUC__)
+#define CLJXLA_EXPORT __attribute__((visibility("default")))
+#else
+#define CLJXLA_EXPORT
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Replaces the plugin entry point of xla_cpu_pjrt / jax_cuda12_pjrt that
+ * clj-xla resolves at pjrt.clj:201-206. */
+CLJXLA_EXPORT const PJRT_Api* GetPjrtApi(void);
+
+/* Number of device kernels launched by executions so far (all executables). */
+CLJXLA_EXPORT int64_t cljxla_b200_kernel_launches(void);
+
+/* Number of LoadedExecutable_Execute calls completed so far. */
+CLJXLA_EXPORT int64_t cljxla_b200_executions(void);
+
+/* Per-kernel CUDA-event timing of subsequent executions (eager launches). */
+CLJXLA_EXPORT void cljxla_b200_profile_enable(int on);
+
+/* Writes the accumulated profile as JSON into out[cap]; returns the size needed. */
+CLJXLA_EXPORT size_t cljxla_b200_profile_dump(char* out, size_t cap);
+
+/* info[0..n): launches, scratch bytes, graph nodes, live nodes, fused
+ * elementwise groups, constant bytes.  Returns 0 on success. */
+CLJXLA_EXPORT int cljxla_b200_plan_info(const PJRT_LoadedExecutable* exec, int64_t* info, int n);
+
+/* Parses and plans MLIR text on the host only (no device needed).  info as
+ * above; returns 0 or a PJRT_Error_Code with the message in err[errcap]. */
+CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, int64_t* info, int n, char* err,
+                                        size_t errcap);
+
+/* The cudaStream_t a client launches on (for event timing by the caller). */
+CLJXLA_EXPORT void* cljxla_b200_stream(const PJRT_Client* client);
+
+/* Device address backing a buffer. */
+CLJXLA_EXPORT void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* buffer);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLJXLA_B200_H_ */

@@ -312,7 +312,8 @@ class Interpreter:
             a = np.asarray(val)
             if dt == "bf16" and a.dtype == np.uint16:
                 a = bf16_bits_to_f32(a)
-            a = to_dtype(a, dt)
+            elif not (dt == "bf16" and a.dtype == np.float32):   # f32 arrays of bf16 values pass as-is
+                a = to_dtype(a, dt)
             if tuple(a.shape) != tuple(shape):
                 a = a.reshape(shape)
             env[pn] = a
@@ -469,8 +470,14 @@ class Interpreter:
         a, b = args
         lf = [i for i in range(a.ndim) if i not in lb and i not in lc]
         rf = [i for i in range(b.ndim) if i not in rb and i not in rc]
-        at = np.transpose(a, lb + lf + lc).astype(np.float32)
-        bt = np.transpose(b, rb + rc + rf).astype(np.float32)
+        if not lb and not rb and b.ndim == 2 and len(lc) == 1 and lc[0] == a.ndim - 1:
+            # plain linear layer: a[..., K] x b (a 2-D view, possibly transposed) - no copies
+            bt = np.asarray(b, np.float32)
+            bt = bt if rc[0] == 0 else bt.T
+            r = np.asarray(a, np.float32).reshape(-1, a.shape[-1]) @ bt
+            return to_dtype(r.reshape(shape), dt)
+        at = np.asarray(np.transpose(a, lb + lf + lc), np.float32)
+        bt = np.asarray(np.transpose(b, rb + rc + rf), np.float32)
         bsz = int(np.prod([a.shape[i] for i in lb])) if lb else 1
         m = int(np.prod([a.shape[i] for i in lf])) if lf else 1
         k = int(np.prod([a.shape[i] for i in lc])) if lc else 1

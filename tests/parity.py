@@ -1,0 +1,35 @@
+"""Comparison helpers shared by the parity tests.
+
+Tolerance form follows the reference's parity harness
+(src/clj_xla/test/parity.clj:36-49, ``|a - b| <= atol + rtol*|b|``) with
+atol = rtol * RMS(b) per tensor; rtol is 1e-4 for f32 and 2e-2 for bf16
+results, and index results are compared bit-exactly.
+"""
+import numpy as np
+
+from oracle import interp
+
+RTOL = {"f32": 1e-4, "bf16": 2e-2, "f16": 1e-2}
+
+
+def as_f32(a: np.ndarray, dt: str) -> np.ndarray:
+    if dt == "bf16":
+        return interp.bf16_bits_to_f32(a) if a.dtype == np.uint16 else a.astype(np.float32)
+    return np.asarray(a, np.float32)
+
+
+def close(got, want, dt, rtol=None, atol_scale=1.0):
+    """Returns (ok, worst_excess, max_abs_err)."""
+    if dt in ("i32", "i1", "i8"):
+        ok = np.array_equal(np.asarray(got).astype(np.int64), np.asarray(want).astype(np.int64))
+        return ok, 0.0, 0.0
+    g = as_f32(np.asarray(got), dt).astype(np.float64)
+    w = as_f32(np.asarray(want), dt).astype(np.float64)
+    rt = RTOL.get(dt, 1e-4) if rtol is None else rtol
+    rms = float(np.sqrt(np.mean(np.square(w)))) if w.size else 0.0
+    atol = rt * rms * atol_scale
+    err = np.abs(g - w)
+    allowed = atol + rt * np.abs(w)
+    ok = bool(np.all(err <= allowed)) and not np.isnan(g).any()
+    excess = float(np.max(err - allowed)) if err.size else 0.0
+    return ok, excess, float(err.max()) if err.size else 0.0
