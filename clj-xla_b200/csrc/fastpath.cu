@@ -12,3 +12,10 @@ void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
 }
 
 }  // namespace cljxla
+
+namespace cljxla {
+void verify_fast_launch(const Plan& p, const Launch& l) {
+  (void)p;
+  fail(E_INTERNAL, std::string("no bounds verifier for kernel kind ") + kernel_kind_name(l.kind));
+}
+}  // namespace cljxla

@@ -927,6 +927,7 @@ void Planner::allocate_arena() {
   }
   plan_.arena_bytes = peak;
   plan_.tmp_offsets = off;
+  plan_.tmp_bytes = tmp_bytes_;
 }
 
 void Planner::run() {
@@ -967,6 +968,7 @@ void Planner::run() {
   emit_all();
   emit_outputs();
   allocate_arena();
+  verify_plan(plan_);
 }
 
 }  // namespace

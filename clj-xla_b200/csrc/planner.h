@@ -47,6 +47,7 @@ struct Plan {
   std::vector<int> out_alias_param;
   int n_nodes = 0, n_live = 0, n_fused_groups = 0;
   std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
+  std::vector<int64_t> tmp_bytes;    // size of each scratch buffer
   // argument table layout: [params][outputs][constant blob][scratch buffers]
   int const_slot() const { return (int)(params.size() + outs.size()); }
   int tmp_slot0() const { return const_slot() + 1; }
@@ -58,5 +59,9 @@ std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
 // Dispatches one launch record (argtab: device pointer of the argument table).
 void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);
 void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);
+
+// Host-side bounds verification of every launch (throws INTERNAL on a violation).
+void verify_plan(const Plan& p);
+void verify_fast_launch(const Plan& p, const Launch& l);
 
 }  // namespace cljxla

@@ -1,0 +1,129 @@
+// Static bounds verification of a launch plan.  Every buffer a kernel can
+// touch is described by a DPtr plus a strided extent; this checks, on the
+// host and before anything runs, that each access region lies inside the
+// buffer its argument-table slot will point at.  A planner bug therefore
+// surfaces as an INTERNAL compile error rather than an out-of-bounds access
+// on the device.
+#include "planner.h"
+
+namespace cljxla {
+namespace {
+
+size_t esz(int dt) { return dt_size((DT)dt); }
+
+struct Checker {
+  const Plan& p;
+  const Launch* cur = nullptr;
+  int64_t slot_bytes(int slot) const {
+    int P = (int)p.params.size(), O = (int)p.outs.size();
+    if (slot < 0) return -1;
+    if (slot < P) return p.params[slot].bytes();
+    if (slot < P + O) return p.outs[slot - P].bytes();
+    if (slot == P + O) return (int64_t)p.const_blob.size();
+    int b = slot - (P + O + 1);
+    if (b < (int)p.tmp_bytes.size()) return p.tmp_bytes[b];
+    return -1;
+  }
+  void region(const DPtr& d, int64_t bytes, const char* what) const {
+    if (bytes <= 0) return;
+    int64_t cap = slot_bytes(d.slot);
+    if (cap < 0 || d.off < 0 || d.off + bytes > cap)
+      fail(E_INTERNAL, std::string("plan bounds check failed: ") + kernel_kind_name(cur->kind) + " '" +
+                           cur->label + "' " + what + " slot " + std::to_string(d.slot) + " range [" +
+                           std::to_string(d.off) + ", " + std::to_string(d.off + bytes) + ") exceeds buffer of " +
+                           std::to_string(cap) + " bytes");
+  }
+  void view(const TView& v, const char* what) const {
+    int64_t hi = 0;
+    for (int i = 0; i < v.rank; ++i) {
+      if (v.shape[i] == 0) return;
+      if (v.stride[i] < 0) fail(E_INTERNAL, "negative stride in plan");
+      hi += (v.shape[i] - 1) * v.stride[i];
+    }
+    region(v.p, (hi + 1) * (int64_t)esz(v.dt), what);
+  }
+  void strided(const DPtr& d, int dt, std::initializer_list<std::pair<int64_t, int64_t>> dims, const char* what) const {
+    int64_t hi = 0;
+    for (auto& ds : dims) {
+      if (ds.first == 0) return;
+      if (ds.second < 0) fail(E_INTERNAL, "negative stride in plan");
+      hi += (ds.first - 1) * ds.second;
+    }
+    region(d, (hi + 1) * (int64_t)esz(dt), what);
+  }
+};
+
+}  // namespace
+
+void verify_plan(const Plan& p) {
+  Checker c{p};
+  for (const Launch& l : p.launches) {
+    c.cur = &l;
+    const void* b = l.blob.data();
+    switch (l.kind) {
+      case K_EW: {
+        const EwParams& e = *(const EwParams*)b;
+        if (e.n == 0) break;
+        for (int i = 0; i < e.nin; ++i) {
+          TView v{};
+          v.p = e.in[i].p;
+          v.dt = e.in[i].dt;
+          v.rank = e.rank;
+          for (int d = 0; d < e.rank; ++d) { v.shape[d] = e.dims[d]; v.stride[d] = e.in[i].stride[d]; }
+          c.view(v, "input");
+        }
+        for (int o = 0; o < e.nout; ++o) c.region(e.out[o].p, e.n * (int64_t)esz(e.out[o].dt), "output");
+        for (int k = 0; k < e.ncode; ++k) {
+          const EwInstr& I = e.code[k];
+          if (I.dst >= EW_NREG || I.a >= EW_NREG || I.b >= EW_NREG || I.c >= EW_NREG)
+            fail(E_INTERNAL, "register index out of range");
+          if (I.op == EW_LOAD && I.aux >= e.nin) fail(E_INTERNAL, "load of a missing input");
+          if (I.op == EW_IOTA && I.aux >= e.rank) fail(E_INTERNAL, "iota dimension out of range");
+        }
+        break;
+      }
+      case K_REDUCE: {
+        const ReduceParams& r = *(const ReduceParams*)b;
+        c.view(r.in, "input");
+        c.region(r.out, r.n_out * (int64_t)esz(r.out_dt), "output");
+        break;
+      }
+      case K_COPY: {
+        const CopyParams& r = *(const CopyParams*)b;
+        c.view(r.src, "source");
+        c.view(r.dst, "destination");
+        break;
+      }
+      case K_GATHER: {
+        const GatherParams& g = *(const GatherParams*)b;
+        c.strided(g.table, g.table_dt, {{g.rows_table, g.table_row_stride}, {g.row_len, 1}}, "table");
+        c.view(g.idx, "indices");
+        c.region(g.out, g.n_rows * g.row_len * (int64_t)esz(g.table_dt), "output");
+        break;
+      }
+      case K_DUS: {
+        const DusParams& d = *(const DusParams*)b;
+        c.view(d.operand, "operand");
+        c.view(d.update, "update");
+        c.region(d.out, d.n * (int64_t)esz(d.dt), "output");
+        for (int i = 0; i < d.rank; ++i) {
+          if (d.upd_shape[i] > d.out_shape[i]) fail(E_INVALID, "dynamic_update_slice update larger than operand");
+          if (d.start_is_ptr[i]) c.region(d.start_ptr[i], (int64_t)esz(d.start_dt[i]), "start index");
+        }
+        break;
+      }
+      case K_GEMM: {
+        const GemmParams& g = *(const GemmParams*)b;
+        c.strided(g.a, g.a_dt, {{g.batch, g.a_sb}, {g.M, g.a_sm}, {g.K, g.a_sk}}, "lhs");
+        c.strided(g.b, g.b_dt, {{g.batch, g.b_sb}, {g.K, g.b_sk}, {g.N, g.b_sn}}, "rhs");
+        c.region(g.c, g.batch * g.M * g.N * (int64_t)esz(g.c_dt), "result");
+        break;
+      }
+      default:
+        verify_fast_launch(p, l);
+        break;
+    }
+  }
+}
+
+}  // namespace cljxla
