@@ -1,0 +1,62 @@
+// Parameter blocks and entry points of the specialised kernels (decode GEMV,
+// fused decode attention, ...), selected by the planner where a graph
+// pattern allows and verified by the same host-side bounds checker.
+#pragma once
+
+#include <functional>
+
+#include "planner.h"
+
+namespace cljxla {
+
+struct GemvParams {
+  DPtr x, w, y;
+  int32_t x_dt, w_dt, y_dt, warps_per_row;
+  int64_t M, N, K;
+  int64_t x_sm, y_sm;  // row strides (elements) of x and y
+};
+
+using RegionFn = std::function<void(const DPtr&, int64_t, const char*)>;
+
+void launch_gemv(const GemvParams& p, const uint64_t* argtab, cudaStream_t s);
+bool make_gemv(const GemmParams& g, Launch& out);
+void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region);
+void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& region);
+
+}  // namespace cljxla
+
+namespace cljxla {
+
+// Fused attention (k_attention.cu).  q [B, nq, Sq, hd], k / v [B, nkv, T, hd],
+// mask [B, nq, Sq, T] (broadcast view of the additive mask), out dense
+// [B, nq, Sq, hd].  The printed score chain (scale / softcap, with its
+// roundings) runs as a register program on each score.
+struct AttnParams {
+  TView q, k, v, mask;
+  DPtr out, part;
+  int32_t B, nq, nkv, Sq, T, hd, group, splits, qtile;
+  int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
+  int32_t nchain, chain_out;
+  float mask_skip;
+  EwInstr chain[12];
+};
+
+void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
+void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
+void verify_attention(const Launch& l, const RegionFn& region);
+
+// Pattern match of the printed attention block (attention.clj:343-365).
+struct AttnMatch {
+  int d2 = -1;          // probs . V dot (the node the fused kernel produces)
+  int d1 = -1;          // q . K^T dot
+  int q = -1, kc = -1, vc = -1;  // q [B,nq,Sq,hd]; K/V caches [B,nkv,T,hd] (before the GQA broadcast)
+  int mask = -1;        // the mask operand of the add ([B,nq,Sq,T] view)
+  int m = -1, sub = -1, exp = -1, div = -1;
+  std::vector<int> chain;  // elementwise nodes from d1 to the mask add (exclusive), in order
+  std::vector<int> absorbed;  // every node the fused kernel replaces (except d2)
+  int group = 1;
+};
+std::vector<AttnMatch> match_attention(const Graph& g, const std::vector<char>& live,
+                                       const std::vector<std::vector<int>>& users);
+
+}  // namespace cljxla

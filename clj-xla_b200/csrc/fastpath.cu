@@ -1,21 +1,23 @@
-// Dispatch for the specialised kernels (decode GEMV, fused attention, row
-// norms, tcgen05 GEMM).  Each kernel family lives in its own file and
-// registers a launcher here.
-#include "planner.h"
+// Dispatch and bounds verification for the specialised kernels.
+#include "fast_kernels.h"
 
 namespace cljxla {
 
 void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
-  (void)argtab;
-  (void)s;
-  fail(E_INTERNAL, std::string("no launcher for kernel kind ") + kernel_kind_name(l.kind));
+  switch (l.kind) {
+    case K_GEMV: launch_gemv(*(const GemvParams*)l.blob.data(), argtab, s); break;
+    case K_ATTN_DECODE: launch_attention(*(const AttnParams*)l.blob.data(), argtab, s); break;
+    case K_ATTN_COMBINE: launch_attention_combine(*(const AttnParams*)l.blob.data(), argtab, s); break;
+    default: fail(E_INTERNAL, std::string("no launcher for kernel kind ") + kernel_kind_name(l.kind));
+  }
 }
 
-}  // namespace cljxla
-
-namespace cljxla {
-void verify_fast_launch(const Plan& p, const Launch& l) {
-  (void)p;
-  fail(E_INTERNAL, std::string("no bounds verifier for kernel kind ") + kernel_kind_name(l.kind));
+void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& region) {
+  switch (l.kind) {
+    case K_GEMV: verify_gemv(p, l, region); break;
+    case K_ATTN_DECODE: case K_ATTN_COMBINE: verify_attention(l, region); break;
+    default: fail(E_INTERNAL, std::string("no bounds verifier for kernel kind ") + kernel_kind_name(l.kind));
+  }
 }
+
 }  // namespace cljxla

@@ -1,0 +1,331 @@
+// Fused grouped-query attention over a KV cache (flash-decoding).
+//
+// Replaces the printed attention block of attention.clj:343-365
+//   scores = dot_general(q, reshape(broadcast_in_dim(K)))      (GQA broadcast)
+//   s      = <scale / softcap chain>(scores)                    (printed as bf16 ops)
+//   m      = s + mask ; p = exp(m - max m) / sum exp(...)       (f32 softmax)
+//   out    = dot_general(p, reshape(broadcast_in_dim(V)))
+// with one kernel that reads each K/V row once per KV head (all query heads of
+// the group share it), keeps the softmax online in registers, and never
+// materialises the broadcast K/V, the score matrix or the probabilities.
+//
+// Grid: (position splits, query tiles, batch * kv heads); 4 warps per CTA,
+// each warp walks positions of the CTA's chunk; per position a lane owns
+// hd/32 consecutive elements of the K and V rows.  Partial (max, sum, acc)
+// triples are merged across warps in shared memory and, when the positions
+// are split across CTAs, across CTAs by attn_combine.
+//
+// Positions whose additive mask is at or below `mask_skip` for every query
+// row of the CTA are skipped without loading K/V.  This is exact for the
+// causal / sliding-window masks the reference prints (-10000,
+// attention.clj:208,224): such a position's softmax weight
+// exp(s - 10000 - max) underflows to exactly 0 in f32 whenever the unmasked
+// scores lie within ~4900 of each other.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "fast_kernels.h"
+
+namespace cljxla {
+namespace {
+
+__device__ __forceinline__ float rnd_dt(float v, int dt) {
+  if (dt == KDT_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == KDT_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+__device__ __forceinline__ float ld_any(const char* base, int64_t i, int dt) {
+  if (dt == KDT_F32) return ((const float*)base)[i];
+  if (dt == KDT_BF16) return __uint_as_float((uint32_t)((const uint16_t*)base)[i] << 16);
+  return __half2float(((const __half*)base)[i]);
+}
+
+// HPL consecutive K/V elements of one row as f32
+template <typename KT, int HPL>
+__device__ __forceinline__ void load_row(const KT* p, float* o);
+
+template <>
+__device__ __forceinline__ void load_row<uint16_t, 8>(const uint16_t* p, float* o) {
+  uint4 v = *(const uint4*)p;
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { o[2 * i] = __uint_as_float(w[i] << 16); o[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u); }
+}
+template <>
+__device__ __forceinline__ void load_row<uint16_t, 4>(const uint16_t* p, float* o) {
+  uint2 v = *(const uint2*)p;
+  o[0] = __uint_as_float(v.x << 16); o[1] = __uint_as_float(v.x & 0xffff0000u);
+  o[2] = __uint_as_float(v.y << 16); o[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void load_row<uint16_t, 2>(const uint16_t* p, float* o) {
+  uint32_t v = *(const uint32_t*)p;
+  o[0] = __uint_as_float(v << 16); o[1] = __uint_as_float(v & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void load_row<uint16_t, 1>(const uint16_t* p, float* o) {
+  o[0] = __uint_as_float((uint32_t)p[0] << 16);
+}
+template <int HPL>
+__device__ __forceinline__ void load_row_f32(const float* p, float* o) {
+#pragma unroll
+  for (int i = 0; i < HPL; ++i) o[i] = p[i];
+}
+template <>
+__device__ __forceinline__ void load_row<float, 1>(const float* p, float* o) { load_row_f32<1>(p, o); }
+template <>
+__device__ __forceinline__ void load_row<float, 2>(const float* p, float* o) {
+  float2 v = *(const float2*)p;
+  o[0] = v.x; o[1] = v.y;
+}
+template <>
+__device__ __forceinline__ void load_row<float, 4>(const float* p, float* o) {
+  float4 v = *(const float4*)p;
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+template <>
+__device__ __forceinline__ void load_row<float, 8>(const float* p, float* o) {
+  float4 a = *(const float4*)p, b = *(const float4*)(p + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
+// the printed scale / softcap chain applied to one score (register 0 holds it)
+__device__ float run_chain(const AttnParams& P, float s) {
+  float R[16];
+  R[0] = s;
+  for (int pc = 0; pc < P.nchain; ++pc) {
+    const EwInstr& I = P.chain[pc];
+    float a = R[I.a], b = R[I.b], z;
+    switch (I.op) {
+      case EW_IMM: z = I.fimm; break;
+      case EW_ADD: z = a + b; break;
+      case EW_SUB: z = a - b; break;
+      case EW_MUL: z = a * b; break;
+      case EW_DIV: z = a / b; break;
+      case EW_MAX: z = fmaxf(a, b); break;
+      case EW_MIN: z = fminf(a, b); break;
+      case EW_TANH: z = tanhf(a); break;
+      case EW_NEG: z = -a; break;
+      case EW_CONVERT: z = a; break;
+      default: z = a; break;
+    }
+    R[I.dst] = rnd_dt(z, I.dt);
+  }
+  return R[P.chain_out];
+}
+
+constexpr int NW = 4;
+
+template <typename KT, int HPL, int NQV>
+__global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ AttnParams P,
+                                                      const uint64_t* __restrict__ argtab) {
+  constexpr int HD = HPL * 32;
+  __shared__ float qs[NQV][HD];
+  __shared__ float wm[NW][NQV], wl[NW][NQV];
+  __shared__ float wacc[NW][NQV][HD];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bk = blockIdx.z;
+  const int b = bk / P.nkv, kh = bk % P.nkv;
+  const int i0 = blockIdx.y * P.qtile;
+  const int nrows = min(P.qtile, P.Sq - i0);
+  const int nqv = nrows * P.group;  // active query vectors: r = qi * group + gi
+  const int split = blockIdx.x;
+  const int64_t chunk = (P.T + P.splits - 1) / P.splits;
+  const int64_t t0 = split * chunk, t1 = min((int64_t)P.T, t0 + chunk);
+  const char* qb = dres(P.q.p, argtab);
+  const KT* kb = (const KT*)dres(P.k.p, argtab);
+  const KT* vb = (const KT*)dres(P.v.p, argtab);
+  const char* mb = dres(P.mask.p, argtab);
+
+  // query vectors of this CTA -> shared (f32)
+  for (int e = threadIdx.x; e < NQV * HD; e += NW * 32) {
+    int r = e / HD, d = e % HD;
+    float val = 0.f;
+    if (r < nqv) {
+      int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+      val = ld_any(qb, b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2] + d * P.q.stride[3], P.q.dt);
+    }
+    qs[r][d] = val;
+  }
+  __syncthreads();
+
+  float m[NQV], l[NQV], acc[NQV][HPL];
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < HPL; ++e) acc[r][e] = 0.f;
+  }
+  const int64_t kbase = b * P.k.stride[0] + kh * P.k.stride[1] + lane * HPL;
+  const int64_t vbase = b * P.v.stride[0] + kh * P.v.stride[1] + lane * HPL;
+  for (int64_t j = t0 + warp; j < t1; j += NW) {
+    // mask values for every active query vector
+    float mk[NQV];
+    bool any = false;
+#pragma unroll
+    for (int r = 0; r < NQV; ++r) {
+      mk[r] = -INFINITY;
+      if (r < nqv) {
+        int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+        mk[r] = ld_any(mb, b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2] + j * P.mask.stride[3],
+                       P.mask.dt);
+        any |= mk[r] > P.mask_skip;
+      }
+    }
+    if (!any) continue;
+    float kr[HPL], vr[HPL];
+    load_row<KT, HPL>(kb + kbase + j * P.k.stride[2], kr);
+    load_row<KT, HPL>(vb + vbase + j * P.v.stride[2], vr);
+#pragma unroll
+    for (int r = 0; r < NQV; ++r) {
+      if (r >= nqv) break;
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < HPL; ++e) s = fmaf(qs[r][lane * HPL + e], kr[e], s);
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) s += __shfl_xor_sync(0xffffffffu, s, sh);
+      s = rnd_dt(s, P.dt_d1);
+      s = run_chain(P, s);
+      float mv = rnd_dt(s + mk[r], P.dt_m);
+      if (mv > m[r]) {
+        float sc = __expf(m[r] - mv);  // m[r] = -inf first: 0
+        if (m[r] == -INFINITY) sc = 0.f;
+        l[r] *= sc;
+#pragma unroll
+        for (int e = 0; e < HPL; ++e) acc[r][e] *= sc;
+        m[r] = mv;
+      }
+      float p = rnd_dt(expf(rnd_dt(mv - m[r], P.dt_sub)), P.dt_exp);
+      l[r] += p;
+#pragma unroll
+      for (int e = 0; e < HPL; ++e) acc[r][e] = fmaf(p, vr[e], acc[r][e]);
+    }
+  }
+  // merge warps
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
+#pragma unroll
+    for (int e = 0; e < HPL; ++e) wacc[warp][r][lane * HPL + e] = acc[r][e];
+  }
+  __syncthreads();
+  const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
+  for (int e = threadIdx.x; e < nqv * HD; e += NW * 32) {
+    int r = e / HD, d = e % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][r]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < NW; ++w) {
+        float sc = wm[w][r] == -INFINITY ? 0.f : __expf(wm[w][r] - M);
+        L += wl[w][r] * sc;
+        A += wacc[w][r][d] * sc;
+      }
+    }
+    int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    int64_t row = ((int64_t)b * P.nq + h) * P.Sq + qi;
+    if (P.splits == 1) {
+      float o = L > 0.f ? A / L : 0.f;
+      char* ob = dres(P.out, argtab);
+      if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = o;
+      else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(o);
+    } else {
+      float* part = (float*)dres(P.part, argtab) + ((int64_t)split * rows_total + row) * (HD + 2);
+      part[2 + d] = A;
+      if (d == 0) { part[0] = M; part[1] = L; }
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const uint64_t* __restrict__ argtab) {
+  const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
+  const int HD = P.hd;
+  const float* part = (const float*)dres(P.part, argtab);
+  char* ob = dres(P.out, argtab);
+  for (int64_t row = blockIdx.x; row < rows_total; row += gridDim.x) {
+    float M = -INFINITY;
+    for (int s = 0; s < P.splits; ++s) M = fmaxf(M, part[((int64_t)s * rows_total + row) * (HD + 2)]);
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+      float L = 0.f, A = 0.f;
+      if (M != -INFINITY) {
+        for (int s = 0; s < P.splits; ++s) {
+          const float* pp = part + ((int64_t)s * rows_total + row) * (HD + 2);
+          if (pp[0] == -INFINITY) continue;
+          float sc = __expf(pp[0] - M);
+          L += pp[1] * sc;
+          A += pp[2 + d] * sc;
+        }
+      }
+      float o = L > 0.f ? A / L : 0.f;
+      if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = o;
+      else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(o);
+    }
+  }
+}
+
+template <typename KT, int HPL>
+void launch_hpl(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  dim3 grid((unsigned)p.splits, (unsigned)((p.Sq + p.qtile - 1) / p.qtile), (unsigned)(p.B * p.nkv));
+  int nqv = p.qtile * p.group;
+  if (nqv <= 1) attn_kernel<KT, HPL, 1><<<grid, NW * 32, 0, s>>>(p, argtab);
+  else if (nqv <= 2) attn_kernel<KT, HPL, 2><<<grid, NW * 32, 0, s>>>(p, argtab);
+  else if (nqv <= 4) attn_kernel<KT, HPL, 4><<<grid, NW * 32, 0, s>>>(p, argtab);
+  else attn_kernel<KT, HPL, 8><<<grid, NW * 32, 0, s>>>(p, argtab);
+}
+
+}  // namespace
+
+void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.k_dt == KDT_BF16) {
+    switch (p.hd) {
+      case 32: launch_hpl<uint16_t, 1>(p, argtab, s); break;
+      case 64: launch_hpl<uint16_t, 2>(p, argtab, s); break;
+      case 128: launch_hpl<uint16_t, 4>(p, argtab, s); break;
+      case 256: launch_hpl<uint16_t, 8>(p, argtab, s); break;
+    }
+  } else {
+    switch (p.hd) {
+      case 32: launch_hpl<float, 1>(p, argtab, s); break;
+      case 64: launch_hpl<float, 2>(p, argtab, s); break;
+      case 128: launch_hpl<float, 4>(p, argtab, s); break;
+      case 256: launch_hpl<float, 8>(p, argtab, s); break;
+    }
+  }
+}
+
+void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  int64_t rows = (int64_t)p.B * p.nq * p.Sq;
+  int g = (int)(rows < 65535 ? rows : 65535);
+  attn_combine_kernel<<<g, p.hd < 256 ? p.hd : 256, 0, s>>>(p, argtab);
+}
+
+void verify_attention(const Launch& l, const RegionFn& region) {
+  const AttnParams& p = *(const AttnParams*)l.blob.data();
+  auto vext = [&](const TView& v, const char* what) {
+    int64_t hi = 0;
+    for (int i = 0; i < v.rank; ++i) {
+      if (v.shape[i] == 0) return;
+      if (v.stride[i] < 0) fail(E_INTERNAL, "negative stride in attention view");
+      hi += (v.shape[i] - 1) * v.stride[i];
+    }
+    region(v.p, (hi + 1) * (int64_t)dt_size((DT)v.dt), what);
+  };
+  vext(p.q, "q");
+  vext(p.k, "k");
+  vext(p.v, "v");
+  vext(p.mask, "mask");
+  int64_t rows = (int64_t)p.B * p.nq * p.Sq;
+  region(p.out, rows * p.hd * (int64_t)dt_size((DT)p.out_dt), "out");
+  if (p.splits > 1) region(p.part, (int64_t)p.splits * rows * (p.hd + 2) * 4, "partials");
+  if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||
+      p.k.shape[1] != p.nkv || p.k.shape[2] != p.T || p.k.shape[3] != p.hd || p.v.shape[2] != p.T ||
+      p.mask.shape[3] != p.T || p.k.stride[3] != 1 || p.v.stride[3] != 1 || p.nq != p.nkv * p.group)
+    fail(E_INTERNAL, "attention view shapes inconsistent");
+  if (p.nchain > 12 || p.chain_out >= 16) fail(E_INTERNAL, "attention chain too long");
+  for (int i = 0; i < p.nchain; ++i)
+    if (p.chain[i].dst >= 16 || p.chain[i].a >= 16 || p.chain[i].b >= 16) fail(E_INTERNAL, "attention chain register");
+}
+
+}  // namespace cljxla

@@ -1,0 +1,194 @@
+// Decode GEMV: y[m, n] = sum_k x[m, k] * W[n, k] for small M (decode batch).
+//
+// The weight matrix is the only large operand and is read exactly once, so
+// the kernel is HBM-bound: every lane streams 16-byte vectors of W with
+// no-allocate loads (four independent vectors in flight per lane), x stays in
+// L1, accumulation is f32, and each output is rounded once to the result type.
+// Rows are split across 1-8 warps (split-K inside the block) so that even
+// small projections put enough bytes in flight to cover HBM latency on all
+// 148 SMs.  Layout: W row-major [N, K] (the transposed-weight operand of
+// clj-xla's Gemma linear layers, gemma.clj:8-23, folded into the kernel).
+#include <cuda_bf16.h>
+
+#include "fast_kernels.h"
+
+namespace cljxla {
+namespace {
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// 8 consecutive x values (bf16 or f32) as f32
+template <typename XT>
+__device__ __forceinline__ void load_x8(const XT* x, float* o);
+template <>
+__device__ __forceinline__ void load_x8<uint16_t>(const uint16_t* x, float* o) {
+  uint4 v = *(const uint4*)x;
+  o[0] = bf_lo(v.x); o[1] = bf_hi(v.x); o[2] = bf_lo(v.y); o[3] = bf_hi(v.y);
+  o[4] = bf_lo(v.z); o[5] = bf_hi(v.z); o[6] = bf_lo(v.w); o[7] = bf_hi(v.w);
+}
+template <>
+__device__ __forceinline__ void load_x8<float>(const float* x, float* o) {
+  float4 a = *(const float4*)x, b = *(const float4*)(x + 4);
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+
+__device__ __forceinline__ float dot8(const uint4& w, const float* x) {
+  float s = bf_lo(w.x) * x[0];
+  s = fmaf(bf_hi(w.x), x[1], s);
+  s = fmaf(bf_lo(w.y), x[2], s);
+  s = fmaf(bf_hi(w.y), x[3], s);
+  s = fmaf(bf_lo(w.z), x[4], s);
+  s = fmaf(bf_hi(w.z), x[5], s);
+  s = fmaf(bf_lo(w.w), x[6], s);
+  s = fmaf(bf_hi(w.w), x[7], s);
+  return s;
+}
+
+__device__ __forceinline__ void store_out(char* y, int64_t i, int dt, float v) {
+  if (dt == KDT_F32) ((float*)y)[i] = v;
+  else ((__nv_bfloat16*)y)[i] = __float2bfloat16_rn(v);
+}
+
+template <int MT, typename XT>
+__global__ void __launch_bounds__(256) gemv_nt_bf16(const __grid_constant__ GemvParams P,
+                                                   const uint64_t* __restrict__ argtab) {
+  __shared__ float red[8][MT];
+  const uint16_t* W = (const uint16_t*)dres(P.w, argtab);
+  const XT* X = (const XT*)dres(P.x, argtab);
+  char* Y = dres(P.y, argtab);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wpr = P.warps_per_row;
+  const int rows_per_block = 8 / wpr;
+  const int64_t row = (int64_t)blockIdx.x * rows_per_block + warp / wpr;
+  const int part = warp % wpr;
+  const bool active = row < P.N;
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+  if (active) {
+    const int64_t kper = P.K / wpr;  // multiple of 8 (checked on the host)
+    const int64_t k0 = part * kper, k1 = (part == wpr - 1) ? P.K : k0 + kper;
+    const uint16_t* wrow = W + row * P.K;
+    int64_t k = k0 + lane * 8;
+    // main loop: 4 independent 16-byte weight vectors in flight per lane
+    for (; k + 3 * 256 < k1; k += 4 * 256) {
+      uint4 w0 = ld_stream(wrow + k), w1 = ld_stream(wrow + k + 256), w2 = ld_stream(wrow + k + 512),
+            w3 = ld_stream(wrow + k + 768);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float xv[8];
+        const XT* xr = X + m * P.x_sm;
+        load_x8<XT>(xr + k, xv);
+        float s = dot8(w0, xv);
+        load_x8<XT>(xr + k + 256, xv);
+        s += dot8(w1, xv);
+        load_x8<XT>(xr + k + 512, xv);
+        s += dot8(w2, xv);
+        load_x8<XT>(xr + k + 768, xv);
+        s += dot8(w3, xv);
+        acc[m] += s;
+      }
+    }
+    for (; k < k1; k += 256) {
+      uint4 w0 = ld_stream(wrow + k);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) {
+        float xv[8];
+        load_x8<XT>(X + m * P.x_sm + k, xv);
+        acc[m] += dot8(w0, xv);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], s);
+  if (wpr > 1) {
+    if (lane == 0)
+#pragma unroll
+      for (int m = 0; m < MT; ++m) red[warp][m] = acc[m];
+    __syncthreads();
+    if (part == 0 && lane == 0 && active) {
+      for (int q = 1; q < wpr; ++q)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) acc[m] += red[warp + q][m];
+    }
+  }
+  if (active && part == 0 && lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m) store_out(Y, m * P.y_sm + row, P.y_dt, acc[m]);
+  }
+}
+
+template <int MT>
+void launch_nt(const GemvParams& p, const uint64_t* argtab, cudaStream_t s) {
+  int rows_per_block = 8 / p.warps_per_row;
+  unsigned grid = (unsigned)((p.N + rows_per_block - 1) / rows_per_block);
+  if (p.x_dt == KDT_F32) gemv_nt_bf16<MT, float><<<grid, 256, 0, s>>>(p, argtab);
+  else gemv_nt_bf16<MT, uint16_t><<<grid, 256, 0, s>>>(p, argtab);
+}
+
+}  // namespace
+
+void launch_gemv(const GemvParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.N == 0) return;
+  switch (p.M) {
+    case 1: launch_nt<1>(p, argtab, s); break;
+    case 2: launch_nt<2>(p, argtab, s); break;
+    case 3: launch_nt<3>(p, argtab, s); break;
+    case 4: launch_nt<4>(p, argtab, s); break;
+    case 5: case 6: case 7: case 8: launch_nt<8>(p, argtab, s); break;
+    default: fail(E_INTERNAL, "gemv: unsupported M");
+  }
+}
+
+bool make_gemv(const GemmParams& g, Launch& out) {
+  // decode shapes only: one batch, few rows, bf16 weights laid out [N, K]
+  if (g.batch != 1 || g.M < 1 || g.M > 8 || g.b_dt != KDT_BF16) return false;
+  if (!(g.a_dt == KDT_BF16 || g.a_dt == KDT_F32) || !(g.c_dt == KDT_BF16 || g.c_dt == KDT_F32)) return false;
+  if (g.b_sk != 1 || g.b_sn != g.K || g.a_sk != 1) return false;
+  if (g.K % 8 != 0 || g.K < 256) return false;
+  if ((g.b.off % 16) != 0 || (g.a.off % 16) != 0) return false;
+  if (g.M > 1 && (g.a_sm % 8) != 0) return false;
+  if (g.M == 5 || g.M == 6 || g.M == 7) return false;  // keep the M=8 path exact-sized
+  GemvParams p{};
+  p.x = g.a;
+  p.w = g.b;
+  p.y = g.c;
+  p.x_dt = g.a_dt;
+  p.w_dt = g.b_dt;
+  p.y_dt = g.c_dt;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.x_sm = g.a_sm;
+  p.y_sm = g.N;
+  // enough warps in flight: split K across up to 8 warps per row
+  int wpr = 1;
+  while (wpr < 8 && g.N * wpr < 148 * 48 && (g.K / (wpr * 2)) % 8 == 0 && g.K / (wpr * 2) >= 256) wpr *= 2;
+  p.warps_per_row = wpr;
+  out.kind = K_GEMV;
+  out.blob.resize(sizeof(p));
+  memcpy(out.blob.data(), &p, sizeof(p));
+  return true;
+}
+
+void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region) {
+  (void)plan;
+  const GemvParams& p = *(const GemvParams*)l.blob.data();
+  region(p.w, p.N * p.K * 2, "weights");
+  int64_t xs = dt_size((DT)p.x_dt);
+  region(p.x, ((p.M - 1) * p.x_sm + p.K) * xs, "x");
+  region(p.y, ((p.M - 1) * p.y_sm + p.N) * (int64_t)dt_size((DT)p.y_dt), "y");
+}
+
+}  // namespace cljxla

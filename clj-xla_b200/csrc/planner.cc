@@ -16,6 +16,7 @@
 // Device pointers go through the argument table (see kernels.h):
 //   [params P][outputs O][constant blob 1][scratch buffers T].
 #include "planner.h"
+#include "fast_kernels.h"
 
 #include <algorithm>
 #include <cmath>
@@ -176,6 +177,8 @@ class Planner {
   std::vector<Loc> loc_;
   std::vector<char> live_;
   std::vector<std::vector<int>> users_;
+  std::vector<std::vector<int>> ins_;         // operands (fused kernels override the graph's)
+  std::map<int, AttnMatch> attn_;             // probs.V dot -> matched attention block
   std::vector<int> uf_;                       // union-find parent (EW nodes)
   std::vector<int> gmin_, gext_, gsize_, gin_;
   std::vector<int> out_claim_;                // node -> output index claimed, or -1
@@ -208,6 +211,8 @@ class Planner {
   void emit_unit(int u);
   void emit_ew_group(const std::vector<int>& members);
   void emit_node_kernel(int n);
+  void emit_attention(int d2);
+  bool splat_value(int n, double& v);
   void emit_outputs();
   void allocate_arena();
 
@@ -587,8 +592,126 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
   }
 }
 
+void Planner::emit_attention(int d2) {
+  const AttnMatch& am = attn_.at(d2);
+  const Node& D2 = g_.nodes[d2];
+  const Node& K = g_.nodes[am.kc];
+  int oslot = ensure_buf(d2);
+  AttnParams P{};
+  P.q = view_of(am.q);
+  P.k = view_of(am.kc);
+  P.v = view_of(am.vc);
+  P.mask = view_of(am.mask);
+  P.B = (int32_t)D2.shape[0];
+  P.nq = (int32_t)D2.shape[1];
+  P.Sq = (int32_t)D2.shape[2];
+  P.hd = (int32_t)D2.shape[3];
+  P.nkv = (int32_t)K.shape[1];
+  P.T = (int32_t)K.shape[2];
+  P.group = am.group;
+  const int hpl = P.hd / 32;
+  // K/V rows must be contiguous along hd and aligned for hd/32-element vector loads
+  auto kv_ok = [&](const TView& v) {
+    int64_t es = (int64_t)dt_size((DT)v.dt);
+    bool ok = v.stride[3] == 1 && (v.p.off % (hpl * es)) == 0;
+    for (int d = 0; d < 3; ++d) ok &= (v.stride[d] % hpl) == 0;
+    return ok;
+  };
+  if (!kv_ok(P.k)) P.k = materialize(P.k, K.shape, K.dt);
+  if (!kv_ok(P.v)) P.v = materialize(P.v, g_.nodes[am.vc].shape, g_.nodes[am.vc].dt);
+  P.k_dt = P.k.dt;
+  P.dt_d1 = kdt(g_.nodes[am.d1].dt);
+  P.dt_m = kdt(g_.nodes[am.m].dt);
+  P.dt_sub = kdt(g_.nodes[am.sub].dt);
+  P.dt_exp = kdt(g_.nodes[am.exp].dt);
+  P.out_dt = kdt(D2.dt);
+  P.mask_skip = -5000.0f;
+  // the score chain as a register program; register 0 holds the incoming score
+  int nreg = 1, cur = 0;
+  auto emit = [&](const EwInstr& I) {
+    if (P.nchain >= 12) fail(E_INTERNAL, "attention score chain too long");
+    P.chain[P.nchain++] = I;
+  };
+  for (int c : am.chain) {
+    const Node& C = g_.nodes[c];
+    std::vector<int> regs;
+    for (int o : C.in) {
+      double v;
+      if (splat_value(o, v)) {
+        EwInstr I{};
+        I.op = EW_IMM;
+        I.dt = (uint8_t)kdt(DT::F32);
+        I.dst = (uint8_t)nreg++;
+        I.fimm = (float)v;
+        emit(I);
+        regs.push_back(I.dst);
+      } else {
+        regs.push_back(cur);
+      }
+    }
+    EwInstr I{};
+    switch (C.op) {
+      case Op::Mul: I.op = EW_MUL; break;
+      case Op::Div: I.op = EW_DIV; break;
+      case Op::Add: I.op = EW_ADD; break;
+      case Op::Sub: I.op = EW_SUB; break;
+      case Op::Max: I.op = EW_MAX; break;
+      case Op::Min: I.op = EW_MIN; break;
+      case Op::Tanh: I.op = EW_TANH; break;
+      case Op::Neg: I.op = EW_NEG; break;
+      default: I.op = EW_CONVERT; break;
+    }
+    I.dt = (uint8_t)kdt(C.dt);
+    I.a = (uint8_t)regs[0];
+    I.b = (uint8_t)(regs.size() > 1 ? regs[1] : 0);
+    I.dst = (uint8_t)nreg++;
+    if (nreg > 16) fail(E_INTERNAL, "attention score chain needs too many registers");
+    emit(I);
+    cur = I.dst;
+  }
+  P.chain_out = cur;
+  const int64_t rows_kv = (int64_t)P.B * P.nkv;
+  P.qtile = P.Sq == 1 ? 1 : std::max(1, std::min(P.Sq, 8 / P.group));
+  if (P.qtile * P.group > 8) P.qtile = 1;
+  if (P.group > 8) fail(E_UNIMPLEMENTED, "attention with more than 8 query heads per KV head");
+  int64_t qtiles = (P.Sq + P.qtile - 1) / P.qtile;
+  int64_t ctas = rows_kv * qtiles;
+  int splits = 1;
+  while (ctas * splits < 2 * 148 && (int64_t)splits * 2 * 64 <= P.T) splits *= 2;
+  P.splits = splits;
+  P.out = slot_ptr(oslot);
+  int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
+  int64_t rows = (int64_t)P.B * P.nq * P.Sq;
+  if (splits > 1) P.part = slot_ptr(new_tmp((int64_t)splits * rows * (P.hd + 2) * 4));
+  push(K_ATTN_DECODE, blob_of(P), D2.name, kvbytes, 4LL * rows * P.T * P.hd);
+  if (splits > 1) {
+    touch(P.part.slot);
+    push(K_ATTN_COMBINE, blob_of(P), D2.name, (int64_t)splits * rows * (P.hd + 2) * 4);
+  }
+}
+
+bool Planner::splat_value(int n, double& v) {
+  // evaluated on the graph: the chain's constants are dead once the block is fused
+  const Node& nd = g_.nodes[n];
+  if (nd.op == Op::Constant) {
+    if (!nd.splat) return false;
+    v = nd.splat_val;
+    return true;
+  }
+  if (is_view_op(nd, g_)) return splat_value(nd.in[0], v);
+  if (nd.op == Op::Convert && dt_is_float(nd.dt) && splat_value(nd.in[0], v)) {
+    v = round_host(v, nd.dt);
+    return true;
+  }
+  return false;
+}
+
 void Planner::emit_node_kernel(int id) {
   const Node& n = g_.nodes[id];
+  if (attn_.count(id)) {
+    emit_attention(id);
+    return;
+  }
   int oslot = ensure_buf(id);
   switch (n.op) {
     case Op::Reduce: {
@@ -796,7 +919,15 @@ void Planner::emit_node_kernel(int id) {
       int64_t bytes = a.numel() * (int64_t)dt_size(a.dt) + b.numel() * (int64_t)dt_size(b.dt) +
                       n.numel() * (int64_t)dt_size(n.dt);
       int64_t flops = 2 * G.batch * G.M * G.N * G.K;
-      push(K_GEMM, blob_of(G), n.name, bytes, flops);
+      Launch fl;
+      if (opt_.fast_kernels && make_gemv(G, fl)) {
+        fl.label = n.name;
+        fl.algo_bytes = bytes;
+        fl.algo_flops = flops;
+        plan_.launches.push_back(std::move(fl));
+      } else {
+        push(K_GEMM, blob_of(G), n.name, bytes, flops);
+      }
       break;
     }
     default:
@@ -868,7 +999,7 @@ void Planner::emit_all() {
   for (int i = 0; i < N; ++i) {
     if (unit[i] < 0) continue;
     units.insert(unit[i]);
-    for (int o : g_.nodes[i].in) {
+    for (int o : ins_[i]) {
       if (is_splat(o)) continue;
       int r = view_root(o);
       if (unit[r] >= 0 && unit[r] != unit[i]) {
@@ -939,17 +1070,31 @@ void Planner::run() {
   for (int p : g_.params) plan_.params.push_back({g_.nodes[p].dt, g_.nodes[p].shape});
   for (int o : g_.outputs) plan_.outs.push_back({g_.nodes[o].dt, g_.nodes[o].shape});
   plan_.out_alias_param.assign(O_, -1);
-  users_.assign(N, {});
-  for (int i = 0; i < N; ++i)
-    for (int x : g_.nodes[i].in) users_[x].push_back(i);
-  live_.assign(N, 0);
-  std::vector<int> stack(g_.outputs.begin(), g_.outputs.end());
-  while (!stack.empty()) {
-    int x = stack.back();
-    stack.pop_back();
-    if (live_[x]) continue;
-    live_[x] = 1;
-    for (int y : g_.nodes[x].in) stack.push_back(y);
+  ins_.assign(N, {});
+  for (int i = 0; i < N; ++i) ins_[i] = g_.nodes[i].in;
+  auto liveness = [&]() {
+    users_.assign(N, {});
+    for (int i = 0; i < N; ++i)
+      for (int x : ins_[i]) users_[x].push_back(i);
+    live_.assign(N, 0);
+    std::vector<int> stack(g_.outputs.begin(), g_.outputs.end());
+    while (!stack.empty()) {
+      int x = stack.back();
+      stack.pop_back();
+      if (live_[x]) continue;
+      live_[x] = 1;
+      for (int y : ins_[x]) stack.push_back(y);
+    }
+  };
+  liveness();
+  if (opt_.fast_kernels) {
+    // fused attention: the matched block's interior disappears, the probs.V
+    // dot becomes one kernel reading q, the K/V caches and the mask
+    for (AttnMatch& am : match_attention(g_, live_, users_)) {
+      ins_[am.d2] = {am.q, am.kc, am.vc, am.mask};
+      attn_[am.d2] = am;
+    }
+    if (!attn_.empty()) liveness();
   }
   for (int i = 0; i < N; ++i) plan_.n_live += live_[i];
   mat_slot_.assign(N, -1);
@@ -969,6 +1114,15 @@ void Planner::run() {
   emit_outputs();
   allocate_arena();
   verify_plan(plan_);
+  if (const char* path = getenv("CLJXLA_B200_DUMP_PLAN")) {
+    if (FILE* f = fopen(path, "a")) {
+      fprintf(f, "# plan %s: %zu launches, arena %lld bytes\n", plan_.name.c_str(), plan_.launches.size(),
+              (long long)plan_.arena_bytes);
+      for (const Launch& l : plan_.launches)
+        fprintf(f, "%s\t%lld\t%s\n", kernel_kind_name(l.kind), (long long)l.algo_bytes, l.label.c_str());
+      fclose(f);
+    }
+  }
 }
 
 }  // namespace

@@ -62,6 +62,5 @@ void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);
 
 // Host-side bounds verification of every launch (throws INTERNAL on a violation).
 void verify_plan(const Plan& p);
-void verify_fast_launch(const Plan& p, const Launch& l);
 
 }  // namespace cljxla

@@ -4,7 +4,7 @@
 // buffer its argument-table slot will point at.  A planner bug therefore
 // surfaces as an INTERNAL compile error rather than an out-of-bounds access
 // on the device.
-#include "planner.h"
+#include "fast_kernels.h"
 
 namespace cljxla {
 namespace {
@@ -120,7 +120,7 @@ void verify_plan(const Plan& p) {
         break;
       }
       default:
-        verify_fast_launch(p, l);
+        verify_fast_launch_impl(p, l, [&](const DPtr& d, int64_t bytes, const char* what) { c.region(d, bytes, what); });
         break;
     }
   }
