@@ -56,6 +56,9 @@ struct Graph {
 // anything outside the supported subset.
 std::unique_ptr<Graph> parse_mlir(const char* text, size_t len);
 
+// Merges structurally identical nodes (common-subexpression elimination).
+std::unique_ptr<Graph> cse_graph(const Graph& g, int* merged);
+
 // Round-to-nearest-even conversions used for literals and host copies.
 uint16_t f32_to_bf16(float f);
 float bf16_to_f32(uint16_t b);

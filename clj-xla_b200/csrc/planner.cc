@@ -301,12 +301,28 @@ void Planner::group_elementwise() {
   gsize_.assign(N, 1);
   gin_.assign(N, 0);
   for (int i = 0; i < N; ++i) uf_[i] = i;
-  auto ext_idx = [&](int o) -> int {  // index of the node an operand needs computed first
-    if (is_splat(o)) return -1;
-    int r = view_root(o);
-    const Node& rn = g_.nodes[r];
-    if (rn.op == Op::Param || rn.op == Op::Constant || is_splat(r)) return -1;
-    return r;
+  // groups: members and external (non-splat) operands, keyed by root
+  std::map<int, std::vector<int>> members, exts;
+  std::vector<int> stamp(N, 0);
+  int cur_stamp = 0;
+  // true if any external operand can reach a member through the graph
+  auto has_path_back = [&](const std::set<int>& mem, const std::set<int>& ext) {
+    int lo = *mem.begin();
+    ++cur_stamp;
+    std::vector<int> stack;
+    for (int o : ext) stack.push_back(o);
+    while (!stack.empty()) {
+      int x = stack.back();
+      stack.pop_back();
+      if (x < lo || stamp[x] == cur_stamp) continue;
+      stamp[x] = cur_stamp;
+      if (mem.count(x)) return true;
+      for (int y : ins_[x]) stack.push_back(y);
+    }
+    return false;
+  };
+  auto inside = [&](int o, const Node& n, const std::set<int>& roots) {
+    return loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape && roots.count(find(o));
   };
   for (int i = 0; i < N; ++i) {
     if (!live_[i] || loc_[i].kind != Loc::EW) continue;
@@ -317,38 +333,44 @@ void Planner::group_elementwise() {
         if (loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape) cands.push_back(find(o));
     std::sort(cands.begin(), cands.end());
     cands.erase(std::unique(cands.begin(), cands.end()), cands.end());
-    std::set<int> merged;
-    auto eval = [&](const std::set<int>& set, int& tmin, int& text, int& tsize, int& tin) {
-      tmin = i;
-      text = -1;
-      tsize = 1;
-      tin = 0;
-      for (int G : set) {
-        tmin = std::min(tmin, gmin_[G]);
-        text = std::max(text, gext_[G]);
-        tsize += gsize_[G];
-        tin += gin_[G];
-      }
-      for (int o : n.in) {
-        if (is_splat(o)) continue;
-        bool inside = loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape && set.count(find(o));
-        if (!inside) { text = std::max(text, ext_idx(o)); tin++; }
-      }
+    // candidate merged group: members + external operands, validity test
+    auto build = [&](const std::set<int>& roots, std::set<int>& mem, std::set<int>& ext) {
+      mem = {i};
+      ext.clear();
+      for (int G : roots)
+        for (int m : members[G]) mem.insert(m);
+      for (int G : roots)
+        for (int o : exts[G])
+          if (!mem.count(o)) ext.insert(o);
+      for (int o : n.in)
+        if (!is_splat(o) && !inside(o, n, roots)) ext.insert(o);
     };
-    for (int G : cands) {
-      std::set<int> trial = merged;
-      trial.insert(G);
-      int tmin, text, tsize, tin;
-      eval(trial, tmin, text, tsize, tin);
-      if (text < tmin && tsize <= 24 && tin <= EW_MAXIN - 2) merged = trial;
+    auto valid = [&](const std::set<int>& roots) {
+      std::set<int> mem, ext;
+      build(roots, mem, ext);
+      if ((int)mem.size() > 24 || (int)ext.size() > EW_MAXIN - 2) return false;
+      return !has_path_back(mem, ext);
+    };
+    std::set<int> merged;
+    std::set<int> all(cands.begin(), cands.end());
+    if (!all.empty() && valid(all)) {
+      merged = all;
+    } else {
+      for (int G : cands) {
+        std::set<int> trial = merged;
+        trial.insert(G);
+        if (valid(trial)) merged = trial;
+      }
     }
-    int tmin, text, tsize, tin;
-    eval(merged, tmin, text, tsize, tin);
-    for (int M : merged) uf_[M] = i;
-    gmin_[i] = tmin;
-    gext_[i] = text;
-    gsize_[i] = tsize;
-    gin_[i] = tin;
+    std::set<int> mem, ext;
+    build(merged, mem, ext);
+    for (int M : merged) {
+      uf_[M] = i;
+      members.erase(M);
+      exts.erase(M);
+    }
+    members[i] = std::vector<int>(mem.begin(), mem.end());
+    exts[i] = std::vector<int>(ext.begin(), ext.end());
   }
 }
 
@@ -1129,6 +1151,14 @@ void Planner::run() {
 
 std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt) {
   auto plan = std::make_unique<Plan>();
+  if (opt.fuse) {
+    int merged = 0;
+    auto g2 = cse_graph(g, &merged);
+    Planner p(*g2, opt, *plan);
+    p.run();
+    plan->n_nodes = (int)g.nodes.size();
+    return plan;
+  }
   Planner p(g, opt, *plan);
   p.run();
   return plan;
