@@ -95,11 +95,16 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParam
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e = tid; e < P.n; e += nthreads) {
     int64_t idx[CLJXLA_MAXR];
-    int64_t rem = e;
-    for (int d = P.rank - 1; d >= 0; --d) {
-      int64_t dim = P.dims[d];
-      idx[d] = rem % dim;
-      rem /= dim;
+    if (P.rank == 1) {
+      idx[0] = e;
+    } else {
+      int64_t rem = e;
+      for (int d = P.rank - 1; d > 0; --d) {
+        int64_t dim = P.dims[d];
+        idx[d] = rem % dim;
+        rem /= dim;
+      }
+      idx[0] = rem;
     }
     uint32_t R[EW_NREG];
     for (int pc = 0; pc < P.ncode; ++pc) {
@@ -110,6 +115,18 @@ __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParam
       switch (I.op) {
         case EW_LOAD: {
           const EwIn& in = P.in[I.aux];
+          if (in.sel_dim >= 0) {
+            const int64_t k = idx[in.sel_dim];
+            if (k < in.sel_lo || k >= in.sel_hi) {  // another concatenate operand covers this index
+              r = R[I.b];
+              break;
+            }
+            int64_t off = (k - in.sel_lo) * in.stride[in.sel_dim];
+            for (int d = 0; d < P.rank; ++d)
+              if (d != in.sel_dim) off += idx[d] * in.stride[d];
+            r = ld_elem(dres(in.p, argtab), off, in.dt);
+            break;
+          }
           int64_t off = 0;
           for (int d = 0; d < P.rank; ++d) off += idx[d] * in.stride[d];
           r = ld_elem(dres(in.p, argtab), off, in.dt);
@@ -211,6 +228,22 @@ __device__ __forceinline__ int64_t view_off(const TView& v, int64_t e) {
     e /= dim;
   }
   return off;
+}
+
+// byte copy between dense buffers: 16-byte vectors when both ends are aligned
+__global__ void copy_bytes_kernel(DPtr srcp, DPtr dstp, int64_t bytes, int vec, const uint64_t* __restrict__ argtab) {
+  const char* src = dres(srcp, argtab);
+  char* dst = dres(dstp, argtab);
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
+  if (vec == 16) {
+    const int64_t n = bytes / 16;
+    for (int64_t i = tid; i < n; i += nt) ((uint4*)dst)[i] = __ldcs(((const uint4*)src) + i);
+  } else if (vec == 4) {
+    const int64_t n = bytes / 4;
+    for (int64_t i = tid; i < n; i += nt) ((uint32_t*)dst)[i] = ((const uint32_t*)src)[i];
+  } else {
+    for (int64_t i = tid; i < bytes; i += nt) dst[i] = src[i];
+  }
 }
 
 __global__ void copy_kernel(const __grid_constant__ CopyParams P, const uint64_t* __restrict__ argtab) {
@@ -369,8 +402,28 @@ void launch_ew(const EwParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.n == 0) return;
   ew_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
 }
+static bool view_is_dense(const TView& v) {
+  int64_t acc = 1;
+  for (int d = v.rank - 1; d >= 0; --d) {
+    if (v.shape[d] != 1 && v.stride[d] != acc) return false;
+    acc *= v.shape[d];
+  }
+  return true;
+}
+
 void launch_copy(const CopyParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.n == 0) return;
+  if (p.src.dt == p.dst.dt && view_is_dense(p.src) && view_is_dense(p.dst)) {
+    const int64_t es = p.src.dt == KDT_F32 || p.src.dt == KDT_I32 || p.src.dt == KDT_U32 ? 4
+                       : (p.src.dt == KDT_BF16 || p.src.dt == KDT_F16 || p.src.dt == KDT_I16) ? 2
+                       : (p.src.dt == KDT_I64 || p.src.dt == KDT_F64) ? 8 : 1;
+    const int64_t bytes = p.n * es;
+    int vec = 1;
+    if (bytes % 16 == 0 && p.src.p.off % 16 == 0 && p.dst.p.off % 16 == 0) vec = 16;
+    else if (bytes % 4 == 0 && p.src.p.off % 4 == 0 && p.dst.p.off % 4 == 0) vec = 4;
+    copy_bytes_kernel<<<grid_for(bytes / vec, 256), 256, 0, s>>>(p.src.p, p.dst.p, bytes, vec, argtab);
+    return;
+  }
   copy_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
 }
 void launch_reduce(const ReduceParams& p, const uint64_t* argtab, cudaStream_t s) {

@@ -61,7 +61,8 @@ constexpr int EW_NREG = 32;
 struct EwIn {
   DPtr p;
   int32_t dt;
-  int32_t pad_;
+  int32_t sel_dim;              // >= 0: concatenate operand, valid for sel_lo <= idx[sel_dim] < sel_hi
+  int64_t sel_lo, sel_hi;       // (loaded at idx[sel_dim] - sel_lo; elsewhere the load yields register b)
   int64_t stride[CLJXLA_MAXR];  // per loop dim, elements (0 = broadcast)
 };
 

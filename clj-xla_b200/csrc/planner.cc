@@ -289,6 +289,14 @@ void Planner::classify() {
       L.kind = Loc::EW;
       continue;
     }
+    if (n.op == Op::Concat && opt_.fuse) {
+      bool ok = true;
+      for (int x : n.in) ok &= !is_splat(x) && g_.nodes[x].dt == n.dt;
+      if (ok) {
+        L.kind = Loc::EW;  // fused as range-predicated loads
+        continue;
+      }
+    }
     L.kind = Loc::BUF;  // produced by its own kernel
   }
 }
@@ -328,7 +336,7 @@ void Planner::group_elementwise() {
     if (!live_[i] || loc_[i].kind != Loc::EW) continue;
     const Node& n = g_.nodes[i];
     std::vector<int> cands;
-    if (opt_.fuse)
+    if (opt_.fuse && n.op != Op::Concat)
       for (int o : n.in)
         if (loc_[o].kind == Loc::EW && g_.nodes[o].shape == n.shape) cands.push_back(find(o));
     std::sort(cands.begin(), cands.end());
@@ -349,6 +357,10 @@ void Planner::group_elementwise() {
       std::set<int> mem, ext;
       build(roots, mem, ext);
       if ((int)mem.size() > 24 || (int)ext.size() > EW_MAXIN - 2) return false;
+      for (int x : mem)  // a fused concatenate reads its operands from memory
+        if (g_.nodes[x].op == Op::Concat)
+          for (int o : g_.nodes[x].in)
+            if (mem.count(o)) return false;
       return !has_path_back(mem, ext);
     };
     std::set<int> merged;
@@ -381,7 +393,8 @@ void Planner::decide_materialisation() {
     bool need = out_claim_[i] >= 0;
     for (int u : users_[i]) {
       if (!live_[u]) continue;
-      bool same = loc_[u].kind == Loc::EW && find(u) == find(i) && g_.nodes[u].shape == g_.nodes[i].shape;
+      bool same = loc_[u].kind == Loc::EW && find(u) == find(i) && g_.nodes[u].shape == g_.nodes[i].shape &&
+                  g_.nodes[u].op != Op::Concat;  // a fused concatenate loads its operands
       if (!same) need = true;
     }
     for (int o : g_.outputs) if (o == i) need = true;
@@ -515,6 +528,47 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
   for (size_t k = 0; k < members.size(); ++k) {
     int id = members[k];
     const Node& n = g_.nodes[id];
+    if (n.op == Op::Concat) {
+      // concatenate: one range-predicated load per (materialised) operand,
+      // chained so each loop index takes the operand that covers it
+      EwInstr Z{};
+      Z.op = EW_IMM;
+      Z.dt = (uint8_t)kdt(n.dt);
+      Z.dst = (uint8_t)alloc_reg();
+      emit(Z);
+      int cur = Z.dst;
+      int64_t off = 0;
+      const int dim = (int)n.i0;
+      for (int o : n.in) {
+        if (P.nin >= EW_MAXIN) fail(E_INTERNAL, "fused elementwise region has too many inputs");
+        const Node& on = g_.nodes[o];
+        TView v = view_of(o);
+        EwIn& in = P.in[P.nin];
+        in.p = v.p;
+        in.dt = v.dt;
+        in.sel_dim = dim;
+        in.sel_lo = off;
+        in.sel_hi = off + on.shape[dim];
+        for (int d = 0; d < P.rank; ++d) in.stride[d] = v.stride[d];
+        bytes += on.numel() * (int64_t)dt_size(on.dt);
+        EwInstr L{};
+        L.op = EW_LOAD;
+        L.dt = (uint8_t)v.dt;
+        L.aux = (uint8_t)P.nin;
+        L.b = (uint8_t)cur;
+        L.dst = (uint8_t)alloc_reg();
+        emit(L);
+        free_regs.push_back(cur);
+        cur = L.dst;
+        P.nin++;
+        off += on.shape[dim];
+      }
+      reg_of[id] = cur;
+      if (loc_[id].slot >= 0) outs.emplace_back(id, cur);
+      if (!label.empty()) label += ",";
+      if (label.size() < 80) label += n.name;
+      continue;
+    }
     std::vector<int> regs;
     for (int o : n.in) {
       if (member_set.count(o) && reg_of.count(o)) { regs.push_back(reg_of[o]); continue; }
@@ -543,6 +597,7 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
         EwIn& in = P.in[P.nin];
         in.p = v.p;
         in.dt = v.dt;
+        in.sel_dim = -1;
         for (int d = 0; d < P.rank; ++d) in.stride[d] = v.stride[d];
         bytes += on.numel() * (int64_t)dt_size(on.dt);
         EwInstr I{};
@@ -595,6 +650,35 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
     if (loc_[id].slot >= 0) outs.emplace_back(id, I.dst);
     if (!label.empty()) label += ",";
     if (label.size() < 80) label += n.name;
+  }
+  // collapse the loop shape: drop size-1 dims and merge adjacent dims that are
+  // contiguous for every input (outputs are dense), unless an iota needs them
+  bool has_iota = false;
+  for (int k = 0; k < P.ncode; ++k) has_iota |= P.code[k].op == EW_IOTA;
+  for (int i = 0; i < P.nin; ++i) has_iota |= P.in[i].sel_dim >= 0;
+  if (!has_iota && P.rank > 1) {
+    std::vector<int64_t> dims;
+    std::vector<std::vector<int64_t>> st(P.nin);
+    for (int d = 0; d < P.rank; ++d) {
+      if (P.dims[d] == 1) continue;
+      bool merge = !dims.empty();
+      for (int i = 0; i < P.nin && merge; ++i) merge = st[i].back() == P.in[i].stride[d] * P.dims[d];
+      if (merge) {
+        dims.back() *= P.dims[d];
+        for (int i = 0; i < P.nin; ++i) st[i].back() = P.in[i].stride[d];
+      } else {
+        dims.push_back(P.dims[d]);
+        for (int i = 0; i < P.nin; ++i) st[i].push_back(P.in[i].stride[d]);
+      }
+    }
+    if (dims.empty()) {
+      dims.push_back(1);
+      for (int i = 0; i < P.nin; ++i) st[i].push_back(0);
+    }
+    P.rank = (int)dims.size();
+    for (int d = 0; d < CLJXLA_MAXR; ++d) P.dims[d] = d < P.rank ? dims[d] : 0;
+    for (int i = 0; i < P.nin; ++i)
+      for (int d = 0; d < CLJXLA_MAXR; ++d) P.in[i].stride[d] = d < P.rank ? st[i][d] : 0;
   }
   // outputs, at most EW_MAXOUT per launch (re-run the program for extra chunks)
   for (size_t s = 0; s < outs.size(); s += EW_MAXOUT) {
@@ -814,6 +898,18 @@ void Planner::emit_node_kernel(int id) {
       D.out = slot_ptr(oslot);
       D.n = n.numel();
       int64_t ub = up.numel() * (int64_t)dt_size(n.dt);
+      if (D.operand.dt == D.dt) {
+        // copy the operand with the vectorised copy, then write the window in place
+        CopyParams C{};
+        C.src = D.operand;
+        C.dst = dense_view(oslot, n.dt, n.shape);
+        C.n = n.numel();
+        push(K_COPY, blob_of(C), n.name + ".copy", 2 * n.numel() * (int64_t)dt_size(n.dt));
+        D.operand = C.dst;
+        D.in_place = 1;
+        push(K_DUS, blob_of(D), n.name, ub);
+        break;
+      }
       push(K_DUS, blob_of(D), n.name, 2 * n.numel() * (int64_t)dt_size(n.dt) + ub);
       break;
     }

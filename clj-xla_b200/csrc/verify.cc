@@ -70,6 +70,12 @@ void verify_plan(const Plan& p) {
           v.dt = e.in[i].dt;
           v.rank = e.rank;
           for (int d = 0; d < e.rank; ++d) { v.shape[d] = e.dims[d]; v.stride[d] = e.in[i].stride[d]; }
+          if (e.in[i].sel_dim >= 0) {  // concatenate operand: only its own index range is loaded
+            const EwIn& in = e.in[i];
+            if (in.sel_dim >= e.rank || in.sel_lo < 0 || in.sel_hi > e.dims[in.sel_dim] || in.sel_lo > in.sel_hi)
+              fail(E_INTERNAL, "bad concatenate operand range");
+            v.shape[in.sel_dim] = in.sel_hi - in.sel_lo;
+          }
           c.view(v, "input");
         }
         for (int o = 0; o < e.nout; ++o) c.region(e.out[o].p, e.n * (int64_t)esz(e.out[o].dt), "output");
