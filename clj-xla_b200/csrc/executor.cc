@@ -27,6 +27,7 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     case K_GATHER: launch_gather(*(const GatherParams*)b, argtab, s); break;
     case K_DUS: launch_dus(*(const DusParams*)b, argtab, s); break;
     case K_GEMM: launch_gemm(*(const GemmParams*)b, argtab, s); break;
+    case K_ROWNORM: launch_row(*(const RowParams*)b, argtab, s); break;
     default: run_fast_launch(l, argtab, s); break;
   }
 }

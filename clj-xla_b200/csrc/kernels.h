@@ -92,6 +92,50 @@ struct EwParams {
   EwOut out[EW_MAXOUT];
 };
 
+// -------------------------------------------------------------- row fusion
+// A fused row region: elementwise work over a loop shape F = [rows..., C]
+// plus reductions along the last axis whose per-row results feed later
+// elementwise work (normalisations, softmax).  One CTA handles a row; the
+// program runs in phases separated by block-wide reductions.  Registers
+// 0..RP_SREG0-1 hold per-element values (recomputed in each phase that needs
+// them), registers RP_SREG0.. hold per-row scalars.
+constexpr int RP_MAXIN = 12;
+constexpr int RP_MAXCODE = 96;
+constexpr int RP_MAXPH = 4;
+constexpr int RP_MAXOUT = 6;
+constexpr int RP_SREG0 = 32;
+constexpr int RP_NREG = 48;
+
+struct RowPhase {
+  uint16_t lo, hi;     // per-element code of this phase: code[lo, hi)
+  uint16_t slo, shi;   // per-row code run after this phase's reduction: code[slo, shi)
+  int8_t red_reg;      // register reduced at the end of the phase (-1: none)
+  uint8_t red_kind;    // 0 add, 1 max
+  uint8_t red_dst;     // scalar register receiving the reduced value
+  uint8_t red_dt;      // result type of the reduce (rounding)
+  float red_init;      // printed init value (0 or -1e30)
+};
+
+struct RowOut {
+  DPtr p;
+  int32_t dt;
+  int16_t reg;
+  int8_t phase;        // per-element output: stored during this phase
+  int8_t scalar;       // 1: per-row output, one value per row
+};
+
+struct RowParams {
+  int64_t rows, C;
+  int32_t rank, nin, nphase, nout;
+  int64_t dims[CLJXLA_MAXR];  // F
+  EwIn in[RP_MAXIN];
+  RowPhase ph[RP_MAXPH];
+  EwInstr code[RP_MAXCODE];
+  RowOut out[RP_MAXOUT];
+};
+
+void launch_row(const RowParams& p, const uint64_t* argtab, cudaStream_t s);
+
 // --------------------------------------------------------------- reduce
 struct ReduceParams {
   TView in;               // full input view

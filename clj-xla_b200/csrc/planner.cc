@@ -159,9 +159,27 @@ bool fold_splat(const Node& n, const std::vector<double>& a, const std::vector<D
 }
 
 struct Loc {
-  enum Kind { NONE, SPLAT, BUF, VIEWOP, EW } kind = NONE;
+  enum Kind { NONE, SPLAT, BUF, VIEWOP, EW, ROW } kind = NONE;
   double splat = 0;
   int slot = -1;  // argtab slot of the node's buffer (BUF / materialised EW)
+};
+
+// A fused row region (see k_row.cu): per-element members over the loop shape
+// F, last-axis reductions, per-row scalar members, and the reshape /
+// broadcast views connecting them.
+struct RowRegion {
+  int root = -1;  // first reduce: the unit id
+  std::vector<int64_t> F;
+  std::set<int> full, scalar, reduces;
+  std::map<int, int> alias;  // view node -> member whose value it is (scalar aliases and broadcasts)
+  std::set<int> bcast;       // aliases that broadcast a scalar back to F
+  std::set<int> all() const {
+    std::set<int> s(full);
+    s.insert(scalar.begin(), scalar.end());
+    s.insert(reduces.begin(), reduces.end());
+    for (auto& kv : alias) s.insert(kv.first);
+    return s;
+  }
 };
 
 class Planner {
@@ -179,6 +197,8 @@ class Planner {
   std::vector<std::vector<int>> users_;
   std::vector<std::vector<int>> ins_;         // operands (fused kernels override the graph's)
   std::map<int, AttnMatch> attn_;             // probs.V dot -> matched attention block
+  std::vector<RowRegion> regions_;
+  std::vector<int> region_of_;                // node -> region index or -1
   std::vector<int> uf_;                       // union-find parent (EW nodes)
   std::vector<int> gmin_, gext_, gsize_, gin_;
   std::vector<int> out_claim_;                // node -> output index claimed, or -1
@@ -211,6 +231,8 @@ class Planner {
   void emit_unit(int u);
   void emit_ew_group(const std::vector<int>& members);
   void emit_node_kernel(int n);
+  void build_row_regions();
+  void emit_row_region(int r);
   void emit_attention(int d2);
   bool splat_value(int n, double& v);
   void emit_outputs();
@@ -443,7 +465,7 @@ TView Planner::view_of(int n) {
     v.p.off = (int64_t)L.splat;
     return v;
   }
-  if (L.kind == Loc::BUF || L.kind == Loc::EW) {
+  if (L.kind == Loc::BUF || L.kind == Loc::EW || L.kind == Loc::ROW) {
     if (L.slot < 0 && nd.op == Op::Param) ensure_buf(n);
     if (L.slot < 0) fail(E_INTERNAL, std::string("value %") + nd.name + " is not materialised");
     return dense_view(L.slot, nd.dt, nd.shape);
@@ -696,6 +718,423 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
     }
     push(K_EW, blob_of(Q), label, bytes + ob);
   }
+}
+
+void Planner::build_row_regions() {
+  const int N = (int)g_.nodes.size();
+  region_of_.assign(N, -1);
+  if (!opt_.fuse) return;
+  std::vector<int> stamp(N, 0);
+  int cur = 0;
+  for (int r0 = 0; r0 < N; ++r0) {
+    const Node& R0 = g_.nodes[r0];
+    if (!live_[r0] || R0.op != Op::Reduce || region_of_[r0] >= 0 || loc_[r0].kind != Loc::BUF) continue;
+    const Node& X = g_.nodes[R0.in[0]];
+    if (!dt_is_float(X.dt) || !dt_is_float(R0.dt) || X.rank() < 1 || X.rank() > CLJXLA_MAXR) continue;
+    if (R0.ia.size() != 1 || R0.ia[0] != X.rank() - 1 || !is_splat(R0.in[1])) continue;
+    RowRegion rg;
+    rg.root = r0;
+    rg.F = X.shape;
+    std::vector<int64_t> sshape(rg.F.begin(), rg.F.end() - 1), sshape1 = sshape;
+    sshape1.push_back(1);
+    auto in_region = [&](int x) { return rg.full.count(x) || rg.scalar.count(x) || rg.reduces.count(x) || rg.alias.count(x); };
+    auto members_min = [&]() {
+      int lo = INT32_MAX;
+      for (int x : rg.full) lo = std::min(lo, x);
+      for (int x : rg.scalar) lo = std::min(lo, x);
+      for (int x : rg.reduces) lo = std::min(lo, x);
+      return lo;
+    };
+    // an external operand must not depend on any region member
+    auto external_ok = [&](int o) {
+      if (is_splat(o)) return true;
+      int lo = members_min();
+      ++cur;
+      std::vector<int> st{o};
+      while (!st.empty()) {
+        int x = st.back();
+        st.pop_back();
+        if (x < lo || stamp[x] == cur) continue;
+        stamp[x] = cur;
+        if (in_region(x)) return false;
+        for (int y : ins_[x]) st.push_back(y);
+      }
+      return true;
+    };
+    auto is_scalar_val = [&](int o) {  // scalar member / reduce / scalar alias
+      if (rg.scalar.count(o) || rg.reduces.count(o)) return true;
+      return rg.alias.count(o) && !rg.bcast.count(o);
+    };
+    auto is_full_val = [&](int o) { return rg.full.count(o) || rg.bcast.count(o); };
+    // producers of the reduced value: elementwise nodes of shape F feeding it
+    std::vector<int> st{R0.in[0]};
+    while (!st.empty()) {
+      int x = st.back();
+      st.pop_back();
+      if (rg.full.count(x)) continue;
+      const Node& xn = g_.nodes[x];
+      if (loc_[x].kind != Loc::EW || xn.op == Op::Concat || xn.shape != rg.F || region_of_[x] >= 0) continue;
+      if (rg.full.size() >= 16) break;
+      rg.full.insert(x);
+      for (int o : ins_[x]) st.push_back(o);
+    }
+    rg.reduces.insert(r0);
+    // all non-member operands of the producers must be external and independent
+    bool ok = true;
+    for (int x : rg.full)
+      for (int o : ins_[x])
+        if (!in_region(o)) ok &= external_ok(o);
+    if (!ok) continue;
+    // grow forward
+    bool changed = true;
+    int nphase_red = 1;
+    while (changed) {
+      changed = false;
+      std::set<int> frontier;
+      for (int x : rg.all())
+        for (int u : users_[x])
+          if (live_[u] && !in_region(u) && region_of_[u] < 0) frontier.insert(u);
+      for (int u : frontier) {
+        const Node& un = g_.nodes[u];
+        if ((int)(rg.full.size() + rg.scalar.size()) >= 40) break;
+        // scalar aliases: reshape / identity views between [rows] and [rows, 1]
+        if (is_view_op(un, g_) && un.op != Op::Broadcast && is_scalar_val(un.in[0]) &&
+            (un.shape == sshape || un.shape == sshape1)) {
+          rg.alias[u] = un.in[0];
+          changed = true;
+          continue;
+        }
+        // broadcast of a per-row scalar back over F (trailing axis broadcast)
+        if (un.op == Op::Broadcast && is_scalar_val(un.in[0]) && un.shape == rg.F) {
+          const Node& sn = g_.nodes[un.in[0]];
+          bool okb = (int)un.ia.size() == sn.rank();
+          for (int i = 0; i < (int)un.ia.size() && okb; ++i) okb = un.ia[i] == i;
+          if (okb && sn.rank() == (int)rg.F.size() && sn.shape.back() != 1) okb = false;
+          if (okb) {
+            rg.alias[u] = un.in[0];
+            rg.bcast.insert(u);
+            changed = true;
+          }
+          continue;
+        }
+        if (loc_[u].kind == Loc::EW && un.op != Op::Concat && un.op != Op::Iota) {
+          bool all_scalar = true, all_full = true;
+          std::vector<int> exts;
+          for (int o : ins_[u]) {
+            if (is_splat(o)) continue;
+            if (!is_scalar_val(o)) all_scalar = false;
+            if (!is_full_val(o)) {
+              all_full = false;
+              exts.push_back(o);
+            }
+          }
+          if ((un.shape == sshape || un.shape == sshape1) && all_scalar &&
+              (int)(rg.scalar.size() + rg.reduces.size()) < RP_NREG - RP_SREG0) {
+            rg.scalar.insert(u);
+            changed = true;
+            continue;
+          }
+          if (un.shape == rg.F) {
+            bool ext_ok = true;
+            for (int o : exts) ext_ok &= !is_scalar_val(o) && external_ok(o);
+            // an external operand must be readable with F-shaped strides
+            for (int o : exts) ext_ok &= g_.nodes[o].shape == rg.F;
+            if (ext_ok) {
+              rg.full.insert(u);
+              changed = true;
+            }
+            (void)all_full;
+            continue;
+          }
+          continue;
+        }
+        if (un.op == Op::Reduce && loc_[u].kind == Loc::BUF && rg.full.count(un.in[0]) && nphase_red < RP_MAXPH - 1 &&
+            un.ia.size() == 1 && un.ia[0] == (int64_t)rg.F.size() - 1 && is_splat(un.in[1]) && dt_is_float(un.dt)) {
+          rg.reduces.insert(u);
+          nphase_red++;
+          changed = true;
+        }
+      }
+    }
+    int id = (int)regions_.size();
+    for (int x : rg.all()) region_of_[x] = id;
+    for (int x : rg.full) loc_[x].kind = Loc::ROW;
+    for (int x : rg.scalar) loc_[x].kind = Loc::ROW;
+    for (int x : rg.reduces) loc_[x].kind = Loc::ROW;
+    regions_.push_back(std::move(rg));
+  }
+}
+
+void Planner::emit_row_region(int rid) {
+  const RowRegion& rg = regions_[rid];
+  RowParams P{};
+  P.rank = (int)rg.F.size();
+  for (int d = 0; d < P.rank; ++d) P.dims[d] = rg.F[d];
+  P.C = rg.F.back();
+  P.rows = 1;
+  for (int d = 0; d + 1 < P.rank; ++d) P.rows *= rg.F[d];
+  auto base = [&](int x) {  // resolve aliases to the member holding the value
+    while (rg.alias.count(x)) x = rg.alias.at(x);
+    return x;
+  };
+  // phases
+  std::map<int, int> phase, level;
+  std::vector<int> order;  // members in index order
+  for (int x : rg.full) order.push_back(x);
+  for (int x : rg.scalar) order.push_back(x);
+  for (int x : rg.reduces) order.push_back(x);
+  std::sort(order.begin(), order.end());
+  for (int x : order) {
+    const Node& n = g_.nodes[x];
+    if (rg.full.count(x)) {
+      int p = 0;
+      for (int o : n.in) {
+        if (is_splat(o)) continue;
+        int b = base(o);
+        if (rg.full.count(b)) p = std::max(p, phase[b]);
+        else if (rg.scalar.count(b) || rg.reduces.count(b)) p = std::max(p, level[b]);
+      }
+      phase[x] = p;
+    } else if (rg.reduces.count(x)) {
+      phase[x] = phase[n.in[0]];
+      level[x] = phase[x] + 1;
+    } else {
+      int l = 0;
+      for (int o : n.in) {
+        if (is_splat(o)) continue;
+        l = std::max(l, level[base(o)]);
+      }
+      level[x] = l;
+    }
+  }
+  int nphase = 1;
+  for (auto& kv : phase) nphase = std::max(nphase, kv.second + 1);
+  for (auto& kv : level) nphase = std::max(nphase, kv.second + 1);
+  if (nphase > RP_MAXPH) fail(E_INTERNAL, "row region has too many phases");
+  // scalar registers
+  std::map<int, int> sreg;
+  int next_sreg = RP_SREG0;
+  for (int x : order)
+    if (rg.scalar.count(x) || rg.reduces.count(x)) {
+      if (next_sreg >= RP_NREG) fail(E_INTERNAL, "row region needs too many per-row registers");
+      sreg[x] = next_sreg++;
+    }
+  // external inputs (shared by all phases)
+  std::map<int, int> in_index;
+  int64_t bytes = 0;
+  auto input_of = [&](int o) {
+    auto it = in_index.find(o);
+    if (it != in_index.end()) return it->second;
+    if (P.nin >= RP_MAXIN) fail(E_INTERNAL, "row region has too many inputs");
+    TView v = view_of(o);
+    EwIn& in = P.in[P.nin];
+    in.p = v.p;
+    in.dt = v.dt;
+    in.sel_dim = -1;
+    for (int d = 0; d < P.rank; ++d) in.stride[d] = d < v.rank ? v.stride[d] : 0;
+    bytes += g_.nodes[o].numel() * (int64_t)dt_size(g_.nodes[o].dt);
+    in_index[o] = P.nin;
+    return P.nin++;
+  };
+  int ncode = 0;
+  auto emit = [&](const EwInstr& I) {
+    if (ncode >= RP_MAXCODE) fail(E_INTERNAL, "row region program too long");
+    P.code[ncode++] = I;
+  };
+  auto opcode = [&](const Node& n, EwInstr& I) {
+    switch (n.op) {
+      case Op::Add: I.op = EW_ADD; break;
+      case Op::Sub: I.op = EW_SUB; break;
+      case Op::Mul: I.op = EW_MUL; break;
+      case Op::Div: I.op = EW_DIV; break;
+      case Op::Max: I.op = EW_MAX; break;
+      case Op::Min: I.op = EW_MIN; break;
+      case Op::Exp: I.op = EW_EXP; break;
+      case Op::Tanh: I.op = EW_TANH; break;
+      case Op::Sqrt: I.op = EW_SQRT; break;
+      case Op::Rsqrt: I.op = EW_RSQRT; break;
+      case Op::Sin: I.op = EW_SIN; break;
+      case Op::Cos: I.op = EW_COS; break;
+      case Op::Logistic: I.op = EW_LOGISTIC; break;
+      case Op::Neg: I.op = EW_NEG; break;
+      case Op::Abs: I.op = EW_ABS; break;
+      case Op::Convert: I.op = EW_CONVERT; I.aux = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
+      case Op::Compare: I.op = EW_CMP; I.aux = (uint8_t)n.i0; I.aux2 = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
+      case Op::Select: I.op = EW_SELECT; break;
+      default: fail(E_INTERNAL, "not an elementwise op in a row region");
+    }
+  };
+  std::vector<std::pair<int, int>> full_outs;  // (node, phase)
+  // materialised members (needed outside the region or returned)
+  auto materialised = [&](int x) {
+    for (int u : users_[x])
+      if (live_[u] && region_of_[u] != rid) return true;
+    for (int o : g_.outputs)
+      if (o == x) return true;
+    return false;
+  };
+  for (int ph = 0; ph < nphase; ++ph) {
+    RowPhase& Ph = P.ph[ph];
+    Ph.red_reg = -1;
+    Ph.lo = (uint16_t)ncode;
+    // roots: reduce inputs of this phase, materialised full members of this phase
+    std::vector<int> roots;
+    int red = -1;
+    for (int r : rg.reduces)
+      if (phase[r] == ph) {
+        if (red >= 0) fail(E_INTERNAL, "two reductions in one row phase");
+        red = r;
+        roots.push_back(g_.nodes[r].in[0]);
+      }
+    for (int x : rg.full)
+      if (phase[x] == ph && materialised(x)) roots.push_back(x);
+    std::set<int> need;
+    std::vector<int> st(roots.begin(), roots.end());
+    while (!st.empty()) {
+      int x = st.back();
+      st.pop_back();
+      if (need.count(x)) continue;
+      need.insert(x);
+      for (int o : g_.nodes[x].in) {
+        int b = base(o);
+        if (rg.full.count(b) && !is_splat(o)) st.push_back(b);
+      }
+    }
+    // per-element program (registers 0..RP_SREG0-1 with reuse)
+    std::map<int, int> reg;
+    std::map<int, int> last_use;
+    std::vector<int> list(need.begin(), need.end());
+    std::sort(list.begin(), list.end());
+    for (size_t k = 0; k < list.size(); ++k)
+      for (int o : g_.nodes[list[k]].in) last_use[base(o)] = (int)k;
+    std::set<int> pinned(roots.begin(), roots.end());
+    std::vector<int> freeregs;
+    for (int r = RP_SREG0 - 1; r >= 0; --r) freeregs.push_back(r);
+    auto alloc = [&]() {
+      if (freeregs.empty()) fail(E_INTERNAL, "row region needs too many registers");
+      int r = freeregs.back();
+      freeregs.pop_back();
+      return r;
+    };
+    std::map<int, int> load_reg, imm_reg;
+    for (size_t k = 0; k < list.size(); ++k) {
+      int x = list[k];
+      const Node& n = g_.nodes[x];
+      std::vector<int> regs;
+      for (int o : n.in) {
+        if (is_splat(o)) {
+          EwInstr I{};
+          I.op = EW_IMM;
+          I.dt = (uint8_t)kdt(g_.nodes[o].dt);
+          I.dst = (uint8_t)alloc();
+          I.fimm = (float)loc_[o].splat;
+          I.iimm = (int32_t)(int64_t)loc_[o].splat;
+          emit(I);
+          regs.push_back(I.dst);
+          continue;
+        }
+        int b = base(o);
+        if (rg.full.count(b)) {
+          regs.push_back(reg.at(b));
+        } else if (sreg.count(b)) {
+          regs.push_back(sreg.at(b));
+        } else {
+          auto it = load_reg.find(o);
+          if (it == load_reg.end()) {
+            EwInstr I{};
+            I.op = EW_LOAD;
+            int ii = input_of(o);
+            I.dt = (uint8_t)P.in[ii].dt;
+            I.aux = (uint8_t)ii;
+            I.dst = (uint8_t)alloc();
+            emit(I);
+            it = load_reg.emplace(o, I.dst).first;
+          }
+          regs.push_back(it->second);
+        }
+      }
+      EwInstr I{};
+      opcode(n, I);
+      I.dt = (uint8_t)kdt(n.dt);
+      if (regs.size() > 0) I.a = (uint8_t)regs[0];
+      if (regs.size() > 1) I.b = (uint8_t)regs[1];
+      if (regs.size() > 2) I.c = (uint8_t)regs[2];
+      I.dst = (uint8_t)alloc();
+      emit(I);
+      // immediates are single use; operand registers die at their last use
+      for (size_t q = 0; q < n.in.size(); ++q) {
+        int o = n.in[q];
+        if (is_splat(o)) { freeregs.push_back(regs[q]); continue; }
+        int b = base(o);
+        if (rg.full.count(b) && last_use[b] == (int)k && !pinned.count(b)) freeregs.push_back(reg[b]);
+      }
+      reg[x] = I.dst;
+    }
+    Ph.hi = (uint16_t)ncode;
+    if (red >= 0) {
+      const Node& rn = g_.nodes[red];
+      Ph.red_reg = (int8_t)reg.at(rn.in[0]);
+      Ph.red_kind = (uint8_t)rn.i0;
+      Ph.red_dst = (uint8_t)sreg.at(red);
+      Ph.red_dt = (uint8_t)kdt(rn.dt);
+      Ph.red_init = (float)loc_[rn.in[1]].splat;
+    }
+    for (int x : rg.full)
+      if (phase[x] == ph && materialised(x)) {
+        if (P.nout >= RP_MAXOUT) fail(E_INTERNAL, "row region has too many outputs");
+        RowOut& o = P.out[P.nout++];
+        o.p = slot_ptr(ensure_buf(x));
+        o.dt = kdt(g_.nodes[x].dt);
+        o.reg = (int16_t)reg.at(x);
+        o.phase = (int8_t)ph;
+        o.scalar = 0;
+        bytes += g_.nodes[x].numel() * (int64_t)dt_size(g_.nodes[x].dt);
+      }
+    // per-row program of the scalars that become available after this phase
+    Ph.slo = (uint16_t)ncode;
+    for (int x : order) {
+      if (!rg.scalar.count(x) || level[x] != ph + 1) continue;
+      const Node& n = g_.nodes[x];
+      std::vector<int> regs;
+      int tmp = 0;
+      for (int o : n.in) {
+        if (is_splat(o)) {
+          EwInstr I{};
+          I.op = EW_IMM;
+          I.dt = (uint8_t)kdt(g_.nodes[o].dt);
+          I.dst = (uint8_t)(tmp++);  // per-element registers are free between phases
+          I.fimm = (float)loc_[o].splat;
+          I.iimm = (int32_t)(int64_t)loc_[o].splat;
+          emit(I);
+          regs.push_back(I.dst);
+        } else {
+          regs.push_back(sreg.at(base(o)));
+        }
+      }
+      EwInstr I{};
+      opcode(n, I);
+      I.dt = (uint8_t)kdt(n.dt);
+      if (regs.size() > 0) I.a = (uint8_t)regs[0];
+      if (regs.size() > 1) I.b = (uint8_t)regs[1];
+      if (regs.size() > 2) I.c = (uint8_t)regs[2];
+      I.dst = (uint8_t)sreg.at(x);
+      emit(I);
+    }
+    Ph.shi = (uint16_t)ncode;
+  }
+  P.nphase = nphase;
+  for (int x : order)
+    if ((rg.scalar.count(x) || rg.reduces.count(x)) && materialised(x)) {
+      if (P.nout >= RP_MAXOUT) fail(E_INTERNAL, "row region has too many outputs");
+      RowOut& o = P.out[P.nout++];
+      o.p = slot_ptr(ensure_buf(x));
+      o.dt = kdt(g_.nodes[x].dt);
+      o.reg = (int16_t)sreg.at(x);
+      o.scalar = 1;
+      bytes += P.rows * (int64_t)dt_size(g_.nodes[x].dt);
+    }
+  std::string label = "row:" + g_.nodes[rg.root].name;
+  push(K_ROWNORM, blob_of(P), label, bytes);
 }
 
 void Planner::emit_attention(int d2) {
@@ -1090,6 +1529,10 @@ void Planner::emit_outputs() {
 
 void Planner::emit_unit(int u) {
   const Node& n = g_.nodes[u];
+  if (loc_[u].kind == Loc::ROW) {
+    emit_row_region(region_of_[u]);
+    return;
+  }
   if (loc_[u].kind == Loc::EW) {
     std::vector<int> members;
     for (size_t i = 0; i < g_.nodes.size(); ++i)
@@ -1110,6 +1553,7 @@ void Planner::emit_all() {
   for (int i = 0; i < N; ++i) {
     if (!live_[i]) continue;
     if (loc_[i].kind == Loc::EW) unit[i] = find(i);
+    else if (loc_[i].kind == Loc::ROW) unit[i] = regions_[region_of_[i]].root;
     else if (loc_[i].kind == Loc::BUF && g_.nodes[i].op != Op::Param && g_.nodes[i].op != Op::Constant) unit[i] = i;
   }
   std::map<int, std::set<int>> deps, rdeps;
@@ -1218,12 +1662,13 @@ void Planner::run() {
   mat_slot_.assign(N, -1);
   out_claim_.assign(N, -1);
   classify();
+  build_row_regions();
   // outputs produced by a kernel are written straight into the result buffer
   for (int k = 0; k < O_; ++k) {
     int n = g_.outputs[k];
     if (out_claim_[n] >= 0) continue;
     if ((loc_[n].kind == Loc::BUF && g_.nodes[n].op != Op::Param && g_.nodes[n].op != Op::Constant) ||
-        loc_[n].kind == Loc::EW)
+        loc_[n].kind == Loc::EW || loc_[n].kind == Loc::ROW)
       out_claim_[n] = k;
   }
   group_elementwise();

@@ -118,6 +118,33 @@ void verify_plan(const Plan& p) {
         }
         break;
       }
+      case K_ROWNORM: {
+        const RowParams& r = *(const RowParams*)b;
+        if (r.rows == 0) break;
+        for (int i = 0; i < r.nin; ++i) {
+          TView v{};
+          v.p = r.in[i].p;
+          v.dt = r.in[i].dt;
+          v.rank = r.rank;
+          for (int d = 0; d < r.rank; ++d) { v.shape[d] = r.dims[d]; v.stride[d] = r.in[i].stride[d]; }
+          c.view(v, "input");
+        }
+        for (int o = 0; o < r.nout; ++o)
+          c.region(r.out[o].p, (r.out[o].scalar ? r.rows : r.rows * r.C) * (int64_t)esz(r.out[o].dt), "output");
+        if (r.nphase < 1 || r.nphase > RP_MAXPH) fail(E_INTERNAL, "bad row phase count");
+        for (int ph = 0; ph < r.nphase; ++ph) {
+          const RowPhase& P = r.ph[ph];
+          if (P.lo > P.hi || P.hi > RP_MAXCODE || P.slo > P.shi || P.shi > RP_MAXCODE || P.red_reg >= RP_NREG ||
+              P.red_dst >= RP_NREG)
+            fail(E_INTERNAL, "bad row phase");
+        }
+        for (int k = 0; k < RP_MAXCODE; ++k) {
+          const EwInstr& I = r.code[k];
+          if (I.dst >= RP_NREG || I.a >= RP_NREG || I.b >= RP_NREG || I.c >= RP_NREG) fail(E_INTERNAL, "row register out of range");
+          if (I.op == EW_LOAD && I.aux >= r.nin) fail(E_INTERNAL, "row load of a missing input");
+        }
+        break;
+      }
       case K_GEMM: {
         const GemmParams& g = *(const GemmParams*)b;
         c.strided(g.a, g.a_dt, {{g.batch, g.a_sb}, {g.M, g.a_sm}, {g.K, g.a_sk}}, "lhs");

@@ -1,0 +1,61 @@
+"""The attention block printed by gqa-causal-attention / causal-self-attention
+(attention.clj:227-375) in isolation: the library's fused kernel (and, with
+fast kernels off, the generic path) against the numpy oracle."""
+import numpy as np
+import pytest
+
+from cljxla_b200.host import core, nn, runner
+from cljxla_b200.host import stablehlo as shlo
+from cljxla_b200.host import tensor as t
+from oracle import interp
+
+from conftest import has_gpu
+from parity import close
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not has_gpu():
+        pytest.skip("no CUDA device")
+    from cljxla_b200 import LIB_PATH
+    return core.init_backend(LIB_PATH)
+
+
+def _rand(shape, seed, scale=1.0):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return interp.f32_to_bf16_bits((rng.standard_normal(shape) * scale).astype(np.float32))
+
+
+@pytest.mark.parametrize("Sq,T,nq,nkv,softcap,window,dynamic", [
+    (1, 16, 4, 2, None, None, True),
+    (1, 40, 4, 2, 50.0, 6, True),
+    (5, 16, 4, 2, None, None, True),
+    (8, 16, 4, 2, None, 6, True),
+    (8, 16, 4, 2, None, None, False),
+    (3, 24, 2, 2, 50.0, None, True),
+    (8, 128, 8, 4, None, None, True),
+])
+def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic):
+    hd = 64
+    B = 1
+
+    def f(q, k, v, kc, vc, ow, pos):
+        p = pos if dynamic else 0
+        out, updated = nn.gqa_causal_attention(q, k, v, ow, nq, nkv, softcap, [kc, vc], p,
+                                               {"scale": 0.125, "sliding-window": window})
+        return [out, updated[0], updated[1]]
+    g = t.trace_graph("attn", [("q", ("tensor", (B, Sq, nq * hd), "bf16")), ("k", ("tensor", (B, Sq, nkv * hd), "bf16")),
+                               ("v", ("tensor", (B, Sq, nkv * hd), "bf16")),
+                               ("kc", ("tensor", (B, nkv, T, hd), "bf16")), ("vc", ("tensor", (B, nkv, T, hd), "bf16")),
+                               ("ow", ("tensor", (nq * hd, nq * hd), "bf16")), ("pos", ("tensor", (1,), "i32"))], f)
+    text = shlo.graph_to_mlir_text(g)
+    pos = np.array([min(T - Sq, 3)], np.int32) if dynamic else np.array([0], np.int32)
+    inputs = [_rand((B, Sq, nq * hd), 1), _rand((B, Sq, nkv * hd), 2), _rand((B, Sq, nkv * hd), 3),
+              _rand((B, nkv, T, hd), 4), _rand((B, nkv, T, hd), 5), _rand((nq * hd, nq * hd), 6, 0.05), pos]
+    want = interp.run_mlir(text, inputs)
+    got = runner.run_graph(ctx, g, inputs, text)
+    for i, ((shape, dt), a, b) in enumerate(zip(runner.out_specs(g), got, want)):
+        ok, excess, maxerr = close(a, b, dt)
+        assert ok, f"output {i} ({dt}{shape}) differs: max err {maxerr:.3g}, excess {excess:.3g}"
