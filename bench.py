@@ -58,6 +58,10 @@ def parse():
     p.add_argument("--cpu-steps", type=int, default=1)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tiny", action="store_true", help="reduced model for quick checks (not a bench line)")
+    p.add_argument("--decode-only", action="store_true",
+                   help="only the decode steps (zero caches, no prefill / e2e / profile): for ncu launch lists")
+    p.add_argument("--layers", type=int, default=0,
+                   help="override the layer count (small ncu captures; not a bench line)")
     return p.parse_args()
 
 
@@ -131,6 +135,8 @@ def model_setup(args):
     if args.tiny:
         cfg = dataclasses.replace(cfg, vocab=2048, d_model=256, layers=4, n_heads=4, n_kv_heads=2, head_dim=64,
                                   mlp=1024, window=64)
+    if args.layers:
+        cfg = dataclasses.replace(cfg, layers=args.layers)
     B, S = args.batch, args.prompt
     T = d.round_up(S + args.gen, 128)
     return cfg, B, S, T
@@ -208,7 +214,10 @@ def run_ours(args, rank, world, local_rank):
     p_pre = core.buffer_from_host_buffer(ctx, d.pos_inputs(cfg, "prefill", B, 0, S), [S], 4)
     pre_times = []
     kv = None
-    for rep in range(max(1, args.prefill_reps) + 1):
+    if args.decode_only:
+        kv = zero_kv()
+        pre_times = [float("nan")]
+    for rep in range(0 if args.decode_only else max(1, args.prefill_reps) + 1):
         kv0 = zero_kv()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -259,6 +268,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
+    if args.decode_only:
+        print(json.dumps({"decode_only": True, "ms_per_step": dec_s / args.steps * 1e3, "launches": launches}))
+        for b in kv + xs + ps + wbufs + [x_pre, p_pre]:
+            api.destroy_buffer(b)
+        return cfg, B, S, T, None
 
     # ---------------- decode end to end (host tokens in, logits out, host argmax)
     logits_bytes = B * cfg.vocab * 4
@@ -355,6 +369,8 @@ def main():
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     cfg, B, S, T, res = run_ours(args, rank, world, local_rank)
+    if res is None:
+        return
     if world > 1:
         t = torch.tensor([res["dec_s"], res["e2e_s"], res["prefill_s"]], device=f"cuda:{local_rank}")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -378,7 +394,8 @@ def main():
             "dtype": cfg.dtype,
             "data": "synthetic (random-init weights N(0,0.02), random token ids)",
             "config": {"workload": f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions"
-                                   + (" [tiny]" if args.tiny else ""),
+                                   + (" [tiny]" if args.tiny else "")
+                                   + (f" [{args.layers} layers]" if args.layers else ""),
                        "model": args.config, "global_batch": B * world, "seq_len": S, "kv_len": T,
                        "parallelism": f"dp{world} (independent replicas)",
                        "l2": "weights stream >> 126 MB L2 every step (no flush needed)"},

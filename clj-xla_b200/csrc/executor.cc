@@ -1,8 +1,10 @@
-// Executes a launch plan: refresh the argument table, replay the captured
-// CUDA graph (or launch eagerly the first time / when profiling).
+// Executes a launch plan: refresh the dynamic part of the argument table,
+// replay the captured CUDA graph (or launch eagerly the first time / when
+// profiling).  Also owns buffer storage and the version chains of in-place
+// KV updates (runtime.h).
 #include <cuda_runtime.h>
 
-#include <chrono>
+#include <algorithm>
 
 #include "runtime.h"
 
@@ -16,6 +18,61 @@ Counters& counters() {
 ProfileState& profile_state() {
   static ProfileState p;
   return p;
+}
+
+Storage::~Storage() {
+  if (ptr) cudaFreeAsync(ptr, client->stream);  // stream ordered after every reader
+}
+
+Version::~Version() {
+  if (undo) cudaFreeAsync(undo, client->stream);
+}
+
+PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims) {
+  auto* b = new PJRT_Buffer();
+  b->client = c;
+  b->dt = dt;
+  b->dims = dims;
+  b->bytes = (size_t)numel(dims) * dt_size(dt);
+  auto st = std::make_shared<Storage>();
+  st->client = c;
+  st->bytes = b->bytes;
+  if (b->bytes) {
+    cudaError_t e = cudaMallocAsync(&st->ptr, b->bytes, c->stream);
+    if (e != cudaSuccess) {
+      st->ptr = nullptr;
+      delete b;
+      CUDA_OK(e);
+    }
+  }
+  b->ver = std::make_shared<Version>();
+  b->ver->storage = st;
+  b->ver->client = c;
+  return b;
+}
+
+void ensure_current(PJRT_Buffer* b) {
+  if (b->current()) return;
+  // versions from b up to (not including) the head
+  std::vector<Version*> chain;
+  for (Version* v = b->ver.get(); v->newer; v = v->newer.get()) chain.push_back(v);
+  PJRT_Client* c = b->client;
+  auto st = std::make_shared<Storage>();
+  st->client = c;
+  st->bytes = b->bytes;
+  if (b->bytes) {
+    CUDA_OK(cudaMallocAsync(&st->ptr, b->bytes, c->stream));
+    CUDA_OK(cudaMemcpyAsync(st->ptr, b->ver->storage->ptr, b->bytes, cudaMemcpyDeviceToDevice, c->stream));
+    for (size_t i = chain.size(); i-- > 0;) {
+      Version* v = chain[i];
+      launch_undo_apply(st->ptr, v->undo, v->rank, v->out_shape, v->upd_shape, (int)v->dt, c->stream);
+    }
+    CUDA_OK(cudaGetLastError());
+  }
+  auto nv = std::make_shared<Version>();
+  nv->storage = st;
+  nv->client = c;
+  b->ver = nv;  // the old version node stays in the chain for older buffers
 }
 
 void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
@@ -32,24 +89,48 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
   }
 }
 
-namespace {
-
-void launch_all(PJRT_LoadedExecutable* ex, cudaStream_t s) {
-  for (const Launch& l : ex->plan->launches) run_launch(l, ex->d_argtab, s);
+void setup_variant(ExecVariant& v, void* arena) {
+  Plan& p = *v.plan;
+  if (!p.const_blob.empty()) {
+    CUDA_OK(cudaMalloc(&v.consts, p.const_blob.size()));
+    CUDA_OK(cudaMemcpy(v.consts, p.const_blob.data(), p.const_blob.size(), cudaMemcpyHostToDevice));
+  }
+  v.h_argtab.assign((size_t)p.argtab_size(), 0);
+  v.h_argtab[p.const_slot()] = (uint64_t)(uintptr_t)v.consts;
+  for (size_t b = 0; b < p.tmp_offsets.size(); ++b)
+    v.h_argtab[p.tmp_slot0() + b] = (uint64_t)(uintptr_t)arena + (uint64_t)p.tmp_offsets[b];
+  CUDA_OK(cudaMalloc(&v.d_argtab, v.h_argtab.size() * 8));
+  CUDA_OK(cudaMemcpy(v.d_argtab, v.h_argtab.data(), v.h_argtab.size() * 8, cudaMemcpyHostToDevice));
 }
 
-void launch_profiled(PJRT_LoadedExecutable* ex, cudaStream_t s) {
+void destroy_variant(ExecVariant& v) {
+  if (v.graph) cudaGraphExecDestroy(v.graph);
+  if (v.graph_def) cudaGraphDestroy(v.graph_def);
+  if (v.consts) cudaFree(v.consts);
+  if (v.d_argtab) cudaFree(v.d_argtab);
+  v = ExecVariant();
+}
+
+namespace {
+
+void launch_all(ExecVariant& v, cudaStream_t s) {
+  for (const Launch& l : v.plan->launches) run_launch(l, v.d_argtab, s);
+}
+
+void launch_profiled(ExecVariant& v, cudaStream_t s) {
   ProfileState& ps = profile_state();
-  std::vector<cudaEvent_t> evs(ex->plan->launches.size() + 1);
+  std::vector<cudaEvent_t> evs(v.plan->launches.size() + 1);
   for (auto& e : evs) CUDA_OK(cudaEventCreate(&e));
+  // the stream waits while the host enqueues, so events time kernels, not launch gaps
+  launch_stream_hold(std::min<int64_t>(200000000, 20000 * (int64_t)v.plan->launches.size()), s);
   CUDA_OK(cudaEventRecord(evs[0], s));
-  for (size_t i = 0; i < ex->plan->launches.size(); ++i) {
-    run_launch(ex->plan->launches[i], ex->d_argtab, s);
+  for (size_t i = 0; i < v.plan->launches.size(); ++i) {
+    run_launch(v.plan->launches[i], v.d_argtab, s);
     CUDA_OK(cudaEventRecord(evs[i + 1], s));
   }
   CUDA_OK(cudaEventSynchronize(evs.back()));
-  for (size_t i = 0; i < ex->plan->launches.size(); ++i) {
-    const Launch& l = ex->plan->launches[i];
+  for (size_t i = 0; i < v.plan->launches.size(); ++i) {
+    const Launch& l = v.plan->launches[i];
     float ms = 0;
     CUDA_OK(cudaEventElapsedTime(&ms, evs[i], evs[i + 1]));
     std::string key = std::string(kernel_kind_name(l.kind)) + "|" + l.label;
@@ -64,80 +145,123 @@ void launch_profiled(PJRT_LoadedExecutable* ex, cudaStream_t s) {
   for (auto& e : evs) cudaEventDestroy(e);
 }
 
+void run_variant(PJRT_Client* c, ExecVariant& v, cudaStream_t s) {
+  const Plan& p = *v.plan;
+  size_t dyn = (size_t)p.dyn_slots() * sizeof(uint64_t);
+  // pageable source: the driver stages it before returning, so h_argtab can be reused
+  if (dyn) CUDA_OK(cudaMemcpyAsync(v.d_argtab, v.h_argtab.data(), dyn, cudaMemcpyHostToDevice, s));
+  if (profile_state().enabled) {
+    launch_profiled(v, s);
+  } else if (c->opt.cuda_graphs && !v.graph_failed && v.runs >= 1) {
+    if (!v.graph) {
+      cudaGraph_t g = nullptr;
+      CUDA_OK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      launch_all(v, s);
+      cudaError_t e = cudaStreamEndCapture(s, &g);
+      if (e != cudaSuccess || !g) {
+        cudaGetLastError();
+        v.graph_failed = true;
+        launch_all(v, s);
+      } else {
+        v.graph_def = g;
+        if (cudaGraphInstantiate(&v.graph, g, 0) != cudaSuccess) {
+          cudaGetLastError();
+          v.graph = nullptr;
+          v.graph_failed = true;
+          launch_all(v, s);
+        }
+      }
+    }
+    if (v.graph) {
+      CUDA_OK(cudaGraphLaunch(v.graph, s));
+      counters().graph_launches++;
+    }
+  } else {
+    launch_all(v, s);
+  }
+  CUDA_OK(cudaGetLastError());
+  v.runs++;
+  counters().executions++;
+  counters().kernel_launches += (int64_t)p.launches.size();
+}
+
 }  // namespace
 
 void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs, PJRT_Buffer** outs) {
-  Plan& p = *ex->plan;
+  const Plan& p0 = *ex->copy.plan;
   PJRT_Client* c = ex->client;
   cudaStream_t s = c->stream;
-  if (nargs != p.params.size())
-    fail(E_INVALID, "executable " + p.name + " expects " + std::to_string(p.params.size()) + " arguments, got " +
+  if (nargs != p0.params.size())
+    fail(E_INVALID, "executable " + p0.name + " expects " + std::to_string(p0.params.size()) + " arguments, got " +
                         std::to_string(nargs));
   for (size_t i = 0; i < nargs; ++i) {
     PJRT_Buffer* b = args[i];
     if (!b) fail(E_INVALID, "null argument buffer " + std::to_string(i));
-    const TensorSpec& t = p.params[i];
+    const TensorSpec& t = p0.params[i];
     if (b->dt != t.dt || b->dims != t.shape)
       fail(E_INVALID, "argument " + std::to_string(i) + " has type " + dt_name(b->dt) + shape_str(b->dims) +
                           ", expected " + dt_name(t.dt) + shape_str(t.shape));
-    ex->h_argtab[i] = (uint64_t)(uintptr_t)b->ptr;
   }
-  std::vector<PJRT_Buffer*> created;
+  // a stale argument (an older version of an in-place updated buffer) is rebuilt first
+  for (size_t i = 0; i < nargs; ++i) ensure_current(args[i]);
+  // in place only when every updated argument is passed once and shares its storage with no other argument
+  bool inplace = ex->inplace.plan != nullptr;
+  if (inplace) {
+    for (const InplaceDus& d : ex->inplace.plan->inplace) {
+      const Storage* st = args[d.param]->ver->storage.get();
+      for (size_t j = 0; j < nargs && inplace; ++j)
+        if ((int)j != d.param && args[j]->ver->storage.get() == st) inplace = false;
+    }
+  }
+  ExecVariant& v = inplace ? ex->inplace : ex->copy;
+  const Plan& p = *v.plan;
+  for (size_t i = 0; i < nargs; ++i) v.h_argtab[i] = (uint64_t)(uintptr_t)args[i]->ptr();
+  std::vector<PJRT_Buffer*> created(p.outs.size(), nullptr);
+  std::vector<std::shared_ptr<Version>> new_heads(p.inplace.size());
+  std::vector<void*> undo(p.inplace.size(), nullptr);
   try {
     for (size_t k = 0; k < p.outs.size(); ++k) {
+      if (p.out_alias_param[k] >= 0) continue;
+      created[k] = new_buffer(c, p.outs[k].dt, p.outs[k].shape);
+      v.h_argtab[p.params.size() + k] = (uint64_t)(uintptr_t)created[k]->ptr();
+    }
+    for (size_t u = 0; u < p.inplace.size(); ++u) {
+      const InplaceDus& d = p.inplace[u];
+      PJRT_Buffer* src = args[d.param];
+      CUDA_OK(cudaMallocAsync(&undo[u], (size_t)d.undo_bytes, s));
+      v.h_argtab[d.undo_slot] = (uint64_t)(uintptr_t)undo[u];
+      v.h_argtab[p.params.size() + d.out] = (uint64_t)(uintptr_t)src->ptr();
       auto* b = new PJRT_Buffer();
-      created.push_back(b);
       b->client = c;
-      b->dt = p.outs[k].dt;
-      b->dims = p.outs[k].shape;
-      b->bytes = (size_t)p.outs[k].bytes();
-      if (b->bytes) CUDA_OK(cudaMallocAsync(&b->ptr, b->bytes, s));
-      ex->h_argtab[p.params.size() + k] = (uint64_t)(uintptr_t)b->ptr;
+      b->dt = p.outs[d.out].dt;
+      b->dims = p.outs[d.out].shape;
+      b->bytes = (size_t)p.outs[d.out].bytes();
+      b->ver = std::make_shared<Version>();
+      b->ver->storage = src->ver->storage;
+      b->ver->client = c;
+      created[d.out] = b;
+      new_heads[u] = b->ver;
     }
   } catch (...) {
-    for (auto* b : created) {
-      if (b->ptr) cudaFreeAsync(b->ptr, s);
-      delete b;
-    }
+    for (auto* b : created) delete b;
+    for (void* u : undo)
+      if (u) cudaFreeAsync(u, s);
     throw;
   }
-  // pageable source: the driver stages it before returning, so h_argtab can be reused
-  size_t dyn = (p.params.size() + p.outs.size()) * sizeof(uint64_t);
-  if (dyn) CUDA_OK(cudaMemcpyAsync(ex->d_argtab, ex->h_argtab.data(), dyn, cudaMemcpyHostToDevice, s));
-
-  if (profile_state().enabled) {
-    launch_profiled(ex, s);
-  } else if (c->opt.cuda_graphs && !ex->graph_failed && ex->runs >= 1) {
-    if (!ex->graph) {
-      cudaGraph_t g = nullptr;
-      CUDA_OK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-      launch_all(ex, s);
-      cudaError_t e = cudaStreamEndCapture(s, &g);
-      if (e != cudaSuccess || !g) {
-        cudaGetLastError();
-        ex->graph_failed = true;
-        launch_all(ex, s);
-      } else {
-        ex->graph_def = g;
-        if (cudaGraphInstantiate(&ex->graph, g, 0) != cudaSuccess) {
-          cudaGetLastError();
-          ex->graph = nullptr;
-          ex->graph_failed = true;
-          launch_all(ex, s);
-        }
-      }
+  run_variant(c, v, s);
+  // the arguments updated in place become versions one behind their results
+  for (size_t u = 0; u < p.inplace.size(); ++u) {
+    const InplaceDus& d = p.inplace[u];
+    Version* old = args[d.param]->ver.get();
+    old->newer = new_heads[u];
+    old->undo = undo[u];
+    old->rank = d.rank;
+    old->dt = d.dt;
+    for (int i = 0; i < d.rank; ++i) {
+      old->out_shape[i] = d.out_shape[i];
+      old->upd_shape[i] = d.upd_shape[i];
     }
-    if (ex->graph) {
-      CUDA_OK(cudaGraphLaunch(ex->graph, s));
-      counters().graph_launches++;
-    }
-  } else {
-    launch_all(ex, s);
   }
-  CUDA_OK(cudaGetLastError());
-  ex->runs++;
-  counters().executions++;
-  counters().kernel_launches += (int64_t)p.launches.size();
   for (size_t k = 0; k < created.size(); ++k) outs[k] = created[k];
 }
 

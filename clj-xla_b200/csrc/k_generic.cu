@@ -178,6 +178,24 @@ __global__ void dus_kernel(const __grid_constant__ DusParams P, const uint64_t* 
   if (P.in_place) {
     int64_t nu = 1;
     for (int d = 0; d < P.rank; ++d) nu *= P.upd_shape[d];
+    if (P.has_undo) {
+      // undo record: clamped start indices, then the window's previous values
+      char* ub = dres(P.undo, argtab);
+      if (blockIdx.x == 0 && threadIdx.x < CLJXLA_MAXR) ((int64_t*)ub)[threadIdx.x] = threadIdx.x < P.rank ? st[threadIdx.x] : 0;
+      char* old = ub + 8 * CLJXLA_MAXR;
+      for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nu; e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t rem = e, oo = 0, ostride = 1;
+        for (int d = P.rank - 1; d >= 0; --d) {
+          int64_t i = rem % P.upd_shape[d];
+          rem /= P.upd_shape[d];
+          oo += (st[d] + i) * ostride;
+          ostride *= P.out_shape[d];
+        }
+        st_elem(old, e, P.dt, ld_elem(out, oo, P.dt));  // same thread reads old then writes new
+        st_elem(out, oo, P.dt, ld_elem(upd, view_off(P.update, e), P.update.dt));
+      }
+      return;
+    }
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nu; e += (int64_t)gridDim.x * blockDim.x) {
       int64_t rem = e, oo = 0, ostride = 1;
       for (int d = P.rank - 1; d >= 0; --d) {
@@ -206,6 +224,30 @@ __global__ void dus_kernel(const __grid_constant__ DusParams P, const uint64_t* 
     uint32_t v = inside ? ld_elem(upd, view_off(P.update, ui), P.update.dt)
                         : ld_elem(opnd, view_off(P.operand, e), P.operand.dt);
     st_elem(out, e, P.dt, v);
+  }
+}
+
+struct UndoGeom {
+  int rank, dt;
+  int64_t out_shape[CLJXLA_MAXR], upd_shape[CLJXLA_MAXR];
+};
+
+__global__ void undo_apply_kernel(char* dst, const char* undo, UndoGeom G) {
+  const int64_t* st = (const int64_t*)undo;
+  const char* old = undo + 8 * CLJXLA_MAXR;
+  int64_t nu = 1;
+  for (int d = 0; d < G.rank; ++d) nu *= G.upd_shape[d];
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nu; e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t rem = e, oo = 0, ostride = 1;
+    for (int d = G.rank - 1; d >= 0; --d) {
+      int64_t i = rem % G.upd_shape[d];
+      rem /= G.upd_shape[d];
+      int64_t s = st[d];
+      s = s < 0 ? 0 : (s > G.out_shape[d] - G.upd_shape[d] ? G.out_shape[d] - G.upd_shape[d] : s);
+      oo += (s + i) * ostride;
+      ostride *= G.out_shape[d];
+    }
+    st_elem(dst, oo, G.dt, ld_elem(old, e, G.dt));
   }
 }
 
@@ -257,6 +299,21 @@ void launch_gather(const GatherParams& p, const uint64_t* argtab, cudaStream_t s
   int64_t g = p.n_rows < 65535 ? p.n_rows : 65535;
   gather_kernel<<<(int)g, 128, 0, s>>>(p, argtab);
 }
+void launch_undo_apply(void* dst, const void* undo, int rank, const int64_t* out_shape, const int64_t* upd_shape,
+                       int dt, cudaStream_t s) {
+  UndoGeom G{};
+  G.rank = rank;
+  G.dt = dt;
+  int64_t nu = 1;
+  for (int d = 0; d < rank; ++d) {
+    G.out_shape[d] = out_shape[d];
+    G.upd_shape[d] = upd_shape[d];
+    nu *= upd_shape[d];
+  }
+  if (nu == 0) return;
+  undo_apply_kernel<<<grid_for(nu, 256), 256, 0, s>>>((char*)dst, (const char*)undo, G);
+}
+
 void launch_dus(const DusParams& p, const uint64_t* argtab, cudaStream_t s) {
   int64_t n = p.n;
   if (p.in_place) {
@@ -266,5 +323,24 @@ void launch_dus(const DusParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (n == 0) return;
   dus_kernel<<<grid_for(n, 256), 256, 0, s>>>(p, argtab);
 }
+
+}  // namespace cljxla
+
+namespace cljxla {
+namespace {
+
+__global__ void stream_hold_kernel(int64_t ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (int i = 0; i < (1 << 22); ++i) {  // bounded: ends after ns or 2^22 sleeps
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if ((int64_t)(t - t0) >= ns) break;
+    __nanosleep(1000);
+  }
+}
+
+}  // namespace
+
+void launch_stream_hold(int64_t ns, cudaStream_t s) { stream_hold_kernel<<<1, 1, 0, s>>>(ns); }
 
 }  // namespace cljxla

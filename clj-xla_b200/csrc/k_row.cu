@@ -76,7 +76,11 @@ __global__ void __launch_bounds__(BLOCK) row_kernel(const __grid_constant__ RowP
 void launch_row(const RowParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.rows == 0) return;
   int64_t g = p.rows < 65535 ? p.rows : 65535;
-  if (p.C >= 1024) row_kernel<256><<<(int)g, 256, 0, s>>>(p, argtab);
+  // few rows (decode: one token) leave most SMs idle, so the row's columns are
+  // spread over as many threads as a CTA holds to shorten each phase
+  if (p.rows <= 296 && p.C >= 2048) row_kernel<1024><<<(int)g, 1024, 0, s>>>(p, argtab);
+  else if (p.rows <= 296 && p.C >= 512) row_kernel<512><<<(int)g, 512, 0, s>>>(p, argtab);
+  else if (p.C >= 1024) row_kernel<256><<<(int)g, 256, 0, s>>>(p, argtab);
   else if (p.C >= 256) row_kernel<128><<<(int)g, 128, 0, s>>>(p, argtab);
   else row_kernel<64><<<(int)g, 64, 0, s>>>(p, argtab);
 }

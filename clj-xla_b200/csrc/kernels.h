@@ -180,7 +180,20 @@ struct DusParams {       // out = operand with update written at clamped starts
   int32_t start_is_ptr[CLJXLA_MAXR];
   int64_t n;
   int32_t in_place;      // operand and out alias: only the update window is written
+  int32_t has_undo;      // in place over a caller's buffer: save the old window first
+  DPtr undo;             // [int64 starts[8]] + old window values (undo record)
 };
+
+// Restores a saved window (an undo record) into a buffer: versioned in-place
+// dynamic_update_slice, see runtime.h.
+void launch_undo_apply(void* dst, const void* undo, int rank, const int64_t* out_shape, const int64_t* upd_shape,
+                       int dt, cudaStream_t s);
+
+// Holds the stream for about `ns` nanoseconds (one thread sleeping on the
+// global timer, at most a fixed number of rounds).  Profiling enqueues it in
+// front of a step so that the step's launches run back to back on the device
+// instead of at the host's launch rate.
+void launch_stream_hold(int64_t ns, cudaStream_t s);
 
 // ------------------------------------------------------------------ GEMM
 // C[b][m][n] = sum_k A[b][m][k] * B[b][k][n]; A/B strided, C dense row-major.

@@ -140,7 +140,7 @@ PJRT_Error* Client_Create(void* a) {
     o.fuse = env_flag("CLJXLA_B200_FUSE", true);
     o.fast_kernels = env_flag("CLJXLA_B200_FAST_KERNELS", true);
     o.cuda_graphs = env_flag("CLJXLA_B200_CUDA_GRAPHS", true);
-    o.kv_in_place = env_flag("CLJXLA_B200_KV_IN_PLACE", false);
+    o.kv_in_place = env_flag("CLJXLA_B200_KV_IN_PLACE", true);
     if (const char* d = getenv("CLJXLA_B200_DEVICE")) o.device = atoi(d);
     size_t stride = sizeof(PJRT_NamedValue);
     if (args->num_options && args->create_options[0].struct_size >= sizeof(PJRT_NamedValue))
@@ -230,19 +230,18 @@ PJRT_Error* Client_Compile(void* a) {
     po.kv_in_place = c->opt.kv_in_place;
     auto ex = std::make_unique<PJRT_LoadedExecutable>();
     ex->client = c;
-    ex->plan = build_plan(*graph, po);
-    Plan& p = *ex->plan;
-    if (p.arena_bytes) CUDA_OK(cudaMalloc(&ex->arena, (size_t)p.arena_bytes));
-    if (!p.const_blob.empty()) {
-      CUDA_OK(cudaMalloc(&ex->consts, p.const_blob.size()));
-      CUDA_OK(cudaMemcpy(ex->consts, p.const_blob.data(), p.const_blob.size(), cudaMemcpyHostToDevice));
+    po.kv_in_place = false;
+    ex->copy.plan = build_plan(*graph, po);
+    if (c->opt.kv_in_place) {
+      po.kv_in_place = true;
+      auto ip = build_plan(*graph, po);
+      if (!ip->inplace.empty()) ex->inplace.plan = std::move(ip);
     }
-    ex->h_argtab.assign((size_t)p.argtab_size(), 0);
-    ex->h_argtab[p.const_slot()] = (uint64_t)(uintptr_t)ex->consts;
-    for (size_t b = 0; b < p.tmp_offsets.size(); ++b)
-      ex->h_argtab[p.tmp_slot0() + b] = (uint64_t)(uintptr_t)ex->arena + (uint64_t)p.tmp_offsets[b];
-    CUDA_OK(cudaMalloc(&ex->d_argtab, ex->h_argtab.size() * 8));
-    CUDA_OK(cudaMemcpy(ex->d_argtab, ex->h_argtab.data(), ex->h_argtab.size() * 8, cudaMemcpyHostToDevice));
+    int64_t arena = ex->copy.plan->arena_bytes;
+    if (ex->inplace.plan) arena = std::max(arena, ex->inplace.plan->arena_bytes);
+    if (arena) CUDA_OK(cudaMalloc(&ex->arena, (size_t)arena));
+    setup_variant(ex->copy, ex->arena);
+    if (ex->inplace.plan) setup_variant(ex->inplace, ex->arena);
     args->executable = ex.release();
   });
 }
@@ -269,16 +268,9 @@ PJRT_Error* Client_BufferFromHostBuffer(void* a) {
     }
     std::lock_guard<std::mutex> lk(c->mu);
     set_device(c);
-    auto b = std::make_unique<PJRT_Buffer>();
-    b->client = c;
-    b->dt = dt;
-    b->dims = dims;
-    b->bytes = bytes;
-    if (bytes) {
-      CUDA_OK(cudaMallocAsync(&b->ptr, bytes, c->stream));
-      if (!args->data) fail(E_INVALID, "null host data");
-      CUDA_OK(cudaMemcpyAsync(b->ptr, args->data, bytes, cudaMemcpyHostToDevice, c->stream));
-    }
+    if (bytes && !args->data) fail(E_INVALID, "null host data");
+    std::unique_ptr<PJRT_Buffer> b(new_buffer(c, dt, dims));
+    if (bytes) CUDA_OK(cudaMemcpyAsync(b->ptr(), args->data, bytes, cudaMemcpyHostToDevice, c->stream));
     // the host buffer may be released once this event completes
     args->done_with_host_buffer = new_event(c);
     args->buffer = b.release();
@@ -290,11 +282,8 @@ PJRT_Error* Buffer_Destroy(void* a) {
     auto* args = args_of<PJRT_Buffer_Destroy_Args>(a);
     PJRT_Buffer* b = args->buffer;
     if (!b) return;
-    if (b->ptr && b->owned) {
-      set_device(b->client);
-      CUDA_OK(cudaFreeAsync(b->ptr, b->client->stream));  // stream ordered after any reader
-    }
-    delete b;
+    set_device(b->client);
+    delete b;  // storage / undo records are released with their last version (stream ordered)
   });
 }
 
@@ -335,10 +324,11 @@ PJRT_Error* Buffer_ToHostBuffer(void* a) {
     }
     std::lock_guard<std::mutex> lk(b->client->mu);
     set_device(b->client);
+    ensure_current(b);
     // the reference host always passes numel*4 bytes (pjrt.clj:535) and reads
     // what it needs; copy the buffer's bytes, never more than dst_size
     size_t n = std::min(b->bytes, args->dst_size);
-    if (n) CUDA_OK(cudaMemcpyAsync(args->dst, b->ptr, n, cudaMemcpyDeviceToHost, b->client->stream));
+    if (n) CUDA_OK(cudaMemcpyAsync(args->dst, b->ptr(), n, cudaMemcpyDeviceToHost, b->client->stream));
     CUDA_OK(cudaStreamSynchronize(b->client->stream));
     args->event = nullptr;
   });
@@ -352,11 +342,9 @@ PJRT_Error* LoadedExecutable_Destroy(void* a) {
     if (!ex) return;
     set_device(ex->client);
     cudaStreamSynchronize(ex->client->stream);
-    if (ex->graph) cudaGraphExecDestroy(ex->graph);
-    if (ex->graph_def) cudaGraphDestroy(ex->graph_def);
+    destroy_variant(ex->copy);
+    destroy_variant(ex->inplace);
     if (ex->arena) cudaFree(ex->arena);
-    if (ex->consts) cudaFree(ex->consts);
-    if (ex->d_argtab) cudaFree(ex->d_argtab);
     delete ex;
   });
 }
@@ -365,7 +353,7 @@ PJRT_Error* Executable_NumOutputs(void* a) {
   return guarded([&] {
     auto* args = args_of<PJRT_Executable_NumOutputs_Args>(a);
     if (!args->executable) fail(E_INVALID, "null executable");
-    args->num_outputs = ((PJRT_LoadedExecutable*)args->executable)->plan->outs.size();
+    args->num_outputs = ((PJRT_LoadedExecutable*)args->executable)->copy.plan->outs.size();
   });
 }
 
@@ -458,15 +446,16 @@ size_t cljxla_b200_profile_dump(char* out, size_t cap) {
 
 int cljxla_b200_plan_info(const PJRT_LoadedExecutable* ex, int64_t* info, int n) {
   if (!ex || !info) return -1;
-  int64_t v[6] = {(int64_t)ex->plan->launches.size(), ex->plan->arena_bytes, ex->plan->n_nodes,
-                  ex->plan->n_live, ex->plan->n_fused_groups, (int64_t)ex->plan->const_blob.size()};
+  const Plan* pl = ex->inplace.plan ? ex->inplace.plan.get() : ex->copy.plan.get();  // the variant normally run
+  int64_t v[6] = {(int64_t)pl->launches.size(), pl->arena_bytes, pl->n_nodes,
+                  pl->n_live, pl->n_fused_groups, (int64_t)pl->const_blob.size()};
   for (int i = 0; i < n && i < 6; ++i) info[i] = v[i];
   return 0;
 }
 
 void* cljxla_b200_stream(const PJRT_Client* c) { return c ? (void*)c->stream : nullptr; }
 
-void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* b) { return b ? b->ptr : nullptr; }
+void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* b) { return b ? b->ptr() : nullptr; }
 
 }  // extern "C"
 
@@ -480,7 +469,8 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
   try {
     auto g = parse_mlir(text, len);
     PlanOptions po;
-    po.fuse = fuse != 0;
+    po.fuse = (fuse & 1) != 0;        // bit 0: fusion
+    po.kv_in_place = (fuse & 2) != 0;  // bit 1: in-place KV-cache updates
     auto p = build_plan(*g, po);
     int64_t v[6] = {(int64_t)p->launches.size(), p->arena_bytes, p->n_nodes, p->n_live, p->n_fused_groups,
                     (int64_t)p->const_blob.size()};

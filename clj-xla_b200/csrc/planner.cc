@@ -191,7 +191,8 @@ class Planner {
   const Graph& g_;
   PlanOptions opt_;
   Plan& plan_;
-  int P_ = 0, O_ = 0;
+  int P_ = 0, O_ = 0, U_ = 0;
+  std::map<int, int> inplace_of_;             // dynamic_update_slice node -> index in plan_.inplace
   std::vector<Loc> loc_;
   std::vector<char> live_;
   std::vector<std::vector<int>> users_;
@@ -207,7 +208,7 @@ class Planner {
   std::vector<int> tmp_first_, tmp_last_;     // liveness (launch indices)
 
   int find(int x) { while (uf_[x] != x) x = uf_[x] = uf_[uf_[x]]; return x; }
-  int tmp_slot(int b) const { return P_ + O_ + 1 + b; }
+  int tmp_slot(int b) const { return P_ + O_ + U_ + 1 + b; }
   int new_tmp(int64_t bytes) {
     tmp_bytes_.push_back(std::max<int64_t>(bytes, 1));
     tmp_first_.push_back((int)plan_.launches.size());
@@ -215,7 +216,7 @@ class Planner {
     return tmp_slot((int)tmp_bytes_.size() - 1);
   }
   void touch(int slot) {
-    int b = slot - (P_ + O_ + 1);
+    int b = slot - (P_ + O_ + U_ + 1);
     if (b >= 0) tmp_last_[b] = std::max(tmp_last_[b], (int)plan_.launches.size());
   }
   int view_root(int n) const {
@@ -280,7 +281,7 @@ void Planner::classify() {
       size_t off = (plan_.const_blob.size() + 255) & ~size_t(255);
       plan_.const_blob.resize(off + n.data.size());
       memcpy(plan_.const_blob.data() + off, n.data.data(), n.data.size());
-      L.slot = P_ + O_;  // const blob; offset recorded in splat field
+      L.slot = P_ + O_ + U_;  // const blob; offset recorded in splat field
       L.splat = (double)off;
       continue;
     }
@@ -961,16 +962,20 @@ void Planner::emit_row_region(int rid) {
       case Op::Convert: I.op = EW_CONVERT; I.aux = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
       case Op::Compare: I.op = EW_CMP; I.aux = (uint8_t)n.i0; I.aux2 = (uint8_t)kdt(g_.nodes[n.in[0]].dt); break;
       case Op::Select: I.op = EW_SELECT; break;
-      default: fail(E_INTERNAL, "not an elementwise op in a row region");
+      default: fail(E_INTERNAL, "not an elementwise op in a row region: " + n.name);
     }
   };
   std::vector<std::pair<int, int>> full_outs;  // (node, phase)
   // materialised members (needed outside the region or returned)
-  auto materialised = [&](int x) {
-    for (int u : users_[x])
-      if (live_[u] && region_of_[u] != rid) return true;
+  // (directly, or through an alias view that is used outside or returned)
+  std::function<bool(int)> materialised = [&](int x) {
     for (int o : g_.outputs)
       if (o == x) return true;
+    for (int u : users_[x]) {
+      if (!live_[u]) continue;
+      if (region_of_[u] != rid) return true;
+      if (rg.alias.count(u) && materialised(u)) return true;
+    }
     return false;
   };
   for (int ph = 0; ph < nphase; ++ph) {
@@ -984,7 +989,8 @@ void Planner::emit_row_region(int rid) {
       if (phase[r] == ph) {
         if (red >= 0) fail(E_INTERNAL, "two reductions in one row phase");
         red = r;
-        roots.push_back(g_.nodes[r].in[0]);
+        // a reduction of an external tensor reads it directly (loaded below)
+        if (rg.full.count(g_.nodes[r].in[0])) roots.push_back(g_.nodes[r].in[0]);
       }
     for (int x : rg.full)
       if (phase[x] == ph && materialised(x)) roots.push_back(x);
@@ -1069,6 +1075,21 @@ void Planner::emit_row_region(int rid) {
         if (rg.full.count(b) && last_use[b] == (int)k && !pinned.count(b)) freeregs.push_back(reg[b]);
       }
       reg[x] = I.dst;
+    }
+    if (red >= 0 && !rg.full.count(g_.nodes[red].in[0])) {
+      int o = g_.nodes[red].in[0];
+      auto it = load_reg.find(o);
+      if (it == load_reg.end()) {
+        EwInstr I{};
+        I.op = EW_LOAD;
+        int ii = input_of(o);
+        I.dt = (uint8_t)P.in[ii].dt;
+        I.aux = (uint8_t)ii;
+        I.dst = (uint8_t)alloc();
+        emit(I);
+        it = load_reg.emplace(o, I.dst).first;
+      }
+      reg[o] = it->second;
     }
     Ph.hi = (uint16_t)ncode;
     if (red >= 0) {
@@ -1337,6 +1358,17 @@ void Planner::emit_node_kernel(int id) {
       D.out = slot_ptr(oslot);
       D.n = n.numel();
       int64_t ub = up.numel() * (int64_t)dt_size(n.dt);
+      auto ip = inplace_of_.find(id);
+      if (ip != inplace_of_.end()) {
+        // in place over the argument's storage (the result slot points at it)
+        const InplaceDus& d = plan_.inplace[ip->second];
+        D.operand = dense_view(oslot, n.dt, n.shape);
+        D.in_place = 1;
+        D.has_undo = 1;
+        D.undo = slot_ptr(d.undo_slot);
+        push(K_DUS, blob_of(D), n.name, 2 * ub);
+        break;
+      }
       if (D.operand.dt == D.dt) {
         // copy the operand with the vectorised copy, then write the window in place
         CopyParams C{};
@@ -1661,6 +1693,44 @@ void Planner::run() {
   for (int i = 0; i < N; ++i) plan_.n_live += live_[i];
   mat_slot_.assign(N, -1);
   out_claim_.assign(N, -1);
+  if (opt_.kv_in_place) {
+    // KV-cache updates returned as results: run them in place over the
+    // argument's storage (the runtime versions the argument, see runtime.h)
+    for (int k = 0; k < O_; ++k) {
+      int n = g_.outputs[k];
+      const Node& nd = g_.nodes[n];
+      if (nd.op != Op::DUS || inplace_of_.count(n) || nd.rank() > CLJXLA_MAXR) continue;
+      int p = nd.in[0];
+      if (g_.nodes[p].op != Op::Param || g_.nodes[p].dt != nd.dt) continue;
+      int live_users = 0;
+      for (int u : users_[p]) live_users += live_[u] ? 1 : 0;
+      bool returned = false;
+      for (int o : g_.outputs) returned |= o == p;
+      if (live_users != 1 || returned) continue;
+      int pidx = -1;
+      for (int q = 0; q < P_; ++q)
+        if (g_.params[q] == p) pidx = q;
+      bool taken = false;
+      for (auto& d : plan_.inplace) taken |= d.param == pidx;
+      if (pidx < 0 || taken) continue;
+      const Node& up = g_.nodes[nd.in[1]];
+      InplaceDus d;
+      d.out = k;
+      d.param = pidx;
+      d.rank = nd.rank();
+      d.dt = nd.dt;
+      for (int i = 0; i < d.rank; ++i) {
+        d.out_shape[i] = nd.shape[i];
+        d.upd_shape[i] = up.shape[i];
+      }
+      d.undo_bytes = 8 * CLJXLA_MAXR + up.numel() * (int64_t)dt_size(nd.dt);
+      d.undo_slot = P_ + O_ + (int)plan_.inplace.size();
+      inplace_of_[n] = (int)plan_.inplace.size();
+      plan_.inplace.push_back(d);
+      plan_.out_alias_param[k] = pidx;
+    }
+    U_ = (int)plan_.inplace.size();
+  }
   classify();
   build_row_regions();
   // outputs produced by a kernel are written straight into the result buffer

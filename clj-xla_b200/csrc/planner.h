@@ -37,8 +37,21 @@ struct PlanOptions {
   bool kv_in_place = false;  // dynamic_update_slice results alias their operand storage
 };
 
+// A dynamic_update_slice executed in place over the storage of the caller's
+// argument `param`, producing result `out` (KV-cache update).  Before writing,
+// the kernel saves the window's old values into an undo record whose device
+// address comes from argument-table slot `undo_slot`.
+struct InplaceDus {
+  int out = -1, param = -1, undo_slot = -1;
+  int rank = 0;
+  DT dt = DT::BF16;
+  int64_t out_shape[CLJXLA_MAXR] = {}, upd_shape[CLJXLA_MAXR] = {};
+  int64_t undo_bytes = 0;
+};
+
 struct Plan {
   std::string name;
+  std::vector<InplaceDus> inplace;
   std::vector<TensorSpec> params, outs;
   std::vector<Launch> launches;
   int64_t arena_bytes = 0;
@@ -48,8 +61,9 @@ struct Plan {
   int n_nodes = 0, n_live = 0, n_fused_groups = 0;
   std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
   std::vector<int64_t> tmp_bytes;    // size of each scratch buffer
-  // argument table layout: [params][outputs][constant blob][scratch buffers]
-  int const_slot() const { return (int)(params.size() + outs.size()); }
+  // argument table layout: [params][outputs][undo records][constant blob][scratch buffers]
+  int dyn_slots() const { return (int)(params.size() + outs.size() + inplace.size()); }
+  int const_slot() const { return dyn_slots(); }
   int tmp_slot0() const { return const_slot() + 1; }
   int argtab_size() const { return tmp_slot0() + (int)tmp_offsets.size(); }
 };

@@ -1,4 +1,14 @@
 // Runtime objects behind the opaque PJRT handles.
+//
+// Buffers are versions of device storage.  Normally a buffer owns its storage
+// (one version, the head).  A KV-cache dynamic_update_slice executed in place
+// (planner.h InplaceDus) writes the new window into the argument's storage and
+// returns a result buffer that becomes the storage's new head; the argument
+// buffer keeps its PJRT meaning (inputs are not donated, pjrt.clj:478-480)
+// through an undo record - the window's previous values - chained to the
+// newer version.  Reading or re-using a stale buffer rebuilds its content into
+// fresh storage (copy of the head, undo records applied newest first); a
+// stale buffer the host destroys (the decode loop's old caches) costs nothing.
 #pragma once
 
 #include <atomic>
@@ -22,14 +32,36 @@ struct PJRT_Device {
 
 struct PJRT_Client;
 
+namespace cljxla {
+
+struct Storage {
+  PJRT_Client* client = nullptr;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  ~Storage();
+};
+
+struct Version {
+  std::shared_ptr<Storage> storage;
+  std::shared_ptr<Version> newer;  // null: this version is the storage's current content
+  void* undo = nullptr;            // undo record turning newer's content into this one's
+  int rank = 0;
+  DT dt = DT::BF16;
+  int64_t out_shape[CLJXLA_MAXR] = {}, upd_shape[CLJXLA_MAXR] = {};
+  PJRT_Client* client = nullptr;
+  ~Version();
+};
+
+}  // namespace cljxla
+
 struct PJRT_Buffer {
   PJRT_Client* client = nullptr;
   cljxla::DT dt = cljxla::DT::F32;
   std::vector<int64_t> dims;
-  void* ptr = nullptr;   // device memory (owned unless `alias` is set)
   size_t bytes = 0;
-  bool owned = true;
-  size_t nbytes() const { return bytes; }
+  std::shared_ptr<cljxla::Version> ver;
+  void* ptr() const { return ver && ver->storage ? ver->storage->ptr : nullptr; }
+  bool current() const { return !ver || !ver->newer; }
 };
 
 struct PJRT_Event {
@@ -38,10 +70,11 @@ struct PJRT_Event {
   std::string msg;
 };
 
-struct PJRT_LoadedExecutable {
-  PJRT_Client* client = nullptr;
-  std::unique_ptr<cljxla::Plan> plan;
-  void* arena = nullptr;
+namespace cljxla {
+
+// One compiled plan with its argument table and captured graph.
+struct ExecVariant {
+  std::unique_ptr<Plan> plan;
   void* consts = nullptr;
   uint64_t* d_argtab = nullptr;
   std::vector<uint64_t> h_argtab;
@@ -49,7 +82,16 @@ struct PJRT_LoadedExecutable {
   cudaGraph_t graph_def = nullptr;
   int runs = 0;
   bool graph_failed = false;
-  std::string hash;
+};
+
+}  // namespace cljxla
+
+struct PJRT_LoadedExecutable {
+  PJRT_Client* client = nullptr;
+  cljxla::ExecVariant copy;     // results in fresh buffers
+  cljxla::ExecVariant inplace;  // KV updates in place (when the graph has any); plan null otherwise
+  void* arena = nullptr;        // scratch shared by both variants (never active together)
+  const cljxla::Plan& plan() const { return *copy.plan; }
 };
 
 struct ClientOptions {
@@ -57,7 +99,7 @@ struct ClientOptions {
   bool fuse = true;
   bool fast_kernels = true;
   bool cuda_graphs = true;
-  bool kv_in_place = false;
+  bool kv_in_place = true;
 };
 
 struct PJRT_Client {
@@ -84,6 +126,12 @@ struct ProfileState {
 };
 ProfileState& profile_state();
 
+// New head-version buffer over fresh storage of `bytes` (stream-ordered allocation).
+PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims);
+// Rebuilds a stale buffer's content into fresh storage so it becomes a head.
+void ensure_current(PJRT_Buffer* b);
 void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs, PJRT_Buffer** outs);
+void setup_variant(ExecVariant& v, void* arena);
+void destroy_variant(ExecVariant& v);
 
 }  // namespace cljxla

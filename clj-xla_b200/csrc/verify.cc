@@ -19,8 +19,10 @@ struct Checker {
     if (slot < 0) return -1;
     if (slot < P) return p.params[slot].bytes();
     if (slot < P + O) return p.outs[slot - P].bytes();
-    if (slot == P + O) return (int64_t)p.const_blob.size();
-    int b = slot - (P + O + 1);
+    int U = (int)p.inplace.size();
+    if (slot < P + O + U) return p.inplace[slot - P - O].undo_bytes;
+    if (slot == P + O + U) return (int64_t)p.const_blob.size();
+    int b = slot - (P + O + U + 1);
     if (b < (int)p.tmp_bytes.size()) return p.tmp_bytes[b];
     return -1;
   }
@@ -112,6 +114,11 @@ void verify_plan(const Plan& p) {
         c.view(d.operand, "operand");
         c.view(d.update, "update");
         c.region(d.out, d.n * (int64_t)esz(d.dt), "output");
+        if (d.has_undo) {
+          int64_t nu = 1;
+          for (int i = 0; i < d.rank; ++i) nu *= d.upd_shape[i];
+          c.region(d.undo, 8 * CLJXLA_MAXR + nu * (int64_t)esz(d.dt), "undo record");
+        }
         for (int i = 0; i < d.rank; ++i) {
           if (d.upd_shape[i] > d.out_shape[i]) fail(E_INVALID, "dynamic_update_slice update larger than operand");
           if (d.start_is_ptr[i]) c.region(d.start_ptr[i], (int64_t)esz(d.start_dt[i]), "start index");

@@ -179,7 +179,8 @@ def plan_text(lib_path: str, text: str, fuse: bool = True) -> dict:
     b = text.encode()
     info = (ctypes.c_int64 * 6)()
     err = ctypes.create_string_buffer(4096)
-    rc = f(b, len(b), 1 if fuse else 0, info, 6, err, 4096)
+    flags = int(fuse) if not isinstance(fuse, bool) else (1 if fuse else 0)  # bit 0 fusion, bit 1 in-place KV
+    rc = f(b, len(b), flags, info, 6, err, 4096)
     if rc != 0:
         raise RuntimeError(f"plan failed ({rc}): {err.value.decode()}")
     keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes"]

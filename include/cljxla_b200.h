@@ -54,8 +54,10 @@ CLJXLA_EXPORT size_t cljxla_b200_profile_dump(char* out, size_t cap);
  * elementwise groups, constant bytes.  Returns 0 on success. */
 CLJXLA_EXPORT int cljxla_b200_plan_info(const PJRT_LoadedExecutable* exec, int64_t* info, int n);
 
-/* Parses and plans MLIR text on the host only (no device needed).  info as
- * above; returns 0 or a PJRT_Error_Code with the message in err[errcap]. */
+/* Parses and plans MLIR text on the host only (no device needed).  `fuse`
+ * holds flags: bit 0 enables fusion and the fast kernels, bit 1 plans
+ * KV-cache updates in place.  info as above; returns 0 or a PJRT_Error_Code
+ * with the message in err[errcap]. */
 CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, int64_t* info, int n, char* err,
                                         size_t errcap);
 
