@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
       s = run_chain(P, s);
       float mv = rnd_dt(s + mk[r], P.dt_m);
       if (mv > m[r]) {
-        float sc = __expf(m[r] - mv);  // m[r] = -inf first: 0
+        float sc = expf(m[r] - mv);  // m[r] = -inf first: 0
         if (m[r] == -INFINITY) sc = 0.f;
         l[r] *= sc;
 #pragma unroll
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
     float L = 0.f, A = 0.f;
     if (M != -INFINITY) {
       for (int w = 0; w < NW; ++w) {
-        float sc = wm[w][r] == -INFINITY ? 0.f : __expf(wm[w][r] - M);
+        float sc = wm[w][r] == -INFINITY ? 0.f : expf(wm[w][r] - M);
         L += wl[w][r] * sc;
         A += wacc[w][r][d] * sc;
       }
@@ -253,7 +253,7 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const 
         for (int s = 0; s < P.splits; ++s) {
           const float* pp = part + ((int64_t)s * rows_total + row) * (HD + 2);
           if (pp[0] == -INFINITY) continue;
-          float sc = __expf(pp[0] - M);
+          float sc = expf(pp[0] - M);
           L += pp[1] * sc;
           A += pp[2 + d] * sc;
         }

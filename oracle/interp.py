@@ -297,11 +297,18 @@ def _int_div(a, b):
 
 
 class Interpreter:
-    """Executes a parsed module; ``run`` returns the outputs (and optionally every SSA value)."""
+    """Executes a parsed module; ``run`` returns the outputs (and optionally every SSA value).
 
-    def __init__(self, text: str):
+    ``ulp_noise_seed``: when set, every f32 ``dot_general`` and sum-reduce
+    result is moved by one f32 ulp up or down at random (seeded) positions - a
+    model of a different, equally valid f32 summation order.  Tests use the spread it
+    causes as the noise floor of a whole bf16 model (see tests/parity.py).
+    """
+
+    def __init__(self, text: str, ulp_noise_seed=None):
         self.module = parse_module(text) if isinstance(text, str) else text
         self._consts: Dict[str, np.ndarray] = {}
+        self._noise = None if ulp_noise_seed is None else np.random.default_rng(ulp_noise_seed)
 
     def run(self, inputs: List[np.ndarray], keep_all: bool = False):
         m = self.module
@@ -423,10 +430,19 @@ class Interpreter:
         if name == "gather":
             return self._gather(op, args, shape, dt)
         if name == "reduce":
-            return self._reduce(op, args, shape, dt)
+            r = self._reduce(op, args, shape, dt)
+            return self._ulp_noise(r, dt) if op.body == "stablehlo.add" else r
         if name == "dot_general":
-            return self._dot(op, args, shape, dt)
+            return self._ulp_noise(self._dot(op, args, shape, dt), dt)
         raise NotImplementedError(f"oracle: op {name} not supported")
+
+    def _ulp_noise(self, r, dt):
+        if self._noise is None or dt != "f32":
+            return r
+        r = np.asarray(r, np.float32)
+        u = self._noise.integers(-1, 2, size=r.shape)
+        up, dn = np.nextafter(r, np.float32(np.inf)), np.nextafter(r, np.float32(-np.inf))
+        return np.where(u > 0, up, np.where(u < 0, dn, r)).astype(np.float32)
 
     def _gather(self, op, args, shape, dt):
         raw = op.attrs["raw"]
@@ -486,5 +502,5 @@ class Interpreter:
         return to_dtype(r.reshape(shape), dt)
 
 
-def run_mlir(text: str, inputs, keep_all=False):
-    return Interpreter(text).run(inputs, keep_all=keep_all)
+def run_mlir(text: str, inputs, keep_all=False, ulp_noise_seed=None):
+    return Interpreter(text, ulp_noise_seed).run(inputs, keep_all=keep_all)

@@ -36,6 +36,26 @@ def close_model(got, want, dt, rtol=None, frac=1e-3, rel_rms=1e-2):
     return (bad <= frac and rr <= rel_rms and not np.isnan(g).any()), bad, rr
 
 
+def close_model_floor(got, want, floors, dt, margin=2.0):
+    """``close_model`` with a measured noise floor.
+
+    ``floors`` are the same outputs from oracle runs whose f32 dot / sum
+    results were moved by one ulp at random (a different, equally valid f32
+    summation order).  Whole bf16 models with scale-1.0 QK-normed attention
+    amplify such 1-ulp differences into visible logit changes (a flipped bf16
+    score rounding moves a softmax weight by tens of percent), so the device
+    result passes when it is no further from the oracle than ``margin`` times
+    the oracle's own spread.  Returns (ok, bad_fraction, rel_rms, floor_bad, floor_rr)."""
+    ok, bad, rr = close_model(got, want, dt)
+    fb = fr = 0.0
+    for f in floors:
+        _, b2, r2 = close_model(f, want, dt)
+        fb, fr = max(fb, b2), max(fr, r2)
+    if not ok and not np.isnan(as_f32(np.asarray(got), dt)).any():
+        ok = bad <= max(1e-3, margin * fb) and rr <= max(1e-2, margin * fr)
+    return ok, bad, rr, fb, fr
+
+
 def close(got, want, dt, rtol=None, atol_scale=1.0):
     """Returns (ok, worst_excess, max_abs_err)."""
     if dt in ("i32", "i1", "i8"):

@@ -106,3 +106,19 @@ def test_decode_step_continues_prefill():
     a, b = out2[0][0, 0], ref[0][0, S]
     rms = float(np.sqrt(np.mean(np.square(b.astype(np.float64)))))
     assert approx_equal(a, b, atol=5e-2 * rms, rtol=5e-2)
+
+
+def test_ulp_noise_moves_f32_dots_by_at_most_one_ulp():
+    """The noise-floor option of the oracle perturbs f32 dot results by one ulp
+    at most, and leaves bf16 results and everything else untouched."""
+    g = t.trace_graph("nz", [("a", ("tensor", (4, 64), "f32")), ("b", ("tensor", (64, 32), "f32"))],
+                      lambda a, b: [t.matmul(a, b), t.add(a, a)])
+    text = shlo.graph_to_mlir_text(g)
+    rng = np.random.Generator(np.random.PCG64(0))
+    a = rng.standard_normal((4, 64)).astype(np.float32)
+    b = rng.standard_normal((64, 32)).astype(np.float32)
+    base = interp.run_mlir(text, [a, b])
+    noisy = interp.run_mlir(text, [a, b], ulp_noise_seed=5)
+    gap = np.abs(noisy[0].astype(np.float64) - base[0]) / np.spacing(np.abs(base[0]))
+    assert gap.max() <= 1.0 + 1e-9 and (gap > 0).any()
+    np.testing.assert_array_equal(noisy[1], base[1])
