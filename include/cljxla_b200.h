@@ -67,6 +67,39 @@ CLJXLA_EXPORT void* cljxla_b200_stream(const PJRT_Client* client);
 /* Device address backing a buffer. */
 CLJXLA_EXPORT void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* buffer);
 
+/* Size of the fixed device scratch used by cljxla_b200_attention_decode_static. */
+#define CLJXLA_STATIC_ATTN_SCRATCH_BYTES (1u << 20)
+
+/* Decode attention of one layer that allocates no device memory.  No
+ * counterpart in the reference: it is the split-KV kernel an executable uses
+ * for the printed attention block (attention.clj:343-365), callable directly
+ * by hosts that cannot allocate at that point (all free memory already handed
+ * to a KV pool, allocator callbacks, code that must not grow the memory pool).
+ *
+ *   q        bf16 [batch, q_heads, 1, head_dim]          (device)
+ *   k_cache  bf16 [batch, kv_heads, positions, head_dim] (device, head_dim/16-byte aligned)
+ *   v_cache  bf16 [batch, kv_heads, positions, head_dim] (device, same alignment)
+ *   mask     f32  [positions] additive mask shared by every batch row and head (device)
+ *   out      f32  [batch, q_heads, 1, head_dim]          (device)
+ *
+ * scores = bf16(bf16(q.k) * bf16(scale)) + mask, softmax in f32, out = p.v:
+ * the printed graph's op order and roundings.  head_dim in {32,64,128,256},
+ * q_heads a multiple of kv_heads with at most 8 per KV head.  Work is enqueued
+ * on `stream` (a cudaStream_t; NULL = legacy default stream) of the calling
+ * thread's current device.
+ *
+ * Partial results live in one file-scope device array per device of
+ * CLJXLA_STATIC_ATTN_SCRATCH_BYTES; calls needing more
+ * (splits * batch * q_heads * (head_dim + 2) * 4 bytes) are rejected before
+ * anything runs.  Nothing in it has to start at zero.  Calls that may overlap
+ * on the device race on the scratch.  The first call on each device looks up
+ * the scratch address (and may load the module): make it before any stream
+ * capture.  Returns 0, or a PJRT_Error_Code with the message in err[errcap]. */
+CLJXLA_EXPORT int cljxla_b200_attention_decode_static(const void* q, const void* k_cache, const void* v_cache,
+                                                      const float* mask, void* out, int64_t batch, int64_t q_heads,
+                                                      int64_t kv_heads, int64_t positions, int64_t head_dim,
+                                                      float scale, void* stream, char* err, size_t errcap);
+
 #ifdef __cplusplus
 }
 #endif
