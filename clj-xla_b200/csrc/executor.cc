@@ -6,6 +6,8 @@
 
 #include <algorithm>
 
+#include "fast_kernels.h"
+#include "jit.h"
 #include "runtime.h"
 
 namespace cljxla {
@@ -75,8 +77,26 @@ void ensure_current(PJRT_Buffer* b) {
   b->ver = nv;  // the old version node stays in the chain for older buffers
 }
 
+void prepare_jit(Plan& p) {
+  if (!jit_enabled()) return;
+  std::vector<std::string> src;
+  std::vector<Launch*> targets;
+  for (Launch& l : p.launches) {
+    std::string s;
+    if (!jit_describe(l, &s, &l.jit_grid, &l.jit_block, &l.jit_cluster, &l.jit_args)) continue;
+    src.push_back(std::move(s));
+    targets.push_back(&l);
+  }
+  std::vector<void*> fns = jit_compile(src);
+  for (size_t i = 0; i < targets.size(); ++i) targets[i]->jit_fn = fns[i];
+}
+
 void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
   const void* b = l.blob.data();
+  if (l.jit_fn) {
+    jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, argtab, l.jit_args, s);
+    return;
+  }
   switch (l.kind) {
     case K_EW: launch_ew(*(const EwParams*)b, argtab, s); break;
     case K_REDUCE: launch_reduce(*(const ReduceParams*)b, argtab, s); break;
@@ -99,6 +119,15 @@ void setup_variant(ExecVariant& v, void* arena) {
   v.h_argtab[p.const_slot()] = (uint64_t)(uintptr_t)v.consts;
   for (size_t b = 0; b < p.tmp_offsets.size(); ++b)
     v.h_argtab[p.tmp_slot0() + b] = (uint64_t)(uintptr_t)arena + (uint64_t)p.tmp_offsets[b];
+  if (!p.tmaps.empty()) {
+    CUDA_OK(cudaMalloc(&v.d_tmaps, (size_t)p.tmap_table_bytes()));
+    CUDA_OK(cudaMemset(v.d_tmaps, 0, (size_t)p.tmap_table_bytes()));
+    CUDA_OK(cudaMallocHost(&v.status_host, sizeof(unsigned)));
+    *v.status_host = 0;
+    v.h_tmaps.assign((size_t)p.tmap_table_bytes() / 8, 0);
+    v.tmap_addr.assign(p.tmaps.size(), ~0ull);
+    v.h_argtab[p.tmap_slot()] = (uint64_t)(uintptr_t)v.d_tmaps;
+  }
   CUDA_OK(cudaMalloc(&v.d_argtab, v.h_argtab.size() * 8));
   CUDA_OK(cudaMemcpy(v.d_argtab, v.h_argtab.data(), v.h_argtab.size() * 8, cudaMemcpyHostToDevice));
 }
@@ -108,8 +137,36 @@ void destroy_variant(ExecVariant& v) {
   if (v.graph_def) cudaGraphDestroy(v.graph_def);
   if (v.consts) cudaFree(v.consts);
   if (v.d_argtab) cudaFree(v.d_argtab);
+  if (v.d_tmaps) cudaFree(v.d_tmaps);
+  if (v.status_host) cudaFreeHost(v.status_host);
   v = ExecVariant();
 }
+
+namespace {
+
+// Re-encodes the tensor maps whose operand address changed since the last run
+// and uploads the table (stream-ordered before the run's kernels).
+void refresh_tmaps(ExecVariant& v, cudaStream_t s) {
+  const Plan& p = *v.plan;
+  if (p.tmaps.empty()) return;
+  if (*v.status_host)
+    fail(E_INTERNAL, "a tensor-core GEMM wait timed out in an earlier execution (status " +
+                         std::to_string(*v.status_host) + ")");
+  bool changed = false;
+  for (size_t i = 0; i < p.tmaps.size(); ++i) {
+    const TmapSpec& t = p.tmaps[i];
+    uint64_t addr = t.base.slot >= 0 ? v.h_argtab[t.base.slot] + (uint64_t)t.base.off : (uint64_t)t.base.off;
+    if (addr == v.tmap_addr[i]) continue;
+    encode_tmap_bf16(&v.h_tmaps[16 * i], (const void*)(uintptr_t)addr, t.inner, t.outer, t.row_bytes, t.box_inner,
+                     t.box_outer);
+    v.tmap_addr[i] = addr;
+    changed = true;
+  }
+  // pageable source: staged by the driver before the call returns
+  if (changed) CUDA_OK(cudaMemcpyAsync(v.d_tmaps, v.h_tmaps.data(), 128 * p.tmaps.size(), cudaMemcpyHostToDevice, s));
+}
+
+}  // namespace
 
 namespace {
 
@@ -150,6 +207,7 @@ void run_variant(PJRT_Client* c, ExecVariant& v, cudaStream_t s) {
   size_t dyn = (size_t)p.dyn_slots() * sizeof(uint64_t);
   // pageable source: the driver stages it before returning, so h_argtab can be reused
   if (dyn) CUDA_OK(cudaMemcpyAsync(v.d_argtab, v.h_argtab.data(), dyn, cudaMemcpyHostToDevice, s));
+  refresh_tmaps(v, s);
   if (profile_state().enabled) {
     launch_profiled(v, s);
   } else if (c->opt.cuda_graphs && !v.graph_failed && v.runs >= 1) {
@@ -180,6 +238,9 @@ void run_variant(PJRT_Client* c, ExecVariant& v, cudaStream_t s) {
     launch_all(v, s);
   }
   CUDA_OK(cudaGetLastError());
+  if (v.status_host)  // checked at the next execution
+    CUDA_OK(cudaMemcpyAsync(v.status_host, (char*)v.d_tmaps + 128 * p.tmaps.size(), sizeof(unsigned),
+                            cudaMemcpyDeviceToHost, s));
   v.runs++;
   counters().executions++;
   counters().kernel_launches += (int64_t)p.launches.size();

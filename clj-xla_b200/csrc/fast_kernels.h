@@ -18,6 +18,27 @@ struct GemvParams {
 
 using RegionFn = std::function<void(const DPtr&, int64_t, const char*)>;
 
+// Tensor-core GEMM (k_gemm_tc.cu): C[M, N] = A[M, K] . B[N, K]^T, bf16
+// operands with unit K stride, C dense row-major in c_dt (bf16 / f32).  The
+// two tensor maps and the status word live in the executable's tensor-map
+// table (Plan::tmaps); `a` / `b` / `a_ld` / `b_ld` tell the executor what to
+// encode into them.
+struct TcGemmParams {
+  DPtr c, tmap_a, tmap_b, status;
+  DPtr a, b;
+  int64_t a_ld, b_ld;  // row strides in elements
+  int32_t M, N, K, c_dt;
+  int32_t tmap_a_index, tmap_b_index;
+};
+
+void launch_tc_gemm(const TcGemmParams& p, const uint64_t* argtab, cudaStream_t s);
+bool make_tc_gemm(const GemmParams& g, TcGemmParams& out);
+void verify_tc_gemm(const TcGemmParams& p, const RegionFn& region);
+void tc_gemm_tile_shape(int* bm, int* bn, int* bk);
+// Encodes a 2-D bf16 tensor map (128-byte swizzle) into out128.
+void encode_tmap_bf16(void* out128, const void* base, int64_t inner, int64_t outer, int64_t row_bytes, int box_inner,
+                      int box_outer);
+
 void launch_gemv(const GemvParams& p, const uint64_t* argtab, cudaStream_t s);
 bool make_gemv(const GemmParams& g, Launch& out);
 void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region);

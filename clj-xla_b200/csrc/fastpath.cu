@@ -8,6 +8,7 @@ void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     case K_GEMV: launch_gemv(*(const GemvParams*)l.blob.data(), argtab, s); break;
     case K_ATTN_DECODE: launch_attention(*(const AttnParams*)l.blob.data(), argtab, s); break;
     case K_ATTN_COMBINE: launch_attention_combine(*(const AttnParams*)l.blob.data(), argtab, s); break;
+    case K_GEMM_TC: launch_tc_gemm(*(const TcGemmParams*)l.blob.data(), argtab, s); break;
     default: fail(E_INTERNAL, std::string("no launcher for kernel kind ") + kernel_kind_name(l.kind));
   }
 }
@@ -16,6 +17,14 @@ void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& reg
   switch (l.kind) {
     case K_GEMV: verify_gemv(p, l, region); break;
     case K_ATTN_DECODE: case K_ATTN_COMBINE: verify_attention(l, region); break;
+    case K_GEMM_TC: {
+      const TcGemmParams& t = *(const TcGemmParams*)l.blob.data();
+      if (t.tmap_a_index < 0 || t.tmap_b_index < 0 || t.tmap_a_index >= (int)p.tmaps.size() ||
+          t.tmap_b_index >= (int)p.tmaps.size() || t.tmap_a.slot != p.tmap_slot())
+        fail(E_INTERNAL, "tensor-core GEMM tensor maps not placed");
+      verify_tc_gemm(t, region);
+      break;
+    }
     default: fail(E_INTERNAL, std::string("no bounds verifier for kernel kind ") + kernel_kind_name(l.kind));
   }
 }

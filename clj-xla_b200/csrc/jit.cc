@@ -1,0 +1,603 @@
+// Code generation and NVRTC compilation of fused kernels (see jit.h).
+//
+// The generated code is a transliteration of the interpreting kernels
+// (ew_exec.cuh, k_generic.cu ew_kernel, k_row.cu row_kernel): the same
+// per-op arithmetic, the same rounding to each op's printed element type,
+// the same index decomposition and the same reduction order, with the
+// program, shapes, strides and types fixed at compile time.
+#include "jit.h"
+
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <thread>
+
+namespace cljxla {
+namespace {
+
+// ------------------------------------------------------------------ prelude
+const char* kPrelude = R"PRELUDE(
+typedef unsigned int u32;
+typedef long long i64;
+typedef unsigned long long u64;
+__device__ __forceinline__ unsigned short f2bf(float x) { unsigned short r; asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(x)); return r; }
+__device__ __forceinline__ unsigned short f2h(float x) { unsigned short r; asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(x)); return r; }
+__device__ __forceinline__ float h2f(unsigned short h) { float r; asm("cvt.f32.f16 %0, %1;" : "=f"(r) : "h"(h)); return r; }
+__device__ __forceinline__ float rbf(float x) { return __uint_as_float((u32)f2bf(x) << 16); }
+__device__ __forceinline__ float rh(float x) { return h2f(f2h(x)); }
+__device__ __forceinline__ float F(u32 v) { return __uint_as_float(v); }
+__device__ __forceinline__ u32 U(float v) { return __float_as_uint(v); }
+__device__ __forceinline__ float fmax_nan(float x, float y) { return (x != x || y != y) ? __int_as_float(0x7fc00000) : fmaxf(x, y); }
+__device__ __forceinline__ float fmin_nan(float x, float y) { return (x != x || y != y) ? __int_as_float(0x7fc00000) : fminf(x, y); }
+// float -> i32 with truncation toward zero and saturation (NaN -> 0)
+__device__ __forceinline__ int f2i_sat(float f) {
+  if (f != f) return 0;
+  if (f >= 2147483647.0f) return 2147483647;
+  if (f <= -2147483648.0f) return (int)0x80000000;
+  return (int)f;
+}
+__device__ __forceinline__ u32 cluster_rank() { u32 r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* p, u32 rank) {
+  u32 a = (u32)__cvta_generic_to_shared(p), b; float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(b) : "r"(a), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(b) : "memory");
+  return v;
+}
+)PRELUDE";
+
+bool is_float(int dt) { return dt == KDT_F32 || dt == KDT_BF16 || dt == KDT_F16 || dt == KDT_F64; }
+
+std::string round_expr(const std::string& f, int dt) {
+  if (dt == KDT_BF16) return "rbf(" + f + ")";
+  if (dt == KDT_F16) return "rh(" + f + ")";
+  return f;
+}
+std::string fbits(const std::string& f, int dt) { return "U(" + round_expr(f, dt) + ")"; }
+
+std::string hex32(uint32_t v) {
+  char b[16];
+  snprintf(b, sizeof b, "0x%08xu", v);
+  return b;
+}
+
+// buffer k of the launch: argument-table slot a.s[k] plus byte offset a.o[k]
+// (a negative slot: a.o[k] is the address), so that programs that differ only
+// in which buffers they touch compile to one kernel
+std::string base_expr(int k) {
+  std::ostringstream s;
+  s << "((char*)(a.s[" << k << "] >= 0 ? argtab[a.s[" << k << "]] + (u64)a.o[" << k << "] : (u64)a.o[" << k << "]))";
+  return s.str();
+}
+
+std::string args_struct() {
+  return "struct JitArgs { int s[" + std::to_string(JIT_MAXBUF) + "]; int pad; long long o[" +
+         std::to_string(JIT_MAXBUF) + "]; };\n";
+}
+
+std::string load_expr(const std::string& base, const std::string& off, int dt) {
+  const std::string o = "[" + off + "]";
+  switch (dt) {
+    case KDT_F32: return "U(((const float*)" + base + ")" + o + ")";
+    case KDT_BF16: return "((u32)((const unsigned short*)" + base + ")" + o + " << 16)";
+    case KDT_F16: return "U(h2f(((const unsigned short*)" + base + ")" + o + "))";
+    case KDT_I32: case KDT_U32: return "(u32)((const int*)" + base + ")" + o;
+    case KDT_I8: return "(u32)(int)((const signed char*)" + base + ")" + o;
+    case KDT_U8: return "(u32)((const unsigned char*)" + base + ")" + o;
+    case KDT_I16: return "(u32)(int)((const short*)" + base + ")" + o;
+    case KDT_I1: return "(((const unsigned char*)" + base + ")" + o + " ? 1u : 0u)";
+    case KDT_I64: return "(u32)(int)((const long long*)" + base + ")" + o;
+    case KDT_F64: return "U((float)((const double*)" + base + ")" + o + ")";
+  }
+  fail(E_INTERNAL, "jit: load of an unknown element type");
+}
+
+std::string store_stmt(const std::string& base, const std::string& off, int dt, const std::string& v) {
+  const std::string o = "[" + off + "]";
+  switch (dt) {
+    case KDT_F32: return "((float*)" + base + ")" + o + " = F(" + v + ");";
+    case KDT_BF16: return "((unsigned short*)" + base + ")" + o + " = f2bf(F(" + v + "));";
+    case KDT_F16: return "((unsigned short*)" + base + ")" + o + " = f2h(F(" + v + "));";
+    case KDT_I32: case KDT_U32: return "((int*)" + base + ")" + o + " = (int)" + v + ";";
+    case KDT_I8: return "((signed char*)" + base + ")" + o + " = (signed char)(int)" + v + ";";
+    case KDT_U8: return "((unsigned char*)" + base + ")" + o + " = (unsigned char)" + v + ";";
+    case KDT_I16: return "((short*)" + base + ")" + o + " = (short)(int)" + v + ";";
+    case KDT_I1: return "((unsigned char*)" + base + ")" + o + " = " + v + " ? 1 : 0;";
+    case KDT_I64: return "((long long*)" + base + ")" + o + " = (long long)(int)" + v + ";";
+    case KDT_F64: return "((double*)" + base + ")" + o + " = (double)F(" + v + ");";
+  }
+  fail(E_INTERNAL, "jit: store of an unknown element type");
+}
+
+std::string convert_expr(const std::string& v, int from, int to) {
+  const bool ff = is_float(from), tf = is_float(to);
+  if (to == KDT_I1) return ff ? "(F(" + v + ") != 0.0f ? 1u : 0u)" : "(" + v + " != 0u ? 1u : 0u)";
+  if (ff && tf) return fbits("F(" + v + ")", to);
+  if (!ff && tf) return fbits(from == KDT_U32 ? "(float)" + v : "(float)(int)" + v, to);
+  std::string r = ff ? "f2i_sat(F(" + v + "))" : "(int)" + v;
+  if (to == KDT_I8) r = "(int)(signed char)" + r;
+  else if (to == KDT_U8) r = "(int)(unsigned char)" + r;
+  else if (to == KDT_I16) r = "(int)(short)" + r;
+  return "(u32)(" + r + ")";
+}
+
+// Emits one program step as "u32 <name> = ...;".  reg[] maps register -> the
+// expression currently holding it; x[] names the loop index per dimension.
+struct Emitter {
+  std::ostringstream& s;
+  const EwIn* ins;
+  int rank;
+  std::vector<std::string> x;  // index variable per loop dim
+  std::vector<std::string> in_base;
+  int counter = 0;
+
+  std::string reg_or_zero(const std::vector<std::string>& reg, int r) {
+    return (r >= 0 && r < (int)reg.size() && !reg[r].empty()) ? reg[r] : std::string("0u");
+  }
+
+  std::string offset(const EwIn& in, int skip_dim, const std::string& extra) {
+    std::ostringstream o;
+    bool any = false;
+    for (int d = 0; d < rank; ++d) {
+      if (d == skip_dim || in.stride[d] == 0) continue;
+      if (any) o << " + ";
+      o << x[d] << " * " << in.stride[d] << "LL";
+      any = true;
+    }
+    if (!extra.empty()) {
+      if (any) o << " + ";
+      o << extra;
+      any = true;
+    }
+    if (!any) o << "0";
+    return o.str();
+  }
+
+  void step(const EwInstr& I, std::vector<std::string>& reg, const std::string& indent) {
+    const std::string v = "v" + std::to_string(counter++);
+    const int dt = I.dt;
+    const bool fl = is_float(dt);
+    auto A = [&] { return reg_or_zero(reg, I.a); };
+    auto B = [&] { return reg_or_zero(reg, I.b); };
+    auto C = [&] { return reg_or_zero(reg, I.c); };
+    std::string e;
+    switch (I.op) {
+      case EW_LOAD: {
+        const EwIn& in = ins[I.aux];
+        const std::string& base = in_base[I.aux];
+        if (in.sel_dim >= 0) {
+          const std::string& k = x[in.sel_dim];
+          const std::string extra = "(" + k + " - " + std::to_string(in.sel_lo) + "LL) * " +
+                                    std::to_string(in.stride[in.sel_dim]) + "LL";
+          s << indent << "u32 " << v << ";\n"
+            << indent << "if (" << k << " >= " << in.sel_lo << "LL && " << k << " < " << in.sel_hi << "LL) " << v
+            << " = " << load_expr(base, offset(in, in.sel_dim, extra), in.dt) << ";\n"
+            << indent << "else " << v << " = " << B() << ";\n";
+          reg[I.dst] = v;
+          return;
+        }
+        e = load_expr(base, offset(in, -1, ""), in.dt);
+        break;
+      }
+      case EW_IMM: e = fl ? hex32(*(const uint32_t*)&I.fimm) : "(u32)" + std::to_string(I.iimm); break;
+      case EW_IOTA: e = fl ? fbits("(float)" + x[I.aux], dt) : "(u32)" + x[I.aux]; break;
+      case EW_ADD: case EW_SUB: case EW_MUL: case EW_DIV: case EW_MAX: case EW_MIN: {
+        if (fl) {
+          const std::string fa = "F(" + A() + ")", fb = "F(" + B() + ")";
+          std::string z;
+          switch (I.op) {
+            case EW_ADD: z = "(" + fa + " + " + fb + ")"; break;
+            case EW_SUB: z = "(" + fa + " - " + fb + ")"; break;
+            case EW_MUL: z = "(" + fa + " * " + fb + ")"; break;
+            case EW_DIV: z = "(" + fa + " / " + fb + ")"; break;
+            case EW_MAX: z = "fmax_nan(" + fa + ", " + fb + ")"; break;
+            default: z = "fmin_nan(" + fa + ", " + fb + ")"; break;
+          }
+          e = fbits(z, dt);
+        } else {
+          const std::string ia = "(int)" + A(), ib = "(int)" + B();
+          std::string z;
+          switch (I.op) {
+            case EW_ADD: z = "(" + ia + " + " + ib + ")"; break;
+            case EW_SUB: z = "(" + ia + " - " + ib + ")"; break;
+            case EW_MUL: z = "(" + ia + " * " + ib + ")"; break;
+            case EW_DIV: z = "(" + ib + " == 0 ? -1 : " + ia + " / " + ib + ")"; break;
+            case EW_MAX: z = "max(" + ia + ", " + ib + ")"; break;
+            default: z = "min(" + ia + ", " + ib + ")"; break;
+          }
+          if (dt == KDT_I1) z = "(" + z + " ? 1 : 0)";
+          e = "(u32)" + z;
+        }
+        break;
+      }
+      case EW_EXP: case EW_TANH: case EW_SQRT: case EW_RSQRT: case EW_SIN: case EW_COS:
+      case EW_LOGISTIC: case EW_NEG: case EW_ABS: {
+        if (fl) {
+          const std::string fx = "F(" + A() + ")";
+          std::string z;
+          switch (I.op) {
+            case EW_EXP: z = "expf(" + fx + ")"; break;
+            case EW_TANH: z = "tanhf(" + fx + ")"; break;
+            case EW_SQRT: z = "sqrtf(" + fx + ")"; break;
+            case EW_RSQRT: z = "(1.0f / sqrtf(" + fx + "))"; break;
+            case EW_SIN: z = "sinf(" + fx + ")"; break;
+            case EW_COS: z = "cosf(" + fx + ")"; break;
+            case EW_LOGISTIC: z = "(1.0f / (1.0f + expf(-" + fx + ")))"; break;
+            case EW_NEG: z = "(-" + fx + ")"; break;
+            default: z = "fabsf(" + fx + ")"; break;
+          }
+          e = fbits(z, dt);
+        } else {
+          const std::string ix = "(int)" + A();
+          if (I.op == EW_NEG) e = "(u32)(-" + ix + ")";
+          else if (I.op == EW_ABS) e = "(u32)(" + ix + " < 0 ? -" + ix + " : " + ix + ")";
+          else e = "(u32)" + ix;
+        }
+        break;
+      }
+      case EW_CONVERT: e = convert_expr(A(), I.aux, dt); break;
+      case EW_CMP: {
+        static const char* ops[] = {"==", "!=", ">=", ">", "<=", "<"};
+        const char* op = ops[I.aux < 6 ? I.aux : 5];
+        if (is_float(I.aux2)) e = "((F(" + A() + ") " + op + " F(" + B() + ")) ? 1u : 0u)";
+        else e = "(((int)" + A() + " " + op + " (int)" + B() + ") ? 1u : 0u)";
+        break;
+      }
+      case EW_SELECT: e = "(" + A() + " ? " + B() + " : " + C() + ")"; break;
+      default: fail(E_INTERNAL, "jit: unknown program step");
+    }
+    s << indent << "const u32 " << v << " = " << e << ";\n";
+    reg[I.dst] = v;
+  }
+};
+
+}  // namespace
+
+// ------------------------------------------------------------------ elementwise
+std::string jit_source_ew(const EwParams& P) {
+  std::ostringstream s;
+  s << kPrelude;
+  s << args_struct();
+  s << "extern \"C\" __global__ void __launch_bounds__(256) k(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  Emitter em{s, P.in, P.rank};
+  for (int i = 0; i < P.nin; ++i) {
+    em.in_base.push_back("in" + std::to_string(i));
+    s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
+  }
+  for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
+  s << "  for (i64 e = (i64)blockIdx.x * 256 + threadIdx.x; e < " << P.n << "LL; e += (i64)gridDim.x * 256) {\n";
+  for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
+  if (P.rank == 1) {
+    s << "    const i64 x0 = e;\n";
+  } else {
+    s << "    i64 rem = e;\n";
+    for (int d = P.rank - 1; d > 0; --d)
+      s << "    const i64 x" << d << " = rem % " << P.dims[d] << "LL; rem /= " << P.dims[d] << "LL;\n";
+    s << "    const i64 x0 = rem;\n";
+  }
+  std::vector<std::string> reg(EW_NREG);
+  for (int pc = 0; pc < P.ncode; ++pc) em.step(P.code[pc], reg, "    ");
+  for (int o = 0; o < P.nout; ++o)
+    s << "    " << store_stmt("out" + std::to_string(o), "e", P.out[o].dt, em.reg_or_zero(reg, P.out[o].reg)) << "\n";
+  s << "  }\n}\n";
+  return s.str();
+}
+
+// ------------------------------------------------------------------ row regions
+void row_launch_shape(const RowParams& p, int* block, int* cluster, int64_t* grid) {
+  int cl = 1;
+  while (cl < 8 && p.rows * cl * 2 <= 2 * 148 && p.C / (cl * 2) >= 32) cl *= 2;
+  if (cl > 1) {
+    const int64_t cols = (p.C + cl - 1) / cl;
+    *block = cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : 256;
+    *grid = p.rows * cl;
+  } else {
+    *block = p.C >= 1024 ? 256 : p.C >= 256 ? 128 : 64;
+    *grid = p.rows < 65535 ? p.rows : 65535;
+  }
+  *cluster = cl;
+}
+
+std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
+  std::ostringstream s;
+  s << kPrelude;
+  s << args_struct();
+  s << "extern \"C\" __global__ void __launch_bounds__(" << BLOCK
+    << ") k(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  s << "  __shared__ float red_f[" << BLOCK / 32 << "];\n  __shared__ float bcast;\n  __shared__ float cl_part["
+    << RP_MAXPH << "];\n";
+  s << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+  s << "  const u32 crank = " << (CL > 1 ? "cluster_rank()" : "0u") << ";\n";
+  const int64_t Cc = (P.C + CL - 1) / CL;
+  s << "  const i64 c0 = (i64)crank * " << Cc << "LL;\n";
+  s << "  const i64 c1 = min((i64)" << P.C << "LL, c0 + " << Cc << "LL);\n";
+  Emitter em{s, P.in, P.rank};
+  for (int i = 0; i < P.nin; ++i) {
+    em.in_base.push_back("in" + std::to_string(i));
+    s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
+  }
+  for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
+  s << "  (void)lane; (void)warp; (void)c1;\n";
+  s << "  for (i64 row = blockIdx.x / " << CL << "; row < " << P.rows << "LL; row += gridDim.x / " << CL << ") {\n";
+  for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
+  s << "    i64 rem = row;\n";
+  for (int d = P.rank - 2; d >= 0; --d)
+    s << "    const i64 x" << d << " = rem % " << P.dims[d] << "LL; rem /= " << P.dims[d] << "LL;\n";
+  s << "    (void)rem;\n";
+  // per-row scalars live for the whole row
+  std::vector<std::string> sreg(RP_NREG);
+  for (int r = RP_SREG0; r < RP_NREG; ++r) s << "    u32 s" << r << " = 0u; (void)s" << r << ";\n";
+  for (int r = RP_SREG0; r < RP_NREG; ++r) sreg[r] = "s" + std::to_string(r);
+  const std::string xc = "x" + std::to_string(P.rank - 1);
+  for (int ph = 0; ph < P.nphase; ++ph) {
+    const RowPhase& Ph = P.ph[ph];
+    const bool sum = Ph.red_kind == 0;
+    s << "    {  // phase " << ph << "\n";
+    s << "      float acc = " << (sum ? "0.0f" : "-__int_as_float(0x7f800000)") << ";\n";
+    s << "      for (i64 " << xc << " = c0 + threadIdx.x; " << xc << " < c1; " << xc << " += " << BLOCK << ") {\n";
+    std::vector<std::string> reg = sreg;  // per-element registers start undefined
+    for (int pc = Ph.lo; pc < Ph.hi; ++pc) em.step(P.code[pc], reg, "        ");
+    if (Ph.red_reg >= 0) {
+      const std::string xv = "F(" + em.reg_or_zero(reg, Ph.red_reg) + ")";
+      s << "        acc = " << (sum ? "acc + " + xv : "fmaxf(acc, " + xv + ")") << ";\n";
+    }
+    for (int o = 0; o < P.nout; ++o)
+      if (!P.out[o].scalar && P.out[o].phase == ph)
+        s << "        "
+          << store_stmt("out" + std::to_string(o), "row * " + std::to_string(P.C) + "LL + " + xc, P.out[o].dt,
+                        em.reg_or_zero(reg, P.out[o].reg))
+          << "\n";
+    s << "      }\n";
+    if (Ph.red_reg >= 0) {
+      const std::string comb = sum ? "t = t + o;" : "t = fmaxf(t, o);";
+      s << "      for (int sh = 16; sh > 0; sh >>= 1) { float o = __shfl_xor_sync(0xffffffffu, acc, sh); "
+        << (sum ? "acc = acc + o;" : "acc = fmaxf(acc, o);") << " }\n";
+      s << "      if (lane == 0) red_f[warp] = acc;\n      __syncthreads();\n";
+      s << "      float t = " << (sum ? "0.0f" : "-__int_as_float(0x7f800000)") << ";\n";
+      s << "      if (threadIdx.x == 0) for (int w = 0; w < " << BLOCK / 32 << "; ++w) { float o = red_f[w]; " << comb
+        << " }\n";
+      if (CL > 1) {
+        s << "      if (threadIdx.x == 0) cl_part[" << ph << "] = t;\n      cluster_sync();\n";
+        s << "      if (threadIdx.x == 0) { t = " << (sum ? "0.0f" : "-__int_as_float(0x7f800000)") << "; for (u32 r = 0; r < "
+          << CL << "; ++r) { float o = ld_cluster_f32(&cl_part[" << ph << "], r); " << comb << " } }\n";
+      }
+      s << "      if (threadIdx.x == 0) { float o = __uint_as_float(" << hex32(*(const uint32_t*)&Ph.red_init) << "); "
+        << comb << " bcast = " << round_expr("t", Ph.red_dt) << "; }\n";
+      s << "      __syncthreads();\n      s" << (int)Ph.red_dst << " = U(bcast);\n      __syncthreads();\n";
+    }
+    // per-row scalar program after this phase (its immediates use fresh names)
+    std::vector<std::string> sc = sreg;
+    for (int pc = Ph.slo; pc < Ph.shi; ++pc) {
+      const EwInstr& I = P.code[pc];
+      if (I.dst >= RP_SREG0) {
+        // scalar results keep their fixed names
+        std::vector<std::string> tmp = sc;
+        em.step(I, tmp, "      ");
+        s << "      s" << (int)I.dst << " = " << tmp[I.dst] << ";\n";
+      } else {
+        em.step(I, sc, "      ");
+      }
+    }
+    s << "    }\n";
+  }
+  s << "    if (threadIdx.x == 0 && crank == 0u) {\n";
+  for (int o = 0; o < P.nout; ++o)
+    if (P.out[o].scalar)
+      s << "      " << store_stmt("out" + std::to_string(o), "row", P.out[o].dt, sreg[P.out[o].reg]) << "\n";
+  s << "    }\n  }\n";
+  if (CL > 1) s << "  cluster_sync();\n";
+  s << "}\n";
+  return s.str();
+}
+
+bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster, JitArgs* args) {
+  *args = JitArgs{};
+  auto put = [&](int k, const DPtr& p) {
+    args->s[k] = p.slot;
+    args->o[k] = p.off;
+  };
+  if (l.kind == K_EW) {
+    const EwParams& e = *(const EwParams*)l.blob.data();
+    if (e.n == 0 || e.nin + e.nout > JIT_MAXBUF) return false;
+    int64_t g = (e.n + 255) / 256;
+    *grid = g > 148 * 64 ? 148 * 64 : (g < 1 ? 1 : g);
+    *block = 256;
+    *cluster = 1;
+    *src = jit_source_ew(e);
+    for (int i = 0; i < e.nin; ++i) put(i, e.in[i].p);
+    for (int o = 0; o < e.nout; ++o) put(e.nin + o, e.out[o].p);
+    return true;
+  }
+  if (l.kind == K_ROWNORM) {
+    const RowParams& r = *(const RowParams*)l.blob.data();
+    if (r.rows == 0 || r.nin + r.nout > JIT_MAXBUF) return false;
+    row_launch_shape(r, block, cluster, grid);
+    *src = jit_source_row(r, *block, *cluster);
+    for (int i = 0; i < r.nin; ++i) put(i, r.in[i].p);
+    for (int o = 0; o < r.nout; ++o) put(r.nin + o, r.out[o].p);
+    return true;
+  }
+  return false;
+}
+
+std::vector<std::string> jit_plan_sources(const Plan& p) {
+  std::vector<std::string> out;
+  for (const Launch& l : p.launches) {
+    std::string s;
+    int64_t g;
+    int b, c;
+    JitArgs a;
+    if (jit_describe(l, &s, &g, &b, &c, &a)) out.push_back(std::move(s));
+  }
+  return out;
+}
+
+// ------------------------------------------------------------------ NVRTC
+namespace {
+
+struct Nvrtc {
+  decltype(&nvrtcCreateProgram) create = nullptr;
+  decltype(&nvrtcCompileProgram) compile = nullptr;
+  decltype(&nvrtcGetProgramLogSize) log_size = nullptr;
+  decltype(&nvrtcGetProgramLog) log = nullptr;
+  decltype(&nvrtcGetCUBINSize) cubin_size = nullptr;
+  decltype(&nvrtcGetCUBIN) cubin = nullptr;
+  decltype(&nvrtcDestroyProgram) destroy = nullptr;
+  bool ok = false;
+};
+
+Nvrtc& nvrtc() {
+  static Nvrtc n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* names[] = {"libnvrtc.so.12", "libnvrtc.so", "/usr/local/cuda/lib64/libnvrtc.so.12"};
+    void* h = nullptr;
+    for (const char* nm : names)
+      if ((h = dlopen(nm, RTLD_NOW | RTLD_LOCAL))) break;
+    if (!h) return;
+    n.create = (decltype(n.create))dlsym(h, "nvrtcCreateProgram");
+    n.compile = (decltype(n.compile))dlsym(h, "nvrtcCompileProgram");
+    n.log_size = (decltype(n.log_size))dlsym(h, "nvrtcGetProgramLogSize");
+    n.log = (decltype(n.log))dlsym(h, "nvrtcGetProgramLog");
+    n.cubin_size = (decltype(n.cubin_size))dlsym(h, "nvrtcGetCUBINSize");
+    n.cubin = (decltype(n.cubin))dlsym(h, "nvrtcGetCUBIN");
+    n.destroy = (decltype(n.destroy))dlsym(h, "nvrtcDestroyProgram");
+    n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
+  });
+  return n;
+}
+
+std::mutex g_cache_mu;
+std::map<std::string, void*> g_cache;  // source -> cudaKernel_t (nullptr: failed)
+
+// NVRTC -> cubin; empty on failure (the log goes to `log` when given)
+std::vector<char> to_cubin(const std::string& src, std::string* log_out) {
+  Nvrtc& n = nvrtc();
+  if (!n.ok) return {};
+  nvrtcProgram prog;
+  if (n.create(&prog, src.c_str(), "fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return {};
+  const char* opts[] = {"-arch=sm_100a", "-fmad=false", "--std=c++17", "-default-device"};
+  nvrtcResult r = n.compile(prog, 4, opts);
+  if (r != NVRTC_SUCCESS) {
+    size_t ls = 0;
+    n.log_size(prog, &ls);
+    std::string log(ls, '\0');
+    n.log(prog, &log[0]);
+    if (log_out) *log_out = log;
+    if (getenv("CLJXLA_B200_JIT_LOG"))
+      fprintf(stderr, "cljxla jit: compile failed:\n%s\n--- source ---\n%s\n", log.c_str(), src.c_str());
+    n.destroy(&prog);
+    return {};
+  }
+  size_t cs = 0;
+  n.cubin_size(prog, &cs);
+  std::vector<char> cubin(cs);
+  n.cubin(prog, cubin.data());
+  n.destroy(&prog);
+  return cubin;
+}
+
+void* compile_one(const std::string& src) {
+  std::vector<char> cubin = to_cubin(src, nullptr);
+  if (cubin.empty()) return nullptr;
+  cudaLibrary_t lib = nullptr;
+  if (cudaLibraryLoadData(&lib, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  cudaKernel_t k = nullptr;
+  if (cudaLibraryGetKernel(&k, lib, "k") != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return (void*)k;  // the library stays loaded for the life of the process
+}
+
+}  // namespace
+
+int jit_check_sources(const std::vector<std::string>& sources, std::string* first_log) {
+  if (!nvrtc().ok) return -1;
+  std::map<std::string, int> uniq;
+  for (const std::string& s : sources) uniq[s] = 1;
+  int failed = 0;
+  for (auto& kv : uniq) {
+    std::string log;
+    if (to_cubin(kv.first, &log).empty()) {
+      if (!failed && first_log) *first_log = log + "\n--- source ---\n" + kv.first;
+      ++failed;
+    }
+  }
+  return failed;
+}
+
+bool jit_enabled() {
+  const char* e = getenv("CLJXLA_B200_JIT");
+  if (e && (e[0] == '0' || e[0] == 'f' || e[0] == 'F' || e[0] == 'n' || e[0] == 'N')) return false;
+  return nvrtc().ok;
+}
+
+std::vector<void*> jit_compile(const std::vector<std::string>& sources) {
+  std::vector<void*> out(sources.size(), nullptr);
+  if (!jit_enabled()) return out;
+  std::vector<std::string> todo;
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    std::map<std::string, int> seen;
+    for (const std::string& s : sources)
+      if (!g_cache.count(s) && !seen.count(s)) {
+        seen[s] = 1;
+        todo.push_back(s);
+      }
+  }
+  std::vector<void*> got(todo.size(), nullptr);
+  const unsigned hw = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
+  std::vector<std::thread> pool;
+  std::mutex next_mu;
+  size_t next = 0;
+  for (unsigned t = 0; t < std::min<size_t>(hw, todo.size()); ++t)
+    pool.emplace_back([&] {
+      for (;;) {
+        size_t i;
+        {
+          std::lock_guard<std::mutex> lk(next_mu);
+          if (next >= todo.size()) return;
+          i = next++;
+        }
+        got[i] = compile_one(todo[i]);
+      }
+    });
+  for (auto& th : pool) th.join();
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  for (size_t i = 0; i < todo.size(); ++i) g_cache[todo[i]] = got[i];
+  for (size_t i = 0; i < sources.size(); ++i) out[i] = g_cache[sources[i]];
+  return out;
+}
+
+void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab, const JitArgs& jargs,
+                cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3((unsigned)block, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (cluster > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  void* args[] = {(void*)&argtab, (void*)&jargs};
+  CUDA_OK(cudaLaunchKernelExC(&cfg, (const void*)kernel, args));
+}
+
+}  // namespace cljxla

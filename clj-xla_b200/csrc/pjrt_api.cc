@@ -10,6 +10,7 @@
 #include <cstring>
 
 #include "../../include/cljxla_b200.h"
+#include "jit.h"
 #include "runtime.h"
 
 using namespace cljxla;
@@ -237,6 +238,8 @@ PJRT_Error* Client_Compile(void* a) {
       auto ip = build_plan(*graph, po);
       if (!ip->inplace.empty()) ex->inplace.plan = std::move(ip);
     }
+    prepare_jit(*ex->copy.plan);
+    if (ex->inplace.plan) prepare_jit(*ex->inplace.plan);
     int64_t arena = ex->copy.plan->arena_bytes;
     if (ex->inplace.plan) arena = std::max(arena, ex->inplace.plan->arena_bytes);
     if (arena) CUDA_OK(cudaMalloc(&ex->arena, (size_t)arena));
@@ -482,6 +485,29 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
   } catch (const std::exception& e) {
     if (err && errcap) snprintf(err, errcap, "%s", e.what());
     return E_INTERNAL;
+  }
+}
+
+CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags, int* kernels, char* err,
+                                        size_t errcap) {
+  try {
+    auto g = parse_mlir(text, len);
+    PlanOptions po;
+    po.fuse = (flags & 1) != 0;
+    po.kv_in_place = (flags & 2) != 0;
+    auto p = build_plan(*g, po);
+    std::vector<std::string> src = jit_plan_sources(*p);
+    if (kernels) *kernels = (int)src.size();
+    std::string log;
+    int failed = jit_check_sources(src, &log);
+    if (failed > 0 && err && errcap) snprintf(err, errcap, "%s", log.c_str());
+    return failed;
+  } catch (const Error& e) {
+    if (err && errcap) snprintf(err, errcap, "%s", e.what());
+    return -2;
+  } catch (const std::exception& e) {
+    if (err && errcap) snprintf(err, errcap, "%s", e.what());
+    return -2;
   }
 }
 

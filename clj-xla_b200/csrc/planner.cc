@@ -1509,11 +1509,33 @@ void Planner::emit_node_kernel(int id) {
                       n.numel() * (int64_t)dt_size(n.dt);
       int64_t flops = 2 * G.batch * G.M * G.N * G.K;
       Launch fl;
+      TcGemmParams tc;
       if (opt_.fast_kernels && make_gemv(G, fl)) {
         fl.label = n.name;
         fl.algo_bytes = bytes;
         fl.algo_flops = flops;
         plan_.launches.push_back(std::move(fl));
+      } else if (opt_.fast_kernels && make_tc_gemm(G, tc)) {
+        int bm, bn, bk;
+        tc_gemm_tile_shape(&bm, &bn, &bk);
+        TmapSpec ta, tb;
+        ta.base = G.a;
+        ta.inner = G.K;
+        ta.outer = G.M;
+        ta.row_bytes = G.a_sm * 2;
+        ta.box_inner = bk;
+        ta.box_outer = bm;
+        tb.base = G.b;
+        tb.inner = G.K;
+        tb.outer = G.N;
+        tb.row_bytes = G.b_sn * 2;
+        tb.box_inner = bk;
+        tb.box_outer = bn;
+        tc.tmap_a_index = (int32_t)plan_.tmaps.size();
+        plan_.tmaps.push_back(ta);
+        tc.tmap_b_index = (int32_t)plan_.tmaps.size();
+        plan_.tmaps.push_back(tb);
+        push(K_GEMM_TC, blob_of(tc), n.name, bytes, flops);
       } else {
         push(K_GEMM, blob_of(G), n.name, bytes, flops);
       }
@@ -1746,6 +1768,15 @@ void Planner::run() {
   emit_all();
   emit_outputs();
   allocate_arena();
+  // tensor maps and the status word sit in the table after the scratch slots
+  for (Launch& l : plan_.launches) {
+    if (l.kind != K_GEMM_TC) continue;
+    TcGemmParams& t = *(TcGemmParams*)l.blob.data();
+    const int slot = plan_.tmap_slot();
+    t.tmap_a = DPtr{slot, 0, 128LL * t.tmap_a_index};
+    t.tmap_b = DPtr{slot, 0, 128LL * t.tmap_b_index};
+    t.status = DPtr{slot, 0, 128LL * (int64_t)plan_.tmaps.size()};
+  }
   verify_plan(plan_);
   if (const char* path = getenv("CLJXLA_B200_DUMP_PLAN")) {
     if (FILE* f = fopen(path, "a")) {

@@ -17,12 +17,27 @@ enum KernelKind : int {
 };
 const char* kernel_kind_name(int k);
 
+// Buffers of a compiled fused kernel, passed by value at launch: buffer k is
+// argument-table slot s[k] plus byte offset o[k] (s[k] < 0: o[k] is the address).
+constexpr int JIT_MAXBUF = 24;
+struct JitArgs {
+  int32_t s[JIT_MAXBUF];
+  int32_t pad;
+  int64_t o[JIT_MAXBUF];
+};
+
 struct Launch {
   int kind = 0;
   std::vector<uint8_t> blob;  // the kernel's POD parameter block
   std::string label;          // for profiling: which graph values it produces
   int64_t algo_bytes = 0;     // algorithmic HBM bytes (roofline accounting)
   int64_t algo_flops = 0;
+  // compiled replacement of an interpreted elementwise / row launch (jit.h);
+  // null: the interpreting kernel runs
+  void* jit_fn = nullptr;
+  int64_t jit_grid = 0;
+  int jit_block = 0, jit_cluster = 1;
+  JitArgs jit_args{};
 };
 
 struct TensorSpec {
@@ -49,9 +64,22 @@ struct InplaceDus {
   int64_t undo_bytes = 0;
 };
 
+// A TMA tensor map the executor encodes (host side) into the executable's
+// tensor-map table whenever the operand's address changes: a 2-D bf16 view
+// `base` of `outer` rows x `inner` elements, `row_bytes` apart, copied in
+// boxes of box_outer x box_inner.
+struct TmapSpec {
+  DPtr base;
+  int64_t inner = 0, outer = 0, row_bytes = 0;
+  int box_inner = 0, box_outer = 0;
+};
+
 struct Plan {
   std::string name;
   std::vector<InplaceDus> inplace;
+  // tensor maps (128 bytes each) followed by one 4-byte status word that
+  // kernels with bounded waits set on a timeout; argument-table slot tmap_slot()
+  std::vector<TmapSpec> tmaps;
   std::vector<TensorSpec> params, outs;
   std::vector<Launch> launches;
   int64_t arena_bytes = 0;
@@ -61,14 +89,20 @@ struct Plan {
   int n_nodes = 0, n_live = 0, n_fused_groups = 0;
   std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
   std::vector<int64_t> tmp_bytes;    // size of each scratch buffer
-  // argument table layout: [params][outputs][undo records][constant blob][scratch buffers]
+  // argument table layout: [params][outputs][undo records][constant blob][scratch buffers][tensor-map table]
   int dyn_slots() const { return (int)(params.size() + outs.size() + inplace.size()); }
   int const_slot() const { return dyn_slots(); }
   int tmp_slot0() const { return const_slot() + 1; }
-  int argtab_size() const { return tmp_slot0() + (int)tmp_offsets.size(); }
+  int tmap_slot() const { return tmp_slot0() + (int)tmp_offsets.size(); }
+  int64_t tmap_table_bytes() const { return tmaps.empty() ? 0 : 128 * (int64_t)tmaps.size() + 128; }
+  int argtab_size() const { return tmap_slot() + (tmaps.empty() ? 0 : 1); }
 };
 
 std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
+
+// Generates and compiles the fused elementwise / row launches of a plan
+// (no-op when runtime compilation is unavailable or disabled).
+void prepare_jit(Plan& p);
 
 // Dispatches one launch record (argtab: device pointer of the argument table).
 void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s);

@@ -78,6 +78,12 @@ struct ExecVariant {
   void* consts = nullptr;
   uint64_t* d_argtab = nullptr;
   std::vector<uint64_t> h_argtab;
+  // tensor-map table (Plan::tmaps + status word): device copy, host image, and
+  // the operand addresses the image was last encoded for
+  void* d_tmaps = nullptr;
+  std::vector<uint64_t> h_tmaps;
+  std::vector<uint64_t> tmap_addr;
+  unsigned* status_host = nullptr;  // pinned copy of the status word, refreshed after each run
   cudaGraphExec_t graph = nullptr;
   cudaGraph_t graph_def = nullptr;
   int runs = 0;

@@ -24,6 +24,7 @@ struct Checker {
     if (slot == P + O + U) return (int64_t)p.const_blob.size();
     int b = slot - (P + O + U + 1);
     if (b < (int)p.tmp_bytes.size()) return p.tmp_bytes[b];
+    if (slot == p.tmap_slot() && !p.tmaps.empty()) return p.tmap_table_bytes();
     return -1;
   }
   void region(const DPtr& d, int64_t bytes, const char* what) const {

@@ -61,6 +61,15 @@ CLJXLA_EXPORT int cljxla_b200_plan_info(const PJRT_LoadedExecutable* exec, int64
 CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, int64_t* info, int n, char* err,
                                         size_t errcap);
 
+/* Host-only check of the compiled fused kernels: plans the MLIR text (flags
+ * as cljxla_b200_plan_text), generates the source of every fused elementwise
+ * and row kernel and compiles each distinct one with NVRTC for sm_100a (no
+ * device needed).  *kernels receives the number of generated kernels.
+ * Returns the number that failed to compile (first log in err), -1 when
+ * NVRTC is not available, -2 when planning failed. */
+CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags, int* kernels, char* err,
+                                        size_t errcap);
+
 /* The cudaStream_t a client launches on (for event timing by the caller). */
 CLJXLA_EXPORT void* cljxla_b200_stream(const PJRT_Client* client);
 

@@ -299,9 +299,10 @@ def _int_div(a, b):
 class Interpreter:
     """Executes a parsed module; ``run`` returns the outputs (and optionally every SSA value).
 
-    ``ulp_noise_seed``: when set, every f32 ``dot_general`` and sum-reduce
-    result is moved by one f32 ulp up or down at random (seeded) positions - a
-    model of a different, equally valid f32 summation order.  Tests use the spread it
+    ``ulp_noise_seed``: when set, the f32 accumulation of every ``dot_general``
+    and sum-reduce is moved by one f32 ulp up or down at random (seeded)
+    positions before it is rounded to the result type - a model of a
+    different, equally valid f32 summation order.  Tests use the spread it
     causes as the noise floor of a whole bf16 model (see tests/parity.py).
     """
 
@@ -431,13 +432,14 @@ class Interpreter:
             return self._gather(op, args, shape, dt)
         if name == "reduce":
             r = self._reduce(op, args, shape, dt)
-            return self._ulp_noise(r, dt) if op.body == "stablehlo.add" else r
+            return r
         if name == "dot_general":
-            return self._ulp_noise(self._dot(op, args, shape, dt), dt)
+            return self._dot(op, args, shape, dt)
         raise NotImplementedError(f"oracle: op {name} not supported")
 
-    def _ulp_noise(self, r, dt):
-        if self._noise is None or dt != "f32":
+    def _ulp_noise(self, r):
+        """One-ulp f32 noise on an f32 accumulation result, before its rounding to the result type."""
+        if self._noise is None:
             return r
         r = np.asarray(r, np.float32)
         u = self._noise.integers(-1, 2, size=r.shape)
@@ -472,7 +474,10 @@ class Interpreter:
                 r = np.maximum(np.max(a, axis=dims).astype(np.float64), float(init))
             else:
                 r = np.maximum(np.max(a, axis=dims), init)
-        return to_dtype(np.asarray(r).reshape(shape), dt)
+        r = np.asarray(r).reshape(shape)
+        if op.body == "stablehlo.add" and dt in _FLOAT and self._noise is not None:
+            r = self._ulp_noise(r.astype(np.float32))
+        return to_dtype(r, dt)
 
     def _dot(self, op, args, shape, dt):
         raw = op.attrs["raw"]
@@ -491,7 +496,7 @@ class Interpreter:
             bt = np.asarray(b, np.float32)
             bt = bt if rc[0] == 0 else bt.T
             r = np.asarray(a, np.float32).reshape(-1, a.shape[-1]) @ bt
-            return to_dtype(r.reshape(shape), dt)
+            return to_dtype(self._ulp_noise(r.reshape(shape)), dt)
         at = np.asarray(np.transpose(a, lb + lf + lc), np.float32)
         bt = np.asarray(np.transpose(b, rb + rc + rf), np.float32)
         bsz = int(np.prod([a.shape[i] for i in lb])) if lb else 1
@@ -499,7 +504,7 @@ class Interpreter:
         k = int(np.prod([a.shape[i] for i in lc])) if lc else 1
         n = int(np.prod([b.shape[i] for i in rf])) if rf else 1
         r = np.matmul(at.reshape(bsz, m, k), bt.reshape(bsz, k, n))
-        return to_dtype(r.reshape(shape), dt)
+        return to_dtype(self._ulp_noise(r.reshape(shape)), dt)
 
 
 def run_mlir(text: str, inputs, keep_all=False, ulp_noise_seed=None):

@@ -93,3 +93,36 @@ def test_loc_suffix_is_ignored(lib_path):
     txt = shlo.graph_to_mlir_text(g)
     assert 'loc("layer0/act")' in txt
     assert core.plan_text(lib_path, txt)["launches"] >= 1
+
+
+def test_generated_fused_kernels_compile(lib_path):
+    """Every fused elementwise / row kernel the planner generates for the
+    model graphs compiles with NVRTC for sm_100a (host only)."""
+    import ctypes
+    import dataclasses
+    from cljxla_b200.host import drivers as d
+    from cljxla_b200.host import stablehlo as shlo
+    lib = ctypes.CDLL(lib_path)
+    f = lib.cljxla_b200_jit_check
+    f.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p,
+                  ctypes.c_size_t]
+    f.restype = ctypes.c_int
+    tiny = {
+        "gpt2": dataclasses.replace(d.GPT2_SMALL, vocab=384, d_model=384, layers=2, n_heads=12, n_kv_heads=12,
+                                    head_dim=32, mlp=768, n_positions=64),
+        "gemma2": dataclasses.replace(d.GEMMA2_2B, vocab=512, d_model=256, layers=2, n_heads=4, n_kv_heads=2,
+                                      head_dim=64, mlp=512, window=6),
+        "gemma3": dataclasses.replace(d.GEMMA3_4B, vocab=512, d_model=256, layers=6, n_heads=4, n_kv_heads=2,
+                                      head_dim=64, mlp=512, window=6),
+    }
+    for name, cfg in tiny.items():
+        for kind in ("prefill", "decode"):
+            text = shlo.graph_to_mlir_text(d.build_graph(cfg, kind, 1, 8, 16, dynamic_prefill=kind == "prefill"))
+            b = text.encode()
+            k = ctypes.c_int(0)
+            err = ctypes.create_string_buffer(1 << 16)
+            rc = f(b, len(b), 3, ctypes.byref(k), err, 1 << 16)
+            if rc == -1:
+                pytest.skip("NVRTC not available")
+            assert rc == 0, f"{name} {kind}: {rc} of {k.value} kernels failed\n{err.value.decode()[:4000]}"
+            assert k.value > 0
