@@ -266,7 +266,8 @@ std::string jit_source_ew(const EwParams& P) {
   std::ostringstream s;
   s << kPrelude;
   s << args_struct();
-  s << "extern \"C\" __global__ void __launch_bounds__(256) k(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  s << "extern \"C\" __global__ void __launch_bounds__(256) cljxla_fused_ew(const u64* __restrict__ argtab, "
+       "const JitArgs a) {\n";
   Emitter em{s, P.in, P.rank};
   for (int i = 0; i < P.nin; ++i) {
     em.in_base.push_back("in" + std::to_string(i));
@@ -311,7 +312,7 @@ std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
   s << kPrelude;
   s << args_struct();
   s << "extern \"C\" __global__ void __launch_bounds__(" << BLOCK
-    << ") k(const u64* __restrict__ argtab, const JitArgs a) {\n";
+    << ") cljxla_fused_row(const u64* __restrict__ argtab, const JitArgs a) {\n";
   s << "  __shared__ float red_f[" << BLOCK / 32 << "];\n  __shared__ float bcast;\n  __shared__ float cl_part["
     << RP_MAXPH << "];\n";
   s << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
@@ -514,7 +515,8 @@ void* compile_one(const std::string& src) {
     return nullptr;
   }
   cudaKernel_t k = nullptr;
-  if (cudaLibraryGetKernel(&k, lib, "k") != cudaSuccess) {
+  const char* entry = src.find("cljxla_fused_row(") != std::string::npos ? "cljxla_fused_row" : "cljxla_fused_ew";
+  if (cudaLibraryGetKernel(&k, lib, entry) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
   }

@@ -24,7 +24,8 @@
 
 namespace cljxla {
 
-// Source of a compiled kernel (entry point "k", parameter: const uint64_t* argtab).
+// Source of a compiled kernel (entry points cljxla_fused_ew / cljxla_fused_row,
+// parameters: the argument table and the launch's JitArgs).
 std::string jit_source_ew(const EwParams& p);
 std::string jit_source_row(const RowParams& p, int block, int cluster);
 

@@ -158,49 +158,94 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
 #pragma unroll
     for (int e = 0; e < HPL; ++e) acc[r][e] = 0.f;
   }
-  const int64_t kbase = b * P.k.stride[0] + kh * P.k.stride[1] + lane * HPL;
-  const int64_t vbase = b * P.v.stride[0] + kh * P.v.stride[1] + lane * HPL;
-  for (int64_t j = t0 + warp; j < t1; j += NW) {
-    // mask values for every active query vector
+  const KT* kbase = kb + b * P.k.stride[0] + kh * P.k.stride[1];
+  const KT* vbase = vb + b * P.v.stride[0] + kh * P.v.stride[1] + lane * HPL;
+  int64_t mrow[NQV];
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    mrow[r] = r < nqv ? b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2] : 0;
+  }
+  // Rounds of 32 positions per warp: each lane owns one position for the scores
+  // (the whole q.k dot product of its own K row, no shuffles), the round's
+  // softmax statistics are warp reductions, and the P.V product walks the
+  // round's unmasked positions with each lane owning hd/32 output elements.
+  for (int64_t j0 = t0 + (int64_t)warp * 32; j0 < t1; j0 += NW * 32) {
+    const int64_t j = j0 + lane;
     float mk[NQV];
     bool any = false;
 #pragma unroll
     for (int r = 0; r < NQV; ++r) {
       mk[r] = -INFINITY;
-      if (r < nqv) {
-        int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
-        mk[r] = ld_any(mb, b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2] + j * P.mask.stride[3],
-                       P.mask.dt);
+      if (r < nqv && j < t1) {
+        mk[r] = ld_any(mb, mrow[r] + j * P.mask.stride[3], P.mask.dt);
         any |= mk[r] > P.mask_skip;
       }
     }
-    if (!any) continue;
-    float kr[HPL], vr[HPL];
-    load_row<KT, HPL>(kb + kbase + j * P.k.stride[2], kr);
-    load_row<KT, HPL>(vb + vbase + j * P.v.stride[2], vr);
+    const unsigned valid = __ballot_sync(0xffffffffu, any);
+    if (!valid) continue;
+    float s[NQV];
+#pragma unroll
+    for (int r = 0; r < NQV; ++r) s[r] = 0.f;
+    if (any) {
+      const KT* krow = kbase + j * P.k.stride[2];
+#pragma unroll 4
+      for (int c = 0; c < HD; c += HPL) {
+        float kr[HPL];
+        load_row<KT, HPL>(krow + c, kr);
+#pragma unroll
+        for (int r = 0; r < NQV; ++r)
+#pragma unroll
+          for (int e = 0; e < HPL; ++e) s[r] = fmaf(qs[r][c + e], kr[e], s[r]);
+      }
+    }
+    float p[NQV];
 #pragma unroll
     for (int r = 0; r < NQV; ++r) {
-      if (r >= nqv) break;
-      float s = 0.f;
+      p[r] = 0.f;
+      if (r >= nqv) continue;  // uniform across the warp
+      float mv = -INFINITY;
+      if (any) mv = rnd_dt(run_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
+      float rm = mv;
 #pragma unroll
-      for (int e = 0; e < HPL; ++e) s = fmaf(qs[r][lane * HPL + e], kr[e], s);
+      for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
+      const float mnew = fmaxf(m[r], rm);
+      if (mnew == -INFINITY) continue;  // uniform
+      if (any) p[r] = rnd_dt(expf(rnd_dt(mv - mnew, P.dt_sub)), P.dt_exp);
+      float ps = p[r];
 #pragma unroll
-      for (int sh = 16; sh > 0; sh >>= 1) s += __shfl_xor_sync(0xffffffffu, s, sh);
-      s = rnd_dt(s, P.dt_d1);
-      s = run_chain(P, s);
-      float mv = rnd_dt(s + mk[r], P.dt_m);
-      if (mv > m[r]) {
-        float sc = expf(m[r] - mv);  // m[r] = -inf first: 0
-        if (m[r] == -INFINITY) sc = 0.f;
-        l[r] *= sc;
+      for (int sh = 16; sh > 0; sh >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, sh);
+      const float sc = m[r] == -INFINITY ? 0.f : expf(m[r] - mnew);
+      l[r] = l[r] * sc + ps;
 #pragma unroll
-        for (int e = 0; e < HPL; ++e) acc[r][e] *= sc;
-        m[r] = mv;
+      for (int e = 0; e < HPL; ++e) acc[r][e] *= sc;
+      m[r] = mnew;
+    }
+    // P.V: four unmasked positions per step so their V rows load together
+    unsigned bits = valid;
+    while (bits) {
+      int src[4];
+      int cnt = 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        src[u] = bits ? __ffs(bits) - 1 : -1;
+        if (bits) { bits &= bits - 1; ++cnt; }
       }
-      float p = rnd_dt(expf(rnd_dt(mv - m[r], P.dt_sub)), P.dt_exp);
-      l[r] += p;
+      float vr[4][HPL];
 #pragma unroll
-      for (int e = 0; e < HPL; ++e) acc[r][e] = fmaf(p, vr[e], acc[r][e]);
+      for (int u = 0; u < 4; ++u)
+        if (src[u] >= 0) load_row<KT, HPL>(vbase + (j0 + src[u]) * P.v.stride[2], vr[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (src[u] < 0) break;  // uniform
+#pragma unroll
+        for (int r = 0; r < NQV; ++r) {
+          const float pj = __shfl_sync(0xffffffffu, p[r], src[u]);
+#pragma unroll
+          for (int e = 0; e < HPL; ++e) acc[r][e] = fmaf(pj, vr[u][e], acc[r][e]);
+        }
+      }
+      (void)cnt;
     }
   }
   // merge warps

@@ -1242,8 +1242,9 @@ void Planner::emit_attention(int d2) {
   if (P.group > 8) fail(E_UNIMPLEMENTED, "attention with more than 8 query heads per KV head");
   int64_t qtiles = (P.Sq + P.qtile - 1) / P.qtile;
   int64_t ctas = rows_kv * qtiles;
-  int splits = 1;
-  while (ctas * splits < 2 * 148 && (int64_t)splits * 2 * 64 <= P.T) splits *= 2;
+  // one 128-position round per warp-group of a CTA, at most two CTAs per SM
+  int splits = (int)std::min<int64_t>((P.T + 127) / 128, std::max<int64_t>(1, 2 * 148 / ctas));
+  if (splits < 1) splits = 1;
   P.splits = splits;
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);

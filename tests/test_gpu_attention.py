@@ -28,17 +28,21 @@ def _rand(shape, seed, scale=1.0):
     return interp.f32_to_bf16_bits((rng.standard_normal(shape) * scale).astype(np.float32))
 
 
-@pytest.mark.parametrize("Sq,T,nq,nkv,softcap,window,dynamic", [
-    (1, 16, 4, 2, None, None, True),
-    (1, 40, 4, 2, 50.0, 6, True),
-    (5, 16, 4, 2, None, None, True),
-    (8, 16, 4, 2, None, 6, True),
-    (8, 16, 4, 2, None, None, False),
-    (3, 24, 2, 2, 50.0, None, True),
-    (8, 128, 8, 4, None, None, True),
+@pytest.mark.parametrize("Sq,T,nq,nkv,softcap,window,dynamic,hd,pos", [
+    (1, 16, 4, 2, None, None, True, 64, None),
+    (1, 40, 4, 2, 50.0, 6, True, 64, None),
+    (5, 16, 4, 2, None, None, True, 64, None),
+    (8, 16, 4, 2, None, 6, True, 64, None),
+    (8, 16, 4, 2, None, None, False, 64, None),
+    (3, 24, 2, 2, 50.0, None, True, 64, None),
+    (8, 128, 8, 4, None, None, True, 64, None),
+    # decode over a long cache: many position splits, sliding window, rounds of 32 positions
+    (1, 2560, 8, 4, None, 1024, True, 256, 2100),
+    (1, 2560, 8, 4, None, None, True, 256, 2559),
+    (1, 700, 8, 4, 50.0, 300, True, 128, 650),
+    (4, 1200, 4, 2, None, None, True, 256, 900),
 ])
-def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic):
-    hd = 64
+def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
     B = 1
 
     def f(q, k, v, kc, vc, ow, pos):
@@ -51,7 +55,9 @@ def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic):
                                ("kc", ("tensor", (B, nkv, T, hd), "bf16")), ("vc", ("tensor", (B, nkv, T, hd), "bf16")),
                                ("ow", ("tensor", (nq * hd, nq * hd), "bf16")), ("pos", ("tensor", (1,), "i32"))], f)
     text = shlo.graph_to_mlir_text(g)
-    pos = np.array([min(T - Sq, 3)], np.int32) if dynamic else np.array([0], np.int32)
+    if pos is None:
+        pos = min(T - Sq, 3)
+    pos = np.array([pos], np.int32) if dynamic else np.array([0], np.int32)
     inputs = [_rand((B, Sq, nq * hd), 1), _rand((B, Sq, nkv * hd), 2), _rand((B, Sq, nkv * hd), 3),
               _rand((B, nkv, T, hd), 4), _rand((B, nkv, T, hd), 5), _rand((nq * hd, nq * hd), 6, 0.05), pos]
     want = interp.run_mlir(text, inputs)
