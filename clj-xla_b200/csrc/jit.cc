@@ -42,6 +42,10 @@ __device__ __forceinline__ int f2i_sat(float f) {
   if (f <= -2147483648.0f) return (int)0x80000000;
   return (int)f;
 }
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ u32 cluster_rank() { u32 r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -274,6 +278,7 @@ std::string jit_source_ew(const EwParams& P) {
     s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
+  s << "  pdl_enter();\n";
   s << "  for (i64 e = (i64)blockIdx.x * 256 + threadIdx.x; e < " << P.n << "LL; e += (i64)gridDim.x * 256) {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   if (P.rank == 1) {
@@ -316,6 +321,7 @@ std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
   s << "  __shared__ float red_f[" << BLOCK / 32 << "];\n  __shared__ float bcast;\n  __shared__ float cl_part["
     << RP_MAXPH << "];\n";
   s << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
+  s << "  pdl_enter();\n";
   s << "  const u32 crank = " << (CL > 1 ? "cluster_rank()" : "0u") << ";\n";
   const int64_t Cc = (P.C + CL - 1) / CL;
   s << "  const i64 c0 = (i64)crank * " << Cc << "LL;\n";
@@ -589,17 +595,34 @@ void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3((unsigned)block, 1, 1);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (cluster > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
   }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
   void* args[] = {(void*)&argtab, (void*)&jargs};
   CUDA_OK(cudaLaunchKernelExC(&cfg, (const void*)kernel, args));
 }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("CLJXLA_B200_PDL");
+    return !(e && (e[0] == '0' || e[0] == 'f' || e[0] == 'F' || e[0] == 'n' || e[0] == 'N'));
+  }();
+  return on;
+}
+
+void launch_failed(cudaError_t e) { fail(E_INTERNAL, std::string("kernel launch failed: ") + cudaGetErrorString(e)); }
 
 }  // namespace cljxla

@@ -120,6 +120,7 @@ constexpr int NW = 4;
 template <typename KT, int HPL, int NQV>
 __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ AttnParams P,
                                                       const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   constexpr int HD = HPL * 32;
   __shared__ float qs[NQV][HD];
   __shared__ float wm[NW][NQV], wl[NW][NQV];
@@ -284,7 +285,203 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 K/V with 16-byte aligned rows: each sub-chunk of CH positions is first
+// staged in shared memory with cp.async (only the rows between the first and
+// last unmasked position), so every K/V byte the CTA needs is in flight at
+// once instead of one row per dependent load.  Rows are padded by 16 bytes so
+// that lanes reading different rows at the same column hit different banks.
+constexpr int CH = 128;  // positions per staged sub-chunk (one 32-position round per warp)
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(gmem)
+               : "memory");
+}
+
+template <int HPL, int NQV>
+__global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constant__ AttnParams P,
+                                                           const uint64_t* __restrict__ argtab) {
+  pdl_enter();
+  constexpr int HD = HPL * 32;
+  constexpr int ROW = HD + 8;  // padded row, bf16 elements
+  extern __shared__ __align__(16) uint16_t kv_smem[];
+  uint16_t* Ks = kv_smem;
+  uint16_t* Vs = kv_smem + CH * ROW;
+  __shared__ float qs[NQV][HD];
+  __shared__ float wm[NW][NQV], wl[NW][NQV];
+  __shared__ float wacc[NW][NQV][HD];
+  __shared__ int s_lo, s_hi;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bk = blockIdx.z;
+  const int b = bk / P.nkv, kh = bk % P.nkv;
+  const int i0 = blockIdx.y * P.qtile;
+  const int nrows = min(P.qtile, P.Sq - i0);
+  const int nqv = nrows * P.group;
+  const int split = blockIdx.x;
+  const int64_t chunk = (P.T + P.splits - 1) / P.splits;
+  const int64_t t0 = split * chunk, t1 = min((int64_t)P.T, t0 + chunk);
+  const char* qb = dres(P.q.p, argtab);
+  const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
+  const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
+  const char* mb = dres(P.mask.p, argtab);
+
+  for (int e = threadIdx.x; e < NQV * HD; e += NW * 32) {
+    int r = e / HD, d = e % HD;
+    float val = 0.f;
+    if (r < nqv) {
+      int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+      val = ld_any(qb, b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2] + d * P.q.stride[3], P.q.dt);
+    }
+    qs[r][d] = val;
+  }
+  int64_t mrow[NQV];
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    mrow[r] = r < nqv ? b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2] : 0;
+  }
+  float m[NQV], l[NQV], acc[NQV][HPL];
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int e = 0; e < HPL; ++e) acc[r][e] = 0.f;
+  }
+  for (int64_t c0 = t0; c0 < t1; c0 += CH) {
+    const int64_t c1 = min(t1, c0 + CH);
+    // this thread's position: mask values and whether any query vector sees it
+    const int64_t j = c0 + warp * 32 + lane;
+    float mk[NQV];
+    bool any = false;
+#pragma unroll
+    for (int r = 0; r < NQV; ++r) {
+      mk[r] = -INFINITY;
+      if (r < nqv && j < c1) {
+        mk[r] = ld_any(mb, mrow[r] + j * P.mask.stride[3], P.mask.dt);
+        any |= mk[r] > P.mask_skip;
+      }
+    }
+    if (threadIdx.x == 0) { s_lo = CH; s_hi = -1; }
+    __syncthreads();  // also orders the previous sub-chunk's reads before the restaging below
+    if (any) {
+      atomicMin(&s_lo, (int)(j - c0));
+      atomicMax(&s_hi, (int)(j - c0));
+    }
+    __syncthreads();
+    const int lo = s_lo, hi = s_hi;
+    if (hi < lo) continue;  // the whole sub-chunk is masked
+    // stage rows [lo, hi] of K and V
+    constexpr int SEGS = HD * 2 / 16;  // 16-byte pieces per row
+    const int nseg = (hi - lo + 1) * SEGS;
+    for (int q = threadIdx.x; q < nseg; q += NW * 32) {
+      const int rr = lo + q / SEGS, sg = q % SEGS;
+      cp_async16(Ks + rr * ROW + sg * 8, kbase + (c0 + rr) * P.k.stride[2] + sg * 8);
+      cp_async16(Vs + rr * ROW + sg * 8, vbase + (c0 + rr) * P.v.stride[2] + sg * 8);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    // scores: lane = position warp*32+lane of the sub-chunk
+    const int pl = warp * 32 + lane;
+    const unsigned valid = __ballot_sync(0xffffffffu, any);
+    if (valid) {
+      float s[NQV];
+#pragma unroll
+      for (int r = 0; r < NQV; ++r) s[r] = 0.f;
+      if (any) {
+        const uint16_t* krow = Ks + pl * ROW;
+#pragma unroll 8
+        for (int c = 0; c < HD; c += 8) {
+          const uint4 w = *(const uint4*)(krow + c);
+          float kr[8];
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            kr[2 * i] = __uint_as_float(ww[i] << 16);
+            kr[2 * i + 1] = __uint_as_float(ww[i] & 0xffff0000u);
+          }
+#pragma unroll
+          for (int r = 0; r < NQV; ++r)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s[r] = fmaf(qs[r][c + e], kr[e], s[r]);
+        }
+      }
+      float p[NQV];
+#pragma unroll
+      for (int r = 0; r < NQV; ++r) {
+        p[r] = 0.f;
+        if (r >= nqv) continue;
+        float mv = -INFINITY;
+        if (any) mv = rnd_dt(run_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
+        float rm = mv;
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
+        const float mnew = fmaxf(m[r], rm);
+        if (mnew == -INFINITY) continue;
+        if (any) p[r] = rnd_dt(expf(rnd_dt(mv - mnew, P.dt_sub)), P.dt_exp);
+        float ps = p[r];
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, sh);
+        const float sc = m[r] == -INFINITY ? 0.f : expf(m[r] - mnew);
+        l[r] = l[r] * sc + ps;
+#pragma unroll
+        for (int e = 0; e < HPL; ++e) acc[r][e] *= sc;
+        m[r] = mnew;
+      }
+      unsigned bits = valid;
+      while (bits) {
+        const int src = __ffs(bits) - 1;
+        bits &= bits - 1;
+        const uint16_t* vrow = Vs + (warp * 32 + src) * ROW + lane * HPL;
+        float vr[HPL];
+        load_row<uint16_t, HPL>(vrow, vr);
+#pragma unroll
+        for (int r = 0; r < NQV; ++r) {
+          const float pj = __shfl_sync(0xffffffffu, p[r], src);
+#pragma unroll
+          for (int e = 0; e < HPL; ++e) acc[r][e] = fmaf(pj, vr[e], acc[r][e]);
+        }
+      }
+    }
+  }
+  // merge warps (as attn_kernel)
+#pragma unroll
+  for (int r = 0; r < NQV; ++r) {
+    if (lane == 0) { wm[warp][r] = m[r]; wl[warp][r] = l[r]; }
+#pragma unroll
+    for (int e = 0; e < HPL; ++e) wacc[warp][r][lane * HPL + e] = acc[r][e];
+  }
+  __syncthreads();
+  const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
+  for (int e = threadIdx.x; e < nqv * HD; e += NW * 32) {
+    int r = e / HD, d = e % HD;
+    float M = -INFINITY;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w][r]);
+    float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
+      for (int w = 0; w < NW; ++w) {
+        float sc = wm[w][r] == -INFINITY ? 0.f : expf(wm[w][r] - M);
+        L += wl[w][r] * sc;
+        A += wacc[w][r][d] * sc;
+      }
+    }
+    int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    int64_t row = ((int64_t)b * P.nq + h) * P.Sq + qi;
+    if (P.splits == 1) {
+      float o = L > 0.f ? A / L : 0.f;
+      char* ob = dres(P.out, argtab);
+      if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = o;
+      else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(o);
+    } else {
+      float* part = (float*)dres(P.part, argtab) + ((int64_t)split * rows_total + row) * (HD + 2);
+      part[2 + d] = A;
+      if (d == 0) { part[0] = M; part[1] = L; }
+    }
+  }
+}
+
 __global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
   const int HD = P.hd;
   const float* part = (const float*)dres(P.part, argtab);
@@ -310,14 +507,50 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const 
   }
 }
 
+template <int HPL, int NQV>
+void launch_smem(const AttnParams& p, const uint64_t* argtab, cudaStream_t s, dim3 grid) {
+  constexpr int HD = HPL * 32;
+  const int dyn = 2 * CH * (HD + 8) * 2;
+  static bool configured = false;  // per instantiation; set before the first launch (host thread)
+  if (!configured) {
+    CUDA_OK(cudaFuncSetAttribute(attn_smem_kernel<HPL, NQV>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    configured = true;
+  }
+  launch_k(attn_smem_kernel<HPL, NQV>, dim3(grid), dim3(NW * 32), dyn, s, 1, p, argtab);
+}
+
+bool smem_ok(const AttnParams& p) {
+  if (p.k_dt != KDT_BF16 || p.k.dt != KDT_BF16 || p.v.dt != KDT_BF16) return false;
+  if ((p.k.p.off % 16) || (p.v.p.off % 16)) return false;
+  for (int d = 0; d < 3; ++d)
+    if ((p.k.stride[d] % 8) || (p.v.stride[d] % 8)) return false;
+  return p.k.stride[3] == 1 && p.v.stride[3] == 1;
+}
+
+template <int HPL>
+void launch_smem_nqv(const AttnParams& p, const uint64_t* argtab, cudaStream_t s, dim3 grid, int nqv) {
+  if (nqv <= 1) launch_smem<HPL, 1>(p, argtab, s, grid);
+  else if (nqv <= 2) launch_smem<HPL, 2>(p, argtab, s, grid);
+  else if (nqv <= 4) launch_smem<HPL, 4>(p, argtab, s, grid);
+  else launch_smem<HPL, 8>(p, argtab, s, grid);
+}
+
 template <typename KT, int HPL>
 void launch_hpl(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   dim3 grid((unsigned)p.splits, (unsigned)((p.Sq + p.qtile - 1) / p.qtile), (unsigned)(p.B * p.nkv));
   int nqv = p.qtile * p.group;
-  if (nqv <= 1) attn_kernel<KT, HPL, 1><<<grid, NW * 32, 0, s>>>(p, argtab);
-  else if (nqv <= 2) attn_kernel<KT, HPL, 2><<<grid, NW * 32, 0, s>>>(p, argtab);
-  else if (nqv <= 4) attn_kernel<KT, HPL, 4><<<grid, NW * 32, 0, s>>>(p, argtab);
-  else attn_kernel<KT, HPL, 8><<<grid, NW * 32, 0, s>>>(p, argtab);
+  if constexpr (sizeof(KT) == 2) {
+    // staging pays off where few CTAs each cover a long stretch of positions
+    // (decode); prefill's many query tiles re-read K/V and keep direct loads
+    if (smem_ok(p) && p.Sq <= p.qtile) {
+      launch_smem_nqv<HPL>(p, argtab, s, grid, nqv);
+      return;
+    }
+  }
+  if (nqv <= 1) launch_k(attn_kernel<KT, HPL, 1>, dim3(grid), dim3(NW * 32), 0, s, 1, p, argtab);
+  else if (nqv <= 2) launch_k(attn_kernel<KT, HPL, 2>, dim3(grid), dim3(NW * 32), 0, s, 1, p, argtab);
+  else if (nqv <= 4) launch_k(attn_kernel<KT, HPL, 4>, dim3(grid), dim3(NW * 32), 0, s, 1, p, argtab);
+  else launch_k(attn_kernel<KT, HPL, 8>, dim3(grid), dim3(NW * 32), 0, s, 1, p, argtab);
 }
 
 }  // namespace
@@ -343,7 +576,7 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   int64_t rows = (int64_t)p.B * p.nq * p.Sq;
   int g = (int)(rows < 65535 ? rows : 65535);
-  attn_combine_kernel<<<g, p.hd < 256 ? p.hd : 256, 0, s>>>(p, argtab);
+  launch_k(attn_combine_kernel, dim3(g), dim3(p.hd < 256 ? p.hd : 256), 0, s, 1, p, argtab);
 }
 
 void verify_attention(const Launch& l, const RegionFn& region) {

@@ -27,6 +27,7 @@ constexpr int TM = 64, TN = 64, TK = 16;
 
 __global__ void __launch_bounds__(256) gemm_generic_kernel(const __grid_constant__ GemmParams P,
                                                            const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   __shared__ float As[TK][TM + 4];
   __shared__ float Bs[TK][TN + 4];
   const int64_t bz = blockIdx.z;
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(256) gemm_generic_kernel(const __grid_constant
 void launch_gemm(const GemmParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.M == 0 || p.N == 0 || p.batch == 0) return;
   dim3 grid((unsigned)((p.N + TN - 1) / TN), (unsigned)((p.M + TM - 1) / TM), (unsigned)p.batch);
-  gemm_generic_kernel<<<grid, 256, 0, s>>>(p, argtab);
+  launch_k(gemm_generic_kernel, dim3(grid), dim3(256), 0, s, 1, p, argtab);
 }
 
 }  // namespace cljxla

@@ -139,6 +139,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const char* tmA = dres(P.tmap_a, argtab);
   const char* tmB = dres(P.tmap_b, argtab);
   unsigned* status = (unsigned*)dres(P.status, argtab);
+  // the predecessor's results (A, and the tensor map table it may share a
+  // stream position with) are complete before anything below reads them, and
+  // tensor memory is only taken once this CTA is really running
+  pdl_enter();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -342,7 +346,7 @@ void launch_tc_gemm(const TcGemmParams& p, const uint64_t* argtab, cudaStream_t 
   const int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = (int)(tiles < sms ? tiles : sms);
   if (grid <= 0) return;
-  tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(p, argtab);
+  launch_k(tc_gemm_kernel, dim3(grid), dim3(THREADS), SMEM_BYTES, s, 1, p, argtab);
 }
 
 bool make_tc_gemm(const GemmParams& g, TcGemmParams& t) {

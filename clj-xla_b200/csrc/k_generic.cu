@@ -16,6 +16,7 @@ namespace {
 
 __global__ void __launch_bounds__(256) ew_kernel(const __grid_constant__ EwParams P,
                                                  const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   for (int64_t e = tid; e < P.n; e += nthreads) {
@@ -51,6 +52,7 @@ __device__ __forceinline__ int64_t view_off(const TView& v, int64_t e) {
 
 // byte copy between dense buffers: 16-byte vectors when both ends are aligned
 __global__ void copy_bytes_kernel(DPtr srcp, DPtr dstp, int64_t bytes, int vec, const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const char* src = dres(srcp, argtab);
   char* dst = dres(dstp, argtab);
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, nt = (int64_t)gridDim.x * blockDim.x;
@@ -66,6 +68,7 @@ __global__ void copy_bytes_kernel(DPtr srcp, DPtr dstp, int64_t bytes, int vec, 
 }
 
 __global__ void copy_kernel(const __grid_constant__ CopyParams P, const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const char* src = dres(P.src.p, argtab);
   char* dst = dres(P.dst.p, argtab);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < P.n; e += (int64_t)gridDim.x * blockDim.x) {
@@ -78,6 +81,7 @@ __global__ void copy_kernel(const __grid_constant__ CopyParams P, const uint64_t
 template <int BLOCK>
 __global__ void __launch_bounds__(BLOCK) reduce_kernel(const __grid_constant__ ReduceParams P,
                                                        const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const char* src = dres(P.in.p, argtab);
   char* dst = dres(P.out, argtab);
   const bool fl = is_float_dt(P.in.dt);
@@ -143,6 +147,7 @@ __global__ void __launch_bounds__(BLOCK) reduce_kernel(const __grid_constant__ R
 }
 
 __global__ void gather_kernel(const __grid_constant__ GatherParams P, const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   const char* table = dres(P.table, argtab);
   const char* idxb = dres(P.idx.p, argtab);
   char* out = dres(P.out, argtab);
@@ -170,6 +175,7 @@ __device__ __forceinline__ int64_t dus_start(const DusParams& P, int d, const ui
 }
 
 __global__ void dus_kernel(const __grid_constant__ DusParams P, const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   int64_t st[CLJXLA_MAXR];
   for (int d = 0; d < P.rank; ++d) st[d] = dus_start(P, d, argtab);
   const char* opnd = dres(P.operand.p, argtab);
@@ -233,6 +239,7 @@ struct UndoGeom {
 };
 
 __global__ void undo_apply_kernel(char* dst, const char* undo, UndoGeom G) {
+  pdl_enter();
   const int64_t* st = (const int64_t*)undo;
   const char* old = undo + 8 * CLJXLA_MAXR;
   int64_t nu = 1;
@@ -261,7 +268,7 @@ inline int grid_for(int64_t n, int block) {
 
 void launch_ew(const EwParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.n == 0) return;
-  ew_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
+  launch_k(ew_kernel, dim3(grid_for(p.n, 256)), dim3(256), 0, s, 1, p, argtab);
 }
 static bool view_is_dense(const TView& v) {
   int64_t acc = 1;
@@ -282,22 +289,22 @@ void launch_copy(const CopyParams& p, const uint64_t* argtab, cudaStream_t s) {
     int vec = 1;
     if (bytes % 16 == 0 && p.src.p.off % 16 == 0 && p.dst.p.off % 16 == 0) vec = 16;
     else if (bytes % 4 == 0 && p.src.p.off % 4 == 0 && p.dst.p.off % 4 == 0) vec = 4;
-    copy_bytes_kernel<<<grid_for(bytes / vec, 256), 256, 0, s>>>(p.src.p, p.dst.p, bytes, vec, argtab);
+    launch_k(copy_bytes_kernel, dim3(grid_for(bytes / vec, 256)), dim3(256), 0, s, 1, p.src.p, p.dst.p, bytes, vec, argtab);
     return;
   }
-  copy_kernel<<<grid_for(p.n, 256), 256, 0, s>>>(p, argtab);
+  launch_k(copy_kernel, dim3(grid_for(p.n, 256)), dim3(256), 0, s, 1, p, argtab);
 }
 void launch_reduce(const ReduceParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.n_out == 0) return;
   int64_t g = p.n_out < 148 * 32 ? p.n_out : 148 * 32;
-  if (p.n_red >= 2048) reduce_kernel<512><<<(int)g, 512, 0, s>>>(p, argtab);
-  else if (p.n_red >= 256) reduce_kernel<256><<<(int)g, 256, 0, s>>>(p, argtab);
-  else reduce_kernel<64><<<(int)g, 64, 0, s>>>(p, argtab);
+  if (p.n_red >= 2048) launch_k(reduce_kernel<512>, dim3((int)g), dim3(512), 0, s, 1, p, argtab);
+  else if (p.n_red >= 256) launch_k(reduce_kernel<256>, dim3((int)g), dim3(256), 0, s, 1, p, argtab);
+  else launch_k(reduce_kernel<64>, dim3((int)g), dim3(64), 0, s, 1, p, argtab);
 }
 void launch_gather(const GatherParams& p, const uint64_t* argtab, cudaStream_t s) {
   if (p.n_rows == 0) return;
   int64_t g = p.n_rows < 65535 ? p.n_rows : 65535;
-  gather_kernel<<<(int)g, 128, 0, s>>>(p, argtab);
+  launch_k(gather_kernel, dim3((int)g), dim3(128), 0, s, 1, p, argtab);
 }
 void launch_undo_apply(void* dst, const void* undo, int rank, const int64_t* out_shape, const int64_t* upd_shape,
                        int dt, cudaStream_t s) {
@@ -311,7 +318,7 @@ void launch_undo_apply(void* dst, const void* undo, int rank, const int64_t* out
     nu *= upd_shape[d];
   }
   if (nu == 0) return;
-  undo_apply_kernel<<<grid_for(nu, 256), 256, 0, s>>>((char*)dst, (const char*)undo, G);
+  launch_k(undo_apply_kernel, dim3(grid_for(nu, 256)), dim3(256), 0, s, 1, (char*)dst, (const char*)undo, G);
 }
 
 void launch_dus(const DusParams& p, const uint64_t* argtab, cudaStream_t s) {
@@ -321,7 +328,7 @@ void launch_dus(const DusParams& p, const uint64_t* argtab, cudaStream_t s) {
     for (int d = 0; d < p.rank; ++d) n *= p.upd_shape[d];
   }
   if (n == 0) return;
-  dus_kernel<<<grid_for(n, 256), 256, 0, s>>>(p, argtab);
+  launch_k(dus_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, 1, p, argtab);
 }
 
 }  // namespace cljxla

@@ -26,6 +26,7 @@ namespace {
 template <int BLOCK, int CL>
 __global__ void __launch_bounds__(BLOCK) row_kernel(const __grid_constant__ RowParams P,
                                                    const uint64_t* __restrict__ argtab) {
+  pdl_enter();
   __shared__ float red_f[BLOCK / 32];
   __shared__ float bcast;
   __shared__ float cl_part[RP_MAXPH];  // this CTA's partial of each phase (read by the cluster)
@@ -102,19 +103,7 @@ __global__ void __launch_bounds__(BLOCK) row_kernel(const __grid_constant__ RowP
 
 template <int BLOCK, int CL>
 void launch_cl(const RowParams& p, const uint64_t* argtab, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.rows * CL), 1, 1);
-  cfg.blockDim = dim3(BLOCK, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = CL;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CUDA_OK(cudaLaunchKernelEx(&cfg, row_kernel<BLOCK, CL>, p, argtab));
+  launch_k(row_kernel<BLOCK, CL>, dim3((unsigned)(p.rows * CL)), dim3(BLOCK), 0, s, CL, p, argtab);
 }
 
 template <int CL>
@@ -143,9 +132,9 @@ void launch_row(const RowParams& p, const uint64_t* argtab, cudaStream_t s) {
   else if (cl == 2) launch_cluster<2>(p, cols, argtab, s);
   else {
     int64_t g = p.rows < 65535 ? p.rows : 65535;
-    if (p.C >= 1024) row_kernel<256, 1><<<(int)g, 256, 0, s>>>(p, argtab);
-    else if (p.C >= 256) row_kernel<128, 1><<<(int)g, 128, 0, s>>>(p, argtab);
-    else row_kernel<64, 1><<<(int)g, 64, 0, s>>>(p, argtab);
+    if (p.C >= 1024) launch_k(row_kernel<256, 1>, dim3((int)g), dim3(256), 0, s, 1, p, argtab);
+    else if (p.C >= 256) launch_k(row_kernel<128, 1>, dim3((int)g), dim3(128), 0, s, 1, p, argtab);
+    else launch_k(row_kernel<64, 1>, dim3((int)g), dim3(64), 0, s, 1, p, argtab);
   }
 }
 

@@ -13,6 +13,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <utility>
+
 namespace cljxla {
 
 #ifndef CLJXLA_MAXR
@@ -29,7 +31,56 @@ struct DPtr {
 __device__ __forceinline__ char* dres(const DPtr& p, const uint64_t* __restrict__ argtab) {
   return p.slot >= 0 ? (char*)(argtab[p.slot] + (uint64_t)p.off) : (char*)(uintptr_t)p.off;
 }
+
+// Programmatic dependent launch.  Every kernel of a plan is launched so that
+// it may start while its predecessor in the stream is still running; before
+// touching anything the predecessor writes it waits for the predecessor's
+// completion (griddepcontrol.wait, a no-op for a normal launch), and only then
+// lets its own successor launch.  A kernel can thus be resident and ready
+// (and prefetch what does not depend on its predecessor, such as weights)
+// when the previous kernel ends, instead of paying the launch latency after.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
 #endif
+
+// Whether plan kernels are launched as programmatic dependents (env
+// CLJXLA_B200_PDL, default on).
+bool pdl_enabled();
+[[noreturn]] void launch_failed(cudaError_t e);
+
+// Launches `kernel` with the programmatic-dependent-launch attribute when
+// enabled (cluster dimension `cluster` along x when > 1).
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster,
+              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) launch_failed(e);
+}
 
 // element type codes used on the device (same numbering as cljxla::DT)
 enum : int32_t { KDT_F32 = 0, KDT_BF16, KDT_F16, KDT_F64, KDT_I32, KDT_I64, KDT_I8, KDT_I16, KDT_U8, KDT_U32, KDT_I1 };
