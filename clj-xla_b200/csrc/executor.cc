@@ -97,6 +97,10 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, argtab, l.jit_args, s);
     return;
   }
+  if (l.kind == K_MULTI) {  // not compiled: the parts one after another (they are independent)
+    for (const Launch& part : l.parts) run_launch(part, argtab, s);
+    return;
+  }
   switch (l.kind) {
     case K_EW: launch_ew(*(const EwParams*)b, argtab, s); break;
     case K_REDUCE: launch_reduce(*(const ReduceParams*)b, argtab, s); break;

@@ -9,12 +9,23 @@
 
 namespace cljxla {
 
+// Decode GEMV over up to GEMV_MAXSEG weight matrices that share the input x
+// (the q / k / v projections of one layer, or gate / up): segment i covers
+// rows [seg_end[i-1], seg_end[i]) of the launch, W_i is [N_i, K] row-major and
+// y_i is [M, N_i].
+constexpr int GEMV_MAXSEG = 4;
 struct GemvParams {
-  DPtr x, w, y;
-  int32_t x_dt, w_dt, y_dt, warps_per_row;
-  int64_t M, N, K;
-  int64_t x_sm, y_sm;  // row strides (elements) of x and y
+  DPtr x;
+  DPtr w[GEMV_MAXSEG], y[GEMV_MAXSEG];
+  int64_t seg_end[GEMV_MAXSEG];
+  int32_t y_dt[GEMV_MAXSEG];
+  int32_t nseg, x_dt, w_dt, warps_per_row;
+  int64_t M, N, K;  // N: rows of all segments
+  int64_t x_sm;     // row stride (elements) of x
 };
+
+// Appends a GEMV whose x, M and K match the launch's as a further segment.
+bool gemv_add_segment(Launch& l, const GemmParams& g);
 
 using RegionFn = std::function<void(const DPtr&, int64_t, const char*)>;
 

@@ -266,20 +266,18 @@ struct Emitter {
 }  // namespace
 
 // ------------------------------------------------------------------ elementwise
-std::string jit_source_ew(const EwParams& P) {
-  std::ostringstream s;
-  s << kPrelude;
-  s << args_struct();
-  s << "extern \"C\" __global__ void __launch_bounds__(256) cljxla_fused_ew(const u64* __restrict__ argtab, "
-       "const JitArgs a) {\n";
+// The program of one elementwise launch as a device function over blocks
+// [0, nblk) (bid = this CTA's block in that range).
+void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& fname) {
+  s << "__device__ __forceinline__ void " << fname
+    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk) {\n";
   Emitter em{s, P.in, P.rank};
   for (int i = 0; i < P.nin; ++i) {
     em.in_base.push_back("in" + std::to_string(i));
     s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
-  s << "  pdl_enter();\n";
-  s << "  for (i64 e = (i64)blockIdx.x * 256 + threadIdx.x; e < " << P.n << "LL; e += (i64)gridDim.x * 256) {\n";
+  s << "  for (i64 e = (i64)bid * 256 + threadIdx.x; e < " << P.n << "LL; e += (i64)nblk * 256) {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   if (P.rank == 1) {
     s << "    const i64 x0 = e;\n";
@@ -294,6 +292,14 @@ std::string jit_source_ew(const EwParams& P) {
   for (int o = 0; o < P.nout; ++o)
     s << "    " << store_stmt("out" + std::to_string(o), "e", P.out[o].dt, em.reg_or_zero(reg, P.out[o].reg)) << "\n";
   s << "  }\n}\n";
+}
+
+std::string jit_source_ew(const EwParams& P) {
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  emit_ew_body(s, P, "ew_body");
+  s << "extern \"C\" __global__ void __launch_bounds__(256) cljxla_fused_ew(const u64* __restrict__ argtab, "
+       "const JitArgs a) {\n  pdl_enter();\n  ew_body(argtab, a, blockIdx.x, gridDim.x);\n}\n";
   return s.str();
 }
 
@@ -312,16 +318,12 @@ void row_launch_shape(const RowParams& p, int* block, int* cluster, int64_t* gri
   *cluster = cl;
 }
 
-std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
-  std::ostringstream s;
-  s << kPrelude;
-  s << args_struct();
-  s << "extern \"C\" __global__ void __launch_bounds__(" << BLOCK
-    << ") cljxla_fused_row(const u64* __restrict__ argtab, const JitArgs a) {\n";
+void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL, const std::string& fname) {
+  s << "__device__ __forceinline__ void " << fname
+    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk) {\n";
   s << "  __shared__ float red_f[" << BLOCK / 32 << "];\n  __shared__ float bcast;\n  __shared__ float cl_part["
     << RP_MAXPH << "];\n";
   s << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
-  s << "  pdl_enter();\n";
   s << "  const u32 crank = " << (CL > 1 ? "cluster_rank()" : "0u") << ";\n";
   const int64_t Cc = (P.C + CL - 1) / CL;
   s << "  const i64 c0 = (i64)crank * " << Cc << "LL;\n";
@@ -333,7 +335,7 @@ std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
   s << "  (void)lane; (void)warp; (void)c1;\n";
-  s << "  for (i64 row = blockIdx.x / " << CL << "; row < " << P.rows << "LL; row += gridDim.x / " << CL << ") {\n";
+  s << "  for (i64 row = bid / " << CL << "; row < " << P.rows << "LL; row += nblk / " << CL << ") {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   s << "    i64 rem = row;\n";
   for (int d = P.rank - 2; d >= 0; --d)
@@ -402,10 +404,22 @@ std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
   s << "    }\n  }\n";
   if (CL > 1) s << "  cluster_sync();\n";
   s << "}\n";
+}
+
+std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  emit_row_body(s, P, BLOCK, CL, "row_body");
+  s << "extern \"C\" __global__ void __launch_bounds__(" << BLOCK
+    << ") cljxla_fused_row(const u64* __restrict__ argtab, const JitArgs a) {\n  pdl_enter();\n"
+       "  row_body(argtab, a, blockIdx.x, gridDim.x);\n}\n";
   return s.str();
 }
 
-bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster, JitArgs* args) {
+namespace {
+
+// shape and buffers of one elementwise / row launch; false for other kinds
+bool describe_one(const Launch& l, int64_t* grid, int* block, int* cluster, JitArgs* args) {
   *args = JitArgs{};
   auto put = [&](int k, const DPtr& p) {
     args->s[k] = p.slot;
@@ -418,7 +432,6 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
     *grid = g > 148 * 64 ? 148 * 64 : (g < 1 ? 1 : g);
     *block = 256;
     *cluster = 1;
-    *src = jit_source_ew(e);
     for (int i = 0; i < e.nin; ++i) put(i, e.in[i].p);
     for (int o = 0; o < e.nout; ++o) put(e.nin + o, e.out[o].p);
     return true;
@@ -427,7 +440,6 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
     const RowParams& r = *(const RowParams*)l.blob.data();
     if (r.rows == 0 || r.nin + r.nout > JIT_MAXBUF) return false;
     row_launch_shape(r, block, cluster, grid);
-    *src = jit_source_row(r, *block, *cluster);
     for (int i = 0; i < r.nin; ++i) put(i, r.in[i].p);
     for (int o = 0; o < r.nout; ++o) put(r.nin + o, r.out[o].p);
     return true;
@@ -435,13 +447,63 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
   return false;
 }
 
+void emit_body(std::ostringstream& s, const Launch& l, int block, int cluster, const std::string& fname) {
+  if (l.kind == K_EW) emit_ew_body(s, *(const EwParams*)l.blob.data(), fname);
+  else emit_row_body(s, *(const RowParams*)l.blob.data(), block, cluster, fname);
+}
+
+}  // namespace
+
+bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster,
+                  std::vector<JitArgs>* args) {
+  args->clear();
+  if (l.kind == K_MULTI) {
+    // one kernel, CTA ranges running the parts' programs in order
+    std::vector<int64_t> grids;
+    for (const Launch& p : l.parts) {
+      int64_t g;
+      int b, c;
+      JitArgs a;
+      if (!describe_one(p, &g, &b, &c, &a)) return false;
+      if (!args->empty() && (c != *cluster || p.kind != l.parts[0].kind)) return false;
+      *block = args->empty() ? b : std::max(*block, b);  // row programs run at the largest block
+      *cluster = c;
+      grids.push_back(g);
+      args->push_back(a);
+    }
+    std::ostringstream s;
+    s << kPrelude << args_struct();
+    s << "struct JitMulti { JitArgs p[" << l.parts.size() << "]; };\n";
+    for (size_t i = 0; i < l.parts.size(); ++i) emit_body(s, l.parts[i], *block, *cluster, "part" + std::to_string(i));
+    s << "extern \"C\" __global__ void __launch_bounds__(" << *block
+      << ") cljxla_fused_multi(const u64* __restrict__ argtab, const JitMulti a) {\n  pdl_enter();\n"
+         "  unsigned b = blockIdx.x;\n";
+    int64_t total = 0;
+    for (size_t i = 0; i < grids.size(); ++i) {
+      s << "  if (b < " << grids[i] << "u) { part" << i << "(argtab, a.p[" << i << "], b, " << grids[i]
+        << "u); return; }\n  b -= " << grids[i] << "u;\n";
+      total += grids[i];
+    }
+    s << "}\n";
+    *grid = total;
+    *src = s.str();
+    return true;
+  }
+  JitArgs a;
+  if (!describe_one(l, grid, block, cluster, &a)) return false;
+  args->push_back(a);
+  if (l.kind == K_EW) *src = jit_source_ew(*(const EwParams*)l.blob.data());
+  else *src = jit_source_row(*(const RowParams*)l.blob.data(), *block, *cluster);
+  return true;
+}
+
 std::vector<std::string> jit_plan_sources(const Plan& p) {
   std::vector<std::string> out;
   for (const Launch& l : p.launches) {
     std::string s;
     int64_t g;
-    int b, c;
-    JitArgs a;
+    int b = 0, c = 1;
+    std::vector<JitArgs> a;
     if (jit_describe(l, &s, &g, &b, &c, &a)) out.push_back(std::move(s));
   }
   return out;
@@ -521,7 +583,9 @@ void* compile_one(const std::string& src) {
     return nullptr;
   }
   cudaKernel_t k = nullptr;
-  const char* entry = src.find("cljxla_fused_row(") != std::string::npos ? "cljxla_fused_row" : "cljxla_fused_ew";
+  const char* entry = src.find("cljxla_fused_multi(") != std::string::npos ? "cljxla_fused_multi"
+                      : src.find("cljxla_fused_row(") != std::string::npos ? "cljxla_fused_row"
+                                                                            : "cljxla_fused_ew";
   if (cudaLibraryGetKernel(&k, lib, entry) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
@@ -589,8 +653,8 @@ std::vector<void*> jit_compile(const std::vector<std::string>& sources) {
   return out;
 }
 
-void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab, const JitArgs& jargs,
-                cudaStream_t s) {
+void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab,
+                const std::vector<JitArgs>& jargs, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3((unsigned)block, 1, 1);
@@ -611,7 +675,8 @@ void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  void* args[] = {(void*)&argtab, (void*)&jargs};
+  // the parts' JitArgs are contiguous, which is the kernel's by-value parameter layout
+  void* args[] = {(void*)&argtab, (void*)jargs.data()};
   CUDA_OK(cudaLaunchKernelExC(&cfg, (const void*)kernel, args));
 }
 

@@ -34,7 +34,8 @@ void row_launch_shape(const RowParams& p, int* block, int* cluster, int64_t* gri
 
 // Source and launch geometry of the compiled replacement of an elementwise /
 // row launch; false for launches that have none.
-bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster, JitArgs* args);
+bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster,
+                  std::vector<JitArgs>* args);
 
 // Compiles the sources (in parallel, cached by text) and returns one kernel
 // handle per source (nullptr where compilation failed or NVRTC is missing).
@@ -52,7 +53,7 @@ std::vector<std::string> jit_plan_sources(const Plan& p);
 
 // Launches a compiled kernel: grid x block threads, thread-block clusters of
 // `cluster` CTAs along x when cluster > 1.
-void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab, const JitArgs& args,
-                cudaStream_t s);
+void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab,
+                const std::vector<JitArgs>& args, cudaStream_t s);
 
 }  // namespace cljxla

@@ -1,13 +1,19 @@
 // Decode GEMV: y[m, n] = sum_k x[m, k] * W[n, k] for small M (decode batch).
 //
-// The weight matrix is the only large operand and is read exactly once, so
-// the kernel is HBM-bound: every lane streams 16-byte vectors of W with
+// The weight matrices are the only large operands and are read exactly once,
+// so the kernel is HBM-bound: every lane streams 16-byte vectors of W with
 // no-allocate loads (four independent vectors in flight per lane), x stays in
 // L1, accumulation is f32, and each output is rounded once to the result type.
 // Rows are split across 1-8 warps (split-K inside the block) so that even
 // small projections put enough bytes in flight to cover HBM latency on all
 // 148 SMs.  Layout: W row-major [N, K] (the transposed-weight operand of
 // clj-xla's Gemma linear layers, gemma.clj:8-23, folded into the kernel).
+//
+// One launch covers every projection of the same input (q / k / v, gate /
+// up): their rows are concatenated into one index space of segments.  The
+// kernel is launched as a programmatic dependent of the kernel before it and
+// asks L2 for its weight rows before waiting for that kernel, so the weight
+// stream starts while the previous (small) kernel is still running.
 #include <cuda_bf16.h>
 
 #include "fast_kernels.h"
@@ -22,6 +28,8 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
                : "l"(p));
   return v;
 }
+
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 __device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
@@ -62,22 +70,27 @@ template <int MT, typename XT>
 __global__ void __launch_bounds__(256) gemv_nt_bf16(const __grid_constant__ GemvParams P,
                                                    const uint64_t* __restrict__ argtab) {
   __shared__ float red[8][MT];
-  const uint16_t* W = (const uint16_t*)dres(P.w, argtab);
-  const XT* X = (const XT*)dres(P.x, argtab);
-  char* Y = dres(P.y, argtab);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpr = P.warps_per_row;
   const int rows_per_block = 8 / wpr;
   const int64_t row = (int64_t)blockIdx.x * rows_per_block + warp / wpr;
   const int part = warp % wpr;
   const bool active = row < P.N;
+  int sg = 0;
+  while (sg < P.nseg - 1 && row >= P.seg_end[sg]) ++sg;
+  const int64_t lrow = row - (sg ? P.seg_end[sg - 1] : 0);
+  const int64_t kper = P.K / wpr;  // multiple of 8 (checked on the host)
+  const int64_t k0 = part * kper, k1 = (part == wpr - 1) ? P.K : k0 + kper;
+  const uint16_t* wrow = (const uint16_t*)dres(P.w[sg], argtab) + lrow * P.K;
+  // weights do not depend on the previous kernel: start them towards L2 now
+  if (active)
+    for (int64_t k = k0 + lane * 64; k < k1; k += 32 * 64) prefetch_l2(wrow + k);
+  pdl_enter();
+  const XT* X = (const XT*)dres(P.x, argtab);
   float acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.f;
   if (active) {
-    const int64_t kper = P.K / wpr;  // multiple of 8 (checked on the host)
-    const int64_t k0 = part * kper, k1 = (part == wpr - 1) ? P.K : k0 + kper;
-    const uint16_t* wrow = W + row * P.K;
     int64_t k = k0 + lane * 8;
     // main loop: 4 independent 16-byte weight vectors in flight per lane
     for (; k + 3 * 256 < k1; k += 4 * 256) {
@@ -124,8 +137,10 @@ __global__ void __launch_bounds__(256) gemv_nt_bf16(const __grid_constant__ Gemv
     }
   }
   if (active && part == 0 && lane == 0) {
+    char* Y = dres(P.y[sg], argtab);
+    const int64_t nseg_rows = P.seg_end[sg] - (sg ? P.seg_end[sg - 1] : 0);
 #pragma unroll
-    for (int m = 0; m < MT; ++m) store_out(Y, m * P.y_sm + row, P.y_dt, acc[m]);
+    for (int m = 0; m < MT; ++m) store_out(Y, m * nseg_rows + lrow, P.y_dt[sg], acc[m]);
   }
 }
 
@@ -133,8 +148,27 @@ template <int MT>
 void launch_nt(const GemvParams& p, const uint64_t* argtab, cudaStream_t s) {
   int rows_per_block = 8 / p.warps_per_row;
   unsigned grid = (unsigned)((p.N + rows_per_block - 1) / rows_per_block);
-  if (p.x_dt == KDT_F32) gemv_nt_bf16<MT, float><<<grid, 256, 0, s>>>(p, argtab);
-  else gemv_nt_bf16<MT, uint16_t><<<grid, 256, 0, s>>>(p, argtab);
+  if (p.x_dt == KDT_F32) launch_k(gemv_nt_bf16<MT, float>, dim3(grid), dim3(256), 0, s, 1, p, argtab);
+  else launch_k(gemv_nt_bf16<MT, uint16_t>, dim3(grid), dim3(256), 0, s, 1, p, argtab);
+}
+
+int choose_warps_per_row(int64_t N, int64_t K) {
+  // enough warps in flight: split K across up to 8 warps per row
+  int wpr = 1;
+  while (wpr < 8 && N * wpr < 148 * 48 && (K / (wpr * 2)) % 8 == 0 && K / (wpr * 2) >= 256) wpr *= 2;
+  return wpr;
+}
+
+bool gemv_shape_ok(const GemmParams& g) {
+  // decode shapes only: one batch, few rows, bf16 weights laid out [N, K]
+  if (g.batch != 1 || g.M < 1 || g.M > 8 || g.b_dt != KDT_BF16) return false;
+  if (!(g.a_dt == KDT_BF16 || g.a_dt == KDT_F32) || !(g.c_dt == KDT_BF16 || g.c_dt == KDT_F32)) return false;
+  if (g.b_sk != 1 || g.b_sn != g.K || g.a_sk != 1) return false;
+  if (g.K % 8 != 0 || g.K < 256) return false;
+  if ((g.b.off % 16) != 0 || (g.a.off % 16) != 0) return false;
+  if (g.M > 1 && (g.a_sm % 8) != 0) return false;
+  if (g.M == 5 || g.M == 6 || g.M == 7) return false;  // keep the M=8 path exact-sized
+  return true;
 }
 
 }  // namespace
@@ -152,43 +186,57 @@ void launch_gemv(const GemvParams& p, const uint64_t* argtab, cudaStream_t s) {
 }
 
 bool make_gemv(const GemmParams& g, Launch& out) {
-  // decode shapes only: one batch, few rows, bf16 weights laid out [N, K]
-  if (g.batch != 1 || g.M < 1 || g.M > 8 || g.b_dt != KDT_BF16) return false;
-  if (!(g.a_dt == KDT_BF16 || g.a_dt == KDT_F32) || !(g.c_dt == KDT_BF16 || g.c_dt == KDT_F32)) return false;
-  if (g.b_sk != 1 || g.b_sn != g.K || g.a_sk != 1) return false;
-  if (g.K % 8 != 0 || g.K < 256) return false;
-  if ((g.b.off % 16) != 0 || (g.a.off % 16) != 0) return false;
-  if (g.M > 1 && (g.a_sm % 8) != 0) return false;
-  if (g.M == 5 || g.M == 6 || g.M == 7) return false;  // keep the M=8 path exact-sized
+  if (!gemv_shape_ok(g)) return false;
   GemvParams p{};
   p.x = g.a;
-  p.w = g.b;
-  p.y = g.c;
+  p.w[0] = g.b;
+  p.y[0] = g.c;
+  p.y_dt[0] = g.c_dt;
+  p.seg_end[0] = g.N;
+  p.nseg = 1;
   p.x_dt = g.a_dt;
   p.w_dt = g.b_dt;
-  p.y_dt = g.c_dt;
   p.M = g.M;
   p.N = g.N;
   p.K = g.K;
   p.x_sm = g.a_sm;
-  p.y_sm = g.N;
-  // enough warps in flight: split K across up to 8 warps per row
-  int wpr = 1;
-  while (wpr < 8 && g.N * wpr < 148 * 48 && (g.K / (wpr * 2)) % 8 == 0 && g.K / (wpr * 2) >= 256) wpr *= 2;
-  p.warps_per_row = wpr;
+  p.warps_per_row = choose_warps_per_row(p.N, p.K);
   out.kind = K_GEMV;
   out.blob.resize(sizeof(p));
   memcpy(out.blob.data(), &p, sizeof(p));
   return true;
 }
 
+bool gemv_add_segment(Launch& l, const GemmParams& g) {
+  if (l.kind != K_GEMV || !gemv_shape_ok(g)) return false;
+  GemvParams p;
+  memcpy(&p, l.blob.data(), sizeof(p));
+  if (p.nseg >= GEMV_MAXSEG || g.M != p.M || g.K != p.K || g.a_dt != p.x_dt || g.a_sm != p.x_sm ||
+      g.a.slot != p.x.slot || g.a.off != p.x.off)
+    return false;
+  p.w[p.nseg] = g.b;
+  p.y[p.nseg] = g.c;
+  p.y_dt[p.nseg] = g.c_dt;
+  p.N += g.N;
+  p.seg_end[p.nseg] = p.N;
+  p.nseg++;
+  p.warps_per_row = choose_warps_per_row(p.N, p.K);
+  memcpy(l.blob.data(), &p, sizeof(p));
+  return true;
+}
+
 void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region) {
   (void)plan;
   const GemvParams& p = *(const GemvParams*)l.blob.data();
-  region(p.w, p.N * p.K * 2, "weights");
+  if (p.nseg < 1 || p.nseg > GEMV_MAXSEG || p.seg_end[p.nseg - 1] != p.N) fail(E_INTERNAL, "gemv: bad segments");
   int64_t xs = dt_size((DT)p.x_dt);
   region(p.x, ((p.M - 1) * p.x_sm + p.K) * xs, "x");
-  region(p.y, ((p.M - 1) * p.y_sm + p.N) * (int64_t)dt_size((DT)p.y_dt), "y");
+  for (int i = 0; i < p.nseg; ++i) {
+    const int64_t n = p.seg_end[i] - (i ? p.seg_end[i - 1] : 0);
+    if (n <= 0) fail(E_INTERNAL, "gemv: empty segment");
+    region(p.w[i], n * p.K * 2, "weights");
+    region(p.y[i], p.M * n * (int64_t)dt_size((DT)p.y_dt[i]), "y");
+  }
 }
 
 }  // namespace cljxla

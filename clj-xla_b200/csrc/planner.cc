@@ -30,7 +30,7 @@ namespace cljxla {
 
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
-                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc"};
+                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc", "fused_multi"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }
 
@@ -232,6 +232,9 @@ class Planner {
   void emit_unit(int u);
   void emit_ew_group(const std::vector<int>& members);
   void emit_node_kernel(int n);
+  GemmParams dot_params(int id, int oslot, int64_t* bytes, int64_t* flops);
+  std::set<int> pre_emitted_;  // units already emitted together with an earlier one (grouped GEMVs)
+  std::set<int> emitted_units_;
   void build_row_regions();
   void emit_row_region(int r);
   void emit_attention(int d2);
@@ -843,6 +846,21 @@ void Planner::build_row_regions() {
             if (ext_ok) {
               rg.full.insert(u);
               changed = true;
+              // external elementwise operands computed only from values outside
+              // the region (the printer's per-consumer converts of a GEMV result)
+              // are recomputed inside it instead of costing a launch of their own
+              std::vector<int> work(exts.begin(), exts.end());
+              while (!work.empty() && (int)(rg.full.size() + rg.scalar.size()) < 40) {
+                int o = work.back();
+                work.pop_back();
+                const Node& on = g_.nodes[o];
+                if (rg.full.count(o) || region_of_[o] >= 0 || loc_[o].kind != Loc::EW || on.op == Op::Concat ||
+                    on.op == Op::Iota || on.shape != rg.F || !external_ok(o))
+                  continue;
+                rg.full.insert(o);
+                for (int oi : ins_[o])
+                  if (!is_splat(oi)) work.push_back(oi);
+              }
             }
             (void)all_full;
             continue;
@@ -1341,8 +1359,8 @@ void Planner::emit_node_kernel(int id) {
       D.rank = n.rank();
       D.dt = kdt(n.dt);
       D.operand = view_of(n.in[0]);
-      D.update = view_of(n.in[1]);
-      const Node& up = g_.nodes[n.in[1]];
+      D.update = view_of(ins_[id][1]);  // may be the unconverted value (rounded on store)
+      const Node& up = g_.nodes[ins_[id][1]];
       for (int d = 0; d < D.rank; ++d) {
         D.out_shape[d] = n.shape[d];
         D.upd_shape[d] = up.shape[d];
@@ -1426,6 +1444,68 @@ void Planner::emit_node_kernel(int id) {
       break;
     }
     case Op::Dot: {
+      int64_t bytes = 0, flops = 0;
+      GemmParams G = dot_params(id, oslot, &bytes, &flops);
+      Launch fl;
+      TcGemmParams tc;
+      if (opt_.fast_kernels && make_gemv(G, fl)) {
+        fl.label = n.name;
+        fl.algo_bytes = bytes;
+        fl.algo_flops = flops;
+        // the other projections of the same input (q / k / v, gate / up) join this launch
+        for (int u : users_[n.in[0]]) {
+          if (u == id || !live_[u] || g_.nodes[u].op != Op::Dot || pre_emitted_.count(u) || attn_.count(u) ||
+              loc_[u].kind != Loc::BUF)
+            continue;
+          const Node& un = g_.nodes[u];
+          if (un.in[0] != n.in[0] || un.ia != n.ia || un.ic != n.ic) continue;
+          const Node& wn = g_.nodes[view_root(un.in[1])];
+          if (wn.op != Op::Param && wn.op != Op::Constant) continue;
+          if (emitted_units_.count(u)) continue;
+          int64_t ub = 0, uf = 0;
+          GemmParams GU = dot_params(u, ensure_buf(u), &ub, &uf);
+          if (!gemv_add_segment(fl, GU)) continue;
+          pre_emitted_.insert(u);
+          fl.label += "," + un.name;
+          fl.algo_bytes += ub;
+          fl.algo_flops += uf;
+        }
+        plan_.launches.push_back(std::move(fl));
+      } else if (opt_.fast_kernels && make_tc_gemm(G, tc)) {
+        int bm, bn, bk;
+        tc_gemm_tile_shape(&bm, &bn, &bk);
+        TmapSpec ta, tb;
+        ta.base = G.a;
+        ta.inner = G.K;
+        ta.outer = G.M;
+        ta.row_bytes = G.a_sm * 2;
+        ta.box_inner = bk;
+        ta.box_outer = bm;
+        tb.base = G.b;
+        tb.inner = G.K;
+        tb.outer = G.N;
+        tb.row_bytes = G.b_sn * 2;
+        tb.box_inner = bk;
+        tb.box_outer = bn;
+        tc.tmap_a_index = (int32_t)plan_.tmaps.size();
+        plan_.tmaps.push_back(ta);
+        tc.tmap_b_index = (int32_t)plan_.tmaps.size();
+        plan_.tmaps.push_back(tb);
+        push(K_GEMM_TC, blob_of(tc), n.name, bytes, flops);
+      } else {
+        push(K_GEMM, blob_of(G), n.name, bytes, flops);
+      }
+      break;
+    }
+    default:
+      fail(E_UNIMPLEMENTED, std::string("no kernel for op ") + op_name(n.op));
+  }
+}
+
+GemmParams Planner::dot_params(int id, int oslot, int64_t* bytes_out, int64_t* flops_out) {
+  const Node& n = g_.nodes[id];
+  {
+    {
       const Node& a = g_.nodes[n.in[0]];
       const Node& b = g_.nodes[n.in[1]];
       std::vector<int64_t> lb = n.ia, rb = n.ib, lc = n.ic, rc = n.id, lf, rf;
@@ -1506,44 +1586,11 @@ void Planner::emit_node_kernel(int id) {
           !(G.b_dt == KDT_F32 || G.b_dt == KDT_BF16 || G.b_dt == KDT_F16) ||
           !(G.c_dt == KDT_F32 || G.c_dt == KDT_BF16 || G.c_dt == KDT_F16))
         fail(E_UNIMPLEMENTED, "dot_general on integer operands");
-      int64_t bytes = a.numel() * (int64_t)dt_size(a.dt) + b.numel() * (int64_t)dt_size(b.dt) +
-                      n.numel() * (int64_t)dt_size(n.dt);
-      int64_t flops = 2 * G.batch * G.M * G.N * G.K;
-      Launch fl;
-      TcGemmParams tc;
-      if (opt_.fast_kernels && make_gemv(G, fl)) {
-        fl.label = n.name;
-        fl.algo_bytes = bytes;
-        fl.algo_flops = flops;
-        plan_.launches.push_back(std::move(fl));
-      } else if (opt_.fast_kernels && make_tc_gemm(G, tc)) {
-        int bm, bn, bk;
-        tc_gemm_tile_shape(&bm, &bn, &bk);
-        TmapSpec ta, tb;
-        ta.base = G.a;
-        ta.inner = G.K;
-        ta.outer = G.M;
-        ta.row_bytes = G.a_sm * 2;
-        ta.box_inner = bk;
-        ta.box_outer = bm;
-        tb.base = G.b;
-        tb.inner = G.K;
-        tb.outer = G.N;
-        tb.row_bytes = G.b_sn * 2;
-        tb.box_inner = bk;
-        tb.box_outer = bn;
-        tc.tmap_a_index = (int32_t)plan_.tmaps.size();
-        plan_.tmaps.push_back(ta);
-        tc.tmap_b_index = (int32_t)plan_.tmaps.size();
-        plan_.tmaps.push_back(tb);
-        push(K_GEMM_TC, blob_of(tc), n.name, bytes, flops);
-      } else {
-        push(K_GEMM, blob_of(G), n.name, bytes, flops);
-      }
-      break;
+      *bytes_out = a.numel() * (int64_t)dt_size(a.dt) + b.numel() * (int64_t)dt_size(b.dt) +
+                   n.numel() * (int64_t)dt_size(n.dt);
+      *flops_out = 2 * G.batch * G.M * G.N * G.K;
+      return G;
     }
-    default:
-      fail(E_UNIMPLEMENTED, std::string("no kernel for op ") + op_name(n.op));
   }
 }
 
@@ -1584,6 +1631,8 @@ void Planner::emit_outputs() {
 
 void Planner::emit_unit(int u) {
   const Node& n = g_.nodes[u];
+  if (pre_emitted_.count(u)) return;
+  emitted_units_.insert(u);
   if (loc_[u].kind == Loc::ROW) {
     emit_row_region(region_of_[u]);
     return;
@@ -1655,15 +1704,25 @@ void Planner::allocate_arena() {
     return tmp_first_[a] != tmp_first_[b] ? tmp_first_[a] < tmp_first_[b] : a < b;
   });
   std::vector<int64_t> off(T, 0);
-  std::multimap<int64_t, int> active;  // offset -> buffer
-  int64_t peak = 0;
+  // buffers under 1 MiB get memory of their own (a decode step's temporaries
+  // total a few MB): no two of them ever share bytes, so the scheduler sees
+  // only true data dependencies between the small kernels that use them
+  int64_t small_end = 0;
   for (int b : order) {
+    if (tmp_bytes_[b] >= (1 << 20)) continue;
+    off[b] = small_end;
+    small_end += (tmp_bytes_[b] + 255) & ~int64_t(255);
+  }
+  std::multimap<int64_t, int> active;  // offset -> buffer (large buffers, reused after the small region)
+  int64_t peak = small_end;
+  for (int b : order) {
+    if (tmp_bytes_[b] < (1 << 20)) continue;
     for (auto it = active.begin(); it != active.end();) {
       if (tmp_last_[it->second] < tmp_first_[b]) it = active.erase(it);
       else ++it;
     }
     int64_t sz = (tmp_bytes_[b] + 255) & ~int64_t(255);
-    int64_t cand = 0;
+    int64_t cand = small_end;
     for (auto& kv : active) {
       int64_t s = kv.first, e = kv.first + ((tmp_bytes_[kv.second] + 255) & ~int64_t(255));
       if (cand + sz <= s) break;
@@ -1712,6 +1771,29 @@ void Planner::run() {
       attn_[am.d2] = am;
     }
     if (!attn_.empty()) liveness();
+  }
+  {
+    // a dynamic_update_slice whose update is a float->float convert reads the
+    // unconverted value and rounds it while storing (the KV-cache write of a
+    // RoPE result computed in f32, attention.clj:108 + :135-168)
+    bool rewired = false;
+    for (int i = 0; i < N; ++i) {
+      const Node& d = g_.nodes[i];
+      if (!live_[i] || d.op != Op::DUS) continue;
+      const int u = ins_[i][1];
+      const Node& un = g_.nodes[u];
+      if (un.op != Op::Convert || !dt_is_float(un.dt) || !dt_is_float(g_.nodes[un.in[0]].dt) ||
+          g_.nodes[un.in[0]].shape != un.shape)
+        continue;
+      int live_users = 0;
+      for (int x : users_[u]) live_users += live_[x] ? 1 : 0;
+      bool returned = false;
+      for (int o : g_.outputs) returned |= o == u;
+      if (live_users != 1 || returned) continue;
+      ins_[i][1] = un.in[0];
+      rewired = true;
+    }
+    if (rewired) liveness();
   }
   for (int i = 0; i < N; ++i) plan_.n_live += live_[i];
   mat_slot_.assign(N, -1);
@@ -1779,6 +1861,10 @@ void Planner::run() {
     t.status = DPtr{slot, 0, 128LL * (int64_t)plan_.tmaps.size()};
   }
   verify_plan(plan_);
+  if (opt_.fuse) {
+    schedule_and_merge(plan_);
+    verify_plan(plan_);
+  }
   if (const char* path = getenv("CLJXLA_B200_DUMP_PLAN")) {
     if (FILE* f = fopen(path, "a")) {
       fprintf(f, "# plan %s: %zu launches, arena %lld bytes\n", plan_.name.c_str(), plan_.launches.size(),

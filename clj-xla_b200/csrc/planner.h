@@ -13,6 +13,7 @@ namespace cljxla {
 enum KernelKind : int {
   K_EW = 0, K_REDUCE, K_COPY, K_GATHER, K_DUS, K_GEMM,
   K_GEMV, K_ATTN_DECODE, K_ATTN_COMBINE, K_ROWNORM, K_GEMM_TC,
+  K_MULTI,  // independent compiled fused kernels merged into one launch (parts)
   K_NUM_KINDS
 };
 const char* kernel_kind_name(int k);
@@ -20,6 +21,7 @@ const char* kernel_kind_name(int k);
 // Buffers of a compiled fused kernel, passed by value at launch: buffer k is
 // argument-table slot s[k] plus byte offset o[k] (s[k] < 0: o[k] is the address).
 constexpr int JIT_MAXBUF = 24;
+constexpr int JIT_MAXPARTS = 8;  // programs merged into one launch at most
 struct JitArgs {
   int32_t s[JIT_MAXBUF];
   int32_t pad;
@@ -37,7 +39,8 @@ struct Launch {
   void* jit_fn = nullptr;
   int64_t jit_grid = 0;
   int jit_block = 0, jit_cluster = 1;
-  JitArgs jit_args{};
+  std::vector<JitArgs> jit_args;  // one per program (several for K_MULTI)
+  std::vector<Launch> parts;      // K_MULTI: the merged launches, in order
 };
 
 struct TensorSpec {
@@ -99,6 +102,10 @@ struct Plan {
 };
 
 std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
+
+// Re-levels the launch list by the memory each launch touches and merges
+// independent compiled fused kernels of one launch shape (schedule.cc).
+void schedule_and_merge(Plan& p);
 
 // Generates and compiles the fused elementwise / row launches of a plan
 // (no-op when runtime compilation is unavailable or disabled).

@@ -1,0 +1,286 @@
+// Launch scheduling and horizontal fusion.
+//
+// The planner emits launches in a topological order of the graph that
+// interleaves independent chains (the q and k branches of a layer: norm,
+// rotate-half, RoPE, cache write).  This pass re-levels the launch list by the
+// memory each launch actually touches - the physical byte ranges of the
+// scratch arena (so buffers that share arena memory at different times stay
+// ordered), the read-only constant and tensor-map tables, and, conservatively,
+// the caller's buffers as one space - and then merges neighbouring launches of
+// the same level that are compiled fused kernels of the same launch shape into
+// one launch whose CTA ranges run the individual programs.  Nothing that
+// conflicts is ever reordered or merged.
+#include <algorithm>
+
+#include "fast_kernels.h"
+#include "jit.h"
+
+namespace cljxla {
+namespace {
+
+enum Space { SP_ARENA, SP_DYN, SP_CONST, SP_TMAP, SP_ABS };
+
+struct Access {
+  int space;
+  int64_t lo, hi;  // bytes in that space (SP_DYN: whole space)
+  bool write;
+};
+
+struct Collector {
+  const Plan& p;
+  std::vector<Access>& out;
+  void add(const DPtr& d, int64_t bytes, bool write) {
+    if (bytes <= 0) return;
+    const int P = (int)p.params.size(), O = (int)p.outs.size(), U = (int)p.inplace.size();
+    Access a{};
+    a.write = write;
+    if (d.slot < 0) {
+      a.space = SP_ABS;
+      a.lo = d.off;
+      a.hi = d.off + bytes;
+    } else if (d.slot < P + O + U) {
+      a.space = SP_DYN;
+      a.lo = 0;
+      a.hi = 1;
+    } else if (d.slot == p.const_slot()) {
+      a.space = SP_CONST;
+      a.lo = d.off;
+      a.hi = d.off + bytes;
+    } else if (d.slot >= p.tmp_slot0() && d.slot < p.tmp_slot0() + (int)p.tmp_offsets.size()) {
+      a.space = SP_ARENA;
+      a.lo = p.tmp_offsets[d.slot - p.tmp_slot0()] + d.off;
+      a.hi = a.lo + bytes;
+    } else {
+      a.space = SP_TMAP;
+      a.lo = d.off;
+      a.hi = d.off + bytes;
+    }
+    out.push_back(a);
+  }
+  void view(const TView& v, bool write) {
+    int64_t hi = 0;
+    for (int i = 0; i < v.rank; ++i) {
+      if (v.shape[i] == 0) return;
+      hi += (v.shape[i] - 1) * v.stride[i];
+    }
+    add(v.p, (hi + 1) * (int64_t)dt_size((DT)v.dt), write);
+  }
+  void strided(const DPtr& d, int dt, std::initializer_list<std::pair<int64_t, int64_t>> dims, bool write) {
+    int64_t hi = 0;
+    for (auto& ds : dims) {
+      if (ds.first == 0) return;
+      hi += (ds.first - 1) * ds.second;
+    }
+    add(d, (hi + 1) * (int64_t)dt_size((DT)dt), write);
+  }
+  void ew_inputs(const EwIn* in, int nin, int rank, const int64_t* dims) {
+    for (int i = 0; i < nin; ++i) {
+      TView v{};
+      v.p = in[i].p;
+      v.dt = in[i].dt;
+      v.rank = rank;
+      for (int d = 0; d < rank; ++d) { v.shape[d] = dims[d]; v.stride[d] = in[i].stride[d]; }
+      if (in[i].sel_dim >= 0) v.shape[in[i].sel_dim] = in[i].sel_hi - in[i].sel_lo;
+      view(v, false);
+    }
+  }
+};
+
+// false: unknown launch kind (treated as a barrier)
+bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
+  Collector c{p, out};
+  const void* b = l.blob.data();
+  switch (l.kind) {
+    case K_EW: {
+      const EwParams& e = *(const EwParams*)b;
+      c.ew_inputs(e.in, e.nin, e.rank, e.dims);
+      for (int o = 0; o < e.nout; ++o) c.add(e.out[o].p, e.n * (int64_t)dt_size((DT)e.out[o].dt), true);
+      return true;
+    }
+    case K_ROWNORM: {
+      const RowParams& r = *(const RowParams*)b;
+      c.ew_inputs(r.in, r.nin, r.rank, r.dims);
+      for (int o = 0; o < r.nout; ++o)
+        c.add(r.out[o].p, (r.out[o].scalar ? r.rows : r.rows * r.C) * (int64_t)dt_size((DT)r.out[o].dt), true);
+      return true;
+    }
+    case K_REDUCE: {
+      const ReduceParams& r = *(const ReduceParams*)b;
+      c.view(r.in, false);
+      c.add(r.out, r.n_out * (int64_t)dt_size((DT)r.out_dt), true);
+      return true;
+    }
+    case K_COPY: {
+      const CopyParams& r = *(const CopyParams*)b;
+      c.view(r.src, false);
+      c.view(r.dst, true);
+      return true;
+    }
+    case K_GATHER: {
+      const GatherParams& g = *(const GatherParams*)b;
+      c.strided(g.table, g.table_dt, {{g.rows_table, g.table_row_stride}, {g.row_len, 1}}, false);
+      c.view(g.idx, false);
+      c.add(g.out, g.n_rows * g.row_len * (int64_t)dt_size((DT)g.table_dt), true);
+      return true;
+    }
+    case K_DUS: {
+      const DusParams& d = *(const DusParams*)b;
+      c.view(d.operand, false);
+      c.view(d.update, false);
+      c.add(d.out, d.n * (int64_t)dt_size((DT)d.dt), true);
+      for (int i = 0; i < d.rank; ++i)
+        if (d.start_is_ptr[i]) c.add(d.start_ptr[i], (int64_t)dt_size((DT)d.start_dt[i]), false);
+      if (d.has_undo) c.add(d.undo, 1, true);
+      return true;
+    }
+    case K_GEMM: {
+      const GemmParams& g = *(const GemmParams*)b;
+      c.strided(g.a, g.a_dt, {{g.batch, g.a_sb}, {g.M, g.a_sm}, {g.K, g.a_sk}}, false);
+      c.strided(g.b, g.b_dt, {{g.batch, g.b_sb}, {g.K, g.b_sk}, {g.N, g.b_sn}}, false);
+      c.add(g.c, g.batch * g.M * g.N * (int64_t)dt_size((DT)g.c_dt), true);
+      return true;
+    }
+    case K_GEMV: {
+      const GemvParams& g = *(const GemvParams*)b;
+      c.add(g.x, ((g.M - 1) * g.x_sm + g.K) * (int64_t)dt_size((DT)g.x_dt), false);
+      for (int i = 0; i < g.nseg; ++i) {
+        const int64_t n = g.seg_end[i] - (i ? g.seg_end[i - 1] : 0);
+        c.add(g.w[i], n * g.K * 2, false);
+        c.add(g.y[i], g.M * n * (int64_t)dt_size((DT)g.y_dt[i]), true);
+      }
+      return true;
+    }
+    case K_ATTN_DECODE: case K_ATTN_COMBINE: {
+      const AttnParams& a = *(const AttnParams*)b;
+      const int64_t rows = (int64_t)a.B * a.nq * a.Sq;
+      const int64_t part = (int64_t)a.splits * rows * (a.hd + 2) * 4;
+      if (l.kind == K_ATTN_DECODE) {
+        c.view(a.q, false);
+        c.view(a.k, false);
+        c.view(a.v, false);
+        c.view(a.mask, false);
+        if (a.splits > 1) c.add(a.part, part, true);
+        else c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
+      } else {
+        c.add(a.part, part, false);
+        c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
+      }
+      return true;
+    }
+    case K_GEMM_TC: {
+      const TcGemmParams& t = *(const TcGemmParams*)b;
+      c.add(t.a, ((int64_t)(t.M - 1) * t.a_ld + t.K) * 2, false);
+      c.add(t.b, ((int64_t)(t.N - 1) * t.b_ld + t.K) * 2, false);
+      c.add(t.c, (int64_t)t.M * t.N * (int64_t)dt_size((DT)t.c_dt), true);
+      c.add(t.tmap_a, 128, false);
+      c.add(t.tmap_b, 128, false);
+      c.add(t.status, 4, true);
+      return true;
+    }
+  }
+  return false;
+}
+
+bool conflict(const std::vector<Access>& a, const std::vector<Access>& b) {
+  for (const Access& x : a)
+    for (const Access& y : b) {
+      if (!x.write && !y.write) continue;
+      if (x.space == SP_ABS || y.space == SP_ABS) return true;
+      if (x.space != y.space) continue;
+      if (x.space == SP_DYN) return true;
+      if (x.lo < y.hi && y.lo < x.hi) return true;
+    }
+  return false;
+}
+
+// launch shape a compiled kernel would use; kinds that are not compiled fused kernels: false
+bool merge_key(const Launch& l, int* kind, int* block, int* cluster) {
+  if (l.kind == K_EW) {
+    *kind = K_EW;
+    *block = 256;
+    *cluster = 1;
+    return ((const EwParams*)l.blob.data())->n > 0;
+  }
+  if (l.kind == K_ROWNORM) {
+    const RowParams& r = *(const RowParams*)l.blob.data();
+    if (r.rows == 0) return false;
+    int64_t g;
+    row_launch_shape(r, block, cluster, &g);
+    *kind = K_ROWNORM;
+    return true;
+  }
+  return false;
+}
+
+}  // namespace
+
+void schedule_and_merge(Plan& p) {
+  const int n = (int)p.launches.size();
+  if (n < 2) return;
+  std::vector<std::vector<Access>> acc(n);
+  std::vector<char> known(n);
+  for (int i = 0; i < n; ++i) known[i] = accesses(p, p.launches[i], acc[i]);
+  // level = 1 + the deepest earlier launch it conflicts with (unknown kinds: barriers)
+  std::vector<int> level(n, 0);
+  int barrier = -1;  // index of the last unknown-kind launch
+  for (int i = 0; i < n; ++i) {
+    int lv = barrier >= 0 ? level[barrier] + 1 : 0;
+    for (int j = std::max(0, barrier); j < i; ++j)
+      if (!known[i] || !known[j] || conflict(acc[i], acc[j])) lv = std::max(lv, level[j] + 1);
+    level[i] = lv;
+    if (!known[i]) barrier = i;
+  }
+  std::vector<int> order(n);
+  for (int i = 0; i < n; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return level[a] < level[b]; });
+  if (const char* path = getenv("CLJXLA_B200_DUMP_SCHEDULE")) {
+    if (FILE* f = fopen(path, "a")) {
+      for (int i : order) {
+        int kind = -1, block = 0, cluster = 0;
+        merge_key(p.launches[i], &kind, &block, &cluster);
+        fprintf(f, "%d\t%s\t%d\t%d\t%s\n", level[i], kernel_kind_name(p.launches[i].kind), block, cluster,
+                p.launches[i].label.c_str());
+      }
+      fclose(f);
+    }
+  }
+  std::vector<Launch> out;
+  out.reserve(n);
+  for (size_t k = 0; k < order.size();) {
+    int kind, block, cluster;
+    Launch& first = p.launches[order[k]];
+    if (!merge_key(first, &kind, &block, &cluster)) {
+      out.push_back(std::move(first));
+      ++k;
+      continue;
+    }
+    size_t e = k + 1;
+    while (e < order.size() && e - k < JIT_MAXPARTS && level[order[e]] == level[order[k]]) {
+      int k2, b2, c2;
+      // row programs of one cluster shape merge at the largest block among them
+      if (!merge_key(p.launches[order[e]], &k2, &b2, &c2) || k2 != kind || c2 != cluster ||
+          (kind == K_EW && b2 != block))
+        break;
+      ++e;
+    }
+    if (e - k == 1) {
+      out.push_back(std::move(first));
+      ++k;
+      continue;
+    }
+    Launch m;
+    m.kind = K_MULTI;
+    for (size_t q = k; q < e; ++q) {
+      Launch& part = p.launches[order[q]];
+      m.label += (m.label.empty() ? "" : "+") + part.label;
+      m.algo_bytes += part.algo_bytes;
+      m.algo_flops += part.algo_flops;
+      m.parts.push_back(std::move(part));
+    }
+    out.push_back(std::move(m));
+    k = e;
+  }
+  p.launches = std::move(out);
+}
+
+}  // namespace cljxla

@@ -58,9 +58,23 @@ struct Checker {
 
 }  // namespace
 
+namespace {
+void verify_launch(const Plan& p, Checker& c, const Launch& l);
+}
+
 void verify_plan(const Plan& p) {
   Checker c{p};
-  for (const Launch& l : p.launches) {
+  for (const Launch& l : p.launches) verify_launch(p, c, l);
+}
+
+namespace {
+void verify_launch(const Plan& p, Checker& c, const Launch& l) {
+  {
+    if (l.kind == K_MULTI) {
+      if (l.parts.size() < 2 || l.parts.size() > (size_t)JIT_MAXPARTS) fail(E_INTERNAL, "bad merged launch");
+      for (const Launch& part : l.parts) verify_launch(p, c, part);
+      return;
+    }
     c.cur = &l;
     const void* b = l.blob.data();
     switch (l.kind) {
@@ -166,5 +180,6 @@ void verify_plan(const Plan& p) {
     }
   }
 }
+}  // namespace
 
 }  // namespace cljxla
