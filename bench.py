@@ -62,6 +62,8 @@ def parse():
                    help="only the decode steps (zero caches, no prefill / e2e / profile): for ncu launch lists")
     p.add_argument("--layers", type=int, default=0,
                    help="override the layer count (small ncu captures; not a bench line)")
+    p.add_argument("--tp", type=int, default=1,
+                   help="tensor-parallel ranks per model replica (Gemma; ranks = --gpus under torchrun)")
     return p.parse_args()
 
 
@@ -177,8 +179,14 @@ def run_ours(args, rank, world, local_rank):
     from cljxla_b200.host.pjrt import DTYPE_ENUM
 
     torch.cuda.set_device(local_rank)
-    cfg, B, S, T = model_setup(args)
-    ctx = core.init_backend(pkg.LIB_PATH, {"device": local_rank})
+    cfg_full, B, S, T = model_setup(args)
+    cfg = d.shard_config(cfg_full, args.tp)
+    if args.tp > 1:
+        from cljxla_b200.host import tp as tpmod
+        ctx = core.init_tp_backend(args.tp, rank % args.tp, tpmod.share_nccl_id(pkg.LIB_PATH), local_rank,
+                                   pkg.LIB_PATH)
+    else:
+        ctx = core.init_backend(pkg.LIB_PATH, {"device": local_rank})
     api, client = ctx["api"], ctx["client"]
     wdt = DTYPE_ENUM[cfg.dtype]
 
@@ -186,7 +194,7 @@ def run_ours(args, rank, world, local_rank):
     host_w = device_weights(cfg, 1234 + rank, f"cuda:{local_rank}")
     specs = d.weight_specs(cfg)
     wbufs = [core.buffer_from_host_buffer(ctx, w, shp, wdt) for w, (_, shp, _) in zip(host_w, specs)]
-    if args.no_cpu_baseline or rank != 0:
+    if args.no_cpu_baseline or rank != 0 or args.tp > 1:
         del host_w
         host_w = None
     t_w = time.time() - t0
@@ -318,6 +326,7 @@ def run_ours(args, rank, world, local_rank):
 
     for b in kv + xs + ps + wbufs + [x_pre, p_pre]:
         api.destroy_buffer(b)
+    core.close_backend(ctx)
 
     tokens = B * args.steps
     res = {
@@ -363,6 +372,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.tp > 1 and args.tp != world:
+        raise SystemExit(f"--tp {args.tp} needs exactly {args.tp} ranks (torchrun --nproc-per-node {args.tp})")
     import torch
     if world > 1:
         import datetime
@@ -378,7 +389,8 @@ def main():
     else:
         dec_s, e2e_s, pre_s = res["dec_s"], res["e2e_s"], res["prefill_s"]
     if rank == 0:
-        value = world * res["tokens"] / dec_s
+        replicas = world // max(1, args.tp)
+        value = replicas * res["tokens"] / dec_s
         dk = res["by_kind"][res["dom"]]
         line = {
             "metric": "decode tokens/s (greedy KV-cached decode step, whole job)",
@@ -389,19 +401,21 @@ def main():
             "warmup": args.warmup,
             "ms_per_step": round(dec_s / args.steps * 1e3, 4),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if args.tp == 1 else "strong",
             "vs_baseline": None,
             "dtype": cfg.dtype,
             "data": "synthetic (random-init weights N(0,0.02), random token ids)",
             "config": {"workload": f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions"
                                    + (" [tiny]" if args.tiny else "")
                                    + (f" [{args.layers} layers]" if args.layers else ""),
-                       "model": args.config, "global_batch": B * world, "seq_len": S, "kv_len": T,
-                       "parallelism": f"dp{world} (independent replicas)",
+                       "model": args.config, "global_batch": B * replicas, "seq_len": S, "kv_len": T,
+                       "parallelism": (f"dp{world} (independent replicas)" if args.tp == 1 else
+                                       f"tp{args.tp}" + (f" x dp{replicas}" if replicas > 1 else "")
+                                       + " (NCCL all-reduce after attention and MLP)"),
                        "l2": "weights stream >> 126 MB L2 every step (no flush needed)"},
-            "prefill": {"value": round(world * B * S / pre_s, 1), "unit": "tokens/s",
+            "prefill": {"value": round(replicas * B * S / pre_s, 1), "unit": "tokens/s",
                         "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill"},
-            "e2e": {"value": round(world * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
+            "e2e": {"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": res["logits_bytes"],
                     "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"},
             "roofline": {"bound": "hbm", "kernel": res["dom"],

@@ -8,6 +8,7 @@
 
 #include "fast_kernels.h"
 #include "jit.h"
+#include "nccl_rt.h"
 #include "runtime.h"
 
 namespace cljxla {
@@ -91,8 +92,29 @@ void prepare_jit(Plan& p) {
   for (size_t i = 0; i < targets.size(); ++i) targets[i]->jit_fn = fns[i];
 }
 
+namespace {
+// the collective context of the executable being launched on this thread
+struct CollectiveCtx {
+  void* comm = nullptr;
+  int ranks = 1;
+  const uint64_t* host_argtab = nullptr;
+};
+thread_local CollectiveCtx g_coll;
+}  // namespace
+
 void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
   const void* b = l.blob.data();
+  if (l.kind == K_ALLREDUCE) {
+    const AllReduceParams& a = *(const AllReduceParams*)b;
+    if (!g_coll.comm) fail(E_PRECOND, "all_reduce in a graph run by a client without a tensor-parallel group");
+    if (a.ranks != g_coll.ranks)
+      fail(E_INVALID, "all_reduce over " + std::to_string(a.ranks) + " ranks on a client of " +
+                          std::to_string(g_coll.ranks));
+    const char* src = (const char*)(uintptr_t)(g_coll.host_argtab[a.src.slot] + (uint64_t)a.src.off);
+    char* dst = (char*)(uintptr_t)(g_coll.host_argtab[a.dst.slot] + (uint64_t)a.dst.off);
+    nccl_all_reduce_sum(src, dst, (size_t)a.count, a.dt, g_coll.comm, s);
+    return;
+  }
   if (l.jit_fn) {
     jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, argtab, l.jit_args, s);
     return;
@@ -212,6 +234,9 @@ void run_variant(PJRT_Client* c, ExecVariant& v, cudaStream_t s) {
   // pageable source: the driver stages it before returning, so h_argtab can be reused
   if (dyn) CUDA_OK(cudaMemcpyAsync(v.d_argtab, v.h_argtab.data(), dyn, cudaMemcpyHostToDevice, s));
   refresh_tmaps(v, s);
+  g_coll.comm = c->nccl_comm;
+  g_coll.ranks = c->opt.tp_size;
+  g_coll.host_argtab = v.h_argtab.data();
   if (profile_state().enabled) {
     launch_profiled(v, s);
   } else if (c->opt.cuda_graphs && !v.graph_failed && v.runs >= 1) {

@@ -22,7 +22,16 @@ struct GemvParams {
   int32_t nseg, x_dt, w_dt, warps_per_row;
   int64_t M, N, K;  // N: rows of all segments
   int64_t x_sm;     // row stride (elements) of x
+  // weights of the next GEMV in the schedule: each CTA, once its rows are done,
+  // asks L2 for its share of them, so they stream in while the small kernels
+  // between the two GEMVs run (byte counts are multiples of 16)
+  DPtr pf[GEMV_MAXSEG];
+  int64_t pf_bytes[GEMV_MAXSEG];
+  int32_t npf, pad_;
 };
+
+// Points every GEMV launch's prefetch at the weights of the next GEMV launch.
+void link_gemv_prefetch(Plan& p);
 
 // Appends a GEMV whose x, M and K match the launch's as a further segment.
 bool gemv_add_segment(Launch& l, const GemmParams& g);
@@ -63,9 +72,16 @@ namespace cljxla {
 // mask [B, nq, Sq, T] (broadcast view of the additive mask), out dense
 // [B, nq, Sq, hd].  The printed score chain (scale / softcap, with its
 // roundings) runs as a register program on each score.
+constexpr int ATTN_MERGE_MAX_SPLITS = 64;  // position splits merged in-kernel (arrival counters)
+
 struct AttnParams {
   TView q, k, v, mask;
   DPtr out, part;
+  // with position splits: one arrival counter per (batch*kv head, query tile),
+  // zero between launches; the last split CTA to arrive merges the partials
+  // itself and resets its counter (use_counters 0: a separate combine launch)
+  DPtr counters;
+  int32_t use_counters, pad_c;
   int32_t B, nq, nkv, Sq, T, hd, group, splits, qtile;
   int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
   int32_t nchain, chain_out;

@@ -20,6 +20,8 @@ enum class Op : uint8_t {
   Reshape, Transpose, Broadcast, Slice, Concat, DUS, Gather,
   // reductions / contractions
   Reduce, Dot,
+  // collectives (tensor parallelism)
+  AllReduce,
 };
 const char* op_name(Op o);
 inline bool op_is_elementwise(Op o) { return o >= Op::Add && o <= Op::Iota; }

@@ -117,6 +117,97 @@ __device__ float run_chain(const AttnParams& P, float s) {
 
 constexpr int NW = 4;
 
+// merged (max, sum, context) of one output row over the position splits, in
+// split order (the same arithmetic as attn_combine_kernel)
+__device__ __forceinline__ float merge_splits(const float* part, int64_t rows_total, int64_t row, int HD, int d,
+                                              int splits) {
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, __ldcg(part + ((int64_t)s * rows_total + row) * (HD + 2)));
+  float L = 0.f, A = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < splits; ++s) {
+      const float* pp = part + ((int64_t)s * rows_total + row) * (HD + 2);
+      const float pm = __ldcg(pp);
+      if (pm == -INFINITY) continue;
+      float sc = expf(pm - M);
+      L += __ldcg(pp + 1) * sc;
+      A += __ldcg(pp + 2 + d) * sc;
+    }
+  }
+  return L > 0.f ? A / L : 0.f;
+}
+
+// With per-launch arrival counters, the last split CTA of a (batch*kv head,
+// query tile) merges everyone's partials (threadfence-ordered, no waiting).
+// One warp per query vector turns the splits' (max, sum) pairs into scale
+// factors in shared memory; then every thread forms two output columns from
+// all splits with independent 8-byte loads.
+__device__ void merge_if_last(const AttnParams& P, const uint64_t* __restrict__ argtab, int b, int kh, int i0,
+                              int nqv) {
+  if (P.splits == 1 || !P.use_counters) return;
+  __shared__ int s_last;
+  __shared__ float s_sc[ATTN_MERGE_MAX_SPLITS][8];
+  __shared__ float s_l[8];
+  __threadfence();  // this CTA's partials are visible before it is counted
+  __syncthreads();
+  unsigned* ctr = (unsigned*)dres(P.counters, argtab) + ((int64_t)blockIdx.z * gridDim.y + blockIdx.y);
+  if (threadIdx.x == 0) s_last = atomicAdd(ctr, 1u) == (unsigned)(P.splits - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
+  const float* part = (const float*)dres(P.part, argtab);
+  char* ob = dres(P.out, argtab);
+  const int HD = P.hd, S = P.splits;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  auto row_of = [&](int r) {
+    const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    return ((int64_t)b * P.nq + h) * P.Sq + qi;
+  };
+  for (int r = warp; r < nqv; r += nw) {
+    const int64_t row = row_of(r);
+    float m = -INFINITY;
+    for (int sp = lane; sp < S; sp += 32) m = fmaxf(m, __ldcg(part + ((int64_t)sp * rows_total + row) * (HD + 2)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float* pp = part + ((int64_t)sp * rows_total + row) * (HD + 2);
+      const float pm = __ldcg(pp);
+      const float sc = (m == -INFINITY || pm == -INFINITY) ? 0.f : expf(pm - m);
+      s_sc[sp][r] = sc;
+      l += sc == 0.f ? 0.f : __ldcg(pp + 1) * sc;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) s_l[r] = l;
+  }
+  __syncthreads();
+  const int half = HD / 2;
+  for (int e = threadIdx.x; e < nqv * half; e += blockDim.x) {
+    const int r = e / half, d = 2 * (e % half);
+    const int64_t row = row_of(r);
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < S; ++sp) {
+      const float2 v = __ldcg((const float2*)(part + ((int64_t)sp * rows_total + row) * (HD + 2) + 2 + d));
+      const float sc = s_sc[sp][r];
+      a0 += v.x * sc;
+      a1 += v.y * sc;
+    }
+    const float l = s_l[r];
+    const float o0 = l > 0.f ? a0 / l : 0.f, o1 = l > 0.f ? a1 / l : 0.f;
+    if (P.out_dt == KDT_F32) {
+      ((float*)ob)[row * HD + d] = o0;
+      ((float*)ob)[row * HD + d + 1] = o1;
+    } else {
+      ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(o0);
+      ((__nv_bfloat16*)ob)[row * HD + d + 1] = __float2bfloat16_rn(o1);
+    }
+  }
+  if (threadIdx.x == 0) *ctr = 0u;  // ready for the next launch
+}
+
 template <typename KT, int HPL, int NQV>
 __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ AttnParams P,
                                                       const uint64_t* __restrict__ argtab) {
@@ -283,6 +374,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
       if (d == 0) { part[0] = M; part[1] = L; }
     }
   }
+  merge_if_last(P, argtab, b, kh, i0, nqv);
 }
 
 // ---------------------------------------------------------------------------
@@ -478,6 +570,7 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
       if (d == 0) { part[0] = M; part[1] = L; }
     }
   }
+  merge_if_last(P, argtab, b, kh, i0, nqv);
 }
 
 __global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const uint64_t* __restrict__ argtab) {
@@ -597,6 +690,10 @@ void verify_attention(const Launch& l, const RegionFn& region) {
   int64_t rows = (int64_t)p.B * p.nq * p.Sq;
   region(p.out, rows * p.hd * (int64_t)dt_size((DT)p.out_dt), "out");
   if (p.splits > 1) region(p.part, (int64_t)p.splits * rows * (p.hd + 2) * 4, "partials");
+  if (p.splits > 1 && p.use_counters) {
+    region(p.counters, 4LL * p.B * p.nkv * ((p.Sq + p.qtile - 1) / p.qtile), "arrival counters");
+    if (p.splits > ATTN_MERGE_MAX_SPLITS || p.qtile * p.group > 8) fail(E_INTERNAL, "attention merge too wide");
+  }
   if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||
       p.k.shape[1] != p.nkv || p.k.shape[2] != p.T || p.k.shape[3] != p.hd || p.v.shape[2] != p.T ||
       p.mask.shape[3] != p.T || p.k.stride[3] != 1 || p.v.stride[3] != 1 || p.nq != p.nkv * p.group)

@@ -73,83 +73,143 @@ __global__ void __launch_bounds__(256) gemv_nt_bf16(const __grid_constant__ Gemv
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wpr = P.warps_per_row;
   const int rows_per_block = 8 / wpr;
-  const int64_t row = (int64_t)blockIdx.x * rows_per_block + warp / wpr;
   const int part = warp % wpr;
-  const bool active = row < P.N;
-  int sg = 0;
-  while (sg < P.nseg - 1 && row >= P.seg_end[sg]) ++sg;
-  const int64_t lrow = row - (sg ? P.seg_end[sg - 1] : 0);
   const int64_t kper = P.K / wpr;  // multiple of 8 (checked on the host)
   const int64_t k0 = part * kper, k1 = (part == wpr - 1) ? P.K : k0 + kper;
-  const uint16_t* wrow = (const uint16_t*)dres(P.w[sg], argtab) + lrow * P.K;
-  // weights do not depend on the previous kernel: start them towards L2 now
-  if (active)
+  const int64_t stride = (int64_t)gridDim.x * rows_per_block;
+  // weights do not depend on the previous kernel: start this warp's rows towards L2 now
+  for (int64_t row = (int64_t)blockIdx.x * rows_per_block + warp / wpr; row < P.N; row += stride) {
+    int sg = 0;
+    while (sg < P.nseg - 1 && row >= P.seg_end[sg]) ++sg;
+    const uint16_t* wrow = (const uint16_t*)dres(P.w[sg], argtab) + (row - (sg ? P.seg_end[sg - 1] : 0)) * P.K;
     for (int64_t k = k0 + lane * 64; k < k1; k += 32 * 64) prefetch_l2(wrow + k);
+  }
   pdl_enter();
   const XT* X = (const XT*)dres(P.x, argtab);
-  float acc[MT];
+  // every warp of the block runs the same number of rounds (block-uniform bound)
+  for (int64_t base = (int64_t)blockIdx.x * rows_per_block; base < P.N; base += stride) {
+    const int64_t row = base + warp / wpr;
+    const bool active = row < P.N;
+    int sg = 0;
+    while (sg < P.nseg - 1 && row >= P.seg_end[sg]) ++sg;
+    const int64_t lrow = row - (sg ? P.seg_end[sg - 1] : 0);
+    const uint16_t* wrow = (const uint16_t*)dres(P.w[sg], argtab) + lrow * P.K;
+    float acc[MT];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
-  if (active) {
-    int64_t k = k0 + lane * 8;
-    // main loop: 4 independent 16-byte weight vectors in flight per lane
-    for (; k + 3 * 256 < k1; k += 4 * 256) {
-      uint4 w0 = ld_stream(wrow + k), w1 = ld_stream(wrow + k + 256), w2 = ld_stream(wrow + k + 512),
-            w3 = ld_stream(wrow + k + 768);
+    for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    if (active) {
+      int64_t k = k0 + lane * 8;
+      // main loop: 4 independent 16-byte weight vectors in flight per lane
+      for (; k + 3 * 256 < k1; k += 4 * 256) {
+        uint4 w0 = ld_stream(wrow + k), w1 = ld_stream(wrow + k + 256), w2 = ld_stream(wrow + k + 512),
+              w3 = ld_stream(wrow + k + 768);
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float xv[8];
-        const XT* xr = X + m * P.x_sm;
-        load_x8<XT>(xr + k, xv);
-        float s = dot8(w0, xv);
-        load_x8<XT>(xr + k + 256, xv);
-        s += dot8(w1, xv);
-        load_x8<XT>(xr + k + 512, xv);
-        s += dot8(w2, xv);
-        load_x8<XT>(xr + k + 768, xv);
-        s += dot8(w3, xv);
-        acc[m] += s;
+        for (int m = 0; m < MT; ++m) {
+          float xv[8];
+          const XT* xr = X + m * P.x_sm;
+          load_x8<XT>(xr + k, xv);
+          float s = dot8(w0, xv);
+          load_x8<XT>(xr + k + 256, xv);
+          s += dot8(w1, xv);
+          load_x8<XT>(xr + k + 512, xv);
+          s += dot8(w2, xv);
+          load_x8<XT>(xr + k + 768, xv);
+          s += dot8(w3, xv);
+          acc[m] += s;
+        }
+      }
+      for (; k < k1; k += 256) {
+        uint4 w0 = ld_stream(wrow + k);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float xv[8];
+          load_x8<XT>(X + m * P.x_sm + k, xv);
+          acc[m] += dot8(w0, xv);
+        }
       }
     }
-    for (; k < k1; k += 256) {
-      uint4 w0 = ld_stream(wrow + k);
 #pragma unroll
-      for (int m = 0; m < MT; ++m) {
-        float xv[8];
-        load_x8<XT>(X + m * P.x_sm + k, xv);
-        acc[m] += dot8(w0, xv);
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int s = 16; s > 0; s >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], s);
+    if (wpr > 1) {
+      if (lane == 0)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) red[warp][m] = acc[m];
+      __syncthreads();
+      if (part == 0 && lane == 0 && active) {
+        for (int q = 1; q < wpr; ++q)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) acc[m] += red[warp + q][m];
       }
+      __syncthreads();  // red is rewritten next round
+    }
+    if (active && part == 0 && lane == 0) {
+      char* Y = dres(P.y[sg], argtab);
+      const int64_t nseg_rows = P.seg_end[sg] - (sg ? P.seg_end[sg - 1] : 0);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) store_out(Y, m * nseg_rows + lrow, P.y_dt[sg], acc[m]);
     }
   }
-#pragma unroll
-  for (int m = 0; m < MT; ++m)
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], s);
-  if (wpr > 1) {
-    if (lane == 0)
-#pragma unroll
-      for (int m = 0; m < MT; ++m) red[warp][m] = acc[m];
-    __syncthreads();
-    if (part == 0 && lane == 0 && active) {
-      for (int q = 1; q < wpr; ++q)
-#pragma unroll
-        for (int m = 0; m < MT; ++m) acc[m] += red[warp + q][m];
+  // this CTA's share of the next GEMV's weights: one bulk L2 prefetch per segment
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.npf; ++i) {
+      const int64_t per = ((P.pf_bytes[i] / gridDim.x) + 15) & ~(int64_t)15;
+      const int64_t lo = per * blockIdx.x;
+      int64_t n = P.pf_bytes[i] - lo;
+      if (n > per) n = per;
+      if (n <= 0) continue;
+      const char* src = dres(P.pf[i], argtab) + lo;
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"((uint32_t)n) : "memory");
     }
   }
-  if (active && part == 0 && lane == 0) {
-    char* Y = dres(P.y[sg], argtab);
-    const int64_t nseg_rows = P.seg_end[sg] - (sg ? P.seg_end[sg - 1] : 0);
-#pragma unroll
-    for (int m = 0; m < MT; ++m) store_out(Y, m * nseg_rows + lrow, P.y_dt[sg], acc[m]);
+}
+
+// Launch shape: the grid is at most one wave of resident blocks, each block
+// striding over row groups; the K split per row (1-8 warps) is the one with
+// the least quantised work per warp, iterations x (K / split + 128).
+struct GemvShape {
+  int wpr;
+  unsigned grid;
+};
+
+GemvShape gemv_shape(int64_t N, int64_t K, int resident_blocks) {
+  GemvShape best{1, 1};
+  double best_cost = 1e300;
+  for (int wpr = 1; wpr <= 8; wpr *= 2) {
+    if (wpr > 1 && ((K / wpr) % 8 != 0 || K / wpr < 256)) break;
+    const int64_t rpb = 8 / wpr;
+    const int64_t groups = (N + rpb - 1) / rpb;
+    const int64_t grid = std::min<int64_t>(groups, resident_blocks);
+    const int64_t iters = (groups + grid - 1) / grid;
+    const double cost = (double)iters * ((double)K / wpr + 128.0);
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = GemvShape{wpr, (unsigned)grid};
+    }
   }
+  return best;
+}
+
+template <int MT, typename XT>
+void launch_nt_t(GemvParams p, const uint64_t* argtab, cudaStream_t s) {
+  static int resident = 0;
+  if (!resident) {
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_nt_bf16<MT, XT>, 256, 0);
+    resident = std::max(1, sms * std::max(1, per_sm));
+  }
+  GemvShape sh = gemv_shape(p.N, p.K, resident);
+  p.warps_per_row = sh.wpr;
+  launch_k(gemv_nt_bf16<MT, XT>, dim3(sh.grid), dim3(256), 0, s, 1, p, argtab);
 }
 
 template <int MT>
 void launch_nt(const GemvParams& p, const uint64_t* argtab, cudaStream_t s) {
-  int rows_per_block = 8 / p.warps_per_row;
-  unsigned grid = (unsigned)((p.N + rows_per_block - 1) / rows_per_block);
-  if (p.x_dt == KDT_F32) launch_k(gemv_nt_bf16<MT, float>, dim3(grid), dim3(256), 0, s, 1, p, argtab);
-  else launch_k(gemv_nt_bf16<MT, uint16_t>, dim3(grid), dim3(256), 0, s, 1, p, argtab);
+  if (p.x_dt == KDT_F32) launch_nt_t<MT, float>(p, argtab, s);
+  else launch_nt_t<MT, uint16_t>(p, argtab, s);
 }
 
 int choose_warps_per_row(int64_t N, int64_t K) {
@@ -225,9 +285,46 @@ bool gemv_add_segment(Launch& l, const GemmParams& g) {
   return true;
 }
 
+void link_gemv_prefetch(Plan& plan) {
+  // off by default: on Gemma-3-4B decode 8 MB changed nothing and 24 / 48 MB
+  // cost 1-3 % (the prefetch competes with the tail of the running GEMV);
+  // CLJXLA_B200_GEMV_PREFETCH_MB sets a budget
+  int64_t kMaxPrefetch = 0;
+  if (const char* e = getenv("CLJXLA_B200_GEMV_PREFETCH_MB")) kMaxPrefetch = atoll(e) << 20;
+  GemvParams* prev = nullptr;
+  Launch* prev_l = nullptr;
+  for (Launch& l : plan.launches) {
+    if (l.kind != K_GEMV) continue;
+    GemvParams cur;
+    memcpy(&cur, l.blob.data(), sizeof(cur));
+    if (prev) {
+      GemvParams& p = *prev;
+      p.npf = 0;
+      int64_t budget = kMaxPrefetch;
+      for (int i = 0; i < cur.nseg && budget > 0; ++i) {
+        const int64_t n = cur.seg_end[i] - (i ? cur.seg_end[i - 1] : 0);
+        int64_t bytes = std::min<int64_t>(n * cur.K * 2, budget) & ~(int64_t)15;
+        if (bytes <= 0) break;
+        p.pf[p.npf] = cur.w[i];
+        p.pf_bytes[p.npf] = bytes;
+        p.npf++;
+        budget -= bytes;
+      }
+      memcpy(prev_l->blob.data(), prev, sizeof(GemvParams));
+    }
+    prev_l = &l;
+    prev = (GemvParams*)l.blob.data();
+  }
+}
+
 void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region) {
   (void)plan;
   const GemvParams& p = *(const GemvParams*)l.blob.data();
+  if (p.npf < 0 || p.npf > GEMV_MAXSEG) fail(E_INTERNAL, "gemv: bad prefetch list");
+  for (int i = 0; i < p.npf; ++i) {
+    if (p.pf_bytes[i] % 16 || p.pf[i].off % 16) fail(E_INTERNAL, "gemv: unaligned prefetch");
+    region(p.pf[i], p.pf_bytes[i], "prefetched weights");
+  }
   if (p.nseg < 1 || p.nseg > GEMV_MAXSEG || p.seg_end[p.nseg - 1] != p.N) fail(E_INTERNAL, "gemv: bad segments");
   int64_t xs = dt_size((DT)p.x_dt);
   region(p.x, ((p.M - 1) * p.x_sm + p.K) * xs, "x");

@@ -34,7 +34,7 @@ const char* op_name(Op o) {
                                 "minimum", "exponential", "tanh", "sqrt", "rsqrt", "sine", "cosine",
                                 "logistic", "negate", "abs", "convert", "compare", "select", "iota",
                                 "reshape", "transpose", "broadcast_in_dim", "slice", "concatenate",
-                                "dynamic_update_slice", "gather", "reduce", "dot_general"};
+                                "dynamic_update_slice", "gather", "reduce", "dot_general", "all_reduce"};
   return names[(int)o];
 }
 
@@ -475,6 +475,47 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
       n.shape = t.shape;
       n.dt = t.dt;
       if (numel(t.shape) != g->nodes[n.in[0]].numel()) perr("reshape changes element count", line);
+      add_node(std::move(n), line);
+      continue;
+    }
+    if (starts(rhs, "\"stablehlo.all_reduce\"(")) {
+      // tensor-parallel sum: region of one stablehlo.add, replica_groups = dense<[[0, .., n-1]]>
+      sv args = rhs.substr(23);
+      size_t close = args.find(')');
+      auto ops = parse_operands(args.substr(0, close), line);
+      if (ops.size() != 1) perr("all_reduce expects 1 operand", line);
+      sv body_line, tail_line;
+      for (int k = 0; k < 3 && p < end; ++k) {
+        const char* nl2 = (const char*)memchr(p, '\n', (size_t)(end - p));
+        if (!nl2) nl2 = end;
+        sv l2 = trim(sv(p, (size_t)(nl2 - p)));
+        p = nl2 + 1;
+        if (k == 1) body_line = l2;
+        if (k == 2 && !starts(l2, "\"stablehlo.return\"")) perr("unexpected all_reduce region", l2);
+      }
+      {
+        const char* nl2 = (const char*)memchr(p, '\n', (size_t)(end - p));
+        if (!nl2) nl2 = end;
+        tail_line = trim(sv(p, (size_t)(nl2 - p)));
+        p = nl2 + 1;
+      }
+      if (body_line.find("stablehlo.add ") == sv::npos)
+        fail(E_UNIMPLEMENTED, "all_reduce body not supported: " + std::string(body_line));
+      if (!starts(tail_line, "})")) perr("bad all_reduce tail", tail_line);
+      size_t g = tail_line.find("replica_groups = dense<[[");
+      if (g == sv::npos) perr("all_reduce without replica_groups", tail_line);
+      sv grp = tail_line.substr(g + 25);
+      size_t ge = grp.find("]]");
+      if (ge == sv::npos) perr("bad replica_groups", tail_line);
+      int64_t count = 1;
+      for (char c : grp.substr(0, ge)) count += c == ',';
+      size_t arrow = tail_line.rfind(" -> ");
+      Type t = parse_type(tail_line.substr(arrow + 4), tail_line);
+      n.op = Op::AllReduce;
+      n.i0 = count;
+      n.in = {lookup(ops[0], line)};
+      n.shape = t.shape;
+      n.dt = t.dt;
       add_node(std::move(n), line);
       continue;
     }

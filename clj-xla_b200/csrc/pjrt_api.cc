@@ -11,6 +11,7 @@
 
 #include "../../include/cljxla_b200.h"
 #include "jit.h"
+#include "nccl_rt.h"
 #include "runtime.h"
 
 using namespace cljxla;
@@ -161,8 +162,12 @@ PJRT_Error* Client_Create(void* a) {
       else if (k == "fast_kernels") o.fast_kernels = as_bool();
       else if (k == "cuda_graphs") o.cuda_graphs = as_bool();
       else if (k == "kv_in_place") o.kv_in_place = as_bool();
+      else if (k == "tp_size" && nv.type == PJRT_NamedValue_kInt64) o.tp_size = (int)nv.int64_value;
+      else if (k == "tp_rank" && nv.type == PJRT_NamedValue_kInt64) o.tp_rank = (int)nv.int64_value;
+      else if (k == "tp_nccl_id" && nv.type == PJRT_NamedValue_kString) o.tp_nccl_id.assign(nv.string_value, nv.value_size);
       // other options (e.g. clj-xla's default {:allocator "platform"}) are accepted and ignored
     }
+    if (o.tp_size < 1 || o.tp_rank < 0 || o.tp_rank >= o.tp_size) fail(E_INVALID, "bad tp_size / tp_rank");
     int ndev = 0;
     CUDA_OK(cudaGetDeviceCount(&ndev));
     if (ndev <= 0) fail(E_PRECOND, "no CUDA device visible");
@@ -181,6 +186,10 @@ PJRT_Error* Client_Create(void* a) {
     CUDA_OK(cudaDeviceGetDefaultMemPool(&pool, o.device));
     uint64_t thresh = UINT64_MAX;
     CUDA_OK(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thresh));
+    if (o.tp_size > 1) {
+      if (o.tp_nccl_id.empty()) fail(E_INVALID, "tp_size > 1 needs tp_nccl_id (cljxla_b200_nccl_unique_id on rank 0)");
+      c->nccl_comm = nccl_comm_init(o.tp_size, o.tp_rank, o.tp_nccl_id);  // every rank joins here
+    }
     args->client = c.release();
   });
 }
@@ -191,6 +200,7 @@ PJRT_Error* Client_Destroy(void* a) {
     if (!args->client) return;
     set_device(args->client);
     cudaStreamSynchronize(args->client->stream);
+    nccl_comm_destroy(args->client->nccl_comm);
     cudaStreamDestroy(args->client->stream);
     delete args->client;
   });
@@ -484,6 +494,19 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
     return e.code;
   } catch (const std::exception& e) {
     if (err && errcap) snprintf(err, errcap, "%s", e.what());
+    return E_INTERNAL;
+  }
+}
+
+CLJXLA_EXPORT int cljxla_b200_nccl_unique_id(char* out, size_t cap) {
+  try {
+    std::string h = nccl_unique_id_hex();
+    if (!out || cap < h.size() + 1) return E_INVALID;
+    memcpy(out, h.c_str(), h.size() + 1);
+    return 0;
+  } catch (const Error& e) {
+    return e.code;
+  } catch (...) {
     return E_INTERNAL;
   }
 }

@@ -30,7 +30,8 @@ namespace cljxla {
 
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
-                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc", "fused_multi"};
+                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
+                            "all_reduce"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }
 
@@ -1262,17 +1263,21 @@ void Planner::emit_attention(int d2) {
   int64_t ctas = rows_kv * qtiles;
   // one 128-position round per warp-group of a CTA, at most two CTAs per SM
   int splits = (int)std::min<int64_t>((P.T + 127) / 128, std::max<int64_t>(1, 2 * 148 / ctas));
-  if (splits < 1) splits = 1;
+  splits = std::max(1, std::min(splits, ATTN_MERGE_MAX_SPLITS));
   P.splits = splits;
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
   int64_t rows = (int64_t)P.B * P.nq * P.Sq;
-  if (splits > 1) P.part = slot_ptr(new_tmp((int64_t)splits * rows * (P.hd + 2) * 4));
-  push(K_ATTN_DECODE, blob_of(P), D2.name, kvbytes, 4LL * rows * P.T * P.hd);
   if (splits > 1) {
-    touch(P.part.slot);
-    push(K_ATTN_COMBINE, blob_of(P), D2.name, (int64_t)splits * rows * (P.hd + 2) * 4);
+    P.part = slot_ptr(new_tmp((int64_t)splits * rows * (P.hd + 2) * 4));
+    // arrival counters (zero in the uploaded constant blob, reset by the merging CTA)
+    const int64_t groups = rows_kv * qtiles;
+    size_t off = (plan_.const_blob.size() + 255) & ~size_t(255);
+    plan_.const_blob.resize(off + 4 * groups, 0);
+    P.counters = slot_ptr(P_ + O_ + U_, (int64_t)off);
+    P.use_counters = 1;
   }
+  push(K_ATTN_DECODE, blob_of(P), D2.name, kvbytes, 4LL * rows * P.T * P.hd);
 }
 
 bool Planner::splat_value(int n, double& v) {
@@ -1441,6 +1446,29 @@ void Planner::emit_node_kernel(int id) {
         push(K_COPY, blob_of(C), n.name, 2 * C.n * (int64_t)dt_size(n.dt));
         off += xn.shape[dim];
       }
+      break;
+    }
+    case Op::AllReduce: {
+      // NCCL reads and writes plain device addresses: a dense arena copy of the
+      // operand in, the arena result slot out (both fixed for the executable)
+      const Node& in = g_.nodes[n.in[0]];
+      if (!(n.dt == DT::F32 || n.dt == DT::BF16 || n.dt == DT::F16) || in.dt != n.dt)
+        fail(E_UNIMPLEMENTED, "all_reduce of element type " + std::string(dt_name(n.dt)));
+      TView v = view_of(n.in[0]);
+      bool dense = v.p.slot >= tmp_slot(0) && v.p.off % 16 == 0;
+      int64_t acc = 1;
+      for (int d = v.rank - 1; d >= 0 && dense; --d) {
+        if (v.shape[d] != 1 && v.stride[d] != acc) dense = false;
+        acc *= v.shape[d];
+      }
+      if (!dense) v = materialize(v, in.shape, in.dt);
+      AllReduceParams A{};
+      A.src = v.p;
+      A.dst = slot_ptr(oslot);
+      A.count = n.numel();
+      A.dt = kdt(n.dt);
+      A.ranks = (int32_t)n.i0;
+      push(K_ALLREDUCE, blob_of(A), n.name, 2 * n.numel() * (int64_t)dt_size(n.dt));
       break;
     }
     case Op::Dot: {
@@ -1842,7 +1870,8 @@ void Planner::run() {
   for (int k = 0; k < O_; ++k) {
     int n = g_.outputs[k];
     if (out_claim_[n] >= 0) continue;
-    if ((loc_[n].kind == Loc::BUF && g_.nodes[n].op != Op::Param && g_.nodes[n].op != Op::Constant) ||
+    if ((loc_[n].kind == Loc::BUF && g_.nodes[n].op != Op::Param && g_.nodes[n].op != Op::Constant &&
+         g_.nodes[n].op != Op::AllReduce) ||  // a collective's result stays in the arena (graph capture)
         loc_[n].kind == Loc::EW || loc_[n].kind == Loc::ROW)
       out_claim_[n] = k;
   }
@@ -1863,6 +1892,7 @@ void Planner::run() {
   verify_plan(plan_);
   if (opt_.fuse) {
     schedule_and_merge(plan_);
+    if (opt_.fast_kernels) link_gemv_prefetch(plan_);
     verify_plan(plan_);
   }
   if (const char* path = getenv("CLJXLA_B200_DUMP_PLAN")) {

@@ -14,9 +14,19 @@ enum KernelKind : int {
   K_EW = 0, K_REDUCE, K_COPY, K_GATHER, K_DUS, K_GEMM,
   K_GEMV, K_ATTN_DECODE, K_ATTN_COMBINE, K_ROWNORM, K_GEMM_TC,
   K_MULTI,  // independent compiled fused kernels merged into one launch (parts)
+  K_ALLREDUCE,  // tensor-parallel sum over the client's NCCL communicator
   K_NUM_KINDS
 };
 const char* kernel_kind_name(int k);
+
+// all_reduce(sum) of `count` elements of type dt from src into dst; both in
+// the scratch arena, whose addresses are fixed for the executable's life, so
+// the collective can be captured into the CUDA graph.
+struct AllReduceParams {
+  DPtr src, dst;
+  int64_t count;
+  int32_t dt, ranks;
+};
 
 // Buffers of a compiled fused kernel, passed by value at launch: buffer k is
 // argument-table slot s[k] plus byte offset o[k] (s[k] < 0: o[k] is the address).

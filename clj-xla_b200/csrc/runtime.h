@@ -106,6 +106,10 @@ struct ClientOptions {
   bool fast_kernels = true;
   bool cuda_graphs = true;
   bool kv_in_place = true;
+  // tensor parallelism: this client is rank tp_rank of tp_size, joined through
+  // the NCCL unique id tp_nccl_id (hex) that every rank was given
+  int tp_size = 1, tp_rank = 0;
+  std::string tp_nccl_id;
 };
 
 struct PJRT_Client {
@@ -115,6 +119,7 @@ struct PJRT_Client {
   cudaStream_t stream = nullptr;
   std::mutex mu;
   std::string platform = "cuda";
+  void* nccl_comm = nullptr;  // tp_size > 1
 };
 
 namespace cljxla {

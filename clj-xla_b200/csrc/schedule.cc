@@ -18,11 +18,16 @@
 namespace cljxla {
 namespace {
 
-enum Space { SP_ARENA, SP_DYN, SP_CONST, SP_TMAP, SP_ABS };
+// Arguments, results and undo records are buffers the executor binds per run:
+// each is its own space (SP_BUF + slot), accessed as a whole.  A result that a
+// KV update writes in place is the storage of its argument, so it shares the
+// argument's space; other arguments may share storage with each other but are
+// only read, and fresh results and undo records alias nothing.
+enum Space { SP_ARENA, SP_CONST, SP_TMAP, SP_ABS, SP_BUF };
 
 struct Access {
   int space;
-  int64_t lo, hi;  // bytes in that space (SP_DYN: whole space)
+  int64_t lo, hi;  // bytes in that space (SP_BUF: the whole buffer)
   bool write;
 };
 
@@ -39,7 +44,10 @@ struct Collector {
       a.lo = d.off;
       a.hi = d.off + bytes;
     } else if (d.slot < P + O + U) {
-      a.space = SP_DYN;
+      int slot = d.slot;
+      for (const InplaceDus& ip : p.inplace)
+        if (slot == P + ip.out) slot = ip.param;
+      a.space = SP_BUF + slot;
       a.lo = 0;
       a.hi = 1;
     } else if (d.slot == p.const_slot()) {
@@ -160,7 +168,9 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
         c.view(a.v, false);
         c.view(a.mask, false);
         if (a.splits > 1) c.add(a.part, part, true);
-        else c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
+        if (a.splits == 1 || a.use_counters) c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
+        if (a.splits > 1 && a.use_counters)
+          c.add(a.counters, 4LL * a.B * a.nkv * ((a.Sq + a.qtile - 1) / a.qtile), true);
       } else {
         c.add(a.part, part, false);
         c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
@@ -187,7 +197,6 @@ bool conflict(const std::vector<Access>& a, const std::vector<Access>& b) {
       if (!x.write && !y.write) continue;
       if (x.space == SP_ABS || y.space == SP_ABS) return true;
       if (x.space != y.space) continue;
-      if (x.space == SP_DYN) return true;
       if (x.lo < y.hi && y.lo < x.hi) return true;
     }
   return false;

@@ -174,6 +174,13 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
         c.region(g.c, g.batch * g.M * g.N * (int64_t)esz(g.c_dt), "result");
         break;
       }
+      case K_ALLREDUCE: {
+        const AllReduceParams& a = *(const AllReduceParams*)b;
+        if (a.ranks < 1 || a.count < 0) fail(E_INTERNAL, "bad all_reduce");
+        c.region(a.src, a.count * (int64_t)esz(a.dt), "all_reduce source");
+        c.region(a.dst, a.count * (int64_t)esz(a.dt), "all_reduce destination");
+        break;
+      }
       default:
         verify_fast_launch_impl(p, l, [&](const DPtr& d, int64_t bytes, const char* what) { c.region(d, bytes, what); });
         break;

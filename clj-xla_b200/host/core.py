@@ -77,6 +77,17 @@ def clear_cache():
     _EXEC_CACHE.clear()
 
 
+def close_backend(ctx: Context):
+    """Destroys the client's cached executables and then the client (a
+    tensor-parallel client also leaves its NCCL group)."""
+    global _DEFAULT_CONTEXT
+    for key in [k for k in _EXEC_CACHE if k[0] == ctx["client"]]:
+        ctx["api"].destroy_executable(_EXEC_CACHE.pop(key)["handle"])
+    ctx["api"].destroy_client(ctx["client"])
+    if _DEFAULT_CONTEXT is ctx:
+        _DEFAULT_CONTEXT = None
+
+
 def buffer_from_host_buffer(ctx: Context, host_data: np.ndarray, shape: Sequence[int], dtype_enum: int) -> int:
     return ctx["api"].buffer_from_host_buffer(ctx["client"], host_data, list(shape), dtype_enum)
 
@@ -167,6 +178,30 @@ def client_stream(ctx: Context) -> int:
     f.argtypes = [ctypes.c_void_p]
     f.restype = ctypes.c_void_p
     return f(ctypes.c_void_p(ctx["client"])) or 0
+
+
+def nccl_unique_id(lib_path: Optional[str] = None) -> str:
+    """Hex NCCL unique id for a tensor-parallel group (made on one rank, passed
+    to every rank's client as ``tp_nccl_id``).  Needs no device."""
+    lib = ctypes.CDLL(lib_path or default_library_path())
+    f = lib.cljxla_b200_nccl_unique_id
+    f.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    f.restype = ctypes.c_int
+    buf = ctypes.create_string_buffer(512)
+    rc = f(buf, 512)
+    if rc != 0:
+        raise RuntimeError(f"cljxla_b200_nccl_unique_id failed ({rc})")
+    return buf.value.decode()
+
+
+def init_tp_backend(tp_size: int, tp_rank: int, nccl_id: str, device: Optional[int] = None,
+                    target: Optional[str] = None) -> Context:
+    """A client that is rank ``tp_rank`` of a ``tp_size``-way tensor-parallel
+    group: every rank calls this with the same ``nccl_id`` (collective)."""
+    opts = {"allocator": "platform", "tp_size": int(tp_size), "tp_rank": int(tp_rank), "tp_nccl_id": nccl_id}
+    if device is not None:
+        opts["device"] = int(device)
+    return init_backend(target, opts)
 
 
 def plan_text(lib_path: str, text: str, fuse: bool = True) -> dict:

@@ -45,6 +45,7 @@ class ModelConfig:
     final_softcap: Optional[float] = None
     window: Optional[int] = None          # local attention window
     n_positions: int = 1024               # GPT-2 learned position table
+    tp: int = 1                           # tensor-parallel ranks this (per-rank) config is a shard of
 
     def is_local(self, i: int) -> bool:
         if self.window is None:
@@ -76,6 +77,39 @@ CONFIGS: Dict[str, ModelConfig] = {
 
 def round_up(n: int, m: int) -> int:
     return ((n + m - 1) // m) * m
+
+
+# ------------------------------------------------------- tensor parallelism
+def shard_config(cfg: ModelConfig, tp: int) -> ModelConfig:
+    """Per-rank config of a tensor-parallel Gemma: query / KV heads and the MLP
+    width split over ``tp`` ranks (Megatron column split of q/k/v and gate/up,
+    row split of o and down), embedding, norms and LM head replicated.  An
+    addition of this repository; the reference runs on one device."""
+    if tp == 1:
+        return cfg
+    if cfg.family == "gpt2":
+        raise ValueError("tensor parallelism is provided for the Gemma families")
+    if cfg.n_heads % tp or cfg.n_kv_heads % tp or cfg.mlp % tp:
+        raise ValueError(f"heads {cfg.n_heads}/{cfg.n_kv_heads} and MLP {cfg.mlp} must divide by tp={tp}")
+    return replace(cfg, n_heads=cfg.n_heads // tp, n_kv_heads=cfg.n_kv_heads // tp, mlp=cfg.mlp // tp, tp=tp)
+
+
+def shard_weights(cfg: ModelConfig, weights: List[np.ndarray], rank: int, tp: int) -> List[np.ndarray]:
+    """Rank ``rank``'s slices of the full weights (invar order of weight_specs)."""
+    if tp == 1:
+        return list(weights)
+    out = []
+    for (name, shp, _), w in zip(weight_specs(cfg), weights):
+        base = name.rsplit("_", 1)[0] if name[-1].isdigit() else name
+        if base in ("q_w", "k_w", "v_w", "gate_w", "up_w"):   # column split: rows of [N, K]
+            n = w.shape[0] // tp
+            out.append(np.ascontiguousarray(w[rank * n:(rank + 1) * n]))
+        elif base in ("o_w", "down_w"):                      # row split: columns of [N, K]
+            k = w.shape[1] // tp
+            out.append(np.ascontiguousarray(w[:, rank * k:(rank + 1) * k]))
+        else:
+            out.append(w)
+    return out
 
 
 # ------------------------------------------------------------------ invars
@@ -147,6 +181,8 @@ def _gemma_layer_maps(cfg: ModelConfig, weight_args):
                 m["attn-softcap"] = cfg.attn_softcap
         if cfg.is_local(i):
             m["sliding-window"] = cfg.window
+        if cfg.tp > 1:
+            m["tp"] = cfg.tp
         maps.append(m)
     return maps
 

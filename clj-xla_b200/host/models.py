@@ -13,7 +13,7 @@ import math
 
 from . import tensor as t
 from .nn import (apply_rope, gelu, gemma_rms_norm, gqa_causal_attention, layer_norm,
-                 causal_self_attention, rms_norm, linear as attn_linear)
+                 causal_self_attention, rms_norm, rms_norm_split, linear as attn_linear)
 
 
 # ------------------------------------------------------------------ gpt2.clj
@@ -118,7 +118,11 @@ def gemma_attention(x, q_w, k_w, v_w, o_w, num_heads, _num_kv_heads, pos_ids, pa
     v_w_t = t.transpose(v_w, [1, 0])
     k = gemma_linear(x, k_w_t, None)
     v_raw = gemma_linear(x, v_w_t, None)
-    v = rms_norm(v_raw, None, 1e-6) if q_norm_w is not None else v_raw
+    tp = opts.get("tp", 1)
+    if q_norm_w is not None:
+        v = rms_norm(v_raw, None, 1e-6) if tp == 1 else rms_norm_split(v_raw, 1e-6, tp)
+    else:
+        v = v_raw
     kv_dim = k.type[1][-1]
     l_nkv = kv_dim // h_dim
     k4 = t.transpose(t.reshape(k, [batch, seq_len, l_nkv, h_dim]), [0, 2, 1, 3])
@@ -148,15 +152,20 @@ def gemma_block(x, w, num_heads, num_kv_heads, pos_ids, past_kv=None, pos=None):
                  "theta-base": w.get("theta-base", 10000.0), "attn-softcap": w.get("attn-softcap"),
                  "rotary-dim": w.get("rotary-dim"), "head-dim": w.get("head-dim"),
                  "rope-proportion": w.get("rope-proportion", 1.0), "norm-fn": norm_fn,
-                 "sliding-window": w.get("sliding-window")}
+                 "sliding-window": w.get("sliding-window"), "tp": w.get("tp", 1)}
     attn_raw, updated, _ = gemma_attention(xn1, w["q-w"], w["k-w"], w["v-w"], w["o-w"], num_heads, num_kv_heads,
                                            pos_ids, past_kv, pos, attn_opts)
+    tp = w.get("tp", 1)
+    if tp > 1:  # tensor parallel: the o-projection of the local heads is a partial sum
+        attn_raw = t.all_reduce(attn_raw, tp)
     pa = w.get("post-attn-ln-w")
     attn_normed = norm_fn(attn_raw, pa, 1e-6) if pa is not None else attn_raw
     attn_out = t.add(attn_normed, x)
     pm = w.get("pre-mlp-ln-w")
     xn2 = norm_fn(attn_out, pm, 1e-6) if pm is not None else attn_out
     mlp_raw = gemma_mlp(xn2, w["gate-w"], w["up-w"], w["down-w"])
+    if tp > 1:  # the down-projection of the local MLP slice is a partial sum
+        mlp_raw = t.all_reduce(mlp_raw, tp)
     po = w.get("post-mlp-ln-w")
     mlp_normed = norm_fn(mlp_raw, po, 1e-6) if po is not None else mlp_raw
     out = t.add(mlp_normed, attn_out)

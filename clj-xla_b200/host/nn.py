@@ -33,6 +33,19 @@ def rms_norm(x, weight, eps=1e-6):
     return x_hat
 
 
+def rms_norm_split(x, eps, tp):
+    """``rms_norm(x, None, eps)`` when the last dimension of ``x`` is split over
+    ``tp`` tensor-parallel ranks: the local sums of squares are all-reduced so
+    every rank divides by the root mean square of the whole, unsplit row (the
+    Gemma-3 value projection is normalised across all heads, gemma.clj:166-167).
+    An addition of this repository for tensor parallelism."""
+    tx = t.emit_constant(x, None)
+    full = tx.type[1][-1] * tp
+    ss = t.all_reduce(t.reduce_sum(t.pow(tx, 2.0), axes=[-1], keep_dims=True), tp)
+    ms = t.div(ss, float(full))
+    return t.div(tx, t.sqrt(t.add(ms, eps)))
+
+
 def gemma_rms_norm(x, weight, eps=1e-6):
     """norm.clj:28-35 - ``... * (1 + w)``."""
     ms = t.reduce_mean(t.pow(x, 2.0), axes=[-1], keep_dims=True)

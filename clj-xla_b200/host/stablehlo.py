@@ -400,6 +400,19 @@ def format_equation(eqn: dict, var_types: Dict[str, str]) -> str:
                 f'      "stablehlo.return"(%arg_res) : (tensor<{in_dt}>) -> ()\n'
                 f"    }}) {{dimensions = array<i64: {', '.join(str(a) for a in na)}>}} : ({it}, tensor<{in_dt}>) -> {rt}\n"
                 f"    %{out} = stablehlo.reshape %{out}_red : ({rt}) -> {ot}")
+    if op == "stablehlo/all_reduce":
+        # tensor-parallel partial sums; an addition of this repository (the
+        # reference prints no collectives: clj-xla runs on one device)
+        iv = invars[0]
+        it = var_types.get(iv, "tensor<f32>")
+        _, dt = parse_tensor_dims(it)
+        n = int(attrs["replica_count"])
+        ranks = ", ".join(str(i) for i in range(n))
+        return (f'    %{out} = "stablehlo.all_reduce"(%{iv}) ({{\n'
+                f"    ^bb0(%arg_a: tensor<{dt}>, %arg_b: tensor<{dt}>):\n"
+                f"      %arg_res = stablehlo.add %arg_a, %arg_b : tensor<{dt}>\n"
+                f'      "stablehlo.return"(%arg_res) : (tensor<{dt}>) -> ()\n'
+                f"    }}) {{replica_groups = dense<[[{ranks}]]> : tensor<1x{n}xi64>}} : ({it}) -> {it}")
     if op == "stablehlo/dot_general":
         lhs, rhs = invars
         lt = var_types.get(lhs, "tensor<1x128x768xf32>")

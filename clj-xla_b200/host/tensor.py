@@ -439,6 +439,18 @@ def argmax(x, axis=-1):
     return reduce_max(masked, axes=[ax], keep_dims=False)
 
 
+def all_reduce(x, replica_count: int):
+    """Sum of ``x`` over the ``replica_count`` ranks of a tensor-parallel group.
+
+    An addition of this repository for tensor parallelism: the reference
+    (clj-xla) has no multi-device code and its tensor API no collectives."""
+    tx = emit_constant(x, None)
+    out_id = gen_var_id("t_allreduce")
+    _emit({"op": "stablehlo/all_reduce", "invars": [tx.id], "outvars": [out_id],
+           "attrs": {"replica_count": int(replica_count)}})
+    return Tracer(out_id, tx.type)
+
+
 def trace_graph(graph_name: str, invars, f) -> dict:
     """trace.clj:6-22 - run ``f`` on input Tracers and collect the EDN graph."""
     global _CTX

@@ -70,6 +70,14 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
 CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags, int* kernels, char* err,
                                         size_t errcap);
 
+/* Tensor parallelism (no counterpart in the reference, which runs on one
+ * device).  A graph with "stablehlo.all_reduce" ops is one rank's shard of a
+ * model; its client is created with the named values tp_size (int64),
+ * tp_rank (int64) and tp_nccl_id (string): the hex id this function returns on
+ * one rank (256 characters + NUL into out[cap]), passed to every rank by the
+ * host.  Returns 0 or a PJRT_Error_Code (9: NCCL could not be loaded). */
+CLJXLA_EXPORT int cljxla_b200_nccl_unique_id(char* out, size_t cap);
+
 /* The cudaStream_t a client launches on (for event timing by the caller). */
 CLJXLA_EXPORT void* cljxla_b200_stream(const PJRT_Client* client);
 

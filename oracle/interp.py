@@ -192,6 +192,16 @@ def parse_module(text: str) -> Module:
             ins, rt = sig.split(" -> ")
             ops.append(Op("reduce", out, args, {"dimensions": dims}, None, parse_type(rt), body_op))
             continue
+        if rhs.startswith('"stablehlo.all_reduce"('):
+            body_line = lines[i + 1].strip()
+            close = lines[i + 3].strip()
+            i += 4
+            body_op = re.match(r"%arg_res = (stablehlo\.\w+)", body_line).group(1)
+            args = re.findall(r"%([\w.]+)", rhs[len('"stablehlo.all_reduce"('):].split(")")[0])
+            groups = re.search(r"replica_groups = dense<\[\[([^\]]*)\]\]>", close).group(1)
+            rt = close.rsplit(" -> ", 1)[1]
+            ops.append(Op("all_reduce", out, args, {"replicas": len(_ints(groups))}, None, parse_type(rt), body_op))
+            continue
         if rhs.startswith("stablehlo.constant dense<"):
             lit, rt = rhs[len("stablehlo.constant dense<"):].rsplit("> : ", 1)
             ops.append(Op("constant", out, [], {"literal": lit}, None, parse_type(rt)))
@@ -306,10 +316,12 @@ class Interpreter:
     causes as the noise floor of a whole bf16 model (see tests/parity.py).
     """
 
-    def __init__(self, text: str, ulp_noise_seed=None):
+    def __init__(self, text: str, ulp_noise_seed=None, collective=None):
         self.module = parse_module(text) if isinstance(text, str) else text
         self._consts: Dict[str, np.ndarray] = {}
         self._noise = None if ulp_noise_seed is None else np.random.default_rng(ulp_noise_seed)
+        # all_reduce: collective(value) -> the sum over the group (see run_mlir_tp)
+        self._collective = collective
 
     def run(self, inputs: List[np.ndarray], keep_all: bool = False):
         m = self.module
@@ -428,6 +440,10 @@ class Interpreter:
                 idx.append(slice(s, s + upd.shape[d]))
             out[tuple(idx)] = upd
             return out
+        if name == "all_reduce":
+            if self._collective is None:
+                raise ValueError("all_reduce needs the ranks of its group (run_mlir_tp)")
+            return to_dtype(self._collective(np.asarray(args[0], np.float32)), dt)
         if name == "gather":
             return self._gather(op, args, shape, dt)
         if name == "reduce":
@@ -509,3 +525,45 @@ class Interpreter:
 
 def run_mlir(text: str, inputs, keep_all=False, ulp_noise_seed=None):
     return Interpreter(text, ulp_noise_seed).run(inputs, keep_all=keep_all)
+
+
+def run_mlir_tp(texts, inputs_per_rank, ulp_noise_seed=None):
+    """Runs the per-rank graphs of a tensor-parallel group together, one thread
+    per rank.  Each all_reduce is the sum, in f64 and in rank order, of the
+    ranks' f32 values, rounded to the result type by the caller's op."""
+    import threading
+    n = len(texts)
+    barrier = threading.Barrier(n)
+    slots = [None] * n
+    result = [None]
+    outs = [None] * n
+    errors = []
+
+    def worker(r):
+        def collective(x):
+            slots[r] = x
+            barrier.wait()
+            if r == 0:
+                acc = np.zeros(x.shape, np.float64)
+                for v in slots:
+                    acc += v
+                result[0] = acc
+            barrier.wait()
+            y = result[0]
+            barrier.wait()
+            return y
+        try:
+            seed = None if ulp_noise_seed is None else ulp_noise_seed + 1000 * r
+            outs[r] = Interpreter(texts[r], seed, collective).run(inputs_per_rank[r])
+        except Exception as e:  # noqa: BLE001 - reported after the join
+            errors.append(e)
+            barrier.abort()
+
+    threads = [threading.Thread(target=worker, args=(r,)) for r in range(n)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    if errors:
+        raise errors[0]
+    return outs

@@ -1,0 +1,93 @@
+"""Tensor-parallel decoding on 2 B200s (one process per GPU, NCCL all-reduce
+inside each rank's executable) against the oracle's tensor-parallel executor
+running the same shard graphs.  Skipped with fewer than 2 GPUs."""
+import dataclasses
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+
+import conftest  # noqa: F401  - registers the cljxla_b200 package (also in spawned ranks)
+from cljxla_b200.host import core, drivers as d, tp
+from oracle import interp
+
+from parity import close, close_model, close_model_floor
+
+pytestmark = pytest.mark.gpu
+
+TINY3 = dataclasses.replace(d.GEMMA3_4B, vocab=512, d_model=256, layers=6, n_heads=4, n_kv_heads=2,
+                            head_dim=64, mlp=512, window=6)
+NOISE_SEEDS = (1, 2, 3, 4)
+
+
+def _gpu_count():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _rank(rank, world, nid, cfg_full, prompt, T, steps, q):
+    try:
+        ctx = core.init_tp_backend(world, rank, nid, device=rank)
+        cfg, gp, gd = tp.shard_graphs(cfg_full, world, prompt.shape[0], prompt.shape[1], T)
+        w = d.shard_weights(cfg_full, d.make_weights(cfg_full), rank, world)
+        toks, logits = tp.greedy_generate(ctx, cfg, gp, gd, w, prompt, T, steps)
+        core.close_backend(ctx)
+        q.put((rank, toks, logits, None))
+    except Exception as e:  # noqa: BLE001 - reported by the parent
+        q.put((rank, None, None, repr(e)))
+
+
+def _run_group(cfg_full, world, prompt, T, steps):
+    nid = core.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, cfg_full, prompt, T, steps, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, toks, logits, err = q.get(timeout=600)
+            assert err is None, f"rank {r}: {err}"
+            res[r] = (toks, logits)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_tp2_greedy_decode_matches_oracle(dtype):
+    cfg = dataclasses.replace(TINY3, dtype=dtype)
+    B, S, T, steps = 1, 6, 32, 12
+    prompt = d.make_prompt(cfg, B, S)
+    w = d.make_weights(cfg)
+    res = _run_group(cfg, 2, prompt, T, steps)
+    o_toks, o_logits = tp.oracle_generate(cfg, 2, w, prompt, T, steps, interp.run_mlir_tp, interp.run_mlir)
+    # every rank holds the same all-reduced logits and picks the same tokens
+    assert res[0][0] == res[1][0]
+    for a, b in zip(res[0][1], res[1][1]):
+        assert np.array_equal(a, b)
+    assert res[0][0] == o_toks
+    floors = None
+    for i, (a, b) in enumerate(zip(res[0][1], o_logits)):
+        if dtype == "f32":
+            ok, excess, err = close(a, b, "f32")
+            assert ok, f"step {i}: f32 logits differ, max err {err:.3g}"
+            continue
+        else:
+            ok, bad, rr = close_model(a, b, "bf16")
+            if not ok:
+                if floors is None:
+                    floors = [tp.oracle_generate(
+                        cfg, 2, w, prompt, T, steps,
+                        lambda texts, ins, sd=sd: interp.run_mlir_tp(texts, ins, ulp_noise_seed=sd),
+                        interp.run_mlir)[1] for sd in NOISE_SEEDS]
+                ok, bad, rr, _, _ = close_model_floor(a, b, [f[i] for f in floors], "bf16")
+        assert ok, f"step {i}: {bad:.2%} out of bound, rel rms {rr:.3g}"

@@ -1,0 +1,144 @@
+"""Tensor parallelism, host side (no device): shard configs and weights, the
+printed all_reduce, planning of shard graphs by the library, the oracle's
+tensor-parallel executor against the unsharded model, and sharing of the NCCL
+id over a 2-rank gloo group."""
+import dataclasses
+import multiprocessing as mp
+import os
+import re
+import socket
+
+import numpy as np
+import pytest
+
+import conftest  # noqa: F401  - registers the cljxla_b200 package (also in spawned ranks)
+from cljxla_b200.host import core, drivers as d, tp
+from cljxla_b200.host import stablehlo as shlo
+from oracle import interp
+
+from parity import close
+
+TINY3 = dataclasses.replace(d.GEMMA3_4B, vocab=512, d_model=256, layers=6, n_heads=4, n_kv_heads=2,
+                            head_dim=64, mlp=512, window=6)
+TINY2 = dataclasses.replace(d.GEMMA2_2B, vocab=512, d_model=256, layers=2, n_heads=4, n_kv_heads=2,
+                            head_dim=64, mlp=512, window=6)
+
+
+@pytest.fixture(scope="module")
+def lib_path():
+    import __graft_entry__
+    __graft_entry__.build()
+    from cljxla_b200 import LIB_PATH
+    return LIB_PATH
+
+
+def test_shard_config_divides_heads_and_mlp():
+    c = d.shard_config(d.GEMMA3_27B, 8)
+    assert (c.n_heads, c.n_kv_heads, c.mlp, c.tp) == (4, 2, 21504 // 8, 8)
+    assert c.d_model == d.GEMMA3_27B.d_model and c.vocab == d.GEMMA3_27B.vocab
+    with pytest.raises(ValueError):
+        d.shard_config(d.GEMMA3_4B, 8)          # 4 KV heads do not split 8 ways
+    with pytest.raises(ValueError):
+        d.shard_config(d.GPT2_SMALL, 2)
+
+
+def test_row_and_column_split_reassemble_the_projection():
+    """Column split of q/gate (output rows) and row split of o/down (input
+    columns): the ranks' partial products sum to the unsharded product."""
+    full = d.make_weights(TINY3)
+    specs = d.weight_specs(TINY3)
+    ws = [d.shard_weights(TINY3, full, r, 2) for r in range(2)]
+    idx = {n: i for i, (n, _, _) in enumerate(specs)}
+    q, o = idx["q_w_0"], idx["o_w_0"]
+    f32 = interp.bf16_bits_to_f32
+    assert np.array_equal(np.concatenate([f32(ws[0][q]), f32(ws[1][q])], 0), f32(full[q]))
+    x = np.random.default_rng(0).standard_normal((3, full[o].shape[1])).astype(np.float32)
+    half = full[o].shape[1] // 2
+    parts = sum(x[:, r * half:(r + 1) * half] @ f32(ws[r][o]).T for r in range(2))
+    np.testing.assert_allclose(parts, x @ f32(full[o]).T, rtol=1e-5, atol=1e-5)
+    # replicated weights are the same objects' values
+    e = idx["embed_tokens"]
+    assert np.array_equal(ws[1][e], full[e])
+
+
+@pytest.mark.parametrize("cfg", [TINY3, TINY2], ids=["gemma3", "gemma2"])
+def test_printed_shard_graph_has_all_reduces(cfg):
+    sc = d.shard_config(cfg, 2)
+    txt = shlo.graph_to_mlir_text(d.build_graph(sc, "decode", 1, 8, 16))
+    n = len(re.findall(r'"stablehlo\.all_reduce"\(', txt))
+    # o-projection and down-projection per layer; Gemma-3 adds the V-norm sum of squares
+    per_layer = 3 if cfg.family == "gemma3" else 2
+    assert n == per_layer * cfg.layers
+    assert "replica_groups = dense<[[0, 1]]> : tensor<1x2xi64>" in txt
+    assert "stablehlo.add" in txt.split('"stablehlo.all_reduce"(', 1)[1].split("})", 1)[0]
+
+
+def test_library_plans_shard_graphs(lib_path):
+    sc = d.shard_config(d.GEMMA3_27B, 8)
+    for kind in ("decode", "prefill"):
+        g = d.build_graph(sc, kind, 1, 16, 128, dynamic_prefill=kind == "prefill")
+        info = core.plan_text(lib_path, shlo.graph_to_mlir_text(g), 3)
+        assert info["launches"] >= 3 * sc.layers
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_tp_oracle_matches_unsharded_oracle(dtype):
+    """The 2-rank oracle (f64 rank-order sums) decodes the same greedy tokens
+    as the unsharded graph.  In f32 the logits agree to the f32 tolerance (the
+    sharding only reorders sums); in bf16 each rank rounds its partial
+    projection to bf16 before the sum, a different rounding than one bf16
+    rounding of the whole dot, so only a loose bound holds there."""
+    cfg = dataclasses.replace(TINY3, dtype=dtype)
+    w = d.make_weights(cfg)
+    prompt = d.make_prompt(cfg, 1, 6)
+    t1, l1 = tp.oracle_generate(cfg, 1, w, prompt, 16, 5, interp.run_mlir_tp, interp.run_mlir)
+    t2, l2 = tp.oracle_generate(cfg, 2, w, prompt, 16, 5, interp.run_mlir_tp, interp.run_mlir)
+    assert t1 == t2
+    for a, b in zip(l2, l1):
+        if dtype == "f32":
+            ok, excess, err = close(a, b, "f32")
+            assert ok, (excess, err)
+        else:
+            rr = float(np.sqrt(np.mean((a - b) ** 2)) / np.sqrt(np.mean(b ** 2)))
+            assert rr < 0.05, rr
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _gloo_rank(rank, world, port, lib, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        q.put((rank, tp.share_nccl_id(lib)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_id_shared_over_two_gloo_ranks(lib_path):
+    try:
+        core.nccl_unique_id(lib_path)
+    except RuntimeError:
+        pytest.skip("NCCL not loadable on this host")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, lib_path, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q.get(timeout=90) for _ in range(2))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert set(got) == {0, 1}
+    assert got[0] == got[1] and len(got[0]) == 256 and int(got[0], 16) >= 0

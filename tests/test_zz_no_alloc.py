@@ -81,7 +81,7 @@ def test_static_scratch_matches_execute_twice(ctx):
     g = attention_graph()
     text = shlo.graph_to_mlir_text(g)
     exe = core.compile_mlir_text(ctx, text, g)
-    assert core.plan_info(ctx, exe)["launches"] == 2  # matched: attention + combine (scratch partials)
+    assert core.plan_info(ctx, exe)["launches"] == 1  # matched: attention, splits merged in-kernel
     host = inputs()
     api, lib = ctx["api"], ctx["api"].lib
     bufs = [core.buffer_from_host_buffer(ctx, a, a.shape, DTYPE_ENUM[dt])
