@@ -326,6 +326,7 @@ def run_ours(args, rank, world, local_rank):
 
     for b in kv + xs + ps + wbufs + [x_pre, p_pre]:
         api.destroy_buffer(b)
+    plan = core.plan_info(ctx, ex_dec)
     core.close_backend(ctx)
 
     tokens = B * args.steps
@@ -334,7 +335,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e_tokens": B * e2e_steps, "launches": launches, "clocks": clk.summary(),
         "by_kind": by_kind, "total_ms": total_ms, "dom": dom[0], "achieved": achieved,
         "hbm_peak": hbm_peak, "peak_src": peak_src, "cpu": cpu, "t_weights": t_w, "t_compile": t_c,
-        "plan": core.plan_info(ctx, ex_dec), "logits_bytes": logits_bytes,
+        "plan": plan, "logits_bytes": logits_bytes,
     }
     return cfg, B, S, T, res
 

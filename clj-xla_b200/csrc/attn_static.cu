@@ -124,6 +124,9 @@ extern "C" CLJXLA_EXPORT int cljxla_b200_attention_decode_static(const void* q, 
   P.chain[1] = mul;
   P.nchain = 2;
   P.chain_out = 2;
+  P.chain_kind = 1;  // the same multiply in closed form
+  P.chain_c = imm.fimm;
+  P.chain_dt = KDT_BF16;
   P.out.slot = -1;
   P.out.off = (int64_t)(uintptr_t)out;
   // same split rule as the planner: enough CTAs for two waves, >= 64 positions per split

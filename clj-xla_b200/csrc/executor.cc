@@ -84,12 +84,16 @@ void prepare_jit(Plan& p) {
   std::vector<Launch*> targets;
   for (Launch& l : p.launches) {
     std::string s;
-    if (!jit_describe(l, &s, &l.jit_grid, &l.jit_block, &l.jit_cluster, &l.jit_args)) continue;
+    if (!jit_describe(l, &s, &l.jit_grid, &l.jit_block, &l.jit_cluster, &l.jit_args, &l.jit_smem)) continue;
     src.push_back(std::move(s));
     targets.push_back(&l);
   }
   std::vector<void*> fns = jit_compile(src);
-  for (size_t i = 0; i < targets.size(); ++i) targets[i]->jit_fn = fns[i];
+  p.n_jit_missing = 0;
+  for (size_t i = 0; i < targets.size(); ++i) {
+    targets[i]->jit_fn = fns[i];
+    if (!fns[i]) ++p.n_jit_missing;
+  }
 }
 
 namespace {
@@ -116,10 +120,15 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     return;
   }
   if (l.jit_fn) {
-    jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, argtab, l.jit_args, s);
+    jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, l.jit_smem, argtab, l.jit_args, s);
     return;
   }
-  if (l.kind == K_MULTI) {  // not compiled: the parts one after another (they are independent)
+  if (l.kind == K_GEMV_FUSED) {  // not compiled: the producer in full, then the GEMV reading its x
+    run_launch(l.parts[0], argtab, s);
+    launch_gemv(*(const GemvParams*)b, argtab, s);
+    return;
+  }
+  if (l.kind == K_MULTI || l.kind == K_FUSED_DUS) {  // not compiled: the parts one after another
     for (const Launch& part : l.parts) run_launch(part, argtab, s);
     return;
   }
@@ -145,7 +154,7 @@ void setup_variant(ExecVariant& v, void* arena) {
   v.h_argtab[p.const_slot()] = (uint64_t)(uintptr_t)v.consts;
   for (size_t b = 0; b < p.tmp_offsets.size(); ++b)
     v.h_argtab[p.tmp_slot0() + b] = (uint64_t)(uintptr_t)arena + (uint64_t)p.tmp_offsets[b];
-  if (!p.tmaps.empty()) {
+  if (p.has_table()) {
     CUDA_OK(cudaMalloc(&v.d_tmaps, (size_t)p.tmap_table_bytes()));
     CUDA_OK(cudaMemset(v.d_tmaps, 0, (size_t)p.tmap_table_bytes()));
     CUDA_OK(cudaMallocHost(&v.status_host, sizeof(unsigned)));
@@ -174,10 +183,11 @@ namespace {
 // and uploads the table (stream-ordered before the run's kernels).
 void refresh_tmaps(ExecVariant& v, cudaStream_t s) {
   const Plan& p = *v.plan;
-  if (p.tmaps.empty()) return;
+  if (!p.has_table()) return;
   if (*v.status_host)
-    fail(E_INTERNAL, "a tensor-core GEMM wait timed out in an earlier execution (status " +
-                         std::to_string(*v.status_host) + ")");
+    fail(E_INTERNAL, "a bounded wait in a kernel (tensor-core GEMM or bulk-copy GEMV) timed out in an earlier "
+                     "execution (status " + std::to_string(*v.status_host) + ")");
+  if (p.tmaps.empty()) return;
   bool changed = false;
   for (size_t i = 0; i < p.tmaps.size(); ++i) {
     const TmapSpec& t = p.tmaps[i];

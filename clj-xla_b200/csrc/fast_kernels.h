@@ -27,7 +27,11 @@ struct GemvParams {
   // between the two GEMVs run (byte counts are multiples of 16)
   DPtr pf[GEMV_MAXSEG];
   int64_t pf_bytes[GEMV_MAXSEG];
-  int32_t npf, pad_;
+  int32_t npf;
+  int32_t pro_out;  // K_GEMV_FUSED: the producer output that is x
+  // the plan's status word (bounded waits of the bulk-copy GEMV report timeouts there)
+  DPtr status;
+  int32_t has_status, pad_s;
 };
 
 // Points every GEMV launch's prefetch at the weights of the next GEMV launch.
@@ -81,15 +85,24 @@ struct AttnParams {
   // zero between launches; the last split CTA to arrive merges the partials
   // itself and resets its counter (use_counters 0: a separate combine launch)
   DPtr counters;
-  int32_t use_counters, pad_c;
+  int32_t use_counters;
+  int32_t use_tc;  // decode on the tensor cores (attn_tc_kernel): 64-position splits
   int32_t B, nq, nkv, Sq, T, hd, group, splits, qtile;
   int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
   int32_t nchain, chain_out;
   float mask_skip;
   EwInstr chain[12];
+  // the chain in closed form where it is one (kernels skip the interpreter):
+  // 0 general, 1 a multiply by chain_c rounded to chain_dt, 2 identity
+  int32_t chain_kind;
+  float chain_c;
+  int32_t chain_dt, pad_k;
 };
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
+// whether the tensor-core decode kernel can run these views (bf16 q / K / V,
+// 16-byte aligned rows, head_dim 64 / 128 / 256, one query tile of <= 8 vectors)
+bool attention_tc_ok(const AttnParams& p);
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
 void verify_attention(const Launch& l, const RegionFn& region);
 

@@ -6,6 +6,7 @@
 // the same index decomposition and the same reduction order, with the
 // program, shapes, strides and types fixed at compile time.
 #include "jit.h"
+#include "fast_kernels.h"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -265,19 +266,91 @@ struct Emitter {
 
 }  // namespace
 
+// Options of an emitted program body: the CTA size its loops stride by, and
+// (smem_out >= 0) an output that is also written to shared memory at xsb,
+// with the global stores only where gst holds (a GEMV prologue, in which every
+// CTA runs the whole program and one CTA stores its results).
+// A KV-window write folded into the program producing its update: output
+// `out` (element e of the dense update) also goes to the in-place cache at the
+// clamped start indices, after the window's old value is saved to the undo
+// record (same thread, so old-before-new holds per element).
+struct DusStore {
+  int out = -1;
+  DusParams d{};
+  int b_cache = -1, b_undo = -1;
+  int b_start[CLJXLA_MAXR] = {};
+};
+
+struct BodyOpts {
+  int block = 256;
+  int smem_out = -1;
+  std::string sync = "__syncthreads()";  // barrier over the threads running the body
+  std::vector<DusStore> dus;
+};
+
+// clamped start indices of each folded KV write (and, CTA 0, its undo header)
+void emit_dus_prelude(std::ostringstream& s, const BodyOpts& bo, const std::string& ind) {
+  for (size_t k = 0; k < bo.dus.size(); ++k) {
+    const DusStore& u = bo.dus[k];
+    for (int d = 0; d < u.d.rank; ++d) {
+      const std::string v = "dst" + std::to_string(k) + "_" + std::to_string(d);
+      const int64_t hi = u.d.out_shape[d] - u.d.upd_shape[d];
+      if (u.d.start_is_ptr[d])
+        s << ind << "i64 " << v << " = (i64)(int)" << load_expr(base_expr(u.b_start[d]), "0", u.d.start_dt[d]) << ";\n";
+      else
+        s << ind << "i64 " << v << " = " << u.d.start_imm[d] << "LL;\n";
+      s << ind << v << " = " << v << " < 0 ? 0 : (" << v << " > " << hi << "LL ? " << hi << "LL : " << v << ");\n";
+    }
+    if (u.b_undo >= 0) {
+      s << ind << "if (bid == 0u && threadIdx.x == 0) {\n";
+      for (int d = 0; d < CLJXLA_MAXR; ++d)
+        s << ind << "  ((long long*)" << base_expr(u.b_undo) << ")[" << d << "] = "
+          << (d < u.d.rank ? "dst" + std::to_string(k) + "_" + std::to_string(d) : std::string("0")) << ";\n";
+      s << ind << "}\n";
+    }
+  }
+}
+
+// the folded KV writes of output o for update element e holding value v
+void emit_dus_stores(std::ostringstream& s, const BodyOpts& bo, int o, const std::string& e, const std::string& v,
+                     const std::string& ind) {
+  for (size_t k = 0; k < bo.dus.size(); ++k) {
+    const DusStore& u = bo.dus[k];
+    if (u.out != o) continue;
+    s << ind << "{\n" << ind << "  i64 rem = " << e << ", off = 0;\n";
+    int64_t ostride = 1;
+    for (int d = u.d.rank - 1; d >= 0; --d) {
+      s << ind << "  { const i64 i = rem % " << u.d.upd_shape[d] << "LL; rem /= " << u.d.upd_shape[d] << "LL; off += (dst" << k
+        << "_" << d << " + i) * " << ostride << "LL; }\n";
+      ostride *= u.d.out_shape[d];
+    }
+    const std::string cache = base_expr(u.b_cache);
+    if (u.b_undo >= 0)
+      s << ind << "  " << store_stmt("(" + base_expr(u.b_undo) + " + " + std::to_string(8 * CLJXLA_MAXR) + ")", e, u.d.dt,
+                                     load_expr(cache, "off", u.d.dt))
+        << "\n";
+    // the update's own rounding first (the value the DUS would have read), then the cache type's
+    const std::string vu = u.d.update.dt == u.d.dt ? v : fbits("F(" + v + ")", u.d.update.dt);
+    s << ind << "  " << store_stmt(cache, "off", u.d.dt, vu) << "\n" << ind << "}\n";
+  }
+}
+
 // ------------------------------------------------------------------ elementwise
 // The program of one elementwise launch as a device function over blocks
 // [0, nblk) (bid = this CTA's block in that range).
-void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& fname) {
+void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& fname, const BodyOpts& bo) {
   s << "__device__ __forceinline__ void " << fname
-    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk) {\n";
+    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk"
+    << (bo.smem_out >= 0 ? ", char* __restrict__ xsb, bool gst" : "") << ") {\n";
   Emitter em{s, P.in, P.rank};
   for (int i = 0; i < P.nin; ++i) {
     em.in_base.push_back("in" + std::to_string(i));
     s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
-  s << "  for (i64 e = (i64)bid * 256 + threadIdx.x; e < " << P.n << "LL; e += (i64)nblk * 256) {\n";
+  emit_dus_prelude(s, bo, "  ");
+  s << "  for (i64 e = (i64)bid * " << bo.block << " + threadIdx.x; e < " << P.n << "LL; e += (i64)nblk * "
+    << bo.block << ") {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   if (P.rank == 1) {
     s << "    const i64 x0 = e;\n";
@@ -289,15 +362,20 @@ void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& f
   }
   std::vector<std::string> reg(EW_NREG);
   for (int pc = 0; pc < P.ncode; ++pc) em.step(P.code[pc], reg, "    ");
-  for (int o = 0; o < P.nout; ++o)
-    s << "    " << store_stmt("out" + std::to_string(o), "e", P.out[o].dt, em.reg_or_zero(reg, P.out[o].reg)) << "\n";
+  for (int o = 0; o < P.nout; ++o) {
+    const std::string v = em.reg_or_zero(reg, P.out[o].reg);
+    s << "    " << (bo.smem_out >= 0 ? "if (gst) " : "") << store_stmt("out" + std::to_string(o), "e", P.out[o].dt, v)
+      << "\n";
+    if (o == bo.smem_out) s << "    " << store_stmt("xsb", "e", P.out[o].dt, v) << "\n";
+    emit_dus_stores(s, bo, o, "e", v, "    ");
+  }
   s << "  }\n}\n";
 }
 
 std::string jit_source_ew(const EwParams& P) {
   std::ostringstream s;
   s << kPrelude << args_struct();
-  emit_ew_body(s, P, "ew_body");
+  emit_ew_body(s, P, "ew_body", BodyOpts{});
   s << "extern \"C\" __global__ void __launch_bounds__(256) cljxla_fused_ew(const u64* __restrict__ argtab, "
        "const JitArgs a) {\n  pdl_enter();\n  ew_body(argtab, a, blockIdx.x, gridDim.x);\n}\n";
   return s.str();
@@ -318,9 +396,11 @@ void row_launch_shape(const RowParams& p, int* block, int* cluster, int64_t* gri
   *cluster = cl;
 }
 
-void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL, const std::string& fname) {
+void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL, const std::string& fname,
+                   const BodyOpts& bo) {
   s << "__device__ __forceinline__ void " << fname
-    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk) {\n";
+    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk"
+    << (bo.smem_out >= 0 ? ", char* __restrict__ xsb, bool gst" : "") << ") {\n";
   s << "  __shared__ float red_f[" << BLOCK / 32 << "];\n  __shared__ float bcast;\n  __shared__ float cl_part["
     << RP_MAXPH << "];\n";
   s << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n";
@@ -335,6 +415,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
   s << "  (void)lane; (void)warp; (void)c1;\n";
+  emit_dus_prelude(s, bo, "  ");
   s << "  for (i64 row = bid / " << CL << "; row < " << P.rows << "LL; row += nblk / " << CL << ") {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   s << "    i64 rem = row;\n";
@@ -359,17 +440,20 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
       s << "        acc = " << (sum ? "acc + " + xv : "fmaxf(acc, " + xv + ")") << ";\n";
     }
     for (int o = 0; o < P.nout; ++o)
-      if (!P.out[o].scalar && P.out[o].phase == ph)
-        s << "        "
-          << store_stmt("out" + std::to_string(o), "row * " + std::to_string(P.C) + "LL + " + xc, P.out[o].dt,
-                        em.reg_or_zero(reg, P.out[o].reg))
-          << "\n";
+      if (!P.out[o].scalar && P.out[o].phase == ph) {
+        const std::string off = "row * " + std::to_string(P.C) + "LL + " + xc;
+        const std::string v = em.reg_or_zero(reg, P.out[o].reg);
+        s << "        " << (bo.smem_out >= 0 ? "if (gst) " : "")
+          << store_stmt("out" + std::to_string(o), off, P.out[o].dt, v) << "\n";
+        if (o == bo.smem_out) s << "        " << store_stmt("xsb", off, P.out[o].dt, v) << "\n";
+        emit_dus_stores(s, bo, o, off, v, "        ");
+      }
     s << "      }\n";
     if (Ph.red_reg >= 0) {
       const std::string comb = sum ? "t = t + o;" : "t = fmaxf(t, o);";
       s << "      for (int sh = 16; sh > 0; sh >>= 1) { float o = __shfl_xor_sync(0xffffffffu, acc, sh); "
         << (sum ? "acc = acc + o;" : "acc = fmaxf(acc, o);") << " }\n";
-      s << "      if (lane == 0) red_f[warp] = acc;\n      __syncthreads();\n";
+      s << "      if (lane == 0) red_f[warp] = acc;\n      " << bo.sync << ";\n";
       s << "      float t = " << (sum ? "0.0f" : "-__int_as_float(0x7f800000)") << ";\n";
       s << "      if (threadIdx.x == 0) for (int w = 0; w < " << BLOCK / 32 << "; ++w) { float o = red_f[w]; " << comb
         << " }\n";
@@ -380,7 +464,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
       }
       s << "      if (threadIdx.x == 0) { float o = __uint_as_float(" << hex32(*(const uint32_t*)&Ph.red_init) << "); "
         << comb << " bcast = " << round_expr("t", Ph.red_dt) << "; }\n";
-      s << "      __syncthreads();\n      s" << (int)Ph.red_dst << " = U(bcast);\n      __syncthreads();\n";
+      s << "      " << bo.sync << ";\n      s" << (int)Ph.red_dst << " = U(bcast);\n      " << bo.sync << ";\n";
     }
     // per-row scalar program after this phase (its immediates use fresh names)
     std::vector<std::string> sc = sreg;
@@ -397,7 +481,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
     }
     s << "    }\n";
   }
-  s << "    if (threadIdx.x == 0 && crank == 0u) {\n";
+  s << "    if (threadIdx.x == 0 && crank == 0u" << (bo.smem_out >= 0 ? " && gst" : "") << ") {\n";
   for (int o = 0; o < P.nout; ++o)
     if (P.out[o].scalar)
       s << "      " << store_stmt("out" + std::to_string(o), "row", P.out[o].dt, sreg[P.out[o].reg]) << "\n";
@@ -409,7 +493,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
 std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
   std::ostringstream s;
   s << kPrelude << args_struct();
-  emit_row_body(s, P, BLOCK, CL, "row_body");
+  emit_row_body(s, P, BLOCK, CL, "row_body", BodyOpts{});
   s << "extern \"C\" __global__ void __launch_bounds__(" << BLOCK
     << ") cljxla_fused_row(const u64* __restrict__ argtab, const JitArgs a) {\n  pdl_enter();\n"
        "  row_body(argtab, a, blockIdx.x, gridDim.x);\n}\n";
@@ -419,6 +503,33 @@ std::string jit_source_row(const RowParams& P, int BLOCK, int CL) {
 namespace {
 
 // shape and buffers of one elementwise / row launch; false for other kinds
+int program_buffers(const Launch& l) {
+  if (l.kind == K_EW) return ((const EwParams*)l.blob.data())->nin + ((const EwParams*)l.blob.data())->nout;
+  if (l.kind == K_ROWNORM) return ((const RowParams*)l.blob.data())->nin + ((const RowParams*)l.blob.data())->nout;
+  return -1;
+}
+
+// the folded KV writes of a K_FUSED_DUS launch, with their buffers numbered
+// after the producer's; empty when they do not fit the argument block
+std::vector<DusStore> dus_stores_of(const Launch& l) {
+  std::vector<DusStore> out;
+  int k = program_buffers(l.parts[0]);
+  const int32_t* outs = (const int32_t*)l.blob.data();
+  if (k < 0 || l.blob.size() != 4 * (l.parts.size() - 1)) return {};
+  for (size_t i = 1; i < l.parts.size(); ++i) {
+    DusStore u;
+    u.out = outs[i - 1];
+    memcpy(&u.d, l.parts[i].blob.data(), sizeof(DusParams));
+    u.b_cache = k++;
+    if (u.d.has_undo) u.b_undo = k++;
+    for (int d = 0; d < u.d.rank; ++d)
+      if (u.d.start_is_ptr[d]) u.b_start[d] = k++;
+    out.push_back(u);
+  }
+  if (k > JIT_MAXBUF) return {};
+  return out;
+}
+
 bool describe_one(const Launch& l, int64_t* grid, int* block, int* cluster, JitArgs* args) {
   *args = JitArgs{};
   auto put = [&](int k, const DPtr& p) {
@@ -444,19 +555,298 @@ bool describe_one(const Launch& l, int64_t* grid, int* block, int* cluster, JitA
     for (int o = 0; o < r.nout; ++o) put(r.nin + o, r.out[o].p);
     return true;
   }
+  if (l.kind == K_FUSED_DUS) {
+    if (l.parts.size() < 2 || !describe_one(l.parts[0], grid, block, cluster, args)) return false;
+    const std::vector<DusStore> ds = dus_stores_of(l);
+    if (ds.empty()) return false;
+    for (const DusStore& u : ds) {
+      put(u.b_cache, u.d.out);
+      if (u.b_undo >= 0) put(u.b_undo, u.d.undo);
+      for (int d = 0; d < u.d.rank; ++d)
+        if (u.d.start_is_ptr[d]) put(u.b_start[d], u.d.start_ptr[d]);
+    }
+    return true;
+  }
   return false;
 }
 
-void emit_body(std::ostringstream& s, const Launch& l, int block, int cluster, const std::string& fname) {
-  if (l.kind == K_EW) emit_ew_body(s, *(const EwParams*)l.blob.data(), fname);
-  else emit_row_body(s, *(const RowParams*)l.blob.data(), block, cluster, fname);
+void emit_body(std::ostringstream& s, const Launch& l, int block, int cluster, const std::string& fname,
+               const BodyOpts& bo = BodyOpts{});
+
+int sm_count() {
+  static const int n = [] {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        v <= 0) {
+      cudaGetLastError();
+      return 148;
+    }
+    return v;
+  }();
+  return n;
+}
+
+// Decode GEMV fed by bulk copies (K_GEMV, and K_GEMV_FUSED with its producer
+// as a prologue).  One CTA per SM owns a contiguous range of weight rows (the
+// segments' rows laid end to end).  A producer warp streams the range through
+// a ring of shared-memory stages with cp.async.bulk (each stage: RPS whole
+// rows, completion counted on an mbarrier), starting before the dependency
+// wait, since weights are never written by a plan kernel; 8 consumer warps
+// compute one row part each per stage (WPR warps per row) from shared memory
+// and release the stage.  x lives in shared memory, in x's element type: read
+// from memory, or computed by the producer's program in every CTA (CTA 0 also
+// stores the producer's outputs).  Every mbarrier wait is bounded; a timeout
+// sets the plan's status word and the CTA stops, after the producer has
+// waited (bounded) for its copies in flight.
+struct GemvGeometry {
+  int wpr, rps, nstage, stage_bytes, x_bytes;
+};
+
+bool gemv_tma_geometry(const GemvParams& G, GemvGeometry* g) {
+  constexpr int WARPS = 8;
+  if (G.M < 1 || G.M > 8 || G.K % 8 != 0) return false;
+  int wpr = 1;
+  while (wpr < WARPS && (G.K / wpr > 2560 || (G.K / wpr) % 8 != 0)) wpr *= 2;
+  if (G.K % wpr != 0 || (G.K / wpr) % 8 != 0 || G.K / wpr > 4096) return false;
+  g->wpr = wpr;
+  g->rps = WARPS / wpr;
+  g->stage_bytes = (int)(g->rps * G.K * 2);
+  g->x_bytes = (int)(G.M * G.K * (G.x_dt == KDT_F32 ? 4 : 2));
+  if (g->x_bytes > 64 * 1024) return false;
+  const int budget = 200 * 1024 - g->x_bytes;
+  g->nstage = std::min(4, budget / g->stage_bytes);
+  return g->nstage >= 2;
+}
+
+bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
+  const bool fused = l.kind == K_GEMV_FUSED;
+  if (!(l.kind == K_GEMV || (fused && l.parts.size() == 1))) return false;
+  const GemvParams& G = *(const GemvParams*)l.blob.data();
+  if (!G.has_status) return false;  // no status word: keep the plain kernel
+  static const bool off = [] {
+    const char* e = getenv("CLJXLA_B200_GEMV_TMA");
+    return e && e[0] == '0';
+  }();
+  if (off) return false;
+  GemvGeometry geo;
+  if (!gemv_tma_geometry(G, &geo)) return false;
+  if (G.M > 1 && G.x_sm != G.K) return false;
+  int npb = 0;
+  *args = JitArgs{};
+  if (fused) {
+    const Launch& pro = l.parts[0];
+    if (pro.kind == K_EW) npb = ((const EwParams*)pro.blob.data())->nin + ((const EwParams*)pro.blob.data())->nout;
+    else if (pro.kind == K_ROWNORM) npb = ((const RowParams*)pro.blob.data())->nin + ((const RowParams*)pro.blob.data())->nout;
+    else return false;
+    int64_t g0;
+    int b0, c0;
+    if (!describe_one(pro, &g0, &b0, &c0, args)) return false;
+  }
+  const int kW = npb, kY = npb + G.nseg, kS = npb + 2 * G.nseg, kX = kS + 1;
+  if (kX + 1 > JIT_MAXBUF) return false;
+  auto put = [&](int k, const DPtr& p) {
+    args->s[k] = p.slot;
+    args->o[k] = p.off;
+  };
+  for (int i = 0; i < G.nseg; ++i) {
+    put(kW + i, G.w[i]);
+    put(kY + i, G.y[i]);
+  }
+  put(kS, G.status);
+  put(kX, G.x);
+  constexpr int WARPS = 8;
+  const int64_t M = G.M, K = G.K, N = G.N;
+  const int WPR = geo.wpr, RPS = geo.rps, NST = geo.nstage;
+  const int64_t KP = K / WPR;
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + RPS - 1) / RPS));
+  const int xes = G.x_dt == KDT_F32 ? 4 : 2;
+  const int stage_stride = (geo.stage_bytes + 1023) & ~1023;
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  s << R"G(__device__ __forceinline__ float bf_lo(u32 u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(u32 u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ u32 sa(const void* p) { return (u32)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mb_init(u32 a, u32 n) { asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(n)); }
+__device__ __forceinline__ void mb_expect(u32 a, u32 bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(u32 a) { asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory"); }
+__device__ __forceinline__ bool mb_try(u32 a, u32 parity) {
+  u32 ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+  return ok != 0;
+}
+// bounded wait: false after the iteration limit
+__device__ __forceinline__ bool mb_wait(u32 a, u32 parity) {
+  for (u32 i = 0; i < (1u << 22); ++i)
+    if (mb_try(a, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(u32 dst, const void* src, u32 bytes, u32 bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ uint4 lds16(u32 a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ bool consumers_any(bool p) {  // OR over the consumer warps (named barrier 1)
+  u32 r;
+  asm volatile("{\n\t.reg .pred q, o;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred o, 1, )G" << WARPS * 32 << R"G(, q;\n\tselp.u32 %0, 1, 0, o;\n\t}"
+               : "=r"(r) : "r"((u32)p) : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, )G" << WARPS * 32 << R"G(;" ::: "memory"); }
+__device__ __forceinline__ float dot8(const uint4& w, const float* x) {
+  float s = bf_lo(w.x) * x[0];
+  s = fmaf(bf_hi(w.x), x[1], s); s = fmaf(bf_lo(w.y), x[2], s); s = fmaf(bf_hi(w.y), x[3], s);
+  s = fmaf(bf_lo(w.z), x[4], s); s = fmaf(bf_hi(w.z), x[5], s); s = fmaf(bf_lo(w.w), x[6], s);
+  s = fmaf(bf_hi(w.w), x[7], s);
+  return s;
+}
+)G";
+  if (xes == 2)
+    s << "__device__ __forceinline__ void xs8(u32 a, float* o) {\n  const uint4 v = lds16(a);\n"
+         "  o[0] = bf_lo(v.x); o[1] = bf_hi(v.x); o[2] = bf_lo(v.y); o[3] = bf_hi(v.y);\n"
+         "  o[4] = bf_lo(v.z); o[5] = bf_hi(v.z); o[6] = bf_lo(v.w); o[7] = bf_hi(v.w);\n}\n";
+  else
+    s << "__device__ __forceinline__ void xs8(u32 a, float* o) {\n  const uint4 u = lds16(a), v = lds16(a + 16);\n"
+         "  o[0] = __uint_as_float(u.x); o[1] = __uint_as_float(u.y); o[2] = __uint_as_float(u.z); o[3] = __uint_as_float(u.w);\n"
+         "  o[4] = __uint_as_float(v.x); o[5] = __uint_as_float(v.y); o[6] = __uint_as_float(v.z); o[7] = __uint_as_float(v.w);\n}\n";
+  if (fused) {
+    BodyOpts bo;
+    bo.block = WARPS * 32;
+    bo.smem_out = G.pro_out;
+    bo.sync = "consumers_sync()";  // the producer warp does not take part
+    emit_body(s, l.parts[0], WARPS * 32, 1, "pro_body", bo);
+  }
+  // segment of a row: index, first row, weights
+  auto seg_chain = [&](const std::string& row, const std::string& ind) {
+    std::ostringstream c;
+    c << ind << "int sg = 0; i64 lo = 0;\n";
+    for (int i = 0; i + 1 < G.nseg; ++i)
+      c << ind << "if (" << row << " >= " << G.seg_end[i] << "LL) { sg = " << i + 1 << "; lo = " << G.seg_end[i] << "LL; }\n";
+    return c.str();
+  };
+  // end of the stage starting at row r: RPS rows, clipped to the CTA's range and the segment
+  s << "__device__ __forceinline__ i64 stage_end(i64 r, i64 r1) {\n  i64 e = r + " << RPS << "LL;\n  if (e > r1) e = r1;\n";
+  for (int i = 0; i + 1 < G.nseg; ++i)
+    s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
+  s << "  return e;\n}\n";
+  s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
+    << ", 1) cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
+  s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
+  s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
+  s << "  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;\n";
+  s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  s << "  unsigned* status = (unsigned*)" << base_expr(kS) << ";\n";
+  s << "  const u32 stage0 = sa(dsm), xsa = stage0 + " << (int64_t)NST * stage_stride << "u;\n";
+  s << "  if (threadIdx.x == 0) {\n    for (int i = 0; i < " << NST << "; ++i) { mb_init(sa(&full_bar[i]), 1u); mb_init(sa(&empty_bar[i]), "
+    << WARPS << "u); }\n";
+  s << "    asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n  }\n  __syncthreads();\n";
+  // producer
+  s << "  if (warp == " << WARPS << ") {\n    if (lane != 0) return;\n";
+  s << "    int st = 0;\n    bool ok = true;\n";
+  s << "    for (i64 r = r0; r < r1; ++st) {\n      const int slot = st % " << NST << ";\n";
+  s << "      if (st >= " << NST << " && !mb_wait(sa(&empty_bar[slot]), (u32)((st / " << NST << " - 1) & 1))) { ok = false; break; }\n";
+  s << "      const i64 e = stage_end(r, r1);\n";
+  s << seg_chain("r", "      ");
+  s << "      const unsigned char* W = (const unsigned char*)";
+  for (int i = 0; i + 1 < G.nseg; ++i) s << "(sg == " << i << " ? " << base_expr(kW + i) << " : ";
+  s << base_expr(kW + G.nseg - 1);
+  for (int i = 0; i + 1 < G.nseg; ++i) s << ")";
+  s << ";\n";
+  s << "      const u32 bytes = (u32)((e - r) * " << K * 2 << "LL);\n";
+  s << "      mb_expect(sa(&full_bar[slot]), bytes);\n";
+  s << "      bulk_g2s(stage0 + (u32)slot * " << stage_stride << "u, W + (r - lo) * " << K * 2 << "LL, bytes, sa(&full_bar[slot]));\n";
+  s << "      r = e;\n    }\n";
+  s << "    if (!ok) atomicOr(status, 4u);\n";
+  // drain: the copies of the last stages issued have landed before the CTA may end
+  s << "    for (int k = st - 1; k >= 0 && k >= st - " << NST << "; --k)\n";
+  s << "      if (!mb_wait(sa(&full_bar[k % " << NST << "]), (u32)((k / " << NST << ") & 1))) atomicOr(status, 8u);\n";
+  s << "    return;\n  }\n";
+  // consumers: x
+  s << "  pdl_enter();\n";
+  if (fused) {
+    s << "  pro_body(argtab, a, 0u, 1u, (char*)(dsm + " << (int64_t)NST * stage_stride << "), blockIdx.x == 0);\n";
+  } else {
+    s << "  {\n    const char* X = " << base_expr(kX) << ";\n";
+    if (M == 1 || G.x_sm == K)
+      s << "    for (int i = threadIdx.x; i < " << M * K * xes / 16 << "; i += " << WARPS * 32
+        << ") *(uint4*)(dsm + " << (int64_t)NST * stage_stride << " + 16 * i) = *(const uint4*)(X + 16 * i);\n";
+    s << "  }\n";
+  }
+  s << "  consumers_sync();\n";
+  s << "  const int rr = warp / " << WPR << ", part = warp % " << WPR << ";\n";
+  s << "  int st = 0;\n";
+  s << "  for (i64 r = r0; r < r1; ++st) {\n    const int slot = st % " << NST << ";\n";
+  s << "    const i64 e = stage_end(r, r1);\n";
+  s << "    bool bad = !mb_wait(sa(&full_bar[slot]), (u32)((st / " << NST << ") & 1));\n";
+  if (WPR > 1) s << "    bad = consumers_any(bad);\n";
+  s << "    if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); break; }\n";
+  s << "    const i64 row = r + rr;\n    const bool active = row < e;\n";
+  s << "    float acc[" << M << "];\n#pragma unroll\n    for (int m = 0; m < " << M << "; ++m) acc[m] = 0.f;\n";
+  s << "    if (active) {\n";
+  s << "      const u32 wa = stage0 + (u32)slot * " << stage_stride << "u + (u32)((rr * " << K << "LL + part * " << KP
+    << "LL) * 2);\n";
+  s << "      const u32 xa = xsa + (u32)(part * " << KP * xes << "LL);\n";
+  s << "#pragma unroll 4\n      for (int v = lane; v < " << KP / 8 << "; v += 32) {\n";
+  s << "        const uint4 w = lds16(wa + 16u * v);\n";
+  s << "#pragma unroll\n        for (int m = 0; m < " << M << "; ++m) {\n          float xv[8];\n";
+  s << "          xs8(xa + (u32)(m * " << K * xes << "LL) + " << 8 * xes << "u * v, xv);\n";
+  s << "          acc[m] += dot8(w, xv);\n        }\n      }\n    }\n";
+  s << "    __syncwarp();\n    if (lane == 0) mb_arrive(sa(&empty_bar[slot]));  // this warp is done with the stage\n";
+  s << "#pragma unroll\n    for (int m = 0; m < " << M << "; ++m)\n";
+  s << "      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);\n";
+  if (WPR > 1) {
+    s << "    if (lane == 0) for (int m = 0; m < " << M << "; ++m) red[slot][warp][m] = acc[m];\n";
+    s << "    consumers_sync();\n";
+    s << "    if (part == 0 && lane == 0 && active)\n      for (int q = 1; q < " << WPR << "; ++q)\n"
+         "        for (int m = 0; m < " << M << "; ++m) acc[m] += red[slot][warp + q][m];\n";
+  }
+  s << "    if (active && part == 0 && lane == 0) {\n";
+  s << seg_chain("row", "      ");
+  for (int i = 0; i < G.nseg; ++i) {
+    const int64_t rows = G.seg_end[i] - (i ? G.seg_end[i - 1] : 0);
+    s << "      if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; for (int m = 0; m < " << M << "; ++m) "
+      << store_stmt("Y", "(i64)m * " + std::to_string(rows) + "LL + (row - lo)", G.y_dt[i], "U(acc[m])") << " }\n";
+  }
+  s << "    }\n    r = e;\n  }\n}\n";
+  *src = s.str();
+  *grid = ctas;
+  *block = (WARPS + 1) * 32;
+  *smem = NST * stage_stride + geo.x_bytes;
+  return true;
+}
+
+void emit_body(std::ostringstream& s, const Launch& l, int block, int cluster, const std::string& fname,
+               const BodyOpts& bo) {
+  if (l.kind == K_FUSED_DUS) {
+    BodyOpts b2 = bo;
+    b2.dus = dus_stores_of(l);
+    emit_body(s, l.parts[0], block, cluster, fname, b2);
+    return;
+  }
+  if (l.kind == K_EW) emit_ew_body(s, *(const EwParams*)l.blob.data(), fname, bo);
+  else emit_row_body(s, *(const RowParams*)l.blob.data(), block, cluster, fname, bo);
 }
 
 }  // namespace
 
 bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster,
-                  std::vector<JitArgs>* args) {
+                  std::vector<JitArgs>* args, int* smem) {
   args->clear();
+  *smem = 0;
+  if (l.kind == K_GEMV_FUSED || l.kind == K_GEMV) {
+    JitArgs a;
+    *cluster = 1;
+    if (!describe_gemv_tma(l, src, grid, block, smem, &a)) return false;
+    args->push_back(a);
+    return true;
+  }
   if (l.kind == K_MULTI) {
     // one kernel, CTA ranges running the parts' programs in order
     std::vector<int64_t> grids;
@@ -465,7 +855,8 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
       int b, c;
       JitArgs a;
       if (!describe_one(p, &g, &b, &c, &a)) return false;
-      if (!args->empty() && (c != *cluster || p.kind != l.parts[0].kind)) return false;
+      auto base = [](const Launch& x) { return x.kind == K_FUSED_DUS ? x.parts[0].kind : x.kind; };
+      if (!args->empty() && (c != *cluster || base(p) != base(l.parts[0]))) return false;
       *block = args->empty() ? b : std::max(*block, b);  // row programs run at the largest block
       *cluster = c;
       grids.push_back(g);
@@ -493,7 +884,16 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
   if (!describe_one(l, grid, block, cluster, &a)) return false;
   args->push_back(a);
   if (l.kind == K_EW) *src = jit_source_ew(*(const EwParams*)l.blob.data());
-  else *src = jit_source_row(*(const RowParams*)l.blob.data(), *block, *cluster);
+  else if (l.kind == K_ROWNORM) *src = jit_source_row(*(const RowParams*)l.blob.data(), *block, *cluster);
+  else {
+    std::ostringstream s;
+    s << kPrelude << args_struct();
+    emit_body(s, l, *block, *cluster, "body");
+    const bool ew = l.parts[0].kind == K_EW;
+    s << "extern \"C\" __global__ void __launch_bounds__(" << *block << ") " << (ew ? "cljxla_fused_ew" : "cljxla_fused_row")
+      << "(const u64* __restrict__ argtab, const JitArgs a) {\n  pdl_enter();\n  body(argtab, a, blockIdx.x, gridDim.x);\n}\n";
+    *src = s.str();
+  }
   return true;
 }
 
@@ -504,7 +904,8 @@ std::vector<std::string> jit_plan_sources(const Plan& p) {
     int64_t g;
     int b = 0, c = 1;
     std::vector<JitArgs> a;
-    if (jit_describe(l, &s, &g, &b, &c, &a)) out.push_back(std::move(s));
+    int sm;
+    if (jit_describe(l, &s, &g, &b, &c, &a, &sm)) out.push_back(std::move(s));
   }
   return out;
 }
@@ -583,10 +984,16 @@ void* compile_one(const std::string& src) {
     return nullptr;
   }
   cudaKernel_t k = nullptr;
-  const char* entry = src.find("cljxla_fused_multi(") != std::string::npos ? "cljxla_fused_multi"
-                      : src.find("cljxla_fused_row(") != std::string::npos ? "cljxla_fused_row"
-                                                                            : "cljxla_fused_ew";
-  if (cudaLibraryGetKernel(&k, lib, entry) != cudaSuccess) {
+  // the entry point: the identifier before the parameter list of the extern "C" kernel
+  std::string entry;
+  const size_t at = src.rfind("extern \"C\" __global__");
+  const size_t paren = at == std::string::npos ? std::string::npos : src.find('(', src.find("cljxla_fused", at));
+  if (paren != std::string::npos) {
+    size_t b = paren;
+    while (b > 0 && (isalnum((unsigned char)src[b - 1]) || src[b - 1] == '_')) --b;
+    entry = src.substr(b, paren - b);
+  }
+  if (entry.empty() || cudaLibraryGetKernel(&k, lib, entry.c_str()) != cudaSuccess) {
     cudaGetLastError();
     return nullptr;
   }
@@ -599,6 +1006,16 @@ int jit_check_sources(const std::vector<std::string>& sources, std::string* firs
   if (!nvrtc().ok) return -1;
   std::map<std::string, int> uniq;
   for (const std::string& s : sources) uniq[s] = 1;
+  if (const char* dir = getenv("CLJXLA_B200_DUMP_JIT")) {  // debugging aid: the distinct sources as files
+    int k = 0;
+    for (auto& kv : uniq) {
+      std::string path = std::string(dir) + "/jit_" + std::to_string(k++) + ".cu";
+      if (FILE* f = fopen(path.c_str(), "w")) {
+        fwrite(kv.first.data(), 1, kv.first.size(), f);
+        fclose(f);
+      }
+    }
+  }
   int failed = 0;
   for (auto& kv : uniq) {
     std::string log;
@@ -653,11 +1070,23 @@ std::vector<void*> jit_compile(const std::vector<std::string>& sources) {
   return out;
 }
 
-void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab,
+void jit_launch(void* kernel, int64_t grid, int block, int cluster, int smem, const uint64_t* argtab,
                 const std::vector<JitArgs>& jargs, cudaStream_t s) {
+  if (smem > 0) {
+    // opt in to the dynamic shared memory once per kernel (static + dynamic may pass 48 KB)
+    static std::mutex mu;
+    static std::map<void*, int> set;
+    std::lock_guard<std::mutex> lk(mu);
+    int& have = set[kernel];
+    if (have < smem) {
+      CUDA_OK(cudaFuncSetAttribute((const void*)kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      have = smem;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3((unsigned)block, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;

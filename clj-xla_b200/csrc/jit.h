@@ -35,7 +35,7 @@ void row_launch_shape(const RowParams& p, int* block, int* cluster, int64_t* gri
 // Source and launch geometry of the compiled replacement of an elementwise /
 // row launch; false for launches that have none.
 bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, int* cluster,
-                  std::vector<JitArgs>* args);
+                  std::vector<JitArgs>* args, int* smem);
 
 // Compiles the sources (in parallel, cached by text) and returns one kernel
 // handle per source (nullptr where compilation failed or NVRTC is missing).
@@ -52,8 +52,8 @@ int jit_check_sources(const std::vector<std::string>& sources, std::string* firs
 std::vector<std::string> jit_plan_sources(const Plan& p);
 
 // Launches a compiled kernel: grid x block threads, thread-block clusters of
-// `cluster` CTAs along x when cluster > 1.
-void jit_launch(void* kernel, int64_t grid, int block, int cluster, const uint64_t* argtab,
+// `cluster` CTAs along x when cluster > 1, `smem` bytes of dynamic shared memory.
+void jit_launch(void* kernel, int64_t grid, int block, int cluster, int smem, const uint64_t* argtab,
                 const std::vector<JitArgs>& args, cudaStream_t s);
 
 }  // namespace cljxla

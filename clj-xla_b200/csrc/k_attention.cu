@@ -91,7 +91,7 @@ __device__ __forceinline__ void load_row<float, 8>(const float* p, float* o) {
 }
 
 // the printed scale / softcap chain applied to one score (register 0 holds it)
-__device__ float run_chain(const AttnParams& P, float s) {
+__device__ __noinline__ float run_chain(const AttnParams& P, float s) {
   float R[16];
   R[0] = s;
   for (int pc = 0; pc < P.nchain; ++pc) {
@@ -113,6 +113,13 @@ __device__ float run_chain(const AttnParams& P, float s) {
     R[I.dst] = rnd_dt(z, I.dt);
   }
   return R[P.chain_out];
+}
+
+// the chain in its closed form where the planner found one
+__device__ __forceinline__ float apply_chain(const AttnParams& P, float s) {
+  if (P.chain_kind == 1) return rnd_dt(s * P.chain_c, P.chain_dt);
+  if (P.chain_kind == 2) return s;
+  return run_chain(P, s);
 }
 
 constexpr int NW = 4;
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
       p[r] = 0.f;
       if (r >= nqv) continue;  // uniform across the warp
       float mv = -INFINITY;
-      if (any) mv = rnd_dt(run_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
+      if (any) mv = rnd_dt(apply_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
       float rm = mv;
 #pragma unroll
       for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
         p[r] = 0.f;
         if (r >= nqv) continue;
         float mv = -INFINITY;
-        if (any) mv = rnd_dt(run_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
+        if (any) mv = rnd_dt(apply_chain(P, rnd_dt(s[r], P.dt_d1)) + mk[r], P.dt_m);
         float rm = mv;
 #pragma unroll
         for (int sh = 16; sh > 0; sh >>= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, sh));
@@ -600,6 +607,283 @@ __global__ void attn_combine_kernel(const __grid_constant__ AttnParams P, const 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention on the tensor cores (mma.sync m16n8k16, bf16 in, f32
+// accumulate).  One CTA per (batch * kv head, position split); its query
+// vectors (the GQA group, at most 8) are the M rows of one 16-row tile.  The
+// CTA walks its positions in chunks of TC_CH: the chunk's mask values go to
+// shared memory, the 16-position steps with any unmasked position are staged
+// (K and V rows, cp.async, double-buffered with the next chunk), and each of
+// the 4 warps computes all scores of a step (S = Q K^T, 16 x 16) and then
+// P V for its quarter of head_dim.  The printed score chain, mask, exp and
+// roundings are replayed on the accumulator elements exactly as in the SIMT
+// kernel.  P (f32) enters the P V product as a bf16 hi + lo pair, so the
+// products keep ~16 significant bits (relative error ~2^-17, well inside the
+// f32 tolerance of the attention output); every warp sees the same scores, so
+// the per-row (max, sum) needs no cross-warp merge.
+constexpr int TC_CH = 64;  // positions per staged chunk
+
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// two f32 as a bf16 pair (round to nearest even): lo in bits 0-15
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ float bf16_lo_f(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ AttnParams P,
+                                                     const uint64_t* __restrict__ argtab) {
+  constexpr int ROW = HD + 8;            // padded smem row (bf16): rows 16 B apart in bank phase
+  constexpr int KSTEPS = HD / 16;        // k-steps of the score product
+  constexpr int NT = HD / 32;            // 8-dim output tiles per warp (a quarter of head_dim)
+  extern __shared__ __align__(16) uint16_t tc_smem[];
+  uint16_t* Kb = tc_smem;                       // [2][TC_CH][ROW]
+  uint16_t* Vb = tc_smem + 2 * TC_CH * ROW;     // [2][TC_CH][ROW]
+  __shared__ float msk[2][8][TC_CH];
+  __shared__ unsigned s_act[2];
+  pdl_enter();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int bk = blockIdx.z;
+  const int b = bk / P.nkv, kh = bk % P.nkv;
+  const int nqv = P.Sq * P.group;  // decode: one query tile holds every query vector of the group
+  const int split = blockIdx.x;
+  const int64_t chunk = (P.T + P.splits - 1) / P.splits;
+  const int64_t t0 = split * chunk, t1 = min((int64_t)P.T, t0 + chunk);
+  const char* qb = dres(P.q.p, argtab);
+  const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
+  const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
+  const char* mb = dres(P.mask.p, argtab);
+  auto qrow = [&](int r, int& qi, int& h) {
+    qi = r / P.group;
+    h = kh * P.group + r % P.group;
+  };
+  // Q as A fragments (rows >= nqv are zero)
+  uint32_t qa[KSTEPS][4];
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = g + 8 * (i & 1), c = 16 * kk + 2 * t + 8 * (i >> 1);
+      uint32_t v = 0;
+      if (r < nqv) {
+        int qi, h;
+        qrow(r, qi, h);
+        const int64_t o = b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2];
+        const float lo = ld_any(qb, o + (int64_t)c * P.q.stride[3], P.q.dt);
+        const float hi = ld_any(qb, o + (int64_t)(c + 1) * P.q.stride[3], P.q.dt);
+        v = pack_bf16(lo, hi);
+      }
+      qa[kk][i] = v;
+    }
+  int64_t mrow[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    int qi, h;
+    qrow(r < nqv ? r : 0, qi, h);
+    mrow[r] = b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2];
+  }
+  // stage chunk c0 into buffer buf: mask values, active steps, K/V rows of active steps
+  auto stage = [&](int64_t c0, int buf) {
+    for (int e = threadIdx.x; e < 8 * TC_CH; e += 128) {
+      const int r = e / TC_CH, j = e % TC_CH;
+      float v = -INFINITY;
+      if (r < nqv && c0 + j < t1) v = ld_any(mb, mrow[r] + (c0 + j) * P.mask.stride[3], P.mask.dt);
+      msk[buf][r][j] = v;
+    }
+    if (threadIdx.x == 0) s_act[buf] = 0u;
+    __syncthreads();
+    if (threadIdx.x < TC_CH) {
+      bool any = false;
+      for (int r = 0; r < nqv; ++r) any |= msk[buf][r][threadIdx.x] > P.mask_skip;
+      if (any) atomicOr(&s_act[buf], 1u << (threadIdx.x / 16));
+    }
+    __syncthreads();
+    const unsigned act = s_act[buf];
+    constexpr int SEGS = HD / 8;  // 16-byte pieces per row
+    for (int q = threadIdx.x; q < TC_CH * SEGS; q += 128) {
+      const int rr = q / SEGS, sg = q % SEGS;
+      if (!((act >> (rr / 16)) & 1u)) continue;
+      uint16_t* kd = Kb + ((size_t)buf * TC_CH + rr) * ROW + sg * 8;
+      uint16_t* vd = Vb + ((size_t)buf * TC_CH + rr) * ROW + sg * 8;
+      if (c0 + rr < t1) {
+        cp_async16(kd, kbase + (c0 + rr) * P.k.stride[2] + sg * 8);
+        cp_async16(vd, vbase + (c0 + rr) * P.v.stride[2] + sg * 8);
+      } else {  // past the split's last position: zeros (never NaN into P V)
+        *(uint4*)kd = make_uint4(0, 0, 0, 0);
+        *(uint4*)vd = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
+  const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
+  int buf = 0;
+  if (t0 < t1) stage(t0, 0);
+  for (int64_t c0 = t0; c0 < t1; c0 += TC_CH, buf ^= 1) {
+    const bool more = c0 + TC_CH < t1;
+    if (more) {
+      stage(c0 + TC_CH, buf ^ 1);  // next chunk in flight while this one is computed
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const unsigned act = s_act[buf];
+#pragma unroll 1
+    for (int st = 0; st < TC_CH / 16; ++st) {
+      if (!((act >> st) & 1u)) continue;
+      const int s0 = st * 16;
+      // scores S[16 rows][16 positions]: two 8-position tiles
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        const int mi = lane >> 3, ri = lane & 7;
+        const uint32_t rowaddr =
+            kb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi >> 1)) * ROW + 8 * (mi & 1)) * 2);
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+          uint32_t bf[4];
+          ldsm_x4(rowaddr + 32u * kk, bf);
+          mma_bf16(sc[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[0], bf[1]);
+          mma_bf16(sc[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[2], bf[3]);
+        }
+      }
+      // chain, mask, online softmax: this thread holds rows g (i = 0, 1) and
+      // g + 8 (i = 2, 3); with at most 8 query vectors only rows g can hold any
+      float pv[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 1
+      for (int hr = 0; hr < 1; ++hr) {
+        const int r = g + 8 * hr;
+        float mv[4];
+        float rmax = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int tile = q >> 1, j = s0 + 8 * tile + 2 * t + (q & 1);
+          const float mk = r < 8 ? msk[buf][r][j] : -INFINITY;
+          const bool valid = r < nqv && mk > P.mask_skip;
+          mv[q] = -INFINITY;
+          if (valid) mv[q] = rnd_dt(apply_chain(P, rnd_dt(sc[tile][2 * hr + (q & 1)], P.dt_d1)) + mk, P.dt_m);
+          rmax = fmaxf(rmax, mv[q]);
+        }
+        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
+        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
+        const float mnew = fmaxf(m[hr], rmax);
+        float ps = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float p = 0.f;
+          if (mnew != -INFINITY && mv[q] != -INFINITY) p = rnd_dt(expf(rnd_dt(mv[q] - mnew, P.dt_sub)), P.dt_exp);
+          pv[q >> 1][2 * hr + (q & 1)] = p;
+          ps += p;
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        if (mnew != -INFINITY) {
+          const float scl = m[hr] == -INFINITY ? 0.f : expf(m[hr] - mnew);
+          l[hr] = l[hr] * scl + ps;
+#pragma unroll
+          for (int n = 0; n < NT; ++n) {
+            o[n][2 * hr] *= scl;
+            o[n][2 * hr + 1] *= scl;
+          }
+          m[hr] = mnew;
+        }
+      }
+      // P as A fragments, hi and lo bf16 parts
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tile = i >> 1, hr = i & 1;
+        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
+        ah[i] = pack_bf16(p0, p1);
+        al[i] = pack_bf16(p0 - bf16_lo_f(ah[i]), p1 - bf16_hi_f(ah[i]));
+      }
+      // O[:, warp quarter] += P V
+      {
+        const int mi = lane >> 3, ri = lane & 7;
+        const uint32_t rowaddr = vb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi & 1)) * ROW +
+                                                    warp * (HD / 4) + 8 * (mi >> 1)) * 2);
+#pragma unroll
+        for (int n = 0; n < NT; n += 2) {
+          uint32_t bf[4];
+          ldsm_x4_t(rowaddr + 32u * (n / 2), bf);
+          mma_bf16(o[n], ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
+          mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
+          mma_bf16(o[n + 1], ah[0], ah[1], ah[2], ah[3], bf[2], bf[3]);
+          mma_bf16(o[n + 1], al[0], al[1], al[2], al[3], bf[2], bf[3]);
+        }
+      }
+    }
+    __syncthreads();  // this buffer is restaged two chunks later
+  }
+  // results: rows g and g + 8 of this warp's quarter of head_dim
+  const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = g + 8 * hr;
+    if (r >= nqv) continue;
+    int qi, h;
+    qrow(r, qi, h);
+    const int64_t row = ((int64_t)b * P.nq + h) * P.Sq + qi;
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int d = warp * (HD / 4) + 8 * n + 2 * t + e;
+        const float A = o[n][2 * hr + e];
+        if (P.splits == 1) {
+          const float v = l[hr] > 0.f ? A / l[hr] : 0.f;
+          char* ob = dres(P.out, argtab);
+          if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = v;
+          else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(v);
+        } else {
+          float* part = (float*)dres(P.part, argtab) + ((int64_t)split * rows_total + row) * (HD + 2);
+          part[2 + d] = A;
+          if (d == 0) {
+            part[0] = m[hr];
+            part[1] = l[hr];
+          }
+        }
+      }
+  }
+  merge_if_last(P, argtab, b, kh, 0, nqv);
+}
+
+template <int HD>
+void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  const int dyn = 2 * 2 * TC_CH * (HD + 8) * 2;
+  static bool configured = false;  // per instantiation; set before the first launch (host thread)
+  if (!configured) {
+    CUDA_OK(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    configured = true;
+  }
+  launch_k(attn_tc_kernel<HD>, dim3((unsigned)p.splits, 1, (unsigned)(p.B * p.nkv)), dim3(128), dyn, s, 1, p, argtab);
+}
+
 template <int HPL, int NQV>
 void launch_smem(const AttnParams& p, const uint64_t* argtab, cudaStream_t s, dim3 grid) {
   constexpr int HD = HPL * 32;
@@ -649,6 +933,14 @@ void launch_hpl(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
 }  // namespace
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.use_tc) {
+    switch (p.hd) {
+      case 64: launch_tc<64>(p, argtab, s); return;
+      case 128: launch_tc<128>(p, argtab, s); return;
+      case 256: launch_tc<256>(p, argtab, s); return;
+    }
+    fail(E_INTERNAL, "tensor-core attention: unsupported head_dim");
+  }
   if (p.k_dt == KDT_BF16) {
     switch (p.hd) {
       case 32: launch_hpl<uint16_t, 1>(p, argtab, s); break;
@@ -664,6 +956,12 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
       case 256: launch_hpl<float, 8>(p, argtab, s); break;
     }
   }
+}
+
+bool attention_tc_ok(const AttnParams& p) {
+  if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || p.q.dt != KDT_BF16) return false;
+  if (p.Sq > p.qtile || p.Sq * p.group > 8 || p.Sq < 1) return false;
+  return smem_ok(p);
 }
 
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
@@ -694,6 +992,7 @@ void verify_attention(const Launch& l, const RegionFn& region) {
     region(p.counters, 4LL * p.B * p.nkv * ((p.Sq + p.qtile - 1) / p.qtile), "arrival counters");
     if (p.splits > ATTN_MERGE_MAX_SPLITS || p.qtile * p.group > 8) fail(E_INTERNAL, "attention merge too wide");
   }
+  if (p.use_tc && !attention_tc_ok(p)) fail(E_INTERNAL, "tensor-core attention on unsupported views");
   if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||
       p.k.shape[1] != p.nkv || p.k.shape[2] != p.T || p.k.shape[3] != p.hd || p.v.shape[2] != p.T ||
       p.mask.shape[3] != p.T || p.k.stride[3] != 1 || p.v.stride[3] != 1 || p.nq != p.nkv * p.group)

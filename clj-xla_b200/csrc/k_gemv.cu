@@ -326,6 +326,7 @@ void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region) {
     region(p.pf[i], p.pf_bytes[i], "prefetched weights");
   }
   if (p.nseg < 1 || p.nseg > GEMV_MAXSEG || p.seg_end[p.nseg - 1] != p.N) fail(E_INTERNAL, "gemv: bad segments");
+  if (p.has_status) region(p.status, 4, "status word");
   int64_t xs = dt_size((DT)p.x_dt);
   region(p.x, ((p.M - 1) * p.x_sm + p.K) * xs, "x");
   for (int i = 0; i < p.nseg; ++i) {

@@ -460,9 +460,9 @@ size_t cljxla_b200_profile_dump(char* out, size_t cap) {
 int cljxla_b200_plan_info(const PJRT_LoadedExecutable* ex, int64_t* info, int n) {
   if (!ex || !info) return -1;
   const Plan* pl = ex->inplace.plan ? ex->inplace.plan.get() : ex->copy.plan.get();  // the variant normally run
-  int64_t v[6] = {(int64_t)pl->launches.size(), pl->arena_bytes, pl->n_nodes,
-                  pl->n_live, pl->n_fused_groups, (int64_t)pl->const_blob.size()};
-  for (int i = 0; i < n && i < 6; ++i) info[i] = v[i];
+  int64_t v[7] = {(int64_t)pl->launches.size(), pl->arena_bytes, pl->n_nodes,
+                  pl->n_live, pl->n_fused_groups, (int64_t)pl->const_blob.size(), pl->n_jit_missing};
+  for (int i = 0; i < n && i < 7; ++i) info[i] = v[i];
   return 0;
 }
 

@@ -31,11 +31,17 @@ namespace cljxla {
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
                             "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
-                            "all_reduce"};
+                            "all_reduce", "gemv_fused", "fused_kv_write"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }
 
 namespace {
+
+// an environment switch set to 0 (for measuring a path against its alternative)
+bool getenv_off(const char* name) {
+  const char* e = getenv(name);
+  return e && e[0] == '0';
+}
 
 template <class T>
 std::vector<uint8_t> blob_of(const T& p) {
@@ -1255,14 +1261,42 @@ void Planner::emit_attention(int d2) {
     cur = I.dst;
   }
   P.chain_out = cur;
+  if (getenv("CLJXLA_B200_DEBUG_ATTN")) {
+    fprintf(stderr, "attention chain (%d ops, out r%d):", P.nchain, P.chain_out);
+    for (int i = 0; i < P.nchain; ++i)
+      fprintf(stderr, " [op %d dt %d r%d <- r%d r%d imm %g]", P.chain[i].op, P.chain[i].dt, P.chain[i].dst,
+              P.chain[i].a, P.chain[i].b, P.chain[i].fimm);
+    fprintf(stderr, " dt_d1 %d dt_m %d dt_sub %d dt_exp %d\n", P.dt_d1, P.dt_m, P.dt_sub, P.dt_exp);
+  }
+  {
+    // closed forms: trailing converts to f32 change no float value (the kernels
+    // hold f32), so drop them; then nothing (identity) or one multiply by a constant
+    int n = P.nchain, out = P.chain_out;
+    while (n > 0 && P.chain[n - 1].op == EW_CONVERT && P.chain[n - 1].dt == KDT_F32 && P.chain[n - 1].dst == out) {
+      out = P.chain[n - 1].a;
+      --n;
+    }
+    if (n == 0 && out == 0) {
+      P.chain_kind = 2;
+    } else if (n == 2 && P.chain[0].op == EW_IMM && P.chain[1].op == EW_MUL && out == P.chain[1].dst &&
+               ((P.chain[1].a == 0 && P.chain[1].b == P.chain[0].dst) ||
+                (P.chain[1].b == 0 && P.chain[1].a == P.chain[0].dst))) {
+      P.chain_kind = 1;
+      P.chain_c = P.chain[0].fimm;
+      P.chain_dt = P.chain[1].dt;
+    }
+  }
   const int64_t rows_kv = (int64_t)P.B * P.nkv;
   P.qtile = P.Sq == 1 ? 1 : std::max(1, std::min(P.Sq, 8 / P.group));
   if (P.qtile * P.group > 8) P.qtile = 1;
   if (P.group > 8) fail(E_UNIMPLEMENTED, "attention with more than 8 query heads per KV head");
   int64_t qtiles = (P.Sq + P.qtile - 1) / P.qtile;
   int64_t ctas = rows_kv * qtiles;
-  // one 128-position round per warp-group of a CTA, at most two CTAs per SM
-  int splits = (int)std::min<int64_t>((P.T + 127) / 128, std::max<int64_t>(1, 2 * 148 / ctas));
+  // one 128-position round per warp-group of a CTA, at most two CTAs per SM;
+  // the tensor-core decode kernel takes 64-position splits
+  P.use_tc = attention_tc_ok(P) && !getenv_off("CLJXLA_B200_ATTN_TC") ? 1 : 0;
+  const int64_t per_split = P.use_tc ? 64 : 128;
+  int splits = (int)std::min<int64_t>((P.T + per_split - 1) / per_split, std::max<int64_t>(1, 2 * 148 / ctas));
   splits = std::max(1, std::min(splits, ATTN_MERGE_MAX_SPLITS));
   P.splits = splits;
   P.out = slot_ptr(oslot);
@@ -1888,6 +1922,13 @@ void Planner::run() {
     t.tmap_a = DPtr{slot, 0, 128LL * t.tmap_a_index};
     t.tmap_b = DPtr{slot, 0, 128LL * t.tmap_b_index};
     t.status = DPtr{slot, 0, 128LL * (int64_t)plan_.tmaps.size()};
+  }
+  for (Launch& l : plan_.launches) {
+    if (l.kind != K_GEMV) continue;
+    GemvParams& g = *(GemvParams*)l.blob.data();
+    plan_.needs_status = true;
+    g.status = DPtr{plan_.tmap_slot(), 0, 128LL * (int64_t)plan_.tmaps.size()};
+    g.has_status = 1;
   }
   verify_plan(plan_);
   if (opt_.fuse) {

@@ -15,6 +15,8 @@ enum KernelKind : int {
   K_GEMV, K_ATTN_DECODE, K_ATTN_COMBINE, K_ROWNORM, K_GEMM_TC,
   K_MULTI,  // independent compiled fused kernels merged into one launch (parts)
   K_ALLREDUCE,  // tensor-parallel sum over the client's NCCL communicator
+  K_GEMV_FUSED,  // compiled GEMV whose x is computed in each CTA by its producer's program (parts[0])
+  K_FUSED_DUS,   // elementwise / row program (parts[0]) that also writes its output into KV windows (parts[1..], K_DUS)
   K_NUM_KINDS
 };
 const char* kernel_kind_name(int k);
@@ -49,6 +51,7 @@ struct Launch {
   void* jit_fn = nullptr;
   int64_t jit_grid = 0;
   int jit_block = 0, jit_cluster = 1;
+  int jit_smem = 0;  // dynamic shared memory bytes
   std::vector<JitArgs> jit_args;  // one per program (several for K_MULTI)
   std::vector<Launch> parts;      // K_MULTI: the merged launches, in order
 };
@@ -100,6 +103,7 @@ struct Plan {
   // outs[i] may alias param alias_param[i] (in-place dynamic_update_slice), else -1
   std::vector<int> out_alias_param;
   int n_nodes = 0, n_live = 0, n_fused_groups = 0;
+  int n_jit_missing = 0;  // launches with a compiled form that did not compile (interpreting fallback runs)
   std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
   std::vector<int64_t> tmp_bytes;    // size of each scratch buffer
   // argument table layout: [params][outputs][undo records][constant blob][scratch buffers][tensor-map table]
@@ -107,8 +111,10 @@ struct Plan {
   int const_slot() const { return dyn_slots(); }
   int tmp_slot0() const { return const_slot() + 1; }
   int tmap_slot() const { return tmp_slot0() + (int)tmp_offsets.size(); }
-  int64_t tmap_table_bytes() const { return tmaps.empty() ? 0 : 128 * (int64_t)tmaps.size() + 128; }
-  int argtab_size() const { return tmap_slot() + (tmaps.empty() ? 0 : 1); }
+  bool needs_status = false;  // kernels with bounded waits that report through the status word
+  bool has_table() const { return !tmaps.empty() || needs_status; }
+  int64_t tmap_table_bytes() const { return has_table() ? 128 * (int64_t)tmaps.size() + 128 : 0; }
+  int argtab_size() const { return tmap_slot() + (has_table() ? 1 : 0); }
 };
 
 std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);

@@ -98,6 +98,11 @@ struct Collector {
 bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
   Collector c{p, out};
   const void* b = l.blob.data();
+  if (l.kind == K_FUSED_DUS) {
+    for (const Launch& part : l.parts)
+      if (!accesses(p, part, out)) return false;
+    return true;
+  }
   switch (l.kind) {
     case K_EW: {
       const EwParams& e = *(const EwParams*)b;
@@ -148,9 +153,13 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
       c.add(g.c, g.batch * g.M * g.N * (int64_t)dt_size((DT)g.c_dt), true);
       return true;
     }
-    case K_GEMV: {
+    case K_GEMV: case K_GEMV_FUSED: {
       const GemvParams& g = *(const GemvParams*)b;
-      c.add(g.x, ((g.M - 1) * g.x_sm + g.K) * (int64_t)dt_size((DT)g.x_dt), false);
+      if (l.kind == K_GEMV_FUSED) {  // x is computed in shared memory by the producer's program
+        if (l.parts.size() != 1 || !accesses(p, l.parts[0], out)) return false;
+      } else {
+        c.add(g.x, ((g.M - 1) * g.x_sm + g.K) * (int64_t)dt_size((DT)g.x_dt), false);
+      }
       for (int i = 0; i < g.nseg; ++i) {
         const int64_t n = g.seg_end[i] - (i ? g.seg_end[i - 1] : 0);
         c.add(g.w[i], n * g.K * 2, false);
@@ -204,6 +213,7 @@ bool conflict(const std::vector<Access>& a, const std::vector<Access>& b) {
 
 // launch shape a compiled kernel would use; kinds that are not compiled fused kernels: false
 bool merge_key(const Launch& l, int* kind, int* block, int* cluster) {
+  if (l.kind == K_FUSED_DUS) return merge_key(l.parts[0], kind, block, cluster);
   if (l.kind == K_EW) {
     *kind = K_EW;
     *block = 256;
@@ -221,9 +231,174 @@ bool merge_key(const Launch& l, int* kind, int* block, int* cluster) {
   return false;
 }
 
+// A KV-window write (in-place dynamic_update_slice) whose update is exactly
+// the dense output of an earlier fused elementwise group or row region moves
+// into that program: the program stores the element into the cache window as
+// well (after saving the old value to the undo record), and the DUS launch
+// disappears.  Only when no launch in between touches what the write reads or
+// writes, so that it may run at the producer's place.
+void fuse_dus_into_producers(Plan& p) {
+  std::vector<Launch>& L = p.launches;
+  for (size_t i = 0; i < L.size(); ++i) {
+    if (L[i].kind != K_DUS) continue;
+    DusParams D;
+    memcpy(&D, L[i].blob.data(), sizeof(D));
+    auto fl = [](int t) { return t == KDT_F32 || t == KDT_BF16 || t == KDT_F16; };
+    if (!D.in_place || D.rank < 1 || D.update.rank != D.rank || !(D.update.dt == D.dt || (fl(D.update.dt) && fl(D.dt))))
+      continue;
+    int64_t nu = 1;
+    bool dense = true;
+    for (int d = D.rank - 1; d >= 0; --d) {
+      if (D.update.shape[d] != D.upd_shape[d]) dense = false;
+      if (D.upd_shape[d] != 1 && D.update.stride[d] != nu) dense = false;
+      nu *= D.upd_shape[d];
+    }
+    if (!dense || nu == 0) continue;
+    std::vector<Access> ua;
+    {
+      Collector c{p, ua};
+      c.add(D.update.p, nu * (int64_t)dt_size((DT)D.update.dt), false);
+    }
+    long j = -1;
+    for (long k = (long)i - 1; k >= 0; --k) {
+      std::vector<Access> a;
+      if (!accesses(p, L[k], a)) break;
+      if (conflict(a, ua)) {
+        j = k;
+        break;
+      }
+    }
+    if (j < 0) continue;
+    Launch& pro = L[j];
+    const Launch& base = pro.kind == K_FUSED_DUS ? pro.parts[0] : pro;
+    int out = -1;
+    if (base.kind == K_EW) {
+      const EwParams& e = *(const EwParams*)base.blob.data();
+      if (e.n != nu) continue;
+      for (int o = 0; o < e.nout; ++o)
+        if (e.out[o].p.slot == D.update.p.slot && e.out[o].p.off == D.update.p.off && e.out[o].dt == D.update.dt) out = o;
+    } else if (base.kind == K_ROWNORM) {
+      const RowParams& r = *(const RowParams*)base.blob.data();
+      if (r.rows * r.C != nu) continue;
+      for (int o = 0; o < r.nout; ++o)
+        if (!r.out[o].scalar && r.out[o].p.slot == D.update.p.slot && r.out[o].p.off == D.update.p.off &&
+            r.out[o].dt == D.update.dt)
+          out = o;
+    } else {
+      continue;
+    }
+    if (out < 0) continue;
+    std::vector<Access> da;
+    if (!accesses(p, L[i], da)) continue;
+    bool movable = true;
+    for (size_t k = (size_t)j + 1; k < i && movable; ++k) {
+      std::vector<Access> a;
+      movable = accesses(p, L[k], a) && !conflict(da, a);
+    }
+    if (!movable) continue;
+    Launch f;
+    if (pro.kind == K_FUSED_DUS) {
+      f = std::move(pro);
+    } else {
+      f.kind = K_FUSED_DUS;
+      f.label = pro.label;
+      f.algo_bytes = pro.algo_bytes;
+      f.parts.push_back(std::move(pro));
+    }
+    const size_t nb = f.blob.size();
+    f.blob.resize(nb + 4);
+    memcpy(f.blob.data() + nb, &out, 4);
+    f.label += "+" + L[i].label;
+    f.algo_bytes += L[i].algo_bytes;
+    f.parts.push_back(std::move(L[i]));
+    L[j] = std::move(f);
+    L.erase(L.begin() + i);
+    --i;
+  }
+}
+
+// The producer of a GEMV's x moves into the GEMV as a prologue when it is a
+// fused elementwise group or row region whose output is exactly x (dense
+// [M, K], x's type), x fits in shared memory, and no launch between the two
+// touches what the producer reads or writes (so the producer may run at the
+// GEMV's place).
+void fuse_gemv_prologues(Plan& p) {
+  std::vector<Launch>& L = p.launches;
+  for (size_t i = 0; i < L.size(); ++i) {
+    if (L[i].kind != K_GEMV) continue;
+    GemvParams G;
+    memcpy(&G, L[i].blob.data(), sizeof(G));
+    const int xes = (int)dt_size((DT)G.x_dt);
+    if ((G.M > 1 && G.x_sm != G.K) || G.M * G.K * xes > 144 * 1024 || G.nseg < 1) continue;
+    // the last earlier launch writing x
+    std::vector<Access> xa;
+    {
+      Collector c{p, xa};
+      c.add(G.x, G.M * G.K * xes, false);
+    }
+    long j = -1;
+    std::vector<Access> acc_j;
+    for (long k = (long)i - 1; k >= 0; --k) {
+      std::vector<Access> a;
+      if (!accesses(p, L[k], a)) break;
+      if (conflict(a, xa)) {
+        j = k;
+        acc_j = std::move(a);
+        break;
+      }
+    }
+    static const bool dbg = getenv("CLJXLA_B200_DEBUG_FUSE") != nullptr;
+    if (dbg) fprintf(stderr, "gemv %s x slot %d off %lld: producer %ld %s\n", L[i].label.c_str(), G.x.slot,
+                     (long long)G.x.off, j, j >= 0 ? L[j].label.c_str() : "-");
+    if (j < 0) continue;
+    const Launch& pro = L[j];
+    int out = -1, nbuf = 0;
+    if (pro.kind == K_ROWNORM) {
+      const RowParams& r = *(const RowParams*)pro.blob.data();
+      if (r.rows != G.M || r.C != G.K) continue;
+      for (int o = 0; o < r.nout; ++o)
+        if (!r.out[o].scalar && r.out[o].p.slot == G.x.slot && r.out[o].p.off == G.x.off && r.out[o].dt == G.x_dt) out = o;
+      nbuf = r.nin + r.nout;
+    } else if (pro.kind == K_EW) {
+      const EwParams& e = *(const EwParams*)pro.blob.data();
+      if (e.n != G.M * G.K) continue;
+      for (int o = 0; o < e.nout; ++o)
+        if (e.out[o].p.slot == G.x.slot && e.out[o].p.off == G.x.off && e.out[o].dt == G.x_dt) out = o;
+      nbuf = e.nin + e.nout;
+    } else {
+      continue;
+    }
+    if (out < 0 || nbuf + 2 * G.nseg > JIT_MAXBUF) continue;
+    bool movable = true;
+    for (size_t k = (size_t)j + 1; k < i && movable; ++k) {
+      std::vector<Access> a;
+      movable = accesses(p, L[k], a) && !conflict(acc_j, a);
+    }
+    if (!movable) continue;
+    G.pro_out = out;
+    Launch f;
+    f.kind = K_GEMV_FUSED;
+    f.blob.resize(sizeof(G));
+    memcpy(f.blob.data(), &G, sizeof(G));
+    f.label = pro.label + "+" + L[i].label;
+    f.algo_bytes = pro.algo_bytes + L[i].algo_bytes;
+    f.algo_flops = pro.algo_flops + L[i].algo_flops;
+    f.parts.push_back(std::move(L[j]));
+    L[i] = std::move(f);
+    L.erase(L.begin() + j);
+    --i;
+  }
+}
+
 }  // namespace
 
 void schedule_and_merge(Plan& p) {
+  if (getenv("CLJXLA_B200_FOLD_KV") == nullptr || getenv("CLJXLA_B200_FOLD_KV")[0] != '0') fuse_dus_into_producers(p);
+  // off by default: on Gemma-3-4B decode every CTA recomputing the norm / GeGLU
+  // before its first stage cost more (4.14 ms / step) than the separate small
+  // kernel whose latency the GEMV's early weight stream hides (3.37 ms / step)
+  if (const char* e = getenv("CLJXLA_B200_GEMV_PROLOGUE"))
+    if (e[0] == '1') fuse_gemv_prologues(p);
   const int n = (int)p.launches.size();
   if (n < 2) return;
   std::vector<std::vector<Access>> acc(n);

@@ -24,7 +24,7 @@ struct Checker {
     if (slot == P + O + U) return (int64_t)p.const_blob.size();
     int b = slot - (P + O + U + 1);
     if (b < (int)p.tmp_bytes.size()) return p.tmp_bytes[b];
-    if (slot == p.tmap_slot() && !p.tmaps.empty()) return p.tmap_table_bytes();
+    if (slot == p.tmap_slot() && p.has_table()) return p.tmap_table_bytes();
     return -1;
   }
   void region(const DPtr& d, int64_t bytes, const char* what) const {
@@ -74,6 +74,24 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
       if (l.parts.size() < 2 || l.parts.size() > (size_t)JIT_MAXPARTS) fail(E_INTERNAL, "bad merged launch");
       for (const Launch& part : l.parts) verify_launch(p, c, part);
       return;
+    }
+    if (l.kind == K_FUSED_DUS) {
+      if (l.parts.size() < 2 || (l.parts[0].kind != K_EW && l.parts[0].kind != K_ROWNORM) ||
+          l.blob.size() != 4 * (l.parts.size() - 1))
+        fail(E_INTERNAL, "bad folded KV write");
+      for (const Launch& part : l.parts) {
+        if (&part != &l.parts[0] && part.kind != K_DUS) fail(E_INTERNAL, "bad folded KV write");
+        verify_launch(p, c, part);
+      }
+      return;
+    }
+    if (l.kind == K_GEMV_FUSED) {
+      if (l.parts.size() != 1 || (l.parts[0].kind != K_EW && l.parts[0].kind != K_ROWNORM))
+        fail(E_INTERNAL, "bad GEMV prologue");
+      const GemvParams& g = *(const GemvParams*)l.blob.data();
+      if ((g.M > 1 && g.x_sm != g.K) || g.M * g.K * (int64_t)esz(g.x_dt) > 144 * 1024)
+        fail(E_INTERNAL, "GEMV prologue x not dense or too large");
+      verify_launch(p, c, l.parts[0]);
     }
     c.cur = &l;
     const void* b = l.blob.data();

@@ -150,9 +150,9 @@ def kernel_launches(ctx: Context) -> int:
 def plan_info(ctx: Context, exe: dict) -> dict:
     f = _lib(ctx).cljxla_b200_plan_info
     f.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
-    info = (ctypes.c_int64 * 6)()
-    f(ctypes.c_void_p(exe["handle"]), info, 6)
-    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes"]
+    info = (ctypes.c_int64 * 7)()
+    f(ctypes.c_void_p(exe["handle"]), info, 7)
+    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes", "jit_missing"]
     return dict(zip(keys, list(info)))
 
 

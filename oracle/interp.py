@@ -310,10 +310,13 @@ class Interpreter:
     """Executes a parsed module; ``run`` returns the outputs (and optionally every SSA value).
 
     ``ulp_noise_seed``: when set, the f32 accumulation of every ``dot_general``
-    and sum-reduce is moved by one f32 ulp up or down at random (seeded)
-    positions before it is rounded to the result type - a model of a
-    different, equally valid f32 summation order.  Tests use the spread it
-    causes as the noise floor of a whole bf16 model (see tests/parity.py).
+    and sum-reduce is moved by a seeded random number of f32 ulps before it is
+    rounded to the result type - a model of a different, equally valid f32
+    summation order.  Two orders of an n-term f32 sum differ by about
+    sqrt(n)/5 ulps of the result (median over random bf16 products; the 90th
+    percentile is 4-6x that), so the shift is normal with that standard
+    deviation (at least one ulp).  Tests use the spread it causes as the noise
+    floor of a whole bf16 model (see tests/parity.py).
     """
 
     def __init__(self, text: str, ulp_noise_seed=None, collective=None):
@@ -453,14 +456,15 @@ class Interpreter:
             return self._dot(op, args, shape, dt)
         raise NotImplementedError(f"oracle: op {name} not supported")
 
-    def _ulp_noise(self, r):
-        """One-ulp f32 noise on an f32 accumulation result, before its rounding to the result type."""
+    def _ulp_noise(self, r, n_terms=1):
+        """Summation-order noise on an f32 accumulation of n_terms terms, before its
+        rounding to the result type: a normal number of ulps, sigma max(1, sqrt(n)/5)."""
         if self._noise is None:
             return r
         r = np.asarray(r, np.float32)
-        u = self._noise.integers(-1, 2, size=r.shape)
-        up, dn = np.nextafter(r, np.float32(np.inf)), np.nextafter(r, np.float32(-np.inf))
-        return np.where(u > 0, up, np.where(u < 0, dn, r)).astype(np.float32)
+        sigma = max(1.0, float(np.sqrt(max(1, n_terms))) / 5.0)
+        u = np.rint(self._noise.normal(0.0, sigma, size=r.shape))
+        return (r.astype(np.float64) + u * np.spacing(np.abs(r)).astype(np.float64)).astype(np.float32)
 
     def _gather(self, op, args, shape, dt):
         raw = op.attrs["raw"]
@@ -492,7 +496,7 @@ class Interpreter:
                 r = np.maximum(np.max(a, axis=dims), init)
         r = np.asarray(r).reshape(shape)
         if op.body == "stablehlo.add" and dt in _FLOAT and self._noise is not None:
-            r = self._ulp_noise(r.astype(np.float32))
+            r = self._ulp_noise(r.astype(np.float32), int(np.prod([a.shape[d] for d in dims])) if dims else 1)
         return to_dtype(r, dt)
 
     def _dot(self, op, args, shape, dt):
@@ -512,7 +516,7 @@ class Interpreter:
             bt = np.asarray(b, np.float32)
             bt = bt if rc[0] == 0 else bt.T
             r = np.asarray(a, np.float32).reshape(-1, a.shape[-1]) @ bt
-            return to_dtype(self._ulp_noise(r.reshape(shape)), dt)
+            return to_dtype(self._ulp_noise(r.reshape(shape), a.shape[-1]), dt)
         at = np.asarray(np.transpose(a, lb + lf + lc), np.float32)
         bt = np.asarray(np.transpose(b, rb + rc + rf), np.float32)
         bsz = int(np.prod([a.shape[i] for i in lb])) if lb else 1
@@ -520,7 +524,7 @@ class Interpreter:
         k = int(np.prod([a.shape[i] for i in lc])) if lc else 1
         n = int(np.prod([b.shape[i] for i in rf])) if rf else 1
         r = np.matmul(at.reshape(bsz, m, k), bt.reshape(bsz, k, n))
-        return to_dtype(self._ulp_noise(r.reshape(shape)), dt)
+        return to_dtype(self._ulp_noise(r.reshape(shape), k), dt)
 
 
 def run_mlir(text: str, inputs, keep_all=False, ulp_noise_seed=None):

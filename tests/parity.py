@@ -40,9 +40,10 @@ def close_model_floor(got, want, floors, dt, margin=2.0):
     """``close_model`` with a measured noise floor.
 
     ``floors`` are the same outputs from oracle runs whose f32 dot / sum
-    results were moved by one ulp at random (a different, equally valid f32
+    results were moved by a summation-order-sized number of ulps at random
+    (about sqrt(K)/5 for a K-term sum: a different, equally valid f32
     summation order).  Whole bf16 models with scale-1.0 QK-normed attention
-    amplify such 1-ulp differences into visible logit changes (a flipped bf16
+    amplify such few-ulp differences into visible logit changes (a flipped bf16
     score rounding moves a softmax weight by tens of percent), so the device
     result passes when it is no further from the oracle than ``margin`` times
     the oracle's own spread.  Returns (ok, bad_fraction, rel_rms, floor_bad, floor_rr)."""

@@ -108,9 +108,10 @@ def test_decode_step_continues_prefill():
     assert approx_equal(a, b, atol=5e-2 * rms, rtol=5e-2)
 
 
-def test_ulp_noise_moves_f32_dots_by_at_most_one_ulp():
-    """The noise-floor option of the oracle perturbs f32 dot results by one ulp
-    at most, and leaves bf16 results and everything else untouched."""
+def test_ulp_noise_is_summation_order_sized():
+    """The noise-floor option of the oracle perturbs f32 dot results by a few
+    ulps (normal, sigma sqrt(K)/5 with K = 64 here: at least one ulp, rarely
+    more than 5), and leaves non-accumulating ops untouched."""
     g = t.trace_graph("nz", [("a", ("tensor", (4, 64), "f32")), ("b", ("tensor", (64, 32), "f32"))],
                       lambda a, b: [t.matmul(a, b), t.add(a, a)])
     text = shlo.graph_to_mlir_text(g)
@@ -120,5 +121,5 @@ def test_ulp_noise_moves_f32_dots_by_at_most_one_ulp():
     base = interp.run_mlir(text, [a, b])
     noisy = interp.run_mlir(text, [a, b], ulp_noise_seed=5)
     gap = np.abs(noisy[0].astype(np.float64) - base[0]) / np.spacing(np.abs(base[0]))
-    assert gap.max() <= 1.0 + 1e-9 and (gap > 0).any()
+    assert gap.max() <= 6.0 + 1e-9 and (gap > 0).any() and np.median(gap) <= 2.0
     np.testing.assert_array_equal(noisy[1], base[1])
