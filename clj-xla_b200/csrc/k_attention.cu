@@ -660,6 +660,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   uint16_t* Vb = tc_smem + 2 * TC_CH * ROW;     // [2][TC_CH][ROW]
   __shared__ float msk[2][8][TC_CH];
   __shared__ unsigned s_act[2];
+  __shared__ __align__(16) uint16_t qsm[8][HD + 8];
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -677,24 +678,25 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     qi = r / P.group;
     h = kh * P.group + r % P.group;
   };
-  // Q as A fragments (rows >= nqv are zero)
-  uint32_t qa[KSTEPS][4];
-#pragma unroll
-  for (int kk = 0; kk < KSTEPS; ++kk)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = g + 8 * (i & 1), c = 16 * kk + 2 * t + 8 * (i >> 1);
-      uint32_t v = 0;
-      if (r < nqv) {
-        int qi, h;
-        qrow(r, qi, h);
-        const int64_t o = b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2];
-        const float lo = ld_any(qb, o + (int64_t)c * P.q.stride[3], P.q.dt);
-        const float hi = ld_any(qb, o + (int64_t)(c + 1) * P.q.stride[3], P.q.dt);
-        v = pack_bf16(lo, hi);
-      }
-      qa[kk][i] = v;
+  // Q (bf16) through shared memory into A fragments: rows >= nqv are zero, and
+  // rows 8-15 of the 16-row tile (a1, a3) are always zero
+  for (int e = threadIdx.x; e < 8 * HD; e += 128) {
+    const int r = e / HD, c = e % HD;
+    uint16_t v = 0;
+    if (r < nqv) {
+      int qi, h;
+      qrow(r, qi, h);
+      v = ((const uint16_t*)qb)[b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2] + c * P.q.stride[3]];
     }
+    qsm[r][c] = v;
+  }
+  __syncthreads();
+  uint32_t qa[KSTEPS][2];
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk) {
+    qa[kk][0] = *(const uint32_t*)&qsm[g][16 * kk + 2 * t];
+    qa[kk][1] = *(const uint32_t*)&qsm[g][16 * kk + 2 * t + 8];
+  }
   int64_t mrow[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
@@ -768,8 +770,8 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
         for (int kk = 0; kk < KSTEPS; ++kk) {
           uint32_t bf[4];
           ldsm_x4(rowaddr + 32u * kk, bf);
-          mma_bf16(sc[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[0], bf[1]);
-          mma_bf16(sc[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], bf[2], bf[3]);
+          mma_bf16(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, bf[0], bf[1]);
+          mma_bf16(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, bf[2], bf[3]);
         }
       }
       // chain, mask, online softmax: this thread holds rows g (i = 0, 1) and

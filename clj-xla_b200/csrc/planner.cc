@@ -231,6 +231,11 @@ class Planner {
     return n;
   }
   bool is_splat(int n) const { return loc_[n].kind == Loc::SPLAT; }
+  // an elementwise node computed inside the fused concatenates that use it
+  // (one op of one memory operand and splats, e.g. the negated half of RoPE's
+  // rotate_half): no buffer, no launch of its own
+  bool concat_inline(int o) const;
+  int concat_inline_operand(int o) const;
 
   void classify();
   void group_elementwise();
@@ -334,6 +339,40 @@ void Planner::classify() {
   }
 }
 
+int Planner::concat_inline_operand(int o) const {
+  const Node& n = g_.nodes[o];
+  int x = -1, cnt = 0;
+  for (int i : n.in)
+    if (!is_splat(i)) {
+      x = i;
+      ++cnt;
+    }
+  return cnt == 1 ? x : -1;
+}
+
+bool Planner::concat_inline(int o) const {
+  if (!opt_.fuse || !live_[o] || loc_[o].kind != Loc::EW || out_claim_[o] >= 0) return false;
+  for (int x : g_.outputs)
+    if (x == o) return false;
+  const Node& n = g_.nodes[o];
+  switch (n.op) {
+    case Op::Neg: case Op::Convert:
+      if (n.in.size() != 1) return false;
+      break;
+    case Op::Add: case Op::Sub: case Op::Mul: case Op::Div: case Op::Max: case Op::Min:
+      if (n.in.size() != 2) return false;
+      break;
+    default: return false;
+  }
+  const int x = concat_inline_operand(o);
+  if (x < 0) return false;
+  const Loc::Kind xk = loc_[x].kind;
+  if (!(xk == Loc::BUF || xk == Loc::VIEWOP || xk == Loc::ROW)) return false;  // read from memory
+  for (int u : users_[o])
+    if (live_[u] && !(g_.nodes[u].op == Op::Concat && loc_[u].kind == Loc::EW)) return false;
+  return true;
+}
+
 void Planner::group_elementwise() {
   const int N = (int)g_.nodes.size();
   uf_.resize(N);
@@ -423,6 +462,7 @@ void Planner::decide_materialisation() {
   const int N = (int)g_.nodes.size();
   for (int i = 0; i < N; ++i) {
     if (!live_[i] || loc_[i].kind != Loc::EW) continue;
+    if (concat_inline(i)) continue;  // recomputed by the concatenates reading it
     bool need = out_claim_[i] >= 0;
     for (int u : users_[i]) {
       if (!live_[u]) continue;
@@ -575,6 +615,107 @@ void Planner::emit_ew_group(const std::vector<int>& members) {
       for (int o : n.in) {
         if (P.nin >= EW_MAXIN) fail(E_INTERNAL, "fused elementwise region has too many inputs");
         const Node& on = g_.nodes[o];
+        if (loc_[o].slot < 0 && concat_inline(o)) {
+          // computed here: load its memory operand over this operand's index range,
+          // apply the op, and keep the result only inside the range
+          const int x = concat_inline_operand(o);
+          const Node& xn = g_.nodes[x];
+          TView v = view_of(x);
+          EwIn& in = P.in[P.nin];
+          in.p = v.p;
+          in.dt = v.dt;
+          in.sel_dim = dim;
+          in.sel_lo = off;
+          in.sel_hi = off + on.shape[dim];
+          for (int d = 0; d < P.rank; ++d) in.stride[d] = v.stride[d];
+          bytes += xn.numel() * (int64_t)dt_size(xn.dt);
+          auto imm = [&](uint8_t dt, double val) {
+            EwInstr I{};
+            I.op = EW_IMM;
+            I.dt = dt;
+            I.dst = (uint8_t)alloc_reg();
+            I.fimm = (float)val;
+            I.iimm = (int32_t)(int64_t)val;
+            emit(I);
+            return (int)I.dst;
+          };
+          const int zero = imm((uint8_t)v.dt, 0.0);
+          EwInstr L{};
+          L.op = EW_LOAD;
+          L.dt = (uint8_t)v.dt;
+          L.aux = (uint8_t)P.nin;
+          L.b = (uint8_t)zero;
+          L.dst = (uint8_t)alloc_reg();
+          emit(L);
+          P.nin++;
+          std::vector<int> regs, tmp = {zero};
+          for (int i : on.in) {
+            if (i == x) {
+              regs.push_back(L.dst);
+            } else {
+              const int r = imm((uint8_t)kdt(g_.nodes[i].dt), loc_[i].splat);
+              regs.push_back(r);
+              tmp.push_back(r);
+            }
+          }
+          EwInstr I{};
+          I.dt = (uint8_t)kdt(on.dt);
+          switch (on.op) {
+            case Op::Neg: I.op = EW_NEG; break;
+            case Op::Convert: I.op = EW_CONVERT; I.aux = (uint8_t)kdt(xn.dt); break;
+            case Op::Add: I.op = EW_ADD; break;
+            case Op::Sub: I.op = EW_SUB; break;
+            case Op::Mul: I.op = EW_MUL; break;
+            case Op::Div: I.op = EW_DIV; break;
+            case Op::Max: I.op = EW_MAX; break;
+            default: I.op = EW_MIN; break;
+          }
+          I.a = (uint8_t)regs[0];
+          I.b = (uint8_t)(regs.size() > 1 ? regs[1] : 0);
+          I.dst = (uint8_t)alloc_reg();
+          emit(I);
+          // index along the concatenated dim within [off, off + len)?
+          EwInstr Io{};
+          Io.op = EW_IOTA;
+          Io.dt = (uint8_t)kdt(DT::I32);
+          Io.aux = (uint8_t)dim;
+          Io.dst = (uint8_t)alloc_reg();
+          emit(Io);
+          const int lo = imm((uint8_t)kdt(DT::I32), (double)off);
+          const int hi = imm((uint8_t)kdt(DT::I32), (double)(off + on.shape[dim]));
+          EwInstr C1{}, C2{}, S1{}, S2{};
+          C1.op = C2.op = EW_CMP;
+          C1.dt = C2.dt = (uint8_t)kdt(DT::I1);
+          C1.aux2 = C2.aux2 = (uint8_t)kdt(DT::I32);
+          C1.aux = 2;  // >=
+          C1.a = Io.dst;
+          C1.b = (uint8_t)lo;
+          C1.dst = (uint8_t)alloc_reg();
+          emit(C1);
+          C2.aux = 5;  // <
+          C2.a = Io.dst;
+          C2.b = (uint8_t)hi;
+          C2.dst = (uint8_t)alloc_reg();
+          emit(C2);
+          S1.op = S2.op = EW_SELECT;
+          S1.dt = S2.dt = (uint8_t)kdt(n.dt);
+          S1.a = C1.dst;
+          S1.b = I.dst;
+          S1.c = (uint8_t)cur;
+          S1.dst = (uint8_t)alloc_reg();
+          emit(S1);
+          S2.a = C2.dst;
+          S2.b = S1.dst;
+          S2.c = (uint8_t)cur;
+          S2.dst = (uint8_t)alloc_reg();
+          emit(S2);
+          for (int r : tmp) free_regs.push_back(r);
+          for (int r : {(int)L.dst, (int)I.dst, (int)Io.dst, lo, hi, (int)C1.dst, (int)C2.dst, (int)S1.dst, cur})
+            free_regs.push_back(r);
+          cur = S2.dst;
+          off += on.shape[dim];
+          continue;
+        }
         TView v = view_of(o);
         EwIn& in = P.in[P.nin];
         in.p = v.p;
