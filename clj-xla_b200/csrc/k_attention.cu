@@ -488,6 +488,10 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
 #pragma unroll
       for (int r = 0; r < NQV; ++r) s[r] = 0.f;
       if (any) {
+        // two partial sums per row (even / odd 8-element groups): two FMA chains in flight
+        float s2[NQV][2];
+#pragma unroll
+        for (int r = 0; r < NQV; ++r) s2[r][0] = s2[r][1] = 0.f;
         const uint16_t* krow = Ks + pl * ROW;
 #pragma unroll 8
         for (int c = 0; c < HD; c += 8) {
@@ -502,8 +506,10 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
 #pragma unroll
           for (int r = 0; r < NQV; ++r)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s[r] = fmaf(qs[r][c + e], kr[e], s[r]);
+            for (int e = 0; e < 8; ++e) s2[r][(c >> 3) & 1] = fmaf(qs[r][c + e], kr[e], s2[r][(c >> 3) & 1]);
         }
+#pragma unroll
+        for (int r = 0; r < NQV; ++r) s[r] = s2[r][0] + s2[r][1];
       }
       float p[NQV];
 #pragma unroll
@@ -660,7 +666,8 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   uint16_t* Vb = tc_smem + 2 * TC_CH * ROW;     // [2][TC_CH][ROW]
   __shared__ float msk[2][8][TC_CH];
   __shared__ unsigned s_act[2];
-  __shared__ __align__(16) uint16_t qsm[8][HD + 8];
+  // Q as bf16 parts: one for bf16 q; three (hi + mid + lo == q exactly) for f32 q
+  __shared__ __align__(16) uint16_t qsm[3][8][HD + 8];
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -678,38 +685,47 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     qi = r / P.group;
     h = kh * P.group + r % P.group;
   };
-  // Q (bf16) through shared memory into A fragments: rows >= nqv are zero, and
-  // rows 8-15 of the 16-row tile (a1, a3) are always zero
-  for (int e = threadIdx.x; e < 8 * HD; e += 128) {
+  // Q through shared memory; A fragments are read per k-step: rows >= nqv are
+  // zero, and rows 8-15 of the 16-row tile (a1, a3) are always zero
+  const bool qf32 = P.q.dt == KDT_F32;
+  const int qparts = qf32 ? 3 : 1;
+  __shared__ int64_t qoff_s[8], moff_s[8];
+  if (threadIdx.x < 8) {
+    const int r = threadIdx.x < nqv ? threadIdx.x : 0;
+    int qi, h;
+    qrow(r, qi, h);
+    qoff_s[threadIdx.x] = b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2];
+    moff_s[threadIdx.x] = b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2];
+  }
+  for (int e = threadIdx.x; e < 3 * 8 * (HD + 8) / 8; e += 128) ((uint4*)&qsm[0][0][0])[e] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  const int64_t qs3 = P.q.stride[3];
+  for (int e = threadIdx.x; e < nqv * HD; e += 128) {
     const int r = e / HD, c = e % HD;
-    uint16_t v = 0;
-    if (r < nqv) {
-      int qi, h;
-      qrow(r, qi, h);
-      v = ((const uint16_t*)qb)[b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2] + c * P.q.stride[3]];
+    const int64_t o = qoff_s[r] + c * qs3;
+    if (qf32) {
+      const float q = ((const float*)qb)[o];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(q);
+      const float r1 = q - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+      qsm[0][r][c] = __bfloat16_as_ushort(hi);
+      qsm[1][r][c] = __bfloat16_as_ushort(mid);
+      qsm[2][r][c] = __bfloat16_as_ushort(lo);
+    } else {
+      qsm[0][r][c] = ((const uint16_t*)qb)[o];
     }
-    qsm[r][c] = v;
   }
   __syncthreads();
-  uint32_t qa[KSTEPS][2];
-#pragma unroll
-  for (int kk = 0; kk < KSTEPS; ++kk) {
-    qa[kk][0] = *(const uint32_t*)&qsm[g][16 * kk + 2 * t];
-    qa[kk][1] = *(const uint32_t*)&qsm[g][16 * kk + 2 * t + 8];
-  }
-  int64_t mrow[8];
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-    int qi, h;
-    qrow(r < nqv ? r : 0, qi, h);
-    mrow[r] = b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2];
-  }
+  const uint32_t qsa = (uint32_t)__cvta_generic_to_shared(&qsm[0][g][2 * t]);
+  constexpr uint32_t QPART = 8 * (HD + 8) * 2;  // bytes between Q parts
+  const int64_t ms3 = P.mask.stride[3];
   // stage chunk c0 into buffer buf: mask values, active steps, K/V rows of active steps
   auto stage = [&](int64_t c0, int buf) {
-    for (int e = threadIdx.x; e < 8 * TC_CH; e += 128) {
+    for (int e = threadIdx.x; e < nqv * TC_CH; e += 128) {
       const int r = e / TC_CH, j = e % TC_CH;
       float v = -INFINITY;
-      if (r < nqv && c0 + j < t1) v = ld_any(mb, mrow[r] + (c0 + j) * P.mask.stride[3], P.mask.dt);
+      if (c0 + j < t1) v = ld_any(mb, moff_s[r] + (c0 + j) * ms3, P.mask.dt);
       msk[buf][r][j] = v;
     }
     if (threadIdx.x == 0) s_act[buf] = 0u;
@@ -761,8 +777,15 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
       if (!((act >> st) & 1u)) continue;
       const int s0 = st * 16;
       // scores S[16 rows][16 positions]: two 8-position tiles
+      // four independent accumulator sets (k-step mod 4) keep four mma chains
+      // in flight instead of one serial chain through all of head_dim
       float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       {
+        float sp[4][2][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sp[a][0][i] = sp[a][1][i] = 0.f;
         const int mi = lane >> 3, ri = lane & 7;
         const uint32_t rowaddr =
             kb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi >> 1)) * ROW + 8 * (mi & 1)) * 2);
@@ -770,9 +793,18 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
         for (int kk = 0; kk < KSTEPS; ++kk) {
           uint32_t bf[4];
           ldsm_x4(rowaddr + 32u * kk, bf);
-          mma_bf16(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, bf[0], bf[1]);
-          mma_bf16(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, bf[2], bf[3]);
+          for (int qp = 0; qp < qparts; ++qp) {
+            uint32_t a0, a2;
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a0) : "r"(qsa + qp * QPART + 32u * kk));
+            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a2) : "r"(qsa + qp * QPART + 32u * kk + 16u));
+            mma_bf16(sp[kk & 3][0], a0, 0u, a2, 0u, bf[0], bf[1]);
+            mma_bf16(sp[kk & 3][1], a0, 0u, a2, 0u, bf[2], bf[3]);
+          }
         }
+#pragma unroll
+        for (int tl = 0; tl < 2; ++tl)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sc[tl][i] = (sp[0][tl][i] + sp[1][tl][i]) + (sp[2][tl][i] + sp[3][tl][i]);
       }
       // chain, mask, online softmax: this thread holds rows g (i = 0, 1) and
       // g + 8 (i = 2, 3); with at most 8 query vectors only rows g can hold any
@@ -961,7 +993,7 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
 }
 
 bool attention_tc_ok(const AttnParams& p) {
-  if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || p.q.dt != KDT_BF16) return false;
+  if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || !(p.q.dt == KDT_BF16 || p.q.dt == KDT_F32)) return false;
   if (p.Sq > p.qtile || p.Sq * p.group > 8 || p.Sq < 1) return false;
   return smem_ok(p);
 }

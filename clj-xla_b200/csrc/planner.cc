@@ -1436,7 +1436,9 @@ void Planner::emit_attention(int d2) {
   // one 128-position round per warp-group of a CTA, at most two CTAs per SM;
   // the tensor-core decode kernel takes 64-position splits
   P.use_tc = attention_tc_ok(P) && !getenv_off("CLJXLA_B200_ATTN_TC") ? 1 : 0;
-  const int64_t per_split = P.use_tc ? 64 : 128;
+  int64_t per_split = P.use_tc ? 64 : 128;
+  if (const char* e = getenv("CLJXLA_B200_ATTN_SPLIT"))  // positions per split (measurement sweeps)
+    if (atoi(e) >= 16) per_split = atoi(e);
   int splits = (int)std::min<int64_t>((P.T + per_split - 1) / per_split, std::max<int64_t>(1, 2 * 148 / ctas));
   splits = std::max(1, std::min(splits, ATTN_MERGE_MAX_SPLITS));
   P.splits = splits;
