@@ -661,11 +661,16 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   constexpr int ROW = HD + 8;            // padded smem row (bf16): rows 16 B apart in bank phase
   constexpr int KSTEPS = HD / 16;        // k-steps of the score product
   constexpr int NT = HD / 32;            // 8-dim output tiles per warp (a quarter of head_dim)
+  static_assert(TC_CH == 4 * 16, "one 16-position score step per warp");
   extern __shared__ __align__(16) uint16_t tc_smem[];
-  uint16_t* Kb = tc_smem;                       // [2][TC_CH][ROW]
-  uint16_t* Vb = tc_smem + 2 * TC_CH * ROW;     // [2][TC_CH][ROW]
+  // K / V chunk buffers: two (double-buffered) when a CTA walks several chunks
+  const int nbuf = (P.T + P.splits - 1) / P.splits > TC_CH ? 2 : 1;
+  uint16_t* Kb = tc_smem;                          // [nbuf][TC_CH][ROW]
+  uint16_t* Vb = tc_smem + nbuf * TC_CH * ROW;     // [nbuf][TC_CH][ROW]
   __shared__ float msk[2][8][TC_CH];
   __shared__ unsigned s_act[2];
+  __shared__ float red_m[4][8], red_l[4][8];      // per-warp row max / sum of a chunk
+  __shared__ uint32_t psm[2][8][TC_CH / 2 + 4];   // P hi / lo bf16 pairs, rows padded against bank conflicts
   // Q as bf16 parts: one for bf16 q; three (hi + mid + lo == q exactly) for f32 q
   __shared__ __align__(16) uint16_t qsm[3][8][HD + 8];
   pdl_enter();
@@ -716,12 +721,13 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
       qsm[0][r][c] = ((const uint16_t*)qb)[o];
     }
   }
-  __syncthreads();
   const uint32_t qsa = (uint32_t)__cvta_generic_to_shared(&qsm[0][g][2 * t]);
   constexpr uint32_t QPART = 8 * (HD + 8) * 2;  // bytes between Q parts
   const int64_t ms3 = P.mask.stride[3];
   // stage chunk c0 into buffer buf: mask values, active steps, K/V rows of active steps
-  auto stage = [&](int64_t c0, int buf) {
+  // staging of a chunk, in two halves around a barrier the caller places:
+  // mask values first, then (once they are visible) the K/V rows of active steps
+  auto stage_mask = [&](int64_t c0, int buf) {
     for (int e = threadIdx.x; e < nqv * TC_CH; e += 128) {
       const int r = e / TC_CH, j = e % TC_CH;
       float v = -INFINITY;
@@ -729,7 +735,8 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
       msk[buf][r][j] = v;
     }
     if (threadIdx.x == 0) s_act[buf] = 0u;
-    __syncthreads();
+  };
+  auto stage_kv = [&](int64_t c0, int buf) {
     if (threadIdx.x < TC_CH) {
       bool any = false;
       for (int r = 0; r < nqv; ++r) any |= msk[buf][r][threadIdx.x] > P.mask_skip;
@@ -761,118 +768,118 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
   int buf = 0;
-  if (t0 < t1) stage(t0, 0);
+  // the first chunk's mask loads overlap the query loads above: one barrier for both
+  if (t0 < t1) stage_mask(t0, 0);
+  __syncthreads();
+  if (t0 < t1) stage_kv(t0, 0);
   for (int64_t c0 = t0; c0 < t1; c0 += TC_CH, buf ^= 1) {
     const bool more = c0 + TC_CH < t1;
     if (more) {
-      stage(c0 + TC_CH, buf ^ 1);  // next chunk in flight while this one is computed
+      stage_mask(c0 + TC_CH, buf ^ 1);  // next chunk in flight while this one is computed
+      __syncthreads();
+      stage_kv(c0 + TC_CH, buf ^ 1);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
     const unsigned act = s_act[buf];
+    // scores of this warp's 16-position step (S = Q K^T, 16 x 16), four
+    // independent accumulator sets (k-step mod 4) so four mma chains are in flight
+    const int s0 = warp * 16;
+    const bool mine = (act >> warp) & 1u;
+    float mv[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (mine) {
+      float sp[4][2][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sp[a][0][i] = sp[a][1][i] = 0.f;
+      const int mi = lane >> 3, ri = lane & 7;
+      const uint32_t rowaddr =
+          kb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi >> 1)) * ROW + 8 * (mi & 1)) * 2);
+#pragma unroll
+      for (int kk = 0; kk < KSTEPS; ++kk) {
+        uint32_t bf[4];
+        ldsm_x4(rowaddr + 32u * kk, bf);
+        for (int qp = 0; qp < qparts; ++qp) {
+          uint32_t a0, a2;
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a0) : "r"(qsa + qp * QPART + 32u * kk));
+          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a2) : "r"(qsa + qp * QPART + 32u * kk + 16u));
+          mma_bf16(sp[kk & 3][0], a0, 0u, a2, 0u, bf[0], bf[1]);
+          mma_bf16(sp[kk & 3][1], a0, 0u, a2, 0u, bf[2], bf[3]);
+        }
+      }
+      // chain and mask on this thread's row-g elements (rows g + 8 are padding:
+      // at most 8 query vectors)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int tile = q >> 1, i = q & 1;
+        const float acc = (sp[0][tile][i] + sp[1][tile][i]) + (sp[2][tile][i] + sp[3][tile][i]);
+        const int j = s0 + 8 * tile + 2 * t + i;
+        const float mk = msk[buf][g][j];
+        if (g < nqv && mk > P.mask_skip)
+          mv[q] = rnd_dt(apply_chain(P, rnd_dt(acc, P.dt_d1)) + mk, P.dt_m);
+      }
+    }
+    float rmax = fmaxf(fmaxf(mv[0], mv[1]), fmaxf(mv[2], mv[3]));
+    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
+    rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
+    if (t == 0) red_m[warp][g] = rmax;
+    __syncthreads();
+    // the chunk's row maximum, the same in every warp
+    const float mnew = fmaxf(fmaxf(m[0], fmaxf(red_m[0][g], red_m[1][g])), fmaxf(red_m[2][g], red_m[3][g]));
+    float pv[4];
+    float ps = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      pv[q] = 0.f;
+      if (mnew != -INFINITY && mv[q] != -INFINITY) pv[q] = rnd_dt(expf(rnd_dt(mv[q] - mnew, P.dt_sub)), P.dt_exp);
+      ps += pv[q];
+    }
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    if (t == 0) red_l[warp][g] = ps;
+    // P of this step as bf16 hi / lo pairs for the P V product of every warp
+#pragma unroll
+    for (int tile = 0; tile < 2; ++tile) {
+      const uint32_t hi = pack_bf16(pv[2 * tile], pv[2 * tile + 1]);
+      const uint32_t lo = pack_bf16(pv[2 * tile] - bf16_lo_f(hi), pv[2 * tile + 1] - bf16_hi_f(hi));
+      psm[0][g][8 * warp + 4 * tile + t] = hi;
+      psm[1][g][8 * warp + 4 * tile + t] = lo;
+    }
+    __syncthreads();
+    if (mnew != -INFINITY) {
+      const float csum = (red_l[0][g] + red_l[1][g]) + (red_l[2][g] + red_l[3][g]);
+      const float scl = m[0] == -INFINITY ? 0.f : expf(m[0] - mnew);
+      l[0] = l[0] * scl + csum;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        o[n][0] *= scl;
+        o[n][1] *= scl;
+      }
+      m[0] = mnew;
+    }
+    // O[:, warp quarter] += P V over the chunk's active steps
 #pragma unroll 1
     for (int st = 0; st < TC_CH / 16; ++st) {
       if (!((act >> st) & 1u)) continue;
-      const int s0 = st * 16;
-      // scores S[16 rows][16 positions]: two 8-position tiles
-      // four independent accumulator sets (k-step mod 4) keep four mma chains
-      // in flight instead of one serial chain through all of head_dim
-      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      {
-        float sp[4][2][4];
+      const uint32_t ah0 = psm[0][g][8 * st + t], ah2 = psm[0][g][8 * st + 4 + t];
+      const uint32_t al0 = psm[1][g][8 * st + t], al2 = psm[1][g][8 * st + 4 + t];
+      const int mi = lane >> 3, ri = lane & 7;
+      const uint32_t rowaddr = vb_s + (uint32_t)((((size_t)buf * TC_CH + 16 * st + ri + 8 * (mi & 1)) * ROW +
+                                                  warp * (HD / 4) + 8 * (mi >> 1)) * 2);
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sp[a][0][i] = sp[a][1][i] = 0.f;
-        const int mi = lane >> 3, ri = lane & 7;
-        const uint32_t rowaddr =
-            kb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi >> 1)) * ROW + 8 * (mi & 1)) * 2);
-#pragma unroll
-        for (int kk = 0; kk < KSTEPS; ++kk) {
-          uint32_t bf[4];
-          ldsm_x4(rowaddr + 32u * kk, bf);
-          for (int qp = 0; qp < qparts; ++qp) {
-            uint32_t a0, a2;
-            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a0) : "r"(qsa + qp * QPART + 32u * kk));
-            asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a2) : "r"(qsa + qp * QPART + 32u * kk + 16u));
-            mma_bf16(sp[kk & 3][0], a0, 0u, a2, 0u, bf[0], bf[1]);
-            mma_bf16(sp[kk & 3][1], a0, 0u, a2, 0u, bf[2], bf[3]);
-          }
-        }
-#pragma unroll
-        for (int tl = 0; tl < 2; ++tl)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) sc[tl][i] = (sp[0][tl][i] + sp[1][tl][i]) + (sp[2][tl][i] + sp[3][tl][i]);
-      }
-      // chain, mask, online softmax: this thread holds rows g (i = 0, 1) and
-      // g + 8 (i = 2, 3); with at most 8 query vectors only rows g can hold any
-      float pv[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll 1
-      for (int hr = 0; hr < 1; ++hr) {
-        const int r = g + 8 * hr;
-        float mv[4];
-        float rmax = -INFINITY;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int tile = q >> 1, j = s0 + 8 * tile + 2 * t + (q & 1);
-          const float mk = r < 8 ? msk[buf][r][j] : -INFINITY;
-          const bool valid = r < nqv && mk > P.mask_skip;
-          mv[q] = -INFINITY;
-          if (valid) mv[q] = rnd_dt(apply_chain(P, rnd_dt(sc[tile][2 * hr + (q & 1)], P.dt_d1)) + mk, P.dt_m);
-          rmax = fmaxf(rmax, mv[q]);
-        }
-        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
-        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
-        const float mnew = fmaxf(m[hr], rmax);
-        float ps = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float p = 0.f;
-          if (mnew != -INFINITY && mv[q] != -INFINITY) p = rnd_dt(expf(rnd_dt(mv[q] - mnew, P.dt_sub)), P.dt_exp);
-          pv[q >> 1][2 * hr + (q & 1)] = p;
-          ps += p;
-        }
-        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
-        if (mnew != -INFINITY) {
-          const float scl = m[hr] == -INFINITY ? 0.f : expf(m[hr] - mnew);
-          l[hr] = l[hr] * scl + ps;
-#pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            o[n][2 * hr] *= scl;
-            o[n][2 * hr + 1] *= scl;
-          }
-          m[hr] = mnew;
-        }
-      }
-      // P as A fragments, hi and lo bf16 parts
-      uint32_t ah[4], al[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int tile = i >> 1, hr = i & 1;
-        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
-        ah[i] = pack_bf16(p0, p1);
-        al[i] = pack_bf16(p0 - bf16_lo_f(ah[i]), p1 - bf16_hi_f(ah[i]));
-      }
-      // O[:, warp quarter] += P V
-      {
-        const int mi = lane >> 3, ri = lane & 7;
-        const uint32_t rowaddr = vb_s + (uint32_t)((((size_t)buf * TC_CH + s0 + ri + 8 * (mi & 1)) * ROW +
-                                                    warp * (HD / 4) + 8 * (mi >> 1)) * 2);
-#pragma unroll
-        for (int n = 0; n < NT; n += 2) {
-          uint32_t bf[4];
-          ldsm_x4_t(rowaddr + 32u * (n / 2), bf);
-          mma_bf16(o[n], ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
-          mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
-          mma_bf16(o[n + 1], ah[0], ah[1], ah[2], ah[3], bf[2], bf[3]);
-          mma_bf16(o[n + 1], al[0], al[1], al[2], al[3], bf[2], bf[3]);
-        }
+      for (int n = 0; n < NT; n += 2) {
+        uint32_t bf[4];
+        ldsm_x4_t(rowaddr + 32u * (n / 2), bf);
+        mma_bf16(o[n], ah0, 0u, ah2, 0u, bf[0], bf[1]);
+        mma_bf16(o[n], al0, 0u, al2, 0u, bf[0], bf[1]);
+        mma_bf16(o[n + 1], ah0, 0u, ah2, 0u, bf[2], bf[3]);
+        mma_bf16(o[n + 1], al0, 0u, al2, 0u, bf[2], bf[3]);
       }
     }
-    __syncthreads();  // this buffer is restaged two chunks later
+    __syncthreads();  // red / psm and this buffer are rewritten by the next chunk
   }
   // results: rows g and g + 8 of this warp's quarter of head_dim
   const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
@@ -909,10 +916,12 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 
 template <int HD>
 void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
-  const int dyn = 2 * 2 * TC_CH * (HD + 8) * 2;
+  const int nbuf = (p.T + p.splits - 1) / p.splits > TC_CH ? 2 : 1;  // as the kernel decides
+  const int dyn = nbuf * 2 * TC_CH * (HD + 8) * 2;
   static bool configured = false;  // per instantiation; set before the first launch (host thread)
   if (!configured) {
-    CUDA_OK(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
+    CUDA_OK(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * 2 * TC_CH * (HD + 8) * 2));
     configured = true;
   }
   launch_k(attn_tc_kernel<HD>, dim3((unsigned)p.splits, 1, (unsigned)(p.B * p.nkv)), dim3(128), dyn, s, 1, p, argtab);
