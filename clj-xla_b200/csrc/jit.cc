@@ -143,6 +143,11 @@ struct Emitter {
   std::vector<std::string> x;  // index variable per loop dim
   std::vector<std::string> in_base;
   int counter = 0;
+  // per-thread register cache of loaded inputs (row bodies whose row fits a few
+  // elements per thread): input i element jj lives in cache_arr[i][cache_j]
+  std::vector<std::string> cache_arr;
+  std::string cache_j;
+  std::vector<char> cached;
 
   std::string reg_or_zero(const std::vector<std::string>& reg, int r) {
     return (r >= 0 && r < (int)reg.size() && !reg[r].empty()) ? reg[r] : std::string("0u");
@@ -190,6 +195,14 @@ struct Emitter {
           return;
         }
         e = load_expr(base, offset(in, -1, ""), in.dt);
+        if (I.aux < (int)cache_arr.size() && !cache_arr[I.aux].empty()) {
+          const std::string slot = cache_arr[I.aux] + "[" + cache_j + "]";
+          if (!cached[I.aux]) {  // first phase to read it loads it; later phases reuse the register
+            s << indent << slot << " = " << e << ";\n";
+            cached[I.aux] = 1;
+          }
+          e = slot;
+        }
         break;
       }
       case EW_IMM: e = fl ? hex32(*(const uint32_t*)&I.fimm) : "(u32)" + std::to_string(I.iimm); break;
@@ -432,13 +445,37 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
   for (int r = RP_SREG0; r < RP_NREG; ++r) s << "    u32 s" << r << " = 0u; (void)s" << r << ";\n";
   for (int r = RP_SREG0; r < RP_NREG; ++r) sreg[r] = "s" + std::to_string(r);
   const std::string xc = "x" + std::to_string(P.rank - 1);
+  // a row of a few elements per thread: every phase walks the same J elements,
+  // so the inputs are loaded once (first phase) and kept in registers
+  const int J = (CL == 1 && Cc <= 4LL * BLOCK) ? (int)((Cc + BLOCK - 1) / BLOCK) : 0;
+  if (J > 0) {
+    em.cache_arr.assign(P.nin, std::string());
+    em.cached.assign(P.nin, 0);
+    em.cache_j = "jj";
+    for (int i = 0; i < P.nin; ++i)
+      if (P.in[i].sel_dim < 0) {
+        em.cache_arr[i] = "cin" + std::to_string(i);
+        s << "    u32 cin" << i << "[" << J << "];\n";
+      }
+  }
   for (int ph = 0; ph < P.nphase; ++ph) {
     const RowPhase& Ph = P.ph[ph];
     const bool sum = Ph.red_kind == 0;
     s << "    {  // phase " << ph << "\n";
     s << "      float acc = " << (sum ? "0.0f" : "-__int_as_float(0x7f800000)") << ";\n";
-    s << "      for (i64 " << xc << " = c0 + threadIdx.x; " << xc << " < c1; " << xc << " += " << BLOCK << ") {\n";
+    if (J > 0)
+      s << "#pragma unroll\n      for (int jj = 0; jj < " << J << "; ++jj) {\n        const i64 " << xc
+        << " = c0 + threadIdx.x + (i64)jj * " << BLOCK << ";\n        if (" << xc << " < c1) {\n";
+    else
+      s << "      for (i64 " << xc << " = c0 + threadIdx.x; " << xc << " < c1; " << xc << " += " << BLOCK << ") {\n";
     std::vector<std::string> reg = sreg;  // per-element registers start undefined
+    if (J > 0 && ph == 0)  // every cached input in flight at once, before any phase needs it
+      for (int i = 0; i < P.nin; ++i)
+        if (!em.cache_arr[i].empty() && !em.cached[i]) {
+          s << "        " << em.cache_arr[i] << "[jj] = "
+            << load_expr(em.in_base[i], em.offset(P.in[i], -1, ""), P.in[i].dt) << ";\n";
+          em.cached[i] = 1;
+        }
     for (int pc = Ph.lo; pc < Ph.hi; ++pc) em.step(P.code[pc], reg, "        ");
     if (Ph.red_reg >= 0) {
       const std::string xv = "F(" + em.reg_or_zero(reg, Ph.red_reg) + ")";
@@ -453,7 +490,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
         if (o == bo.smem_out) s << "        " << store_stmt("xsb", off, P.out[o].dt, v) << "\n";
         emit_dus_stores(s, bo, o, off, v, "        ");
       }
-    s << "      }\n";
+    s << (J > 0 ? "        }\n      }\n" : "      }\n");
     if (Ph.red_reg >= 0) {
       const std::string comb = sum ? "t = t + o;" : "t = fmaxf(t, o);";
       s << "      for (int sh = 16; sh > 0; sh >>= 1) { float o = __shfl_xor_sync(0xffffffffu, acc, sh); "

@@ -154,40 +154,47 @@ __device__ void merge_if_last(const AttnParams& P, const uint64_t* __restrict__ 
   if (P.splits == 1 || !P.use_counters) return;
   __shared__ int s_last;
   __shared__ float s_sc[ATTN_MERGE_MAX_SPLITS][8];
+  __shared__ float s_pl[ATTN_MERGE_MAX_SPLITS][8];
   __shared__ float s_l[8];
-  __threadfence();  // this CTA's partials are visible before it is counted
+  // the barrier orders every thread's partial stores before thread 0's release;
+  // the acquire of the last arrival orders its reads after everyone's stores
   __syncthreads();
   unsigned* ctr = (unsigned*)dres(P.counters, argtab) + ((int64_t)blockIdx.z * gridDim.y + blockIdx.y);
-  if (threadIdx.x == 0) s_last = atomicAdd(ctr, 1u) == (unsigned)(P.splits - 1);
+  if (threadIdx.x == 0) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+    s_last = old == (unsigned)(P.splits - 1);
+  }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   const int64_t rows_total = (int64_t)P.B * P.nq * P.Sq;
   const float* part = (const float*)dres(P.part, argtab);
   char* ob = dres(P.out, argtab);
   const int HD = P.hd, S = P.splits;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   auto row_of = [&](int r) {
     const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
     return ((int64_t)b * P.nq + h) * P.Sq + qi;
   };
-  for (int r = warp; r < nqv; r += nw) {
-    const int64_t row = row_of(r);
+  // every split's (max, sum) of every row at once, then the scale factors
+  for (int e = threadIdx.x; e < S * nqv; e += blockDim.x) {
+    const int sp = e / nqv, r = e % nqv;
+    const float* pp = part + ((int64_t)sp * rows_total + row_of(r)) * (HD + 2);
+    s_sc[sp][r] = __ldcg(pp);
+    s_pl[sp][r] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < nqv) {
+    const int r = threadIdx.x;
     float m = -INFINITY;
-    for (int sp = lane; sp < S; sp += 32) m = fmaxf(m, __ldcg(part + ((int64_t)sp * rows_total + row) * (HD + 2)));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    for (int sp = 0; sp < S; ++sp) m = fmaxf(m, s_sc[sp][r]);
     float l = 0.f;
-    for (int sp = lane; sp < S; sp += 32) {
-      const float* pp = part + ((int64_t)sp * rows_total + row) * (HD + 2);
-      const float pm = __ldcg(pp);
+    for (int sp = 0; sp < S; ++sp) {
+      const float pm = s_sc[sp][r];
       const float sc = (m == -INFINITY || pm == -INFINITY) ? 0.f : expf(pm - m);
       s_sc[sp][r] = sc;
-      l += sc == 0.f ? 0.f : __ldcg(pp + 1) * sc;
+      l += sc == 0.f ? 0.f : s_pl[sp][r] * sc;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) s_l[r] = l;
+    s_l[r] = l;
   }
   __syncthreads();
   const int half = HD / 2;
@@ -736,14 +743,16 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     }
     if (threadIdx.x == 0) s_act[buf] = 0u;
   };
-  auto stage_kv = [&](int64_t c0, int buf) {
+  // active 16-position steps of a staged mask (after a barrier; one follows)
+  auto stage_active = [&](int buf) {
     if (threadIdx.x < TC_CH) {
       bool any = false;
       for (int r = 0; r < nqv; ++r) any |= msk[buf][r][threadIdx.x] > P.mask_skip;
       if (any) atomicOr(&s_act[buf], 1u << (threadIdx.x / 16));
     }
-    __syncthreads();
-    const unsigned act = s_act[buf];
+  };
+  // K/V rows of the steps in `act` (one cp.async group)
+  auto stage_copy = [&](int64_t c0, int buf, unsigned act) {
     constexpr int SEGS = HD / 8;  // 16-byte pieces per row
     for (int q = threadIdx.x; q < TC_CH * SEGS; q += 128) {
       const int rr = q / SEGS, sg = q % SEGS;
@@ -768,16 +777,23 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
   int buf = 0;
-  // the first chunk's mask loads overlap the query loads above: one barrier for both
-  if (t0 < t1) stage_mask(t0, 0);
+  // the first chunk's K/V rows (all of them: the mask is not known yet), its
+  // mask values and the queries above are all in flight together
+  if (t0 < t1) {
+    stage_copy(t0, 0, 0xfu);
+    stage_mask(t0, 0);
+  }
   __syncthreads();
-  if (t0 < t1) stage_kv(t0, 0);
+  if (t0 < t1) stage_active(0);
+  __syncthreads();
   for (int64_t c0 = t0; c0 < t1; c0 += TC_CH, buf ^= 1) {
     const bool more = c0 + TC_CH < t1;
     if (more) {
       stage_mask(c0 + TC_CH, buf ^ 1);  // next chunk in flight while this one is computed
       __syncthreads();
-      stage_kv(c0 + TC_CH, buf ^ 1);
+      stage_active(buf ^ 1);
+      __syncthreads();
+      stage_copy(c0 + TC_CH, buf ^ 1, s_act[buf ^ 1]);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
