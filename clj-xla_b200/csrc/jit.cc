@@ -641,8 +641,18 @@ int sm_count() {
 // sets the plan's status word and the CTA stops, after the producer has
 // waited (bounded) for its copies in flight.
 struct GemvGeometry {
-  int wpr, rps, nstage, stage_bytes, x_bytes;
+  int wpr, rps, nstage, stage_bytes, x_bytes, ctas_per_sm;
 };
+
+// CTAs per SM of the bulk-copy GEMV (CLJXLA_B200_GEMV_CTAS, 1 or 2): two halve
+// each CTA's ring so that two pipelines share an SM
+int gemv_ctas_per_sm() {
+  static const int n = [] {
+    const char* e = getenv("CLJXLA_B200_GEMV_CTAS");
+    return e && e[0] == '2' ? 2 : 1;
+  }();
+  return n;
+}
 
 bool gemv_tma_geometry(const GemvParams& G, GemvGeometry* g) {
   constexpr int WARPS = 8;
@@ -655,7 +665,8 @@ bool gemv_tma_geometry(const GemvParams& G, GemvGeometry* g) {
   g->stage_bytes = (int)(g->rps * G.K * 2);
   g->x_bytes = (int)(G.M * G.K * (G.x_dt == KDT_F32 ? 4 : 2));
   if (g->x_bytes > 64 * 1024) return false;
-  const int budget = 200 * 1024 - g->x_bytes;
+  g->ctas_per_sm = gemv_ctas_per_sm();
+  const int budget = (g->ctas_per_sm == 2 ? 108 : 200) * 1024 - g->x_bytes;
   g->nstage = std::min(4, budget / g->stage_bytes);
   return g->nstage >= 2;
 }
@@ -700,7 +711,8 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
   const int64_t M = G.M, K = G.K, N = G.N;
   const int WPR = geo.wpr, RPS = geo.rps, NST = geo.nstage;
   const int64_t KP = K / WPR;
-  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + RPS - 1) / RPS));
+  const int64_t ctas =
+      std::max<int64_t>(1, std::min<int64_t>((int64_t)geo.ctas_per_sm * sm_count(), (N + RPS - 1) / RPS));
   const int xes = G.x_dt == KDT_F32 ? 4 : 2;
   const int stage_stride = (geo.stage_bytes + 1023) & ~1023;
   std::ostringstream s;
@@ -778,7 +790,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
   s << "  return e;\n}\n";
   s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
-    << ", 1) cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
+    << ", " << geo.ctas_per_sm << ") cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
   s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
   s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
   s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
@@ -823,6 +835,14 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   }
   s << "  consumers_sync();\n";
   s << "  const int rr = warp / " << WPR << ", part = warp % " << WPR << ";\n";
+  // M = 1: x is the same for every row; each lane keeps its x vectors in registers
+  const int NV = (M == 1 && (KP / 8 + 31) / 32 <= 12) ? (int)((KP / 8 + 31) / 32) : 0;
+  if (NV > 0) {
+    s << "  float xr[" << NV << "][8];\n#pragma unroll\n  for (int i = 0; i < " << NV << "; ++i) {\n";
+    s << "    const int v = lane + 32 * i;\n";
+    s << "    if (v < " << KP / 8 << ") xs8(xsa + (u32)(part * " << KP * xes << "LL) + " << 8 * xes << "u * v, xr[i]);\n";
+    s << "    else for (int e = 0; e < 8; ++e) xr[i][e] = 0.f;\n  }\n";
+  }
   s << "  int st = 0;\n";
   s << "  for (i64 r = r0; r < r1; ++st) {\n    const int slot = st % " << NST << ";\n";
   s << "    const i64 e = stage_end(r, r1);\n";
@@ -835,11 +855,16 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "      const u32 wa = stage0 + (u32)slot * " << stage_stride << "u + (u32)((rr * " << K << "LL + part * " << KP
     << "LL) * 2);\n";
   s << "      const u32 xa = xsa + (u32)(part * " << KP * xes << "LL);\n";
-  s << "#pragma unroll 4\n      for (int v = lane; v < " << KP / 8 << "; v += 32) {\n";
-  s << "        const uint4 w = lds16(wa + 16u * v);\n";
-  s << "#pragma unroll\n        for (int m = 0; m < " << M << "; ++m) {\n          float xv[8];\n";
-  s << "          xs8(xa + (u32)(m * " << K * xes << "LL) + " << 8 * xes << "u * v, xv);\n";
-  s << "          acc[m] += dot8(w, xv);\n        }\n      }\n    }\n";
+  if (NV > 0) {  // one row: this lane's x vectors are in registers
+    s << "#pragma unroll\n      for (int i = 0; i < " << NV << "; ++i) {\n        const int v = lane + 32 * i;\n";
+    s << "        if (v < " << KP / 8 << ") acc[0] += dot8(lds16(wa + 16u * v), xr[i]);\n      }\n    }\n";
+  } else {
+    s << "#pragma unroll 4\n      for (int v = lane; v < " << KP / 8 << "; v += 32) {\n";
+    s << "        const uint4 w = lds16(wa + 16u * v);\n";
+    s << "#pragma unroll\n        for (int m = 0; m < " << M << "; ++m) {\n          float xv[8];\n";
+    s << "          xs8(xa + (u32)(m * " << K * xes << "LL) + " << 8 * xes << "u * v, xv);\n";
+    s << "          acc[m] += dot8(w, xv);\n        }\n      }\n    }\n";
+  }
   s << "    __syncwarp();\n    if (lane == 0) mb_arrive(sa(&empty_bar[slot]));  // this warp is done with the stage\n";
   s << "#pragma unroll\n    for (int m = 0; m < " << M << "; ++m)\n";
   s << "      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);\n";

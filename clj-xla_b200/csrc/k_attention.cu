@@ -183,18 +183,23 @@ __device__ void merge_if_last(const AttnParams& P, const uint64_t* __restrict__ 
     s_pl[sp][r] = __ldcg(pp + 1);
   }
   __syncthreads();
-  if (threadIdx.x < nqv) {
-    const int r = threadIdx.x;
+  // one warp per row: the splits' maximum, their scale factors and the sum
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = warp; r < nqv; r += nw) {
     float m = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) m = fmaxf(m, s_sc[sp][r]);
+    for (int sp = lane; sp < S; sp += 32) m = fmaxf(m, s_sc[sp][r]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float l = 0.f;
-    for (int sp = 0; sp < S; ++sp) {
+    for (int sp = lane; sp < S; sp += 32) {
       const float pm = s_sc[sp][r];
       const float sc = (m == -INFINITY || pm == -INFINITY) ? 0.f : expf(pm - m);
       s_sc[sp][r] = sc;
       l += sc == 0.f ? 0.f : s_pl[sp][r] * sc;
     }
-    s_l[r] = l;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) s_l[r] = l;
   }
   __syncthreads();
   const int half = HD / 2;
