@@ -794,6 +794,11 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
   s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
   s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
+  {
+    const int64_t max_rows = (N + ctas - 1) / ctas;
+    if (WPR > 1 && M == 1 && max_rows * WPR * 4 <= 16 * 1024)
+      s << "  __shared__ float rowpart[" << max_rows << "][" << WPR << "];\n";
+  }
   s << "  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;\n";
   s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
   s << "  unsigned* status = (unsigned*)" << base_expr(kS) << ";\n";
@@ -847,7 +852,11 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "  for (i64 r = r0; r < r1; ++st) {\n    const int slot = st % " << NST << ";\n";
   s << "    const i64 e = stage_end(r, r1);\n";
   s << "    bool bad = !mb_wait(sa(&full_bar[slot]), (u32)((st / " << NST << ") & 1));\n";
-  if (WPR > 1) s << "    bad = consumers_any(bad);\n";
+  // one row split over WPR warps: with M = 1 the parts of each of the CTA's rows
+  // wait in shared memory and are summed once after the loop (no barrier per stage)
+  const int64_t max_rows = (N + ctas - 1) / ctas;
+  const bool late_sum = WPR > 1 && M == 1 && max_rows * WPR * 4 <= 16 * 1024;
+  if (WPR > 1 && !late_sum) s << "    bad = consumers_any(bad);\n";
   s << "    if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); break; }\n";
   s << "    const i64 row = r + rr;\n    const bool active = row < e;\n";
   s << "    float acc[" << M << "];\n#pragma unroll\n    for (int m = 0; m < " << M << "; ++m) acc[m] = 0.f;\n";
@@ -868,6 +877,25 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "    __syncwarp();\n    if (lane == 0) mb_arrive(sa(&empty_bar[slot]));  // this warp is done with the stage\n";
   s << "#pragma unroll\n    for (int m = 0; m < " << M << "; ++m)\n";
   s << "      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);\n";
+  if (late_sum) {
+    s << "    if (lane == 0 && active) rowpart[row - r0][part] = acc[0];\n    r = e;\n  }\n";
+    s << "  consumers_sync();\n";
+    s << "  for (i64 row = r0 + threadIdx.x; row < r1; row += " << WARPS * 32 << ") {\n";
+    s << "    float t = 0.f;\n    for (int q = 0; q < " << WPR << "; ++q) t += rowpart[row - r0][q];\n";
+    s << seg_chain("row", "    ");
+    for (int i = 0; i < G.nseg; ++i) {
+      const int64_t rows = G.seg_end[i] - (i ? G.seg_end[i - 1] : 0);
+      s << "    if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; "
+        << store_stmt("Y", "row - lo", G.y_dt[i], "U(t)") << " }\n";
+      (void)rows;
+    }
+    s << "  }\n}\n";
+    *src = s.str();
+    *grid = ctas;
+    *block = (WARPS + 1) * 32;
+    *smem = NST * stage_stride + geo.x_bytes;
+    return true;
+  }
   if (WPR > 1) {
     s << "    if (lane == 0) for (int m = 0; m < " << M << "; ++m) red[slot][warp][m] = acc[m];\n";
     s << "    consumers_sync();\n";

@@ -782,15 +782,14 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
   int buf = 0;
-  // the first chunk's K/V rows (all of them: the mask is not known yet), its
-  // mask values and the queries above are all in flight together
-  if (t0 < t1) {
-    stage_copy(t0, 0, 0xfu);
-    stage_mask(t0, 0);
-  }
+  // the first chunk's mask values load together with the queries above; then
+  // only the K/V rows of its active steps (a CTA whose positions are all masked,
+  // as most are in a sliding-window layer, reads no K/V)
+  if (t0 < t1) stage_mask(t0, 0);
   __syncthreads();
   if (t0 < t1) stage_active(0);
   __syncthreads();
+  if (t0 < t1) stage_copy(t0, 0, s_act[0]);
   for (int64_t c0 = t0; c0 < t1; c0 += TC_CH, buf ^= 1) {
     const bool more = c0 + TC_CH < t1;
     if (more) {
