@@ -671,6 +671,164 @@ bool gemv_tma_geometry(const GemvParams& G, GemvGeometry* g) {
   return g->nstage >= 2;
 }
 
+// Batched decode rows (2 <= M <= 8) on the tensor cores: the same bulk-copy
+// ring, 8 weight rows per stage (one 8-column mma tile; each row copied to a
+// 16-byte-padded shared row so ldmatrix is conflict-free), x in shared memory
+// as bf16 (f32 x as an exact hi + mid + lo split), the 8 consumer warps each
+// covering an eighth of K with mma.sync m16n8k16 (rows M..15 of the A tile are
+// zero) and summing their partials through shared memory per stage.
+bool describe_gemv_mma(const GemvParams& G, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
+  constexpr int WARPS = 8;
+  const int64_t M = G.M, K = G.K, N = G.N;
+  if (M < 2 || M > 8 || K % 128 != 0 || (M > 1 && G.x_sm != G.K)) return false;
+  const int XP = G.x_dt == KDT_F32 ? 3 : 1;
+  if (!(G.x_dt == KDT_BF16 || G.x_dt == KDT_F32)) return false;
+  const int64_t rowb = (K + 8) * 2;                   // padded shared row, bytes
+  const int64_t stage_b = 8 * rowb, x_b = XP * 8 * rowb;
+  const int NST = (int)std::min<int64_t>(4, (200 * 1024 - x_b) / stage_b);
+  if (NST < 2) return false;
+  *args = JitArgs{};
+  const int kW = 0, kY = G.nseg, kS = 2 * G.nseg, kX = kS + 1;
+  if (kX + 1 > JIT_MAXBUF) return false;
+  auto put = [&](int k, const DPtr& p) {
+    args->s[k] = p.slot;
+    args->o[k] = p.off;
+  };
+  for (int i = 0; i < G.nseg; ++i) {
+    put(kW + i, G.w[i]);
+    put(kY + i, G.y[i]);
+  }
+  put(kS, G.status);
+  put(kX, G.x);
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + 7) / 8));
+  const int64_t KW = K / WARPS, KS = KW / 16;  // columns and k-steps per warp
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  s << R"G(__device__ __forceinline__ u32 sa(const void* p) { return (u32)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mb_init(u32 a, u32 n) { asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(n)); }
+__device__ __forceinline__ void mb_expect(u32 a, u32 bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(u32 a) { asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory"); }
+__device__ __forceinline__ bool mb_try(u32 a, u32 parity) {
+  u32 ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mb_wait(u32 a, u32 parity) {
+  for (u32 i = 0; i < (1u << 22); ++i)
+    if (mb_try(a, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(u32 dst, const void* src, u32 bytes, u32 bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ u32 lds32(u32 a) { u32 v; asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a)); return v; }
+__device__ __forceinline__ void ldsm_x2(u32 a, u32& r0, u32& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+__device__ __forceinline__ void mma16816(float* c, u32 a0, u32 a2, u32 b0, u32 b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+               : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3]) : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ bool consumers_any(bool p) {
+  u32 r;
+  asm volatile("{\n\t.reg .pred q, o;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred o, 1, 256, q;\n\tselp.u32 %0, 1, 0, o;\n\t}"
+               : "=r"(r) : "r"((u32)p) : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+)G";
+  s << "__device__ __forceinline__ i64 stage_end(i64 r, i64 r1) {\n  i64 e = r + 8LL;\n  if (e > r1) e = r1;\n";
+  for (int i = 0; i + 1 < G.nseg; ++i)
+    s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
+  s << "  return e;\n}\n";
+  auto seg_chain = [&](const std::string& row, const std::string& ind) {
+    std::ostringstream c;
+    c << ind << "int sg = 0; i64 lo = 0;\n";
+    for (int i = 0; i + 1 < G.nseg; ++i)
+      c << ind << "if (" << row << " >= " << G.seg_end[i] << "LL) { sg = " << i + 1 << "; lo = " << G.seg_end[i] << "LL; }\n";
+    return c.str();
+  };
+  s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
+    << ", 1) cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
+  s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
+  s << "  __shared__ float red[" << NST << "][8][8][8];\n";
+  s << "  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;\n";
+  s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  s << "  unsigned* status = (unsigned*)" << base_expr(kS) << ";\n";
+  s << "  const u32 stage0 = sa(dsm), xs0 = stage0 + " << (int64_t)NST * stage_b << "u;\n";
+  s << "  if (threadIdx.x == 0) {\n    for (int i = 0; i < " << NST << "; ++i) { mb_init(sa(&full_bar[i]), 1u); mb_init(sa(&empty_bar[i]), "
+    << WARPS << "u); }\n";
+  s << "    asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n  }\n  __syncthreads();\n";
+  // producer: each weight row of a stage to its padded shared row, one mbarrier per stage
+  s << "  if (warp == " << WARPS << ") {\n    if (lane != 0) return;\n    int st = 0;\n    bool ok = true;\n";
+  s << "    for (i64 r = r0; r < r1; ++st) {\n      const int slot = st % " << NST << ";\n";
+  s << "      if (st >= " << NST << " && !mb_wait(sa(&empty_bar[slot]), (u32)((st / " << NST << " - 1) & 1))) { ok = false; break; }\n";
+  s << "      const i64 e = stage_end(r, r1);\n";
+  s << seg_chain("r", "      ");
+  s << "      const unsigned char* W = (const unsigned char*)";
+  for (int i = 0; i + 1 < G.nseg; ++i) s << "(sg == " << i << " ? " << base_expr(kW + i) << " : ";
+  s << base_expr(kW + G.nseg - 1);
+  for (int i = 0; i + 1 < G.nseg; ++i) s << ")";
+  s << ";\n";
+  s << "      mb_expect(sa(&full_bar[slot]), (u32)((e - r) * " << K * 2 << "LL));\n";
+  s << "      for (i64 q = r; q < e; ++q)\n        bulk_g2s(stage0 + (u32)slot * " << stage_b << "u + (u32)(q - r) * " << rowb
+    << "u, W + (q - lo) * " << K * 2 << "LL, " << K * 2 << "u, sa(&full_bar[slot]));\n";
+  s << "      r = e;\n    }\n    if (!ok) atomicOr(status, 4u);\n";
+  s << "    for (int k = st - 1; k >= 0 && k >= st - " << NST << "; --k)\n";
+  s << "      if (!mb_wait(sa(&full_bar[k % " << NST << "]), (u32)((k / " << NST << ") & 1))) atomicOr(status, 8u);\n";
+  s << "    return;\n  }\n";
+  // consumers: x as bf16 parts in padded rows (rows >= M zero)
+  s << "  pdl_enter();\n  {\n    const char* X = " << base_expr(kX) << ";\n";
+  s << "    for (int e = threadIdx.x; e < " << 8 * K << "; e += 256) {\n";
+  s << "      const int m = e / " << K << ", k = e % " << K << ";\n";
+  s << "      unsigned short p[3] = {0, 0, 0};\n";
+  if (XP == 1) {
+    s << "      if (m < " << M << ") p[0] = ((const unsigned short*)X)[(i64)m * " << K << " + k];\n";
+  } else {
+    s << "      if (m < " << M << ") {\n        const float q = ((const float*)X)[(i64)m * " << K << " + k];\n";
+    s << "        p[0] = f2bf(q);\n        const float r1 = q - __uint_as_float((u32)p[0] << 16);\n";
+    s << "        p[1] = f2bf(r1);\n        p[2] = f2bf(r1 - __uint_as_float((u32)p[1] << 16));\n      }\n";
+  }
+  s << "      for (int part = 0; part < " << XP << "; ++part)\n";
+  s << "        *(unsigned short*)(dsm + " << (int64_t)NST * stage_b << " + part * " << 8 * rowb << " + m * " << rowb
+    << " + k * 2) = p[part];\n    }\n  }\n  consumers_sync();\n";
+  s << "  const u32 xa = xs0 + (u32)(g * " << rowb << " + (warp * " << KW << " + 2 * t) * 2);\n";
+  s << "  const u32 wrow = (u32)((lane & 7) * " << rowb << " + (warp * " << KW << " + 8 * ((lane >> 3) & 1)) * 2);\n";
+  s << "  int st = 0;\n  for (i64 r = r0; r < r1; ++st) {\n    const int slot = st % " << NST << ";\n";
+  s << "    const i64 e = stage_end(r, r1);\n";
+  s << "    bool bad = !mb_wait(sa(&full_bar[slot]), (u32)((st / " << NST << ") & 1));\n";
+  s << "    bad = consumers_any(bad);\n    if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); break; }\n";
+  s << "    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};\n";
+  s << "    const u32 wb = stage0 + (u32)slot * " << stage_b << "u + wrow;\n";
+  s << "#pragma unroll 4\n    for (int kk = 0; kk < " << KS << "; ++kk) {\n      u32 b0, b1;\n      ldsm_x2(wb + 32u * kk, b0, b1);\n";
+  for (int part = 0; part < XP; ++part)
+    s << "      mma16816(acc[kk & 1], lds32(xa + " << part * 8 * rowb << "u + 32u * kk), lds32(xa + " << part * 8 * rowb
+      << "u + 32u * kk + 16u), b0, b1);\n";
+  s << "    }\n    __syncwarp();\n    if (lane == 0) mb_arrive(sa(&empty_bar[slot]));\n";
+  s << "    if (g < " << M << ") {\n      red[slot][warp][g][2 * t] = acc[0][0] + acc[1][0];\n"
+       "      red[slot][warp][g][2 * t + 1] = acc[0][1] + acc[1][1];\n    }\n    consumers_sync();\n";
+  s << "    if (threadIdx.x < " << M * 8 << ") {\n      const int m = threadIdx.x >> 3, n = threadIdx.x & 7;\n";
+  s << "      const i64 row = r + n;\n      if (row < e) {\n        float v = 0.f;\n";
+  s << "        for (int w = 0; w < " << WARPS << "; ++w) v += red[slot][w][m][n];\n";
+  s << seg_chain("row", "        ");
+  for (int i = 0; i < G.nseg; ++i) {
+    const int64_t rows = G.seg_end[i] - (i ? G.seg_end[i - 1] : 0);
+    s << "        if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; "
+      << store_stmt("Y", "(i64)m * " + std::to_string(rows) + "LL + (row - lo)", G.y_dt[i], "U(v)") << " }\n";
+  }
+  s << "      }\n    }\n    r = e;\n  }\n}\n";
+  *src = s.str();
+  *grid = ctas;
+  *block = (WARPS + 1) * 32;
+  *smem = (int)((int64_t)NST * stage_b + x_b);
+  return true;
+}
+
 bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
   const bool fused = l.kind == K_GEMV_FUSED;
   if (!(l.kind == K_GEMV || (fused && l.parts.size() == 1))) return false;
@@ -681,6 +839,7 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
     return e && e[0] == '0';
   }();
   if (off) return false;
+  if (G.M >= 2 && !fused && describe_gemv_mma(G, src, grid, block, smem, args)) return true;
   GemvGeometry geo;
   if (!gemv_tma_geometry(G, &geo)) return false;
   if (G.M > 1 && G.x_sm != G.K) return false;

@@ -5,7 +5,7 @@ f32 summation-order error; bf16 results may differ from the correctly rounded
 value by at most one bf16 ulp (an f32 sum in another order can fall on the
 other side of a rounding boundary), and only rarely.  Covers the shapes of the
 Gemma decode projections, several projections of one input grouped into one
-launch, f32 x, and batched rows (M > 1)."""
+launch, f32 x, and batched rows (M > 1, on the tensor cores where K allows)."""
 import numpy as np
 import pytest
 
@@ -55,8 +55,12 @@ def _check(got, want64, dt):
     (1, 2048, (2560,), "f32", "bf16"),               # o projection of the f32 attention output
     (1, 2560, (4096,), "bf16", "f32"),               # f32 result (logits)
     (1, 256, (256, 128, 128), "bf16", "bf16"),       # small test-model shapes
-    (4, 3840, (512, 256), "bf16", "bf16"),           # batched decode rows
-    (8, 1024, (768,), "f32", "f32"),
+    (4, 3840, (512, 256), "bf16", "bf16"),           # batched decode rows (tensor cores)
+    (8, 1024, (768,), "f32", "f32"),                 # f32 x as three bf16 parts
+    (2, 2560, (2048, 1024, 1024), "bf16", "bf16"),
+    (8, 3840, (7680, 7680), "bf16", "bf16"),         # Gemma-3-12B gate / up at TP2, batch 8
+    (8, 2048, (3840,), "f32", "bf16"),               # its o projection
+    (8, 7680, (3840,), "bf16", "bf16"),              # its down projection (CUDA-core path)
 ])
 def test_decode_gemv_exact(ctx, M, K, Ns, x_dt, out_dt):
     def f(x, *ws):
