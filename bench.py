@@ -13,6 +13,9 @@ host).  Prefill tokens/s of the same model is reported in ``prefill``.
 With ``--gpus N`` (torchrun, one process per GPU) every rank runs an
 independent replica of the workload (data parallel, no collective on the data
 path; ``scaling: weak``); value = all ranks' tokens / max time over ranks.
+With ``--tp N`` (torchrun with N ranks) the ranks instead hold the N shards of
+one model (Gemma: heads and MLP split, an NCCL all-reduce after the attention
+and MLP blocks; ``scaling: strong``), e.g. ``--config gemma3-12b --tp 4``.
 
 ``--impl reference`` times the CPU restatement of the reference's execution
 path (oracle/interp.py running the same printed graph on the host cores).
@@ -243,6 +246,18 @@ def run_ours(args, rank, world, local_rank):
                 api.destroy_buffer(b)
         kv = outs[1:]
     prefill_s = float(np.median(pre_times))
+    # one profiled prefill (per-kernel events): where the prefill time goes
+    pre_by_kind = {}
+    if not args.decode_only:
+        kvp = zero_kv()
+        core.profile_enable(ctx, True)
+        outs = api.execute_executable(ex_pre["handle"], [x_pre, p_pre] + wbufs + kvp, len(g_pre["outvars"]))
+        torch.cuda.synchronize()
+        for e in core.profile_dump(ctx):
+            pre_by_kind[e["kind"]] = round(pre_by_kind.get(e["kind"], 0.0) + e["ms"], 3)
+        core.profile_enable(ctx, False)
+        for b in kvp + outs:
+            api.destroy_buffer(b)
 
     # ---------------- decode, device-resident inputs
     n_total = args.warmup + args.steps
@@ -332,6 +347,7 @@ def run_ours(args, rank, world, local_rank):
     tokens = B * args.steps
     res = {
         "rank": rank, "dec_s": dec_s, "tokens": tokens, "prefill_s": prefill_s, "e2e_s": e2e_s,
+        "pre_by_kind": pre_by_kind,
         "e2e_tokens": B * e2e_steps, "launches": launches, "clocks": clk.summary(),
         "by_kind": by_kind, "total_ms": total_ms, "dom": dom[0], "achieved": achieved,
         "hbm_peak": hbm_peak, "peak_src": peak_src, "cpu": cpu, "t_weights": t_w, "t_compile": t_c,
@@ -415,7 +431,8 @@ def main():
                                        + " (NCCL all-reduce after attention and MLP)"),
                        "l2": "weights stream >> 126 MB L2 every step (no flush needed)"},
             "prefill": {"value": round(replicas * B * S / pre_s, 1), "unit": "tokens/s",
-                        "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill"},
+                        "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill",
+                        "kernel_time_by_kind_ms": res["pre_by_kind"]},
             "e2e": {"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": res["logits_bytes"],
                     "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"},

@@ -671,40 +671,9 @@ bool gemv_tma_geometry(const GemvParams& G, GemvGeometry* g) {
   return g->nstage >= 2;
 }
 
-// Batched decode rows (2 <= M <= 8) on the tensor cores: the same bulk-copy
-// ring, 8 weight rows per stage (one 8-column mma tile; each row copied to a
-// 16-byte-padded shared row so ldmatrix is conflict-free), x in shared memory
-// as bf16 (f32 x as an exact hi + mid + lo split), the 8 consumer warps each
-// covering an eighth of K with mma.sync m16n8k16 (rows M..15 of the A tile are
-// zero) and summing their partials through shared memory per stage.
-bool describe_gemv_mma(const GemvParams& G, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
-  constexpr int WARPS = 8;
-  const int64_t M = G.M, K = G.K, N = G.N;
-  if (M < 2 || M > 8 || K % 128 != 0 || (M > 1 && G.x_sm != G.K)) return false;
-  const int XP = G.x_dt == KDT_F32 ? 3 : 1;
-  if (!(G.x_dt == KDT_BF16 || G.x_dt == KDT_F32)) return false;
-  const int64_t rowb = (K + 8) * 2;                   // padded shared row, bytes
-  const int64_t stage_b = 8 * rowb, x_b = XP * 8 * rowb;
-  const int NST = (int)std::min<int64_t>(4, (200 * 1024 - x_b) / stage_b);
-  if (NST < 2) return false;
-  *args = JitArgs{};
-  const int kW = 0, kY = G.nseg, kS = 2 * G.nseg, kX = kS + 1;
-  if (kX + 1 > JIT_MAXBUF) return false;
-  auto put = [&](int k, const DPtr& p) {
-    args->s[k] = p.slot;
-    args->o[k] = p.off;
-  };
-  for (int i = 0; i < G.nseg; ++i) {
-    put(kW + i, G.w[i]);
-    put(kY + i, G.y[i]);
-  }
-  put(kS, G.status);
-  put(kX, G.x);
-  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + 7) / 8));
-  const int64_t KW = K / WARPS, KS = KW / 16;  // columns and k-steps per warp
-  std::ostringstream s;
-  s << kPrelude << args_struct();
-  s << R"G(__device__ __forceinline__ u32 sa(const void* p) { return (u32)__cvta_generic_to_shared(p); }
+// device helpers of the batched (tensor-core) GEMV kernels
+std::string gemv_mma_helpers() {
+  return std::string(R"G(__device__ __forceinline__ u32 sa(const void* p) { return (u32)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mb_init(u32 a, u32 n) { asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(n)); }
 __device__ __forceinline__ void mb_expect(u32 a, u32 bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes) : "memory");
@@ -740,7 +709,51 @@ __device__ __forceinline__ bool consumers_any(bool p) {
   return r != 0;
 }
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-)G";
+__device__ __forceinline__ float2 lds64f(u32 a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ u32 pack2(float lo, float hi) { u32 r; asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo)); return r; }
+__device__ __forceinline__ float lo_bf(u32 v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float hi_bf(u32 v) { return __uint_as_float(v & 0xffff0000u); }
+)G");
+}
+
+// Batched decode rows (2 <= M <= 8) on the tensor cores: the same bulk-copy
+// ring, 8 weight rows per stage (one 8-column mma tile; each row copied to a
+// 16-byte-padded shared row so ldmatrix is conflict-free), x in shared memory
+// as bf16 (f32 x as an exact hi + mid + lo split), the 8 consumer warps each
+// covering an eighth of K with mma.sync m16n8k16 (rows M..15 of the A tile are
+// zero) and summing their partials through shared memory per stage.
+bool describe_gemv_mma(const GemvParams& G, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
+  constexpr int WARPS = 8;
+  const int64_t M = G.M, K = G.K, N = G.N;
+  if (M < 2 || M > 8 || K % 128 != 0 || (M > 1 && G.x_sm != G.K)) return false;
+  const int XP = G.x_dt == KDT_F32 ? 3 : 1;
+  if (!(G.x_dt == KDT_BF16 || G.x_dt == KDT_F32)) return false;
+  const int64_t rowb = (K + 8) * 2;                   // padded shared row, bytes
+  const int64_t stage_b = 8 * rowb, x_b = XP * 8 * rowb;
+  const int NST = (int)std::min<int64_t>(4, (200 * 1024 - x_b) / stage_b);
+  if (NST < 2) return false;
+  *args = JitArgs{};
+  const int kW = 0, kY = G.nseg, kS = 2 * G.nseg, kX = kS + 1;
+  if (kX + 1 > JIT_MAXBUF) return false;
+  auto put = [&](int k, const DPtr& p) {
+    args->s[k] = p.slot;
+    args->o[k] = p.off;
+  };
+  for (int i = 0; i < G.nseg; ++i) {
+    put(kW + i, G.w[i]);
+    put(kY + i, G.y[i]);
+  }
+  put(kS, G.status);
+  put(kX, G.x);
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + 7) / 8));
+  const int64_t KW = K / WARPS, KS = KW / 16;  // columns and k-steps per warp
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  s << gemv_mma_helpers();
   s << "__device__ __forceinline__ i64 stage_end(i64 r, i64 r1) {\n  i64 e = r + 8LL;\n  if (e > r1) e = r1;\n";
   for (int i = 0; i + 1 < G.nseg; ++i)
     s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
@@ -829,6 +842,165 @@ __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 256
   return true;
 }
 
+// Batched rows when x does not fit in shared memory whole (large K, or f32 x):
+// each stage holds 8 weight rows x KC columns and the matching KC columns of
+// the M rows of x (raw element type; f32 x is split into three bf16 parts when
+// the fragments are built), so a tile of 8 rows takes K / KC stages whose
+// partial products accumulate in the warps' registers.  The producer issues
+// the weight copies of the first stages before the dependency wait and the x
+// copies (x comes from the previous kernel) after it.
+bool describe_gemv_mma_chunked(const GemvParams& G, std::string* src, int64_t* grid, int* block, int* smem,
+                               JitArgs* args) {
+  constexpr int WARPS = 8;
+  const int64_t M = G.M, K = G.K, N = G.N;
+  if (M < 2 || M > 8 || K % 128 != 0 || G.x_sm != G.K) return false;
+  if (!(G.x_dt == KDT_BF16 || G.x_dt == KDT_F32)) return false;
+  const int xes = G.x_dt == KDT_F32 ? 4 : 2;
+  int64_t KC = 0;
+  for (int64_t c = 128; c <= 2048 && c <= K; c += 128)
+    if (K % c == 0) KC = c;
+  if (KC == 0) return false;
+  const int64_t NKC = K / KC;
+  const int64_t wrowb = (KC + 8) * 2, xrowb = KC * xes + 16;
+  const int64_t stage_b = ((8 * wrowb + M * xrowb) + 127) / 128 * 128;
+  const int NST = (int)std::min<int64_t>(4, (200 * 1024) / stage_b);
+  if (NST < 2) return false;
+  *args = JitArgs{};
+  const int kW = 0, kY = G.nseg, kS = 2 * G.nseg, kX = kS + 1;
+  if (kX + 1 > JIT_MAXBUF) return false;
+  auto put = [&](int k, const DPtr& p) {
+    args->s[k] = p.slot;
+    args->o[k] = p.off;
+  };
+  for (int i = 0; i < G.nseg; ++i) {
+    put(kW + i, G.w[i]);
+    put(kY + i, G.y[i]);
+  }
+  put(kS, G.status);
+  put(kX, G.x);
+  const int64_t ctas = std::max<int64_t>(1, std::min<int64_t>(sm_count(), (N + 7) / 8));
+  const int64_t KW = KC / WARPS, KS = KW / 16;
+  const int XP = xes == 4 ? 3 : 1;
+  std::ostringstream s;
+  s << kPrelude << args_struct();
+  s << gemv_mma_helpers();
+  s << "__device__ __forceinline__ void mb_expect_only(u32 a, u32 bytes) {\n"
+       "  asm volatile(\"mbarrier.expect_tx.shared::cta.b64 [%0], %1;\" ::\"r\"(a), \"r\"(bytes) : \"memory\");\n}\n";
+  s << "__device__ __forceinline__ i64 tile_end(i64 r, i64 r1) {\n  i64 e = r + 8LL;\n  if (e > r1) e = r1;\n";
+  for (int i = 0; i + 1 < G.nseg; ++i)
+    s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
+  s << "  return e;\n}\n";
+  auto seg_chain = [&](const std::string& row, const std::string& ind) {
+    std::ostringstream c;
+    c << ind << "int sg = 0; i64 lo = 0;\n";
+    for (int i = 0; i + 1 < G.nseg; ++i)
+      c << ind << "if (" << row << " >= " << G.seg_end[i] << "LL) { sg = " << i + 1 << "; lo = " << G.seg_end[i] << "LL; }\n";
+    return c.str();
+  };
+  s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
+    << ", 1) cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
+  s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
+  s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
+  s << "  __shared__ float red[8][8][8];\n";
+  s << "  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;\n";
+  s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  s << "  unsigned* status = (unsigned*)" << base_expr(kS) << ";\n";
+  s << "  const u32 stage0 = sa(dsm);\n";
+  s << "  if (threadIdx.x == 0) {\n    for (int i = 0; i < " << NST << "; ++i) { mb_init(sa(&full_bar[i]), 1u); mb_init(sa(&empty_bar[i]), "
+    << WARPS << "u); }\n";
+  s << "    asm volatile(\"fence.mbarrier_init.release.cluster;\" ::: \"memory\");\n  }\n  __syncthreads();\n";
+  // producer
+  s << "  if (warp == " << WARPS << ") {\n    if (lane != 0) return;\n";
+  s << "    const char* X = " << base_expr(kX) << ";\n";
+  auto wcopies = [&](const std::string& ind) {
+    std::ostringstream c;
+    c << seg_chain("r", ind);
+    c << ind << "const unsigned char* W = (const unsigned char*)";
+    for (int i = 0; i + 1 < G.nseg; ++i) c << "(sg == " << i << " ? " << base_expr(kW + i) << " : ";
+    c << base_expr(kW + G.nseg - 1);
+    for (int i = 0; i + 1 < G.nseg; ++i) c << ")";
+    c << ";\n";
+    c << ind << "for (i64 q = r; q < e; ++q)\n" << ind << "  bulk_g2s(stage0 + (u32)slot * " << stage_b << "u + (u32)(q - r) * "
+      << wrowb << "u, W + (q - lo) * " << K * 2 << "LL + (i64)kc * " << KC * 2 << "LL, " << KC * 2
+      << "u, sa(&full_bar[slot]));\n";
+    return c.str();
+  };
+  auto xcopies = [&](const std::string& ind) {
+    std::ostringstream c;
+    c << ind << "for (int m = 0; m < " << M << "; ++m)\n" << ind << "  bulk_g2s(stage0 + (u32)slot * " << stage_b << "u + "
+      << 8 * wrowb << "u + (u32)m * " << xrowb << "u, X + ((i64)m * " << K << " + (i64)kc * " << KC << ") * " << xes
+      << ", " << KC * xes << "u, sa(&full_bar[slot]));\n";
+    return c.str();
+  };
+  // weights of the first stages before the dependency wait
+  s << "    {\n      int st = 0;\n      for (i64 r = r0; r < r1 && st < " << NST << ";) {\n";
+  s << "        const i64 e = tile_end(r, r1);\n";
+  s << "        for (int kc = 0; kc < " << NKC << " && st < " << NST << "; ++kc, ++st) {\n";
+  s << "          const int slot = st;\n";
+  s << "          mb_expect_only(sa(&full_bar[slot]), (u32)((e - r) * " << KC * 2 << "LL));\n";
+  s << wcopies("          ");
+  s << "        }\n        r = e;\n      }\n    }\n";
+  s << "    asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+  s << "    int st = 0;\n    bool ok = true;\n";
+  s << "    for (i64 r = r0; r < r1 && ok;) {\n      const i64 e = tile_end(r, r1);\n";
+  s << "      for (int kc = 0; kc < " << NKC << "; ++kc, ++st) {\n        const int slot = st % " << NST << ";\n";
+  s << "        if (st >= " << NST << ") {\n";
+  s << "          if (!mb_wait(sa(&empty_bar[slot]), (u32)((st / " << NST << " - 1) & 1))) { ok = false; break; }\n";
+  s << "          mb_expect(sa(&full_bar[slot]), (u32)((e - r) * " << KC * 2 << "LL + " << M * KC * xes << "LL));\n";
+  s << wcopies("          ");
+  s << "        } else {\n          mb_expect(sa(&full_bar[slot]), " << M * KC * xes << "u);\n        }\n";
+  s << xcopies("        ");
+  s << "      }\n      r = e;\n    }\n    if (!ok) atomicOr(status, 4u);\n";
+  s << "    for (int k = st - 1; k >= 0 && k >= st - " << NST << "; --k)\n";
+  s << "      if (!mb_wait(sa(&full_bar[k % " << NST << "]), (u32)((k / " << NST << ") & 1))) atomicOr(status, 8u);\n";
+  s << "    return;\n  }\n";
+  // consumers
+  s << "  pdl_enter();\n";
+  s << "  const u32 wofs = (u32)((lane & 7) * " << wrowb << " + (warp * " << KW << " + 8 * ((lane >> 3) & 1)) * 2);\n";
+  s << "  const u32 xofs = " << 8 * wrowb << "u + (u32)(g * " << xrowb << " + (warp * " << KW << " + 2 * t) * " << xes << ");\n";
+  s << "  int st = 0;\n  bool bad = false;\n";
+  s << "  for (i64 r = r0; r < r1 && !bad;) {\n    const i64 e = tile_end(r, r1);\n";
+  s << "    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};\n";
+  s << "    for (int kc = 0; kc < " << NKC << "; ++kc, ++st) {\n      const int slot = st % " << NST << ";\n";
+  s << "      bad = consumers_any(!mb_wait(sa(&full_bar[slot]), (u32)((st / " << NST << ") & 1)));\n";
+  s << "      if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); break; }\n";
+  s << "      const u32 sb = stage0 + (u32)slot * " << stage_b << "u;\n";
+  s << "#pragma unroll 4\n      for (int kk = 0; kk < " << KS << "; ++kk) {\n        u32 b0, b1;\n";
+  s << "        ldsm_x2(sb + wofs + 32u * kk, b0, b1);\n";
+  if (XP == 1) {
+    s << "        const u32 a0 = g < " << M << " ? lds32(sb + xofs + 32u * kk) : 0u;\n";
+    s << "        const u32 a2 = g < " << M << " ? lds32(sb + xofs + 32u * kk + 16u) : 0u;\n";
+    s << "        mma16816(acc[kk & 1], a0, a2, b0, b1);\n";
+  } else {
+    s << "        float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;\n";
+    s << "        if (g < " << M << ") {\n          const float2 u = lds64f(sb + xofs + 64u * kk), v = lds64f(sb + xofs + 64u * kk + 32u);\n";
+    s << "          q0 = u.x; q1 = u.y; q2 = v.x; q3 = v.y;\n        }\n";
+    s << "        for (int part = 0; part < 3; ++part) {\n";
+    s << "          const u32 a0 = pack2(q0, q1), a2 = pack2(q2, q3);\n";
+    s << "          mma16816(acc[kk & 1], a0, a2, b0, b1);\n";
+    s << "          q0 -= lo_bf(a0); q1 -= hi_bf(a0); q2 -= lo_bf(a2); q3 -= hi_bf(a2);\n        }\n";
+  }
+  s << "      }\n      __syncwarp();\n      if (lane == 0) mb_arrive(sa(&empty_bar[slot]));\n    }\n";
+  s << "    if (bad) break;\n";
+  s << "    if (g < " << M << ") {\n      red[warp][g][2 * t] = acc[0][0] + acc[1][0];\n"
+       "      red[warp][g][2 * t + 1] = acc[0][1] + acc[1][1];\n    }\n    consumers_sync();\n";
+  s << "    if (threadIdx.x < " << M * 8 << ") {\n      const int m = threadIdx.x >> 3, n = threadIdx.x & 7;\n";
+  s << "      const i64 row = r + n;\n      if (row < e) {\n        float v = 0.f;\n";
+  s << "        for (int w = 0; w < " << WARPS << "; ++w) v += red[w][m][n];\n";
+  s << seg_chain("row", "        ");
+  for (int i = 0; i < G.nseg; ++i) {
+    const int64_t rows = G.seg_end[i] - (i ? G.seg_end[i - 1] : 0);
+    s << "        if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; "
+      << store_stmt("Y", "(i64)m * " + std::to_string(rows) + "LL + (row - lo)", G.y_dt[i], "U(v)") << " }\n";
+  }
+  s << "      }\n    }\n    r = e;\n  }\n}\n";
+  *src = s.str();
+  *grid = ctas;
+  *block = (WARPS + 1) * 32;
+  *smem = (int)((int64_t)NST * stage_b);
+  return true;
+}
+
 bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
   const bool fused = l.kind == K_GEMV_FUSED;
   if (!(l.kind == K_GEMV || (fused && l.parts.size() == 1))) return false;
@@ -839,7 +1011,9 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
     return e && e[0] == '0';
   }();
   if (off) return false;
-  if (G.M >= 2 && !fused && describe_gemv_mma(G, src, grid, block, smem, args)) return true;
+  if (G.M >= 2 && !fused &&
+      (describe_gemv_mma(G, src, grid, block, smem, args) || describe_gemv_mma_chunked(G, src, grid, block, smem, args)))
+    return true;
   GemvGeometry geo;
   if (!gemv_tma_geometry(G, &geo)) return false;
   if (G.M > 1 && G.x_sm != G.K) return false;

@@ -42,7 +42,12 @@ def _check(got, want64, dt):
     ulp = np.spacing(np.abs(interp.bf16_bits_to_f32(interp.f32_to_bf16_bits(want64.astype(np.float32)))).astype(
         np.float32)).astype(np.float64) * 65536.0
     off = np.abs(g - want64)
-    assert (off <= ulp * 1.0 + 1e-30).all(), f"max {float((off / ulp).max()):.2f} bf16 ulps"
+    # plus f32 summation noise where a sum cancels to a value far below the
+    # typical one (about 2^-17 of the RMS: an order above a K-term f32 sum's error)
+    tol = ulp + 2.0 ** -17 * float(np.sqrt(np.mean(want64 ** 2)))
+    worst = np.unravel_index(int(np.argmax(off / tol)), off.shape)
+    assert (off <= tol).all(), (f"{float((off / tol).max()):.2f} x tolerance at {worst}: "
+                                f"got {float(g[worst])!r} exact {float(want64[worst])!r}")
     # a flipped rounding needs the exact value within a few f32 ulps of a boundary: rare
     exact = interp.f32_to_bf16_bits(want64.astype(np.float32))
     assert np.mean(got != exact) < 0.01
@@ -60,7 +65,10 @@ def _check(got, want64, dt):
     (2, 2560, (2048, 1024, 1024), "bf16", "bf16"),
     (8, 3840, (7680, 7680), "bf16", "bf16"),         # Gemma-3-12B gate / up at TP2, batch 8
     (8, 2048, (3840,), "f32", "bf16"),               # its o projection
-    (8, 7680, (3840,), "bf16", "bf16"),              # its down projection (CUDA-core path)
+    (8, 7680, (3840,), "bf16", "bf16"),              # its down projection (K in chunks of the stage)
+    (8, 15360, (3840,), "bf16", "bf16"),             # Gemma-3-12B down at TP1
+    (8, 4096, (3840,), "f32", "bf16"),               # f32 x that does not fit shared memory whole
+    (3, 5376, (1024,), "bf16", "f32"),
 ])
 def test_decode_gemv_exact(ctx, M, K, Ns, x_dt, out_dt):
     def f(x, *ws):
