@@ -53,10 +53,17 @@ struct TcGemmParams {
   int64_t a_ld, b_ld;  // row strides in elements
   int32_t M, N, K, c_dt;
   int32_t tmap_a_index, tmap_b_index;
+  // a_parts 3: A is an f32 matrix split exactly into three bf16 planes
+  // (hi, mid, lo; plane p holds rows p * a_plane_rows ..), each multiplied by
+  // the same B tile into one accumulator; a_parts 1: A is bf16
+  int32_t a_parts, a_plane_rows;
 };
 
 void launch_tc_gemm(const TcGemmParams& p, const uint64_t* argtab, cudaStream_t s);
 bool make_tc_gemm(const GemmParams& g, TcGemmParams& out);
+// f32 x bf16 product through three bf16 planes of the f32 operand (the caller
+// supplies the planes as A; g.a_dt names the original f32 operand)
+bool make_tc_gemm_split(const GemmParams& g, TcGemmParams& out);
 void verify_tc_gemm(const TcGemmParams& p, const RegionFn& region);
 void tc_gemm_tile_shape(int* bm, int* bn, int* bk);
 // Encodes a 2-D bf16 tensor map (128-byte swizzle) into out128.
@@ -86,7 +93,7 @@ struct AttnParams {
   // itself and resets its counter (use_counters 0: a separate combine launch)
   DPtr counters;
   int32_t use_counters;
-  int32_t use_tc;  // decode on the tensor cores (attn_tc_kernel): 64-position splits
+  int32_t use_tc;  // 1: decode on the tensor cores (64-position splits); 2: prefill on the tensor cores
   int32_t B, nq, nkv, Sq, T, hd, group, splits, qtile;
   int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
   int32_t nchain, chain_out;
@@ -103,6 +110,8 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
 // whether the tensor-core decode kernel can run these views (bf16 q / K / V,
 // 16-byte aligned rows, head_dim 64 / 128 / 256, one query tile of <= 8 vectors)
 bool attention_tc_ok(const AttnParams& p);
+// the tensor-core prefill kernel (64 query vectors per CTA, no position splits)
+bool attention_tc_prefill_ok(const AttnParams& p);
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
 void verify_attention(const Launch& l, const RegionFn& region);
 

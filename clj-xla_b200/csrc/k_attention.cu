@@ -934,6 +934,265 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   merge_if_last(P, argtab, b, kh, 0, nqv);
 }
 
+// ---------------------------------------------------------------------------
+// Prefill attention on the tensor cores (FA2-style, mma.sync m16n8k16 bf16 ->
+// f32).  One CTA per (batch * kv head, 64 query vectors): query vector
+// r = qi * group + gi of the tile's query positions, so the GQA group shares
+// every staged K/V row.  8 warps: warp w owns rows 16 (w & 3) .. + 15 and
+// half (w >> 2) of head_dim; the two warps of a row group compute the same
+// scores (S = Q K^T over a 64-position chunk), so their online-softmax state
+// agrees without exchange.  Chunks whose mask is at or below mask_skip for
+// every row are skipped (the causal upper triangle); K/V chunks are staged
+// with cp.async, double-buffered.  The printed score chain, mask, exp and
+// roundings are replayed per element; P enters P V as bf16 hi + lo, f32
+// queries as an exact hi + mid + lo split.
+constexpr int PF_CH = 64;   // positions per staged chunk
+constexpr int PF_ROWS = 64; // query vectors per CTA
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_constant__ AttnParams P,
+                                                                 const uint64_t* __restrict__ argtab) {
+  constexpr int ROW = HD + 8;           // padded bf16 row of K / V / bf16 Q
+  constexpr int QROWF = HD + 4;         // padded f32 row of an f32 Q
+  constexpr int KSTEPS = HD / 16;
+  constexpr int NTO = HD / 16;          // 8-dim output tiles per warp (half of head_dim)
+  extern __shared__ __align__(16) unsigned char pf_smem[];
+  uint16_t* Kb = (uint16_t*)pf_smem;                    // [2][PF_CH][ROW]
+  uint16_t* Vb = Kb + 2 * PF_CH * ROW;                  // [2][PF_CH][ROW]
+  unsigned char* Qs = (unsigned char*)(Vb + 2 * PF_CH * ROW);  // bf16 [64][ROW] or f32 [64][QROWF]
+  __shared__ int64_t qoff_s[PF_ROWS], moff_s[PF_ROWS];
+  pdl_enter();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int rg = warp & 3, dh = warp >> 2;
+  const int bk = blockIdx.z, b = bk / P.nkv, kh = bk % P.nkv;
+  const int QT = PF_ROWS / P.group;  // query positions per CTA
+  const int i0 = blockIdx.y * QT;
+  const int nrows = min(QT, P.Sq - i0) * P.group;
+  const bool qf32 = P.q.dt == KDT_F32;
+  const char* qb = dres(P.q.p, argtab);
+  const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
+  const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
+  const char* mb = dres(P.mask.p, argtab);
+  if (threadIdx.x < PF_ROWS) {
+    const int r = threadIdx.x < nrows ? threadIdx.x : 0;
+    const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    qoff_s[threadIdx.x] = b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2];
+    moff_s[threadIdx.x] = b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2];
+  }
+  __syncthreads();
+  // Q -> shared (rows >= nrows zero)
+  for (int e = threadIdx.x; e < PF_ROWS * HD; e += 256) {
+    const int r = e / HD, c = e % HD;
+    if (qf32) {
+      float v = 0.f;
+      if (r < nrows) v = ((const float*)qb)[qoff_s[r] + c * P.q.stride[3]];
+      ((float*)Qs)[r * QROWF + c] = v;
+    } else {
+      uint16_t v = 0;
+      if (r < nrows) v = ((const uint16_t*)qb)[qoff_s[r] + c * P.q.stride[3]];
+      ((uint16_t*)Qs)[r * ROW + c] = v;
+    }
+  }
+  const int64_t ms3 = P.mask.stride[3];
+  // does chunk c0 hold any position above mask_skip for any row? (all threads)
+  auto chunk_live = [&](int64_t c0) {
+    bool any = false;
+    for (int e = threadIdx.x; e < nrows * PF_CH; e += 256) {
+      const int r = e / PF_CH, j = e % PF_CH;
+      if (c0 + j < P.T && ld_any(mb, moff_s[r] + (c0 + j) * ms3, P.mask.dt) > P.mask_skip) any = true;
+    }
+    return __syncthreads_or(any) != 0;
+  };
+  auto stage = [&](int64_t c0, int buf) {
+    constexpr int SEGS = HD / 8;
+    for (int q = threadIdx.x; q < PF_CH * SEGS; q += 256) {
+      const int rr = q / SEGS, sg = q % SEGS;
+      uint16_t* kd = Kb + ((size_t)buf * PF_CH + rr) * ROW + sg * 8;
+      uint16_t* vd = Vb + ((size_t)buf * PF_CH + rr) * ROW + sg * 8;
+      if (c0 + rr < P.T) {
+        cp_async16(kd, kbase + (c0 + rr) * P.k.stride[2] + sg * 8);
+        cp_async16(vd, vbase + (c0 + rr) * P.v.stride[2] + sg * 8);
+      } else {
+        *(uint4*)kd = make_uint4(0, 0, 0, 0);
+        *(uint4*)vd = make_uint4(0, 0, 0, 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  float o[NTO][4];
+#pragma unroll
+  for (int n = 0; n < NTO; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
+  const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
+  const int rA = 16 * rg + g, rB = rA + 8;  // this thread's two rows
+  // chunks: the first live one, then each next live one staged while the current computes
+  int64_t c = 0;
+  while (c < P.T && !chunk_live(c)) c += PF_CH;
+  if (c < P.T) stage(c, 0);
+  __syncthreads();  // Q in shared memory
+  int buf = 0;
+  while (c < P.T) {
+    int64_t nx = c + PF_CH;
+    while (nx < P.T && !chunk_live(nx)) nx += PF_CH;
+    if (nx < P.T) {
+      stage(nx, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    // scores of this warp's 16 rows over the chunk: 8 tiles of 8 positions
+    float sc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sc[n][i] = 0.f;
+    const int mi = lane >> 3, ri = lane & 7;
+#pragma unroll 2
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      // A fragments of the warp's rows (f32 queries: three exact bf16 parts)
+      float qf[4][2];
+      uint32_t a[4];
+      if (qf32) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = (i & 1) ? rB : rA, col = 16 * kk + 2 * t + 8 * (i >> 1);
+          const float2 v = *(const float2*)(Qs + (size_t)(row * QROWF + col) * 4);
+          qf[i][0] = v.x;
+          qf[i][1] = v.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = (i & 1) ? rB : rA, col = 16 * kk + 2 * t + 8 * (i >> 1);
+          a[i] = *(const uint32_t*)(Qs + (size_t)(row * ROW + col) * 2);
+        }
+      }
+      const int parts = qf32 ? 3 : 1;
+      for (int part = 0; part < parts; ++part) {
+        if (qf32)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            a[i] = pack_bf16(qf[i][0], qf[i][1]);
+            qf[i][0] -= bf16_lo_f(a[i]);
+            qf[i][1] -= bf16_hi_f(a[i]);
+          }
+#pragma unroll
+        for (int n = 0; n < 8; n += 2) {
+          uint32_t bf[4];
+          ldsm_x4(kb_s + (uint32_t)((((size_t)buf * PF_CH + 8 * n + ri + 8 * (mi >> 1)) * ROW + 16 * kk + 8 * (mi & 1)) * 2), bf);
+          mma_bf16(sc[n], a[0], a[1], a[2], a[3], bf[0], bf[1]);
+          mma_bf16(sc[n + 1], a[0], a[1], a[2], a[3], bf[2], bf[3]);
+        }
+      }
+    }
+    // chain, mask, online softmax per row (rows rA: elements 0, 1; rB: 2, 3)
+    float pv[8][4];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = hr ? rB : rA;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int64_t j = c + 8 * n + 2 * t + e;
+          float v = -INFINITY;
+          if (r < nrows && j < P.T) {
+            const float mk = ld_any(mb, moff_s[r] + j * ms3, P.mask.dt);
+            if (mk > P.mask_skip) v = rnd_dt(apply_chain(P, rnd_dt(sc[n][2 * hr + e], P.dt_d1)) + mk, P.dt_m);
+          }
+          sc[n][2 * hr + e] = v;
+          mx = fmaxf(mx, v);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mnew = fmaxf(m[hr], mx);
+      float ps = 0.f;
+#pragma unroll
+      for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = sc[n][2 * hr + e];
+          const float p = (mnew != -INFINITY && v != -INFINITY) ? rnd_dt(expf(rnd_dt(v - mnew, P.dt_sub)), P.dt_exp) : 0.f;
+          pv[n][2 * hr + e] = p;
+          ps += p;
+        }
+      ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      if (mnew != -INFINITY) {
+        const float scl = m[hr] == -INFINITY ? 0.f : expf(m[hr] - mnew);
+        l[hr] = l[hr] * scl + ps;
+#pragma unroll
+        for (int n = 0; n < NTO; ++n) {
+          o[n][2 * hr] *= scl;
+          o[n][2 * hr + 1] *= scl;
+        }
+        m[hr] = mnew;
+      }
+    }
+    // O[:, half] += P V: 4 k-steps of 16 positions, P as bf16 hi + lo
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t ah[4], al[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tile = 2 * ks + (i >> 1), hr = i & 1;
+        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
+        ah[i] = pack_bf16(p0, p1);
+        al[i] = pack_bf16(p0 - bf16_lo_f(ah[i]), p1 - bf16_hi_f(ah[i]));
+      }
+#pragma unroll
+      for (int n = 0; n < NTO; n += 2) {
+        uint32_t bf[4];
+        ldsm_x4_t(vb_s + (uint32_t)((((size_t)buf * PF_CH + 16 * ks + ri + 8 * (mi & 1)) * ROW + dh * (HD / 2) + 8 * n + 8 * (mi >> 1)) * 2), bf);
+        mma_bf16(o[n], ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
+        mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
+        mma_bf16(o[n + 1], ah[0], ah[1], ah[2], ah[3], bf[2], bf[3]);
+        mma_bf16(o[n + 1], al[0], al[1], al[2], al[3], bf[2], bf[3]);
+      }
+    }
+    __syncthreads();  // this buffer is restaged by the next iteration
+    c = nx;
+    buf ^= 1;
+  }
+  // out = O / l for this warp's rows and half of head_dim
+  char* ob = dres(P.out, argtab);
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int r = hr ? rB : rA;
+    if (r >= nrows) continue;
+    const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
+    const int64_t row = ((int64_t)b * P.nq + h) * P.Sq + qi;
+#pragma unroll
+    for (int n = 0; n < NTO; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int d = dh * (HD / 2) + 8 * n + 2 * t + e;
+        const float v = l[hr] > 0.f ? o[n][2 * hr + e] / l[hr] : 0.f;
+        if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = v;
+        else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(v);
+      }
+  }
+}
+
+template <int HD>
+void launch_tc_prefill(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  const int qbytes = p.q.dt == KDT_F32 ? PF_ROWS * (HD + 4) * 4 : PF_ROWS * (HD + 8) * 2;
+  const int dyn = 2 * 2 * PF_CH * (HD + 8) * 2 + qbytes;
+  static bool configured = false;  // per instantiation; set before the first launch (host thread)
+  if (!configured) {
+    CUDA_OK(cudaFuncSetAttribute(attn_tc_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 2 * 2 * PF_CH * (HD + 8) * 2 + PF_ROWS * (HD + 4) * 4));
+    configured = true;
+  }
+  const int qt = PF_ROWS / p.group;
+  launch_k(attn_tc_prefill_kernel<HD>, dim3(1, (unsigned)((p.Sq + qt - 1) / qt), (unsigned)(p.B * p.nkv)), dim3(256),
+           dyn, s, 1, p, argtab);
+}
+
 template <int HD>
 void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   const int nbuf = (p.T + p.splits - 1) / p.splits > TC_CH ? 2 : 1;  // as the kernel decides
@@ -996,6 +1255,14 @@ void launch_hpl(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
 }  // namespace
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.use_tc == 2) {
+    switch (p.hd) {
+      case 64: launch_tc_prefill<64>(p, argtab, s); return;
+      case 128: launch_tc_prefill<128>(p, argtab, s); return;
+      case 256: launch_tc_prefill<256>(p, argtab, s); return;
+    }
+    fail(E_INTERNAL, "tensor-core prefill attention: unsupported head_dim");
+  }
   if (p.use_tc) {
     switch (p.hd) {
       case 64: launch_tc<64>(p, argtab, s); return;
@@ -1019,6 +1286,12 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
       case 256: launch_hpl<float, 8>(p, argtab, s); break;
     }
   }
+}
+
+bool attention_tc_prefill_ok(const AttnParams& p) {
+  if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || !(p.q.dt == KDT_BF16 || p.q.dt == KDT_F32)) return false;
+  if (!(p.group == 1 || p.group == 2 || p.group == 4 || p.group == 8)) return false;
+  return smem_ok(p);
 }
 
 bool attention_tc_ok(const AttnParams& p) {
@@ -1055,7 +1328,9 @@ void verify_attention(const Launch& l, const RegionFn& region) {
     region(p.counters, 4LL * p.B * p.nkv * ((p.Sq + p.qtile - 1) / p.qtile), "arrival counters");
     if (p.splits > ATTN_MERGE_MAX_SPLITS || p.qtile * p.group > 8) fail(E_INTERNAL, "attention merge too wide");
   }
-  if (p.use_tc && !attention_tc_ok(p)) fail(E_INTERNAL, "tensor-core attention on unsupported views");
+  if (p.use_tc == 1 && !attention_tc_ok(p)) fail(E_INTERNAL, "tensor-core attention on unsupported views");
+  if (p.use_tc == 2 && (!attention_tc_prefill_ok(p) || p.splits != 1))
+    fail(E_INTERNAL, "tensor-core prefill attention on unsupported views");
   if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||
       p.k.shape[1] != p.nkv || p.k.shape[2] != p.T || p.k.shape[3] != p.hd || p.v.shape[2] != p.T ||
       p.mask.shape[3] != p.T || p.k.stride[3] != 1 || p.v.stride[3] != 1 || p.nq != p.nkv * p.group)

@@ -18,6 +18,12 @@
 // Tiles are walked M-fastest so CTAs running at the same time share the weight
 // tile (read from HBM once) while the small activation matrix stays in L2.
 //
+// f32 activations times a bf16 weight (the attention-output projection of a
+// Gemma prefill, whose context vectors are f32): the activation is first split
+// exactly into three bf16 planes x = hi + mid + lo (8 + 8 + 8 significand
+// bits), and the k-loop runs over the three planes against the same weight
+// tiles, accumulating hi.w + mid.w + lo.w in one f32 accumulator.
+//
 // Tensor maps live in a per-executable device table that the executor
 // re-encodes when the operand addresses change; the producer acquires them
 // through the tensormap proxy before the first copy.  Every mbarrier wait is
@@ -136,6 +142,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const int tiles_m = (P.M + BM - 1) / BM, tiles_n = (P.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
   const int kblocks = (P.K + BK - 1) / BK;
+  const int kb_total = kblocks * (P.a_parts > 1 ? P.a_parts : 1);
   const char* tmA = dres(P.tmap_a, argtab);
   const char* tmB = dres(P.tmap_b, argtab);
   unsigned* status = (unsigned*)dres(P.status, argtab);
@@ -180,12 +187,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = 0; kb < kb_total; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1)) { ok = false; break; }
         if (*(volatile int*)&s_failed) { ok = false; break; }
+        const int part = kb / kblocks, kk = kb - part * kblocks;
         mbar_expect_tx(&full[stage], STAGE_BYTES);
-        tma_load_2d(sA + stage * A_BYTES, tmA, &full[stage], kb * BK, m0);
-        tma_load_2d(sB + stage * B_BYTES, tmB, &full[stage], kb * BK, n0);
+        tma_load_2d(sA + stage * A_BYTES, tmA, &full[stage], kk * BK, part * P.a_plane_rows + m0);
+        tma_load_2d(sB + stage * B_BYTES, tmB, &full[stage], kk * BK, n0);
         issued[stage] = true;
         issued_parity[stage] = phase;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -207,7 +215,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) { ok = false; break; }
       tc_fence_after();
       const uint32_t d = tmem + (uint32_t)(acc * BN);
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = 0; kb < kb_total; ++kb) {
         if (!mbar_wait(&full[stage], phase)) { ok = false; break; }
         tc_fence_after();
         const uint64_t ad = sw128_desc(smem_u32(sA + stage * A_BYTES));
@@ -368,11 +376,35 @@ bool make_tc_gemm(const GemmParams& g, TcGemmParams& t) {
   t.c_dt = g.c_dt;
   t.a_ld = g.a_sm;
   t.b_ld = g.b_sn;
+  t.a_parts = 1;
+  t.a_plane_rows = t.M;
+  return true;
+}
+
+bool make_tc_gemm_split(const GemmParams& g, TcGemmParams& t) {
+  // A: the dense [3 * M, K] bf16 planes of the split f32 activation (placed by the caller)
+  if (g.batch != 1 || g.a_dt != KDT_F32 || g.b_dt != KDT_BF16) return false;
+  if (!(g.c_dt == KDT_BF16 || g.c_dt == KDT_F32)) return false;
+  if (g.b_sk != 1 || g.M < 16 || g.N < 16 || g.K < 16 || (g.K % 8)) return false;
+  if (3 * g.M > (1 << 30) || g.N > (1 << 30) || g.K > (1 << 30)) return false;
+  if ((g.b.off % 16) || (g.c.off % 16) || ((g.b_sn * 2) % 16) || g.b_sn < g.K) return false;
+  t = TcGemmParams{};
+  t.c = g.c;
+  t.b = g.b;
+  t.M = (int32_t)g.M;
+  t.N = (int32_t)g.N;
+  t.K = (int32_t)g.K;
+  t.c_dt = g.c_dt;
+  t.a_ld = g.K;
+  t.b_ld = g.b_sn;
+  t.a_parts = 3;
+  t.a_plane_rows = t.M;
   return true;
 }
 
 void verify_tc_gemm(const TcGemmParams& p, const RegionFn& region) {
-  region(p.a, ((int64_t)(p.M - 1) * p.a_ld + p.K) * 2, "lhs");
+  if (!(p.a_parts == 1 || p.a_parts == 3) || p.a_plane_rows != p.M) fail(E_INTERNAL, "bad tensor-core GEMM planes");
+  region(p.a, ((int64_t)(p.a_parts * p.M - 1) * p.a_ld + p.K) * 2, "lhs");
   region(p.b, ((int64_t)(p.N - 1) * p.b_ld + p.K) * 2, "rhs");
   region(p.c, (int64_t)p.M * p.N * (int64_t)dt_size((DT)p.c_dt), "result");
   region(p.tmap_a, 128, "lhs tensor map");

@@ -245,6 +245,7 @@ class Planner {
   void emit_ew_group(const std::vector<int>& members);
   void emit_node_kernel(int n);
   GemmParams dot_params(int id, int oslot, int64_t* bytes, int64_t* flops);
+  bool emit_split_dot(int id, int oslot);
   std::set<int> pre_emitted_;  // units already emitted together with an earlier one (grouped GEMVs)
   std::set<int> emitted_units_;
   void build_row_regions();
@@ -523,6 +524,24 @@ TView Planner::view_of(int n) {
   }
   // view ops
   if (mat_slot_[n] >= 0) return dense_view(mat_slot_[n], nd.dt, nd.shape);
+  if (nd.op == Op::Reshape) {
+    // a reshape of a reshape is one reshape of the first one's operand: a
+    // head merge followed by the split back (printed around the attention
+    // block) stays a strided view instead of a materialised copy
+    int src = nd.in[0];
+    while (g_.nodes[src].op == Op::Reshape && loc_[src].kind == Loc::VIEWOP && mat_slot_[src] < 0)
+      src = g_.nodes[src].in[0];
+    if (src != nd.in[0] && g_.nodes[src].dt == nd.dt) {
+      TView base = view_of(src);
+      std::vector<int64_t> os(base.shape, base.shape + base.rank), ost(base.stride, base.stride + base.rank), ns;
+      if (reshape_strides(os, ost, nd.shape, ns)) {
+        TView v = base;
+        v.rank = nd.rank();
+        for (int i = 0; i < v.rank; ++i) v.shape[i] = nd.shape[i], v.stride[i] = ns[i];
+        return v;
+      }
+    }
+  }
   TView in = view_of(nd.in[0]);
   TView v = in;
   v.rank = nd.rank();
@@ -1436,11 +1455,13 @@ void Planner::emit_attention(int d2) {
   // one 128-position round per warp-group of a CTA, at most two CTAs per SM;
   // the tensor-core decode kernel takes 64-position splits
   P.use_tc = attention_tc_ok(P) && !getenv_off("CLJXLA_B200_ATTN_TC") ? 1 : 0;
+  if (!P.use_tc && P.Sq > P.qtile && attention_tc_prefill_ok(P) && !getenv_off("CLJXLA_B200_ATTN_TC")) P.use_tc = 2;
   int64_t per_split = P.use_tc ? 64 : 128;
   if (const char* e = getenv("CLJXLA_B200_ATTN_SPLIT"))  // positions per split (measurement sweeps)
     if (atoi(e) >= 16) per_split = atoi(e);
   int splits = (int)std::min<int64_t>((P.T + per_split - 1) / per_split, std::max<int64_t>(1, 2 * 148 / ctas));
   splits = std::max(1, std::min(splits, ATTN_MERGE_MAX_SPLITS));
+  if (P.use_tc == 2) splits = 1;  // whole rows per CTA
   P.splits = splits;
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
@@ -1650,6 +1671,7 @@ void Planner::emit_node_kernel(int id) {
     }
     case Op::Dot: {
       int64_t bytes = 0, flops = 0;
+      if (opt_.fast_kernels && !getenv_off("CLJXLA_B200_SPLIT_GEMM") && emit_split_dot(id, oslot)) break;
       GemmParams G = dot_params(id, oslot, &bytes, &flops);
       Launch fl;
       TcGemmParams tc;
@@ -1705,6 +1727,140 @@ void Planner::emit_node_kernel(int id) {
     default:
       fail(E_UNIMPLEMENTED, std::string("no kernel for op ") + op_name(n.op));
   }
+}
+
+// f32 activations [M, K] times a bf16 weight [N, K] with M >= 16 (a prefill
+// attention-output projection): one elementwise program reads the activation
+// through its printed view and writes it as three exact bf16 planes
+// hi / mid / lo; the tensor-core GEMM then accumulates the three plane
+// products in f32.  Nothing is emitted unless both launches apply.
+bool Planner::emit_split_dot(int id, int oslot) {
+  const Node& n = g_.nodes[id];
+  const Node& a = g_.nodes[n.in[0]];
+  const Node& b = g_.nodes[n.in[1]];
+  if (a.dt != DT::F32 || b.dt != DT::BF16 || !(n.dt == DT::F32 || n.dt == DT::BF16)) return false;
+  auto has = [](const std::vector<int64_t>& v, int64_t d) { return std::find(v.begin(), v.end(), d) != v.end(); };
+  for (int64_t d : n.ia)
+    if (a.shape[d] != 1) return false;
+  for (int64_t d : n.ib)
+    if (b.shape[d] != 1) return false;
+  std::vector<int64_t> lf, rf;
+  int64_t M = 1, K = 1, N = 1;
+  for (int d = 0; d < a.rank(); ++d)
+    if (!has(n.ia, d) && !has(n.ic, d)) lf.push_back(d), M *= a.shape[d];
+  for (int64_t d : n.ic) K *= a.shape[d];
+  for (int d = 0; d < b.rank(); ++d)
+    if (!has(n.ib, d) && !has(n.id, d)) rf.push_back(d), N *= b.shape[d];
+  if (M < 16 || N < 16 || K < 16 || (K % 8) || (int)(lf.size() + n.ic.size()) > CLJXLA_MAXR) return false;
+  // the weight: contracting dims collapse to unit stride, free dims to one row stride
+  TView bv = view_of(n.in[1]);
+  auto collapse = [&](const std::vector<int64_t>& dims, int64_t& stride) {
+    int64_t prev = -1;
+    stride = 0;
+    for (int64_t d : dims) {
+      if (bv.shape[d] == 1) continue;
+      if (prev >= 0 && prev != bv.stride[d] * bv.shape[d]) return false;
+      prev = bv.stride[d];
+    }
+    stride = prev < 0 ? 0 : prev;
+    return true;
+  };
+  int64_t sk = 0, sn = 0;
+  if (!collapse(n.id, sk) || !collapse(rf, sn) || sk != 1) return false;
+  GemmParams G{};
+  G.batch = 1;
+  G.M = M;
+  G.N = N;
+  G.K = K;
+  G.a_dt = KDT_F32;
+  G.b_dt = KDT_BF16;
+  G.c_dt = kdt(n.dt);
+  G.b = bv.p;
+  G.b_sk = 1;
+  G.b_sn = sn;
+  G.c = slot_ptr(oslot);
+  TcGemmParams tc;
+  if (!make_tc_gemm_split(G, tc)) return false;
+  // the three planes: rows in the printed free-dim order, K in contracting order
+  EwParams E{};
+  E.rank = 0;
+  bool natural = true;  // [M, K] row-major is the operand's own element order
+  {
+    int k = 0;
+    for (int d = 0; d < a.rank(); ++d) {
+      if (has(n.ia, d)) continue;
+      const int64_t want = k < (int)lf.size() ? lf[k] : n.ic[k - lf.size()];
+      if (want != d) natural = false;
+      ++k;
+    }
+  }
+  int src = n.in[0];
+  // a reshape of a permuted view (the heads of an attention context merged
+  // into K) keeps the element order: read the reshape's operand directly
+  // instead of materialising it
+  while (natural && g_.nodes[src].op == Op::Reshape && loc_[src].kind == Loc::VIEWOP && mat_slot_[src] < 0 &&
+         g_.nodes[g_.nodes[src].in[0]].rank() <= CLJXLA_MAXR)
+    src = g_.nodes[src].in[0];
+  TView av = view_of(src);
+  if (src != n.in[0]) {
+    for (int d = 0; d < av.rank; ++d) E.dims[E.rank] = av.shape[d], E.in[0].stride[E.rank++] = av.stride[d];
+  } else {
+    for (int64_t d : lf) E.dims[E.rank] = a.shape[d], E.in[0].stride[E.rank++] = av.stride[d];
+    for (int64_t d : n.ic) E.dims[E.rank] = a.shape[d], E.in[0].stride[E.rank++] = av.stride[d];
+  }
+  E.n = M * K;
+  E.in[0].p = av.p;
+  E.in[0].dt = av.dt;
+  E.in[0].sel_dim = -1;
+  E.nin = 1;
+  auto op = [&](int opc, int dt, int dst, int x, int y, int aux) {
+    EwInstr I{};
+    I.op = (uint8_t)opc;
+    I.dt = (uint8_t)dt;
+    I.dst = (uint8_t)dst;
+    I.a = (uint8_t)x;
+    I.b = (uint8_t)y;
+    I.aux = (uint8_t)aux;
+    E.code[E.ncode++] = I;
+  };
+  op(EW_LOAD, KDT_F32, 0, 0, 0, 0);
+  op(EW_CONVERT, KDT_BF16, 1, 0, 0, KDT_F32);  // hi
+  op(EW_SUB, KDT_F32, 2, 0, 1, 0);             // exact remainder
+  op(EW_CONVERT, KDT_BF16, 3, 2, 0, KDT_F32);  // mid
+  op(EW_SUB, KDT_F32, 4, 2, 3, 0);
+  op(EW_CONVERT, KDT_BF16, 5, 4, 0, KDT_F32);  // lo
+  const int64_t plane = M * K * 2;
+  const int slot = new_tmp(3 * plane);
+  for (int p = 0; p < 3; ++p) {
+    E.out[p].p = slot_ptr(slot, p * plane);
+    E.out[p].dt = KDT_BF16;
+    E.out[p].reg = 1 + 2 * p;
+  }
+  E.nout = 3;
+  push(K_EW, blob_of(E), n.name + ".planes", M * K * 4 + 3 * plane);
+  tc.a = slot_ptr(slot);
+  int bm, bn, bk;
+  tc_gemm_tile_shape(&bm, &bn, &bk);
+  TmapSpec ta, tb;
+  ta.base = tc.a;
+  ta.inner = K;
+  ta.outer = 3 * M;
+  ta.row_bytes = K * 2;
+  ta.box_inner = bk;
+  ta.box_outer = bm;
+  tb.base = G.b;
+  tb.inner = K;
+  tb.outer = N;
+  tb.row_bytes = sn * 2;
+  tb.box_inner = bk;
+  tb.box_outer = bn;
+  tc.tmap_a_index = (int32_t)plan_.tmaps.size();
+  plan_.tmaps.push_back(ta);
+  tc.tmap_b_index = (int32_t)plan_.tmaps.size();
+  plan_.tmaps.push_back(tb);
+  push(K_GEMM_TC, blob_of(tc), n.name,
+       a.numel() * 4 + b.numel() * 2 + n.numel() * (int64_t)dt_size(n.dt), 2 * M * N * K);
+  return true;
 }
 
 GemmParams Planner::dot_params(int id, int oslot, int64_t* bytes_out, int64_t* flops_out) {

@@ -188,7 +188,7 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
     }
     case K_GEMM_TC: {
       const TcGemmParams& t = *(const TcGemmParams*)b;
-      c.add(t.a, ((int64_t)(t.M - 1) * t.a_ld + t.K) * 2, false);
+      c.add(t.a, ((int64_t)(t.a_parts * t.M - 1) * t.a_ld + t.K) * 2, false);
       c.add(t.b, ((int64_t)(t.N - 1) * t.b_ld + t.K) * 2, false);
       c.add(t.c, (int64_t)t.M * t.N * (int64_t)dt_size((DT)t.c_dt), true);
       c.add(t.tmap_a, 128, false);

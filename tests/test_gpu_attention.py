@@ -41,8 +41,33 @@ def _rand(shape, seed, scale=1.0):
     (1, 2560, 8, 4, None, None, True, 256, 2559),
     (1, 700, 8, 4, 50.0, 300, True, 128, 650),
     (4, 1200, 4, 2, None, None, True, 256, 900),
+    # prefill on the tensor cores: 64 query vectors per CTA, causal chunks skipped
+    (100, 128, 8, 4, None, None, True, 64, 20),
+    (70, 96, 4, 1, 50.0, 24, True, 128, 0),
+    (130, 160, 2, 2, None, None, False, 256, None),
+    (64, 64, 8, 1, None, None, True, 64, 0),
+    (200, 512, 8, 4, None, 64, True, 256, 300),
 ])
 def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
+    _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos)
+
+
+@pytest.mark.parametrize("Sq,T,nq,nkv,window,hd", [
+    (100, 128, 8, 4, None, 64),
+    (70, 96, 4, 1, 24, 128),
+])
+def test_attention_prefill_simt_path(ctx, monkeypatch, Sq, T, nq, nkv, window, hd):
+    """The CUDA-core prefill kernel (taken where the tensor-core one cannot run)
+    on the same blocks."""
+    monkeypatch.setenv("CLJXLA_B200_ATTN_TC", "0")
+    core.clear_cache()  # the switch is read when a program is compiled
+    try:
+        _check_attention(ctx, Sq, T, nq, nkv, None, window, True, hd, 0)
+    finally:
+        core.clear_cache()
+
+
+def _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
     B = 1
 
     def f(q, k, v, kc, vc, ow, pos):
@@ -62,6 +87,18 @@ def test_attention_block(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos)
               _rand((B, nkv, T, hd), 4), _rand((B, nkv, T, hd), 5), _rand((nq * hd, nq * hd), 6, 0.05), pos]
     want = interp.run_mlir(text, inputs)
     got = runner.run_graph(ctx, g, inputs, text)
+    floors = None
     for i, ((shape, dt), a, b) in enumerate(zip(runner.out_specs(g), got, want)):
         ok, excess, maxerr = close(a, b, dt)
+        if not ok and dt == "f32" and not np.isnan(a).any():
+            # the bf16 scores of this block round once per element: a valid f32
+            # summation order different from the oracle's flips a few of those
+            # roundings, and over a short window one flip moves an output by more
+            # than the f32 tolerance.  Such a result must stay within twice the
+            # spread of oracle runs with summation-order noise on every f32 sum.
+            if floors is None:
+                floors = [interp.run_mlir(text, inputs, ulp_noise_seed=s) for s in range(4)]
+            spread = max(close(f[i], b, dt)[2] for f in floors)
+            ok = maxerr <= 2.0 * spread
+            excess = maxerr - 2.0 * spread
         assert ok, f"output {i} ({dt}{shape}) differs: max err {maxerr:.3g}, excess {excess:.3g}"

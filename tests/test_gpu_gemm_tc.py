@@ -99,3 +99,49 @@ def test_gemma3_prefill_through_tensor_cores(ctx):
             floors = [interp.run_mlir(text, inputs, ulp_noise_seed=sd) for sd in (1, 2, 3, 4)]
         ok, bad, rr, fb, fr = close_model_floor(a, b, [f[i] for f in floors], edt)
         assert ok, f"output {i}: {bad:.2%} out of bound, rel rms {rr:.3g} (floor {fb:.2%}, {fr:.3g})"
+
+
+def _f32(shape, seed, scale=1.0):
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return (rng.standard_normal(shape) * scale).astype(np.float32)
+
+
+@pytest.mark.parametrize("S,K,N", [
+    (128, 256, 192),
+    (200, 320, 300),     # ragged M / N: plane tiles read into the next plane's rows
+    (512, 2048, 640),
+])
+def test_f32_activation_times_bf16_weight_on_tensor_cores(ctx, S, K, N):
+    """f32 x bf16 -> f32 (the attention-output projection of a Gemma prefill,
+    gemma.clj attention block): the activation is split exactly into three bf16
+    planes and the tcgen05 GEMM accumulates the three products, so the result
+    matches the f32 oracle at the f32 tolerance."""
+    g = t.trace_graph("tc_split", [("x", ("tensor", (1, S, K), "f32")), ("w", ("tensor", (N, K), "bf16"))],
+                      lambda x, w: [models.gemma_linear(x, w)])
+    text = shlo.graph_to_mlir_text(g)
+    inputs = [_f32((1, S, K), 7), _bf16((N, K), 8, 0.05)]
+    want = interp.run_mlir(text, inputs)
+    got, prof = _run_profiled(ctx, g, inputs, text)
+    kinds = [e["kind"] for e in prof]
+    assert "gemm_tc" in kinds and "gemm_generic" not in kinds, kinds
+    ok, excess, maxerr = close(got[0], want[0], "f32")
+    assert ok, f"max err {maxerr:.3g}, excess {excess:.3g}"
+
+
+def test_split_planes_read_through_head_merge(ctx):
+    """The attention context [1, heads, S, hd] f32, transposed and reshaped to
+    [1, S, heads * hd] as printed before the output projection: the planes are
+    written straight from the permuted view (no materialised copy)."""
+    H, S, hd, N = 4, 96, 64, 320
+    def f(x, w):
+        y = t.reshape(t.transpose(x, [0, 2, 1, 3]), [1, S, H * hd])
+        return [models.gemma_linear(y, w)]
+    g = t.trace_graph("tc_split_view", [("x", ("tensor", (1, H, S, hd), "f32")), ("w", ("tensor", (N, H * hd), "bf16"))], f)
+    text = shlo.graph_to_mlir_text(g)
+    inputs = [_f32((1, H, S, hd), 9), _bf16((N, H * hd), 10, 0.05)]
+    want = interp.run_mlir(text, inputs)
+    got, prof = _run_profiled(ctx, g, inputs, text)
+    kinds = [e["kind"] for e in prof]
+    assert "gemm_tc" in kinds and "copy" not in kinds, kinds
+    ok, excess, maxerr = close(got[0], want[0], "f32")
+    assert ok, f"max err {maxerr:.3g}, excess {excess:.3g}"
