@@ -659,6 +659,11 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
                : "r"(addr));
 }
 // two f32 as a bf16 pair (round to nearest even): lo in bits 0-15
+// bulk prefetch of [p, p + bytes) into L2 (16-byte aligned address and size)
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -685,6 +690,29 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   __shared__ uint32_t psm[2][8][TC_CH / 2 + 4];   // P hi / lo bf16 pairs, rows padded against bank conflicts
   // Q as bf16 parts: one for bf16 q; three (hi + mid + lo == q exactly) for f32 q
   __shared__ __align__(16) uint16_t qsm[3][8][HD + 8];
+  // Before the dependency wait: pull this split's K/V rows towards L2.  A
+  // prefetch returns nothing to the thread, so a row that the preceding
+  // kernel is still writing (the new position) is read correctly after the wait.
+  {
+    const int64_t ch = (P.T + P.splits - 1) / P.splits;
+    const int64_t p0 = blockIdx.x * ch, p1 = min((int64_t)P.T, p0 + ch);
+    const int kb = blockIdx.z / P.nkv, kk = blockIdx.z % P.nkv;
+    const uint16_t* kr = (const uint16_t*)dres(P.k.p, argtab) + kb * P.k.stride[0] + kk * P.k.stride[1];
+    const uint16_t* vr = (const uint16_t*)dres(P.v.p, argtab) + kb * P.v.stride[0] + kk * P.v.stride[1];
+    if (P.k.stride[2] == HD && P.v.stride[2] == HD) {  // contiguous rows: 16 KB pieces
+      const int64_t bytes = (p1 - p0) * HD * 2;
+      for (int64_t i = threadIdx.x; i * 16384 < bytes; i += 128) {
+        const uint32_t n = (uint32_t)min((int64_t)16384, bytes - i * 16384);
+        l2_prefetch_bulk((const char*)(kr + p0 * HD) + i * 16384, n);
+        l2_prefetch_bulk((const char*)(vr + p0 * HD) + i * 16384, n);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < p1 - p0; i += 128) {
+        l2_prefetch_bulk(kr + (p0 + i) * P.k.stride[2], HD * 2);
+        l2_prefetch_bulk(vr + (p0 + i) * P.v.stride[2], HD * 2);
+      }
+    }
+  }
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -717,11 +745,24 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   for (int e = threadIdx.x; e < 3 * 8 * (HD + 8) / 8; e += 128) ((uint4*)&qsm[0][0][0])[e] = make_uint4(0, 0, 0, 0);
   __syncthreads();
   const int64_t qs3 = P.q.stride[3];
-  for (int e = threadIdx.x; e < nqv * HD; e += 128) {
+  // all of this thread's query loads in flight before the shared stores
+  float qv[8 * HD / 128];
+#pragma unroll
+  for (int u = 0; u < 8 * HD / 128; ++u) {
+    const int e = threadIdx.x + 128 * u;
+    qv[u] = 0.f;
+    if (e < nqv * HD) {
+      const int64_t o = qoff_s[e / HD] + (e % HD) * qs3;
+      qv[u] = qf32 ? ((const float*)qb)[o] : __uint_as_float((uint32_t)((const uint16_t*)qb)[o]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 8 * HD / 128; ++u) {
+    const int e = threadIdx.x + 128 * u;
+    if (e >= nqv * HD) break;
     const int r = e / HD, c = e % HD;
-    const int64_t o = qoff_s[r] + c * qs3;
     if (qf32) {
-      const float q = ((const float*)qb)[o];
+      const float q = qv[u];
       const __nv_bfloat16 hi = __float2bfloat16_rn(q);
       const float r1 = q - __bfloat162float(hi);
       const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
@@ -730,7 +771,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
       qsm[1][r][c] = __bfloat16_as_ushort(mid);
       qsm[2][r][c] = __bfloat16_as_ushort(lo);
     } else {
-      qsm[0][r][c] = ((const uint16_t*)qb)[o];
+      qsm[0][r][c] = (uint16_t)__float_as_uint(qv[u]);
     }
   }
   const uint32_t qsa = (uint32_t)__cvta_generic_to_shared(&qsm[0][g][2 * t]);
@@ -941,15 +982,26 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 // every staged K/V row.  8 warps: warp w owns rows 16 (w & 3) .. + 15 and
 // half (w >> 2) of head_dim; the two warps of a row group compute the same
 // scores (S = Q K^T over a 64-position chunk), so their online-softmax state
-// agrees without exchange.  Chunks whose mask is at or below mask_skip for
-// every row are skipped (the causal upper triangle); K/V chunks are staged
-// with cp.async, double-buffered.  The printed score chain, mask, exp and
-// roundings are replayed per element; P enters P V as bf16 hi + lo, f32
-// queries as an exact hi + mid + lo split.
+// agrees without exchange.  One pass over the CTA's mask rows first marks the
+// 64-position chunks holding any position above mask_skip (the causal upper
+// triangle and positions outside a sliding window drop out); only those are
+// staged, K / V with cp.async, double-buffered.  Tiles are issued longest
+// first (the last query positions see the most chunks).  P enters P V as
+// bf16 hi + lo, f32 queries as an exact hi + mid + lo split.
+//
+// FAST: the additive mask is f32 with 16-byte aligned rows and the score
+// chain has a closed form with f32 softmax arithmetic (the printed Gemma and
+// GPT-2 blocks): each chunk's mask tile is staged into shared memory with K / V
+// and the per-score work is a few register operations.  Otherwise the printed
+// chain and roundings are replayed per score with the mask read from memory.
 constexpr int PF_CH = 64;   // positions per staged chunk
 constexpr int PF_ROWS = 64; // query vectors per CTA
+constexpr int PF_MROW = PF_CH + 4;  // padded f32 row of a staged mask tile
+constexpr int PF_LIVE_WORDS = 32;   // live-chunk bitmap: T <= 32 * 32 * 64 positions
 
-template <int HD>
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <int HD, bool FAST>
 __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_constant__ AttnParams P,
                                                                  const uint64_t* __restrict__ argtab) {
   constexpr int ROW = HD + 8;           // padded bf16 row of K / V / bf16 Q
@@ -959,51 +1011,95 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   extern __shared__ __align__(16) unsigned char pf_smem[];
   uint16_t* Kb = (uint16_t*)pf_smem;                    // [2][PF_CH][ROW]
   uint16_t* Vb = Kb + 2 * PF_CH * ROW;                  // [2][PF_CH][ROW]
-  unsigned char* Qs = (unsigned char*)(Vb + 2 * PF_CH * ROW);  // bf16 [64][ROW] or f32 [64][QROWF]
+  float* Ms = (float*)(Vb + 2 * PF_CH * ROW);           // FAST: [2][PF_ROWS][PF_MROW]
+  unsigned char* Qs = (unsigned char*)(Ms + (FAST ? 2 * PF_ROWS * PF_MROW : 0));  // bf16 [64][ROW] / f32 [64][QROWF]
   __shared__ int64_t qoff_s[PF_ROWS], moff_s[PF_ROWS];
+  __shared__ unsigned live_s[PF_LIVE_WORDS];
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rg = warp & 3, dh = warp >> 2;
   const int bk = blockIdx.z, b = bk / P.nkv, kh = bk % P.nkv;
   const int QT = PF_ROWS / P.group;  // query positions per CTA
-  const int i0 = blockIdx.y * QT;
+  const int i0 = (int)(gridDim.y - 1 - blockIdx.y) * QT;  // longest tiles first
   const int nrows = min(QT, P.Sq - i0) * P.group;
   const bool qf32 = P.q.dt == KDT_F32;
   const char* qb = dres(P.q.p, argtab);
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
   const char* mb = dres(P.mask.p, argtab);
+  const float* mf = (const float*)mb;
   if (threadIdx.x < PF_ROWS) {
     const int r = threadIdx.x < nrows ? threadIdx.x : 0;
     const int qi = i0 + r / P.group, h = kh * P.group + r % P.group;
     qoff_s[threadIdx.x] = b * P.q.stride[0] + h * P.q.stride[1] + qi * P.q.stride[2];
     moff_s[threadIdx.x] = b * P.mask.stride[0] + h * P.mask.stride[1] + qi * P.mask.stride[2];
   }
+  if (threadIdx.x < PF_LIVE_WORDS) live_s[threadIdx.x] = 0u;
   __syncthreads();
-  // Q -> shared (rows >= nrows zero)
-  for (int e = threadIdx.x; e < PF_ROWS * HD; e += 256) {
-    const int r = e / HD, c = e % HD;
-    if (qf32) {
-      float v = 0.f;
-      if (r < nrows) v = ((const float*)qb)[qoff_s[r] + c * P.q.stride[3]];
-      ((float*)Qs)[r * QROWF + c] = v;
-    } else {
-      uint16_t v = 0;
-      if (r < nrows) v = ((const uint16_t*)qb)[qoff_s[r] + c * P.q.stride[3]];
-      ((uint16_t*)Qs)[r * ROW + c] = v;
+  // Q -> shared (rows >= nrows zero); eight loads in flight per thread before
+  // their shared stores
+  for (int e0 = threadIdx.x; e0 < PF_ROWS * HD; e0 += 8 * 256) {
+    uint32_t val[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + 256 * u, r = e / HD, c = e % HD;
+      val[u] = 0u;
+      if (r < nrows) {
+        const int64_t o = qoff_s[r] + c * P.q.stride[3];
+        val[u] = qf32 ? __float_as_uint(((const float*)qb)[o]) : (uint32_t)((const uint16_t*)qb)[o];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + 256 * u, r = e / HD, c = e % HD;
+      if (qf32) ((uint32_t*)Qs)[r * QROWF + c] = val[u];
+      else ((uint16_t*)Qs)[r * ROW + c] = (uint16_t)val[u];
     }
   }
   const int64_t ms3 = P.mask.stride[3];
-  // does chunk c0 hold any position above mask_skip for any row? (all threads)
-  auto chunk_live = [&](int64_t c0) {
+  const int nchunks = (P.T + PF_CH - 1) / PF_CH;
+  // live chunks: one warp per chunk, stopping at the first position above mask_skip
+  for (int ch = warp; ch < nchunks; ch += 8) {
+    const int64_t c0 = (int64_t)ch * PF_CH;
     bool any = false;
-    for (int e = threadIdx.x; e < nrows * PF_CH; e += 256) {
-      const int r = e / PF_CH, j = e % PF_CH;
-      if (c0 + j < P.T && ld_any(mb, moff_s[r] + (c0 + j) * ms3, P.mask.dt) > P.mask_skip) any = true;
+    if (FAST) {  // 16 float4 per mask row of the chunk (T is a multiple of 4)
+      for (int e0 = 0; e0 < nrows * 16; e0 += 128) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + 32 * u + lane;
+          const int64_t pos = c0 + 4 * (e & 15);
+          if (e < nrows * 16 && pos < P.T) {
+            const float4 m4 = *(const float4*)(mf + moff_s[e >> 4] + pos);
+            any |= fmaxf(fmaxf(m4.x, m4.y), fmaxf(m4.z, m4.w)) > P.mask_skip;
+          }
+        }
+        if (__any_sync(0xffffffffu, any)) break;
+      }
+    } else {
+      for (int e0 = 0; e0 < nrows * PF_CH; e0 += 128) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + 32 * u + lane;
+          const int64_t pos = c0 + (e % PF_CH);
+          if (e < nrows * PF_CH && pos < P.T && ld_any(mb, moff_s[e / PF_CH] + pos * ms3, P.mask.dt) > P.mask_skip)
+            any = true;
+        }
+        if (__any_sync(0xffffffffu, any)) break;
+      }
     }
-    return __syncthreads_or(any) != 0;
+    if (__any_sync(0xffffffffu, any) && lane == 0) atomicOr(&live_s[ch >> 5], 1u << (ch & 31));
+  }
+  __syncthreads();
+  auto next_live = [&](int from) {
+    while (from < nchunks) {
+      const unsigned w = live_s[from >> 5] >> (from & 31);
+      if (w) return from + __ffs(w) - 1;
+      from = (from | 31) + 1;
+    }
+    return nchunks;
   };
-  auto stage = [&](int64_t c0, int buf) {
+  auto stage = [&](int ch, int buf) {
+    const int64_t c0 = (int64_t)ch * PF_CH;
     constexpr int SEGS = HD / 8;
     for (int q = threadIdx.x; q < PF_CH * SEGS; q += 256) {
       const int rr = q / SEGS, sg = q % SEGS;
@@ -1017,8 +1113,20 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         *(uint4*)vd = make_uint4(0, 0, 0, 0);
       }
     }
+    if (FAST) {  // the chunk's mask tile; -inf past T and in rows past nrows
+      for (int q = threadIdx.x; q < PF_ROWS * 16; q += 256) {
+        const int r = q >> 4, sg = q & 15;
+        const int64_t pos = c0 + 4 * sg;
+        float* md = Ms + ((size_t)buf * PF_ROWS + r) * PF_MROW + 4 * sg;
+        if (r < nrows && pos < P.T) cp_async16(md, mf + moff_s[r] + pos);
+        else *(float4*)md = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      }
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
+  // the closed-form chain (FAST): d1 rounding, multiply, its rounding
+  const bool d1b = P.dt_d1 == KDT_BF16, mul = P.chain_kind == 1, mulb = P.chain_dt == KDT_BF16;
+  const float cmul = P.chain_c, skip = P.mask_skip;
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
   float o[NTO][4];
 #pragma unroll
@@ -1027,22 +1135,20 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
   const int rA = 16 * rg + g, rB = rA + 8;  // this thread's two rows
-  // chunks: the first live one, then each next live one staged while the current computes
-  int64_t c = 0;
-  while (c < P.T && !chunk_live(c)) c += PF_CH;
-  if (c < P.T) stage(c, 0);
+  int ch = next_live(0);
+  if (ch < nchunks) stage(ch, 0);
   __syncthreads();  // Q in shared memory
   int buf = 0;
-  while (c < P.T) {
-    int64_t nx = c + PF_CH;
-    while (nx < P.T && !chunk_live(nx)) nx += PF_CH;
-    if (nx < P.T) {
+  while (ch < nchunks) {
+    const int nx = next_live(ch + 1);
+    if (nx < nchunks) {
       stage(nx, buf ^ 1);
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
+    const int64_t c = (int64_t)ch * PF_CH;
     // scores of this warp's 16 rows over the chunk: 8 tiles of 8 positions
     float sc[8][4];
 #pragma unroll
@@ -1095,18 +1201,36 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
       const int r = hr ? rB : rA;
       float mx = -INFINITY;
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < 8; ++n) {
+        if (FAST) {
+          const float2 mk2 = *(const float2*)(Ms + ((size_t)buf * PF_ROWS + r) * PF_MROW + 8 * n + 2 * t);
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int64_t j = c + 8 * n + 2 * t + e;
-          float v = -INFINITY;
-          if (r < nrows && j < P.T) {
-            const float mk = ld_any(mb, moff_s[r] + j * ms3, P.mask.dt);
-            if (mk > P.mask_skip) v = rnd_dt(apply_chain(P, rnd_dt(sc[n][2 * hr + e], P.dt_d1)) + mk, P.dt_m);
+          for (int e = 0; e < 2; ++e) {
+            const float mk = e ? mk2.y : mk2.x;
+            float s = sc[n][2 * hr + e];
+            if (d1b) s = bf16_round(s);
+            if (mul) {
+              s *= cmul;
+              if (mulb) s = bf16_round(s);
+            }
+            const float v = mk > skip ? s + mk : -INFINITY;
+            sc[n][2 * hr + e] = v;
+            mx = fmaxf(mx, v);
           }
-          sc[n][2 * hr + e] = v;
-          mx = fmaxf(mx, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int64_t j = c + 8 * n + 2 * t + e;
+            float v = -INFINITY;
+            if (r < nrows && j < P.T) {
+              const float mk = ld_any(mb, moff_s[r] + j * ms3, P.mask.dt);
+              if (mk > skip) v = rnd_dt(apply_chain(P, rnd_dt(sc[n][2 * hr + e], P.dt_d1)) + mk, P.dt_m);
+            }
+            sc[n][2 * hr + e] = v;
+            mx = fmaxf(mx, v);
+          }
         }
+      }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float mnew = fmaxf(m[hr], mx);
@@ -1116,7 +1240,8 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = sc[n][2 * hr + e];
-          const float p = (mnew != -INFINITY && v != -INFINITY) ? rnd_dt(expf(rnd_dt(v - mnew, P.dt_sub)), P.dt_exp) : 0.f;
+          float p = 0.f;
+          if (v != -INFINITY) p = FAST ? expf(v - mnew) : rnd_dt(expf(rnd_dt(v - mnew, P.dt_sub)), P.dt_exp);
           pv[n][2 * hr + e] = p;
           ps += p;
         }
@@ -1155,7 +1280,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
       }
     }
     __syncthreads();  // this buffer is restaged by the next iteration
-    c = nx;
+    ch = nx;
     buf ^= 1;
   }
   // out = O / l for this warp's rows and half of head_dim
@@ -1178,19 +1303,42 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   }
 }
 
-template <int HD>
-void launch_tc_prefill(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
-  const int qbytes = p.q.dt == KDT_F32 ? PF_ROWS * (HD + 4) * 4 : PF_ROWS * (HD + 8) * 2;
-  const int dyn = 2 * 2 * PF_CH * (HD + 8) * 2 + qbytes;
+// dynamic shared memory of the prefill kernel
+int prefill_smem(const AttnParams& p, bool fast) {
+  const int qbytes = p.q.dt == KDT_F32 ? PF_ROWS * (p.hd + 4) * 4 : PF_ROWS * (p.hd + 8) * 2;
+  return 2 * 2 * PF_CH * (p.hd + 8) * 2 + (fast ? 2 * PF_ROWS * PF_MROW * 4 : 0) + qbytes;
+}
+constexpr int PF_SMEM_MAX = 227 * 1024 - 2048;  // the opt-in limit less the static shared memory
+
+// the specialised form applies: f32 mask with 16-byte aligned rows, f32
+// softmax arithmetic, a closed-form chain, and the mask tiles fit
+bool prefill_fast(const AttnParams& p) {
+  if (p.mask.dt != KDT_F32 || p.mask.stride[3] != 1 || (p.mask.p.off % 16) || (p.T % 4)) return false;
+  for (int d = 0; d < 3; ++d)
+    if (p.mask.stride[d] % 4) return false;
+  if (p.dt_m != KDT_F32 || p.dt_sub != KDT_F32 || p.dt_exp != KDT_F32) return false;
+  if (!(p.dt_d1 == KDT_BF16 || p.dt_d1 == KDT_F32)) return false;
+  if (!(p.chain_kind == 2 || (p.chain_kind == 1 && (p.chain_dt == KDT_BF16 || p.chain_dt == KDT_F32)))) return false;
+  return prefill_smem(p, true) <= PF_SMEM_MAX;
+}
+
+template <int HD, bool FAST>
+void launch_tc_prefill_t(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   static bool configured = false;  // per instantiation; set before the first launch (host thread)
   if (!configured) {
-    CUDA_OK(cudaFuncSetAttribute(attn_tc_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * 2 * PF_CH * (HD + 8) * 2 + PF_ROWS * (HD + 4) * 4));
+    CUDA_OK(cudaFuncSetAttribute(attn_tc_prefill_kernel<HD, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PF_SMEM_MAX));
     configured = true;
   }
   const int qt = PF_ROWS / p.group;
-  launch_k(attn_tc_prefill_kernel<HD>, dim3(1, (unsigned)((p.Sq + qt - 1) / qt), (unsigned)(p.B * p.nkv)), dim3(256),
-           dyn, s, 1, p, argtab);
+  launch_k(attn_tc_prefill_kernel<HD, FAST>, dim3(1, (unsigned)((p.Sq + qt - 1) / qt), (unsigned)(p.B * p.nkv)),
+           dim3(256), prefill_smem(p, FAST), s, 1, p, argtab);
+}
+
+template <int HD>
+void launch_tc_prefill(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (prefill_fast(p)) launch_tc_prefill_t<HD, true>(p, argtab, s);
+  else launch_tc_prefill_t<HD, false>(p, argtab, s);
 }
 
 template <int HD>
@@ -1291,6 +1439,7 @@ void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t 
 bool attention_tc_prefill_ok(const AttnParams& p) {
   if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || !(p.q.dt == KDT_BF16 || p.q.dt == KDT_F32)) return false;
   if (!(p.group == 1 || p.group == 2 || p.group == 4 || p.group == 8)) return false;
+  if (p.T > PF_LIVE_WORDS * 32 * PF_CH || prefill_smem(p, false) > PF_SMEM_MAX) return false;
   return smem_ok(p);
 }
 

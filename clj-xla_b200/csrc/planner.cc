@@ -1462,6 +1462,11 @@ void Planner::emit_attention(int d2) {
   int splits = (int)std::min<int64_t>((P.T + per_split - 1) / per_split, std::max<int64_t>(1, 2 * 148 / ctas));
   splits = std::max(1, std::min(splits, ATTN_MERGE_MAX_SPLITS));
   if (P.use_tc == 2) splits = 1;  // whole rows per CTA
+  if (getenv("CLJXLA_B200_DEBUG_ATTN"))
+    fprintf(stderr, "attention %s: Sq %d T %d use_tc %d chain_kind %d chain_dt %d mask dt %d off %lld strides %lld %lld %lld %lld\n",
+            D2.name.c_str(), P.Sq, P.T, P.use_tc, P.chain_kind, P.chain_dt, P.mask.dt, (long long)P.mask.p.off,
+            (long long)P.mask.stride[0], (long long)P.mask.stride[1], (long long)P.mask.stride[2],
+            (long long)P.mask.stride[3]);
   P.splits = splits;
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
