@@ -986,8 +986,10 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 // 64-position chunks holding any position above mask_skip (the causal upper
 // triangle and positions outside a sliding window drop out); only those are
 // staged, K / V with cp.async, double-buffered.  Tiles are issued longest
-// first (the last query positions see the most chunks).  P enters P V as
-// bf16 hi + lo, f32 queries as an exact hi + mid + lo split.
+// first (the last query positions see the most chunks).  K (with the mask
+// tile) is double-buffered; V has one buffer, restaged after each P V so that
+// an f32 query tile still fits beside the K, V and mask tiles at head_dim 256.
+// P enters P V as bf16 hi + lo, f32 queries as an exact hi + mid + lo split.
 //
 // FAST: the additive mask is f32 with 16-byte aligned rows and the score
 // chain has a closed form with f32 softmax arithmetic (the printed Gemma and
@@ -1010,8 +1012,8 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   constexpr int NTO = HD / 16;          // 8-dim output tiles per warp (half of head_dim)
   extern __shared__ __align__(16) unsigned char pf_smem[];
   uint16_t* Kb = (uint16_t*)pf_smem;                    // [2][PF_CH][ROW]
-  uint16_t* Vb = Kb + 2 * PF_CH * ROW;                  // [2][PF_CH][ROW]
-  float* Ms = (float*)(Vb + 2 * PF_CH * ROW);           // FAST: [2][PF_ROWS][PF_MROW]
+  uint16_t* Vb = Kb + 2 * PF_CH * ROW;                  // [PF_CH][ROW]
+  float* Ms = (float*)(Vb + PF_CH * ROW);               // FAST: [2][PF_ROWS][PF_MROW]
   unsigned char* Qs = (unsigned char*)(Ms + (FAST ? 2 * PF_ROWS * PF_MROW : 0));  // bf16 [64][ROW] / f32 [64][QROWF]
   __shared__ int64_t qoff_s[PF_ROWS], moff_s[PF_ROWS];
   __shared__ unsigned live_s[PF_LIVE_WORDS];
@@ -1098,20 +1100,26 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
     }
     return nchunks;
   };
+  constexpr int SEGS = HD / 8;
+  // V rows of a chunk into the single V buffer (one cp.async group)
+  auto stage_v = [&](int ch) {
+    const int64_t c0 = (int64_t)ch * PF_CH;
+    for (int q = threadIdx.x; q < PF_CH * SEGS; q += 256) {
+      const int rr = q / SEGS, sg = q % SEGS;
+      uint16_t* vd = Vb + (size_t)rr * ROW + sg * 8;
+      if (c0 + rr < P.T) cp_async16(vd, vbase + (c0 + rr) * P.v.stride[2] + sg * 8);
+      else *(uint4*)vd = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  // K rows and (FAST) the mask tile of a chunk into K buffer buf (one group)
   auto stage = [&](int ch, int buf) {
     const int64_t c0 = (int64_t)ch * PF_CH;
-    constexpr int SEGS = HD / 8;
     for (int q = threadIdx.x; q < PF_CH * SEGS; q += 256) {
       const int rr = q / SEGS, sg = q % SEGS;
       uint16_t* kd = Kb + ((size_t)buf * PF_CH + rr) * ROW + sg * 8;
-      uint16_t* vd = Vb + ((size_t)buf * PF_CH + rr) * ROW + sg * 8;
-      if (c0 + rr < P.T) {
-        cp_async16(kd, kbase + (c0 + rr) * P.k.stride[2] + sg * 8);
-        cp_async16(vd, vbase + (c0 + rr) * P.v.stride[2] + sg * 8);
-      } else {
-        *(uint4*)kd = make_uint4(0, 0, 0, 0);
-        *(uint4*)vd = make_uint4(0, 0, 0, 0);
-      }
+      if (c0 + rr < P.T) cp_async16(kd, kbase + (c0 + rr) * P.k.stride[2] + sg * 8);
+      else *(uint4*)kd = make_uint4(0, 0, 0, 0);
     }
     if (FAST) {  // the chunk's mask tile; -inf past T and in rows past nrows
       for (int q = threadIdx.x; q < PF_ROWS * 16; q += 256) {
@@ -1135,17 +1143,22 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
     for (int i = 0; i < 4; ++i) o[n][i] = 0.f;
   const uint32_t kb_s = (uint32_t)__cvta_generic_to_shared(Kb), vb_s = (uint32_t)__cvta_generic_to_shared(Vb);
   const int rA = 16 * rg + g, rB = rA + 8;  // this thread's two rows
+  // cp.async groups in commit order: K(ch) V(ch) K(nx) V(nx) ...; the K group of
+  // a chunk is waited for before its scores, its V group before its P V
   int ch = next_live(0);
-  if (ch < nchunks) stage(ch, 0);
+  if (ch < nchunks) {
+    stage(ch, 0);
+    stage_v(ch);
+  }
   __syncthreads();  // Q in shared memory
   int buf = 0;
   while (ch < nchunks) {
     const int nx = next_live(ch + 1);
     if (nx < nchunks) {
       stage(nx, buf ^ 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
+      asm volatile("cp.async.wait_group 2;" ::: "memory");
     } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
     }
     __syncthreads();
     const int64_t c = (int64_t)ch * PF_CH;
@@ -1258,6 +1271,10 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         m[hr] = mnew;
       }
     }
+    // this chunk's V rows
+    if (nx < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
     // O[:, half] += P V: 4 k-steps of 16 positions, P as bf16 hi + lo
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
@@ -1272,14 +1289,15 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
 #pragma unroll
       for (int n = 0; n < NTO; n += 2) {
         uint32_t bf[4];
-        ldsm_x4_t(vb_s + (uint32_t)((((size_t)buf * PF_CH + 16 * ks + ri + 8 * (mi & 1)) * ROW + dh * (HD / 2) + 8 * n + 8 * (mi >> 1)) * 2), bf);
+        ldsm_x4_t(vb_s + (uint32_t)((((size_t)16 * ks + ri + 8 * (mi & 1)) * ROW + dh * (HD / 2) + 8 * n + 8 * (mi >> 1)) * 2), bf);
         mma_bf16(o[n], ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
         mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
         mma_bf16(o[n + 1], ah[0], ah[1], ah[2], ah[3], bf[2], bf[3]);
         mma_bf16(o[n + 1], al[0], al[1], al[2], al[3], bf[2], bf[3]);
       }
     }
-    __syncthreads();  // this buffer is restaged by the next iteration
+    __syncthreads();  // this K buffer and the V buffer are restaged from here on
+    if (nx < nchunks) stage_v(nx);
     ch = nx;
     buf ^= 1;
   }
@@ -1306,7 +1324,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
 // dynamic shared memory of the prefill kernel
 int prefill_smem(const AttnParams& p, bool fast) {
   const int qbytes = p.q.dt == KDT_F32 ? PF_ROWS * (p.hd + 4) * 4 : PF_ROWS * (p.hd + 8) * 2;
-  return 2 * 2 * PF_CH * (p.hd + 8) * 2 + (fast ? 2 * PF_ROWS * PF_MROW * 4 : 0) + qbytes;
+  return 3 * PF_CH * (p.hd + 8) * 2 + (fast ? 2 * PF_ROWS * PF_MROW * 4 : 0) + qbytes;
 }
 constexpr int PF_SMEM_MAX = 227 * 1024 - 2048;  // the opt-in limit less the static shared memory
 

@@ -67,7 +67,18 @@ def test_attention_prefill_simt_path(ctx, monkeypatch, Sq, T, nq, nkv, window, h
         core.clear_cache()
 
 
-def _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
+@pytest.mark.parametrize("Sq,T,nq,nkv,window,hd", [
+    (130, 192, 8, 4, None, 256),
+    (100, 128, 4, 2, 40, 128),
+])
+def test_attention_prefill_f32_queries(ctx, Sq, T, nq, nkv, window, hd):
+    """f32 queries (the Gemma-3 prefill: RoPE in f32 feeds the score product):
+    three exact bf16 parts on the tensor cores, the f32 tile in shared memory
+    beside the K, V and mask tiles."""
+    _check_attention(ctx, Sq, T, nq, nkv, None, window, True, hd, 0, qdt="f32")
+
+
+def _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos, qdt="bf16"):
     B = 1
 
     def f(q, k, v, kc, vc, ow, pos):
@@ -75,7 +86,7 @@ def _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
         out, updated = nn.gqa_causal_attention(q, k, v, ow, nq, nkv, softcap, [kc, vc], p,
                                                {"scale": 0.125, "sliding-window": window})
         return [out, updated[0], updated[1]]
-    g = t.trace_graph("attn", [("q", ("tensor", (B, Sq, nq * hd), "bf16")), ("k", ("tensor", (B, Sq, nkv * hd), "bf16")),
+    g = t.trace_graph("attn", [("q", ("tensor", (B, Sq, nq * hd), qdt)), ("k", ("tensor", (B, Sq, nkv * hd), "bf16")),
                                ("v", ("tensor", (B, Sq, nkv * hd), "bf16")),
                                ("kc", ("tensor", (B, nkv, T, hd), "bf16")), ("vc", ("tensor", (B, nkv, T, hd), "bf16")),
                                ("ow", ("tensor", (nq * hd, nq * hd), "bf16")), ("pos", ("tensor", (1,), "i32"))], f)
@@ -83,7 +94,10 @@ def _check_attention(ctx, Sq, T, nq, nkv, softcap, window, dynamic, hd, pos):
     if pos is None:
         pos = min(T - Sq, 3)
     pos = np.array([pos], np.int32) if dynamic else np.array([0], np.int32)
-    inputs = [_rand((B, Sq, nq * hd), 1), _rand((B, Sq, nkv * hd), 2), _rand((B, Sq, nkv * hd), 3),
+    q_in = _rand((B, Sq, nq * hd), 1)
+    if qdt == "f32":
+        q_in = np.random.Generator(np.random.PCG64(11)).standard_normal((B, Sq, nq * hd)).astype(np.float32)
+    inputs = [q_in, _rand((B, Sq, nkv * hd), 2), _rand((B, Sq, nkv * hd), 3),
               _rand((B, nkv, T, hd), 4), _rand((B, nkv, T, hd), 5), _rand((nq * hd, nq * hd), 6, 0.05), pos]
     want = interp.run_mlir(text, inputs)
     got = runner.run_graph(ctx, g, inputs, text)
