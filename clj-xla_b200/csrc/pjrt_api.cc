@@ -202,6 +202,7 @@ PJRT_Error* Client_Destroy(void* a) {
     cudaStreamSynchronize(args->client->stream);
     nccl_comm_destroy(args->client->nccl_comm);
     cudaStreamDestroy(args->client->stream);
+    if (args->client->pinned) cudaFreeHost(args->client->pinned);
     delete args->client;
   });
 }
@@ -341,8 +342,24 @@ PJRT_Error* Buffer_ToHostBuffer(void* a) {
     // the reference host always passes numel*4 bytes (pjrt.clj:535) and reads
     // what it needs; copy the buffer's bytes, never more than dst_size
     size_t n = std::min(b->bytes, args->dst_size);
-    if (n) CUDA_OK(cudaMemcpyAsync(args->dst, b->ptr(), n, cudaMemcpyDeviceToHost, b->client->stream));
-    CUDA_OK(cudaStreamSynchronize(b->client->stream));
+    PJRT_Client* c = b->client;
+    if (n >= (64u << 10)) {
+      // large reads (decode logits): DMA into pinned staging, then one host copy;
+      // a copy into pageable memory goes through the driver's smaller bounce buffer
+      if (c->pinned_bytes < n) {
+        if (c->pinned) CUDA_OK(cudaFreeHost(c->pinned));
+        c->pinned = nullptr;
+        c->pinned_bytes = 0;
+        CUDA_OK(cudaMallocHost(&c->pinned, n));
+        c->pinned_bytes = n;
+      }
+      CUDA_OK(cudaMemcpyAsync(c->pinned, b->ptr(), n, cudaMemcpyDeviceToHost, c->stream));
+      CUDA_OK(cudaStreamSynchronize(c->stream));
+      memcpy(args->dst, c->pinned, n);
+    } else {
+      if (n) CUDA_OK(cudaMemcpyAsync(args->dst, b->ptr(), n, cudaMemcpyDeviceToHost, c->stream));
+      CUDA_OK(cudaStreamSynchronize(c->stream));
+    }
     args->event = nullptr;
   });
 }

@@ -118,6 +118,9 @@ struct PJRT_Client {
   PJRT_Device* device_list[1] = {&device};
   cudaStream_t stream = nullptr;
   std::mutex mu;
+  // pinned staging for large device-to-host reads (grown on demand)
+  void* pinned = nullptr;
+  size_t pinned_bytes = 0;
   std::string platform = "cuda";
   void* nccl_comm = nullptr;  // tp_size > 1
 };
