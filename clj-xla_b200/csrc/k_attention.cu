@@ -980,9 +980,11 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 // f32).  One CTA per (batch * kv head, 64 query vectors): query vector
 // r = qi * group + gi of the tile's query positions, so the GQA group shares
 // every staged K/V row.  8 warps: warp w owns rows 16 (w & 3) .. + 15 and
-// half (w >> 2) of head_dim; the two warps of a row group compute the same
-// scores (S = Q K^T over a 64-position chunk), so their online-softmax state
-// agrees without exchange.  One pass over the CTA's mask rows first marks the
+// half (w >> 2) of head_dim.  The two warps of a row group share its
+// rows; each scores half of a 64-position chunk (S = Q K^T), they exchange
+// their row maxima and P fragments through shared memory (a 64-thread named
+// barrier per pair), and apply the same rescaling, so their online-softmax
+// states agree.  One pass over the CTA's mask rows first marks the
 // 64-position chunks holding any position above mask_skip (the causal upper
 // triangle and positions outside a sliding window drop out); only those are
 // staged, K / V with cp.async, double-buffered.  Tiles are issued longest
@@ -1003,6 +1005,9 @@ constexpr int PF_LIVE_WORDS = 32;   // live-chunk bitmap: T <= 32 * 32 * 64 posi
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// the two warps (64 threads) of row group rg: named barrier 1 + rg
+__device__ __forceinline__ void pair_sync(int rg) { asm volatile("bar.sync %0, 64;" ::"r"(1 + rg) : "memory"); }
+
 template <int HD, bool FAST>
 __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_constant__ AttnParams P,
                                                                  const uint64_t* __restrict__ argtab) {
@@ -1017,6 +1022,8 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   unsigned char* Qs = (unsigned char*)(Ms + (FAST ? 2 * PF_ROWS * PF_MROW : 0));  // bf16 [64][ROW] / f32 [64][QROWF]
   __shared__ int64_t qoff_s[PF_ROWS], moff_s[PF_ROWS];
   __shared__ unsigned live_s[PF_LIVE_WORDS];
+  __shared__ float pm_s[2][PF_ROWS];                  // per-half row maxima (then sums)
+  __shared__ uint32_t pf_s[4][2][2][8][32];           // P fragments [row group][half][k-step][reg][lane]
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rg = warp & 3, dh = warp >> 2;
@@ -1162,10 +1169,11 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
     }
     __syncthreads();
     const int64_t c = (int64_t)ch * PF_CH;
-    // scores of this warp's 16 rows over the chunk: 8 tiles of 8 positions
-    float sc[8][4];
+    // scores of this warp's 16 rows over its half of the chunk: tiles
+    // 4 dh .. 4 dh + 3 of 8 positions (the partner warp scores the other half)
+    float sc[4][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) sc[n][i] = 0.f;
     const int mi = lane >> 3, ri = lane & 7;
@@ -1199,24 +1207,25 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
             qf[i][1] -= bf16_hi_f(a[i]);
           }
 #pragma unroll
-        for (int n = 0; n < 8; n += 2) {
+        for (int n = 0; n < 4; n += 2) {
           uint32_t bf[4];
-          ldsm_x4(kb_s + (uint32_t)((((size_t)buf * PF_CH + 8 * n + ri + 8 * (mi >> 1)) * ROW + 16 * kk + 8 * (mi & 1)) * 2), bf);
+          ldsm_x4(kb_s + (uint32_t)((((size_t)buf * PF_CH + 8 * (4 * dh + n) + ri + 8 * (mi >> 1)) * ROW + 16 * kk + 8 * (mi & 1)) * 2), bf);
           mma_bf16(sc[n], a[0], a[1], a[2], a[3], bf[0], bf[1]);
           mma_bf16(sc[n + 1], a[0], a[1], a[2], a[3], bf[2], bf[3]);
         }
       }
     }
-    // chain, mask, online softmax per row (rows rA: elements 0, 1; rB: 2, 3)
-    float pv[8][4];
+    // chain and mask (rows rA: elements 0, 1; rB: 2, 3), this half's row maxima
+    float mxr[2];
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
       const int r = hr ? rB : rA;
       float mx = -INFINITY;
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+      for (int n = 0; n < 4; ++n) {
+        const int tile = 4 * dh + n;
         if (FAST) {
-          const float2 mk2 = *(const float2*)(Ms + ((size_t)buf * PF_ROWS + r) * PF_MROW + 8 * n + 2 * t);
+          const float2 mk2 = *(const float2*)(Ms + ((size_t)buf * PF_ROWS + r) * PF_MROW + 8 * tile + 2 * t);
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const float mk = e ? mk2.y : mk2.x;
@@ -1233,7 +1242,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         } else {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int64_t j = c + 8 * n + 2 * t + e;
+            const int64_t j = c + 8 * tile + 2 * t + e;
             float v = -INFINITY;
             if (r < nrows && j < P.T) {
               const float mk = ld_any(mb, moff_s[r] + j * ms3, P.mask.dt);
@@ -1246,10 +1255,24 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float mnew = fmaxf(m[hr], mx);
+      mxr[hr] = mx;
+    }
+    // the chunk's row maxima: this half's and the partner's, the same in both warps
+    if (t == 0) {
+      pm_s[dh][rA] = mxr[0];
+      pm_s[dh][rB] = mxr[1];
+    }
+    pair_sync(rg);
+    mxr[0] = fmaxf(mxr[0], pm_s[dh ^ 1][rA]);
+    mxr[1] = fmaxf(mxr[1], pm_s[dh ^ 1][rB]);
+    // online softmax: both warps apply the same maxima, each keeps the sum of its half
+    float pv[4][4];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const float mnew = fmaxf(m[hr], mxr[hr]);
       float ps = 0.f;
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = sc[n][2 * hr + e];
@@ -1271,7 +1294,21 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         m[hr] = mnew;
       }
     }
-    // this chunk's V rows
+    // P of this half as bf16 hi + lo A fragments (k-steps 2 dh, 2 dh + 1), kept
+    // in registers and published to the partner through shared memory
+    uint32_t pa[2][8];
+#pragma unroll
+    for (int kl = 0; kl < 2; ++kl)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tile = 2 * kl + (i >> 1), hr = i & 1;
+        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
+        pa[kl][i] = pack_bf16(p0, p1);
+        pa[kl][4 + i] = pack_bf16(p0 - bf16_lo_f(pa[kl][i]), p1 - bf16_hi_f(pa[kl][i]));
+        pf_s[rg][dh][kl][i][lane] = pa[kl][i];
+        pf_s[rg][dh][kl][4 + i][lane] = pa[kl][4 + i];
+      }
+    // this chunk's V rows (the barrier also publishes the P fragments)
     if (nx < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
     else asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
@@ -1279,12 +1316,13 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       uint32_t ah[4], al[4];
+      const int kl = ks & 1;
+      if ((ks >> 1) == dh) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int tile = 2 * ks + (i >> 1), hr = i & 1;
-        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
-        ah[i] = pack_bf16(p0, p1);
-        al[i] = pack_bf16(p0 - bf16_lo_f(ah[i]), p1 - bf16_hi_f(ah[i]));
+        for (int i = 0; i < 4; ++i) ah[i] = pa[kl][i], al[i] = pa[kl][4 + i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ah[i] = pf_s[rg][dh ^ 1][kl][i][lane], al[i] = pf_s[rg][dh ^ 1][kl][4 + i][lane];
       }
 #pragma unroll
       for (int n = 0; n < NTO; n += 2) {
@@ -1301,7 +1339,14 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
     ch = nx;
     buf ^= 1;
   }
-  // out = O / l for this warp's rows and half of head_dim
+  // out = O / l for this warp's rows and half of head_dim; l sums both halves
+  if (t == 0) {
+    pm_s[dh][rA] = l[0];
+    pm_s[dh][rB] = l[1];
+  }
+  pair_sync(rg);
+  l[0] += pm_s[dh ^ 1][rA];
+  l[1] += pm_s[dh ^ 1][rB];
   char* ob = dres(P.out, argtab);
 #pragma unroll
   for (int hr = 0; hr < 2; ++hr) {
@@ -1326,7 +1371,7 @@ int prefill_smem(const AttnParams& p, bool fast) {
   const int qbytes = p.q.dt == KDT_F32 ? PF_ROWS * (p.hd + 4) * 4 : PF_ROWS * (p.hd + 8) * 2;
   return 3 * PF_CH * (p.hd + 8) * 2 + (fast ? 2 * PF_ROWS * PF_MROW * 4 : 0) + qbytes;
 }
-constexpr int PF_SMEM_MAX = 227 * 1024 - 2048;  // the opt-in limit less the static shared memory
+constexpr int PF_SMEM_MAX = 227 * 1024 - 20 * 1024;  // the opt-in limit less the static shared memory
 
 // the specialised form applies: f32 mask with 16-byte aligned rows, f32
 // softmax arithmetic, a closed-form chain, and the mask tiles fit
