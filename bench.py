@@ -188,6 +188,8 @@ def run_ours(args, rank, world, local_rank):
         from cljxla_b200.host import tp as tpmod
         ctx = core.init_tp_backend(args.tp, rank % args.tp, tpmod.share_nccl_id(pkg.LIB_PATH), local_rank,
                                    pkg.LIB_PATH)
+        if os.environ.get("CLJXLA_B200_P2P", "1") != "0":
+            tpmod.setup_p2p(ctx)  # small all_reduce ops: one-shot kernel over NVLink peer memory
     else:
         ctx = core.init_backend(pkg.LIB_PATH, {"device": local_rank})
     api, client = ctx["api"], ctx["client"]

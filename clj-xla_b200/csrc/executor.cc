@@ -100,6 +100,7 @@ namespace {
 // the collective context of the executable being launched on this thread
 struct CollectiveCtx {
   void* comm = nullptr;
+  P2PAllReduce* p2p = nullptr;
   int ranks = 1;
   const uint64_t* host_argtab = nullptr;
 };
@@ -116,7 +117,8 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
                           std::to_string(g_coll.ranks));
     const char* src = (const char*)(uintptr_t)(g_coll.host_argtab[a.src.slot] + (uint64_t)a.src.off);
     char* dst = (char*)(uintptr_t)(g_coll.host_argtab[a.dst.slot] + (uint64_t)a.dst.off);
-    nccl_all_reduce_sum(src, dst, (size_t)a.count, a.dt, g_coll.comm, s);
+    if (g_coll.p2p && g_coll.p2p->fits(a.count, a.dt)) g_coll.p2p->run(src, dst, a.count, a.dt, s);
+    else nccl_all_reduce_sum(src, dst, (size_t)a.count, a.dt, g_coll.comm, s);
     return;
   }
   if (l.jit_fn) {
@@ -244,7 +246,9 @@ void run_variant(PJRT_Client* c, ExecVariant& v, cudaStream_t s) {
   // pageable source: the driver stages it before returning, so h_argtab can be reused
   if (dyn) CUDA_OK(cudaMemcpyAsync(v.d_argtab, v.h_argtab.data(), dyn, cudaMemcpyHostToDevice, s));
   refresh_tmaps(v, s);
+  if (c->p2p) c->p2p->check();
   g_coll.comm = c->nccl_comm;
+  g_coll.p2p = c->p2p;
   g_coll.ranks = c->opt.tp_size;
   g_coll.host_argtab = v.h_argtab.data();
   if (profile_state().enabled) {

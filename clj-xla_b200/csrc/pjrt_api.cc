@@ -200,6 +200,8 @@ PJRT_Error* Client_Destroy(void* a) {
     if (!args->client) return;
     set_device(args->client);
     cudaStreamSynchronize(args->client->stream);
+    delete args->client->p2p;
+    args->client->p2p = nullptr;
     nccl_comm_destroy(args->client->nccl_comm);
     cudaStreamDestroy(args->client->stream);
     if (args->client->pinned) cudaFreeHost(args->client->pinned);
@@ -511,6 +513,39 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
     return e.code;
   } catch (const std::exception& e) {
     if (err && errcap) snprintf(err, errcap, "%s", e.what());
+    return E_INTERNAL;
+  }
+}
+
+CLJXLA_EXPORT int cljxla_b200_p2p_export(void* client, int64_t slot_bytes, char* out, size_t cap) {
+  try {
+    auto* c = (PJRT_Client*)client;
+    if (!c || c->opt.tp_size < 2) return E_INVALID;
+    std::lock_guard<std::mutex> lk(c->mu);
+    set_device(c);
+    if (!c->p2p) c->p2p = new P2PAllReduce();
+    std::string h = c->p2p->export_handle(c->opt.tp_size, c->opt.tp_rank, slot_bytes);
+    if (!out || cap < h.size() + 1) return E_INVALID;
+    memcpy(out, h.c_str(), h.size() + 1);
+    return 0;
+  } catch (const Error& e) {
+    return e.code;
+  } catch (...) {
+    return E_INTERNAL;
+  }
+}
+
+CLJXLA_EXPORT int cljxla_b200_p2p_import(void* client, const char* handles, size_t len) {
+  try {
+    auto* c = (PJRT_Client*)client;
+    if (!c || !c->p2p || !handles) return E_INVALID;
+    std::lock_guard<std::mutex> lk(c->mu);
+    set_device(c);
+    c->p2p->import_handles(std::string(handles, len));
+    return 0;
+  } catch (const Error& e) {
+    return e.code;
+  } catch (...) {
     return E_INTERNAL;
   }
 }

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "ir.h"
+#include "nccl_rt.h"
 #include "planner.h"
 
 struct PJRT_Error {
@@ -123,6 +124,7 @@ struct PJRT_Client {
   size_t pinned_bytes = 0;
   std::string platform = "cuda";
   void* nccl_comm = nullptr;  // tp_size > 1
+  cljxla::P2PAllReduce* p2p = nullptr;  // one-shot peer all-reduce, once its handles are exchanged
 };
 
 namespace cljxla {

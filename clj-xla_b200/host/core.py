@@ -204,6 +204,30 @@ def init_tp_backend(tp_size: int, tp_rank: int, nccl_id: str, device: Optional[i
     return init_backend(target, opts)
 
 
+def p2p_export(ctx: Context, slot_bytes: int = 32 << 10) -> str:
+    """This rank's exchange-buffer handle for the one-shot peer all-reduce."""
+    f = _lib(ctx).cljxla_b200_p2p_export
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_char_p, ctypes.c_size_t]
+    f.restype = ctypes.c_int
+    out = ctypes.create_string_buffer(256)
+    rc = f(ctypes.c_void_p(ctx["client"]), int(slot_bytes), out, 256)
+    if rc != 0:
+        raise RuntimeError(f"cljxla_b200_p2p_export failed ({rc})")
+    return out.value.decode()
+
+
+def p2p_import(ctx: Context, handles: Sequence[str]):
+    """Maps every rank's exchange buffer (handles in rank order); from here on
+    small all_reduce ops run as the one-shot peer kernel."""
+    f = _lib(ctx).cljxla_b200_p2p_import
+    f.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]
+    f.restype = ctypes.c_int
+    b = "".join(handles).encode()
+    rc = f(ctypes.c_void_p(ctx["client"]), b, len(b))
+    if rc != 0:
+        raise RuntimeError(f"cljxla_b200_p2p_import failed ({rc})")
+
+
 def plan_text(lib_path: str, text: str, fuse: bool = True) -> dict:
     """Host-only parse+plan through the library (no device needed)."""
     lib = ctypes.CDLL(lib_path)

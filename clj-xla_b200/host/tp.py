@@ -38,6 +38,15 @@ def share_nccl_id(lib_path: Optional[str] = None) -> str:
     return obj[0]
 
 
+def setup_p2p(ctx: core.Context, slot_bytes: int = 32 << 10):
+    """Switches the group's small all_reduce ops to the one-shot peer kernel:
+    handles exchanged over the default torch.distributed group (a collective)."""
+    import torch.distributed as dist
+    hs = [None] * dist.get_world_size()
+    dist.all_gather_object(hs, core.p2p_export(ctx, slot_bytes))
+    core.p2p_import(ctx, hs)
+
+
 def join_group(device: Optional[int] = None, lib_path: Optional[str] = None) -> core.Context:
     """Client of this process's rank in a group spanning the default
     torch.distributed group (a collective: every rank calls it)."""

@@ -79,6 +79,19 @@ CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags,
  * host.  Returns 0 or a PJRT_Error_Code (9: NCCL could not be loaded). */
 CLJXLA_EXPORT int cljxla_b200_nccl_unique_id(char* out, size_t cap);
 
+/* One-shot all-reduce over NVLink peer memory for tensor-parallel clients (no
+ * counterpart in the reference).  Once every rank of a group has called
+ * cljxla_b200_p2p_export (a CUDA IPC handle of a new exchange buffer with two
+ * phases of one slot_bytes slot per rank, as hex: 128 characters + NUL into
+ * out[cap]) and then cljxla_b200_p2p_import with all ranks' handles
+ * concatenated in rank order, every all_reduce of at most slot_bytes (f32 or
+ * bf16, 16-byte multiple) runs as one kernel per rank that stores its operand
+ * into every rank's buffer, waits (bounded, about 16 s) for the others and
+ * sums in rank order; larger ones stay on NCCL.  A wait that runs out makes
+ * the client's next execution fail.  `client` is the PJRT_Client*. */
+CLJXLA_EXPORT int cljxla_b200_p2p_export(void* client, int64_t slot_bytes, char* out, size_t cap);
+CLJXLA_EXPORT int cljxla_b200_p2p_import(void* client, const char* handles, size_t len);
+
 /* The cudaStream_t a client launches on (for event timing by the caller). */
 CLJXLA_EXPORT void* cljxla_b200_stream(const PJRT_Client* client);
 

@@ -28,9 +28,12 @@ def _gpu_count():
         return 0
 
 
-def _rank(rank, world, nid, cfg_full, prompt, T, steps, q):
+def _rank(rank, world, nid, cfg_full, prompt, T, steps, q, hq=None, hin=None):
     try:
         ctx = core.init_tp_backend(world, rank, nid, device=rank)
+        if hq is not None:  # one-shot peer all-reduce: handles through the parent
+            hq.put((rank, core.p2p_export(ctx)))
+            core.p2p_import(ctx, hin.get(timeout=300))
         cfg, gp, gd = tp.shard_graphs(cfg_full, world, prompt.shape[0], prompt.shape[1], T)
         w = d.shard_weights(cfg_full, d.make_weights(cfg_full), rank, world)
         toks, logits = tp.greedy_generate(ctx, cfg, gp, gd, w, prompt, T, steps)
@@ -40,15 +43,22 @@ def _rank(rank, world, nid, cfg_full, prompt, T, steps, q):
         q.put((rank, None, None, repr(e)))
 
 
-def _run_group(cfg_full, world, prompt, T, steps):
+def _run_group(cfg_full, world, prompt, T, steps, p2p=False):
     nid = core.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, cfg_full, prompt, T, steps, q)) for r in range(world)]
+    hq = ctx.Queue() if p2p else None
+    hins = [ctx.Queue() for _ in range(world)] if p2p else [None] * world
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, cfg_full, prompt, T, steps, q, hq, hins[r]))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
     try:
+        if p2p:
+            hs = dict(hq.get(timeout=300) for _ in range(world))
+            for hin in hins:
+                hin.put([hs[r] for r in range(world)])
         for _ in range(world):
             r, toks, logits, err = q.get(timeout=600)
             assert err is None, f"rank {r}: {err}"
@@ -62,13 +72,15 @@ def _run_group(cfg_full, world, prompt, T, steps):
 
 
 @pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_tp2_greedy_decode_matches_oracle(dtype):
+@pytest.mark.parametrize("dtype,p2p", [("f32", False), ("bf16", False), ("f32", True), ("bf16", True)])
+def test_tp2_greedy_decode_matches_oracle(dtype, p2p):
+    """2-rank decode against the sharded oracle, the all_reduce ops on NCCL or
+    (p2p) on the one-shot kernel over NVLink peer memory (rank-order sum)."""
     cfg = dataclasses.replace(TINY3, dtype=dtype)
     B, S, T, steps = 1, 6, 32, 12
     prompt = d.make_prompt(cfg, B, S)
     w = d.make_weights(cfg)
-    res = _run_group(cfg, 2, prompt, T, steps)
+    res = _run_group(cfg, 2, prompt, T, steps, p2p)
     o_toks, o_logits = tp.oracle_generate(cfg, 2, w, prompt, T, steps, interp.run_mlir_tp, interp.run_mlir)
     # every rank holds the same all-reduced logits and picks the same tokens
     assert res[0][0] == res[1][0]
