@@ -322,7 +322,7 @@ void fuse_dus_into_producers(Plan& p) {
 // [M, K], x's type), x fits in shared memory, and no launch between the two
 // touches what the producer reads or writes (so the producer may run at the
 // GEMV's place).
-void fuse_gemv_prologues(Plan& p) {
+void fuse_gemv_prologues(Plan& p, bool ew_only) {
   std::vector<Launch>& L = p.launches;
   for (size_t i = 0; i < L.size(); ++i) {
     if (L[i].kind != K_GEMV) continue;
@@ -353,7 +353,7 @@ void fuse_gemv_prologues(Plan& p) {
     if (j < 0) continue;
     const Launch& pro = L[j];
     int out = -1, nbuf = 0;
-    if (pro.kind == K_ROWNORM) {
+    if (pro.kind == K_ROWNORM && !ew_only) {
       const RowParams& r = *(const RowParams*)pro.blob.data();
       if (r.rows != G.M || r.C != G.K) continue;
       for (int o = 0; o < r.nout; ++o)
@@ -398,7 +398,7 @@ void schedule_and_merge(Plan& p) {
   // before its first stage cost more (4.14 ms / step) than the separate small
   // kernel whose latency the GEMV's early weight stream hides (3.37 ms / step)
   if (const char* e = getenv("CLJXLA_B200_GEMV_PROLOGUE"))
-    if (e[0] == '1') fuse_gemv_prologues(p);
+    if (e[0] == '1' || e[0] == '2') fuse_gemv_prologues(p, e[0] == '2');  // 2: elementwise producers only
   const int n = (int)p.launches.size();
   if (n < 2) return;
   std::vector<std::vector<Access>> acc(n);
