@@ -88,82 +88,93 @@ extern "C" CLJXLA_EXPORT int cljxla_b200_attention_decode_static(const void* q, 
   if ((uintptr_t)k_cache % vec_bytes || (uintptr_t)v_cache % vec_bytes)
     return put_err(err, errcap, E_INVALID, "attention_decode_static: K/V caches must be aligned to head_dim/16 bytes");
 
-  AttnParams P{};
-  P.B = (int32_t)batch;
-  P.nq = (int32_t)q_heads;
-  P.nkv = (int32_t)kv_heads;
-  P.Sq = 1;
-  P.T = (int32_t)positions;
-  P.hd = (int32_t)head_dim;
-  P.group = (int32_t)(q_heads / kv_heads);
-  P.qtile = 1;
-  P.q = dense4(q, KDT_BF16, batch, q_heads, 1, head_dim);
-  P.k = dense4(k_cache, KDT_BF16, batch, kv_heads, positions, head_dim);
-  P.v = dense4(v_cache, KDT_BF16, batch, kv_heads, positions, head_dim);
-  P.mask = dense4(mask, KDT_F32, batch, q_heads, 1, positions);
-  P.mask.stride[0] = P.mask.stride[1] = P.mask.stride[2] = 0;  // one additive row shared by all heads
-  P.k_dt = KDT_BF16;
-  // printed attention.clj:343-365 with a bf16 model: q.k^T rounded to bf16,
-  // times the bf16 scale constant (rounded to bf16), + f32 mask, f32 softmax
-  P.dt_d1 = KDT_BF16;
-  P.dt_m = P.dt_sub = P.dt_exp = KDT_F32;
-  P.out_dt = KDT_F32;
-  P.mask_skip = -5000.0f;
-  EwInstr imm{};
-  imm.op = EW_IMM;
-  imm.dt = (uint8_t)KDT_F32;
-  imm.dst = 1;
-  imm.fimm = bf16_to_f32(f32_to_bf16(scale));
-  EwInstr mul{};
-  mul.op = EW_MUL;
-  mul.dt = (uint8_t)KDT_BF16;
-  mul.a = 0;
-  mul.b = 1;
-  mul.dst = 2;
-  P.chain[0] = imm;
-  P.chain[1] = mul;
-  P.nchain = 2;
-  P.chain_out = 2;
-  P.chain_kind = 1;  // the same multiply in closed form
-  P.chain_c = imm.fimm;
-  P.chain_dt = KDT_BF16;
-  P.out.slot = -1;
-  P.out.off = (int64_t)(uintptr_t)out;
-  // same split rule as the planner: enough CTAs for two waves, >= 64 positions per split
-  const int64_t ctas = batch * kv_heads;
-  int splits = 1;
-  while (ctas * splits < 2 * 148 && (int64_t)splits * 2 * 64 <= positions) splits *= 2;
-  P.splits = splits;
-  const int64_t part_bytes = (int64_t)splits * batch * q_heads * (head_dim + 2) * 4;
-  if (splits > 1 && part_bytes > (int64_t)CLJXLA_STATIC_ATTN_SCRATCH_BYTES)
-    return put_err(err, errcap, E_INVALID,
-                   "attention_decode_static: partial results need " + std::to_string(part_bytes) +
-                       " bytes, more than the static scratch of " +
-                       std::to_string((long long)CLJXLA_STATIC_ATTN_SCRATCH_BYTES));
-  if (splits > 1) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return put_err(err, errcap, E_INTERNAL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
-    if (dev < 0 || dev >= kMaxDevices) return put_err(err, errcap, E_INTERNAL, "device ordinal out of range");
-    void* scratch = nullptr;
-    {
-      std::lock_guard<std::mutex> lk(g_scratch_mu);
-      if (!g_scratch_addr[dev]) {
-        e = cudaGetSymbolAddress(&g_scratch_addr[dev], g_static_attn_scratch);
-        if (e != cudaSuccess) {
-          g_scratch_addr[dev] = nullptr;
-          return put_err(err, errcap, E_INTERNAL, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+  // a failed launch inside surfaces as cljxla::Error; it must not cross the C ABI
+  try {
+    cudaGetLastError();  // a non-sticky error left by an earlier, unrelated call is not this call's failure
+    AttnParams P{};
+    P.B = (int32_t)batch;
+    P.nq = (int32_t)q_heads;
+    P.nkv = (int32_t)kv_heads;
+    P.Sq = 1;
+    P.T = (int32_t)positions;
+    P.hd = (int32_t)head_dim;
+    P.group = (int32_t)(q_heads / kv_heads);
+    P.qtile = 1;
+    P.q = dense4(q, KDT_BF16, batch, q_heads, 1, head_dim);
+    P.k = dense4(k_cache, KDT_BF16, batch, kv_heads, positions, head_dim);
+    P.v = dense4(v_cache, KDT_BF16, batch, kv_heads, positions, head_dim);
+    P.mask = dense4(mask, KDT_F32, batch, q_heads, 1, positions);
+    P.mask.stride[0] = P.mask.stride[1] = P.mask.stride[2] = 0;  // one additive row shared by all heads
+    P.k_dt = KDT_BF16;
+    // printed attention.clj:343-365 with a bf16 model: q.k^T rounded to bf16,
+    // times the bf16 scale constant (rounded to bf16), + f32 mask, f32 softmax
+    P.dt_d1 = KDT_BF16;
+    P.dt_m = P.dt_sub = P.dt_exp = KDT_F32;
+    P.out_dt = KDT_F32;
+    P.mask_skip = -5000.0f;
+    EwInstr imm{};
+    imm.op = EW_IMM;
+    imm.dt = (uint8_t)KDT_F32;
+    imm.dst = 1;
+    imm.fimm = bf16_to_f32(f32_to_bf16(scale));
+    EwInstr mul{};
+    mul.op = EW_MUL;
+    mul.dt = (uint8_t)KDT_BF16;
+    mul.a = 0;
+    mul.b = 1;
+    mul.dst = 2;
+    P.chain[0] = imm;
+    P.chain[1] = mul;
+    P.nchain = 2;
+    P.chain_out = 2;
+    P.chain_kind = 1;  // the same multiply in closed form
+    P.chain_c = imm.fimm;
+    P.chain_dt = KDT_BF16;
+    P.out.slot = -1;
+    P.out.off = (int64_t)(uintptr_t)out;
+    // same split rule as the planner: enough CTAs for two waves, >= 64 positions per split
+    const int64_t ctas = batch * kv_heads;
+    const int64_t sms = device_sm_count();
+    int splits = 1;
+    while (ctas * splits < 2 * sms && (int64_t)splits * 2 * 64 <= positions) splits *= 2;
+    P.splits = splits;
+    const int64_t part_bytes = (int64_t)splits * batch * q_heads * (head_dim + 2) * 4;
+    if (splits > 1 && part_bytes > (int64_t)CLJXLA_STATIC_ATTN_SCRATCH_BYTES)
+      return put_err(err, errcap, E_INVALID,
+                     "attention_decode_static: partial results need " + std::to_string(part_bytes) +
+                         " bytes, more than the static scratch of " +
+                         std::to_string((long long)CLJXLA_STATIC_ATTN_SCRATCH_BYTES));
+    if (splits > 1) {
+      int dev = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e != cudaSuccess) return put_err(err, errcap, E_INTERNAL, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+      if (dev < 0 || dev >= kMaxDevices) return put_err(err, errcap, E_INTERNAL, "device ordinal out of range");
+      void* scratch = nullptr;
+      {
+        std::lock_guard<std::mutex> lk(g_scratch_mu);
+        if (!g_scratch_addr[dev]) {
+          e = cudaGetSymbolAddress(&g_scratch_addr[dev], g_static_attn_scratch);
+          if (e != cudaSuccess) {
+            g_scratch_addr[dev] = nullptr;
+            return put_err(err, errcap, E_INTERNAL, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+          }
         }
+        scratch = g_scratch_addr[dev];
       }
-      scratch = g_scratch_addr[dev];
+      P.part.slot = -1;
+      P.part.off = (int64_t)(uintptr_t)scratch;
     }
-    P.part.slot = -1;
-    P.part.off = (int64_t)(uintptr_t)scratch;
+    cudaStream_t s = (cudaStream_t)stream;
+    launch_attention(P, nullptr, s);
+    if (splits > 1) launch_attention_combine(P, nullptr, s);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return put_err(err, errcap, E_INTERNAL, std::string("launch: ") + cudaGetErrorString(e));
+    return 0;
+  } catch (const Error& e) {
+    return put_err(err, errcap, e.code, std::string("attention_decode_static: ") + e.what());
+  } catch (const std::exception& e) {
+    return put_err(err, errcap, E_INTERNAL, std::string("attention_decode_static: ") + e.what());
+  } catch (...) {
+    return put_err(err, errcap, E_INTERNAL, "attention_decode_static: unknown failure");
   }
-  cudaStream_t s = (cudaStream_t)stream;
-  launch_attention(P, nullptr, s);
-  if (splits > 1) launch_attention_combine(P, nullptr, s);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return put_err(err, errcap, E_INTERNAL, std::string("launch: ") + cudaGetErrorString(e));
-  return 0;
 }

@@ -70,4 +70,12 @@ struct Counters {
 };
 Counters& counters();
 
+// Facts about the current device, kept per device ordinal because a process
+// may drive clients on several GPUs: its SM count (148 on B200), and the
+// opt-in to more than 48 KB of dynamic shared memory, which
+// cudaFuncSetAttribute applies to the current device only and is therefore
+// recorded per (kernel, device).  Both throw Error on a CUDA failure.
+int device_sm_count();
+void ensure_smem_optin(const void* kernel, int bytes);
+
 }  // namespace cljxla

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "fast_kernels.h"
 #include "jit.h"
@@ -16,6 +18,40 @@ namespace cljxla {
 Counters& counters() {
   static Counters c;
   return c;
+}
+
+namespace {
+std::mutex g_dev_mu;
+std::map<int, int> g_dev_sms;
+std::map<std::pair<const void*, int>, int> g_smem_optin;
+
+int current_device() {
+  int dev = 0;
+  CUDA_OK(cudaGetDevice(&dev));
+  return dev;
+}
+}  // namespace
+
+int device_sm_count() {
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  auto it = g_dev_sms.find(dev);
+  if (it != g_dev_sms.end()) return it->second;
+  int v = 0;
+  CUDA_OK(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+  if (v <= 0) fail(E_INTERNAL, "device reports no multiprocessors");
+  g_dev_sms[dev] = v;
+  return v;
+}
+
+void ensure_smem_optin(const void* kernel, int bytes) {
+  if (bytes <= 48 * 1024) return;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  int& have = g_smem_optin[{kernel, dev}];
+  if (have >= bytes) return;
+  CUDA_OK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  have = bytes;
 }
 
 ProfileState& profile_state() {

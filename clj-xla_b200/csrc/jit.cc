@@ -615,17 +615,14 @@ bool describe_one(const Launch& l, int64_t* grid, int* block, int* cluster, JitA
 void emit_body(std::ostringstream& s, const Launch& l, int block, int cluster, const std::string& fname,
                const BodyOpts& bo = BodyOpts{});
 
+// SM count of the current device; 148 (B200) when planning on a host without a GPU
 int sm_count() {
-  static const int n = [] {
-    int dev = 0, v = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        v <= 0) {
-      cudaGetLastError();
-      return 148;
-    }
-    return v;
-  }();
-  return n;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    return 148;
+  }
+  return device_sm_count();
 }
 
 // Decode GEMV fed by bulk copies (K_GEMV, and K_GEMV_FUSED with its producer
@@ -1500,17 +1497,8 @@ std::vector<void*> jit_compile(const std::vector<std::string>& sources) {
 
 void jit_launch(void* kernel, int64_t grid, int block, int cluster, int smem, const uint64_t* argtab,
                 const std::vector<JitArgs>& jargs, cudaStream_t s) {
-  if (smem > 0) {
-    // opt in to the dynamic shared memory once per kernel (static + dynamic may pass 48 KB)
-    static std::mutex mu;
-    static std::map<void*, int> set;
-    std::lock_guard<std::mutex> lk(mu);
-    int& have = set[kernel];
-    if (have < smem) {
-      CUDA_OK(cudaFuncSetAttribute((const void*)kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      have = smem;
-    }
-  }
+  // a library kernel is device-independent; its shared-memory opt-in is per device
+  if (smem > 0) ensure_smem_optin((const void*)kernel, smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
   cfg.blockDim = dim3((unsigned)block, 1, 1);

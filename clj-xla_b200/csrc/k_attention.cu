@@ -1387,12 +1387,7 @@ bool prefill_fast(const AttnParams& p) {
 
 template <int HD, bool FAST>
 void launch_tc_prefill_t(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
-  static bool configured = false;  // per instantiation; set before the first launch (host thread)
-  if (!configured) {
-    CUDA_OK(cudaFuncSetAttribute(attn_tc_prefill_kernel<HD, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 PF_SMEM_MAX));
-    configured = true;
-  }
+  ensure_smem_optin((const void*)attn_tc_prefill_kernel<HD, FAST>, PF_SMEM_MAX);
   const int qt = PF_ROWS / p.group;
   launch_k(attn_tc_prefill_kernel<HD, FAST>, dim3(1, (unsigned)((p.Sq + qt - 1) / qt), (unsigned)(p.B * p.nkv)),
            dim3(256), prefill_smem(p, FAST), s, 1, p, argtab);
@@ -1408,12 +1403,7 @@ template <int HD>
 void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   const int nbuf = (p.T + p.splits - 1) / p.splits > TC_CH ? 2 : 1;  // as the kernel decides
   const int dyn = nbuf * 2 * TC_CH * (HD + 8) * 2;
-  static bool configured = false;  // per instantiation; set before the first launch (host thread)
-  if (!configured) {
-    CUDA_OK(cudaFuncSetAttribute(attn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 2 * 2 * TC_CH * (HD + 8) * 2));
-    configured = true;
-  }
+  ensure_smem_optin((const void*)attn_tc_kernel<HD>, 2 * 2 * TC_CH * (HD + 8) * 2);
   launch_k(attn_tc_kernel<HD>, dim3((unsigned)p.splits, 1, (unsigned)(p.B * p.nkv)), dim3(128), dyn, s, 1, p, argtab);
 }
 
@@ -1421,11 +1411,7 @@ template <int HPL, int NQV>
 void launch_smem(const AttnParams& p, const uint64_t* argtab, cudaStream_t s, dim3 grid) {
   constexpr int HD = HPL * 32;
   const int dyn = 2 * CH * (HD + 8) * 2;
-  static bool configured = false;  // per instantiation; set before the first launch (host thread)
-  if (!configured) {
-    CUDA_OK(cudaFuncSetAttribute(attn_smem_kernel<HPL, NQV>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn));
-    configured = true;
-  }
+  ensure_smem_optin((const void*)attn_smem_kernel<HPL, NQV>, dyn);
   launch_k(attn_smem_kernel<HPL, NQV>, dim3(grid), dim3(NW * 32), dyn, s, 1, p, argtab);
 }
 

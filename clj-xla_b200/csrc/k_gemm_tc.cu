@@ -343,14 +343,8 @@ void tc_gemm_tile_shape(int* bm, int* bn, int* bk) {
 }
 
 void launch_tc_gemm(const TcGemmParams& p, const uint64_t* argtab, cudaStream_t s) {
-  static int sms = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
+  const int sms = device_sm_count();
+  ensure_smem_optin((const void*)tc_gemm_kernel, SMEM_BYTES);
   const int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = (int)(tiles < sms ? tiles : sms);
   if (grid <= 0) return;

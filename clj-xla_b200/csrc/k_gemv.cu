@@ -193,14 +193,13 @@ GemvShape gemv_shape(int64_t N, int64_t K, int resident_blocks) {
 
 template <int MT, typename XT>
 void launch_nt_t(GemvParams p, const uint64_t* argtab, cudaStream_t s) {
-  static int resident = 0;
-  if (!resident) {
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_nt_bf16<MT, XT>, 256, 0);
-    resident = std::max(1, sms * std::max(1, per_sm));
+  static int per_sm = 0;  // occupancy is a property of the kernel on sm_100a, the same on every B200
+  if (!per_sm) {
+    int v = 1;
+    CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, gemv_nt_bf16<MT, XT>, 256, 0));
+    per_sm = std::max(1, v);
   }
+  const int resident = device_sm_count() * per_sm;
   GemvShape sh = gemv_shape(p.N, p.K, resident);
   p.warps_per_row = sh.wpr;
   launch_k(gemv_nt_bf16<MT, XT>, dim3(sh.grid), dim3(256), 0, s, 1, p, argtab);

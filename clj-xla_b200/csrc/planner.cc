@@ -30,7 +30,7 @@ namespace cljxla {
 
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
-                            "gemm_generic", "gemv", "attn_decode", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
+                            "gemm_generic", "gemv", "attention", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
                             "all_reduce", "gemv_fused", "fused_kv_write"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }

@@ -114,7 +114,12 @@ CLJXLA_EXPORT void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* buffer)
  *   out      f32  [batch, q_heads, 1, head_dim]          (device)
  *
  * scores = bf16(bf16(q.k) * bf16(scale)) + mask, softmax in f32, out = p.v:
- * the printed graph's op order and roundings.  head_dim in {32,64,128,256},
+ * the printed graph's op order and roundings.  A position whose mask value is
+ * at or below -5000 is skipped: it contributes weight 0, which is what the
+ * formula gives for the -10000 causal mask whenever some position of the row
+ * is unmasked.  A row whose every position is at or below -5000 therefore
+ * yields zeros (the formula would give the uniform average, or NaN for -inf).
+ * Failures (bad sizes, a failed launch) are returned, never thrown.  head_dim in {32,64,128,256},
  * q_heads a multiple of kv_heads with at most 8 per KV head.  Work is enqueued
  * on `stream` (a cudaStream_t; NULL = legacy default stream) of the calling
  * thread's current device.

@@ -274,11 +274,15 @@ def _f64_to_bf16(a: np.ndarray) -> np.ndarray:
     """Correctly rounded f64 -> bf16 (avoids f64->f32->bf16 double rounding)."""
     a = np.asarray(a, dtype=np.float64)
     f = a.astype(np.float32)
-    lo = round_bf16(f)
-    # candidate neighbours in bf16 spacing around the f32 rounding
+    lo = np.atleast_1d(round_bf16(f))   # arrays: unsigned wrap-around below is silent and masked
+    # candidate neighbours in bf16 spacing around the f32 rounding; the one below
+    # a zero is the smallest bf16 of the opposite sign
     u = lo.view(np.uint32)
     up = (u + np.uint32(0x10000)).view(np.float32)
-    dn = (u - np.uint32(0x10000)).view(np.float32)
+    at_zero = (u & np.uint32(0x7FFFFFFF)) == 0
+    dn = np.where(at_zero, (u ^ np.uint32(0x80000000)) | np.uint32(0x10000),
+                  u - np.uint32(0x10000)).astype(np.uint32).view(np.float32)
+    a = a.reshape(lo.shape)
     best = lo.copy()
     err = np.abs(a - lo.astype(np.float64))
     for c in (up, dn):
@@ -288,7 +292,7 @@ def _f64_to_bf16(a: np.ndarray) -> np.ndarray:
         sel = better | tie
         best = np.where(sel, c, best)
         err = np.where(sel, e, err)
-    return best.astype(np.float32)
+    return best.astype(np.float32).reshape(f.shape)
 
 
 def _ew(fn, args, rdt):
