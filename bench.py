@@ -147,33 +147,6 @@ def model_setup(args):
     return cfg, B, S, T
 
 
-def device_weights(cfg, seed, device):
-    """Seeded random-init weights in invar order, generated on the GPU, as host
-    arrays (bf16 bit patterns) ready for BufferFromHostBuffer."""
-    import torch
-    from cljxla_b200.host import drivers as d
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    out = []
-    for name, shp, kind in d.weight_specs(cfg):
-        if kind == "mat":
-            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02)
-        elif kind == "gemma_norm":
-            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02)
-        elif kind == "plain_norm":
-            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02).add_(1.0)
-        elif kind == "one":
-            w = torch.ones(shp, device=device)
-        else:
-            w = torch.zeros(shp, device=device)
-        if cfg.dtype == "bf16":
-            out.append(w.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16))
-        else:
-            out.append(w.cpu().numpy())
-        del w
-    return out
-
-
 def run_ours(args, rank, world, local_rank):
     import torch
     pkg = _pkg()
@@ -196,7 +169,7 @@ def run_ours(args, rank, world, local_rank):
     wdt = DTYPE_ENUM[cfg.dtype]
 
     t0 = time.time()
-    host_w = device_weights(cfg, 1234 + rank, f"cuda:{local_rank}")
+    host_w = d.device_weights(cfg, 1234 + rank, f"cuda:{local_rank}")
     specs = d.weight_specs(cfg)
     wbufs = [core.buffer_from_host_buffer(ctx, w, shp, wdt) for w, (_, shp, _) in zip(host_w, specs)]
     if args.no_cpu_baseline or rank != 0 or args.tp > 1:

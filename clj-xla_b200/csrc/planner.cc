@@ -1042,6 +1042,23 @@ void Planner::build_row_regions() {
         }
       }
     }
+    // a region stores at most RP_MAXOUT values; with more (a graph that returns
+    // its intermediates) the members stay separate kernels
+    std::function<bool(int)> needed = [&](int x) {
+      for (int o : g_.outputs)
+        if (o == x) return true;
+      for (int u : users_[x]) {
+        if (!live_[u]) continue;
+        if (!in_region(u)) return true;
+        if (rg.alias.count(u) && needed(u)) return true;
+      }
+      return false;
+    };
+    int nout = 0;
+    for (int x : rg.full) nout += needed(x);
+    for (int x : rg.scalar) nout += needed(x);
+    for (int x : rg.reduces) nout += needed(x);
+    if (nout > RP_MAXOUT) continue;
     int id = (int)regions_.size();
     for (int x : rg.all()) region_of_[x] = id;
     for (int x : rg.full) loc_[x].kind = Loc::ROW;

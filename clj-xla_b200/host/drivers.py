@@ -274,6 +274,33 @@ def make_weights(cfg: ModelConfig, seed: int = 0) -> List[np.ndarray]:
     return out
 
 
+def device_weights(cfg: ModelConfig, seed: int, device: str = "cuda:0") -> List[np.ndarray]:
+    """Seeded random-init weights in invar order, drawn on the GPU with torch
+    (a few seconds for the largest configs, where a host generator takes
+    minutes), returned as host arrays ready for BufferFromHostBuffer: bf16 bit
+    patterns (uint16) for bf16 configs, float32 otherwise.  Same distributions
+    as ``make_weights``."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = []
+    for name, shp, kind in weight_specs(cfg):
+        if kind in ("mat", "gemma_norm"):
+            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02)
+        elif kind == "plain_norm":
+            w = torch.randn(shp, generator=g, device=device, dtype=torch.float32).mul_(0.02).add_(1.0)
+        elif kind == "one":
+            w = torch.ones(shp, device=device)
+        else:
+            w = torch.zeros(shp, device=device)
+        if cfg.dtype == "bf16":
+            out.append(w.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16))
+        else:
+            out.append(w.cpu().numpy())
+        del w
+    return out
+
+
 def make_prompt(cfg: ModelConfig, batch: int, prompt_len: int, seed: int = 1) -> np.ndarray:
     rng = np.random.Generator(np.random.PCG64(seed))
     return rng.integers(0, cfg.vocab, size=(batch, prompt_len), dtype=np.int64).astype(np.int32)

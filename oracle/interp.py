@@ -260,8 +260,15 @@ def _parse_literal(lit: str, shape, dt) -> np.ndarray:
             raise ValueError("dense literal size mismatch")
         arr = vals.reshape(shape)
     else:
+        # a splat: convert the one value, then a read-only broadcast view (every
+        # op makes a new array for its result, so the view is never written)
         v = float(lit) if dt in _FLOAT else int(lit)
-        arr = np.full(shape, v, dtype=np.float64 if dt in _FLOAT else np.int64)
+        one = np.array(v, dtype=np.float64 if dt in _FLOAT else np.int64)
+        if dt in _FLOAT:
+            one = _f64_to_bf16(one) if dt == "bf16" else to_dtype(one, dt)
+        else:
+            one = to_dtype(one, dt)
+        return np.broadcast_to(one, shape)
     if dt in _FLOAT:
         # decimal -> nearest f64 -> nearest value of the element type
         if dt == "bf16":

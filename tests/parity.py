@@ -72,3 +72,30 @@ def close(got, want, dt, rtol=None, atol_scale=1.0):
     ok = bool(np.all(err <= allowed)) and not np.isnan(g).any()
     excess = float(np.max(err - allowed)) if err.size else 0.0
     return ok, excess, float(err.max()) if err.size else 0.0
+
+
+def returning_every_value(text: str, skip_ops=("constant",)):
+    """The printed module with every SSA value it defines (except literals)
+    appended to its results, for comparing each intermediate of a graph with
+    the oracle's.  Returns (text, [(name, shape, dtype)] of the appended values).
+    The printer's func signature and return line (stablehlo.clj:582-600) are
+    rewritten in place; the op lines are untouched."""
+    m = interp.parse_module(text)
+    extra = [(op.out, op.rtype[0], op.rtype[1]) for op in m.ops
+             if op.name not in skip_ops and op.out not in m.returns]
+
+    def ty(shape, dt):
+        return "tensor<" + "".join(f"{d}x" for d in shape) + dt + ">"
+
+    lines = text.split("\n")
+    for i, ln in enumerate(lines):
+        s = ln.strip()
+        if s.startswith("func.func @main("):
+            head, rest = ln.rsplit("-> (", 1)
+            types, tail = rest.rsplit(")", 1)
+            lines[i] = head + "-> (" + types + ", " + ", ".join(ty(sh, dt) for _, sh, dt in extra) + ")" + tail
+        elif s.startswith("return "):
+            names, types = ln.split(" : ", 1)
+            lines[i] = (names + ", " + ", ".join("%" + n for n, _, _ in extra) + " : " + types + ", "
+                        + ", ".join(ty(sh, dt) for _, sh, dt in extra))
+    return "\n".join(lines), extra

@@ -118,8 +118,13 @@ def test_gather_rows_and_clamp(ctx):
         return t.gather(tab, ids)
     g = t.trace_graph("gth", [("tab", ("tensor", (50, 24), "bf16")), ("ids", ("tensor", (2, 7), "i32"))], f)
     ids = np.array([[0, 5, 49, 50, 1000, -3, 7], [1, 2, 3, 4, 5, 6, 7]], np.int32)
-    got = check_graph(ctx, g, [rand((50, 24), "bf16", 12), ids])
-    assert got[0].dtype == np.uint16  # bit-exact row copies compared above
+    inputs = [rand((50, 24), "bf16", 12), ids]
+    got = check_graph(ctx, g, inputs)
+    # row copies are bit-exact: same bf16 bit patterns as the oracle's clamped rows
+    want = interp.f32_to_bf16_bits(interp.run_mlir(shlo.graph_to_mlir_text(g), inputs)[0])
+    assert got[0].dtype == np.uint16 and np.array_equal(got[0], want)
+    rows = np.clip(ids, 0, 49)
+    assert np.array_equal(got[0], inputs[0][rows])
 
 
 def test_dynamic_update_slice_tracer_and_constant_index(ctx):
