@@ -45,7 +45,8 @@ int device_sm_count() {
 }
 
 void ensure_smem_optin(const void* kernel, int bytes) {
-  if (bytes <= 48 * 1024) return;
+  // also below 48 KB: the default limit is 48 KB less the kernel's static shared memory
+  if (bytes <= 0) return;
   const int dev = current_device();
   std::lock_guard<std::mutex> lk(g_dev_mu);
   int& have = g_smem_optin[{kernel, dev}];

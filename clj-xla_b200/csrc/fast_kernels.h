@@ -93,7 +93,8 @@ struct AttnParams {
   // itself and resets its counter (use_counters 0: a separate combine launch)
   DPtr counters;
   int32_t use_counters;
-  int32_t use_tc;  // 1: decode on the tensor cores (64-position splits); 2: prefill on the tensor cores
+  int32_t use_tc;  // 1: decode on the tensor cores (64-position splits); 2: prefill on the tensor cores;
+                   // 3: decode with bulk-copy staged K/V (one wave of CTAs, SIMT f32 arithmetic)
   int32_t B, nq, nkv, Sq, T, hd, group, splits, qtile;
   int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
   int32_t nchain, chain_out;
@@ -104,12 +105,21 @@ struct AttnParams {
   int32_t chain_kind;
   float chain_c;
   int32_t chain_dt, pad_k;
+  // use_tc 3 (bulk-copy staged decode): positions per split and per staged chunk,
+  // and the plan's status word, where a bounded wait that gives up is recorded
+  int32_t dec_per_split, dec_chunk;
+  DPtr status;
+  int32_t has_status, pad_s;
 };
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);
 // whether the tensor-core decode kernel can run these views (bf16 q / K / V,
 // 16-byte aligned rows, head_dim 64 / 128 / 256, one query tile of <= 8 vectors)
 bool attention_tc_ok(const AttnParams& p);
+// the bulk-copy staged decode kernel (Sq 1, bf16 K / V rows, 16-byte aligned),
+// and its split / chunk sizes for one wave over `sms` SMs
+bool attention_dec_ok(const AttnParams& p);
+void plan_attention_dec(AttnParams& p, int sms);
 // the tensor-core prefill kernel (64 query vectors per CTA, no position splits)
 bool attention_tc_prefill_ok(const AttnParams& p);
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);

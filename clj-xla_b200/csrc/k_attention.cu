@@ -976,6 +976,303 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 }
 
 // ---------------------------------------------------------------------------
+// Decode attention with bulk-copy staged K/V (use_tc 3).  A decode step reads
+// each cached K/V row once and does ~2 flops per byte, so the kernel is built
+// for latency: one wave of CTAs (the planner sizes the position splits so that
+// splits * batch * kv heads is about the SM count), 8 warps each.  Before the
+// dependency wait a CTA asks L2 for its split's rows; after it, one thread
+// issues cp.async.bulk copies of the first chunk's K and V rows into shared
+// memory (a contiguous cache needs one copy per tensor) while every thread
+// loads the query vectors into registers and the chunk's mask values into
+// shared memory, so the step pays one memory round trip before computing.
+// Arithmetic is f32 on the CUDA cores (f32 queries need no split): a lane owns
+// HD/32 consecutive dims, each warp scores every 8th position of the chunk
+// (lane partial dot products, warp shuffle sums), the printed score chain,
+// mask and roundings are applied, the chunk's softmax runs over the scores in
+// shared memory, and each warp accumulates P V over its positions.  Chunks
+// beyond the first are double-buffered; the warps' contexts are summed through
+// shared memory, and the position splits merged by the last CTA to arrive.
+constexpr int DEC_THREADS = 256;
+
+__device__ __forceinline__ uint32_t dec_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool dec_mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = dec_smem_u32(bar);
+  for (uint32_t i = 0; i < (1u << 22); ++i) {  // bounded: a copy that never lands is reported, not waited for
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void dec_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dec_smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(dec_smem_u32(bar))
+               : "memory");
+}
+
+template <int HD, int NQ>
+__global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_constant__ AttnParams P,
+                                                               const uint64_t* __restrict__ argtab) {
+  constexpr int VPL = HD / 32;  // consecutive dims of a row per lane
+  constexpr int NWARP = DEC_THREADS / 32;
+  const int CH = P.dec_chunk;
+  extern __shared__ __align__(128) unsigned char dec_smem[];
+  const int nst = P.dec_per_split > CH ? 2 : 1;
+  uint16_t* Kb = (uint16_t*)dec_smem;                      // [nst][CH][HD]
+  uint16_t* Vb = Kb + (size_t)nst * CH * HD;               // [nst][CH][HD]
+  float* msk = (float*)(Vb + (size_t)nst * CH * HD);       // [2][NQ][CH]
+  float* sc = msk + 2 * NQ * CH;                           // [NQ][CH] scores, then probabilities
+  __shared__ __align__(8) uint64_t bar[2];
+  __shared__ float s_red[NWARP][NQ];
+  __shared__ float s_m[NQ], s_l[NQ], s_scl[NQ];
+  __shared__ int64_t s_qoff[NQ], s_moff[NQ];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bk = blockIdx.y, b = bk / P.nkv, kh = bk % P.nkv;
+  const int nqv = P.group;  // Sq == 1: one query vector per head of the group
+  const int64_t t0 = (int64_t)blockIdx.x * P.dec_per_split, t1 = min((int64_t)P.T, t0 + P.dec_per_split);
+  const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
+  const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
+  const bool dense = P.k.stride[2] == HD && P.v.stride[2] == HD;
+  // before the dependency wait: the split's rows towards L2 (rows < the new
+  // position were written by earlier steps; a prefetch returns nothing, so the
+  // new row is read correctly after the wait), barriers initialised
+  if (t0 < t1) {
+    if (dense) {
+      const int64_t bytes = (t1 - t0) * HD * 2;
+      for (int64_t i = threadIdx.x; i * 16384 < bytes; i += DEC_THREADS) {
+        const uint32_t n = (uint32_t)min((int64_t)16384, bytes - i * 16384);
+        l2_prefetch_bulk((const char*)(kbase + t0 * HD) + i * 16384, n);
+        l2_prefetch_bulk((const char*)(vbase + t0 * HD) + i * 16384, n);
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < t1 - t0; i += DEC_THREADS) {
+        l2_prefetch_bulk(kbase + (t0 + i) * P.k.stride[2], HD * 2);
+        l2_prefetch_bulk(vbase + (t0 + i) * P.v.stride[2], HD * 2);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x < NQ) {
+    const int r = threadIdx.x < nqv ? threadIdx.x : 0;
+    const int h = kh * P.group + r;
+    s_qoff[threadIdx.x] = b * P.q.stride[0] + h * P.q.stride[1];
+    s_moff[threadIdx.x] = b * P.mask.stride[0] + h * P.mask.stride[1];
+    s_m[threadIdx.x] = -INFINITY;
+    s_l[threadIdx.x] = 0.f;
+  }
+  __syncthreads();
+  pdl_enter();
+  unsigned* status = P.has_status ? (unsigned*)dres(P.status, argtab) : nullptr;
+  // stage chunk c (positions c0 .. c0 + n) into buffer st: one thread, after
+  // the barrier that ended every generic access of the buffer
+  auto issue = [&](int64_t c0, int n, int st) {
+    uint64_t* bb = &bar[st];
+    const uint32_t row = HD * 2;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(dec_smem_u32(bb)),
+                 "r"((uint32_t)(2 * n) * row)
+                 : "memory");
+    uint16_t* kd = Kb + (size_t)st * CH * HD;
+    uint16_t* vd = Vb + (size_t)st * CH * HD;
+    if (dense) {
+      dec_bulk(kd, kbase + c0 * HD, (uint32_t)n * row, bb);
+      dec_bulk(vd, vbase + c0 * HD, (uint32_t)n * row, bb);
+    } else {
+      for (int j = 0; j < n; ++j) {
+        dec_bulk(kd + (size_t)j * HD, kbase + (c0 + j) * P.k.stride[2], row, bb);
+        dec_bulk(vd + (size_t)j * HD, vbase + (c0 + j) * P.v.stride[2], row, bb);
+      }
+    }
+  };
+  const char* mb = dres(P.mask.p, argtab);
+  const int64_t ms3 = P.mask.stride[3];
+  // mask values of a chunk into msk[buf] (-inf past the split); returns
+  // whether any value this thread stored is live
+  auto load_mask = [&](int64_t c0, int n, int buf) {
+    float* m = msk + buf * NQ * CH;
+    bool any = false;
+    for (int e = threadIdx.x; e < NQ * CH; e += DEC_THREADS) {
+      const int r = e / CH, j = e % CH;
+      float v = -INFINITY;
+      if (r < nqv && j < n) v = ld_any(mb, s_moff[r] + (c0 + j) * ms3, P.mask.dt);
+      m[e] = v;
+      any |= v > P.mask_skip;
+    }
+    return any;
+  };
+  const int nch = t0 < t1 ? (int)((t1 - t0 + CH - 1) / CH) : 0;
+  if (threadIdx.x == 0 && nch > 0) issue(t0, (int)min((int64_t)CH, t1 - t0), 0);
+  // queries: lane-owned dims of every query vector, f32
+  float q[NQ][VPL];
+  {
+    const char* qb = dres(P.q.p, argtab);
+    const int64_t qs3 = P.q.stride[3];
+#pragma unroll
+    for (int r = 0; r < NQ; ++r)
+#pragma unroll
+      for (int i = 0; i < VPL; ++i)
+        q[r][i] = r < nqv ? ld_any(qb, s_qoff[r] + (int64_t)(lane * VPL + i) * qs3, P.q.dt) : 0.f;
+  }
+  bool any_cur = nch > 0 && load_mask(t0, (int)min((int64_t)CH, t1 - t0), 0);
+  float acc[NQ][VPL];
+#pragma unroll
+  for (int r = 0; r < NQ; ++r)
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) acc[r][i] = 0.f;
+  bool ok = true;
+  for (int c = 0; c < nch; ++c) {
+    const int buf = c & 1, st = nst == 2 ? buf : 0;
+    const int64_t c0 = t0 + (int64_t)c * CH;
+    const int n = (int)min((int64_t)CH, t1 - c0);
+    // this chunk's mask visible (and whether any of it is live); the previous chunk's buffers free
+    const bool live = __syncthreads_or(any_cur) != 0;
+    if (c + 1 < nch && nst == 2 && threadIdx.x == 0)
+      issue(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), st ^ 1);
+    const uint32_t parity = (uint32_t)((nst == 2 ? c >> 1 : c) & 1);
+    bool landed = dec_mbar_wait(&bar[st], parity);
+    if (!landed) landed = dec_mbar_wait(&bar[st], parity);  // once more: the copy may still land
+    ok = __syncthreads_and(ok && landed) != 0;
+    if (!ok && status && threadIdx.x == 0) atomicOr(status, 32u);
+    if (live && ok) {
+      const float* m = msk + buf * NQ * CH;
+      const uint16_t* kc = Kb + (size_t)st * CH * HD;
+      // scores: warp w takes positions w, w + 8, ...
+      for (int j = warp; j < n; j += NWARP) {
+        bool any = false;
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) any |= r < nqv && m[r * CH + j] > P.mask_skip;
+        if (!any) {
+          if (lane < NQ) sc[lane * CH + j] = -INFINITY;
+          continue;
+        }
+        float kv[VPL];
+        load_row<uint16_t, VPL>(kc + (size_t)j * HD + lane * VPL, kv);
+        float part[NQ];
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) s = fmaf(q[r][i], kv[i], s);
+          part[r] = s;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+          for (int r = 0; r < NQ; ++r) part[r] += __shfl_xor_sync(0xffffffffu, part[r], o);
+        if (lane < NQ) {
+          float v = -INFINITY;
+#pragma unroll
+          for (int r = 0; r < NQ; ++r)
+            if (r == lane && r < nqv && m[r * CH + j] > P.mask_skip)
+              v = rnd_dt(apply_chain(P, rnd_dt(part[r], P.dt_d1)) + m[r * CH + j], P.dt_m);
+          sc[lane * CH + j] = v;
+        }
+      }
+    }
+    // the next chunk's mask values load while this one is finished
+    if (c + 1 < nch) any_cur = load_mask(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), buf ^ 1);
+    __syncthreads();
+    if (live && ok) {
+      // chunk softmax: warp r reduces row r
+      if (warp < nqv) {
+        float mx = -INFINITY;
+        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[warp * CH + j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mold = s_m[warp], mnew = fmaxf(mold, mx);
+        float sum = 0.f;
+        for (int j = lane; j < n; j += 32) {
+          const float s = sc[warp * CH + j];
+          float p = 0.f;
+          if (mnew != -INFINITY && s != -INFINITY) p = rnd_dt(expf(rnd_dt(s - mnew, P.dt_sub)), P.dt_exp);
+          sc[warp * CH + j] = p;
+          sum += p;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) {
+          const float scl = (mold == -INFINITY || mnew == -INFINITY) ? (mnew == -INFINITY ? 1.f : 0.f)
+                                                                     : expf(mold - mnew);
+          s_scl[warp] = scl;
+          s_l[warp] = s_l[warp] * scl + sum;
+          s_m[warp] = mnew;
+        }
+      }
+      __syncthreads();
+      // P V over this warp's positions
+      const uint16_t* vc = Vb + (size_t)st * CH * HD;
+#pragma unroll
+      for (int r = 0; r < NQ; ++r) {
+        const float scl = r < nqv ? s_scl[r] : 1.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) acc[r][i] *= scl;
+      }
+      for (int j = warp; j < n; j += NWARP) {
+        float p[NQ];
+        bool nz = false;
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) {
+          p[r] = r < nqv ? sc[r * CH + j] : 0.f;
+          nz |= p[r] != 0.f;
+        }
+        if (!nz) continue;
+        float vv[VPL];
+        load_row<uint16_t, VPL>(vc + (size_t)j * HD + lane * VPL, vv);
+#pragma unroll
+        for (int r = 0; r < NQ; ++r)
+#pragma unroll
+          for (int i = 0; i < VPL; ++i) acc[r][i] = fmaf(p[r], vv[i], acc[r][i]);
+      }
+    }
+    if (nst == 1 && c + 1 < nch) {  // single buffer: restage after everyone is done with it
+      __syncthreads();
+      if (threadIdx.x == 0) issue(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), 0);
+    }
+  }
+  __syncthreads();  // every chunk's buffers free: the warps' contexts are summed in shared memory
+  float* red = (float*)dec_smem;  // [NWARP][NQ][HD]
+#pragma unroll
+  for (int r = 0; r < NQ; ++r)
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) red[((size_t)warp * NQ + r) * HD + lane * VPL + i] = acc[r][i];
+  __syncthreads();
+  const int64_t rows_total = (int64_t)P.B * P.nq;
+  for (int e = threadIdx.x; e < nqv * HD; e += DEC_THREADS) {
+    const int r = e / HD, d = e % HD;
+    float A = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) A += red[((size_t)w * NQ + r) * HD + d];
+    const int64_t row = (int64_t)b * P.nq + kh * P.group + r;
+    if (P.splits == 1) {
+      const float l = s_l[r];
+      const float v = l > 0.f ? A / l : 0.f;
+      char* ob = dres(P.out, argtab);
+      if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = v;
+      else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(v);
+    } else {
+      float* part = (float*)dres(P.part, argtab) + ((int64_t)blockIdx.x * rows_total + row) * (HD + 2);
+      part[2 + d] = A;
+      if (d == 0) {
+        part[0] = s_m[r];
+        part[1] = s_l[r];
+      }
+    }
+  }
+  merge_if_last(P, argtab, b, kh, 0, nqv);
+}
+
+// ---------------------------------------------------------------------------
 // Prefill attention on the tensor cores (FA2-style, mma.sync m16n8k16 bf16 ->
 // f32).  One CTA per (batch * kv head, 64 query vectors): query vector
 // r = qi * group + gi of the tile's query positions, so the GQA group shares
@@ -1407,6 +1704,33 @@ void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
   launch_k(attn_tc_kernel<HD>, dim3((unsigned)p.splits, 1, (unsigned)(p.B * p.nkv)), dim3(128), dyn, s, 1, p, argtab);
 }
 
+int dec_smem_bytes(const AttnParams& p, int nq) {
+  const int nst = p.dec_per_split > p.dec_chunk ? 2 : 1;
+  const int64_t stage = (int64_t)nst * 4 * p.dec_chunk * p.hd + 12LL * nq * p.dec_chunk;
+  const int64_t red = 32LL * nq * p.hd;
+  return (int)std::max(stage, red);
+}
+
+int dec_nq(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
+
+template <int HD, int NQ>
+void launch_dec_t(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  const int smem = dec_smem_bytes(p, NQ);
+  ensure_smem_optin((const void*)attn_dec_kernel<HD, NQ>, smem);
+  launch_k(attn_dec_kernel<HD, NQ>, dim3((unsigned)p.splits, (unsigned)(p.B * p.nkv)), dim3(DEC_THREADS), smem, s, 1,
+           p, argtab);
+}
+
+template <int HD>
+void launch_dec(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  switch (dec_nq(p.group)) {
+    case 1: launch_dec_t<HD, 1>(p, argtab, s); return;
+    case 2: launch_dec_t<HD, 2>(p, argtab, s); return;
+    case 4: launch_dec_t<HD, 4>(p, argtab, s); return;
+    default: launch_dec_t<HD, 8>(p, argtab, s); return;
+  }
+}
+
 template <int HPL, int NQV>
 void launch_smem(const AttnParams& p, const uint64_t* argtab, cudaStream_t s, dim3 grid) {
   constexpr int HD = HPL * 32;
@@ -1452,6 +1776,15 @@ void launch_hpl(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
 }  // namespace
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
+  if (p.use_tc == 3) {
+    switch (p.hd) {
+      case 32: launch_dec<32>(p, argtab, s); return;
+      case 64: launch_dec<64>(p, argtab, s); return;
+      case 128: launch_dec<128>(p, argtab, s); return;
+      case 256: launch_dec<256>(p, argtab, s); return;
+    }
+    fail(E_INTERNAL, "staged decode attention: unsupported head_dim");
+  }
   if (p.use_tc == 2) {
     switch (p.hd) {
       case 64: launch_tc_prefill<64>(p, argtab, s); return;
@@ -1492,6 +1825,24 @@ bool attention_tc_prefill_ok(const AttnParams& p) {
   return smem_ok(p);
 }
 
+bool attention_dec_ok(const AttnParams& p) {
+  if (!(p.hd == 32 || p.hd == 64 || p.hd == 128 || p.hd == 256) || p.Sq != 1 || p.group < 1 || p.group > 8) return false;
+  if (!(p.q.dt == KDT_BF16 || p.q.dt == KDT_F32 || p.q.dt == KDT_F16)) return false;
+  if (!(p.mask.dt == KDT_BF16 || p.mask.dt == KDT_F32 || p.mask.dt == KDT_F16)) return false;
+  return smem_ok(p);
+}
+
+void plan_attention_dec(AttnParams& p, int sms) {
+  const int64_t ctas = (int64_t)p.B * p.nkv;
+  const int chmax = 96 * 256 / p.hd;  // 48 KB of K (and of V) rows per staged chunk
+  int64_t splits = std::max<int64_t>(1, std::min<int64_t>((sms + ctas - 1) / ctas, ATTN_MERGE_MAX_SPLITS));
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, (p.T + 15) / 16));
+  int64_t per = (p.T + splits - 1) / splits;
+  p.splits = (int32_t)((p.T + per - 1) / per);
+  p.dec_per_split = (int32_t)per;
+  p.dec_chunk = (int32_t)std::max<int64_t>(64, std::min<int64_t>(chmax, (per + 7) / 8 * 8));
+}
+
 bool attention_tc_ok(const AttnParams& p) {
   if (!(p.hd == 64 || p.hd == 128 || p.hd == 256) || !(p.q.dt == KDT_BF16 || p.q.dt == KDT_F32)) return false;
   if (p.Sq > p.qtile || p.Sq * p.group > 8 || p.Sq < 1) return false;
@@ -1527,6 +1878,14 @@ void verify_attention(const Launch& l, const RegionFn& region) {
     if (p.splits > ATTN_MERGE_MAX_SPLITS || p.qtile * p.group > 8) fail(E_INTERNAL, "attention merge too wide");
   }
   if (p.use_tc == 1 && !attention_tc_ok(p)) fail(E_INTERNAL, "tensor-core attention on unsupported views");
+  if (p.use_tc == 3) {
+    if (!attention_dec_ok(p)) fail(E_INTERNAL, "staged decode attention on unsupported views");
+    if (p.dec_per_split < 1 || (int64_t)p.splits * p.dec_per_split < p.T ||
+        (int64_t)(p.splits - 1) * p.dec_per_split >= p.T || p.dec_chunk < 8 || p.dec_chunk % 8 ||
+        p.dec_chunk > 96 * 256 / p.hd || dec_smem_bytes(p, dec_nq(p.group)) > 220 * 1024)
+      fail(E_INTERNAL, "staged decode attention: bad split / chunk sizes");
+    if (p.has_status) region(p.status, 4, "status word");
+  }
   if (p.use_tc == 2 && (!attention_tc_prefill_ok(p) || p.splits != 1))
     fail(E_INTERNAL, "tensor-core prefill attention on unsupported views");
   if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||

@@ -1485,6 +1485,11 @@ void Planner::emit_attention(int d2) {
             (long long)P.mask.stride[0], (long long)P.mask.stride[1], (long long)P.mask.stride[2],
             (long long)P.mask.stride[3]);
   P.splits = splits;
+  if (P.Sq == 1 && attention_dec_ok(P) && !getenv_off("CLJXLA_B200_ATTN_DEC")) {
+    P.use_tc = 3;
+    plan_attention_dec(P, 148);
+    splits = P.splits;
+  }
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
   int64_t rows = (int64_t)P.B * P.nq * P.Sq;
@@ -2243,6 +2248,14 @@ void Planner::run() {
     t.tmap_a = DPtr{slot, 0, 128LL * t.tmap_a_index};
     t.tmap_b = DPtr{slot, 0, 128LL * t.tmap_b_index};
     t.status = DPtr{slot, 0, 128LL * (int64_t)plan_.tmaps.size()};
+  }
+  for (Launch& l : plan_.launches) {
+    if (l.kind != K_ATTN_DECODE) continue;
+    AttnParams& a = *(AttnParams*)l.blob.data();
+    if (a.use_tc != 3) continue;
+    plan_.needs_status = true;
+    a.status = DPtr{plan_.tmap_slot(), 0, 128LL * (int64_t)plan_.tmaps.size()};
+    a.has_status = 1;
   }
   for (Launch& l : plan_.launches) {
     if (l.kind != K_GEMV) continue;

@@ -14,20 +14,29 @@ on the same graphs, weights and inputs.
 
 Each run compares the prefill's logits and every K/V cache, the logits of every
 decode step, and every cache after the last step (the windows all 32 steps
-wrote).  The greedy tokens of both sides must be the same for all 32 steps
-(``argmax-host``'s lowest-index rule, scripts/gemma4_inference.clj:399-411);
-the decode loop is the one of scripts/gemma3_inference.clj:307-343.
+wrote).  Every decode step is fed the oracle's greedy token, so each step
+compares identical inputs, and the device's greedy token (``argmax-host``'s
+lowest-index rule, scripts/gemma4_inference.clj:399-411) must equal the
+oracle's at every step - which is the same as the two free-running loops of
+scripts/gemma3_inference.clj:307-343 producing the same tokens.  In the bf16
+models a step whose token the oracle itself changes under f32 summation-order
+noise is reported but does not bind.
 
 Tolerances (src/clj_xla/test/parity.clj:36-49 form, ``|a-b| <= atol +
 rtol*|b|`` with atol = rtol * RMS(b)): f32 every element within 1e-4; bf16
 graphs 2e-2 with the whole-model criterion of ``parity.close_model`` (at most
-0.1% of the elements outside the per-element bound, relative RMS <= 1%); the
-fraction outside the per-element bound is reported for every compared tensor.
+0.1% of the elements outside the per-element bound, relative RMS <= 1%), or
+no more than twice the spread of an oracle run with f32 summation-order noise
+where the oracle itself moves further than that; the fraction outside the
+per-element bound, the relative RMS error and the noisy oracle's figures are
+reported for every compared tensor.
 
 A second test runs one full-width layer of each model (the full vocabulary
 included) with every SSA value of the printed graph returned, and compares each
 intermediate with the oracle's: gather, iota, compare and integer results
-bit-exactly, f32 values at 1e-4, bf16 values at 2e-2.
+bit-exactly, every floating value of the f32 model at 1e-4 and of the bf16
+models at 2e-2 (a bf16 model's f32-typed values are computed from bf16
+operands, whose one-ulp rounding differences alone exceed 1e-4).
 
 Weights are drawn on the GPU with torch (seeded; drivers.device_weights) and
 copied to the host for both sides: a host generator needs minutes for 3.9 B
@@ -79,42 +88,59 @@ def ctx():
 
 
 def _host_ram_ok(cfg, S):
-    """Both sides' weights (bf16 bits + f32 values), the prefill logits a few
-    times over and the caches must fit in host memory with room to spare."""
+    """Both sides' weights (bf16 bits + f32 values), two oracle trajectories'
+    prefill logits and caches must fit in host memory with room to spare."""
     import psutil
     n = sum(int(np.prod(shp)) for _, shp, _ in d.weight_specs(cfg))
-    need = n * (4 + (2 if cfg.dtype == "bf16" else 4)) + 5 * S * cfg.vocab * 4 + (8 << 30)
+    need = n * (4 + (2 if cfg.dtype == "bf16" else 4)) + 8 * S * cfg.vocab * 4 + (16 << 30)
     return psutil.virtual_memory().available > 1.3 * need, need
 
 
-def _cmp(got, want, dt, what):
-    """One tensor: (ok, figures).  f32 strict; bf16 whole-model criterion."""
-    g, w = as_f32(np.asarray(got), dt), as_f32(np.asarray(want), dt)
-    strict, excess, maxerr = close(g, w, "f32" if dt == "f32" else "bf16")
-    fig = {"what": what, "dtype": dt, "shape": list(np.shape(want)), "max_abs_err": maxerr}
+def _dist(got, want, dt):
+    """(fraction outside the per-element bound, relative RMS error, max abs error)."""
+    g, w = as_f32(np.asarray(got), dt).astype(np.float64), as_f32(np.asarray(want), dt).astype(np.float64)
+    rt = 1e-4 if dt == "f32" else 2e-2
+    rms = float(np.sqrt(np.mean(np.square(w)))) if w.size else 0.0
+    err = np.abs(g - w)
+    bad = float(np.mean(err > rt * rms + rt * np.abs(w))) if w.size else 0.0
+    rr = float(np.sqrt(np.mean(np.square(g - w)))) / rms if rms > 0 else 0.0
+    if np.isnan(g).any():
+        bad = rr = float("inf")
+    return bad, rr, float(err.max()) if err.size else 0.0
+
+
+def _judge(dev, noisy, dt):
+    """f32 models: every element within 1e-4.  bf16 models: at most 0.1% of the
+    elements outside 2e-2 and relative RMS <= 1% - or, where the oracle itself
+    moves further than that under summation-order noise, no more than twice
+    its own spread (parity.close_model_floor's rule)."""
+    bad, rr, _ = dev
     if dt == "f32":
-        fig["ok"] = bool(strict)
-        return strict, fig
-    ok, bad, rr = close_model(g, w, "bf16")
-    fig.update({"ok": bool(ok), "frac_outside_2e-2": bad, "rel_rms": rr, "every_element_within_2e-2": bool(strict)})
-    return ok, fig
-
-
-def _top2(row):
-    i = int(np.argmax(row))
-    r = row.copy()
-    r[i] = -np.inf
-    return i, float(row[i] - r.max())
+        return bad == 0.0
+    if bad <= 1e-3 and rr <= 1e-2:
+        return True
+    nb, nr, _ = noisy
+    return bad <= max(1e-3, 2 * nb) and rr <= max(1e-2, 2 * nr)
 
 
 @pytest.mark.parametrize("name", list(FULL))
 def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
+    """Prefill, then 32 decode steps fed the oracle's greedy tokens (so every
+    step compares the same inputs); the device's argmax must equal the
+    oracle's at every step, which is the same as both free-running greedy
+    loops producing the same 32 tokens.  For bf16 models a second oracle
+    trajectory with f32 summation-order noise (seed 1) measures how far the
+    oracle moves by itself; a step whose greedy token that noise changes does
+    not bind the device (the model's own answer there is not determined at this
+    precision), and a tensor further than 2e-2 may be no further than twice
+    the noisy oracle."""
     cfg, S, gen, dynamic = FULL[name]
     ok_ram, need = _host_ram_ok(cfg, S)
     if not ok_ram:
         pytest.skip(f"host RAM below the {need / 2**30:.0f} GiB this comparison needs")
     B, T, V = 1, d.round_up(S + gen, 128), cfg.vocab
     dt = cfg.dtype
+    floors = dt == "bf16"
     api = ctx["api"]
     t0 = time.time()
     host_w = d.device_weights(cfg, 20261202)
@@ -130,82 +156,87 @@ def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
     toks = d.make_prompt(cfg, B, S)
     cache0 = d.zero_cache(cfg, B, T)
     cshape = list(cache0.shape)
-    figs, fails = [], []
-
-    def check(got, want, what, kind_dt):
-        ok, fig = _cmp(got, want, kind_dt, what)
-        figs.append(fig)
-        if not ok:
-            fails.append(fig)
-
-    # ---------------- prefill
     pos = d.pos_inputs(cfg, "prefill", B, 0, S)
+
+    # ---------------- device prefill
     x_b = core.buffer_from_host_buffer(ctx, toks, [B, S], 4)
     p_b = core.buffer_from_host_buffer(ctx, pos, list(pos.shape), 4)
     kv0 = [core.buffer_from_host_buffer(ctx, cache0, cshape, wdt) for _ in range(2 * cfg.layers)]
     outs = api.execute_executable(ex_pre["handle"], [x_b, p_b] + wbufs + kv0, len(g_pre["outvars"]))
     for b in kv0 + [x_b, p_b]:
         api.destroy_buffer(b)
-    dev_logits = core.buffer_to_numpy(ctx, outs[0], (B, S, V), "f32")
+    dev_pre = [core.buffer_to_numpy(ctx, outs[0], (B, S, V), "f32")]
     api.destroy_buffer(outs[0])
     kv = outs[1:]
+    dev_pre += [core.buffer_to_numpy(ctx, b, cshape, dt) for b in kv]
     t_dev = time.time() - t0
+
+    # ---------------- oracle prefill (and the noisy one)
     t1 = time.time()
     zero = np.zeros(cache0.shape, np.float32)
-    o = interp.run_mlir(t_pre, [toks, pos] + wf + [zero] * (2 * cfg.layers))
-    t_oracle = time.time() - t1
-    check(dev_logits, o[0], "prefill logits", dt)
-    o_kv = o[1:]
-    for i, b in enumerate(kv):
-        check(core.buffer_to_numpy(ctx, b, cshape, dt), o_kv[i], f"prefill cache {i}", dt)
-    dev_tok = [d.argmax_host(dev_logits[0, S - 1])]
-    o_tok = [d.argmax_host(o[0][0, S - 1])]
-    margins = [_top2(o[0][0, S - 1].astype(np.float32))[1]]
-    del dev_logits, o
+    orc_pre = interp.run_mlir(t_pre, [toks, pos] + wf + [zero] * (2 * cfg.layers))
+    nz_pre = interp.run_mlir(t_pre, [toks, pos] + wf + [zero] * (2 * cfg.layers), ulp_noise_seed=1) if floors else None
+    names = ["prefill logits"] + [f"prefill {'k' if i % 2 == 0 else 'v'} cache, layer {i // 2}"
+                                  for i in range(2 * cfg.layers)]
+    figs = []
 
-    # ---------------- greedy decode, each side on its own tokens
-    diverged = None
+    def compare(what, dev_v, orc_v, nz_v):
+        dv = _dist(dev_v, orc_v, dt)
+        nv = _dist(nz_v, orc_v, dt) if nz_v is not None else (0.0, 0.0, 0.0)
+        figs.append({"what": what, "dev": [round(x, 6) for x in dv], "noisy_oracle": [round(x, 6) for x in nv],
+                     "ok": bool(_judge(dv, nv, dt))})
+
+    for i, nm in enumerate(names):
+        compare(nm, dev_pre[i], orc_pre[i], nz_pre[i] if floors else None)
+    last = lambda lg, j: d.argmax_host(np.asarray(lg, np.float32).reshape(-1, V)[j])
+    tok_o = [last(orc_pre[0], S - 1)]
+    tok_d = [last(dev_pre[0], S - 1)]
+    tok_n = [last(nz_pre[0], S - 1)] if floors else list(tok_o)
+    o_kv = orc_pre[1:]
+    n_kv = nz_pre[1:] if floors else None
+    del dev_pre, orc_pre, nz_pre
+
+    # ---------------- decode: every side is fed the oracle's greedy token
     for step in range(STEPS):
-        if dev_tok[-1] != o_tok[-1]:
-            diverged = step
-            break
-        p = S + step
-        tok = np.array([[o_tok[-1]]] * B, np.int32)
-        pos = d.pos_inputs(cfg, "decode", B, p, 1)
+        tok = np.array([[tok_o[-1]]] * B, np.int32)
+        p = d.pos_inputs(cfg, "decode", B, S + step, 1)
         x_b = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
-        p_b = core.buffer_from_host_buffer(ctx, pos, list(pos.shape), 4)
+        p_b = core.buffer_from_host_buffer(ctx, p, list(p.shape), 4)
         outs = api.execute_executable(ex_dec["handle"], [x_b, p_b] + wbufs + kv, len(g_dec["outvars"]))
         for b in kv + [x_b, p_b]:
             api.destroy_buffer(b)
         lg = core.buffer_to_numpy(ctx, outs[0], (B, 1, V), "f32")
         api.destroy_buffer(outs[0])
         kv = outs[1:]
-        t1 = time.time()
-        o = interp.run_mlir(t_dec, [tok, pos] + wf + o_kv)
-        t_oracle += time.time() - t1
+        o = interp.run_mlir(t_dec, [tok, p] + wf + o_kv)
         o_kv = o[1:]
-        check(lg, o[0], f"decode step {step} logits", dt)
-        dev_tok.append(d.argmax_host(lg[0, 0]))
-        o_tok.append(d.argmax_host(o[0][0, 0]))
-        margins.append(_top2(o[0][0, 0].astype(np.float32))[1])
-    if diverged is None and dev_tok[-1] != o_tok[-1]:
-        diverged = STEPS
+        nz = None
+        if floors:
+            nz = interp.run_mlir(t_dec, [tok, p] + wf + n_kv, ulp_noise_seed=100 + step)
+            n_kv = nz[1:]
+        compare(f"decode step {step} logits", lg, o[0], nz[0] if floors else None)
+        tok_o.append(last(o[0], 0))
+        tok_d.append(last(lg, 0))
+        tok_n.append(last(nz[0], 0) if floors else tok_o[-1])
+    t_oracle = time.time() - t1
     for i, b in enumerate(kv):
-        check(core.buffer_to_numpy(ctx, b, cshape, dt), o_kv[i], f"cache {i} after {STEPS} steps", dt)
+        dv = core.buffer_to_numpy(ctx, b, cshape, dt)
+        compare(f"{'k' if i % 2 == 0 else 'v'} cache, layer {i // 2}, after {STEPS} steps", dv, o_kv[i],
+                n_kv[i] if floors else None)
     for b in kv + wbufs:
         api.destroy_buffer(b)
-    bf = [f for f in figs if "frac_outside_2e-2" in f]
-    _report({"config": name, "prompt": S, "cache": T, "steps": STEPS, "tokens_device": dev_tok,
-             "tokens_oracle": o_tok, "diverged_at": diverged,
-             "oracle_top2_margin_min": min(margins), "oracle_top2_margin_at_divergence":
-                 margins[diverged] if diverged is not None and diverged < len(margins) else None,
+    binding = [s for s in range(len(tok_o)) if tok_n[s] == tok_o[s]]
+    token_fail = [s for s in binding if tok_d[s] != tok_o[s]]
+    fails = [f for f in figs if not f["ok"]]
+    _report({"config": name, "prompt": S, "cache": T, "steps": STEPS,
+             "tokens_oracle": tok_o, "tokens_device": tok_d, "tokens_noisy_oracle": tok_n,
+             "device_equals_oracle_steps": sum(int(a == b) for a, b in zip(tok_d, tok_o)),
+             "noisy_equals_oracle_steps": sum(int(a == b) for a, b in zip(tok_n, tok_o)),
+             "binding_steps": len(binding), "token_failures": token_fail,
              "tensors_compared": len(figs), "tensors_failing": len(fails),
-             "max_frac_outside_2e-2": max((f["frac_outside_2e-2"] for f in bf), default=0.0),
-             "max_rel_rms": max((f["rel_rms"] for f in bf), default=0.0),
-             "max_abs_err": max(f["max_abs_err"] for f in figs),
-             "seconds_device_side": round(t_dev, 1), "seconds_oracle": round(t_oracle, 1),
-             "worst": sorted(figs, key=lambda f: -f.get("frac_outside_2e-2", f["max_abs_err"]))[:5]})
-    assert diverged is None, f"{name}: greedy tokens differ from step {diverged}: {dev_tok} vs {o_tok}"
+             "seconds_device_prefill_and_upload": round(t_dev, 1), "seconds_oracle": round(t_oracle, 1),
+             "figures [frac outside bound, rel rms, max abs err]": figs})
+    assert not token_fail, f"{name}: greedy tokens differ from the oracle at steps {token_fail}: {tok_d} vs {tok_o}"
     assert not fails, f"{name}: {len(fails)} tensors outside tolerance, first: {fails[0]}"
 
 
@@ -248,6 +279,7 @@ def test_one_layer_every_intermediate(ctx, name):
     for b in bufs:
         api.destroy_buffer(b)
     want = interp.run_mlir(text, inputs)
+    rtol = 1e-4 if base.dtype == "f32" else 2e-2
     figs, fails = [], []
     for nm, (shape, dt), a, w in zip(m.returns, m.ret_types, got, want):
         op = kinds.get(nm, "output")
@@ -258,10 +290,12 @@ def test_one_layer_every_intermediate(ctx, name):
             ok = np.array_equal(np.asarray(a).astype(np.int64), wb.astype(np.int64))
             fig = {"what": f"%{nm} ({op})", "dtype": dt, "bit_exact": bool(ok), "ok": bool(ok)}
         else:
-            strict, excess, maxerr = close(a, w, dt)
+            # the model's precision sets the bound: a bf16 model's f32-typed values
+            # (softmax, RoPE products, converts) carry its bf16 inputs' rounding
+            strict, excess, maxerr = close(a, w, dt, rtol=rtol)
             fig = {"what": f"%{nm} ({op})", "dtype": dt, "max_abs_err": maxerr, "ok": bool(strict)}
-            if dt == "bf16" and not strict:
-                okm, bad, rr = close_model(a, w, "bf16")
+            if base.dtype == "bf16" and not strict:
+                okm, bad, rr = close_model(as_f32(np.asarray(a), dt), as_f32(np.asarray(w), dt), "bf16")
                 fig.update({"frac_outside_2e-2": bad, "rel_rms": rr, "ok": bool(okm)})
         figs.append(fig)
         if not fig["ok"]:
