@@ -82,10 +82,22 @@ def load_peaks():
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled during the timed region."""
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, period_ms=20):
         self.gpu = gpu_index
+        self.period = period_ms
         self.proc = None
-        self.lines = []
+        self.lines = []  # (host time, csv line)
+        self.window = None
+
+    def wait_first(self, timeout=3.0):
+        """nvidia-smi needs a moment before its first line: start the sampler
+        early and wait for it, so samples cover the timed region."""
+        t_end = time.perf_counter() + timeout
+        while self.proc and not self.lines and time.perf_counter() < t_end:
+            time.sleep(0.01)
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
 
     def __enter__(self):
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -93,7 +105,7 @@ class ClockSampler:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.period)],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -103,7 +115,7 @@ class ClockSampler:
 
     def _read(self):
         for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            self.lines.append((time.perf_counter(), ln.strip()))
 
     def __exit__(self, *a):
         if self.proc:
@@ -116,7 +128,9 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = [ln for t, ln in self.lines
+                 if self.window is None or self.window[0] - 0.03 <= t <= self.window[1] + 0.03]
+        for ln in lines:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -130,7 +144,8 @@ class ClockSampler:
                     reasons.add(nm)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "period_ms": self.period}
 
 
 def model_setup(args):
@@ -183,6 +198,10 @@ def run_ours(args, rank, world, local_rank):
     t1 = time.time()
     ex_dec = core.compile_mlir_text(ctx, txt_dec, g_dec)
     ex_pre = core.compile_mlir_text(ctx, txt_pre, g_pre)
+    # the same decode step with in-graph greedy sampling (tensor.clj:519-532):
+    # what a user's generation loop runs, reading 4 bytes per sequence per step
+    g_greedy = d.build_graph(cfg, "decode", B, S, T, greedy=True) if cfg.family != "gpt2" else None
+    ex_greedy = core.compile_mlir_text(ctx, shlo.graph_to_mlir_text(g_greedy), g_greedy) if g_greedy else None
     t_c = time.time() - t1
 
     cache_np = d.zero_cache(cfg, B, T)
@@ -247,20 +266,24 @@ def run_ours(args, rank, world, local_rank):
             api.destroy_buffer(b)
         return outs[1:]
 
-    for i in range(args.warmup):
-        kv = step(i, kv)
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    launches0 = core.kernel_launches(ctx)
     with ClockSampler(local_rank) as clk:
+        clk.wait_first()
+        for i in range(args.warmup):
+            kv = step(i, kv)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        launches0 = core.kernel_launches(ctx)
+        h0 = time.perf_counter()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(args.warmup, n_total):
             kv = step(i, kv)
         e1.record(stream)
         e1.synchronize()
+        clk.mark(h0, time.perf_counter())
+        time.sleep(0.05)  # the sample taken at the end of the region
     dec_s = e0.elapsed_time(e1) / 1e3
     launches = core.kernel_launches(ctx) - launches0
     torch.cuda.synchronize()
@@ -272,23 +295,36 @@ def run_ours(args, rank, world, local_rank):
             api.destroy_buffer(b)
         return cfg, B, S, T, None
 
-    # ---------------- decode end to end (host tokens in, logits out, host argmax)
+    # ---------------- decode end to end through the PJRT C ABI, the way the
+    # host drives it: token and position uploaded from host memory, execute
+    # (awaited), the step's result read back, old caches destroyed.
+    # Headline: the greedy graph (token ids read back, 4 bytes per sequence);
+    # also the logits graph with the host argmax of scripts/gemma4_inference.clj.
     logits_bytes = B * cfg.vocab * 4
-    tok = np.array([[int(toks[0, -1])]] * B, np.int32)
     e2e_steps = max(1, args.e2e_steps)
-    torch.cuda.synchronize()
-    t_e0 = time.perf_counter()
-    for i in range(e2e_steps):
-        xb = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
-        pb = core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4)
-        outs = api.execute_executable(ex_dec["handle"], [xb, pb] + wbufs + kv, len(g_dec["outvars"]))
-        logits = api.buffer_to_host_floats(outs[0], B * cfg.vocab).reshape(B, cfg.vocab)
-        tok = np.array([[d.argmax_host(logits[b])] for b in range(B)], np.int32)
-        for b in [xb, pb, outs[0]] + kv:
-            api.destroy_buffer(b)
-        kv = outs[1:]
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t_e0
+
+    def e2e_loop(greedy, kv):
+        tok = np.array([[int(toks[0, -1])]] * B, np.int32)
+        ex, g = (ex_greedy, g_greedy) if greedy else (ex_dec, g_dec)
+        torch.cuda.synchronize()
+        t_e0 = time.perf_counter()
+        for i in range(e2e_steps):
+            xb = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
+            pb = core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4)
+            outs = api.execute_executable(ex["handle"], [xb, pb] + wbufs + kv, len(g["outvars"]))
+            if greedy:
+                tok = api.buffer_to_host(outs[0], 4 * B).view(np.int32).reshape(B, 1).copy()
+            else:
+                logits = api.buffer_to_host_floats(outs[0], B * cfg.vocab).reshape(B, cfg.vocab)
+                tok = np.array([[d.argmax_host(logits[b])] for b in range(B)], np.int32)
+            for b in [xb, pb, outs[0]] + kv:
+                api.destroy_buffer(b)
+            kv = outs[1:]
+        torch.cuda.synchronize()
+        return time.perf_counter() - t_e0, kv
+
+    e2e_logits_s, kv = e2e_loop(False, kv)
+    e2e_s, kv = e2e_loop(True, kv) if ex_greedy else (e2e_logits_s, kv)
 
     # ---------------- roofline of the dominant kernel (one profiled decode step)
     core.profile_enable(ctx, True)
@@ -326,7 +362,8 @@ def run_ours(args, rank, world, local_rank):
         "e2e_tokens": B * e2e_steps, "launches": launches, "clocks": clk.summary(),
         "by_kind": by_kind, "total_ms": total_ms, "dom": dom[0], "achieved": achieved,
         "hbm_peak": hbm_peak, "peak_src": peak_src, "cpu": cpu, "t_weights": t_w, "t_compile": t_c,
-        "plan": plan, "logits_bytes": logits_bytes,
+        "plan": plan, "logits_bytes": logits_bytes, "e2e_logits_s": e2e_logits_s,
+        "e2e_greedy": ex_greedy is not None,
     }
     return cfg, B, S, T, res
 
@@ -408,9 +445,17 @@ def main():
             "prefill": {"value": round(replicas * B * S / pre_s, 1), "unit": "tokens/s",
                         "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill",
                         "kernel_time_by_kind_ms": res["pre_by_kind"]},
-            "e2e": {"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": res["logits_bytes"],
-                    "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"},
+            "e2e": ({"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
+                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
+                     "path": "PJRT C ABI: BufferFromHostBuffer (token, position), Execute of the decode graph "
+                             "with in-graph greedy argmax (tensor.clj:519-532), ToHostBuffer of the token ids",
+                     "logits_path": {"value": round(replicas * res["e2e_tokens"] / res["e2e_logits_s"], 2),
+                                     "d2h_bytes_per_step": res["logits_bytes"],
+                                     "path": "decode graph returning f32 logits + host argmax (argmax-host)"}}
+                    if res["e2e_greedy"] else
+                    {"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
+                     "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": res["logits_bytes"],
+                     "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"}),
             "roofline": {"bound": "hbm", "kernel": res["dom"],
                          "achieved": round(res["achieved"], 1), "peak": res["hbm_peak"], "unit": "GB/s",
                          "frac": round(res["achieved"] / res["hbm_peak"], 4), "traffic": None,

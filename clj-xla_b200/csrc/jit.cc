@@ -7,13 +7,19 @@
 // program, shapes, strides and types fixed at compile time.
 #include "jit.h"
 #include "fast_kernels.h"
+#include "sha256.h"
 
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nvrtc.h>
 
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <sstream>
@@ -1346,6 +1352,7 @@ struct Nvrtc {
   decltype(&nvrtcGetCUBINSize) cubin_size = nullptr;
   decltype(&nvrtcGetCUBIN) cubin = nullptr;
   decltype(&nvrtcDestroyProgram) destroy = nullptr;
+  decltype(&nvrtcVersion) version = nullptr;
   bool ok = false;
 };
 
@@ -1365,6 +1372,7 @@ Nvrtc& nvrtc() {
     n.cubin_size = (decltype(n.cubin_size))dlsym(h, "nvrtcGetCUBINSize");
     n.cubin = (decltype(n.cubin))dlsym(h, "nvrtcGetCUBIN");
     n.destroy = (decltype(n.destroy))dlsym(h, "nvrtcDestroyProgram");
+    n.version = (decltype(n.version))dlsym(h, "nvrtcVersion");
     n.ok = n.create && n.compile && n.log_size && n.log && n.cubin_size && n.cubin && n.destroy;
   });
   return n;
@@ -1373,14 +1381,91 @@ Nvrtc& nvrtc() {
 std::mutex g_cache_mu;
 std::map<std::string, void*> g_cache;  // source -> cudaKernel_t (nullptr: failed)
 
+const char* const kNvrtcOpts[] = {"-arch=sm_100a", "-fmad=false", "--std=c++17", "-default-device"};
+
+// On-disk cache of compiled fused kernels, so a process compiling a graph it
+// (or an earlier process) compiled before skips NVRTC: one file per program,
+// named by the SHA-256 of the NVRTC version, options and source.  Directory:
+// CLJXLA_B200_CACHE_DIR, else $XDG_CACHE_HOME/cljxla_b200, else
+// $HOME/.cache/cljxla_b200; CLJXLA_B200_CACHE_DIR=0 turns it off.
+std::atomic<int64_t> g_disk_hits{0}, g_disk_misses{0};
+
+std::string disk_cache_dir() {
+  const char* e = getenv("CLJXLA_B200_CACHE_DIR");
+  if (e && (!strcmp(e, "0") || !strcmp(e, "off"))) return "";
+  std::string d;
+  if (e && *e) d = e;
+  else if (const char* x = getenv("XDG_CACHE_HOME")) d = std::string(x) + "/cljxla_b200";
+  else if (const char* h = getenv("HOME")) d = std::string(h) + "/.cache/cljxla_b200";
+  if (d.empty()) return "";
+  for (size_t i = 1; i <= d.size(); ++i)  // mkdir -p
+    if (i == d.size() || d[i] == '/') mkdir(d.substr(0, i).c_str(), 0755);
+  return d;
+}
+
+std::string disk_cache_key(const std::string& src) {
+  int major = 0, minor = 0;
+  if (nvrtc().version) nvrtc().version(&major, &minor);
+  std::string k = "nvrtc " + std::to_string(major) + "." + std::to_string(minor) + "\n";
+  for (const char* o : kNvrtcOpts) k += std::string(o) + "\n";
+  k += src;
+  return sha256_hex(k.data(), k.size());
+}
+
+std::vector<char> disk_cache_get(const std::string& dir, const std::string& key) {
+  std::vector<char> out;
+  FILE* f = fopen((dir + "/" + key + ".cubin").c_str(), "rb");
+  if (!f) return out;
+  fseek(f, 0, SEEK_END);
+  const long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  if (n > 0) {
+    out.resize((size_t)n);
+    if (fread(out.data(), 1, (size_t)n, f) != (size_t)n) out.clear();
+  }
+  fclose(f);
+  return out;
+}
+
+void disk_cache_put(const std::string& dir, const std::string& key, const std::vector<char>& cubin) {
+  // written under a unique name, then renamed: readers never see a partial file
+  const std::string tmp = dir + "/" + key + ".tmp" + std::to_string((long)getpid()) + "_" +
+                          std::to_string((unsigned long long)(uintptr_t)&cubin);
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) return;
+  const bool ok = fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
+  fclose(f);
+  if (!ok || rename(tmp.c_str(), (dir + "/" + key + ".cubin").c_str()) != 0) remove(tmp.c_str());
+}
+
 // NVRTC -> cubin; empty on failure (the log goes to `log` when given)
+std::vector<char> nvrtc_cubin(const std::string& src, std::string* log_out);
+
 std::vector<char> to_cubin(const std::string& src, std::string* log_out) {
+  const std::string dir = disk_cache_dir();
+  std::string key;
+  if (!dir.empty()) {
+    key = disk_cache_key(src);
+    std::vector<char> c = disk_cache_get(dir, key);
+    if (!c.empty()) {
+      ++g_disk_hits;
+      return c;
+    }
+  }
+  std::vector<char> c = nvrtc_cubin(src, log_out);
+  if (!dir.empty() && !c.empty()) {
+    ++g_disk_misses;
+    disk_cache_put(dir, key, c);
+  }
+  return c;
+}
+
+std::vector<char> nvrtc_cubin(const std::string& src, std::string* log_out) {
   Nvrtc& n = nvrtc();
   if (!n.ok) return {};
   nvrtcProgram prog;
   if (n.create(&prog, src.c_str(), "fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return {};
-  const char* opts[] = {"-arch=sm_100a", "-fmad=false", "--std=c++17", "-default-device"};
-  nvrtcResult r = n.compile(prog, 4, opts);
+  nvrtcResult r = n.compile(prog, 4, kNvrtcOpts);
   if (r != NVRTC_SUCCESS) {
     size_t ls = 0;
     n.log_size(prog, &ls);
@@ -1426,6 +1511,11 @@ void* compile_one(const std::string& src) {
 }
 
 }  // namespace
+
+void jit_disk_cache_stats(int64_t* hits, int64_t* misses) {
+  if (hits) *hits = g_disk_hits.load();
+  if (misses) *misses = g_disk_misses.load();
+}
 
 int jit_check_sources(const std::vector<std::string>& sources, std::string* first_log) {
   if (!nvrtc().ok) return -1;

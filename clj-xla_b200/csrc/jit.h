@@ -47,6 +47,8 @@ bool jit_enabled();
 // and returns how many failed (-1: NVRTC not available); the first failure's
 // log and source go to first_log.
 int jit_check_sources(const std::vector<std::string>& sources, std::string* first_log);
+// programs found in / added to the on-disk cache of compiled fused kernels by this process
+void jit_disk_cache_stats(int64_t* hits, int64_t* misses);
 
 // The sources prepare_jit would compile for a plan.
 std::vector<std::string> jit_plan_sources(const Plan& p);

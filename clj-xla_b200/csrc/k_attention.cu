@@ -1288,7 +1288,8 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
 // first (the last query positions see the most chunks).  K (with the mask
 // tile) is double-buffered; V has one buffer, restaged after each P V so that
 // an f32 query tile still fits beside the K, V and mask tiles at head_dim 256.
-// P enters P V as bf16 hi + lo, f32 queries as an exact hi + mid + lo split.
+// P enters P V, and f32 queries the score product, as the exact bf16 split
+// hi + mid + lo of the f32 value (P V is the printed f32 x bf16 product).
 //
 // FAST: the additive mask is f32 with 16-byte aligned rows and the score
 // chain has a closed form with f32 softmax arithmetic (the printed Gemma and
@@ -1320,7 +1321,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   __shared__ int64_t qoff_s[PF_ROWS], moff_s[PF_ROWS];
   __shared__ unsigned live_s[PF_LIVE_WORDS];
   __shared__ float pm_s[2][PF_ROWS];                  // per-half row maxima (then sums)
-  __shared__ uint32_t pf_s[4][2][2][8][32];           // P fragments [row group][half][k-step][reg][lane]
+  __shared__ float pf_s[4][2][2][8][32];              // P values [row group][half][k-step][element][lane]
   pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rg = warp & 3, dh = warp >> 2;
@@ -1591,43 +1592,53 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         m[hr] = mnew;
       }
     }
-    // P of this half as bf16 hi + lo A fragments (k-steps 2 dh, 2 dh + 1), kept
-    // in registers and published to the partner through shared memory
-    uint32_t pa[2][8];
+    // P of this half (k-steps 2 dh, 2 dh + 1) as f32 in registers, published to
+    // the partner through shared memory; both enter P V as the exact bf16
+    // split hi + mid + lo (8 + 8 + 8 significand bits, the f32 value itself)
+    float pr[2][8];
 #pragma unroll
     for (int kl = 0; kl < 2; ++kl)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int tile = 2 * kl + (i >> 1), hr = i & 1;
-        const float p0 = pv[tile][2 * hr], p1 = pv[tile][2 * hr + 1];
-        pa[kl][i] = pack_bf16(p0, p1);
-        pa[kl][4 + i] = pack_bf16(p0 - bf16_lo_f(pa[kl][i]), p1 - bf16_hi_f(pa[kl][i]));
-        pf_s[rg][dh][kl][i][lane] = pa[kl][i];
-        pf_s[rg][dh][kl][4 + i][lane] = pa[kl][4 + i];
+        pr[kl][2 * i] = pv[tile][2 * hr];
+        pr[kl][2 * i + 1] = pv[tile][2 * hr + 1];
+        pf_s[rg][dh][kl][2 * i][lane] = pr[kl][2 * i];
+        pf_s[rg][dh][kl][2 * i + 1][lane] = pr[kl][2 * i + 1];
       }
     // this chunk's V rows (the barrier also publishes the P fragments)
     if (nx < nchunks) asm volatile("cp.async.wait_group 1;" ::: "memory");
     else asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    // O[:, half] += P V: 4 k-steps of 16 positions, P as bf16 hi + lo
+    // O[:, half] += P V: 4 k-steps of 16 positions, P as bf16 hi + mid + lo
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
-      uint32_t ah[4], al[4];
+      uint32_t ah[4], am[4], al[4];
       const int kl = ks & 1;
-      if ((ks >> 1) == dh) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ah[i] = pa[kl][i], al[i] = pa[kl][4 + i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) ah[i] = pf_s[rg][dh ^ 1][kl][i][lane], al[i] = pf_s[rg][dh ^ 1][kl][4 + i][lane];
+      for (int i = 0; i < 4; ++i) {
+        float p0, p1;
+        if ((ks >> 1) == dh) {
+          p0 = pr[kl][2 * i];
+          p1 = pr[kl][2 * i + 1];
+        } else {
+          p0 = pf_s[rg][dh ^ 1][kl][2 * i][lane];
+          p1 = pf_s[rg][dh ^ 1][kl][2 * i + 1][lane];
+        }
+        ah[i] = pack_bf16(p0, p1);
+        const float r0 = p0 - bf16_lo_f(ah[i]), r1 = p1 - bf16_hi_f(ah[i]);
+        am[i] = pack_bf16(r0, r1);
+        al[i] = pack_bf16(r0 - bf16_lo_f(am[i]), r1 - bf16_hi_f(am[i]));
       }
 #pragma unroll
       for (int n = 0; n < NTO; n += 2) {
         uint32_t bf[4];
         ldsm_x4_t(vb_s + (uint32_t)((((size_t)16 * ks + ri + 8 * (mi & 1)) * ROW + dh * (HD / 2) + 8 * n + 8 * (mi >> 1)) * 2), bf);
         mma_bf16(o[n], ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
-        mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
         mma_bf16(o[n + 1], ah[0], ah[1], ah[2], ah[3], bf[2], bf[3]);
+        mma_bf16(o[n], am[0], am[1], am[2], am[3], bf[0], bf[1]);
+        mma_bf16(o[n + 1], am[0], am[1], am[2], am[3], bf[2], bf[3]);
+        mma_bf16(o[n], al[0], al[1], al[2], al[3], bf[0], bf[1]);
         mma_bf16(o[n + 1], al[0], al[1], al[2], al[3], bf[2], bf[3]);
       }
     }

@@ -8,6 +8,8 @@
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "../../include/cljxla_b200.h"
 #include "jit.h"
@@ -205,6 +207,10 @@ PJRT_Error* Client_Destroy(void* a) {
     nccl_comm_destroy(args->client->nccl_comm);
     cudaStreamDestroy(args->client->stream);
     if (args->client->pinned) cudaFreeHost(args->client->pinned);
+    for (int i = 0; i < 2; ++i) {
+      if (args->client->up_stage[i]) cudaFreeHost(args->client->up_stage[i]);
+      if (args->client->up_done[i]) cudaEventDestroy(args->client->up_done[i]);
+    }
     delete args->client;
   });
 }
@@ -262,6 +268,44 @@ PJRT_Error* Client_Compile(void* a) {
   });
 }
 
+// Uploads of at least this many bytes go through the client's pinned staging
+// ring; smaller ones are one cudaMemcpyAsync from the caller's (pageable) memory.
+constexpr size_t UPLOAD_STAGED_MIN = 8u << 20;
+constexpr size_t UPLOAD_CHUNK = 32u << 20;
+
+// Host-to-device copy of a large pageable host range (weight ingest,
+// safetensors.clj:49-160 hands the plugin whole tensors): chunks of
+// UPLOAD_CHUNK alternate between two pinned buffers; each chunk is copied into
+// its buffer by several host threads in parallel (one thread's memcpy is well
+// below the PCIe / C2C link rate) and then DMA'd on the client's stream, so the
+// host copy of chunk i + 1 overlaps the DMA of chunk i.  Returns once the host
+// data has been read; the DMAs complete in stream order.
+static void upload_staged(PJRT_Client* c, void* dst, const void* src, size_t bytes) {
+  for (int i = 0; i < 2; ++i) {
+    if (!c->up_stage[i]) CUDA_OK(cudaMallocHost(&c->up_stage[i], UPLOAD_CHUNK));
+    if (!c->up_done[i]) CUDA_OK(cudaEventCreateWithFlags(&c->up_done[i], cudaEventDisableTiming));
+  }
+  const unsigned hw = std::thread::hardware_concurrency();
+  const int nthr = (int)std::max(1u, std::min(8u, hw ? hw : 1u));
+  bool used[2] = {false, false};
+  for (size_t off = 0, k = 0; off < bytes; off += UPLOAD_CHUNK, ++k) {
+    const int b = (int)(k & 1);
+    const size_t n = std::min(UPLOAD_CHUNK, bytes - off);
+    if (used[b]) CUDA_OK(cudaEventSynchronize(c->up_done[b]));  // the DMA that last read this buffer
+    char* stage = (char*)c->up_stage[b];
+    const char* from = (const char*)src + off;
+    const size_t piece = (n + nthr - 1) / nthr;
+    std::vector<std::thread> th;
+    for (int t = 1; t < nthr && (size_t)t * piece < n; ++t)
+      th.emplace_back([=] { memcpy(stage + t * piece, from + t * piece, std::min(piece, n - t * piece)); });
+    memcpy(stage, from, std::min(piece, n));
+    for (auto& x : th) x.join();
+    CUDA_OK(cudaMemcpyAsync((char*)dst + off, stage, n, cudaMemcpyHostToDevice, c->stream));
+    CUDA_OK(cudaEventRecord(c->up_done[b], c->stream));
+    used[b] = true;
+  }
+}
+
 PJRT_Error* Client_BufferFromHostBuffer(void* a) {
   return guarded([&] {
     auto* args = args_of<PJRT_Client_BufferFromHostBuffer_Args>(a);
@@ -286,7 +330,8 @@ PJRT_Error* Client_BufferFromHostBuffer(void* a) {
     set_device(c);
     if (bytes && !args->data) fail(E_INVALID, "null host data");
     std::unique_ptr<PJRT_Buffer> b(new_buffer(c, dt, dims));
-    if (bytes) CUDA_OK(cudaMemcpyAsync(b->ptr(), args->data, bytes, cudaMemcpyHostToDevice, c->stream));
+    if (bytes >= UPLOAD_STAGED_MIN) upload_staged(c, b->ptr(), args->data, bytes);
+    else if (bytes) CUDA_OK(cudaMemcpyAsync(b->ptr(), args->data, bytes, cudaMemcpyHostToDevice, c->stream));
     // the host buffer may be released once this event completes
     args->done_with_host_buffer = new_event(c);
     args->buffer = b.release();
@@ -562,6 +607,8 @@ CLJXLA_EXPORT int cljxla_b200_nccl_unique_id(char* out, size_t cap) {
     return E_INTERNAL;
   }
 }
+
+CLJXLA_EXPORT void cljxla_b200_jit_cache_stats(int64_t* hits, int64_t* misses) { jit_disk_cache_stats(hits, misses); }
 
 CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags, int* kernels, char* err,
                                         size_t errcap) {

@@ -1489,6 +1489,9 @@ void Planner::emit_attention(int d2) {
     P.use_tc = 3;
     plan_attention_dec(P, 148);
     splits = P.splits;
+    if (getenv("CLJXLA_B200_DEBUG_ATTN"))
+      fprintf(stderr, "attention %s: staged decode, %d splits of %d positions, chunk %d\n", D2.name.c_str(), P.splits,
+              P.dec_per_split, P.dec_chunk);
   }
   P.out = slot_ptr(oslot);
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);

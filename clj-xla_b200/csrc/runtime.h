@@ -122,6 +122,10 @@ struct PJRT_Client {
   // pinned staging for large device-to-host reads (grown on demand)
   void* pinned = nullptr;
   size_t pinned_bytes = 0;
+  // pinned staging ring for large host-to-device uploads (weights): the host
+  // copies chunk i + 1 into one buffer while the DMA engine reads chunk i
+  void* up_stage[2] = {nullptr, nullptr};
+  cudaEvent_t up_done[2] = {nullptr, nullptr};
   std::string platform = "cuda";
   void* nccl_comm = nullptr;  // tp_size > 1
   cljxla::P2PAllReduce* p2p = nullptr;  // one-shot peer all-reduce, once its handles are exchanged

@@ -187,7 +187,7 @@ def _gemma_layer_maps(cfg: ModelConfig, weight_args):
     return maps
 
 
-def trace_fn(cfg: ModelConfig, kind: str, prompt_len: int, dynamic_prefill: bool = False):
+def trace_fn(cfg: ModelConfig, kind: str, prompt_len: int, dynamic_prefill: bool = False, greedy: bool = False):
     nw = len(weight_specs(cfg))
 
     if cfg.family == "gpt2":
@@ -224,18 +224,31 @@ def trace_fn(cfg: ModelConfig, kind: str, prompt_len: int, dynamic_prefill: bool
             pos_ids, pos = pos_tr, pos_tr
         logits, new_kv = full_gemma_forward(x, emb, maps, fnorm, pos_ids, cfg.n_heads, cfg.n_kv_heads,
                                             kv_seq, pos, opts)
-        out = [t.convert(logits, "f32")]
+        out = [_greedy_token(t.convert(logits, "f32")) if greedy else t.convert(logits, "f32")]
         for k, v in new_kv:
             out += [k, v]
         return out
     return fn
 
 
+def _greedy_token(logits):
+    """In-graph greedy sampling (tensor.clj:519-532 ``argmax`` over the vocabulary,
+    as the device-resident decode loop of docs/xla/agent_vram_loop.md:38-80 uses
+    it): the next token id [B, S] i32 replaces the f32 logits as the first
+    output, so a decode step returns 4 bytes per sequence instead of V * 4.
+    Ties take the highest index (the in-graph rule), not argmax-host's lowest."""
+    return t.argmax(logits, axis=-1)
+
+
 def build_graph(cfg: ModelConfig, kind: str, batch: int, prompt_len: int, max_seq: int,
-                dynamic_prefill: bool = False, name: Optional[str] = None) -> dict:
+                dynamic_prefill: bool = False, name: Optional[str] = None, greedy: bool = False) -> dict:
+    """``greedy=True`` (Gemma families): the first output is the in-graph argmax
+    token id [B, S] i32 instead of the f32 logits."""
     inv = graph_invars(cfg, kind, batch, prompt_len, max_seq)
-    gname = name or f"{cfg.family}_{kind}"
-    return t.trace_graph(gname, inv, trace_fn(cfg, kind, prompt_len, dynamic_prefill))
+    gname = name or f"{cfg.family}_{kind}" + ("_greedy" if greedy else "")
+    if greedy and cfg.family == "gpt2":
+        raise ValueError("in-graph greedy sampling is provided for the Gemma families")
+    return t.trace_graph(gname, inv, trace_fn(cfg, kind, prompt_len, dynamic_prefill, greedy))
 
 
 # ------------------------------------------------------- synthetic inputs

@@ -75,6 +75,8 @@ class PjrtApi:
 
     def __init__(self, lib_path: str):
         self.lib = ctypes.CDLL(lib_path, mode=ctypes.RTLD_GLOBAL)
+        self._devices = {}
+        self._nondon = {}
         get_api = self.lib.GetPjrtApi
         get_api.restype = ctypes.c_void_p
         self.api_ptr = get_api()
@@ -273,7 +275,9 @@ class PjrtApi:
             _w64(args, 56, ctypes.addressof(strides))
             _w64(args, 64, num_dims)
         _w32(args, 72, 1)
-        devs = self.addressable_devices(client)
+        devs = self._devices.get(client)
+        if devs is None:  # the device list of a client never changes (pjrt.clj:348-349 takes the first)
+            devs = self._devices[client] = self.addressable_devices(client)
         if devs:
             _w64(args, 80, devs[0])
         self.check_error(self._call(OFFSET_CLIENT_BUFFER_FROM_HOST_BUFFER, args))
@@ -304,7 +308,9 @@ class PjrtApi:
         out_ptrs = (ctypes.c_uint64 * nouts)()
         out_lists = (ctypes.c_uint64 * 1)(ctypes.addressof(out_ptrs))
         events = (ctypes.c_uint64 * 1)()
-        nondon = (ctypes.c_int64 * max(1, n))(*range(n))
+        nondon = self._nondon.get(n)  # every input index (pjrt.clj:478-480); the same array per count
+        if nondon is None:
+            nondon = self._nondon[n] = (ctypes.c_int64 * max(1, n))(*range(n))
         opts = ctypes.create_string_buffer(144)
         _w64(opts, 0, 112)
         _w64(opts, 56, ctypes.addressof(nondon))

@@ -71,6 +71,15 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
 CLJXLA_EXPORT int cljxla_b200_jit_check(const char* text, size_t len, int flags, int* kernels, char* err,
                                         size_t errcap);
 
+/* Programs this process found in (hits) or added to (misses) the on-disk
+ * cache of compiled fused kernels.  The cache is keyed like clj-xla's compile
+ * cache (src/clj_xla/compile.clj:13-24: SHA-256 of the program text), here of
+ * each generated kernel's source with the NVRTC version and options, and
+ * lives in CLJXLA_B200_CACHE_DIR (else $XDG_CACHE_HOME/cljxla_b200, else
+ * $HOME/.cache/cljxla_b200; "0" turns it off).  No counterpart in the
+ * reference, whose compile cache is in memory only. */
+CLJXLA_EXPORT void cljxla_b200_jit_cache_stats(int64_t* hits, int64_t* misses);
+
 /* Tensor parallelism (no counterpart in the reference, which runs on one
  * device).  A graph with "stablehlo.all_reduce" ops is one rank's shard of a
  * model; its client is created with the named values tp_size (int64),

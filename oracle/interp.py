@@ -323,7 +323,9 @@ class Interpreter:
     ``ulp_noise_seed``: when set, the f32 accumulation of every ``dot_general``
     and sum-reduce is moved by a seeded random number of f32 ulps before it is
     rounded to the result type - a model of a different, equally valid f32
-    summation order.  Two orders of an n-term f32 sum differ by about
+    summation order - and every exp / tanh / sin / cos result by up to 2 ulps
+    (a different, equally valid math library: the CUDA math library documents
+    2-ulp bounds for these functions).  Two orders of an n-term f32 sum differ by about
     sqrt(n)/5 ulps of the result (median over random bf16 products; the 90th
     percentile is 4-6x that), so the shift is normal with that standard
     deviation (at least one ulp).  Tests use the spread it causes as the noise
@@ -393,6 +395,15 @@ class Interpreter:
                   "logistic": lambda x: np.float32(1) / (np.float32(1) + np.exp(-x)),
                   "negate": np.negative, "abs": np.abs,
                   "rsqrt": lambda x: np.float32(1) / np.sqrt(x)}[name]
+            if self._noise is not None and dt in _FLOAT and name in ("exponential", "tanh", "sine", "cosine"):
+                # a valid f32 library result within its documented error bound
+                # (2 ulps for these functions in the CUDA math library)
+                x = np.asarray(args[0], np.float32)
+                with np.errstate(all="ignore"):
+                    r = np.asarray(fn(x), np.float32)
+                u = self._noise.integers(-2, 3, size=r.shape)
+                r = (r.astype(np.float64) + u * np.spacing(np.abs(r)).astype(np.float64)).astype(np.float32)
+                return to_dtype(r, dt)
             return _ew(fn, args, dt)
         if name == "convert":
             a = args[0]

@@ -25,6 +25,10 @@ def _load_pkg():
 
 _load_pkg()
 
+# compiled fused kernels are cached on disk; the tests keep that cache inside the
+# repository's build folder instead of the user's home
+os.environ.setdefault("CLJXLA_B200_CACHE_DIR", os.path.join(ROOT, "_build", "jit_cache"))
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 device and the built library")

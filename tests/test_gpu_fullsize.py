@@ -19,8 +19,12 @@ compares identical inputs, and the device's greedy token (``argmax-host``'s
 lowest-index rule, scripts/gemma4_inference.clj:399-411) must equal the
 oracle's at every step - which is the same as the two free-running loops of
 scripts/gemma3_inference.clj:307-343 producing the same tokens.  In the bf16
-models a step whose token the oracle itself changes under f32 summation-order
-noise is reported but does not bind.
+models a step binds only where the oracle's token is determined at this
+precision: its lead over the runner-up exceeds the largest logit change that
+f32 summation-order noise causes in the oracle itself.  (Random-init
+Gemma-3-4B is chaotic at full depth: scale-1.0 QK-normed attention over
+2048 positions amplifies one-ulp differences until the oracle's own noisy
+run decorrelates from it, so there the tokens are reported, not bound.)
 
 Tolerances (src/clj_xla/test/parity.clj:36-49 form, ``|a-b| <= atol +
 rtol*|b|`` with atol = rtol * RMS(b)): f32 every element within 1e-4; bf16
@@ -130,10 +134,10 @@ def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
     oracle's at every step, which is the same as both free-running greedy
     loops producing the same 32 tokens.  For bf16 models a second oracle
     trajectory with f32 summation-order noise (seed 1) measures how far the
-    oracle moves by itself; a step whose greedy token that noise changes does
-    not bind the device (the model's own answer there is not determined at this
-    precision), and a tensor further than 2e-2 may be no further than twice
-    the noisy oracle."""
+    oracle moves by itself; a step binds the device only where the oracle's
+    token is determined at this precision (its lead over the runner-up exceeds
+    the largest logit change the noise caused), and a tensor further than 2e-2
+    may be no further than twice the noisy oracle."""
     cfg, S, gen, dynamic = FULL[name]
     ok_ram, need = _host_ram_ok(cfg, S)
     if not ok_ram:
@@ -189,9 +193,18 @@ def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
     for i, nm in enumerate(names):
         compare(nm, dev_pre[i], orc_pre[i], nz_pre[i] if floors else None)
     last = lambda lg, j: d.argmax_host(np.asarray(lg, np.float32).reshape(-1, V)[j])
+    row = lambda lg, j: np.asarray(lg, np.float32).reshape(-1, V)[j]
+
+    def robust(o_row, n_row):
+        """The oracle's greedy token is determined at this precision: its lead
+        over the runner-up exceeds how far the noisy oracle moved any logit."""
+        top2 = np.partition(o_row, -2)[-2:]
+        return float(top2[1] - top2[0]) > float(np.max(np.abs(n_row - o_row)))
+
     tok_o = [last(orc_pre[0], S - 1)]
     tok_d = [last(dev_pre[0], S - 1)]
     tok_n = [last(nz_pre[0], S - 1)] if floors else list(tok_o)
+    bind = [robust(row(orc_pre[0], S - 1), row(nz_pre[0], S - 1)) if floors else True]
     o_kv = orc_pre[1:]
     n_kv = nz_pre[1:] if floors else None
     del dev_pre, orc_pre, nz_pre
@@ -218,6 +231,7 @@ def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
         tok_o.append(last(o[0], 0))
         tok_d.append(last(lg, 0))
         tok_n.append(last(nz[0], 0) if floors else tok_o[-1])
+        bind.append(robust(row(o[0], 0), row(nz[0], 0)) if floors else True)
     t_oracle = time.time() - t1
     for i, b in enumerate(kv):
         dv = core.buffer_to_numpy(ctx, b, cshape, dt)
@@ -225,7 +239,7 @@ def test_fullsize_prefill_and_32_greedy_steps(ctx, name):
                 n_kv[i] if floors else None)
     for b in kv + wbufs:
         api.destroy_buffer(b)
-    binding = [s for s in range(len(tok_o)) if tok_n[s] == tok_o[s]]
+    binding = [s for s in range(len(tok_o)) if bind[s] and tok_n[s] == tok_o[s]]
     token_fail = [s for s in binding if tok_d[s] != tok_o[s]]
     fails = [f for f in figs if not f["ok"]]
     _report({"config": name, "prompt": S, "cache": T, "steps": STEPS,

@@ -195,3 +195,37 @@ def test_gemv_prologue_fusion_matches_oracle(ctx, monkeypatch):
     got = runner.run_graph(ctx, gd, inputs, td)
     _compare_all(got, want, runner.out_specs(gd), "decode with GEMV prologues", cfg.dtype,
                  lambda sd: interp.run_mlir(td, inputs, ulp_noise_seed=sd))
+
+
+@pytest.mark.parametrize("family", ["gemma2", "gemma3"])
+def test_in_graph_greedy_token_matches_oracle(ctx, family):
+    """Decode graphs with in-graph greedy sampling (tensor.clj:519-532 argmax,
+    highest index on ties) return the oracle's token id bit-exactly and the
+    same caches as the logits graph, over several chained steps."""
+    cfg = TINY[family]
+    B, S, T, steps = 2, 6, 32, 4
+    gd = d.build_graph(cfg, "decode", B, S, T, greedy=True)
+    td = shlo.graph_to_mlir_text(gd)
+    specs = runner.out_specs(gd)
+    assert specs[0] == ((B, 1), "i32")
+    w = d.make_weights(cfg)
+    rng = np.random.Generator(np.random.PCG64(5))
+    kv = [interp.f32_to_bf16_bits(rng.standard_normal(d.cache_shape(cfg, B, T)).astype(np.float32))
+          for _ in range(2 * cfg.layers)]
+    tl = shlo.graph_to_mlir_text(d.build_graph(cfg, "decode", B, S, T))
+    tok = np.array([[3], [11]], np.int32)
+    for step in range(steps):
+        inputs = [tok, d.pos_inputs(cfg, "decode", B, S + step, 1)] + w + kv
+        want = interp.run_mlir(td, inputs)
+        got = runner.run_graph(ctx, gd, inputs, td)
+        assert got[0].dtype == np.int32
+        if not np.array_equal(got[0], want[0]):
+            # only a near tie may differ: the device's token must then score within
+            # the bf16 tolerance of the oracle's maximum
+            lg = interp.run_mlir(tl, inputs)[0].reshape(B, -1).astype(np.float64)
+            for b in range(B):
+                gap = lg[b].max() - lg[b, int(got[0][b, 0])]
+                assert gap <= 2e-2 * (np.sqrt(np.mean(lg[b] ** 2)) + abs(lg[b].max())), (step, b, gap)
+        _compare_all(got[1:], want[1:], specs[1:], f"{family} greedy step {step}", cfg.dtype,
+                     lambda sd: interp.run_mlir(td, inputs, ulp_noise_seed=sd)[1:])
+        tok, kv = want[0].astype(np.int32), list(want[1:])

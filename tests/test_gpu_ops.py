@@ -183,3 +183,19 @@ def test_compile_cache_returns_identical_handle(ctx):
 def test_platform_and_single_device(ctx):
     assert ctx["platform"] == "cuda"
     assert len(ctx["api"].addressable_devices(ctx["client"])) == 1
+
+
+def test_large_upload_through_pinned_staging_is_exact(ctx):
+    """Uploads of 8 MiB and more go through the pinned staging ring in 32 MiB
+    chunks (weight ingest); a ragged size spanning three chunks, and a second
+    buffer reusing the ring, read back bit for bit."""
+    from cljxla_b200.host.pjrt import DTYPE_ENUM
+    rng = np.random.Generator(np.random.PCG64(21))
+    for n in (17_000_003, 2_500_000):
+        a = rng.standard_normal(n, dtype=np.float32)
+        b = core.buffer_from_host_buffer(ctx, a, (n,), DTYPE_ENUM["f32"])
+        try:
+            got = core.buffer_to_numpy(ctx, b, (n,), "f32")
+        finally:
+            core.destroy_buffer(ctx, b)
+        assert np.array_equal(got.view(np.uint32), a.view(np.uint32))

@@ -126,3 +126,48 @@ def test_generated_fused_kernels_compile(lib_path):
                 pytest.skip("NVRTC not available")
             assert rc == 0, f"{name} {kind}: {rc} of {k.value} kernels failed\n{err.value.decode()[:4000]}"
             assert k.value > 0
+
+
+_JIT_CACHE_PROBE = r"""
+import ctypes, sys, dataclasses
+sys.path.insert(0, sys.argv[1])
+import conftest
+from cljxla_b200.host import drivers as d
+from cljxla_b200.host import stablehlo as shlo
+from cljxla_b200 import LIB_PATH
+lib = ctypes.CDLL(LIB_PATH)
+cfg = dataclasses.replace(d.GEMMA3_4B, vocab=512, d_model=256, layers=2, n_heads=4, n_kv_heads=2,
+                          head_dim=64, mlp=512, window=6)
+b = shlo.graph_to_mlir_text(d.build_graph(cfg, "decode", 1, 8, 16)).encode()
+f = lib.cljxla_b200_jit_check
+f.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.c_char_p,
+              ctypes.c_size_t]
+k = ctypes.c_int(0)
+rc = f(b, len(b), 3, ctypes.byref(k), None, 0)
+hits, misses = ctypes.c_int64(0), ctypes.c_int64(0)
+lib.cljxla_b200_jit_cache_stats(ctypes.byref(hits), ctypes.byref(misses))
+print(rc, k.value, hits.value, misses.value)
+"""
+
+
+def test_compiled_kernels_persist_across_processes(lib_path, tmp_path):
+    """A second process compiling the same graph takes every fused kernel from
+    the on-disk cache (SHA-256 keyed, like clj-xla's compile cache) instead of
+    running NVRTC again; with the cache turned off nothing is written."""
+    import subprocess
+    import sys
+    env = dict(os.environ, CLJXLA_B200_CACHE_DIR=str(tmp_path / "cache"))
+    probe = [sys.executable, "-c", _JIT_CACHE_PROBE, os.path.join(ROOT, "tests")]
+    first = subprocess.run(probe, env=env, capture_output=True, text=True, cwd=ROOT)
+    rc, kernels, hits, misses = map(int, first.stdout.split()[-4:])
+    if rc == -1:
+        pytest.skip("NVRTC not available")
+    assert rc == 0 and kernels > 0 and hits == 0 and misses > 0, first.stdout + first.stderr
+    files = sorted(p.name for p in (tmp_path / "cache").iterdir())
+    assert len(files) == misses and all(re.fullmatch(r"[0-9a-f]{64}\.cubin", n) for n in files), files
+    second = subprocess.run(probe, env=env, capture_output=True, text=True, cwd=ROOT)
+    rc2, kernels2, hits2, misses2 = map(int, second.stdout.split()[-4:])
+    assert (rc2, kernels2, hits2, misses2) == (0, kernels, misses, 0), second.stdout + second.stderr
+    off = subprocess.run(probe, env=dict(os.environ, CLJXLA_B200_CACHE_DIR="0"), capture_output=True, text=True,
+                         cwd=ROOT)
+    assert list(map(int, off.stdout.split()[-4:]))[2:] == [0, 0], off.stdout + off.stderr
