@@ -67,7 +67,87 @@ def parse():
                    help="override the layer count (small ncu captures; not a bench line)")
     p.add_argument("--tp", type=int, default=1,
                    help="tensor-parallel ranks per model replica (Gemma; ranks = --gpus under torchrun)")
+    p.add_argument("--no-tp-block", action="store_true",
+                   help="skip the tensor-parallel Gemma-3-12B batch-8 decode measurement added to the line")
+    p.add_argument("--tp-steps", type=int, default=16)
     return p.parse_args()
+
+
+def tp_block(args, rank, world, local_rank):
+    """Gemma-3-12B bf16 batch 8 decode (prompt 4096, KV cache 4608 positions),
+    tensor-parallel over every rank of the job (TP = world; one GPU: TP 1).
+    Each rank holds its shard (heads and MLP width split, an all-reduce after
+    the attention and MLP blocks: the one-shot peer kernel for messages that
+    fit its slot, NCCL above), weights random-init on the device, caches
+    zero, the decode graph replayed at positions 4096 + i with device-resident
+    token ids.  Returns the device time per step (max over ranks)."""
+    import torch
+    from cljxla_b200.host import core, drivers as d
+    from cljxla_b200.host import stablehlo as shlo
+    from cljxla_b200.host.pjrt import DTYPE_ENUM
+    pkg = _pkg()
+    cfg_full, B, S = d.GEMMA3_12B, 8, 4096
+    T = d.round_up(S + 512, 128)
+    cfg = d.shard_config(cfg_full, world)
+    if world > 1:
+        from cljxla_b200.host import tp as tpmod
+        ctx = core.init_tp_backend(world, rank, tpmod.share_nccl_id(pkg.LIB_PATH), local_rank, pkg.LIB_PATH)
+        tpmod.setup_p2p(ctx, 128 << 10)  # a [8, 3840] bf16 block sum (61 KB) fits one slot
+    else:
+        ctx = core.init_backend(pkg.LIB_PATH, {"device": local_rank})
+    api = ctx["api"]
+    wdt = DTYPE_ENUM[cfg.dtype]
+    host_w = d.device_weights(cfg, 4321 + rank, f"cuda:{local_rank}")
+    wbufs = [core.buffer_from_host_buffer(ctx, w, shp, wdt) for w, (_, shp, _) in zip(host_w, d.weight_specs(cfg))]
+    del host_w
+    g = d.build_graph(cfg, "decode", B, S, T)
+    ex = core.compile_mlir_text(ctx, shlo.graph_to_mlir_text(g), g)
+    cache = d.zero_cache(cfg, B, T)
+    kv = [core.buffer_from_host_buffer(ctx, cache, list(cache.shape), wdt) for _ in range(2 * cfg.layers)]
+    n = args.warmup + args.tp_steps
+    rng = np.random.Generator(np.random.PCG64(11))  # the same ids on every rank
+    xs = [core.buffer_from_host_buffer(ctx, rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64).astype(np.int32),
+                                       [B, 1], 4) for _ in range(n)]
+    ps = [core.buffer_from_host_buffer(ctx, np.array([S + i], np.int32), [1], 4) for i in range(n)]
+    stream = torch.cuda.ExternalStream(core.client_stream(ctx), device=f"cuda:{local_rank}")
+
+    def step(i, kv):
+        outs = api.execute_executable(ex["handle"], [xs[i], ps[i]] + wbufs + kv, len(g["outvars"]), wait=False)
+        api.destroy_buffer(outs[0])
+        for b in kv:
+            api.destroy_buffer(b)
+        return outs[1:]
+
+    for i in range(args.warmup):
+        kv = step(i, kv)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.warmup, n):
+        kv = step(i, kv)
+    e1.record(stream)
+    e1.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([dt], device=f"cuda:{local_rank}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dt = float(t.item())
+    plan = core.plan_info(ctx, ex)
+    for b in kv + xs + ps + wbufs:
+        api.destroy_buffer(b)
+    core.close_backend(ctx)
+    ms = dt / args.tp_steps * 1e3
+    # per-GPU weight bytes streamed per step (the decode is HBM-bound): the
+    # shard's weights once per step, over the measured copy bandwidth
+    w_bytes = sum(int(np.prod(shp)) for _, shp, _ in d.weight_specs(cfg)) * 2
+    hbm, _, src = load_peaks()
+    return {"config": "gemma3-12b decode, batch 8, prompt 4096, KV cache 4608 positions", "tp": world,
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B * args.tp_steps / dt, 2),
+            "weight_bytes_per_gpu": w_bytes, "weight_floor_ms": round(w_bytes / (hbm * 1e9) * 1e3, 4),
+            "steps": args.tp_steps, "launches_per_step": plan["launches"],
+            "timing": "CUDA events on each rank's stream, max over ranks"}
 
 
 def load_peaks():
@@ -417,6 +497,9 @@ def main():
         dec_s, e2e_s, pre_s = [float(x) for x in t.tolist()]
     else:
         dec_s, e2e_s, pre_s = res["dec_s"], res["e2e_s"], res["prefill_s"]
+    tp = None
+    if not args.no_tp_block and args.tp == 1 and not args.tiny and not args.layers and world in (1, 2, 4, 8):
+        tp = tp_block(args, rank, world, local_rank)
     if rank == 0:
         replicas = world // max(1, args.tp)
         value = replicas * res["tokens"] / dec_s
@@ -467,6 +550,8 @@ def main():
             "kernel_time_by_kind_ms": {k: round(v["ms"] / 2, 4) for k, v in res["by_kind"].items()},
             "plan": res["plan"],
         }
+        if tp is not None:
+            line["tp"] = tp
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -483,6 +568,9 @@ def run_reference(args, rank, world):
     from cljxla_b200.host import drivers as d
     from cljxla_b200.host import stablehlo as shlo
     cfg, B, S, T = model_setup(args)
+    # the same global batch as the repo arm at this N (one sequence batch per
+    # data-parallel replica), decoded by the one CPU process
+    B = B * max(1, world // max(1, args.tp))
     rng = np.random.Generator(np.random.PCG64(1234))
     wf = []
     for name, shp, kind in d.weight_specs(cfg):

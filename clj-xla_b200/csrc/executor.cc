@@ -60,13 +60,36 @@ ProfileState& profile_state() {
   return p;
 }
 
-Storage::~Storage() {
-  if (ptr) cudaFreeAsync(ptr, client->stream);  // stream ordered after every reader
+void* client_alloc(PJRT_Client* c, size_t bytes) {
+  if (!bytes) return nullptr;
+  const int64_t lim = c->opt.memory_limit;
+  const int64_t now = c->held_bytes.fetch_add((int64_t)bytes) + (int64_t)bytes;
+  if (lim > 0 && now > lim) {
+    c->held_bytes.fetch_sub((int64_t)bytes);
+    fail(E_OOM, "RESOURCE_EXHAUSTED: allocating " + std::to_string(bytes) + " bytes would hold " +
+                    std::to_string(now) + " bytes, above the client's memory_limit_bytes " + std::to_string(lim));
+  }
+  void* p = nullptr;
+  cudaError_t e = cudaMallocAsync(&p, bytes, c->stream);
+  if (e != cudaSuccess) {
+    c->held_bytes.fetch_sub((int64_t)bytes);
+    cudaGetLastError();
+    fail(e == cudaErrorMemoryAllocation ? E_OOM : E_INTERNAL,
+         std::string(e == cudaErrorMemoryAllocation ? "RESOURCE_EXHAUSTED: " : "") + "device allocation of " +
+             std::to_string(bytes) + " bytes failed: " + cudaGetErrorString(e));
+  }
+  return p;
 }
 
-Version::~Version() {
-  if (undo) cudaFreeAsync(undo, client->stream);
+void client_free(PJRT_Client* c, void* p, size_t bytes) {
+  if (!p) return;
+  cudaFreeAsync(p, c->stream);  // stream ordered after every reader
+  c->held_bytes.fetch_sub((int64_t)bytes);
 }
+
+Storage::~Storage() { client_free(client, ptr, bytes); }
+
+Version::~Version() { client_free(client, undo, undo_bytes); }
 
 PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims) {
   auto* b = new PJRT_Buffer();
@@ -78,11 +101,12 @@ PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims)
   st->client = c;
   st->bytes = b->bytes;
   if (b->bytes) {
-    cudaError_t e = cudaMallocAsync(&st->ptr, b->bytes, c->stream);
-    if (e != cudaSuccess) {
+    try {
+      st->ptr = client_alloc(c, b->bytes);
+    } catch (...) {
       st->ptr = nullptr;
       delete b;
-      CUDA_OK(e);
+      throw;
     }
   }
   b->ver = std::make_shared<Version>();
@@ -101,7 +125,7 @@ void ensure_current(PJRT_Buffer* b) {
   st->client = c;
   st->bytes = b->bytes;
   if (b->bytes) {
-    CUDA_OK(cudaMallocAsync(&st->ptr, b->bytes, c->stream));
+    st->ptr = client_alloc(c, b->bytes);
     CUDA_OK(cudaMemcpyAsync(st->ptr, b->ver->storage->ptr, b->bytes, cudaMemcpyDeviceToDevice, c->stream));
     for (size_t i = chain.size(); i-- > 0;) {
       Version* v = chain[i];
@@ -369,7 +393,7 @@ void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs,
     for (size_t u = 0; u < p.inplace.size(); ++u) {
       const InplaceDus& d = p.inplace[u];
       PJRT_Buffer* src = args[d.param];
-      CUDA_OK(cudaMallocAsync(&undo[u], (size_t)d.undo_bytes, s));
+      undo[u] = client_alloc(c, (size_t)d.undo_bytes);
       v.h_argtab[d.undo_slot] = (uint64_t)(uintptr_t)undo[u];
       v.h_argtab[p.params.size() + d.out] = (uint64_t)(uintptr_t)src->ptr();
       auto* b = new PJRT_Buffer();
@@ -385,8 +409,7 @@ void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs,
     }
   } catch (...) {
     for (auto* b : created) delete b;
-    for (void* u : undo)
-      if (u) cudaFreeAsync(u, s);
+    for (size_t u = 0; u < undo.size(); ++u) client_free(c, undo[u], (size_t)p.inplace[u].undo_bytes);
     throw;
   }
   run_variant(c, v, s);
@@ -396,6 +419,7 @@ void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs,
     Version* old = args[d.param]->ver.get();
     old->newer = new_heads[u];
     old->undo = undo[u];
+    old->undo_bytes = (size_t)d.undo_bytes;
     old->rank = d.rank;
     old->dt = d.dt;
     for (int i = 0; i < d.rank; ++i) {

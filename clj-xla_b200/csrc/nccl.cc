@@ -7,6 +7,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <mutex>
 
 namespace cljxla {
@@ -25,8 +26,15 @@ Nccl& lib() {
   static Nccl n;
   static std::once_flag once;
   std::call_once(once, [] {
-    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    // CLJXLA_B200_NCCL_LIB names the library to load instead (an NCCL outside
+    // the loader path; tests point it at a missing file to make the load fail)
+    void* h = nullptr;
+    if (const char* path = getenv("CLJXLA_B200_NCCL_LIB")) {
+      h = dlopen(path, RTLD_NOW | RTLD_GLOBAL);
+    } else {
+      h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+      if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    }
     if (!h) return;
     n.get_id = (decltype(n.get_id))dlsym(h, "ncclGetUniqueId");
     n.init_rank = (decltype(n.init_rank))dlsym(h, "ncclCommInitRank");

@@ -26,6 +26,8 @@ struct P2PAllReduce {
   unsigned* d_epoch = nullptr;       // calls completed (advanced by the kernel)
   unsigned* h_err = nullptr;         // mapped host word: a wait ran out
   unsigned* d_err = nullptr;
+  // polls before a wait gives up (CLJXLA_B200_P2P_WAIT_POLLS; default 2^24, ~16 s)
+  uint32_t wait_polls = 1u << 24;
   bool ready = false;
   ~P2PAllReduce();
   std::string export_handle(int ranks, int rank, int64_t slot_bytes);  // allocates on first use

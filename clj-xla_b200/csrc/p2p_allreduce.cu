@@ -22,6 +22,9 @@
 #include <cstring>
 #include <string>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.h"
 #include "kernels.h"
 #include "nccl_rt.h"
@@ -29,11 +32,11 @@
 namespace cljxla {
 namespace {
 
-// polls before a wait gives up: the first P2P_FAST_POLLS about 64 ns apart, then
-// about 1 us apart, ~16 s in all (ranks reach their first call after compiling
-// their own executables, which need not take the same time)
+// polls before a wait gives up (P2PAllReduce::wait_polls): the first
+// P2P_FAST_POLLS about 64 ns apart, then about 1 us apart, ~16 s in all by
+// default (ranks reach their first call after compiling their own
+// executables, which need not take the same time)
 constexpr uint32_t P2P_FAST_POLLS = 1u << 14;
-constexpr uint32_t P2P_WAIT_LIMIT = 1u << 24;
 constexpr int P2P_THREADS = 1024;
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -49,7 +52,7 @@ __global__ void __launch_bounds__(P2P_THREADS) p2p_allreduce_kernel(const char* 
                                                                     int64_t count, int dt,
                                                                     const uint64_t* __restrict__ peers, int rank,
                                                                     int ranks, int64_t slot_bytes, unsigned* epoch,
-                                                                    unsigned* err) {
+                                                                    unsigned* err, uint32_t wait_polls) {
   __shared__ unsigned s_ep;
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -81,7 +84,7 @@ __global__ void __launch_bounds__(P2P_THREADS) p2p_allreduce_kernel(const char* 
     const unsigned* f = (const unsigned*)((const char*)(uintptr_t)peers[rank] + flag_off) + phase * ranks + threadIdx.x;
     uint32_t n = 0;
     while (ld_acquire_sys(f) != ep) {
-      if (++n > P2P_WAIT_LIMIT) {
+      if (++n > wait_polls) {
         atomicOr(err, 1u);
         s_ok = 0;
         break;
@@ -122,6 +125,8 @@ P2PAllReduce::~P2PAllReduce() {
 std::string P2PAllReduce::export_handle(int ranks_, int rank_, int64_t slot) {
   if (ranks_ < 2 || ranks_ > P2P_MAX_RANKS || rank_ < 0 || rank_ >= ranks_ || slot < 16 || slot % 16)
     fail(E_INVALID, "bad one-shot all-reduce group");
+  if (const char* e = getenv("CLJXLA_B200_P2P_WAIT_POLLS"))
+    if (atoll(e) > 0) wait_polls = (uint32_t)std::min<long long>(atoll(e), 1LL << 30);
   if (!local) {
     ranks = ranks_;
     rank = rank_;
@@ -179,7 +184,7 @@ bool P2PAllReduce::fits(int64_t count, int dt) const {
 void P2PAllReduce::run(const void* src, void* dst, int64_t count, int dt, cudaStream_t s) {
   if (((uintptr_t)src | (uintptr_t)dst) & 15) fail(E_INTERNAL, "one-shot all-reduce operands not 16-byte aligned");
   p2p_allreduce_kernel<<<1, P2P_THREADS, 0, s>>>((const char*)src, (char*)dst, count, dt, d_peers, rank, ranks,
-                                                 slot_bytes, d_epoch, d_err);
+                                                 slot_bytes, d_epoch, d_err, wait_polls);
   CUDA_OK(cudaGetLastError());
 }
 

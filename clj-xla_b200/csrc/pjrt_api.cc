@@ -146,6 +146,7 @@ PJRT_Error* Client_Create(void* a) {
     o.cuda_graphs = env_flag("CLJXLA_B200_CUDA_GRAPHS", true);
     o.kv_in_place = env_flag("CLJXLA_B200_KV_IN_PLACE", true);
     if (const char* d = getenv("CLJXLA_B200_DEVICE")) o.device = atoi(d);
+    if (const char* m = getenv("CLJXLA_B200_MEMORY_LIMIT")) o.memory_limit = atoll(m);
     size_t stride = sizeof(PJRT_NamedValue);
     if (args->num_options && args->create_options[0].struct_size >= sizeof(PJRT_NamedValue))
       stride = args->create_options[0].struct_size;  // clj-xla writes 64-byte elements
@@ -167,6 +168,7 @@ PJRT_Error* Client_Create(void* a) {
       else if (k == "tp_size" && nv.type == PJRT_NamedValue_kInt64) o.tp_size = (int)nv.int64_value;
       else if (k == "tp_rank" && nv.type == PJRT_NamedValue_kInt64) o.tp_rank = (int)nv.int64_value;
       else if (k == "tp_nccl_id" && nv.type == PJRT_NamedValue_kString) o.tp_nccl_id.assign(nv.string_value, nv.value_size);
+      else if (k == "memory_limit_bytes" && nv.type == PJRT_NamedValue_kInt64) o.memory_limit = nv.int64_value;
       // other options (e.g. clj-xla's default {:allocator "platform"}) are accepted and ignored
     }
     if (o.tp_size < 1 || o.tp_rank < 0 || o.tp_rank >= o.tp_size) fail(E_INVALID, "bad tp_size / tp_rank");
@@ -261,7 +263,11 @@ PJRT_Error* Client_Compile(void* a) {
     if (ex->inplace.plan) prepare_jit(*ex->inplace.plan);
     int64_t arena = ex->copy.plan->arena_bytes;
     if (ex->inplace.plan) arena = std::max(arena, ex->inplace.plan->arena_bytes);
-    if (arena) CUDA_OK(cudaMalloc(&ex->arena, (size_t)arena));
+    if (arena) {
+      ex->arena = client_alloc(c, (size_t)arena);
+      ex->arena_bytes = (size_t)arena;
+      CUDA_OK(cudaStreamSynchronize(c->stream));  // the arena is used on other streams' schedules too
+    }
     setup_variant(ex->copy, ex->arena);
     if (ex->inplace.plan) setup_variant(ex->inplace, ex->arena);
     args->executable = ex.release();
@@ -421,7 +427,10 @@ PJRT_Error* LoadedExecutable_Destroy(void* a) {
     cudaStreamSynchronize(ex->client->stream);
     destroy_variant(ex->copy);
     destroy_variant(ex->inplace);
-    if (ex->arena) cudaFree(ex->arena);
+    if (ex->arena) {
+      client_free(ex->client, ex->arena, ex->arena_bytes);
+      cudaStreamSynchronize(ex->client->stream);
+    }
     delete ex;
   });
 }

@@ -46,6 +46,7 @@ struct Version {
   std::shared_ptr<Storage> storage;
   std::shared_ptr<Version> newer;  // null: this version is the storage's current content
   void* undo = nullptr;            // undo record turning newer's content into this one's
+  size_t undo_bytes = 0;
   int rank = 0;
   DT dt = DT::BF16;
   int64_t out_shape[CLJXLA_MAXR] = {}, upd_shape[CLJXLA_MAXR] = {};
@@ -98,6 +99,7 @@ struct PJRT_LoadedExecutable {
   cljxla::ExecVariant copy;     // results in fresh buffers
   cljxla::ExecVariant inplace;  // KV updates in place (when the graph has any); plan null otherwise
   void* arena = nullptr;        // scratch shared by both variants (never active together)
+  size_t arena_bytes = 0;
   const cljxla::Plan& plan() const { return *copy.plan; }
 };
 
@@ -111,6 +113,9 @@ struct ClientOptions {
   // the NCCL unique id tp_nccl_id (hex) that every rank was given
   int tp_size = 1, tp_rank = 0;
   std::string tp_nccl_id;
+  // cap on the device memory this client holds (buffers, undo records, executable
+  // scratch); 0 = no cap.  A request past it fails with RESOURCE_EXHAUSTED.
+  int64_t memory_limit = 0;
 };
 
 struct PJRT_Client {
@@ -128,6 +133,7 @@ struct PJRT_Client {
   cudaEvent_t up_done[2] = {nullptr, nullptr};
   std::string platform = "cuda";
   void* nccl_comm = nullptr;  // tp_size > 1
+  std::atomic<int64_t> held_bytes{0};  // device memory held through client_alloc
   cljxla::P2PAllReduce* p2p = nullptr;  // one-shot peer all-reduce, once its handles are exchanged
 };
 
@@ -145,6 +151,12 @@ struct ProfileState {
   std::map<std::string, ProfileEntry> entries;
 };
 ProfileState& profile_state();
+
+// Stream-ordered device allocation charged to the client (its memory_limit
+// applies; RESOURCE_EXHAUSTED past it or when the device is out of memory),
+// and its release.
+void* client_alloc(PJRT_Client* c, size_t bytes);
+void client_free(PJRT_Client* c, void* p, size_t bytes);
 
 // New head-version buffer over fresh storage of `bytes` (stream-ordered allocation).
 PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims);

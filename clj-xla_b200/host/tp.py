@@ -29,13 +29,28 @@ from .pjrt import DTYPE_ENUM
 from .stablehlo import graph_to_mlir_text
 
 
+class GroupError(RuntimeError):
+    """A tensor-parallel group could not be formed; raised on every rank."""
+
+
 def share_nccl_id(lib_path: Optional[str] = None) -> str:
     """Rank 0's NCCL id, broadcast over the default torch.distributed group
-    (any backend: the id is host data)."""
+    (any backend: the id is host data).  If rank 0 cannot make one (NCCL not
+    loadable, no network interface for its bootstrap), the failure is what
+    gets broadcast, so every rank raises GroupError instead of the others
+    waiting in the collective client creation for a rank that never joins."""
     import torch.distributed as dist
-    obj = [core.nccl_unique_id(lib_path) if dist.get_rank() == 0 else None]
+    obj = [None]
+    if dist.get_rank() == 0:
+        try:
+            obj = [("ok", core.nccl_unique_id(lib_path))]
+        except Exception as e:  # noqa: BLE001 - reported to every rank
+            obj = [("error", f"rank 0 could not create the NCCL id: {e}")]
     dist.broadcast_object_list(obj, src=0)
-    return obj[0]
+    status, value = obj[0]
+    if status != "ok":
+        raise GroupError(value)
+    return value
 
 
 def setup_p2p(ctx: core.Context, slot_bytes: int = 32 << 10):

@@ -199,3 +199,36 @@ def test_large_upload_through_pinned_staging_is_exact(ctx):
         finally:
             core.destroy_buffer(ctx, b)
         assert np.array_equal(got.view(np.uint32), a.view(np.uint32))
+
+
+def test_memory_limit_gives_resource_exhausted(ctx):
+    """A client created with memory_limit_bytes refuses allocations past it
+    with PJRT RESOURCE_EXHAUSTED (code 8) - uploads and execution outputs
+    alike - and accepts them again once buffers are released."""
+    from cljxla_b200.host.pjrt import DTYPE_ENUM, PJRTError
+    api = ctx["api"]
+    client = api.create_client({"memory_limit_bytes": 64 << 20})
+    c2 = core.Context(ctx, client=client)
+    try:
+        _memory_limit_checks(api, c2, DTYPE_ENUM["f32"], PJRTError)
+    finally:
+        core.close_backend(c2)
+
+
+def _memory_limit_checks(api, c2, f32, PJRTError):
+    a = np.ones(8 << 20, np.float32)           # 32 MiB
+    b1 = core.buffer_from_host_buffer(c2, a, a.shape, f32)
+    with pytest.raises(PJRTError) as e:
+        core.buffer_from_host_buffer(c2, np.ones(10 << 20, np.float32), (10 << 20,), f32)  # 40 MiB more
+    assert e.value.code == 8 and "RESOURCE_EXHAUSTED" in str(e.value)
+    g = t.trace_graph("twice", [("x", ("tensor", (8 << 20,), "f32"))], lambda x: [t.add(x, x)])
+    exe = core.compile_mlir_text(c2, shlo.graph_to_mlir_text(g), g)
+    out = api.execute_executable(exe["handle"], [b1], 1)    # 32 + 32 MiB: at the cap, allowed
+    with pytest.raises(PJRTError) as e:
+        api.execute_executable(exe["handle"], [b1], 1)      # a third 32 MiB is not
+    assert e.value.code == 8
+    core.destroy_buffer(c2, out)
+    out = api.execute_executable(exe["handle"], [b1], 1)    # released memory counts again
+    assert np.array_equal(core.buffer_to_numpy(c2, out, (8 << 20,), "f32"), 2 * a)
+    core.destroy_buffer(c2, out)
+    core.destroy_buffer(c2, b1)

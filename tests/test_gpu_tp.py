@@ -103,3 +103,83 @@ def test_tp2_greedy_decode_matches_oracle(dtype, p2p):
                         interp.run_mlir)[1] for sd in NOISE_SEEDS]
                 ok, bad, rr, _, _ = close_model_floor(a, b, [f[i] for f in floors], "bf16")
         assert ok, f"step {i}: {bad:.2%} out of bound, rel rms {rr:.3g}"
+
+
+def _rank_skip(rank, world, nid, q, hq, hin, go):
+    """Rank of a 2-rank group whose rank 1 leaves after the first step."""
+    import os
+    os.environ["CLJXLA_B200_P2P_WAIT_POLLS"] = "20000"  # about 20 ms before a wait gives up
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from cljxla_b200.host import stablehlo as shlo
+    from cljxla_b200.host import tensor as t
+    from cljxla_b200.host.pjrt import PJRTError
+    try:
+        ctx = core.init_tp_backend(world, rank, nid, device=rank)
+        hq.put((rank, core.p2p_export(ctx)))
+        core.p2p_import(ctx, hin.get(timeout=300))
+        g = t.trace_graph("ar", [("x", ("tensor", (1, 64), "f32"))], lambda x: [t.all_reduce(x, 2)])
+        exe = core.compile_mlir_text(ctx, shlo.graph_to_mlir_text(g), g)
+        x = np.full((1, 64), rank + 1.0, np.float32)
+
+        def step():
+            b = core.buffer_from_host_buffer(ctx, x, (1, 64), 11)
+            try:
+                out = ctx["api"].execute_executable(exe["handle"], [b], 1)
+                try:
+                    return core.buffer_to_numpy(ctx, out, (1, 64), "f32")
+                finally:
+                    core.destroy_buffer(ctx, out)
+            finally:
+                core.destroy_buffer(ctx, b)
+
+        first = step()
+        ok = bool(np.all(first == 3.0))
+        if rank == 1:  # leaves between steps, nothing in flight, and waits for the end
+            q.put((rank, ok, "left"))
+            go.get(timeout=300)
+            core.close_backend(ctx)
+            return
+        step()  # the peer never arrives: the kernel's bounded wait runs out and it returns
+        try:
+            step()
+            msg = "no error"
+        except PJRTError as e:
+            msg = str(e)
+        core.close_backend(ctx)
+        q.put((rank, ok, msg))
+    except Exception as e:  # noqa: BLE001 - reported by the parent
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+def test_p2p_wait_runs_out_when_a_rank_leaves():
+    """A rank leaves the group between steps; the other rank's one-shot
+    all-reduce waits a short, bounded time for its flag, gives up, and the
+    next execution on that rank reports the group out of step as a PJRT
+    error - the GPU and the context stay usable (the client closes cleanly)."""
+    nid = core.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q, hq, go = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    hins = [ctx.Queue() for _ in range(2)]
+    procs = [ctx.Process(target=_rank_skip, args=(r, 2, nid, q, hq, hins[r], go)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        hs = dict(hq.get(timeout=300) for _ in range(2))
+        for hin in hins:
+            hin.put([hs[r] for r in range(2)])
+        for _ in range(2):
+            r, ok, msg = q.get(timeout=300)
+            res[r] = (ok, msg)
+            if r == 0:
+                go.put("done")
+    finally:
+        go.put("done")
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert res[0][0] and res[1][0], res
+    assert res[1][1] == "left"
+    assert "out of step" in res[0][1], res[0][1]

@@ -142,3 +142,46 @@ def test_nccl_id_shared_over_two_gloo_ranks(lib_path):
                 p.kill()
     assert set(got) == {0, 1}
     assert got[0] == got[1] and len(got[0]) == 256 and int(got[0], 16) >= 0
+
+
+def _gloo_rank_failing_nccl(rank, world, port, lib, q):
+    import datetime
+    import torch.distributed as dist
+    if rank == 0:  # the injected failure: rank 0's NCCL cannot be loaded
+        os.environ["CLJXLA_B200_NCCL_LIB"] = "/nonexistent/libnccl.so.2"
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    try:
+        tp.share_nccl_id(lib)
+        q.put((rank, "joined"))
+    except tp.GroupError as e:
+        q.put((rank, "GroupError: " + str(e)))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, f"{type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_init_failure_reaches_every_gloo_rank(lib_path):
+    """An NCCL that cannot be loaded on rank 0 (injected through
+    CLJXLA_B200_NCCL_LIB) ends the group set-up on both ranks with GroupError,
+    naming the cause, well before the process group's timeout."""
+    import time
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank_failing_nccl, args=(r, 2, port, lib_path, q)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q.get(timeout=90) for _ in range(2))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert set(got) == {0, 1}
+    for r in (0, 1):
+        assert got[r].startswith("GroupError") and "NCCL" in got[r], got
+    assert time.time() - t0 < 60
