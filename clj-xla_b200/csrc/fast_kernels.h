@@ -120,6 +120,8 @@ bool attention_tc_ok(const AttnParams& p);
 // and its split / chunk sizes for one wave over `sms` SMs
 bool attention_dec_ok(const AttnParams& p);
 void plan_attention_dec(AttnParams& p, int sms);
+// bytes of the per-split partial results an attention launch with splits > 1 needs
+int64_t attention_part_bytes(const AttnParams& p);
 // the tensor-core prefill kernel (64 query vectors per CTA, no position splits)
 bool attention_tc_prefill_ok(const AttnParams& p);
 void launch_attention_combine(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);

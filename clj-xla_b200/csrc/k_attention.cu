@@ -978,21 +978,26 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
 // ---------------------------------------------------------------------------
 // Decode attention with bulk-copy staged K/V (use_tc 3).  A decode step reads
 // each cached K/V row once and does ~2 flops per byte, so the kernel is built
-// for latency: one wave of CTAs (the planner sizes the position splits so that
-// splits * batch * kv heads is about the SM count), 8 warps each.  Before the
-// dependency wait a CTA asks L2 for its split's rows; after it, one thread
-// issues cp.async.bulk copies of the first chunk's K and V rows into shared
-// memory (a contiguous cache needs one copy per tensor) while every thread
-// loads the query vectors into registers and the chunk's mask values into
-// shared memory, so the step pays one memory round trip before computing.
-// Arithmetic is f32 on the CUDA cores (f32 queries need no split): a lane owns
-// HD/32 consecutive dims, each warp scores every 8th position of the chunk
-// (lane partial dot products, warp shuffle sums), the printed score chain,
-// mask and roundings are applied, the chunk's softmax runs over the scores in
-// shared memory, and each warp accumulates P V over its positions.  Chunks
-// beyond the first are double-buffered; the warps' contexts are summed through
-// shared memory, and the position splits merged by the last CTA to arrive.
-constexpr int DEC_THREADS = 256;
+// for latency and for many short CTAs: 4 warps, a split of DEC_CH (64)
+// positions per CTA (more, in chunks of DEC_CH, when a cache is longer than 64
+// splits), so a layer is one or two waves.  Before the dependency wait a CTA
+// asks L2 for its split's rows.  After it, the CTA loads the chunk's mask
+// values and its query vectors (registers, lane-owned dims), finds the live
+// positions (any query's mask above mask_skip), and one thread copies just
+// those K / V rows into shared memory with cp.async.bulk; a chunk with no live
+// position (most chunks of a sliding-window layer) reads no K / V at all.
+// Scores are f32 on the CUDA cores (f32 queries need no split): each warp
+// takes 32 / NQ positions at a time, every lane accumulating its dims of all
+// of them for every query vector, and one reduce-scatter across the lanes
+// (16 + 8 + 4 + 2 + 1 shuffles) leaves lane l holding the score of position
+// l / NQ for query l % NQ; the printed chain, mask and roundings follow.  The
+// chunk softmax runs over the scores in shared memory and each warp
+// accumulates P V over its positions; the warps' contexts are summed through
+// shared memory.  Splits are merged by the last CTA of a (batch, kv head) to
+// arrive, which copies every split's partial row block into shared memory
+// with one bulk copy each (rows padded to 16-byte multiples for that).
+constexpr int DEC_THREADS = 128;
+constexpr int DEC_CH = 64;  // positions per staged chunk (and per split when it fits)
 
 __device__ __forceinline__ uint32_t dec_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -1017,21 +1022,45 @@ __device__ __forceinline__ void dec_bulk(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+__device__ __forceinline__ void dec_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(dec_smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// floats per partial row of the staged decode kernel: (max, sum, 2 pad, context[HD]),
+// a 16-byte multiple so that a (split, batch, kv head) block is one bulk copy
+__host__ __device__ constexpr int dec_part_stride(int hd) { return hd + 4; }
+
+// reduce-scatter of 32 values across a warp: lane l returns the warp-wide sum of v[l]
+__device__ __forceinline__ float warp_reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
 template <int HD, int NQ>
 __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_constant__ AttnParams P,
                                                                const uint64_t* __restrict__ argtab) {
-  constexpr int VPL = HD / 32;  // consecutive dims of a row per lane
+  constexpr int VPL = HD / 32;        // consecutive dims of a row per lane
   constexpr int NWARP = DEC_THREADS / 32;
-  const int CH = P.dec_chunk;
+  constexpr int PG = 32 / NQ;         // positions a warp scores at a time (PG * NQ == 32)
+  constexpr int PS = dec_part_stride(HD);
   extern __shared__ __align__(128) unsigned char dec_smem[];
-  const int nst = P.dec_per_split > CH ? 2 : 1;
-  uint16_t* Kb = (uint16_t*)dec_smem;                      // [nst][CH][HD]
-  uint16_t* Vb = Kb + (size_t)nst * CH * HD;               // [nst][CH][HD]
-  float* msk = (float*)(Vb + (size_t)nst * CH * HD);       // [2][NQ][CH]
-  float* sc = msk + 2 * NQ * CH;                           // [NQ][CH] scores, then probabilities
-  __shared__ __align__(8) uint64_t bar[2];
-  __shared__ float s_red[NWARP][NQ];
+  uint16_t* Kb = (uint16_t*)dec_smem;                 // [DEC_CH][HD]
+  uint16_t* Vb = Kb + DEC_CH * HD;                    // [DEC_CH][HD]
+  float* msk = (float*)(Vb + DEC_CH * HD);            // [NQ][DEC_CH]
+  float* sc = msk + NQ * DEC_CH;                      // [NQ][DEC_CH] scores, then probabilities
+  __shared__ __align__(8) uint64_t bar;
   __shared__ float s_m[NQ], s_l[NQ], s_scl[NQ];
+  __shared__ int s_lo[2], s_hi[2];
   __shared__ int64_t s_qoff[NQ], s_moff[NQ];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bk = blockIdx.y, b = bk / P.nkv, kh = bk % P.nkv;
@@ -1039,28 +1068,28 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
   const int64_t t0 = (int64_t)blockIdx.x * P.dec_per_split, t1 = min((int64_t)P.T, t0 + P.dec_per_split);
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
-  const bool dense = P.k.stride[2] == HD && P.v.stride[2] == HD;
-  // before the dependency wait: the split's rows towards L2 (rows < the new
+  const int64_t ks = P.k.stride[2], vs = P.v.stride[2];
+  const bool dense = ks == HD && vs == HD;
+  // before the dependency wait: the split's rows towards L2 (rows before the new
   // position were written by earlier steps; a prefetch returns nothing, so the
-  // new row is read correctly after the wait), barriers initialised
+  // new row is read correctly after the wait)
   if (t0 < t1) {
     if (dense) {
       const int64_t bytes = (t1 - t0) * HD * 2;
-      for (int64_t i = threadIdx.x; i * 16384 < bytes; i += DEC_THREADS) {
-        const uint32_t n = (uint32_t)min((int64_t)16384, bytes - i * 16384);
-        l2_prefetch_bulk((const char*)(kbase + t0 * HD) + i * 16384, n);
-        l2_prefetch_bulk((const char*)(vbase + t0 * HD) + i * 16384, n);
+      for (int64_t i = threadIdx.x; i * 8192 < bytes; i += DEC_THREADS) {
+        const uint32_t n = (uint32_t)min((int64_t)8192, bytes - i * 8192);
+        l2_prefetch_bulk((const char*)(kbase + t0 * HD) + i * 8192, n);
+        l2_prefetch_bulk((const char*)(vbase + t0 * HD) + i * 8192, n);
       }
     } else {
       for (int64_t i = threadIdx.x; i < t1 - t0; i += DEC_THREADS) {
-        l2_prefetch_bulk(kbase + (t0 + i) * P.k.stride[2], HD * 2);
-        l2_prefetch_bulk(vbase + (t0 + i) * P.v.stride[2], HD * 2);
+        l2_prefetch_bulk(kbase + (t0 + i) * ks, HD * 2);
+        l2_prefetch_bulk(vbase + (t0 + i) * vs, HD * 2);
       }
     }
   }
   if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar[0])) : "memory");
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar[1])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < NQ) {
@@ -1074,45 +1103,8 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
   __syncthreads();
   pdl_enter();
   unsigned* status = P.has_status ? (unsigned*)dres(P.status, argtab) : nullptr;
-  // stage chunk c (positions c0 .. c0 + n) into buffer st: one thread, after
-  // the barrier that ended every generic access of the buffer
-  auto issue = [&](int64_t c0, int n, int st) {
-    uint64_t* bb = &bar[st];
-    const uint32_t row = HD * 2;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(dec_smem_u32(bb)),
-                 "r"((uint32_t)(2 * n) * row)
-                 : "memory");
-    uint16_t* kd = Kb + (size_t)st * CH * HD;
-    uint16_t* vd = Vb + (size_t)st * CH * HD;
-    if (dense) {
-      dec_bulk(kd, kbase + c0 * HD, (uint32_t)n * row, bb);
-      dec_bulk(vd, vbase + c0 * HD, (uint32_t)n * row, bb);
-    } else {
-      for (int j = 0; j < n; ++j) {
-        dec_bulk(kd + (size_t)j * HD, kbase + (c0 + j) * P.k.stride[2], row, bb);
-        dec_bulk(vd + (size_t)j * HD, vbase + (c0 + j) * P.v.stride[2], row, bb);
-      }
-    }
-  };
   const char* mb = dres(P.mask.p, argtab);
   const int64_t ms3 = P.mask.stride[3];
-  // mask values of a chunk into msk[buf] (-inf past the split); returns
-  // whether any value this thread stored is live
-  auto load_mask = [&](int64_t c0, int n, int buf) {
-    float* m = msk + buf * NQ * CH;
-    bool any = false;
-    for (int e = threadIdx.x; e < NQ * CH; e += DEC_THREADS) {
-      const int r = e / CH, j = e % CH;
-      float v = -INFINITY;
-      if (r < nqv && j < n) v = ld_any(mb, s_moff[r] + (c0 + j) * ms3, P.mask.dt);
-      m[e] = v;
-      any |= v > P.mask_skip;
-    }
-    return any;
-  };
-  const int nch = t0 < t1 ? (int)((t1 - t0 + CH - 1) / CH) : 0;
-  if (threadIdx.x == 0 && nch > 0) issue(t0, (int)min((int64_t)CH, t1 - t0), 0);
   // queries: lane-owned dims of every query vector, f32
   float q[NQ][VPL];
   {
@@ -1124,152 +1116,247 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
       for (int i = 0; i < VPL; ++i)
         q[r][i] = r < nqv ? ld_any(qb, s_qoff[r] + (int64_t)(lane * VPL + i) * qs3, P.q.dt) : 0.f;
   }
-  bool any_cur = nch > 0 && load_mask(t0, (int)min((int64_t)CH, t1 - t0), 0);
   float acc[NQ][VPL];
 #pragma unroll
   for (int r = 0; r < NQ; ++r)
 #pragma unroll
     for (int i = 0; i < VPL; ++i) acc[r][i] = 0.f;
+  uint32_t phase = 0;
   bool ok = true;
-  for (int c = 0; c < nch; ++c) {
-    const int buf = c & 1, st = nst == 2 ? buf : 0;
-    const int64_t c0 = t0 + (int64_t)c * CH;
-    const int n = (int)min((int64_t)CH, t1 - c0);
-    // this chunk's mask visible (and whether any of it is live); the previous chunk's buffers free
-    const bool live = __syncthreads_or(any_cur) != 0;
-    if (c + 1 < nch && nst == 2 && threadIdx.x == 0)
-      issue(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), st ^ 1);
-    const uint32_t parity = (uint32_t)((nst == 2 ? c >> 1 : c) & 1);
-    bool landed = dec_mbar_wait(&bar[st], parity);
-    if (!landed) landed = dec_mbar_wait(&bar[st], parity);  // once more: the copy may still land
-    ok = __syncthreads_and(ok && landed) != 0;
-    if (!ok && status && threadIdx.x == 0) atomicOr(status, 32u);
-    if (live && ok) {
-      const float* m = msk + buf * NQ * CH;
-      const uint16_t* kc = Kb + (size_t)st * CH * HD;
-      // scores: warp w takes positions w, w + 8, ...
-      for (int j = warp; j < n; j += NWARP) {
-        bool any = false;
-#pragma unroll
-        for (int r = 0; r < NQ; ++r) any |= r < nqv && m[r * CH + j] > P.mask_skip;
-        if (!any) {
-          if (lane < NQ) sc[lane * CH + j] = -INFINITY;
-          continue;
+  if (threadIdx.x == 0) {
+    s_lo[0] = DEC_CH;
+    s_hi[0] = -1;
+  }
+  for (int64_t c0 = t0, k = 0; c0 < t1; c0 += DEC_CH, ++k) {
+    const int n = (int)min((int64_t)DEC_CH, t1 - c0);
+    const int kp = (int)(k & 1);
+    __syncthreads();  // the previous chunk is done with every buffer; this chunk's s_lo / s_hi reset
+    // mask values of the chunk and its live positions [lo, hi]
+    int lo = DEC_CH, hi = -1;
+    for (int e = threadIdx.x; e < NQ * DEC_CH; e += DEC_THREADS) {
+      const int r = e / DEC_CH, j = e % DEC_CH;
+      float v = -INFINITY;
+      if (r < nqv && j < n) v = ld_any(mb, s_moff[r] + (c0 + j) * ms3, P.mask.dt);
+      msk[e] = v;
+      if (v > P.mask_skip) {
+        lo = min(lo, j);
+        hi = max(hi, j);
+      }
+    }
+    if (hi >= 0) {
+      atomicMin(&s_lo[kp], lo);
+      atomicMax(&s_hi[kp], hi);
+    }
+    __syncthreads();
+    lo = s_lo[kp];
+    hi = s_hi[kp];
+    if (threadIdx.x == 0) {  // the next chunk's (last read before the barrier above)
+      s_lo[kp ^ 1] = DEC_CH;
+      s_hi[kp ^ 1] = -1;
+    }
+    if (hi < 0) continue;  // nothing live in this chunk: no K / V read (uniform)
+    const int nl = hi - lo + 1;
+    if (threadIdx.x == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      dec_expect(&bar, (uint32_t)(2 * nl * HD * 2));
+      if (dense) {
+        dec_bulk(Kb + lo * HD, kbase + (c0 + lo) * HD, (uint32_t)(nl * HD * 2), &bar);
+        dec_bulk(Vb + lo * HD, vbase + (c0 + lo) * HD, (uint32_t)(nl * HD * 2), &bar);
+      } else {
+        for (int j = lo; j <= hi; ++j) {
+          dec_bulk(Kb + j * HD, kbase + (c0 + j) * ks, HD * 2, &bar);
+          dec_bulk(Vb + j * HD, vbase + (c0 + j) * vs, HD * 2, &bar);
         }
+      }
+    }
+    bool landed = dec_mbar_wait(&bar, phase);
+    if (!landed) landed = dec_mbar_wait(&bar, phase);  // once more: the copy may still land
+    phase ^= 1u;
+    ok = __syncthreads_and(ok && landed) != 0;
+    if (!ok) {
+      if (status && threadIdx.x == 0) atomicOr(status, 32u);
+      break;
+    }
+    // scores: warp w takes positions lo + PG g .. + PG - 1 for g = w, w + NWARP, ...
+    for (int g0 = lo + warp * PG; g0 <= hi; g0 += NWARP * PG) {
+      float part[32];
+#pragma unroll
+      for (int p = 0; p < PG; ++p) {
+        const int j = g0 + p;
         float kv[VPL];
-        load_row<uint16_t, VPL>(kc + (size_t)j * HD + lane * VPL, kv);
-        float part[NQ];
+        if (j <= hi) load_row<uint16_t, VPL>(Kb + j * HD + lane * VPL, kv);
 #pragma unroll
         for (int r = 0; r < NQ; ++r) {
           float s = 0.f;
+          if (j <= hi) {
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) s = fmaf(q[r][i], kv[i], s);
-          part[r] = s;
+            for (int i = 0; i < VPL; ++i) s = fmaf(q[r][i], kv[i], s);
+          }
+          part[p * NQ + r] = s;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-          for (int r = 0; r < NQ; ++r) part[r] += __shfl_xor_sync(0xffffffffu, part[r], o);
-        if (lane < NQ) {
-          float v = -INFINITY;
-#pragma unroll
-          for (int r = 0; r < NQ; ++r)
-            if (r == lane && r < nqv && m[r * CH + j] > P.mask_skip)
-              v = rnd_dt(apply_chain(P, rnd_dt(part[r], P.dt_d1)) + m[r * CH + j], P.dt_m);
-          sc[lane * CH + j] = v;
-        }
+      }
+      const float dot = warp_reduce_scatter32(part, lane);
+      const int j = g0 + lane / NQ, r = lane % NQ;
+      if (j <= hi && r < nqv) {
+        const float mk = msk[r * DEC_CH + j];
+        sc[r * DEC_CH + j] = mk > P.mask_skip ? rnd_dt(apply_chain(P, rnd_dt(dot, P.dt_d1)) + mk, P.dt_m) : -INFINITY;
       }
     }
-    // the next chunk's mask values load while this one is finished
-    if (c + 1 < nch) any_cur = load_mask(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), buf ^ 1);
     __syncthreads();
-    if (live && ok) {
-      // chunk softmax: warp r reduces row r
-      if (warp < nqv) {
-        float mx = -INFINITY;
-        for (int j = lane; j < n; j += 32) mx = fmaxf(mx, sc[warp * CH + j]);
+    // chunk softmax: warp r reduces row r over [lo, hi]
+    for (int r = warp; r < nqv; r += NWARP) {
+      float mx = -INFINITY;
+      for (int j = lo + lane; j <= hi; j += 32) mx = fmaxf(mx, sc[r * DEC_CH + j]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float mold = s_m[warp], mnew = fmaxf(mold, mx);
-        float sum = 0.f;
-        for (int j = lane; j < n; j += 32) {
-          const float s = sc[warp * CH + j];
-          float p = 0.f;
-          if (mnew != -INFINITY && s != -INFINITY) p = rnd_dt(expf(rnd_dt(s - mnew, P.dt_sub)), P.dt_exp);
-          sc[warp * CH + j] = p;
-          sum += p;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-          const float scl = (mold == -INFINITY || mnew == -INFINITY) ? (mnew == -INFINITY ? 1.f : 0.f)
-                                                                     : expf(mold - mnew);
-          s_scl[warp] = scl;
-          s_l[warp] = s_l[warp] * scl + sum;
-          s_m[warp] = mnew;
-        }
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mold = s_m[r], mnew = fmaxf(mold, mx);
+      float sum = 0.f;
+      for (int j = lo + lane; j <= hi; j += 32) {
+        const float s = sc[r * DEC_CH + j];
+        float p = 0.f;
+        if (mnew != -INFINITY && s != -INFINITY) p = rnd_dt(expf(rnd_dt(s - mnew, P.dt_sub)), P.dt_exp);
+        sc[r * DEC_CH + j] = p;
+        sum += p;
       }
-      __syncthreads();
-      // P V over this warp's positions
-      const uint16_t* vc = Vb + (size_t)st * CH * HD;
 #pragma unroll
-      for (int r = 0; r < NQ; ++r) {
-        const float scl = r < nqv ? s_scl[r] : 1.f;
-#pragma unroll
-        for (int i = 0; i < VPL; ++i) acc[r][i] *= scl;
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) {
+        const float scl = mnew == -INFINITY ? 1.f : (mold == -INFINITY ? 0.f : expf(mold - mnew));
+        s_scl[r] = scl;
+        s_l[r] = s_l[r] * scl + sum;
+        s_m[r] = mnew;
       }
-      for (int j = warp; j < n; j += NWARP) {
-        float p[NQ];
-        bool nz = false;
+    }
+    __syncthreads();
+    // P V: warp w takes positions lo + w, lo + w + NWARP, ...
 #pragma unroll
-        for (int r = 0; r < NQ; ++r) {
-          p[r] = r < nqv ? sc[r * CH + j] : 0.f;
-          nz |= p[r] != 0.f;
-        }
-        if (!nz) continue;
-        float vv[VPL];
-        load_row<uint16_t, VPL>(vc + (size_t)j * HD + lane * VPL, vv);
+    for (int r = 0; r < NQ; ++r) {
+      const float scl = r < nqv ? s_scl[r] : 1.f;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) acc[r][i] *= scl;
+    }
+    int j = lo + warp;
+    for (; j + 3 * NWARP <= hi; j += 4 * NWARP) {  // four positions in flight
+      float vv[4][VPL], p[4][NQ];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        load_row<uint16_t, VPL>(Vb + (j + u * NWARP) * HD + lane * VPL, vv[u]);
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) p[u][r] = r < nqv ? sc[r * DEC_CH + j + u * NWARP] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
 #pragma unroll
         for (int r = 0; r < NQ; ++r)
 #pragma unroll
-          for (int i = 0; i < VPL; ++i) acc[r][i] = fmaf(p[r], vv[i], acc[r][i]);
+          for (int i = 0; i < VPL; ++i) acc[r][i] = fmaf(p[u][r], vv[u][i], acc[r][i]);
+    }
+    for (; j <= hi; j += NWARP) {
+      float vv[VPL];
+      load_row<uint16_t, VPL>(Vb + j * HD + lane * VPL, vv);
+#pragma unroll
+      for (int r = 0; r < NQ; ++r) {
+        const float p = r < nqv ? sc[r * DEC_CH + j] : 0.f;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) acc[r][i] = fmaf(p, vv[i], acc[r][i]);
       }
     }
-    if (nst == 1 && c + 1 < nch) {  // single buffer: restage after everyone is done with it
-      __syncthreads();
-      if (threadIdx.x == 0) issue(c0 + CH, (int)min((int64_t)CH, t1 - c0 - CH), 0);
-    }
   }
-  __syncthreads();  // every chunk's buffers free: the warps' contexts are summed in shared memory
+  // the warps' contexts summed through shared memory (the chunk buffers are free)
+  __syncthreads();
   float* red = (float*)dec_smem;  // [NWARP][NQ][HD]
 #pragma unroll
   for (int r = 0; r < NQ; ++r)
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) red[((size_t)warp * NQ + r) * HD + lane * VPL + i] = acc[r][i];
+    for (int i = 0; i < VPL; ++i) red[(warp * NQ + r) * HD + lane * VPL + i] = acc[r][i];
   __syncthreads();
   const int64_t rows_total = (int64_t)P.B * P.nq;
+  const int64_t row0 = (int64_t)b * P.nq + kh * P.group;  // this head group's first output row
+  float* part = P.splits > 1 ? (float*)dres(P.part, argtab) : nullptr;
   for (int e = threadIdx.x; e < nqv * HD; e += DEC_THREADS) {
     const int r = e / HD, d = e % HD;
     float A = 0.f;
 #pragma unroll
-    for (int w = 0; w < NWARP; ++w) A += red[((size_t)w * NQ + r) * HD + d];
-    const int64_t row = (int64_t)b * P.nq + kh * P.group + r;
+    for (int w = 0; w < NWARP; ++w) A += red[(w * NQ + r) * HD + d];
     if (P.splits == 1) {
       const float l = s_l[r];
       const float v = l > 0.f ? A / l : 0.f;
       char* ob = dres(P.out, argtab);
-      if (P.out_dt == KDT_F32) ((float*)ob)[row * HD + d] = v;
-      else ((__nv_bfloat16*)ob)[row * HD + d] = __float2bfloat16_rn(v);
+      if (P.out_dt == KDT_F32) ((float*)ob)[(row0 + r) * HD + d] = v;
+      else ((__nv_bfloat16*)ob)[(row0 + r) * HD + d] = __float2bfloat16_rn(v);
     } else {
-      float* part = (float*)dres(P.part, argtab) + ((int64_t)blockIdx.x * rows_total + row) * (HD + 2);
-      part[2 + d] = A;
+      float* pr = part + ((int64_t)blockIdx.x * rows_total + row0 + r) * PS;
+      pr[4 + d] = A;
       if (d == 0) {
-        part[0] = s_m[r];
-        part[1] = s_l[r];
+        pr[0] = s_m[r];
+        pr[1] = s_l[r];
       }
     }
   }
-  merge_if_last(P, argtab, b, kh, 0, nqv);
+  if (P.splits == 1) return;
+  // the last split to arrive merges: every split's block of partial rows comes
+  // in with one bulk copy (issued by the four warps in turn) into shared memory
+  __shared__ int s_last;
+  __shared__ float s_w[ATTN_MERGE_MAX_SPLITS][NQ];
+  __shared__ float s_tot[NQ];
+  __syncthreads();  // every thread's partial stores before thread 0's release
+  unsigned* ctr = (unsigned*)dres(P.counters, argtab) + bk;
+  if (threadIdx.x == 0) {
+    unsigned old;
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+    s_last = old == (unsigned)(P.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int S = P.splits;
+  float* pm = (float*)dec_smem;  // [S][nqv][PS]
+  const uint32_t blk = (uint32_t)(nqv * PS * 4);
+  if (threadIdx.x == 0) {
+    // the partials were written by other CTAs (generic proxy, made visible by
+    // the acquire above); the async-proxy reads below are ordered after it
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    dec_expect(&bar, blk * (uint32_t)S);
+  }
+  __syncthreads();
+  for (int sp = threadIdx.x; sp < S; sp += DEC_THREADS)
+    dec_bulk(pm + (size_t)sp * nqv * PS, part + ((int64_t)sp * rows_total + row0) * PS, blk, &bar);
+  bool landed = dec_mbar_wait(&bar, phase);
+  if (!landed) landed = dec_mbar_wait(&bar, phase);
+  if (!__syncthreads_and(landed)) {
+    if (status && threadIdx.x == 0) atomicOr(status, 64u);
+    if (threadIdx.x == 0) *ctr = 0u;
+    return;
+  }
+  // the splits' weights exp(m_s - M) per query vector, one warp per vector
+  for (int r = warp; r < nqv; r += NWARP) {
+    float M = -INFINITY;
+    for (int sp = lane; sp < S; sp += 32) M = fmaxf(M, pm[(sp * nqv + r) * PS]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float m = pm[(sp * nqv + r) * PS];
+      const float w = (M == -INFINITY || m == -INFINITY) ? 0.f : expf(m - M);
+      s_w[sp][r] = w;
+      L += w == 0.f ? 0.f : pm[(sp * nqv + r) * PS + 1] * w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) s_tot[r] = L;
+  }
+  __syncthreads();
+  char* ob = dres(P.out, argtab);
+  for (int e = threadIdx.x; e < nqv * HD; e += DEC_THREADS) {
+    const int r = e / HD, d = e % HD;
+    float A = 0.f;
+    for (int sp = 0; sp < S; ++sp) A += pm[(sp * nqv + r) * PS + 4 + d] * s_w[sp][r];
+    const float L = s_tot[r];
+    const float v = L > 0.f ? A / L : 0.f;
+    if (P.out_dt == KDT_F32) ((float*)ob)[(row0 + r) * HD + d] = v;
+    else ((__nv_bfloat16*)ob)[(row0 + r) * HD + d] = __float2bfloat16_rn(v);
+  }
+  if (threadIdx.x == 0) *ctr = 0u;  // ready for the next launch
 }
 
 // ---------------------------------------------------------------------------
@@ -1716,10 +1803,10 @@ void launch_tc(const AttnParams& p, const uint64_t* argtab, cudaStream_t s) {
 }
 
 int dec_smem_bytes(const AttnParams& p, int nq) {
-  const int nst = p.dec_per_split > p.dec_chunk ? 2 : 1;
-  const int64_t stage = (int64_t)nst * 4 * p.dec_chunk * p.hd + 12LL * nq * p.dec_chunk;
-  const int64_t red = 32LL * nq * p.hd;
-  return (int)std::max(stage, red);
+  const int64_t stage = 4LL * DEC_CH * p.hd + 8LL * nq * DEC_CH;    // K, V rows; mask and score rows
+  const int64_t red = 4LL * (DEC_THREADS / 32) * nq * p.hd;         // the warps' contexts
+  const int64_t merge = p.splits > 1 ? 4LL * p.splits * p.group * dec_part_stride(p.hd) : 0;  // every split's rows
+  return (int)std::max(stage, std::max(red, merge));
 }
 
 int dec_nq(int group) { return group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8; }
@@ -1844,14 +1931,23 @@ bool attention_dec_ok(const AttnParams& p) {
 }
 
 void plan_attention_dec(AttnParams& p, int sms) {
-  const int64_t ctas = (int64_t)p.B * p.nkv;
-  const int chmax = 96 * 256 / p.hd;  // 48 KB of K (and of V) rows per staged chunk
-  int64_t splits = std::max<int64_t>(1, std::min<int64_t>((sms + ctas - 1) / ctas, ATTN_MERGE_MAX_SPLITS));
-  splits = std::min<int64_t>(splits, std::max<int64_t>(1, (p.T + 15) / 16));
-  int64_t per = (p.T + splits - 1) / splits;
+  (void)sms;  // a split per DEC_CH positions: the CTAs are short, several run per SM
+  int64_t per = DEC_CH;
+  if (const char* e = getenv("CLJXLA_B200_ATTN_SPLIT"))  // positions per split (measurement sweeps)
+    if (atoi(e) >= 16) per = atoi(e);
+  // at most ATTN_MERGE_MAX_SPLITS splits, and the merging CTA's copy of every
+  // split's partial rows within 200 KB of shared memory
+  const int64_t cap = std::max<int64_t>(1, std::min<int64_t>(ATTN_MERGE_MAX_SPLITS,
+                                                             200 * 1024 / (4LL * p.group * dec_part_stride(p.hd))));
+  while ((p.T + per - 1) / per > cap) per += DEC_CH;
   p.splits = (int32_t)((p.T + per - 1) / per);
   p.dec_per_split = (int32_t)per;
-  p.dec_chunk = (int32_t)std::max<int64_t>(64, std::min<int64_t>(chmax, (per + 7) / 8 * 8));
+  p.dec_chunk = DEC_CH;
+}
+
+int64_t attention_part_bytes(const AttnParams& p) {
+  const int64_t rows = (int64_t)p.B * p.nq * p.Sq;
+  return (int64_t)p.splits * rows * (p.use_tc == 3 ? dec_part_stride(p.hd) : p.hd + 2) * 4;
 }
 
 bool attention_tc_ok(const AttnParams& p) {
@@ -1883,7 +1979,7 @@ void verify_attention(const Launch& l, const RegionFn& region) {
   vext(p.mask, "mask");
   int64_t rows = (int64_t)p.B * p.nq * p.Sq;
   region(p.out, rows * p.hd * (int64_t)dt_size((DT)p.out_dt), "out");
-  if (p.splits > 1) region(p.part, (int64_t)p.splits * rows * (p.hd + 2) * 4, "partials");
+  if (p.splits > 1) region(p.part, attention_part_bytes(p), "partials");
   if (p.splits > 1 && p.use_counters) {
     region(p.counters, 4LL * p.B * p.nkv * ((p.Sq + p.qtile - 1) / p.qtile), "arrival counters");
     if (p.splits > ATTN_MERGE_MAX_SPLITS || p.qtile * p.group > 8) fail(E_INTERNAL, "attention merge too wide");
@@ -1892,8 +1988,9 @@ void verify_attention(const Launch& l, const RegionFn& region) {
   if (p.use_tc == 3) {
     if (!attention_dec_ok(p)) fail(E_INTERNAL, "staged decode attention on unsupported views");
     if (p.dec_per_split < 1 || (int64_t)p.splits * p.dec_per_split < p.T ||
-        (int64_t)(p.splits - 1) * p.dec_per_split >= p.T || p.dec_chunk < 8 || p.dec_chunk % 8 ||
-        p.dec_chunk > 96 * 256 / p.hd || dec_smem_bytes(p, dec_nq(p.group)) > 220 * 1024)
+        (int64_t)(p.splits - 1) * p.dec_per_split >= p.T || p.dec_chunk != DEC_CH ||
+        dec_smem_bytes(p, dec_nq(p.group)) > 220 * 1024 || (p.splits > 1 && !p.use_counters) ||
+        (p.part.off % 16))
       fail(E_INTERNAL, "staged decode attention: bad split / chunk sizes");
     if (p.has_status) region(p.status, 4, "status word");
   }

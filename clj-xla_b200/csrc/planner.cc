@@ -1497,7 +1497,7 @@ void Planner::emit_attention(int d2) {
   int64_t kvbytes = 2 * (int64_t)P.B * P.nkv * P.T * P.hd * (int64_t)dt_size((DT)P.k_dt);
   int64_t rows = (int64_t)P.B * P.nq * P.Sq;
   if (splits > 1) {
-    P.part = slot_ptr(new_tmp((int64_t)splits * rows * (P.hd + 2) * 4));
+    P.part = slot_ptr(new_tmp(attention_part_bytes(P)));
     // arrival counters (zero in the uploaded constant blob, reset by the merging CTA)
     const int64_t groups = rows_kv * qtiles;
     size_t off = (plan_.const_blob.size() + 255) & ~size_t(255);
@@ -1728,7 +1728,7 @@ void Planner::emit_node_kernel(int id) {
           fl.algo_flops += uf;
         }
         plan_.launches.push_back(std::move(fl));
-      } else if (opt_.fast_kernels && make_tc_gemm(G, tc)) {
+      } else if (opt_.fast_kernels && !getenv_off("CLJXLA_B200_TC_GEMM") && make_tc_gemm(G, tc)) {
         int bm, bn, bk;
         tc_gemm_tile_shape(&bm, &bn, &bk);
         TmapSpec ta, tb;

@@ -228,4 +228,5 @@ def test_in_graph_greedy_token_matches_oracle(ctx, family):
                 assert gap <= 2e-2 * (np.sqrt(np.mean(lg[b] ** 2)) + abs(lg[b].max())), (step, b, gap)
         _compare_all(got[1:], want[1:], specs[1:], f"{family} greedy step {step}", cfg.dtype,
                      lambda sd: interp.run_mlir(td, inputs, ulp_noise_seed=sd)[1:])
-        tok, kv = want[0].astype(np.int32), list(want[1:])
+        tok = want[0].astype(np.int32)
+        kv = [interp.f32_to_bf16_bits(c) for c in want[1:]]
