@@ -75,6 +75,18 @@ bool make_gemv(const GemmParams& g, Launch& out);
 void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region);
 void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& region);
 
+// Greedy-sampling argmax over the last axis (k_argmax.cu): in [..., V] float,
+// out [rows] i32, the highest index among equal maxima (tensor.clj:519-532).
+struct ArgmaxParams {
+  TView in;
+  DPtr out, part, counters;  // part / counters: ctas > 1 (a row split over CTAs)
+  int64_t rows, V;
+  int32_t ctas, pad;
+};
+void launch_argmax(const ArgmaxParams& p, const uint64_t* argtab, cudaStream_t s);
+void verify_argmax(const ArgmaxParams& p, const RegionFn& region);
+int64_t argmax_part_bytes(const ArgmaxParams& p);
+
 }  // namespace cljxla
 
 namespace cljxla {

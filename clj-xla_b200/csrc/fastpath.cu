@@ -9,6 +9,7 @@ void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     case K_ATTN_DECODE: launch_attention(*(const AttnParams*)l.blob.data(), argtab, s); break;
     case K_ATTN_COMBINE: launch_attention_combine(*(const AttnParams*)l.blob.data(), argtab, s); break;
     case K_GEMM_TC: launch_tc_gemm(*(const TcGemmParams*)l.blob.data(), argtab, s); break;
+    case K_ARGMAX: launch_argmax(*(const ArgmaxParams*)l.blob.data(), argtab, s); break;
     default: fail(E_INTERNAL, std::string("no launcher for kernel kind ") + kernel_kind_name(l.kind));
   }
 }
@@ -25,6 +26,7 @@ void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& reg
       verify_tc_gemm(t, region);
       break;
     }
+    case K_ARGMAX: verify_argmax(*(const ArgmaxParams*)l.blob.data(), region); break;
     default: fail(E_INTERNAL, std::string("no bounds verifier for kernel kind ") + kernel_kind_name(l.kind));
   }
 }

@@ -31,7 +31,7 @@ namespace cljxla {
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
                             "gemm_generic", "gemv", "attention", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
-                            "all_reduce", "gemv_fused", "fused_kv_write"};
+                            "all_reduce", "gemv_fused", "fused_kv_write", "argmax"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }
 
@@ -205,6 +205,8 @@ class Planner {
   std::vector<std::vector<int>> users_;
   std::vector<std::vector<int>> ins_;         // operands (fused kernels override the graph's)
   std::map<int, AttnMatch> attn_;             // probs.V dot -> matched attention block
+  std::map<int, int> argmax_;                 // final i32 reduce of a printed argmax -> the float logits it reads
+  int match_argmax(int r) const;
   std::vector<RowRegion> regions_;
   std::vector<int> region_of_;                // node -> region index or -1
   std::vector<int> uf_;                       // union-find parent (EW nodes)
@@ -1360,6 +1362,88 @@ void Planner::emit_row_region(int rid) {
   push(K_ROWNORM, blob_of(P), label, bytes);
 }
 
+// The printed argmax over the last axis of x (tensor.clj:519-532):
+//   reduce_max_i32( convert_i32( compare_EQ(x, broadcast(reduce_max(x))) ) * broadcast(iota literal) )
+// Returns x when node r is the final reduce of that chain, else -1.
+int Planner::match_argmax(int r) const {
+  const Node& R = g_.nodes[r];
+  if (R.op != Op::Reduce || R.i0 != RED_MAX || R.dt != DT::I32 || R.in.size() != 2) return -1;
+  const Node& M = g_.nodes[R.in[0]];
+  const int rank = M.rank();
+  if (M.op != Op::Mul || M.dt != DT::I32 || rank < 1 || R.ia.size() != 1 || R.ia[0] != rank - 1) return -1;
+  double init;
+  if (!const_cast<Planner*>(this)->splat_value(R.in[1], init) || init > 0) return -1;
+  const int64_t V = M.shape.back();
+  auto strip = [&](int n) {  // through reshapes and broadcasts
+    while (g_.nodes[n].op == Op::Reshape || g_.nodes[n].op == Op::Broadcast) n = g_.nodes[n].in[0];
+    return n;
+  };
+  // a chain of reshapes / broadcasts that only adds or repeats leading dims,
+  // keeping the last axis: the value at (..., j) is the source's element j
+  auto keeps_last = [&](int n, int src) {
+    for (; n != src; n = g_.nodes[n].in[0]) {
+      const Node& a = g_.nodes[n];
+      const Node& b = g_.nodes[a.in[0]];
+      if (b.shape.empty() || b.shape.back() != V) return false;
+      for (size_t d = 0; d + 1 < b.shape.size(); ++d)
+        if (b.shape[d] != 1) return false;
+      if (a.op == Op::Broadcast && (a.ia.empty() || a.ia.back() != a.rank() - 1)) return false;
+    }
+    return true;
+  };
+  for (int side = 0; side < 2; ++side) {
+    const Node& C = g_.nodes[M.in[side]];
+    const int io = M.in[1 - side];
+    if (C.op != Op::Convert || g_.nodes[C.in[0]].op != Op::Compare) continue;
+    const Node& E = g_.nodes[C.in[0]];
+    if (E.i0 != CMP_EQ) continue;
+    // the index operand: an i32 literal 0 .. V-1 along the last axis
+    const int ic = strip(io);
+    const Node& K = g_.nodes[ic];
+    if (K.op != Op::Constant || K.dt != DT::I32 || K.splat || K.numel() != V || !keeps_last(io, ic)) continue;
+    const int32_t* kv = (const int32_t*)K.data.data();
+    if (K.data.size() != (size_t)V * 4) continue;
+    bool iota = true;
+    for (int64_t j = 0; j < V && iota; ++j) iota = kv[j] == j;
+    if (!iota) continue;
+    // x compared with the broadcast of its own row maximum
+    for (int e = 0; e < 2; ++e) {
+      const int x = E.in[e], bm = E.in[1 - e];
+      const Node& X = g_.nodes[x];
+      if (!dt_is_float(X.dt) || X.shape != M.shape) continue;
+      const int mx = strip(bm);
+      const Node& Mx = g_.nodes[mx];
+      if (Mx.op != Op::Reduce || Mx.i0 != RED_MAX || Mx.in[0] != x || Mx.ia.size() != 1 || Mx.ia[0] != rank - 1)
+        continue;
+      double minit;
+      if (!const_cast<Planner*>(this)->splat_value(Mx.in[1], minit) || minit > -1e30) continue;
+      // the row maximum at every position of its row: broadcast(reshape(mx) to
+      // [..., 1]) with identity dimensions, or broadcast(mx) over the last axis
+      std::vector<int64_t> lead(M.shape.begin(), M.shape.end() - 1), lead1 = lead;
+      lead1.push_back(1);
+      const Node& B = g_.nodes[bm];
+      if (B.op != Op::Broadcast || Mx.shape != lead) continue;
+      const Node& Bi = g_.nodes[B.in[0]];
+      bool ok = false;
+      if (B.in[0] == mx) {
+        ok = (int)B.ia.size() == rank - 1;
+        for (int d = 0; d < rank - 1 && ok; ++d) ok = B.ia[d] == d;
+      } else if (Bi.op == Op::Reshape && Bi.in[0] == mx && Bi.shape == lead1) {
+        ok = (int)B.ia.size() == rank;
+        for (int d = 0; d < rank && ok; ++d) ok = B.ia[d] == d;
+      }
+      if (!ok) continue;
+      // logits widened to f32 only for the comparison: the kernel reads the
+      // narrower values (the widening is exact, so the result is the same)
+      if (X.op == Op::Convert && (g_.nodes[X.in[0]].dt == DT::BF16 || g_.nodes[X.in[0]].dt == DT::F16) &&
+          X.dt == DT::F32 && g_.nodes[X.in[0]].shape == X.shape)
+        return X.in[0];
+      return x;
+    }
+  }
+  return -1;
+}
+
 void Planner::emit_attention(int d2) {
   const AttnMatch& am = attn_.at(d2);
   const Node& D2 = g_.nodes[d2];
@@ -1533,6 +1617,25 @@ void Planner::emit_node_kernel(int id) {
   int oslot = ensure_buf(id);
   switch (n.op) {
     case Op::Reduce: {
+      if (argmax_.count(id)) {
+        const int x = argmax_.at(id);
+        ArgmaxParams A{};
+        A.in = view_of(x);
+        A.out = slot_ptr(oslot);
+        A.V = g_.nodes[x].shape.back();
+        A.rows = g_.nodes[x].numel() / std::max<int64_t>(1, A.V);
+        // a wave of CTAs over all rows, at least 2048 logits per CTA
+        A.ctas = (int32_t)std::max<int64_t>(1, std::min<int64_t>((2 * 148 + A.rows - 1) / A.rows, A.V / 2048));
+        A.ctas = std::min<int32_t>(A.ctas, 1024);
+        if (A.ctas > 1) {
+          A.part = slot_ptr(new_tmp(argmax_part_bytes(A)));
+          size_t off = (plan_.const_blob.size() + 255) & ~size_t(255);
+          plan_.const_blob.resize(off + 4 * A.rows, 0);
+          A.counters = slot_ptr(P_ + O_ + U_, (int64_t)off);
+        }
+        push(K_ARGMAX, blob_of(A), n.name, g_.nodes[x].numel() * (int64_t)dt_size(g_.nodes[x].dt) + A.rows * 4);
+        break;
+      }
       const Node& in = g_.nodes[n.in[0]];
       if (!is_splat(n.in[1])) fail(E_UNIMPLEMENTED, "reduce with a non-constant init value");
       TView v = view_of(n.in[0]);
@@ -2162,6 +2265,15 @@ void Planner::run() {
       attn_[am.d2] = am;
     }
     if (!attn_.empty()) liveness();
+    // greedy sampling: the printed argmax (tensor.clj:519-532) becomes one kernel
+    for (int i = 0; i < N; ++i) {
+      if (!live_[i]) continue;
+      const int x = match_argmax(i);
+      if (x < 0) continue;
+      ins_[i] = {x};
+      argmax_[i] = x;
+    }
+    if (!argmax_.empty()) liveness();
   }
   {
     // a dynamic_update_slice whose update is a float->float convert reads the

@@ -17,6 +17,7 @@ enum KernelKind : int {
   K_ALLREDUCE,  // tensor-parallel sum over the client's NCCL communicator
   K_GEMV_FUSED,  // compiled GEMV whose x is computed in each CTA by its producer's program (parts[0])
   K_FUSED_DUS,   // elementwise / row program (parts[0]) that also writes its output into KV windows (parts[1..], K_DUS)
+  K_ARGMAX,      // the printed in-graph argmax as one kernel (k_argmax.cu)
   K_NUM_KINDS
 };
 const char* kernel_kind_name(int k);

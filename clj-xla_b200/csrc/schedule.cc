@@ -186,6 +186,26 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
       }
       return true;
     }
+    case K_ARGMAX: {
+      const ArgmaxParams& a = *(const ArgmaxParams*)b;
+      c.view(a.in, false);
+      c.add(a.out, a.rows * 4, true);
+      if (a.ctas > 1) {
+        c.add(a.part, argmax_part_bytes(a), true);
+        c.add(a.counters, a.rows * 4, true);
+      }
+      return true;
+    }
+    case K_ALLREDUCE: {
+      // a collective orders only against what touches its operand and result:
+      // every rank plans the same graph, so every rank issues its collectives in
+      // the same (re-levelled) order
+      const AllReduceParams& a = *(const AllReduceParams*)b;
+      const int64_t bytes = a.count * (int64_t)dt_size((DT)a.dt);
+      c.add(a.src, bytes, false);
+      c.add(a.dst, bytes, true);
+      return true;
+    }
     case K_GEMM_TC: {
       const TcGemmParams& t = *(const TcGemmParams*)b;
       c.add(t.a, ((int64_t)(t.a_parts * t.M - 1) * t.a_ld + t.K) * 2, false);

@@ -149,17 +149,25 @@ class PjrtApi:
         return out
 
     # ------------------------------------------------------------ events
+    def _args24(self):
+        """A reusable 24-byte argument struct (struct_size 24, one pointer at
+        16) for the per-step Event_Await / Event_Destroy / Buffer_Destroy calls:
+        the same bytes the reference writes, without a new allocation per call."""
+        a = self.__dict__.get("_a24")
+        if a is None:
+            a = self._a24 = ctypes.create_string_buffer(24)
+            _w64(a, 0, 24)
+            self._a24_addr = _addr(a)
+        return a
+
     def _await_destroy(self, event_ptr: int):
         if not event_ptr:
             return
-        aw = ctypes.create_string_buffer(24)
-        _w64(aw, 0, 24)
-        _w64(aw, 16, event_ptr)
-        err = self._call(OFFSET_EVENT_AWAIT, aw)
-        d = ctypes.create_string_buffer(24)
-        _w64(d, 0, 24)
-        _w64(d, 16, event_ptr)
-        self._call(OFFSET_EVENT_DESTROY, d)
+        a = self._args24()
+        _w64(a, 16, event_ptr)
+        err = self._fn(OFFSET_EVENT_AWAIT)(self._a24_addr) or 0
+        _w64(a, 16, event_ptr)
+        self._fn(OFFSET_EVENT_DESTROY)(self._a24_addr)
         self.check_error(err)
 
     # ------------------------------------------------------------ client
@@ -288,10 +296,11 @@ class PjrtApi:
     def destroy_buffer(self, buf: int):
         if not buf:
             return
-        args = ctypes.create_string_buffer(24)
-        _w64(args, 0, 24)
-        _w64(args, 16, buf)
-        self.check_error(self._call(OFFSET_BUFFER_DESTROY, args))
+        a = self._args24()
+        _w64(a, 16, buf)
+        err = self._fn(OFFSET_BUFFER_DESTROY)(self._a24_addr)
+        if err:
+            self.check_error(err)
 
     def execute_executable(self, exe: int, input_buffers: Sequence[int], num_outputs: int = 1,
                            wait: bool = True):

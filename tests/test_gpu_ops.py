@@ -96,6 +96,31 @@ def test_reductions_and_argmax(ctx, dt):
     check_graph(ctx, g, [rand((3, 50, 300), dt, 7)])
 
 
+@pytest.mark.parametrize("dt,rows,V", [("f32", 3, 262144), ("bf16", 8, 262144), ("bf16", 2, 1000)])
+def test_argmax_kernel_with_planted_ties(ctx, dt, rows, V):
+    """The printed argmax (tensor.clj:519-532) runs as one kernel (rows split
+    over CTAs at vocabulary size); the token ids equal the oracle's bit for bit,
+    including the highest-index rule for ties planted across CTA boundaries,
+    for f32 logits and for bf16 logits widened to f32 as the Gemma graphs print."""
+    def f(x):
+        return [t.argmax(t.convert(x, "f32") if dt == "bf16" else x)]
+    g = t.trace_graph("amax", [("x", ("tensor", (rows, 1, V), dt))], f)
+    text = shlo.graph_to_mlir_text(g)
+    exe = core.compile_mlir_text(ctx, text, g)
+    assert core.plan_info(ctx, exe)["launches"] <= 2  # the argmax kernel (+ the reshaped result)
+    x = interp.bf16_bits_to_f32(rand((rows, 1, V), "bf16", 31)) if dt == "bf16" else rand((rows, 1, V), "f32", 31)
+    x = np.array(x, np.float32)
+    for r in range(rows):  # the same maximum at indices far apart
+        top = np.float32(9.0 + r)
+        for j in (5 * r, V // 3 + r, V - 1 - 7 * r):
+            x[r, 0, j] = top
+    inp = interp.f32_to_bf16_bits(x) if dt == "bf16" else x
+    want = interp.run_mlir(text, [inp])[0]
+    got = runner.run_graph(ctx, g, [inp], text)[0]
+    assert got.dtype == np.int32 and np.array_equal(got, want), (got.ravel(), want.ravel())
+    assert np.array_equal(got.ravel(), [V - 1 - 7 * r for r in range(rows)])
+
+
 @pytest.mark.parametrize("dt", ["f32", "bf16"])
 def test_dot_general_forms(ctx, dt):
     def f(x, w, q, k):
