@@ -191,6 +191,11 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     launch_gemv(*(const GemvParams*)b, argtab, s);
     return;
   }
+  if (l.kind == K_GEMV_TAIL) {  // not compiled: the GEMV, then its tail programs one after another
+    launch_gemv(*(const GemvParams*)b, argtab, s);
+    for (const Launch& part : l.parts) run_launch(part, argtab, s);
+    return;
+  }
   if (l.kind == K_MULTI || l.kind == K_FUSED_DUS) {  // not compiled: the parts one after another
     for (const Launch& part : l.parts) run_launch(part, argtab, s);
     return;

@@ -29,6 +29,9 @@ struct GemvParams {
   int64_t pf_bytes[GEMV_MAXSEG];
   int32_t npf;
   int32_t pro_out;  // K_GEMV_FUSED: the producer output that is x
+  // K_GEMV_TAIL: arrival counter of the CTAs (zero between launches; the last
+  // CTA to arrive runs the tail programs and resets it)
+  DPtr tail_ctr;
   // the plan's status word (bounded waits of the bulk-copy GEMV report timeouts there)
   DPtr status;
   int32_t has_status, pad_s;
@@ -36,6 +39,9 @@ struct GemvParams {
 
 // Points every GEMV launch's prefetch at the weights of the next GEMV launch.
 void link_gemv_prefetch(Plan& p);
+// Points each staged decode attention's L2 hints at the weights of the GEMVs
+// that follow it, up to a byte budget.
+void link_attention_hints(Plan& p);
 
 // Appends a GEMV whose x, M and K match the launch's as a further segment.
 bool gemv_add_segment(Launch& l, const GemmParams& g);
@@ -96,6 +102,7 @@ namespace cljxla {
 // [B, nq, Sq, hd].  The printed score chain (scale / softcap, with its
 // roundings) runs as a register program on each score.
 constexpr int ATTN_MERGE_MAX_SPLITS = 64;  // position splits merged in-kernel (arrival counters)
+constexpr int ATTN_MAX_HINTS = 4;          // weight regions a decode attention prefetches into L2
 
 struct AttnParams {
   TView q, k, v, mask;
@@ -122,6 +129,12 @@ struct AttnParams {
   int32_t dec_per_split, dec_chunk;
   DPtr status;
   int32_t has_status, pad_s;
+  // weights of the GEMVs that follow, asked into L2 by this kernel's CTAs
+  // before their dependency wait (the HBM is otherwise idle while a decode
+  // attention runs); regions are 16-byte aligned multiples of 16 bytes
+  DPtr hint[ATTN_MAX_HINTS];
+  int64_t hint_bytes[ATTN_MAX_HINTS];
+  int32_t nhint, pad_h;
 };
 
 void launch_attention(const AttnParams& p, const uint64_t* argtab, cudaStream_t s);

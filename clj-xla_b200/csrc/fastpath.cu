@@ -16,7 +16,7 @@ void run_fast_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
 
 void verify_fast_launch_impl(const Plan& p, const Launch& l, const RegionFn& region) {
   switch (l.kind) {
-    case K_GEMV: case K_GEMV_FUSED: verify_gemv(p, l, region); break;
+    case K_GEMV: case K_GEMV_FUSED: case K_GEMV_TAIL: verify_gemv(p, l, region); break;
     case K_ATTN_DECODE: case K_ATTN_COMBINE: verify_attention(l, region); break;
     case K_GEMM_TC: {
       const TcGemmParams& t = *(const TcGemmParams*)l.blob.data();

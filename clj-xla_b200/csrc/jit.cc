@@ -94,7 +94,28 @@ std::string args_struct() {
          std::to_string(JIT_MAXBUF) + "]; };\n";
 }
 
+// set while emitting the tail programs of a GEMV: their inputs include rows
+// other CTAs of the same kernel wrote, so loads go through L2 (ld.global.cg)
+thread_local bool g_l2_loads = false;
+
 std::string load_expr(const std::string& base, const std::string& off, int dt) {
+  if (g_l2_loads) {
+    auto L = [&](const char* type) {
+      return std::string("__ldcg((const ") + type + "*)(" + base + ") + (" + off + "))";
+    };
+    switch (dt) {
+      case KDT_F32: return "U(" + L("float") + ")";
+      case KDT_BF16: return "((u32)" + L("unsigned short") + " << 16)";
+      case KDT_F16: return "U(h2f(" + L("unsigned short") + "))";
+      case KDT_I32: case KDT_U32: return "(u32)" + L("int");
+      case KDT_I8: return "(u32)(int)" + L("signed char");
+      case KDT_U8: return "(u32)" + L("unsigned char");
+      case KDT_I16: return "(u32)(int)" + L("short");
+      case KDT_I1: return "(" + L("unsigned char") + " ? 1u : 0u)";
+      case KDT_I64: return "(u32)(int)" + L("long long");
+      case KDT_F64: return "U((float)" + L("double") + ")";
+    }
+  }
   const std::string o = "[" + off + "]";
   switch (dt) {
     case KDT_F32: return "U(((const float*)" + base + ")" + o + ")";
@@ -1006,15 +1027,17 @@ bool describe_gemv_mma_chunked(const GemvParams& G, std::string* src, int64_t* g
 
 bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* block, int* smem, JitArgs* args) {
   const bool fused = l.kind == K_GEMV_FUSED;
-  if (!(l.kind == K_GEMV || (fused && l.parts.size() == 1))) return false;
+  const bool tail = l.kind == K_GEMV_TAIL;
+  if (!(l.kind == K_GEMV || (fused && l.parts.size() == 1) || (tail && !l.parts.empty()))) return false;
   const GemvParams& G = *(const GemvParams*)l.blob.data();
+  if (tail && (G.M != 1 || !jit_gemv_tail_ok(G))) return false;
   if (!G.has_status) return false;  // no status word: keep the plain kernel
   static const bool off = [] {
     const char* e = getenv("CLJXLA_B200_GEMV_TMA");
     return e && e[0] == '0';
   }();
   if (off) return false;
-  if (G.M >= 2 && !fused &&
+  if (G.M >= 2 && !fused && !tail &&
       (describe_gemv_mma(G, src, grid, block, smem, args) || describe_gemv_mma_chunked(G, src, grid, block, smem, args)))
     return true;
   GemvGeometry geo;
@@ -1031,8 +1054,8 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
     int b0, c0;
     if (!describe_one(pro, &g0, &b0, &c0, args)) return false;
   }
-  const int kW = npb, kY = npb + G.nseg, kS = npb + 2 * G.nseg, kX = kS + 1;
-  if (kX + 1 > JIT_MAXBUF) return false;
+  const int kW = npb, kY = npb + G.nseg, kS = npb + 2 * G.nseg, kX = kS + 1, kT = kX + 1;
+  if (kT + 1 > JIT_MAXBUF) return false;
   auto put = [&](int k, const DPtr& p) {
     args->s[k] = p.slot;
     args->o[k] = p.off;
@@ -1043,6 +1066,7 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
   }
   put(kS, G.status);
   put(kX, G.x);
+  if (tail) put(kT, G.tail_ctr);
   constexpr int WARPS = 8;
   const int64_t M = G.M, K = G.K, N = G.N;
   const int WPR = geo.wpr, RPS = geo.rps, NST = geo.nstage;
@@ -1051,6 +1075,22 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
       std::max<int64_t>(1, std::min<int64_t>((int64_t)geo.ctas_per_sm * sm_count(), (N + RPS - 1) / RPS));
   const int xes = G.x_dt == KDT_F32 ? 4 : 2;
   const int stage_stride = (geo.stage_bytes + 1023) & ~1023;
+  // tail: the last CTA to arrive runs the programs after the GEMV (the acquire
+  // orders its loads after every CTA's rows; they read through L2)
+  std::string tail_code;
+  if (tail) {
+    std::ostringstream t;
+    const std::string ctr = "((unsigned*)" + base_expr(kT) + ")";
+    t << "  {\n    __shared__ unsigned tail_last;\n    consumers_sync();\n";
+    t << "    if (threadIdx.x == 0) {\n      unsigned old;\n";
+    t << "      asm volatile(\"atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;\" : \"=r\"(old) : \"l\"(" << ctr
+      << ") : \"memory\");\n";
+    t << "      tail_last = old == gridDim.x - 1u;\n    }\n    consumers_sync();\n    if (tail_last) {\n";
+    for (size_t i = 0; i < l.parts.size(); ++i)
+      t << "      tail" << i << "(argtab, t.p[" << i << "], 0u, 1u);\n      consumers_sync();\n";
+    t << "      if (threadIdx.x == 0) *" << ctr << " = 0u;  // ready for the next launch\n    }\n  }\n";
+    tail_code = t.str();
+  }
   std::ostringstream s;
   s << kPrelude << args_struct();
   s << R"G(__device__ __forceinline__ float bf_lo(u32 u) { return __uint_as_float(u << 16); }
@@ -1125,8 +1165,21 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   for (int i = 0; i + 1 < G.nseg; ++i)
     s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
   s << "  return e;\n}\n";
+  if (tail) {
+    // the tail programs, each a body run by the 256 consumer threads of one CTA
+    s << "struct JitTail { JitArgs g; JitArgs p[" << l.parts.size() << "]; };\n";
+    g_l2_loads = true;
+    for (size_t i = 0; i < l.parts.size(); ++i) {
+      BodyOpts bo;
+      bo.block = WARPS * 32;
+      bo.sync = "consumers_sync()";
+      emit_body(s, l.parts[i], WARPS * 32, 1, "tail" + std::to_string(i), bo);
+    }
+    g_l2_loads = false;
+  }
   s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
-    << ", " << geo.ctas_per_sm << ") cljxla_fused_gemv(const u64* __restrict__ argtab, const JitArgs a) {\n";
+    << ", " << geo.ctas_per_sm << ") cljxla_fused_gemv(const u64* __restrict__ argtab, const "
+    << (tail ? "JitTail t) {\n  const JitArgs& a = t.g;\n" : "JitArgs a) {\n");
   s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
   s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
   s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
@@ -1225,7 +1278,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
         << store_stmt("Y", "row - lo", G.y_dt[i], "U(t)") << " }\n";
       (void)rows;
     }
-    s << "  }\n}\n";
+    s << "  }\n" << tail_code << "}\n";
     *src = s.str();
     *grid = ctas;
     *block = (WARPS + 1) * 32;
@@ -1245,7 +1298,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     s << "      if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; for (int m = 0; m < " << M << "; ++m) "
       << store_stmt("Y", "(i64)m * " + std::to_string(rows) + "LL + (row - lo)", G.y_dt[i], "U(acc[m])") << " }\n";
   }
-  s << "    }\n    r = e;\n  }\n}\n";
+  s << "    }\n    r = e;\n  }\n" << tail_code << "}\n";
   *src = s.str();
   *grid = ctas;
   *block = (WARPS + 1) * 32;
@@ -1271,11 +1324,19 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
                   std::vector<JitArgs>* args, int* smem) {
   args->clear();
   *smem = 0;
-  if (l.kind == K_GEMV_FUSED || l.kind == K_GEMV) {
+  if (l.kind == K_GEMV_FUSED || l.kind == K_GEMV || l.kind == K_GEMV_TAIL) {
     JitArgs a;
     *cluster = 1;
     if (!describe_gemv_tma(l, src, grid, block, smem, &a)) return false;
     args->push_back(a);
+    if (l.kind == K_GEMV_TAIL)
+      for (const Launch& p : l.parts) {
+        int64_t g;
+        int b, c;
+        JitArgs pa;
+        if (!describe_one(p, &g, &b, &c, &pa) || c != 1) return false;
+        args->push_back(pa);
+      }
     return true;
   }
   if (l.kind == K_MULTI) {
@@ -1511,6 +1572,30 @@ void* compile_one(const std::string& src) {
 }
 
 }  // namespace
+
+bool jit_gemv_tail_ok(const GemvParams& g) {
+  if (!jit_enabled() || !g.has_status || g.M != 1) return false;
+  if (const char* e = getenv("CLJXLA_B200_GEMV_TMA"))
+    if (e[0] == '0') return false;
+  GemvGeometry geo;
+  return gemv_tma_geometry(g, &geo);
+}
+
+bool jit_tail_program_ok(const Launch& l) {
+  int64_t g;
+  int b, c;
+  JitArgs a;
+  const Launch& base = l.kind == K_FUSED_DUS && !l.parts.empty() ? l.parts[0] : l;
+  if (base.kind == K_ROWNORM) {
+    const RowParams& r = *(const RowParams*)base.blob.data();
+    if (r.rows > 64) return false;
+  } else if (base.kind == K_EW) {
+    if (((const EwParams*)base.blob.data())->n > (1 << 16)) return false;
+  } else {
+    return false;
+  }
+  return describe_one(l, &g, &b, &c, &a) && c == 1;
+}
 
 void jit_disk_cache_stats(int64_t* hits, int64_t* misses) {
   if (hits) *hits = g_disk_hits.load();

@@ -20,6 +20,7 @@
 #include <string>
 #include <vector>
 
+#include "fast_kernels.h"
 #include "planner.h"
 
 namespace cljxla {
@@ -47,6 +48,12 @@ bool jit_enabled();
 // and returns how many failed (-1: NVRTC not available); the first failure's
 // log and source go to first_log.
 int jit_check_sources(const std::vector<std::string>& sources, std::string* first_log);
+// whether a decode GEMV compiles to the bulk-copy kernel that can carry a tail
+// (one x row), and whether a launch can be one of its tail programs (a small
+// elementwise / row program, with folded KV writes, run by one CTA)
+bool jit_gemv_tail_ok(const GemvParams& g);
+bool jit_tail_program_ok(const Launch& l);
+
 // programs found in / added to the on-disk cache of compiled fused kernels by this process
 void jit_disk_cache_stats(int64_t* hits, int64_t* misses);
 

@@ -1088,6 +1088,18 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
       }
     }
   }
+  // the following GEMVs' weights towards L2 (never written by a plan kernel):
+  // this CTA's slice of each region, in region order
+  {
+    const int64_t nct = (int64_t)gridDim.x * gridDim.y, me = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
+    for (int h = 0; h < P.nhint; ++h) {
+      const int64_t per = ((P.hint_bytes[h] + nct - 1) / nct + 15) & ~(int64_t)15;
+      const int64_t lo = me * per, hi = min(P.hint_bytes[h], lo + per);
+      const char* base = dres(P.hint[h], argtab);
+      for (int64_t o = lo + (int64_t)threadIdx.x * 4096; o < hi; o += (int64_t)DEC_THREADS * 4096)
+        l2_prefetch_bulk(base + o, (uint32_t)min((int64_t)4096, hi - o));
+    }
+  }
   if (threadIdx.x == 0) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dec_smem_u32(&bar)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1993,6 +2005,12 @@ void verify_attention(const Launch& l, const RegionFn& region) {
         (p.part.off % 16))
       fail(E_INTERNAL, "staged decode attention: bad split / chunk sizes");
     if (p.has_status) region(p.status, 4, "status word");
+    if (p.nhint < 0 || p.nhint > ATTN_MAX_HINTS) fail(E_INTERNAL, "staged decode attention: bad hint list");
+    for (int h = 0; h < p.nhint; ++h) {
+      if (p.hint_bytes[h] % 16 || p.hint[h].off % 16 || p.hint_bytes[h] <= 0)
+        fail(E_INTERNAL, "staged decode attention: unaligned hint");
+      region(p.hint[h], p.hint_bytes[h], "prefetched weights");
+    }
   }
   if (p.use_tc == 2 && (!attention_tc_prefill_ok(p) || p.splits != 1))
     fail(E_INTERNAL, "tensor-core prefill attention on unsupported views");

@@ -316,6 +316,42 @@ void link_gemv_prefetch(Plan& plan) {
   }
 }
 
+void link_attention_hints(Plan& plan) {
+  // the HBM idles while a decode attention runs (its K / V come from L2,
+  // prefetched during the kernel before it): the attention asks L2 for the
+  // weights of the GEMVs after it, in launch order, up to CLJXLA_B200_L2_HINT_MB
+  // (off by default: the prefetch slowed the step down at every budget tried)
+  int64_t budget_all = 0;  // measured: 24 / 64 / 112 / 160 MB cost 1 / 2 / 4 / 10 % on Gemma-3-4B decode
+  if (const char* e = getenv("CLJXLA_B200_L2_HINT_MB")) budget_all = atoll(e) << 20;
+  const int n = (int)plan.launches.size();
+  for (int i = 0; i < n; ++i) {
+    Launch& l = plan.launches[i];
+    if (l.kind != K_ATTN_DECODE) continue;
+    AttnParams& a = *(AttnParams*)l.blob.data();
+    a.nhint = 0;
+    if (a.use_tc != 3 || budget_all <= 0) continue;
+    int64_t budget = budget_all;
+    for (int j = i + 1; j < n && budget > 0 && a.nhint < ATTN_MAX_HINTS; ++j) {
+      const Launch& g = plan.launches[j];
+      if (g.kind == K_ATTN_DECODE) break;  // the next layer's attention prefetches its own
+      if (g.kind != K_GEMV) continue;
+      const GemvParams& gp = *(const GemvParams*)g.blob.data();
+      if (gp.w_dt != KDT_BF16 && gp.w_dt != KDT_F32) continue;
+      const int64_t es = gp.w_dt == KDT_F32 ? 4 : 2;
+      for (int s = 0; s < gp.nseg && budget > 0 && a.nhint < ATTN_MAX_HINTS; ++s) {
+        if (gp.w[s].off % 16) continue;
+        const int64_t rows = gp.seg_end[s] - (s ? gp.seg_end[s - 1] : 0);
+        const int64_t bytes = std::min<int64_t>(rows * gp.K * es, budget) & ~(int64_t)15;
+        if (bytes <= 0) break;
+        a.hint[a.nhint] = gp.w[s];
+        a.hint_bytes[a.nhint] = bytes;
+        a.nhint++;
+        budget -= bytes;
+      }
+    }
+  }
+}
+
 void verify_gemv(const Plan& plan, const Launch& l, const RegionFn& region) {
   (void)plan;
   const GemvParams& p = *(const GemvParams*)l.blob.data();

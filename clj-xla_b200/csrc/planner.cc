@@ -31,7 +31,7 @@ namespace cljxla {
 const char* kernel_kind_name(int k) {
   static const char* n[] = {"fused_elementwise", "reduce", "copy", "gather", "dynamic_update_slice",
                             "gemm_generic", "gemv", "attention", "attn_combine", "rownorm", "gemm_tc", "fused_multi",
-                            "all_reduce", "gemv_fused", "fused_kv_write", "argmax"};
+                            "all_reduce", "gemv_fused", "fused_kv_write", "argmax", "gemv_tail"};
   return k >= 0 && k < K_NUM_KINDS ? n[k] : "?";
 }
 
@@ -2382,7 +2382,11 @@ void Planner::run() {
   verify_plan(plan_);
   if (opt_.fuse) {
     schedule_and_merge(plan_);
-    if (opt_.fast_kernels) link_gemv_prefetch(plan_);
+    if (opt_.fast_kernels) {
+      link_gemv_prefetch(plan_);
+      link_attention_hints(plan_);
+      fuse_gemv_tails(plan_);
+    }
     verify_plan(plan_);
   }
   if (const char* path = getenv("CLJXLA_B200_DUMP_PLAN")) {

@@ -18,6 +18,7 @@ enum KernelKind : int {
   K_GEMV_FUSED,  // compiled GEMV whose x is computed in each CTA by its producer's program (parts[0])
   K_FUSED_DUS,   // elementwise / row program (parts[0]) that also writes its output into KV windows (parts[1..], K_DUS)
   K_ARGMAX,      // the printed in-graph argmax as one kernel (k_argmax.cu)
+  K_GEMV_TAIL,   // compiled GEMV whose last CTA to finish then runs the small programs after it (parts)
   K_NUM_KINDS
 };
 const char* kernel_kind_name(int k);
@@ -123,6 +124,11 @@ std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
 // Re-levels the launch list by the memory each launch touches and merges
 // independent compiled fused kernels of one launch shape (schedule.cc).
 void schedule_and_merge(Plan& p);
+
+// Appends the small compiled programs that directly follow a decode GEMV to it
+// as a tail its last CTA runs (K_GEMV_TAIL), removing their kernel boundaries
+// (schedule.cc).
+void fuse_gemv_tails(Plan& p);
 
 // Generates and compiles the fused elementwise / row launches of a plan
 // (no-op when runtime compilation is unavailable or disabled).

@@ -153,8 +153,13 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
       c.add(g.c, g.batch * g.M * g.N * (int64_t)dt_size((DT)g.c_dt), true);
       return true;
     }
-    case K_GEMV: case K_GEMV_FUSED: {
+    case K_GEMV: case K_GEMV_FUSED: case K_GEMV_TAIL: {
       const GemvParams& g = *(const GemvParams*)b;
+      if (l.kind == K_GEMV_TAIL) {
+        for (const Launch& part : l.parts)
+          if (!accesses(p, part, out)) return false;
+        c.add(g.tail_ctr, 4, true);
+      }
       if (l.kind == K_GEMV_FUSED) {  // x is computed in shared memory by the producer's program
         if (l.parts.size() != 1 || !accesses(p, l.parts[0], out)) return false;
       } else {
@@ -411,6 +416,67 @@ void fuse_gemv_prologues(Plan& p, bool ew_only) {
 }
 
 }  // namespace
+
+void fuse_gemv_tails(Plan& p) {
+  if (getenv("CLJXLA_B200_GEMV_TAIL") && getenv("CLJXLA_B200_GEMV_TAIL")[0] == '0') return;
+  std::vector<Launch> out;
+  out.reserve(p.launches.size());
+  const size_t n = p.launches.size();
+  for (size_t i = 0; i < n;) {
+    Launch& l = p.launches[i];
+    GemvParams g;
+    if (l.kind != K_GEMV || l.blob.size() != sizeof(GemvParams)) {
+      out.push_back(std::move(l));
+      ++i;
+      continue;
+    }
+    memcpy(&g, l.blob.data(), sizeof g);
+    // the small programs right after the GEMV (flattening merged launches),
+    // at most 8, up to the next launch of any other kind
+    std::vector<Launch> tail;
+    size_t j = i + 1;
+    if (jit_gemv_tail_ok(g)) {
+      for (; j < n; ++j) {
+        Launch& t = p.launches[j];
+        std::vector<Launch*> progs;
+        if (t.kind == K_MULTI) {
+          for (Launch& q : t.parts) progs.push_back(&q);
+        } else {
+          progs.push_back(&t);
+        }
+        bool ok = !progs.empty() && tail.size() + progs.size() <= 8;
+        for (Launch* q : progs) ok = ok && jit_tail_program_ok(*q);
+        if (!ok) break;
+        for (Launch* q : progs) tail.push_back(std::move(*q));
+      }
+    }
+    if (tail.empty()) {
+      out.push_back(std::move(l));
+      ++i;
+      continue;
+    }
+    // the arrival counter: a zero word in the constant blob
+    size_t off = (p.const_blob.size() + 255) & ~size_t(255);
+    p.const_blob.resize(off + 4, 0);
+    g.tail_ctr = DPtr{p.const_slot(), 0, (int64_t)off};
+    Launch f;
+    f.kind = K_GEMV_TAIL;
+    f.blob.resize(sizeof g);
+    memcpy(f.blob.data(), &g, sizeof g);
+    f.label = l.label;
+    f.algo_bytes = l.algo_bytes;
+    f.algo_flops = l.algo_flops;
+    for (Launch& t : tail) {
+      f.label += "|" + t.label;
+      f.algo_bytes += t.algo_bytes;
+      f.algo_flops += t.algo_flops;
+    }
+    f.parts = std::move(tail);
+    out.push_back(std::move(f));
+    i = j;
+  }
+  p.launches = std::move(out);
+}
 
 void schedule_and_merge(Plan& p) {
   if (getenv("CLJXLA_B200_FOLD_KV") == nullptr || getenv("CLJXLA_B200_FOLD_KV")[0] != '0') fuse_dus_into_producers(p);

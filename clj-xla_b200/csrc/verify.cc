@@ -85,6 +85,17 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
       }
       return;
     }
+    if (l.kind == K_GEMV_TAIL) {
+      const GemvParams& g = *(const GemvParams*)l.blob.data();
+      if (l.parts.empty()) fail(E_INTERNAL, "GEMV tail without programs");
+      for (const Launch& part : l.parts) {
+        if (part.kind != K_EW && part.kind != K_ROWNORM && part.kind != K_FUSED_DUS)
+          fail(E_INTERNAL, "bad GEMV tail program");
+        verify_launch(p, c, part);
+      }
+      c.cur = &l;
+      c.region(g.tail_ctr, 4, "tail arrival counter");
+    }
     if (l.kind == K_GEMV_FUSED) {
       if (l.parts.size() != 1 || (l.parts[0].kind != K_EW && l.parts[0].kind != K_ROWNORM))
         fail(E_INTERNAL, "bad GEMV prologue");
