@@ -323,6 +323,7 @@ struct DusStore {
 
 struct BodyOpts {
   int block = 256;
+  int row_cache = 4;  // row programs keep their inputs in registers for rows of up to row_cache * block elements
   int smem_out = -1;
   std::string sync = "__syncthreads()";  // barrier over the threads running the body
   std::vector<DusStore> dus;
@@ -474,7 +475,7 @@ void emit_row_body(std::ostringstream& s, const RowParams& P, int BLOCK, int CL,
   const std::string xc = "x" + std::to_string(P.rank - 1);
   // a row of a few elements per thread: every phase walks the same J elements,
   // so the inputs are loaded once (first phase) and kept in registers
-  const int J = (CL == 1 && Cc <= 4LL * BLOCK) ? (int)((Cc + BLOCK - 1) / BLOCK) : 0;
+  const int J = (CL == 1 && Cc <= (int64_t)bo.row_cache * BLOCK) ? (int)((Cc + BLOCK - 1) / BLOCK) : 0;
   if (J > 0) {
     em.cache_arr.assign(P.nin, std::string());
     em.cached.assign(P.nin, 0);
@@ -1150,6 +1151,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     bo.block = WARPS * 32;
     bo.smem_out = G.pro_out;
     bo.sync = "consumers_sync()";  // the producer warp does not take part
+    bo.row_cache = 12;             // a decode row on 256 threads: every input load in flight at once
     emit_body(s, l.parts[0], WARPS * 32, 1, "pro_body", bo);
   }
   // segment of a row: index, first row, weights
@@ -1173,6 +1175,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
       BodyOpts bo;
       bo.block = WARPS * 32;
       bo.sync = "consumers_sync()";
+      bo.row_cache = 12;  // a decode row on 256 threads: its inputs stay in registers across phases
       emit_body(s, l.parts[i], WARPS * 32, 1, "tail" + std::to_string(i), bo);
     }
     g_l2_loads = false;
@@ -1586,11 +1589,15 @@ bool jit_tail_program_ok(const Launch& l) {
   int b, c;
   JitArgs a;
   const Launch& base = l.kind == K_FUSED_DUS && !l.parts.empty() ? l.parts[0] : l;
+  // one CTA runs the tail: a single row (the decode norms), or an elementwise
+  // program of at most two elements per thread; more serial work than that in
+  // one CTA costs more than the kernel boundary it removes (measured: the head
+  // norms, RoPE and GeGLU of a Gemma-3-4B layer as tails doubled the step time)
   if (base.kind == K_ROWNORM) {
     const RowParams& r = *(const RowParams*)base.blob.data();
-    if (r.rows > 64) return false;
+    if (r.rows != 1 || r.C > 12 * 256) return false;
   } else if (base.kind == K_EW) {
-    if (((const EwParams*)base.blob.data())->n > (1 << 16)) return false;
+    if (((const EwParams*)base.blob.data())->n > 512) return false;
   } else {
     return false;
   }

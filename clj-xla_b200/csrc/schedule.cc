@@ -175,7 +175,7 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
     case K_ATTN_DECODE: case K_ATTN_COMBINE: {
       const AttnParams& a = *(const AttnParams*)b;
       const int64_t rows = (int64_t)a.B * a.nq * a.Sq;
-      const int64_t part = (int64_t)a.splits * rows * (a.hd + 2) * 4;
+      const int64_t part = attention_part_bytes(a);
       if (l.kind == K_ATTN_DECODE) {
         c.view(a.q, false);
         c.view(a.k, false);
@@ -347,7 +347,7 @@ void fuse_dus_into_producers(Plan& p) {
 // [M, K], x's type), x fits in shared memory, and no launch between the two
 // touches what the producer reads or writes (so the producer may run at the
 // GEMV's place).
-void fuse_gemv_prologues(Plan& p, bool ew_only) {
+void fuse_gemv_prologues(Plan& p, bool ew_only, bool rows_only) {
   std::vector<Launch>& L = p.launches;
   for (size_t i = 0; i < L.size(); ++i) {
     if (L[i].kind != K_GEMV) continue;
@@ -384,7 +384,7 @@ void fuse_gemv_prologues(Plan& p, bool ew_only) {
       for (int o = 0; o < r.nout; ++o)
         if (!r.out[o].scalar && r.out[o].p.slot == G.x.slot && r.out[o].p.off == G.x.off && r.out[o].dt == G.x_dt) out = o;
       nbuf = r.nin + r.nout;
-    } else if (pro.kind == K_EW) {
+    } else if (pro.kind == K_EW && !rows_only) {
       const EwParams& e = *(const EwParams*)pro.blob.data();
       if (e.n != G.M * G.K) continue;
       for (int o = 0; o < e.nout; ++o)
@@ -418,7 +418,13 @@ void fuse_gemv_prologues(Plan& p, bool ew_only) {
 }  // namespace
 
 void fuse_gemv_tails(Plan& p) {
-  if (getenv("CLJXLA_B200_GEMV_TAIL") && getenv("CLJXLA_B200_GEMV_TAIL")[0] == '0') return;
+  // opt-in (CLJXLA_B200_GEMV_TAIL=1): on Gemma-3-4B decode the two single-row
+  // norms per layer as tails took 2.55 ms / step against 2.50 ms as their own
+  // kernels, and the head norms, RoPE and GeGLU as tails 4.57 ms: the tail
+  // waits for every CTA of the GEMV just as the kernel boundary does, and one
+  // CTA runs what several did
+  const char* e = getenv("CLJXLA_B200_GEMV_TAIL");
+  if (!e || e[0] != '1') return;
   std::vector<Launch> out;
   out.reserve(p.launches.size());
   const size_t n = p.launches.size();
@@ -480,11 +486,17 @@ void fuse_gemv_tails(Plan& p) {
 
 void schedule_and_merge(Plan& p) {
   if (getenv("CLJXLA_B200_FOLD_KV") == nullptr || getenv("CLJXLA_B200_FOLD_KV")[0] != '0') fuse_dus_into_producers(p);
-  // off by default: on Gemma-3-4B decode every CTA recomputing the norm / GeGLU
-  // before its first stage cost more (4.14 ms / step) than the separate small
-  // kernel whose latency the GEMV's early weight stream hides (3.37 ms / step)
-  if (const char* e = getenv("CLJXLA_B200_GEMV_PROLOGUE"))
-    if (e[0] == '1' || e[0] == '2') fuse_gemv_prologues(p, e[0] == '2');  // 2: elementwise producers only
+  // CLJXLA_B200_GEMV_PROLOGUE: 3 (default) the single-row norm producers only,
+  // 1 every producer, 2 elementwise producers only, 0 none.  Measured on
+  // Gemma-3-4B decode B=1: row producers as prologues 2.43 ms / step against
+  // 2.50 ms as their own kernels; the GeGLU (elementwise) producers recomputed
+  // in every CTA of the down projection cost more than they save (4.14 ms /
+  // step for all producers against 3.37 ms with an earlier GEMV)
+  {
+    const char* e = getenv("CLJXLA_B200_GEMV_PROLOGUE");
+    const char m = e && e[0] ? e[0] : '3';
+    if (m == '1' || m == '2' || m == '3') fuse_gemv_prologues(p, m == '2', m == '3');
+  }
   const int n = (int)p.launches.size();
   if (n < 2) return;
   std::vector<std::vector<Access>> acc(n);

@@ -177,13 +177,15 @@ def test_every_fused_program_is_compiled(ctx, family):
         assert info["jit_missing"] == 0, (kind, info)
 
 
-def test_gemv_prologue_fusion_matches_oracle(ctx, monkeypatch):
-    """The opt-in GEMV prologue fusion (the norm / GeGLU producer recomputed in
-    every GEMV CTA) computes the same decode step as the oracle."""
-    monkeypatch.setenv("CLJXLA_B200_GEMV_PROLOGUE", "1")
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_gemv_prologue_fusion_matches_oracle(ctx, monkeypatch, mode):
+    """GEMV prologue fusion with every producer recomputed in each GEMV CTA
+    (mode 1) and with none (mode 0) computes the same decode step as the
+    oracle (the default, row producers only, runs in every other test)."""
+    monkeypatch.setenv("CLJXLA_B200_GEMV_PROLOGUE", mode)
     cfg = TINY["gemma3"]
     B, S, T = 1, 6, 32
-    gd = d.build_graph(cfg, "decode", B, S, T, name="gemma3_decode_prologue")
+    gd = d.build_graph(cfg, "decode", B, S, T, name="gemma3_decode_prologue" + mode)
     td = shlo.graph_to_mlir_text(gd)
     rng = np.random.Generator(np.random.PCG64(4))
     kv = [interp.f32_to_bf16_bits(rng.standard_normal(d.cache_shape(cfg, B, T)).astype(np.float32))
