@@ -376,8 +376,9 @@ def run_ours(args, rank, world, local_rank):
         return cfg, B, S, T, None
 
     # ---------------- decode end to end through the PJRT C ABI, the way the
-    # host drives it: token and position uploaded from host memory, execute
-    # (awaited), the step's result read back, old caches destroyed.
+    # host drives it: token and position uploaded from host memory, execute,
+    # the step's result read back (which waits for the step), and the previous
+    # step's buffers destroyed while this step runs on the device.
     # Headline: the greedy graph (token ids read back, 4 bytes per sequence);
     # also the logits graph with the host argmax of scripts/gemma4_inference.clj.
     logits_bytes = B * cfg.vocab * 4
@@ -388,18 +389,22 @@ def run_ours(args, rank, world, local_rank):
         ex, g = (ex_greedy, g_greedy) if greedy else (ex_dec, g_dec)
         torch.cuda.synchronize()
         t_e0 = time.perf_counter()
+        prev = []
         for i in range(e2e_steps):
             xb = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
             pb = core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4)
-            outs = api.execute_executable(ex["handle"], [xb, pb] + wbufs + kv, len(g["outvars"]))
+            outs = api.execute_executable(ex["handle"], [xb, pb] + wbufs + kv, len(g["outvars"]), wait=False)
+            for b in prev:  # the previous step has completed (its result was read back)
+                api.destroy_buffer(b)
+            prev = [xb, pb, outs[0]] + kv
+            kv = outs[1:]
             if greedy:
                 tok = api.buffer_to_host(outs[0], 4 * B).view(np.int32).reshape(B, 1).copy()
             else:
                 logits = api.buffer_to_host_floats(outs[0], B * cfg.vocab).reshape(B, cfg.vocab)
                 tok = np.array([[d.argmax_host(logits[b])] for b in range(B)], np.int32)
-            for b in [xb, pb, outs[0]] + kv:
-                api.destroy_buffer(b)
-            kv = outs[1:]
+        for b in prev:
+            api.destroy_buffer(b)
         torch.cuda.synchronize()
         return time.perf_counter() - t_e0, kv
 

@@ -327,6 +327,9 @@ struct BodyOpts {
   int smem_out = -1;
   std::string sync = "__syncthreads()";  // barrier over the threads running the body
   std::vector<DusStore> dus;
+  // elementwise body over the element range [e0, e1) given as arguments (a GEMV
+  // epilogue) instead of a grid-stride share of every element
+  bool ranged = false;
 };
 
 // clamped start indices of each folded KV write (and, CTA 0, its undo header)
@@ -380,8 +383,8 @@ void emit_dus_stores(std::ostringstream& s, const BodyOpts& bo, int o, const std
 // The program of one elementwise launch as a device function over blocks
 // [0, nblk) (bid = this CTA's block in that range).
 void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& fname, const BodyOpts& bo) {
-  s << "__device__ __forceinline__ void " << fname
-    << "(const u64* __restrict__ argtab, const JitArgs& a, unsigned bid, unsigned nblk"
+  s << "__device__ __forceinline__ void " << fname << "(const u64* __restrict__ argtab, const JitArgs& a, "
+    << (bo.ranged ? "i64 e0, i64 e1" : "unsigned bid, unsigned nblk")
     << (bo.smem_out >= 0 ? ", char* __restrict__ xsb, bool gst" : "") << ") {\n";
   Emitter em{s, P.in, P.rank};
   for (int i = 0; i < P.nin; ++i) {
@@ -390,8 +393,11 @@ void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& f
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
   emit_dus_prelude(s, bo, "  ");
-  s << "  for (i64 e = (i64)bid * " << bo.block << " + threadIdx.x; e < " << P.n << "LL; e += (i64)nblk * "
-    << bo.block << ") {\n";
+  if (bo.ranged)
+    s << "  for (i64 e = e0 + threadIdx.x; e < e1; e += " << bo.block << ") {\n";
+  else
+    s << "  for (i64 e = (i64)bid * " << bo.block << " + threadIdx.x; e < " << P.n << "LL; e += (i64)nblk * "
+      << bo.block << ") {\n";
   for (int d = 0; d < P.rank; ++d) em.x.push_back("x" + std::to_string(d));
   if (P.rank == 1) {
     s << "    const i64 x0 = e;\n";
@@ -1038,6 +1044,16 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
     return e && e[0] == '0';
   }();
   if (off) return false;
+  // epilogue: an elementwise program over the GEMV's rows runs in each CTA once
+  // its rows are done; with two equal segments a CTA takes the same rows of
+  // both (gate and up of a GeGLU), so every element it computes is local
+  const bool epi = !l.epi.empty();
+  const bool paired = epi && G.nseg == 2;
+  const int64_t EF = paired ? G.seg_end[0] : G.N;  // rows per pass
+  const int NP = paired ? 2 : 1;
+  if (epi && (tail || G.M != 1 || G.nseg > 2 || (paired && G.seg_end[1] != 2 * G.seg_end[0]) ||
+              l.epi.size() != 1 || l.epi[0].kind != K_EW))
+    return false;
   if (G.M >= 2 && !fused && !tail &&
       (describe_gemv_mma(G, src, grid, block, smem, args) || describe_gemv_mma_chunked(G, src, grid, block, smem, args)))
     return true;
@@ -1180,19 +1196,36 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     }
     g_l2_loads = false;
   }
+  if (epi) {
+    s << "struct JitEpi { JitArgs g; JitArgs e; };\n";
+    BodyOpts bo;
+    bo.block = WARPS * 32;
+    bo.sync = "consumers_sync()";
+    bo.ranged = true;
+    emit_body(s, l.epi[0], WARPS * 32, 1, "epi_body", bo);
+  }
   s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
     << ", " << geo.ctas_per_sm << ") cljxla_fused_gemv(const u64* __restrict__ argtab, const "
-    << (tail ? "JitTail t) {\n  const JitArgs& a = t.g;\n" : "JitArgs a) {\n");
+    << (tail ? "JitTail t) {\n  const JitArgs& a = t.g;\n" : epi ? "JitEpi t) {\n  const JitArgs& a = t.g;\n" : "JitArgs a) {\n");
   s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
   s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
   s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
-  {
-    const int64_t max_rows = (N + ctas - 1) / ctas;
-    if (WPR > 1 && M == 1 && max_rows * WPR * 4 <= 16 * 1024)
-      s << "  __shared__ float rowpart[" << max_rows << "][" << WPR << "];\n";
-  }
+  // rows of one CTA: with an epilogue, NP passes of at most ceil(EF / ctas) rows
+  const int64_t max_rows = epi ? NP * ((EF + ctas - 1) / ctas) : (N + ctas - 1) / ctas;
+  const bool late_sum = WPR > 1 && M == 1 && max_rows * WPR * 4 <= 16 * 1024;
+  if (late_sum) s << "  __shared__ float rowpart[" << max_rows << "][" << WPR << "];\n";
   s << "  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;\n";
-  s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  if (epi)
+    s << "  const i64 pa = (i64)" << EF << "LL * blockIdx.x / gridDim.x, pb = (i64)" << EF
+      << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  else
+    s << "  const i64 r0 = (i64)" << N << "LL * blockIdx.x / gridDim.x, r1 = (i64)" << N << "LL * (blockIdx.x + 1) / gridDim.x;\n";
+  // with an epilogue the row loops run once per pass over [pa, pb) + pass * EF
+  const std::string pass_open = epi ? "  for (int pass = 0; pass < " + std::to_string(NP) +
+                                          " && !quit; ++pass) {\n  const i64 r0 = pa + pass * " + std::to_string(EF) +
+                                          "LL, r1 = pb + pass * " + std::to_string(EF) + "LL, rb = pass * (pb - pa);\n"
+                                    : "";
+  const std::string pass_close = epi ? "  }\n" : "";
   s << "  unsigned* status = (unsigned*)" << base_expr(kS) << ";\n";
   s << "  const u32 stage0 = sa(dsm), xsa = stage0 + " << (int64_t)NST * stage_stride << "u;\n";
   s << "  if (threadIdx.x == 0) {\n    for (int i = 0; i < " << NST << "; ++i) { mb_init(sa(&full_bar[i]), 1u); mb_init(sa(&empty_bar[i]), "
@@ -1201,6 +1234,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   // producer
   s << "  if (warp == " << WARPS << ") {\n    if (lane != 0) return;\n";
   s << "    int st = 0;\n    bool ok = true;\n";
+  if (epi) s << "    bool quit = false;\n" << pass_open;
   s << "    for (i64 r = r0; r < r1; ++st) {\n      const int slot = st % " << NST << ";\n";
   s << "      if (st >= " << NST << " && !mb_wait(sa(&empty_bar[slot]), (u32)((st / " << NST << " - 1) & 1))) { ok = false; break; }\n";
   s << "      const i64 e = stage_end(r, r1);\n";
@@ -1214,6 +1248,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "      mb_expect(sa(&full_bar[slot]), bytes);\n";
   s << "      bulk_g2s(stage0 + (u32)slot * " << stage_stride << "u, W + (r - lo) * " << K * 2 << "LL, bytes, sa(&full_bar[slot]));\n";
   s << "      r = e;\n    }\n";
+  if (epi) s << "    quit = !ok;\n" << pass_close;
   s << "    if (!ok) atomicOr(status, 4u);\n";
   // drain: the copies of the last stages issued have landed before the CTA may end
   s << "    for (int k = st - 1; k >= 0 && k >= st - " << NST << "; --k)\n";
@@ -1241,15 +1276,14 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     s << "    else for (int e = 0; e < 8; ++e) xr[i][e] = 0.f;\n  }\n";
   }
   s << "  int st = 0;\n";
+  if (epi) s << "  bool quit = false;\n" << pass_open;
   s << "  for (i64 r = r0; r < r1; ++st) {\n    const int slot = st % " << NST << ";\n";
   s << "    const i64 e = stage_end(r, r1);\n";
   s << "    bool bad = !mb_wait(sa(&full_bar[slot]), (u32)((st / " << NST << ") & 1));\n";
   // one row split over WPR warps: with M = 1 the parts of each of the CTA's rows
   // wait in shared memory and are summed once after the loop (no barrier per stage)
-  const int64_t max_rows = (N + ctas - 1) / ctas;
-  const bool late_sum = WPR > 1 && M == 1 && max_rows * WPR * 4 <= 16 * 1024;
   if (WPR > 1 && !late_sum) s << "    bad = consumers_any(bad);\n";
-  s << "    if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); break; }\n";
+  s << "    if (bad) { if (threadIdx.x == 0) atomicOr(status, 16u); " << (epi ? "quit = true; " : "") << "break; }\n";
   s << "    const i64 row = r + rr;\n    const bool active = row < e;\n";
   s << "    float acc[" << M << "];\n#pragma unroll\n    for (int m = 0; m < " << M << "; ++m) acc[m] = 0.f;\n";
   s << "    if (active) {\n";
@@ -1270,10 +1304,16 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   s << "#pragma unroll\n    for (int m = 0; m < " << M << "; ++m)\n";
   s << "      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);\n";
   if (late_sum) {
-    s << "    if (lane == 0 && active) rowpart[row - r0][part] = acc[0];\n    r = e;\n  }\n";
-    s << "  consumers_sync();\n";
-    s << "  for (i64 row = r0 + threadIdx.x; row < r1; row += " << WARPS * 32 << ") {\n";
-    s << "    float t = 0.f;\n    for (int q = 0; q < " << WPR << "; ++q) t += rowpart[row - r0][q];\n";
+    s << "    if (lane == 0 && active) rowpart[" << (epi ? "rb + " : "") << "row - r0][part] = acc[0];\n    r = e;\n  }\n";
+    s << pass_close << "  consumers_sync();\n";
+    if (epi) {  // the CTA's rows of every pass, v-th in pass order
+      s << "  for (i64 v = threadIdx.x; v < " << NP << " * (pb - pa); v += " << WARPS * 32 << ") {\n";
+      s << "    const i64 row = v < pb - pa ? pa + v : " << EF << "LL + pa + (v - (pb - pa));\n";
+      s << "    float t = 0.f;\n    for (int q = 0; q < " << WPR << "; ++q) t += rowpart[v][q];\n";
+    } else {
+      s << "  for (i64 row = r0 + threadIdx.x; row < r1; row += " << WARPS * 32 << ") {\n";
+      s << "    float t = 0.f;\n    for (int q = 0; q < " << WPR << "; ++q) t += rowpart[row - r0][q];\n";
+    }
     s << seg_chain("row", "    ");
     for (int i = 0; i < G.nseg; ++i) {
       const int64_t rows = G.seg_end[i] - (i ? G.seg_end[i - 1] : 0);
@@ -1281,7 +1321,11 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
         << store_stmt("Y", "row - lo", G.y_dt[i], "U(t)") << " }\n";
       (void)rows;
     }
-    s << "  }\n" << tail_code << "}\n";
+    s << "  }\n" << tail_code;
+    // the epilogue over this CTA's elements [pa, pb): its GEMV inputs were
+    // stored above by the CTA's own threads (ordered by the barrier)
+    if (epi) s << "  consumers_sync();\n  if (!quit) epi_body(argtab, t.e, pa, pb);\n";
+    s << "}\n";
     *src = s.str();
     *grid = ctas;
     *block = (WARPS + 1) * 32;
@@ -1301,7 +1345,9 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
     s << "      if (sg == " << i << ") { char* Y = " << base_expr(kY + i) << "; for (int m = 0; m < " << M << "; ++m) "
       << store_stmt("Y", "(i64)m * " + std::to_string(rows) + "LL + (row - lo)", G.y_dt[i], "U(acc[m])") << " }\n";
   }
-  s << "    }\n    r = e;\n  }\n" << tail_code << "}\n";
+  s << "    }\n    r = e;\n  }\n" << pass_close << tail_code;
+  if (epi) s << "  consumers_sync();\n  if (!quit) epi_body(argtab, t.e, pa, pb);\n";
+  s << "}\n";
   *src = s.str();
   *grid = ctas;
   *block = (WARPS + 1) * 32;
@@ -1332,6 +1378,13 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
     *cluster = 1;
     if (!describe_gemv_tma(l, src, grid, block, smem, &a)) return false;
     args->push_back(a);
+    for (const Launch& e : l.epi) {  // the epilogue program's buffers
+      int64_t g;
+      int b, c;
+      JitArgs ea;
+      if (!describe_one(e, &g, &b, &c, &ea)) return false;
+      args->push_back(ea);
+    }
     if (l.kind == K_GEMV_TAIL)
       for (const Launch& p : l.parts) {
         int64_t g;

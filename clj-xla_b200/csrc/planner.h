@@ -56,6 +56,10 @@ struct Launch {
   int jit_smem = 0;  // dynamic shared memory bytes
   std::vector<JitArgs> jit_args;  // one per program (several for K_MULTI)
   std::vector<Launch> parts;      // K_MULTI: the merged launches, in order
+  // K_GEMV / K_GEMV_FUSED: an elementwise program over the GEMV's rows that each
+  // CTA runs on its own rows once they are done (a GeGLU over paired gate / up
+  // segments); not compiled: it runs as its own launch after the GEMV
+  std::vector<Launch> epi;
 };
 
 struct TensorSpec {
@@ -124,6 +128,11 @@ std::unique_ptr<Plan> build_plan(const Graph& g, const PlanOptions& opt);
 // Re-levels the launch list by the memory each launch touches and merges
 // independent compiled fused kernels of one launch shape (schedule.cc).
 void schedule_and_merge(Plan& p);
+
+// Moves the elementwise program consuming a decode GEMV's rows element by
+// element (the GeGLU after the gate / up projection) into the GEMV as an
+// epilogue each CTA runs on its own rows (schedule.cc).
+void fuse_gemv_epilogues(Plan& p);
 
 // Appends the small compiled programs that directly follow a decode GEMV to it
 // as a tail its last CTA runs (K_GEMV_TAIL), removing their kernel boundaries

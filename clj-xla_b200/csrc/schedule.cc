@@ -160,6 +160,8 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
           if (!accesses(p, part, out)) return false;
         c.add(g.tail_ctr, 4, true);
       }
+      for (const Launch& e : l.epi)
+        if (!accesses(p, e, out)) return false;
       if (l.kind == K_GEMV_FUSED) {  // x is computed in shared memory by the producer's program
         if (l.parts.size() != 1 || !accesses(p, l.parts[0], out)) return false;
       } else {
@@ -417,6 +419,79 @@ void fuse_gemv_prologues(Plan& p, bool ew_only, bool rows_only) {
 
 }  // namespace
 
+void fuse_gemv_epilogues(Plan& p) {
+  const char* env = getenv("CLJXLA_B200_GEMV_EPILOGUE");
+  if (env && env[0] == '0') return;
+  std::vector<Launch>& L = p.launches;
+  for (size_t i = 0; i < L.size(); ++i) {
+    Launch& gl = L[i];
+    if ((gl.kind != K_GEMV && gl.kind != K_GEMV_FUSED) || !gl.epi.empty()) continue;
+    const GemvParams& G = *(const GemvParams*)gl.blob.data();
+    if (G.M != 1 || G.nseg > 2 || (G.nseg == 2 && G.seg_end[1] != 2 * G.seg_end[0])) continue;
+    const int64_t F = G.nseg == 2 ? G.seg_end[0] : G.N;
+    // the first later launch touching the GEMV's outputs
+    std::vector<Access> ya;
+    {
+      Collector c{p, ya};
+      for (int s = 0; s < G.nseg; ++s) c.add(G.y[s], F * (int64_t)dt_size((DT)G.y_dt[s]), true);
+    }
+    size_t k = i + 1;
+    std::vector<Access> ak;
+    for (; k < L.size(); ++k) {
+      ak.clear();
+      if (!accesses(p, L[k], ak)) break;
+      if (conflict(ak, ya)) break;
+    }
+    if (k >= L.size() || L[k].kind != K_EW) continue;
+    const EwParams& e = *(const EwParams*)L[k].blob.data();
+    if (e.n != F || e.nout < 1) continue;
+    // every input on a GEMV output reads it at the element's own index; nothing
+    // else the program touches overlaps the GEMV's outputs
+    int64_t dense[CLJXLA_MAXR];
+    {
+      int64_t st = 1;
+      for (int d = e.rank - 1; d >= 0; --d) {
+        dense[d] = st;
+        st *= e.dims[d];
+      }
+    }
+    bool ok = true;
+    std::vector<Access> rest;
+    Collector rc{p, rest};
+    for (int j = 0; j < e.nin && ok; ++j) {
+      const EwIn& in = e.in[j];
+      int seg = -1;
+      for (int s = 0; s < G.nseg; ++s)
+        if (in.p.slot == G.y[s].slot && in.p.off == G.y[s].off) seg = s;
+      if (seg < 0) {
+        int64_t hi = 0;
+        for (int d = 0; d < e.rank; ++d) hi += (e.dims[d] - 1) * in.stride[d];
+        rc.add(in.p, (hi + 1) * (int64_t)dt_size((DT)in.dt), false);
+        continue;
+      }
+      if (in.sel_dim >= 0 || in.dt != G.y_dt[seg]) ok = false;
+      for (int d = 0; d < e.rank && ok; ++d)
+        if (e.dims[d] > 1 && in.stride[d] != dense[d]) ok = false;
+    }
+    for (int o = 0; o < e.nout; ++o) rc.add(e.out[o].p, e.n * (int64_t)dt_size((DT)e.out[o].dt), true);
+    if (!ok || conflict(rest, ya)) continue;
+    // the program may run at the GEMV's place: no launch between touches what it does
+    std::vector<Access> ae;
+    if (!accesses(p, L[k], ae)) continue;
+    bool movable = true;
+    for (size_t m = i + 1; m < k && movable; ++m) {
+      std::vector<Access> a;
+      movable = accesses(p, L[m], a) && !conflict(ae, a);
+    }
+    if (!movable) continue;
+    gl.label += "+" + L[k].label;
+    gl.algo_bytes += L[k].algo_bytes;
+    gl.algo_flops += L[k].algo_flops;
+    gl.epi.push_back(std::move(L[k]));
+    L.erase(L.begin() + (long)k);
+  }
+}
+
 void fuse_gemv_tails(Plan& p) {
   // opt-in (CLJXLA_B200_GEMV_TAIL=1): on Gemma-3-4B decode the two single-row
   // norms per layer as tails took 2.55 ms / step against 2.50 ms as their own
@@ -431,7 +506,7 @@ void fuse_gemv_tails(Plan& p) {
   for (size_t i = 0; i < n;) {
     Launch& l = p.launches[i];
     GemvParams g;
-    if (l.kind != K_GEMV || l.blob.size() != sizeof(GemvParams)) {
+    if (l.kind != K_GEMV || l.blob.size() != sizeof(GemvParams) || !l.epi.empty()) {
       out.push_back(std::move(l));
       ++i;
       continue;

@@ -96,6 +96,15 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
       c.cur = &l;
       c.region(g.tail_ctr, 4, "tail arrival counter");
     }
+    if (!l.epi.empty()) {
+      const GemvParams& g = *(const GemvParams*)l.blob.data();
+      if ((l.kind != K_GEMV && l.kind != K_GEMV_FUSED) || l.epi.size() != 1 || l.epi[0].kind != K_EW || g.M != 1 ||
+          g.nseg > 2 || (g.nseg == 2 && g.seg_end[1] != 2 * g.seg_end[0]) ||
+          ((const EwParams*)l.epi[0].blob.data())->n != (g.nseg == 2 ? g.seg_end[0] : g.N))
+        fail(E_INTERNAL, "bad GEMV epilogue");
+      verify_launch(p, c, l.epi[0]);
+      c.cur = &l;
+    }
     if (l.kind == K_GEMV_FUSED) {
       if (l.parts.size() != 1 || (l.parts[0].kind != K_EW && l.parts[0].kind != K_ROWNORM))
         fail(E_INTERNAL, "bad GEMV prologue");

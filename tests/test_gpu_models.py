@@ -177,6 +177,35 @@ def test_every_fused_program_is_compiled(ctx, family):
         assert info["jit_missing"] == 0, (kind, info)
 
 
+@pytest.mark.parametrize("family", ["gemma2", "gemma3"])
+def test_gemv_epilogue_matches_oracle(ctx, monkeypatch, family):
+    """The GeGLU after the gate / up projection runs as the GEMV's epilogue
+    (each CTA computes the same rows of both segments, then the GeGLU of
+    those elements): at least one launch fewer per layer, and the decode step equals
+    the oracle's with the epilogue and without it."""
+    cfg = TINY[family]
+    B, S, T = 1, 6, 32
+    rng = np.random.Generator(np.random.PCG64(5))
+    kv = [interp.f32_to_bf16_bits(rng.standard_normal(d.cache_shape(cfg, B, T)).astype(np.float32))
+          for _ in range(2 * cfg.layers)]
+    launches = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("CLJXLA_B200_GEMV_EPILOGUE", mode)
+        gd = d.build_graph(cfg, "decode", B, S, T, name=f"{family}_decode_epilogue{mode}")
+        td = shlo.graph_to_mlir_text(gd)
+        inputs = [np.array([[5]], np.int32), d.pos_inputs(cfg, "decode", B, S, 1)] + d.make_weights(cfg) + kv
+        exe = core.compile_mlir_text(ctx, td, gd)
+        info = core.plan_info(ctx, exe)
+        assert info["jit_missing"] == 0, info
+        launches[mode] = info["launches"]
+        got = runner.run_graph(ctx, gd, inputs, td)
+        want = interp.run_mlir(td, inputs)
+        _compare_all(got, want, runner.out_specs(gd), f"{family} decode, GEMV epilogue {mode}", cfg.dtype,
+                     lambda sd: interp.run_mlir(td, inputs, ulp_noise_seed=sd))
+    # one per layer, plus the LM head's own elementwise consumer (softcap / convert)
+    assert launches["0"] - launches["1"] >= cfg.layers, launches
+
+
 @pytest.mark.parametrize("mode", ["1", "0"])
 def test_gemv_prologue_fusion_matches_oracle(ctx, monkeypatch, mode):
     """GEMV prologue fusion with every producer recomputed in each GEMV CTA
