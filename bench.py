@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--tiny", action="store_true", help="reduced model for quick checks (not a bench line)")
     p.add_argument("--decode-only", action="store_true",
                    help="only the decode steps (zero caches, no prefill / e2e / profile): for ncu launch lists")
+    p.add_argument("--profile", action="store_true",
+                   help="with --decode-only: also print per-kind device time of a profiled step")
     p.add_argument("--layers", type=int, default=0,
                    help="override the layer count (small ncu captures; not a bench line)")
     p.add_argument("--tp", type=int, default=1,
@@ -277,7 +279,8 @@ def run_ours(args, rank, world, local_rank):
     txt_dec, txt_pre = shlo.graph_to_mlir_text(g_dec), shlo.graph_to_mlir_text(g_pre)
     t1 = time.time()
     ex_dec = core.compile_mlir_text(ctx, txt_dec, g_dec)
-    ex_pre = core.compile_mlir_text(ctx, txt_pre, g_pre)
+    # (decode-only runs never execute the prefill graph, whose scratch can be large)
+    ex_pre = None if args.decode_only else core.compile_mlir_text(ctx, txt_pre, g_pre)
     # the same decode step with in-graph greedy sampling (tensor.clj:519-532):
     # what a user's generation loop runs, reading 4 bytes per sequence per step
     g_greedy = d.build_graph(cfg, "decode", B, S, T, greedy=True) if cfg.family != "gpt2" else None
@@ -296,7 +299,8 @@ def run_ours(args, rank, world, local_rank):
     # ---------------- prefill (dynamic-position prefill graph, one sequence batch)
     toks = d.make_prompt(cfg, B, S, seed=1 + rank)
     x_pre = core.buffer_from_host_buffer(ctx, toks, [B, S], 4)
-    p_pre = core.buffer_from_host_buffer(ctx, d.pos_inputs(cfg, "prefill", B, 0, S), [S], 4)
+    pos_pre = d.pos_inputs(cfg, "prefill", B, 0, S)
+    p_pre = core.buffer_from_host_buffer(ctx, pos_pre, list(pos_pre.shape), 4)
     pre_times = []
     kv = None
     if args.decode_only:
@@ -337,7 +341,11 @@ def run_ours(args, rank, world, local_rank):
     n_total = args.warmup + args.steps
     xs = [core.buffer_from_host_buffer(ctx, rng.integers(0, cfg.vocab, size=(B, 1), dtype=np.int64).astype(np.int32),
                                        [B, 1], 4) for _ in range(n_total)]
-    ps = [core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4) for i in range(n_total)]
+    def pos_buf(pos):  # the decode step's position invar ([1], or [B, 1] for GPT-2)
+        a = d.pos_inputs(cfg, "decode", B, pos, 1)
+        return core.buffer_from_host_buffer(ctx, a, list(a.shape), 4)
+
+    ps = [pos_buf(S + (i % (T - S))) for i in range(n_total)]
 
     def step(i, kv):
         outs = api.execute_executable(ex_dec["handle"], [xs[i], ps[i]] + wbufs + kv, len(g_dec["outvars"]), wait=False)
@@ -370,7 +378,23 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         torch.distributed.barrier()
     if args.decode_only:
-        print(json.dumps({"decode_only": True, "ms_per_step": dec_s / args.steps * 1e3, "launches": launches}))
+        line = {"decode_only": True, "ms_per_step": dec_s / args.steps * 1e3, "launches": launches}
+        if args.profile:  # per-kind device time of two steps with events around every launch
+            core.profile_enable(ctx, True)
+            for i in range(2):
+                kv = step(i % n_total, kv)
+            torch.cuda.synchronize()
+            agg = {}
+            for e in core.profile_dump(ctx):
+                a = agg.setdefault(e["kind"], [0.0, 0, 0])
+                a[0] += e["ms"] / 2
+                a[1] += e["bytes"] // 2
+                a[2] += e["calls"] // 2
+            core.profile_enable(ctx, False)
+            line["kernel_ms_per_step"] = {k: round(v[0], 4) for k, v in agg.items()}
+            line["gb_per_s"] = {k: round(v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in agg.items() if v[0] > 0}
+            line["launches_per_step"] = {k: v[2] for k, v in agg.items()}
+        print(json.dumps(line))
         for b in kv + xs + ps + wbufs + [x_pre, p_pre]:
             api.destroy_buffer(b)
         return cfg, B, S, T, None
@@ -392,7 +416,7 @@ def run_ours(args, rank, world, local_rank):
         prev = []
         for i in range(e2e_steps):
             xb = core.buffer_from_host_buffer(ctx, tok, [B, 1], 4)
-            pb = core.buffer_from_host_buffer(ctx, np.array([S + (i % (T - S))], np.int32), [1], 4)
+            pb = pos_buf(S + (i % (T - S)))
             outs = api.execute_executable(ex["handle"], [xb, pb] + wbufs + kv, len(g["outvars"]), wait=False)
             for b in prev:  # the previous step has completed (its result was read back)
                 api.destroy_buffer(b)
@@ -472,7 +496,7 @@ def cpu_baseline(cfg, B, S, T, txt_dec, host_w, steps):
     x = np.zeros((B, 1), np.int32)
     t0 = time.perf_counter()
     for i in range(max(1, steps)):
-        it.run([x, np.array([S + i], np.int32)] + wf + kv)
+        it.run([x, d.pos_inputs(cfg, "decode", B, S + i, 1)] + wf + kv)
     dt = (time.perf_counter() - t0) / max(1, steps)
     return {"value": B / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{max(1, steps)} decode step(s) of the same graph at position {S}, numpy oracle "
@@ -595,10 +619,10 @@ def run_reference(args, rank, world):
     kv = [np.zeros(d.cache_shape(cfg, B, T), np.float32) for _ in range(2 * cfg.layers)]
     x = np.zeros((B, 1), np.int32)
     for i in range(args.warmup):
-        it.run([x, np.array([S + i], np.int32)] + wf + kv)
+        it.run([x, d.pos_inputs(cfg, "decode", B, S + i, 1)] + wf + kv)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        outs = it.run([x, np.array([S + i], np.int32)] + wf + kv)
+        outs = it.run([x, d.pos_inputs(cfg, "decode", B, S + i, 1)] + wf + kv)
         kv = outs[1:]
     dt = time.perf_counter() - t0
     v = B * args.steps / dt

@@ -63,7 +63,20 @@ struct TcGemmParams {
   // (hi, mid, lo; plane p holds rows p * a_plane_rows ..), each multiplied by
   // the same B tile into one accumulator; a_parts 1: A is bf16
   int32_t a_parts, a_plane_rows;
+  // tile width along N (256, or 64 for few rows of A: batched decode), rows of
+  // A per copy (a multiple of 8, at most 128: only the rows a short A has), and
+  // the K splits: with ksplit > 1 each (N tile, K split) unit stores its f32
+  // partial tile in `part` ([ksplit][M][N]) and the last unit of an N tile to
+  // arrive (counters: one per N tile, zero between launches) sums them in
+  // split order, rounds and stores C
+  int32_t bn, a_box, ksplit;
+  // B is a graph parameter no launch writes (a weight): its first stages are
+  // copied before the dependency wait
+  int32_t b_const;
+  DPtr part, counters;
 };
+// tile width and K splits for an M x N x K product on `sms` SMs
+void tc_gemm_choose(int64_t M, int64_t N, int64_t K, int sms, int* bn, int* a_box, int* ksplit);
 
 void launch_tc_gemm(const TcGemmParams& p, const uint64_t* argtab, cudaStream_t s);
 bool make_tc_gemm(const GemmParams& g, TcGemmParams& out);

@@ -248,6 +248,26 @@ class Planner {
   void emit_node_kernel(int n);
   GemmParams dot_params(int id, int oslot, int64_t* bytes, int64_t* flops);
   bool emit_split_dot(int id, int oslot);
+  // tile width, A rows per copy and K splits of a tensor-core GEMM (narrow
+  // tiles and split K for a few rows of A), with the tensor-map boxes and the
+  // split-K partials / counters they need
+  void tc_tiling(TcGemmParams& tc, TmapSpec& ta, TmapSpec& tb) {
+    int bn = 256, ab = 128, ks = 1;
+    if (!getenv_off("CLJXLA_B200_TC_NARROW"))
+      tc_gemm_choose(tc.M, tc.N, (int64_t)tc.K * tc.a_parts, 148, &bn, &ab, &ks);
+    tc.bn = bn;
+    tc.a_box = ab;
+    tc.ksplit = ks;
+    ta.box_outer = ab;
+    tb.box_outer = bn;
+    if (ks > 1) {
+      tc.part = slot_ptr(new_tmp((int64_t)ks * tc.M * tc.N * 4));
+      const int64_t tiles = ((tc.M + 127) / 128) * ((tc.N + bn - 1) / bn);
+      const size_t off = (plan_.const_blob.size() + 15) & ~size_t(15);
+      plan_.const_blob.resize(off + 4 * tiles, 0);
+      tc.counters = slot_ptr(P_ + O_ + U_, (int64_t)off);
+    }
+  }
   std::set<int> pre_emitted_;  // units already emitted together with an earlier one (grouped GEMVs)
   std::set<int> emitted_units_;
   void build_row_regions();
@@ -1847,6 +1867,7 @@ void Planner::emit_node_kernel(int id) {
         tb.row_bytes = G.b_sn * 2;
         tb.box_inner = bk;
         tb.box_outer = bn;
+        tc_tiling(tc, ta, tb);
         tc.tmap_a_index = (int32_t)plan_.tmaps.size();
         plan_.tmaps.push_back(ta);
         tc.tmap_b_index = (int32_t)plan_.tmaps.size();
@@ -1987,6 +2008,7 @@ bool Planner::emit_split_dot(int id, int oslot) {
   tb.row_bytes = sn * 2;
   tb.box_inner = bk;
   tb.box_outer = bn;
+  tc_tiling(tc, ta, tb);
   tc.tmap_a_index = (int32_t)plan_.tmaps.size();
   plan_.tmaps.push_back(ta);
   tc.tmap_b_index = (int32_t)plan_.tmaps.size();
@@ -2359,6 +2381,15 @@ void Planner::run() {
   for (Launch& l : plan_.launches) {
     if (l.kind != K_GEMM_TC) continue;
     TcGemmParams& t = *(TcGemmParams*)l.blob.data();
+    // B copied before the dependency wait (CLJXLA_B200_TC_EARLY_B=1): a
+    // parameter (a weight) that no launch writes (in-place KV updates write
+    // their parameters).  Off by default: measured slower (Gemma-2-2B batch-32
+    // decode 4.29 against 4.17 ms per step, Gemma-3-4B prefill 44.8 against
+    // 44.2 ms), the early copies competing with the predecessor's traffic.
+    const char* eb = getenv("CLJXLA_B200_TC_EARLY_B");
+    t.b_const = eb && eb[0] == '1' && t.b.slot >= 0 && t.b.slot < (int)plan_.params.size() ? 1 : 0;
+    for (const InplaceDus& ip : plan_.inplace)
+      if (ip.param == t.b.slot) t.b_const = 0;
     const int slot = plan_.tmap_slot();
     t.tmap_a = DPtr{slot, 0, 128LL * t.tmap_a_index};
     t.tmap_b = DPtr{slot, 0, 128LL * t.tmap_b_index};

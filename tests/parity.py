@@ -45,15 +45,20 @@ def close_model_floor(got, want, floors, dt, margin=2.0):
     summation order).  Whole bf16 models with scale-1.0 QK-normed attention
     amplify such few-ulp differences into visible logit changes (a flipped bf16
     score rounding moves a softmax weight by tens of percent), so the device
-    result passes when it is no further from the oracle than ``margin`` times
-    the oracle's own spread.  Returns (ok, bad_fraction, rel_rms, floor_bad, floor_rr)."""
+    result passes when its relative RMS error is at most ``margin`` times the
+    oracle's own spread, with the fraction of elements outside the per-element
+    bound at most 1.5 ``margin`` times the oracle's (the fraction counts every
+    flipped rounding equally and is the noisier of the two; tensor-core
+    accumulation, which drops low bits of the f32 sum, moves it more than an
+    exact f32 sum in another order does).
+    Returns (ok, bad_fraction, rel_rms, floor_bad, floor_rr)."""
     ok, bad, rr = close_model(got, want, dt)
     fb = fr = 0.0
     for f in floors:
         _, b2, r2 = close_model(f, want, dt)
         fb, fr = max(fb, b2), max(fr, r2)
     if not ok and not np.isnan(as_f32(np.asarray(got), dt)).any():
-        ok = bad <= max(1e-3, margin * fb) and rr <= max(1e-2, margin * fr)
+        ok = rr <= max(1e-2, margin * fr) and bad <= max(1e-3, 1.5 * margin * fb)
     return ok, bad, rr, fb, fr
 
 

@@ -2,8 +2,8 @@
 
 Gemma's linear layer is dot_general(x[.., K], W[N, K]) contracting the
 weight's last dim when N != K (gemma.clj:8-23), bf16 operands; the planner
-sends M >= 16 of them to the tcgen05
-kernel.  Each case checks that the kernel actually ran (profile entries of kind
+sends the ones with more than 8 rows to the tcgen05 kernel (128 x 256 tiles,
+or 64-wide weight tiles with K split over CTAs for at most 128 rows).  Each case checks that the kernel actually ran (profile entries of kind
 gemm_tc) and compares with the numpy oracle at the bf16 tolerance; ragged M / N
 / K exercise the TMA zero-filled tile edges and the guarded epilogue.
 """
@@ -53,6 +53,11 @@ def _run_profiled(ctx, g, inputs, text):
     (17, 64, 40),        # smaller than a tile
     (512, 2560, 1024),   # Gemma-3-4B k/v projection shape, four M tiles
     (256, 1024, 2304),   # N spans nine 256-wide tiles
+    # a few rows (batched decode): 64-wide weight tiles, K split over CTAs
+    (32, 2304, 2048),    # Gemma-2-2B batch-32 q projection: 32 tiles x 4 K splits
+    (9, 2304, 1000),     # 9 rows (A copies of 16 rows), ragged N inside a 64-wide tile
+    (16, 5376, 512),     # Gemma-3-27B TP8 shard: 8 tiles x 18 K splits
+    (100, 704, 2560),    # more than 64 rows: 256-wide tiles, 10 tiles x 2 K splits
 ])
 def test_linear_layer_on_tensor_cores(ctx, S, K, N):
     g = t.trace_graph("tc_linear", [("x", ("tensor", (1, S, K), "bf16")), ("w", ("tensor", (N, K), "bf16"))],
@@ -110,6 +115,8 @@ def _f32(shape, seed, scale=1.0):
     (128, 256, 192),
     (200, 320, 300),     # ragged M / N: plane tiles read into the next plane's rows
     (512, 2048, 640),
+    (32, 2048, 2304),    # a few rows: 64-wide tiles, K blocks of the three planes split over CTAs
+    (20, 512, 300),
 ])
 def test_f32_activation_times_bf16_weight_on_tensor_cores(ctx, S, K, N):
     """f32 x bf16 -> f32 (the attention-output projection of a Gemma prefill,
