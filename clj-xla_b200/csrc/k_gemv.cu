@@ -220,7 +220,12 @@ int choose_warps_per_row(int64_t N, int64_t K) {
 
 bool gemv_shape_ok(const GemmParams& g) {
   // decode shapes only: one batch, few rows, bf16 weights laid out [N, K]
-  if (g.batch != 1 || g.M < 1 || g.M > 8 || g.b_dt != KDT_BF16) return false;
+  // CLJXLA_B200_GEMV_MAX_ROWS (default 8): more rows take the tensor-core GEMM
+  static const int max_rows = [] {
+    const char* e = getenv("CLJXLA_B200_GEMV_MAX_ROWS");
+    return e && atoi(e) >= 1 ? std::min(8, atoi(e)) : 8;
+  }();
+  if (g.batch != 1 || g.M < 1 || g.M > max_rows || g.b_dt != KDT_BF16) return false;
   if (!(g.a_dt == KDT_BF16 || g.a_dt == KDT_F32) || !(g.c_dt == KDT_BF16 || g.c_dt == KDT_F32)) return false;
   if (g.b_sk != 1 || g.b_sn != g.K || g.a_sk != 1) return false;
   if (g.K % 8 != 0 || g.K < 256) return false;

@@ -55,6 +55,9 @@ __global__ void __launch_bounds__(P2P_THREADS) p2p_allreduce_kernel(const char* 
                                                                     unsigned* err, uint32_t wait_polls) {
   __shared__ unsigned s_ep;
   __shared__ int s_ok;
+  // launched as a programmatic dependent: resident before the producer of src
+  // ends, and the launch after it may become resident early in turn
+  pdl_enter();
   if (threadIdx.x == 0) {
     s_ep = *epoch + 1u;
     s_ok = 1;
@@ -183,9 +186,8 @@ bool P2PAllReduce::fits(int64_t count, int dt) const {
 
 void P2PAllReduce::run(const void* src, void* dst, int64_t count, int dt, cudaStream_t s) {
   if (((uintptr_t)src | (uintptr_t)dst) & 15) fail(E_INTERNAL, "one-shot all-reduce operands not 16-byte aligned");
-  p2p_allreduce_kernel<<<1, P2P_THREADS, 0, s>>>((const char*)src, (char*)dst, count, dt, d_peers, rank, ranks,
-                                                 slot_bytes, d_epoch, d_err, wait_polls);
-  CUDA_OK(cudaGetLastError());
+  launch_k(p2p_allreduce_kernel, dim3(1), dim3(P2P_THREADS), 0, s, 1, (const char*)src, (char*)dst, count, dt,
+           (const uint64_t*)d_peers, rank, ranks, slot_bytes, d_epoch, d_err, wait_polls);
 }
 
 void P2PAllReduce::check() const {
