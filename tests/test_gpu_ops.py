@@ -138,6 +138,18 @@ def test_dot_general_forms(ctx, dt):
                          rand((1, 4, 3, 32), dt, 10, 0.5), rand((1, 4, 9, 32), dt, 11, 0.5)])
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 768, 2304), (1, 768, 3072), (1, 3072, 768), (3, 768, 1000), (8, 256, 520)])
+def test_few_row_f32_products(ctx, M, K, N):
+    """f32 x [M, K] against f32 weights in both layouts GPT-2 decode uses:
+    [K, N] (Conv1D, N contiguous) and transpose([N, K]) (the tied LM head),
+    on the few-row kernels that stream each weight once."""
+    def f(x, w, v):
+        return [t.matmul(x, w), t.matmul(x, t.transpose(v, [1, 0]))]
+    g = t.trace_graph("f32rows", [("x", ("tensor", (M, K), "f32")), ("w", ("tensor", (K, N), "f32")),
+                                  ("v", ("tensor", (N, K), "f32"))], f)
+    check_graph(ctx, g, [rand((M, K), "f32", 21, 0.5), rand((K, N), "f32", 22, 0.05), rand((N, K), "f32", 23, 0.05)])
+
+
 def test_gather_rows_and_clamp(ctx):
     def f(tab, ids):
         return t.gather(tab, ids)
