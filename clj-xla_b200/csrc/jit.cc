@@ -392,6 +392,7 @@ void emit_ew_body(std::ostringstream& s, const EwParams& P, const std::string& f
     s << "  const char* in" << i << " = " << base_expr(i) << ";\n";
   }
   for (int o = 0; o < P.nout; ++o) s << "  char* out" << o << " = " << base_expr(P.nin + o) << ";\n";
+  if (bo.ranged) s << "  const unsigned bid = e0 == 0 ? 0u : 1u;  // (the range holding element 0 writes undo headers)\n";
   emit_dus_prelude(s, bo, "  ");
   if (bo.ranged)
     s << "  for (i64 e = e0 + threadIdx.x; e < e1; e += " << bo.block << ") {\n";
@@ -1410,17 +1411,44 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
       grids.push_back(g);
       args->push_back(a);
     }
+    // a row program's epilogue (an elementwise program over the elements of
+    // its rows, schedule.cc fuse_row_epilogues): its buffers follow the parts'
+    std::vector<int> epi_arg(l.parts.size(), -1);
+    for (size_t i = 0; i < l.parts.size(); ++i) {
+      if (l.parts[i].epi.empty()) continue;
+      if (*cluster != 1 || l.parts[i].kind != K_ROWNORM || grids[i] != ((const RowParams*)l.parts[i].blob.data())->rows)
+        return false;
+      int64_t g;
+      int b, c;
+      JitArgs ea;
+      if (!describe_one(l.parts[i].epi[0], &g, &b, &c, &ea)) return false;
+      epi_arg[i] = (int)args->size();
+      args->push_back(ea);
+    }
     std::ostringstream s;
     s << kPrelude << args_struct();
-    s << "struct JitMulti { JitArgs p[" << l.parts.size() << "]; };\n";
-    for (size_t i = 0; i < l.parts.size(); ++i) emit_body(s, l.parts[i], *block, *cluster, "part" + std::to_string(i));
+    s << "struct JitMulti { JitArgs p[" << args->size() << "]; };\n";
+    for (size_t i = 0; i < l.parts.size(); ++i) {
+      emit_body(s, l.parts[i], *block, *cluster, "part" + std::to_string(i));
+      if (epi_arg[i] >= 0) {
+        BodyOpts bo;
+        bo.block = *block;
+        bo.ranged = true;
+        emit_body(s, l.parts[i].epi[0], *block, 1, "epi" + std::to_string(i), bo);
+      }
+    }
     s << "extern \"C\" __global__ void __launch_bounds__(" << *block
       << ") cljxla_fused_multi(const u64* __restrict__ argtab, const JitMulti a) {\n  pdl_enter();\n"
          "  unsigned b = blockIdx.x;\n";
     int64_t total = 0;
     for (size_t i = 0; i < grids.size(); ++i) {
-      s << "  if (b < " << grids[i] << "u) { part" << i << "(argtab, a.p[" << i << "], b, " << grids[i]
-        << "u); return; }\n  b -= " << grids[i] << "u;\n";
+      s << "  if (b < " << grids[i] << "u) {\n    part" << i << "(argtab, a.p[" << i << "], b, " << grids[i] << "u);\n";
+      if (epi_arg[i] >= 0) {  // this CTA's row(s), now in memory, through the epilogue
+        const int64_t C = ((const RowParams*)l.parts[i].blob.data())->C;
+        s << "    __syncthreads();\n    epi" << i << "(argtab, a.p[" << epi_arg[i] << "], (i64)b * " << C << "LL, (i64)(b + 1) * "
+          << C << "LL);\n";
+      }
+      s << "    return;\n  }\n  b -= " << grids[i] << "u;\n";
       total += grids[i];
     }
     s << "}\n";

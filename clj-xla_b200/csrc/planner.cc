@@ -2415,6 +2415,7 @@ void Planner::run() {
     schedule_and_merge(plan_);
     if (opt_.fast_kernels) {
       fuse_gemv_epilogues(plan_);
+      fuse_row_epilogues(plan_);
       link_gemv_prefetch(plan_);
       link_attention_hints(plan_);
       fuse_gemv_tails(plan_);

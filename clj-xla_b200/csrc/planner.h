@@ -134,6 +134,11 @@ void schedule_and_merge(Plan& p);
 // epilogue each CTA runs on its own rows (schedule.cc).
 void fuse_gemv_epilogues(Plan& p);
 
+// Moves an elementwise program that reads a row program's outputs only within
+// each element's own row (RoPE after the per-head norms) into the row program's
+// launch, run by the CTA of each row right after the row (schedule.cc).
+void fuse_row_epilogues(Plan& p);
+
 // Appends the small compiled programs that directly follow a decode GEMV to it
 // as a tail its last CTA runs (K_GEMV_TAIL), removing their kernel boundaries
 // (schedule.cc).

@@ -98,6 +98,8 @@ struct Collector {
 bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
   Collector c{p, out};
   const void* b = l.blob.data();
+  for (const Launch& e : l.epi)  // an epilogue program runs inside the launch
+    if (!accesses(p, e, out)) return false;
   if (l.kind == K_FUSED_DUS) {
     for (const Launch& part : l.parts)
       if (!accesses(p, part, out)) return false;
@@ -160,8 +162,6 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
           if (!accesses(p, part, out)) return false;
         c.add(g.tail_ctr, 4, true);
       }
-      for (const Launch& e : l.epi)
-        if (!accesses(p, e, out)) return false;
       if (l.kind == K_GEMV_FUSED) {  // x is computed in shared memory by the producer's program
         if (l.parts.size() != 1 || !accesses(p, l.parts[0], out)) return false;
       } else {
@@ -495,6 +495,136 @@ void fuse_gemv_epilogues(Plan& p) {
     gl.algo_flops += L[k].algo_flops;
     gl.epi.push_back(std::move(L[k]));
     L.erase(L.begin() + (long)k);
+  }
+}
+
+namespace {
+
+// The elementwise program `e` reads the outputs of row program `r` only
+// within the row of each element it computes (element i of e belongs to row
+// i / C of r): dense leading dims, the last dim within one row (a slice or a
+// concatenate operand of it, as RoPE's rotate_half reads it).  It reads no
+// other output of `others`.
+bool row_local(const Plan& p, const RowParams& r, const EwParams& e, const std::vector<const Launch*>& others) {
+  if (e.n != r.rows * r.C || e.rank < 1 || e.dims[e.rank - 1] != r.C) return false;
+  int64_t dense[CLJXLA_MAXR];
+  {
+    int64_t st = 1;
+    for (int d = e.rank - 1; d >= 0; --d) {
+      dense[d] = st;
+      st *= e.dims[d];
+    }
+  }
+  std::vector<Access> other_w;
+  {
+    for (const Launch* o : others) {
+      std::vector<Access> a;
+      if (!accesses(p, *o, a)) return false;
+      for (const Access& x : a)
+        if (x.write) other_w.push_back(x);
+    }
+  }
+  for (int j = 0; j < e.nin; ++j) {
+    const EwIn& in = e.in[j];
+    int out = -1;
+    int64_t base = 0;
+    for (int o = 0; o < r.nout; ++o) {
+      if (r.out[o].scalar || r.out[o].p.slot != in.p.slot || in.p.slot < 0) continue;
+      const int64_t es = (int64_t)dt_size((DT)r.out[o].dt);
+      const int64_t d = in.p.off - r.out[o].p.off;
+      if (d >= 0 && d < r.rows * r.C * es && d % es == 0 && in.dt == r.out[o].dt) {
+        out = o;
+        base = d / es;
+      }
+    }
+    std::vector<Access> ia;
+    {
+      Collector ic{p, ia};
+      int64_t hi = 0;
+      for (int d = 0; d < e.rank; ++d) hi += (e.dims[d] - 1) * in.stride[d];
+      ic.add(in.p, (hi + 1) * (int64_t)dt_size((DT)in.dt), false);
+    }
+    if (conflict(ia, other_w)) return false;
+    if (out < 0) {  // not an output of r: must not be one either (another slot, or outside r's outputs)
+      std::vector<Access> rw;
+      Collector rc{p, rw};
+      for (int o = 0; o < r.nout; ++o)
+        if (!r.out[o].scalar) rc.add(r.out[o].p, r.rows * r.C * (int64_t)dt_size((DT)r.out[o].dt), true);
+      if (conflict(ia, rw)) return false;
+      continue;
+    }
+    if (base >= r.C) return false;  // the view starts in the first row
+    for (int d = 0; d + 1 < e.rank; ++d)
+      if (e.dims[d] > 1 && in.stride[d] != dense[d]) return false;
+    if (in.stride[e.rank - 1] != 1) return false;
+    const int64_t len = in.sel_dim == e.rank - 1 ? in.sel_hi - in.sel_lo : e.dims[e.rank - 1];
+    if (in.sel_dim >= 0 && in.sel_dim != e.rank - 1) return false;
+    if (base + len > r.C) return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+void fuse_row_epilogues(Plan& p) {
+  const char* env = getenv("CLJXLA_B200_ROW_EPILOGUE");
+  if (env && env[0] == '0') return;
+  std::vector<Launch>& L = p.launches;
+  for (size_t i = 0; i + 1 < L.size(); ++i) {
+    if (L[i].kind != K_MULTI) continue;
+    Launch& nx = L[i + 1];
+    // the next launch's programs, one at a time
+    std::vector<Launch> next;
+    if (nx.kind == K_MULTI) next = nx.parts;
+    else if (nx.kind == K_EW || nx.kind == K_FUSED_DUS) next.push_back(nx);
+    else continue;
+    std::vector<Launch> keep;
+    bool moved = false;
+    for (Launch& q : next) {
+      const Launch& qb = q.kind == K_FUSED_DUS ? q.parts[0] : q;
+      bool done = false;
+      if (qb.kind == K_EW) {
+        const EwParams& e = *(const EwParams*)qb.blob.data();
+        for (size_t k = 0; k < L[i].parts.size() && !done; ++k) {
+          Launch& rp = L[i].parts[k];
+          if (rp.kind != K_ROWNORM || !rp.epi.empty()) continue;
+          const RowParams& r = *(const RowParams*)rp.blob.data();
+          int blk, cl;
+          int64_t grid;
+          row_launch_shape(r, &blk, &cl, &grid);
+          if (cl != 1 || grid != r.rows) continue;
+          std::vector<const Launch*> others;
+          for (size_t o = 0; o < L[i].parts.size(); ++o)
+            if (o != k) others.push_back(&L[i].parts[o]);
+          if (!row_local(p, r, e, others)) continue;
+          // what the program writes is touched by no other part of the launch
+          std::vector<Access> qa, oa;
+          if (!accesses(p, q, qa)) continue;
+          bool clash = false;
+          for (const Launch* o : others) {
+            oa.clear();
+            if (!accesses(p, *o, oa) || conflict(qa, oa)) clash = true;
+          }
+          if (clash) continue;
+          L[i].algo_bytes += q.algo_bytes;
+          L[i].label += "+" + q.label;
+          rp.label += "+" + q.label;
+          rp.epi.push_back(q);
+          done = moved = true;
+        }
+      }
+      if (!done) keep.push_back(std::move(q));
+    }
+    if (!moved) continue;
+    if (keep.empty()) {
+      L.erase(L.begin() + (long)(i + 1));
+    } else if (nx.kind == K_MULTI) {
+      if (keep.size() == 1) {
+        nx = std::move(keep[0]);
+      } else {
+        nx.parts = std::move(keep);
+      }
+    }
   }
 }
 

@@ -96,7 +96,15 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
       c.cur = &l;
       c.region(g.tail_ctr, 4, "tail arrival counter");
     }
-    if (!l.epi.empty()) {
+    if (!l.epi.empty() && l.kind == K_ROWNORM) {  // row program with an elementwise epilogue over its rows
+      const Launch& e = l.epi[0];
+      const Launch& eb = e.kind == K_FUSED_DUS ? e.parts[0] : e;
+      if (l.epi.size() != 1 || eb.kind != K_EW ||
+          ((const EwParams*)eb.blob.data())->n != ((const RowParams*)l.blob.data())->rows * ((const RowParams*)l.blob.data())->C)
+        fail(E_INTERNAL, "bad row epilogue");
+      verify_launch(p, c, e);
+      c.cur = &l;
+    } else if (!l.epi.empty()) {
       const GemvParams& g = *(const GemvParams*)l.blob.data();
       if ((l.kind != K_GEMV && l.kind != K_GEMV_FUSED) || l.epi.size() != 1 || l.epi[0].kind != K_EW || g.M != 1 ||
           g.nseg > 2 || (g.nseg == 2 && g.seg_end[1] != 2 * g.seg_end[0]) ||

@@ -181,8 +181,9 @@ def test_every_fused_program_is_compiled(ctx, family):
 def test_gemv_epilogue_matches_oracle(ctx, monkeypatch, family):
     """The GeGLU after the gate / up projection runs as the GEMV's epilogue
     (each CTA computes the same rows of both segments, then the GeGLU of
-    those elements): at least one launch fewer per layer, and the decode step equals
-    the oracle's with the epilogue and without it."""
+    those elements), and Gemma-3's RoPE runs in the CTAs of its per-head norms
+    (each row's elements right after the row): fewer launches per layer, and
+    the decode step equals the oracle's with these epilogues and without them."""
     cfg = TINY[family]
     B, S, T = 1, 6, 32
     rng = np.random.Generator(np.random.PCG64(5))
@@ -191,6 +192,7 @@ def test_gemv_epilogue_matches_oracle(ctx, monkeypatch, family):
     launches = {}
     for mode in ("1", "0"):
         monkeypatch.setenv("CLJXLA_B200_GEMV_EPILOGUE", mode)
+        monkeypatch.setenv("CLJXLA_B200_ROW_EPILOGUE", mode)
         gd = d.build_graph(cfg, "decode", B, S, T, name=f"{family}_decode_epilogue{mode}")
         td = shlo.graph_to_mlir_text(gd)
         inputs = [np.array([[5]], np.int32), d.pos_inputs(cfg, "decode", B, S, 1)] + d.make_weights(cfg) + kv
@@ -202,8 +204,10 @@ def test_gemv_epilogue_matches_oracle(ctx, monkeypatch, family):
         want = interp.run_mlir(td, inputs)
         _compare_all(got, want, runner.out_specs(gd), f"{family} decode, GEMV epilogue {mode}", cfg.dtype,
                      lambda sd: interp.run_mlir(td, inputs, ulp_noise_seed=sd))
-    # one per layer, plus the LM head's own elementwise consumer (softcap / convert)
-    assert launches["0"] - launches["1"] >= cfg.layers, launches
+    # per layer the GeGLU, and for Gemma-3 the RoPE launch (its programs run in
+    # the CTAs of the per-head norms), plus the LM head's elementwise consumer
+    per_layer = 2 if family == "gemma3" else 1
+    assert launches["0"] - launches["1"] >= per_layer * cfg.layers, launches
 
 
 @pytest.mark.parametrize("mode", ["1", "0"])
