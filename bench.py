@@ -477,6 +477,25 @@ def run_ours(args, rank, world, local_rank):
     return cfg, B, S, T, res
 
 
+# DRAM traffic per launch of the dominant kernel class, from one ncu capture
+# of the same kernels (dram__bytes_read.sum + dram__bytes_write.sum; the
+# command and per-launch table are in profiles/gemv_bulk_copy_gemma3-4b_decode.md)
+NCU_TRAFFIC = {
+    ("gemma3-4b decode, batch 1, prompt 2048, KV cache 2560 positions", "gemv_fused"): 63128992,
+}
+
+
+def ncu_traffic(workload, kind, dk):
+    """The roofline's `traffic` (bytes per launch, from the ncu capture) beside
+    the algorithmic bytes per launch it compares with; null for a workload or
+    kernel class without a capture."""
+    t = NCU_TRAFFIC.get((workload, kind))
+    algo = dk["bytes"] / dk["calls"] if dk.get("calls") else None
+    return {"traffic": t, "algorithmic_bytes_per_launch": round(algo) if algo else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean per launch"
+                              if t else None}
+
+
 def cpu_baseline(cfg, B, S, T, txt_dec, host_w, steps):
     """Times the numpy oracle on the same decode graph (all host threads)."""
     try:
@@ -533,6 +552,8 @@ def main():
         replicas = world // max(1, args.tp)
         value = replicas * res["tokens"] / dec_s
         dk = res["by_kind"][res["dom"]]
+        wl = (f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions"
+              + (" [tiny]" if args.tiny else "") + (f" [{args.layers} layers]" if args.layers else ""))
         line = {
             "metric": "decode tokens/s (greedy KV-cached decode step, whole job)",
             "value": round(value, 2),
@@ -546,9 +567,7 @@ def main():
             "vs_baseline": None,
             "dtype": cfg.dtype,
             "data": "synthetic (random-init weights N(0,0.02), random token ids)",
-            "config": {"workload": f"{args.config} decode, batch {B}, prompt {S}, KV cache {T} positions"
-                                   + (" [tiny]" if args.tiny else "")
-                                   + (f" [{args.layers} layers]" if args.layers else ""),
+            "config": {"workload": wl,
                        "model": args.config, "global_batch": B * replicas, "seq_len": S, "kv_len": T,
                        "parallelism": (f"dp{world} (independent replicas)" if args.tp == 1 else
                                        f"tp{args.tp}" + (f" x dp{replicas}" if replicas > 1 else "")
@@ -570,7 +589,8 @@ def main():
                      "path": "PJRT C ABI (BufferFromHostBuffer, Execute, ToHostBuffer) + host argmax"}),
             "roofline": {"bound": "hbm", "kernel": res["dom"],
                          "achieved": round(res["achieved"], 1), "peak": res["hbm_peak"], "unit": "GB/s",
-                         "frac": round(res["achieved"] / res["hbm_peak"], 4), "traffic": None,
+                         "frac": round(res["achieved"] / res["hbm_peak"], 4),
+                         **ncu_traffic(wl, res["dom"], dk),
                          "peak_source": res["peak_src"],
                          "share_of_step": round(dk["ms"] / res["total_ms"], 4) if res["total_ms"] else None},
             "cpu_baseline": res["cpu"],
