@@ -309,11 +309,13 @@ class PjrtApi:
         a caller can enqueue several steps back to back."""
         n = len(input_buffers)
         nouts = max(1, int(num_outputs))
-        arg_ptrs = (ctypes.c_uint64 * max(1, n))(*input_buffers)
-        for i, b in enumerate(input_buffers):
-            if not b:
-                raise PJRTError(f"NULL input buffer {i}")
-        arg_lists = (ctypes.c_uint64 * 1)(ctypes.addressof(arg_ptrs))
+        # the argument list as one uint64 array (numpy: a few µs for the ~500
+        # buffers of a decode step, where a ctypes array built from a list costs
+        # 150 µs)
+        arg_ptrs = np.fromiter(input_buffers, dtype=np.uint64, count=n) if n else np.zeros(1, np.uint64)
+        if n and not arg_ptrs.all():
+            raise PJRTError(f"NULL input buffer {int(np.flatnonzero(arg_ptrs == 0)[0])}")
+        arg_lists = (ctypes.c_uint64 * 1)(arg_ptrs.ctypes.data)
         out_ptrs = (ctypes.c_uint64 * nouts)()
         out_lists = (ctypes.c_uint64 * 1)(ctypes.addressof(out_ptrs))
         events = (ctypes.c_uint64 * 1)()
@@ -343,7 +345,7 @@ class PjrtApi:
             self._call(OFFSET_EVENT_DESTROY, d)
         if nouts == 1:
             return out_ptrs[0]
-        return [out_ptrs[i] for i in range(nouts)]
+        return list(out_ptrs)
 
     def buffer_to_host(self, buf: int, nbytes: int, out: Optional[np.ndarray] = None) -> np.ndarray:
         """pjrt.clj:527-563 (dst_size given by the caller; the reference passes numel*4)."""
