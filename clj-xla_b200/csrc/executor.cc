@@ -62,6 +62,16 @@ ProfileState& profile_state() {
 
 void* client_alloc(PJRT_Client* c, size_t bytes) {
   if (!bytes) return nullptr;
+  if (bytes <= PJRT_Client::kSmallBlock) {
+    bytes = (bytes + 255) & ~(size_t)255;
+    std::lock_guard<std::mutex> lk(c->small_mu);
+    auto it = c->small_free.find(bytes);
+    if (it != c->small_free.end() && !it->second.empty()) {
+      void* p = it->second.back();
+      it->second.pop_back();
+      return p;
+    }
+  }
   const int64_t lim = c->opt.memory_limit;
   const int64_t now = c->held_bytes.fetch_add((int64_t)bytes) + (int64_t)bytes;
   if (lim > 0 && now > lim) {
@@ -83,8 +93,23 @@ void* client_alloc(PJRT_Client* c, size_t bytes) {
 
 void client_free(PJRT_Client* c, void* p, size_t bytes) {
   if (!p) return;
+  if (bytes <= PJRT_Client::kSmallBlock) {  // kept for the next allocation of this size
+    std::lock_guard<std::mutex> lk(c->small_mu);
+    c->small_free[(bytes + 255) & ~(size_t)255].push_back(p);
+    return;
+  }
   cudaFreeAsync(p, c->stream);  // stream ordered after every reader
   c->held_bytes.fetch_sub((int64_t)bytes);
+}
+
+void client_release_cached(PJRT_Client* c) {
+  std::lock_guard<std::mutex> lk(c->small_mu);
+  for (auto& kv : c->small_free)
+    for (void* p : kv.second) {
+      cudaFreeAsync(p, c->stream);
+      c->held_bytes.fetch_sub((int64_t)kv.first);
+    }
+  c->small_free.clear();
 }
 
 Storage::~Storage() { client_free(client, ptr, bytes); }
@@ -391,10 +416,13 @@ void exec_run(PJRT_LoadedExecutable* ex, PJRT_Buffer* const* args, size_t nargs,
   // in place only when every updated argument is passed once and shares its storage with no other argument
   bool inplace = ex->inplace.plan != nullptr;
   if (inplace) {
+    std::vector<const Storage*> st(nargs);
+    for (size_t j = 0; j < nargs; ++j) st[j] = args[j]->ver->storage.get();
+    std::sort(st.begin(), st.end());
     for (const InplaceDus& d : ex->inplace.plan->inplace) {
-      const Storage* st = args[d.param]->ver->storage.get();
-      for (size_t j = 0; j < nargs && inplace; ++j)
-        if ((int)j != d.param && args[j]->ver->storage.get() == st) inplace = false;
+      const Storage* s0 = args[d.param]->ver->storage.get();
+      const auto r = std::equal_range(st.begin(), st.end(), s0);
+      if (r.second - r.first > 1) inplace = false;
     }
   }
   ExecVariant& v = inplace ? ex->inplace : ex->copy;

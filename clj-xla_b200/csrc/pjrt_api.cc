@@ -204,6 +204,8 @@ PJRT_Error* Client_Destroy(void* a) {
     if (!args->client) return;
     set_device(args->client);
     cudaStreamSynchronize(args->client->stream);
+    client_release_cached(args->client);
+    cudaStreamSynchronize(args->client->stream);
     delete args->client->p2p;
     args->client->p2p = nullptr;
     nccl_comm_destroy(args->client->nccl_comm);
@@ -336,10 +338,24 @@ PJRT_Error* Client_BufferFromHostBuffer(void* a) {
     set_device(c);
     if (bytes && !args->data) fail(E_INVALID, "null host data");
     std::unique_ptr<PJRT_Buffer> b(new_buffer(c, dt, dims));
-    if (bytes >= UPLOAD_STAGED_MIN) upload_staged(c, b->ptr(), args->data, bytes);
-    else if (bytes) CUDA_OK(cudaMemcpyAsync(b->ptr(), args->data, bytes, cudaMemcpyHostToDevice, c->stream));
-    // the host buffer may be released once this event completes
-    args->done_with_host_buffer = new_event(c);
+    if (bytes >= UPLOAD_STAGED_MIN) {
+      upload_staged(c, b->ptr(), args->data, bytes);
+      // the host buffer may be released once this event completes
+      args->done_with_host_buffer = new_event(c);
+    } else {
+      // a host-to-device cudaMemcpyAsync from pageable memory copies the data
+      // into the driver's staging memory before it returns: the host buffer is
+      // free now, which a NULL event says (pjrt.clj:420-433 awaits only a
+      // non-NULL one); from page-locked memory the copy reads it later
+      bool pinned = false;
+      if (bytes) {
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, args->data) == cudaSuccess) pinned = at.type == cudaMemoryTypeHost;
+        cudaGetLastError();
+        CUDA_OK(cudaMemcpyAsync(b->ptr(), args->data, bytes, cudaMemcpyHostToDevice, c->stream));
+      }
+      args->done_with_host_buffer = pinned ? new_event(c) : nullptr;
+    }
     args->buffer = b.release();
   });
 }

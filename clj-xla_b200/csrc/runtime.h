@@ -134,6 +134,13 @@ struct PJRT_Client {
   std::string platform = "cuda";
   void* nccl_comm = nullptr;  // tp_size > 1
   std::atomic<int64_t> held_bytes{0};  // device memory held through client_alloc
+  // freed blocks of at most kSmallBlock bytes, by rounded size, reused by the
+  // next allocation of that size (every use is ordered on the client's stream):
+  // a decode step's undo records and result buffers cost no allocator call.
+  // They stay in held_bytes while cached.
+  static constexpr size_t kSmallBlock = 4u << 20;
+  std::mutex small_mu;
+  std::map<size_t, std::vector<void*>> small_free;
   cljxla::P2PAllReduce* p2p = nullptr;  // one-shot peer all-reduce, once its handles are exchanged
 };
 
@@ -157,6 +164,8 @@ ProfileState& profile_state();
 // and its release.
 void* client_alloc(PJRT_Client* c, size_t bytes);
 void client_free(PJRT_Client* c, void* p, size_t bytes);
+// returns the cached small blocks to the device allocator (client teardown)
+void client_release_cached(PJRT_Client* c);
 
 // New head-version buffer over fresh storage of `bytes` (stream-ordered allocation).
 PJRT_Buffer* new_buffer(PJRT_Client* c, DT dt, const std::vector<int64_t>& dims);
