@@ -21,7 +21,12 @@
 #include <cerrno>
 #include <cmath>
 #include <cstdlib>
+#include <algorithm>
+#include <cstring>
+#include <string>
 #include <string_view>
+#include <thread>
+#include <vector>
 
 #include "ir.h"
 
@@ -274,15 +279,81 @@ double round_to_dt(double v, DT dt) {
   }
 }
 
+// Decimal numbers of up to 15 significant digits and a power of ten within
+// 10^+-22 (every value the printer writes with %.6e, stablehlo.clj:269-270,
+// and every integer literal) convert exactly: the digits form an integer
+// below 2^53 and both it and the power of ten are exact doubles, so one
+// multiplication or division rounds once, as strtod does (Clinger's fast
+// path).  Anything else (more digits, larger exponents, inf / nan) goes to
+// strtod.  Returns false when the token is not a number of this form.
+bool fast_decimal(const char*& c, const char* e, double* out) {
+  static const double kPow10[23] = {1e0,  1e1,  1e2,  1e3,  1e4,  1e5,  1e6,  1e7,  1e8,  1e9,  1e10, 1e11,
+                                    1e12, 1e13, 1e14, 1e15, 1e16, 1e17, 1e18, 1e19, 1e20, 1e21, 1e22};
+  const char* p = c;
+  bool neg = false;
+  if (p < e && (*p == '-' || *p == '+')) neg = *p++ == '-';
+  uint64_t m = 0;
+  int digits = 0, frac = 0;
+  bool any = false;
+  while (p < e && *p >= '0' && *p <= '9') {
+    if (m || *p != '0') ++digits;
+    m = m * 10 + (uint64_t)(*p++ - '0');
+    any = true;
+    if (digits > 15) return false;
+  }
+  if (p < e && *p == '.') {
+    ++p;
+    while (p < e && *p >= '0' && *p <= '9') {
+      if (m || *p != '0') ++digits;
+      m = m * 10 + (uint64_t)(*p++ - '0');
+      ++frac;
+      any = true;
+      if (digits > 15) return false;
+    }
+  }
+  if (!any) return false;
+  int ex = 0;
+  if (p < e && (*p == 'e' || *p == 'E')) {
+    ++p;
+    bool eneg = false;
+    if (p < e && (*p == '-' || *p == '+')) eneg = *p++ == '-';
+    if (p >= e || *p < '0' || *p > '9') return false;
+    while (p < e && *p >= '0' && *p <= '9') {
+      ex = ex * 10 + (*p++ - '0');
+      if (ex > 400) return false;
+    }
+    if (eneg) ex = -ex;
+  }
+  if (p < e && ((*p >= 'a' && *p <= 'z') || (*p >= 'A' && *p <= 'Z'))) return false;  // e.g. "inf"
+  const int k = ex - frac;
+  double v = (double)m;
+  if (k < -22 || k > 22) return false;
+  v = k < 0 ? v / kPow10[-k] : v * kPow10[k];
+  *out = neg ? -v : v;
+  c = p;
+  return true;
+}
+
 double parse_scalar_token(const char*& c, const char* e, sv line) {
   while (c < e && *c == ' ') c++;
   if (e - c >= 4 && !memcmp(c, "true", 4)) { c += 4; return 1.0; }
   if (e - c >= 5 && !memcmp(c, "false", 5)) { c += 5; return 0.0; }
+  double v;
+  if (fast_decimal(c, e, &v)) return v;
   char* nx;
-  double v = strtod(c, &nx);
+  v = strtod(c, &nx);
   if (nx == c) perr("bad literal value", line);
   c = nx;
   return v;
+}
+
+// the comma-separated values between c and e (no brackets) into vals, in order
+void parse_values(const char* c, const char* e, std::vector<double>& vals, sv line) {
+  while (c < e) {
+    while (c < e && (*c == ' ' || *c == ',' || *c == '[' || *c == ']')) c++;
+    if (c >= e) break;
+    vals.push_back(parse_scalar_token(c, e, line));
+  }
 }
 
 }  // namespace
@@ -447,12 +518,46 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
       const char* e = c + lit.size();
       if (!lit.empty() && lit[0] == '[') {
         std::vector<double> vals;
-        vals.reserve((size_t)std::max<int64_t>(1, n.numel()));
         c++;
-        while (c < e) {
-          while (c < e && (*c == ' ' || *c == ',')) c++;
-          if (c >= e || *c == ']') break;
-          vals.push_back(parse_scalar_token(c, e, line));
+        const char* close = e;
+        while (close > c && close[-1] != ']') --close;  // the literal's closing bracket
+        if (close > c) --close;
+        const size_t len = (size_t)(close - c);
+        // large literals (the [S, T] masks and [S, hd] RoPE tables of a
+        // static-position prefill) are split at commas over host threads
+        const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+        const size_t nthr = len < (1u << 20) ? 1 : std::min<size_t>(hw, std::min<size_t>(32, len >> 18));
+        if (nthr <= 1) {
+          vals.reserve((size_t)std::max<int64_t>(1, n.numel()));
+          parse_values(c, close, vals, line);
+        } else {
+          std::vector<const char*> cut(nthr + 1);
+          cut[0] = c;
+          cut[nthr] = close;
+          for (size_t t = 1; t < nthr; ++t) {
+            const char* q = c + len * t / nthr;
+            while (q < close && *q != ',') ++q;
+            cut[t] = std::max(q, cut[t - 1]);
+          }
+          std::vector<std::vector<double>> parts(nthr);
+          std::vector<std::string> errs(nthr);
+          std::vector<std::thread> th;
+          for (size_t t = 0; t < nthr; ++t)
+            th.emplace_back([&, t] {
+              try {
+                parts[t].reserve((size_t)(cut[t + 1] - cut[t]) / 8 + 1);
+                parse_values(cut[t], cut[t + 1], parts[t], line);
+              } catch (const std::exception& x) {
+                errs[t] = x.what();
+              }
+            });
+          for (auto& x : th) x.join();
+          for (const auto& m : errs)
+            if (!m.empty()) perr("bad literal value", line);
+          size_t tot = 0;
+          for (const auto& v : parts) tot += v.size();
+          vals.reserve(tot);
+          for (auto& v : parts) vals.insert(vals.end(), v.begin(), v.end());
         }
         if ((int64_t)vals.size() != n.numel()) perr("dense literal has wrong element count", line);
         store_literal(n, vals);

@@ -150,6 +150,25 @@ def test_few_row_f32_products(ctx, M, K, N):
     check_graph(ctx, g, [rand((M, K), "f32", 21, 0.5), rand((K, N), "f32", 22, 0.05), rand((N, K), "f32", 23, 0.05)])
 
 
+def test_large_dense_literal(ctx):
+    """A dense literal of 400 K values (about 5 MB of printed text, the size of
+    a static-position prefill mask) is parsed in chunks on several host threads
+    and through the exact decimal fast path: every value equals the oracle's."""
+    n = 400_000
+    rng = np.random.Generator(np.random.PCG64(31))
+    vals = (rng.standard_normal(n) * 10.0 ** rng.integers(-6, 6, n)).astype(np.float32)
+    vals[::7] = -10000.0
+    vals[::11] = 0.0
+    g = t.trace_graph("biglit", [("x", ("tensor", (n,), "f32"))],
+                      lambda x: [t.add(x, t.emit_constant([float(v) for v in vals], ("tensor", (n,), "f32")))])
+    text = shlo.graph_to_mlir_text(g)
+    assert len(text) > 4 << 20
+    x = np.zeros(n, np.float32)
+    got = runner.run_graph(ctx, g, [x], text)[0]
+    want = interp.run_mlir(text, [x])[0]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_gather_rows_and_clamp(ctx):
     def f(tab, ids):
         return t.gather(tab, ids)
