@@ -211,11 +211,12 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
     jit_launch(l.jit_fn, l.jit_grid, l.jit_block, l.jit_cluster, l.jit_smem, argtab, l.jit_args, s);
     return;
   }
-  if (!l.epi.empty() && (l.kind == K_GEMV || l.kind == K_GEMV_FUSED)) {
-    // not compiled: the GEMV (its producer first), then the epilogue program
+  if ((!l.epi.empty() || !l.gtail.empty()) && (l.kind == K_GEMV || l.kind == K_GEMV_FUSED)) {
+    // not compiled: the GEMV (its producer first), then the epilogue and group-tail programs
     if (l.kind == K_GEMV_FUSED) run_launch(l.parts[0], argtab, s);
     launch_gemv(*(const GemvParams*)b, argtab, s);
     for (const Launch& e : l.epi) run_launch(e, argtab, s);
+    for (const Launch& q : l.gtail) run_launch(q, argtab, s);
     return;
   }
   if (!l.epi.empty()) {  // not compiled: the program, then its epilogue as its own launch

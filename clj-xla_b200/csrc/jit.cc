@@ -1055,6 +1055,9 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
   if (epi && (tail || G.M != 1 || G.nseg > 2 || (paired && G.seg_end[1] != 2 * G.seg_end[0]) ||
               l.epi.size() != 1 || l.epi[0].kind != K_EW))
     return false;
+  // group tails: row programs over whole groups of output rows
+  const bool gt = !l.gtail.empty();
+  if (gt && (tail || epi || G.M != 1)) return false;
   if (G.M >= 2 && !fused && !tail &&
       (describe_gemv_mma(G, src, grid, block, smem, args) || describe_gemv_mma_chunked(G, src, grid, block, smem, args)))
     return true;
@@ -1084,7 +1087,7 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
   }
   put(kS, G.status);
   put(kX, G.x);
-  if (tail) put(kT, G.tail_ctr);
+  if (tail || gt) put(kT, G.tail_ctr);
   constexpr int WARPS = 8;
   const int64_t M = G.M, K = G.K, N = G.N;
   const int WPR = geo.wpr, RPS = geo.rps, NST = geo.nstage;
@@ -1107,6 +1110,62 @@ bool describe_gemv_tma(const Launch& l, std::string* src, int64_t* grid, int* bl
     for (size_t i = 0; i < l.parts.size(); ++i)
       t << "      tail" << i << "(argtab, t.p[" << i << "], 0u, 1u);\n      consumers_sync();\n";
     t << "      if (threadIdx.x == 0) *" << ctr << " = 0u;  // ready for the next launch\n    }\n  }\n";
+    tail_code = t.str();
+  }
+  // group tails: each row r of part i covers GEMV rows [G0, G1) of one segment;
+  // a CTA that wrote some of them arrives on the group's counter, and the one
+  // completing it (the count of CTAs whose row range meets [G0, G1) is fixed by
+  // the partition r0 = N c / grid) runs the row and its epilogue; the rows are
+  // read through L2 after the acquire
+  struct GroupTail {
+    int part, row, args, epi_args;
+    int64_t g0, g1, target, rows, C;
+  };
+  std::vector<GroupTail> groups;
+  if (gt) {
+    int ai = 0;
+    for (size_t i = 0; i < l.gtail.size(); ++i) {
+      const Launch& q = l.gtail[i];
+      const Launch& qb = q.kind == K_FUSED_DUS ? q.parts[0] : q;
+      if (qb.kind != K_ROWNORM) return false;
+      const RowParams& r = *(const RowParams*)qb.blob.data();
+      int seg = -1;
+      for (int j = 0; j < r.nin && seg < 0; ++j)
+        for (int k = 0; k < G.nseg; ++k)
+          if (r.in[j].p.slot == G.y[k].slot && r.in[j].p.off == G.y[k].off) seg = k;
+      if (seg < 0) return false;
+      const int64_t s0 = seg ? G.seg_end[seg - 1] : 0;
+      if (G.seg_end[seg] - s0 != r.rows * r.C) return false;
+      const int a = ai++;
+      const int ea = q.epi.empty() ? -1 : ai++;
+      for (int64_t row = 0; row < r.rows; ++row) {
+        GroupTail g{(int)i, (int)row, a, ea, s0 + row * r.C, s0 + (row + 1) * r.C, 0, r.rows, r.C};
+        for (int64_t c = 0; c < ctas; ++c) {
+          const int64_t c0 = N * c / ctas, c1 = N * (c + 1) / ctas;
+          if (c0 < g.g1 && g.g0 < c1) ++g.target;
+        }
+        groups.push_back(g);
+      }
+    }
+    std::ostringstream t;
+    const std::string ctr = "((unsigned*)" + base_expr(kT) + ")";
+    t << "  {\n    __shared__ int gt_run;\n    __threadfence();  // this CTA's rows, before its arrivals\n"
+         "    consumers_sync();\n";
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+      const GroupTail& g = groups[gi];
+      t << "    if (r0 < " << g.g1 << "LL && " << g.g0 << "LL < r1) {\n";
+      t << "      if (threadIdx.x == 0) {\n        unsigned old;\n";
+      t << "        asm volatile(\"atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;\" : \"=r\"(old) : \"l\"(" << ctr << " + "
+        << gi << ") : \"memory\");\n";
+      t << "        gt_run = old == " << g.target - 1 << "u;\n      }\n      consumers_sync();\n      if (gt_run) {\n";
+      t << "        gt" << g.part << "(argtab, t.p[" << g.args << "], " << g.row << "u, " << g.rows << "u);\n";
+      if (g.epi_args >= 0)
+        t << "        consumers_sync();\n        gte" << g.part << "(argtab, t.p[" << g.epi_args << "], " << g.row * g.C
+          << "LL, " << (g.row + 1) * g.C << "LL);\n";
+      t << "        consumers_sync();\n        if (threadIdx.x == 0) " << ctr << "[" << gi << "] = 0u;  // ready for the next launch\n";
+      t << "      }\n      consumers_sync();\n    }\n";
+    }
+    t << "  }\n";
     tail_code = t.str();
   }
   std::ostringstream s;
@@ -1184,6 +1243,28 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   for (int i = 0; i + 1 < G.nseg; ++i)
     s << "  if (r < " << G.seg_end[i] << "LL && e > " << G.seg_end[i] << "LL) e = " << G.seg_end[i] << "LL;\n";
   s << "  return e;\n}\n";
+  if (gt) {
+    // the group-tail programs, bodies run by the 256 consumer threads of one CTA
+    int np = 0;
+    for (const Launch& q : l.gtail) np += 1 + (q.epi.empty() ? 0 : 1);
+    s << "struct JitTail { JitArgs g; JitArgs p[" << np << "]; };\n";
+    g_l2_loads = true;
+    for (size_t i = 0; i < l.gtail.size(); ++i) {
+      BodyOpts bo;
+      bo.block = WARPS * 32;
+      bo.sync = "consumers_sync()";
+      bo.row_cache = 12;
+      emit_body(s, l.gtail[i], WARPS * 32, 1, "gt" + std::to_string(i), bo);
+      if (!l.gtail[i].epi.empty()) {
+        BodyOpts be;
+        be.block = WARPS * 32;
+        be.sync = "consumers_sync()";
+        be.ranged = true;
+        emit_body(s, l.gtail[i].epi[0], WARPS * 32, 1, "gte" + std::to_string(i), be);
+      }
+    }
+    g_l2_loads = false;
+  }
   if (tail) {
     // the tail programs, each a body run by the 256 consumer threads of one CTA
     s << "struct JitTail { JitArgs g; JitArgs p[" << l.parts.size() << "]; };\n";
@@ -1207,7 +1288,7 @@ __device__ __forceinline__ float dot8(const uint4& w, const float* x) {
   }
   s << "extern \"C\" __global__ void __launch_bounds__(" << (WARPS + 1) * 32
     << ", " << geo.ctas_per_sm << ") cljxla_fused_gemv(const u64* __restrict__ argtab, const "
-    << (tail ? "JitTail t) {\n  const JitArgs& a = t.g;\n" : epi ? "JitEpi t) {\n  const JitArgs& a = t.g;\n" : "JitArgs a) {\n");
+    << (tail || gt ? "JitTail t) {\n  const JitArgs& a = t.g;\n" : epi ? "JitEpi t) {\n  const JitArgs& a = t.g;\n" : "JitArgs a) {\n");
   s << "  extern __shared__ __align__(1024) unsigned char dsm[];\n";
   s << "  __shared__ __align__(8) unsigned long long full_bar[" << NST << "], empty_bar[" << NST << "];\n";
   s << "  __shared__ float red[" << NST << "][" << WARPS << "][" << M << "];\n";
@@ -1385,6 +1466,17 @@ bool jit_describe(const Launch& l, std::string* src, int64_t* grid, int* block, 
       JitArgs ea;
       if (!describe_one(e, &g, &b, &c, &ea)) return false;
       args->push_back(ea);
+    }
+    for (const Launch& q : l.gtail) {  // each group-tail program's buffers, then its epilogue's
+      int64_t g;
+      int b, c;
+      JitArgs qa;
+      if (!describe_one(q, &g, &b, &c, &qa)) return false;
+      args->push_back(qa);
+      for (const Launch& e : q.epi) {
+        if (!describe_one(e, &g, &b, &c, &qa)) return false;
+        args->push_back(qa);
+      }
     }
     if (l.kind == K_GEMV_TAIL)
       for (const Launch& p : l.parts) {

@@ -2416,6 +2416,7 @@ void Planner::run() {
     if (opt_.fast_kernels) {
       fuse_gemv_epilogues(plan_);
       fuse_row_epilogues(plan_);
+      fuse_gemv_group_tails(plan_);
       link_gemv_prefetch(plan_);
       link_attention_hints(plan_);
       fuse_gemv_tails(plan_);

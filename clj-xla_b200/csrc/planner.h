@@ -60,6 +60,11 @@ struct Launch {
   // CTA runs on its own rows once they are done (a GeGLU over paired gate / up
   // segments); not compiled: it runs as its own launch after the GEMV
   std::vector<Launch> epi;
+  // K_GEMV / K_GEMV_FUSED (one row of x): row programs over the GEMV's output
+  // rows, each row (a group of GEMV rows) run by the CTA that completes it
+  // (per-group arrival counters in GemvParams::tail_ctr); not compiled: they
+  // run as their own launches after the GEMV
+  std::vector<Launch> gtail;
 };
 
 struct TensorSpec {
@@ -133,6 +138,11 @@ void schedule_and_merge(Plan& p);
 // element (the GeGLU after the gate / up projection) into the GEMV as an
 // epilogue each CTA runs on its own rows (schedule.cc).
 void fuse_gemv_epilogues(Plan& p);
+
+// Moves the row programs that read a one-row GEMV's output by whole rows (the
+// per-head q / k norms with their RoPE epilogue, the v norm) into the GEMV:
+// the CTA that completes a row's GEMV rows runs that row (schedule.cc).
+void fuse_gemv_group_tails(Plan& p);
 
 // Moves an elementwise program that reads a row program's outputs only within
 // each element's own row (RoPE after the per-head norms) into the row program's

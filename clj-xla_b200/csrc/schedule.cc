@@ -100,6 +100,8 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
   const void* b = l.blob.data();
   for (const Launch& e : l.epi)  // an epilogue program runs inside the launch
     if (!accesses(p, e, out)) return false;
+  for (const Launch& e : l.gtail)  // and so do group-tail programs
+    if (!accesses(p, e, out)) return false;
   if (l.kind == K_FUSED_DUS) {
     for (const Launch& part : l.parts)
       if (!accesses(p, part, out)) return false;
@@ -161,6 +163,12 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
         for (const Launch& part : l.parts)
           if (!accesses(p, part, out)) return false;
         c.add(g.tail_ctr, 4, true);
+      }
+      if (!l.gtail.empty()) {
+        int64_t groups = 0;
+        for (const Launch& q : l.gtail)
+          groups += ((const RowParams*)(q.kind == K_FUSED_DUS ? q.parts[0] : q).blob.data())->rows;
+        c.add(g.tail_ctr, 4 * groups, true);
       }
       if (l.kind == K_GEMV_FUSED) {  // x is computed in shared memory by the producer's program
         if (l.parts.size() != 1 || !accesses(p, l.parts[0], out)) return false;
@@ -565,6 +573,105 @@ bool row_local(const Plan& p, const RowParams& r, const EwParams& e, const std::
 }
 
 }  // namespace
+
+void fuse_gemv_group_tails(Plan& p) {
+  // opt-in (CLJXLA_B200_GEMV_GROUP_TAIL=1): on Gemma-3-4B decode the per-head
+  // norms, RoPE and KV writes run by the q/k/v GEMV's completing CTAs took 2.45
+  // ms / step against 2.27 ms as their own launch (13 CTAs of 512 threads
+  // right after the GEMV): the completing CTAs are the GEMV's last ones, and a
+  // CTA that completes several heads runs them one after another
+  const char* env = getenv("CLJXLA_B200_GEMV_GROUP_TAIL");
+  if (!env || env[0] != '1') return;
+  std::vector<Launch>& L = p.launches;
+  for (size_t i = 0; i + 1 < L.size(); ++i) {
+    Launch& gl = L[i];
+    if ((gl.kind != K_GEMV && gl.kind != K_GEMV_FUSED) || !gl.epi.empty() || !gl.gtail.empty()) continue;
+    GemvParams G;
+    memcpy(&G, gl.blob.data(), sizeof(G));
+    if (G.M != 1) continue;
+    Launch& nx = L[i + 1];
+    std::vector<Launch> parts;
+    if (nx.kind == K_MULTI) parts = nx.parts;
+    else if (nx.kind == K_ROWNORM || nx.kind == K_FUSED_DUS) parts.push_back(nx);
+    else continue;
+    std::vector<Access> ga, yw;
+    if (!accesses(p, gl, ga)) continue;
+    {
+      Collector c{p, yw};
+      for (int s = 0; s < G.nseg; ++s)
+        c.add(G.y[s], (G.seg_end[s] - (s ? G.seg_end[s - 1] : 0)) * (int64_t)dt_size((DT)G.y_dt[s]), true);
+    }
+    bool ok = parts.size() <= 6;
+    int64_t groups = 0;
+    for (const Launch& q : parts) {
+      if (!ok) break;
+      const Launch& qb = q.kind == K_FUSED_DUS ? q.parts[0] : q;
+      if (qb.kind != K_ROWNORM || q.epi.size() > 1) { ok = false; break; }
+      const RowParams& r = *(const RowParams*)qb.blob.data();
+      int blk, cl;
+      int64_t grid;
+      row_launch_shape(r, &blk, &cl, &grid);
+      if (cl != 1 || grid != r.rows || r.C > 12 * 256) { ok = false; break; }
+      // one input is a whole GEMV segment read row by row, densely
+      int seg = -1;
+      int64_t dense[CLJXLA_MAXR];
+      {
+        int64_t st = 1;
+        for (int d = r.rank - 1; d >= 0; --d) {
+          dense[d] = st;
+          st *= r.dims[d];
+        }
+      }
+      for (int j = 0; j < r.nin; ++j) {
+        const EwIn& in = r.in[j];
+        int sj = -1;
+        for (int k = 0; k < G.nseg; ++k)
+          if (in.p.slot == G.y[k].slot && in.p.off == G.y[k].off) sj = k;
+        std::vector<Access> ia;
+        {
+          Collector ic{p, ia};
+          int64_t hi = 0;
+          for (int d = 0; d < r.rank; ++d) hi += (r.dims[d] - 1) * in.stride[d];
+          ic.add(in.p, (hi + 1) * (int64_t)dt_size((DT)in.dt), false);
+        }
+        if (sj < 0) {
+          if (conflict(ia, yw)) ok = false;  // part of a GEMV output, not read as a whole segment
+          continue;
+        }
+        if (seg >= 0 && seg != sj) ok = false;
+        seg = sj;
+        if (in.sel_dim >= 0 || in.dt != G.y_dt[sj] ||
+            G.seg_end[sj] - (sj ? G.seg_end[sj - 1] : 0) != r.rows * r.C)
+          ok = false;
+        for (int d = 0; d < r.rank && ok; ++d)
+          if (r.dims[d] > 1 && in.stride[d] != dense[d]) ok = false;
+      }
+      if (seg < 0) ok = false;
+      // what the part (and its epilogue) writes is not something the GEMV touches
+      std::vector<Access> qa;
+      if (!ok || !accesses(p, q, qa)) { ok = false; break; }
+      std::vector<Access> qw;
+      for (const Access& x : qa)
+        if (x.write) qw.push_back(x);
+      if (conflict(qw, ga)) ok = false;
+      // the epilogue reads no GEMV output directly
+      for (const Launch& e : q.epi) {
+        std::vector<Access> ea;
+        if (!accesses(p, e, ea) || conflict(ea, yw)) ok = false;
+      }
+      groups += r.rows;
+    }
+    if (!ok || groups == 0 || groups > 64) continue;
+    const size_t off = (p.const_blob.size() + 15) & ~size_t(15);
+    p.const_blob.resize(off + 4 * (size_t)groups, 0);
+    G.tail_ctr = DPtr{p.const_slot(), 0, (int64_t)off};
+    memcpy(gl.blob.data(), &G, sizeof(G));
+    gl.label += "+" + nx.label;
+    gl.algo_bytes += nx.algo_bytes;
+    gl.gtail = std::move(parts);
+    L.erase(L.begin() + (long)(i + 1));
+  }
+}
 
 void fuse_row_epilogues(Plan& p) {
   const char* env = getenv("CLJXLA_B200_ROW_EPILOGUE");

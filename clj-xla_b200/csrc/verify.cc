@@ -96,6 +96,19 @@ void verify_launch(const Plan& p, Checker& c, const Launch& l) {
       c.cur = &l;
       c.region(g.tail_ctr, 4, "tail arrival counter");
     }
+    if (!l.gtail.empty()) {  // row programs run by the CTAs completing their groups of GEMV rows
+      if (l.kind != K_GEMV && l.kind != K_GEMV_FUSED) fail(E_INTERNAL, "group tails on a launch that is no GEMV");
+      const GemvParams& g = *(const GemvParams*)l.blob.data();
+      int64_t groups = 0;
+      for (const Launch& q : l.gtail) {
+        const Launch& qb = q.kind == K_FUSED_DUS ? q.parts[0] : q;
+        if (qb.kind != K_ROWNORM || g.M != 1) fail(E_INTERNAL, "bad GEMV group tail");
+        groups += ((const RowParams*)qb.blob.data())->rows;
+        verify_launch(p, c, q);
+      }
+      c.cur = &l;
+      c.region(g.tail_ctr, 4 * groups, "group-tail arrival counters");
+    }
     if (!l.epi.empty() && l.kind == K_ROWNORM) {  // row program with an elementwise epilogue over its rows
       const Launch& e = l.epi[0];
       const Launch& eb = e.kind == K_FUSED_DUS ? e.parts[0] : e;
