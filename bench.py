@@ -550,7 +550,10 @@ def main():
         dec_s, e2e_s, pre_s = res["dec_s"], res["e2e_s"], res["prefill_s"]
     tp = None
     if not args.no_tp_block and args.tp == 1 and not args.tiny and not args.layers and world in (1, 2, 4, 8):
-        tp = tp_block(args, rank, world, local_rank)
+        try:
+            tp = tp_block(args, rank, world, local_rank)
+        except Exception as e:  # noqa: BLE001 - the data-parallel line stands; the block says what failed
+            tp = {"error": repr(e)[:300]}
     if rank == 0:
         replicas = world // max(1, args.tp)
         value = replicas * res["tokens"] / dec_s
