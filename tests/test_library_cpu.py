@@ -128,6 +128,35 @@ def test_generated_fused_kernels_compile(lib_path):
             assert k.value > 0
 
 
+def test_decode_plan_fusions(lib_path, monkeypatch):
+    """The decode plan's launch count with and without each fusion (host-only
+    planning): the GeGLU runs as the gate / up GEMV's epilogue, RoPE in the
+    CTAs of the per-head norms, and single-row norms as GEMV prologues; every
+    fused kernel still has its compiled form (checked in
+    test_generated_fused_kernels_compile)."""
+    import dataclasses
+    from cljxla_b200.host import drivers as d
+    from cljxla_b200.host import stablehlo as shlo
+    cfg = dataclasses.replace(d.GEMMA3_4B, vocab=512, d_model=256, layers=6, n_heads=4, n_kv_heads=2,
+                              head_dim=64, mlp=512, window=6)
+    text = shlo.graph_to_mlir_text(d.build_graph(cfg, "decode", 1, 8, 32))
+
+    def launches(**env):
+        for k in ("CLJXLA_B200_GEMV_EPILOGUE", "CLJXLA_B200_ROW_EPILOGUE", "CLJXLA_B200_GEMV_PROLOGUE"):
+            monkeypatch.delenv(k, raising=False)
+        for k, v in env.items():
+            monkeypatch.setenv(k, v)
+        return core.plan_text(lib_path, text, fuse=3)["launches"]
+
+    full = launches()
+    assert launches(CLJXLA_B200_GEMV_EPILOGUE="0") >= full + cfg.layers
+    assert launches(CLJXLA_B200_ROW_EPILOGUE="0") >= full + cfg.layers
+    assert launches(CLJXLA_B200_GEMV_PROLOGUE="0") >= full + cfg.layers
+    # six launches per layer: attention, o, gate/up (+ norm prologue, GeGLU epilogue), down,
+    # q/k/v (+ input norm prologue), per-head norms (+ RoPE and the KV writes)
+    assert full <= 6 * cfg.layers + 8, full
+
+
 _JIT_CACHE_PROBE = r"""
 import ctypes, sys, dataclasses
 sys.path.insert(0, sys.argv[1])
