@@ -479,6 +479,23 @@ def run_ours(args, rank, world, local_rank):
     return cfg, B, S, T, res
 
 
+def prefill_roofline(cfg, B, S, seconds):
+    """Tensor roofline of one prefill (per GPU): algorithmic FLOPs = 2 B S x
+    (every weight element, the tied LM head counted with the embedding) + per
+    layer 2 x 2 B nq hd x (S^2 / 2 causal, or S W inside a window), against
+    the measured burst bf16 GEMM peak."""
+    from cljxla_b200.host import drivers as d
+    params = sum(int(np.prod(shp)) for _, shp, _ in d.weight_specs(cfg))
+    flops = 2.0 * B * S * params
+    for i in range(cfg.layers):
+        span = S * min(S, cfg.window) if cfg.is_local(i) else S * S / 2
+        flops += 4.0 * B * cfg.n_heads * cfg.head_dim * span
+    _, tc_peak, src = load_peaks()
+    tf = flops / seconds / 1e12
+    return {"bound": "tensor", "achieved": round(tf, 1), "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": round(tf / tc_peak, 4), "flops": round(flops), "peak_source": src + " (burst)"}
+
+
 # DRAM traffic per launch of the dominant kernel class, from one ncu capture
 # of the same kernels (dram__bytes_read.sum + dram__bytes_write.sum; the
 # command and per-launch table are in profiles/gemv_bulk_copy_gemma3-4b_decode.md):
@@ -581,6 +598,7 @@ def main():
                        "l2": "weights stream >> 126 MB L2 every step (no flush needed)"},
             "prefill": {"value": round(replicas * B * S / pre_s, 1), "unit": "tokens/s",
                         "ms": round(pre_s * 1e3, 3), "graph": "dynamic-position prefill",
+                        "roofline": prefill_roofline(cfg, B, S, pre_s),
                         "kernel_time_by_kind_ms": res["pre_by_kind"]},
             "e2e": ({"value": round(replicas * res["e2e_tokens"] / e2e_s, 2), "unit": "tokens/s",
                      "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B,
