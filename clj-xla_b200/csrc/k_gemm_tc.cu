@@ -1,4 +1,5 @@
-// Prefill dot_general on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Prefill and batched-decode dot_general on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA).
 //
 // C[M, N] = A[M, K] . B[N, K]^T with bf16 operands, f32 accumulation in tensor
 // memory and the result rounded once to the printed type (bf16 or f32).  This
@@ -17,6 +18,17 @@
 //                       is meanwhile being filled for the next tile.
 // Tiles are walked M-fastest so CTAs running at the same time share the weight
 // tile (read from HBM once) while the small activation matrix stays in L2.
+//
+// Batched decode (at most 64 rows of A; a few hundred bytes of activations
+// against megabytes of weights): the weight matrix is the stream, so the tile
+// is 64 weight rows wide (MMA N = 64) and a stage carries four 64-wide K
+// blocks (512 contiguous bytes of every weight row, 3-5 stages in flight); A
+// is copied for its own rows only (the MMA's other rows read stale shared
+// memory and their results are never stored).  When the 64-row tiles leave
+// SMs idle, each tile's K blocks are split over CTAs: a (tile, split) unit
+// stores its f32 partial tile, and the last split of the tile to arrive (an
+// acq_rel counter) sums the partials in split order and stores C, so the
+// result does not depend on which CTA finishes first.
 //
 // f32 activations times a bf16 weight (the attention-output projection of a
 // Gemma prefill, whose context vectors are f32): the activation is first split
