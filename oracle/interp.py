@@ -25,8 +25,11 @@ reference's own examples (README.md:50-55 graph, pjrt_test.clj:37-41,
 compile_test.clj:12-16, rocm_e2e_test.clj:38-51) and the one numeric
 known-answer test in the reference (rocm_e2e_test.clj:38-51, ``y = 2.5 x``,
 x = 0..15) - see tests/test_oracle.py.  No reference test pins model outputs
-(the reference's own model tests check traced shapes only), so model-level
-parity is "unpinned" beyond these anchors.
+(the reference's own model tests check traced shapes only).  At model level the
+interpreter is pinned to the Hugging Face ``transformers`` implementations of
+GPT-2, Gemma-2 and Gemma-3, the anchor of the reference's verification scripts
+(verification/verify_torch_vs_clojure.py): f32 logits of a prefill and cached
+decode steps agree within 1e-4 on the same weights (tests/test_oracle_hf.py).
 """
 from __future__ import annotations
 
