@@ -131,6 +131,16 @@ struct AttnParams {
   int32_t k_dt, dt_d1, dt_m, dt_sub, dt_exp, out_dt;
   int32_t nchain, chain_out;
   float mask_skip;
+  // mask_mode 1: the additive mask is computed in the kernel, not read (the
+  // planner proved it equal to the printed causal / sliding-window form, see
+  // MaskForm): mask_mv where j - qpos > mask_gt or j - qpos < mask_lt, else
+  // mask_z, with qpos = pos + qi + mask_off and pos the i32 at mask_pos when
+  // has_mask_pos (else 0).  The mask view then has strides {0, 0, 1, 0}, so a
+  // kernel's mask row offset is the query index qi.
+  int32_t mask_mode, mask_gt, mask_lt, mask_off;
+  float mask_mv, mask_z;
+  DPtr mask_pos;
+  int32_t has_mask_pos, pad_m;
   EwInstr chain[12];
   // the chain in closed form where it is one (kernels skip the interpreter):
   // 0 general, 1 a multiply by chain_c rounded to chain_dt, 2 identity
@@ -176,6 +186,19 @@ struct AttnMatch {
   std::vector<int> absorbed;  // every node the fused kernel replaces (except d2)
   int group = 1;
 };
+// An attention mask operand proven equal to the causal / sliding-window form
+// attention.clj:189-224 prints, either as the iota / compare / select chain of
+// a traced position or as a dense literal: value mv where j - qpos > gt or
+// (has_lt) j - qpos < lt, else z, with qpos = pos + qi + off and pos element 0
+// of the i32 graph parameter pos_param (-1: none, pos = 0).
+struct MaskForm {
+  int pos_param = -1;
+  int64_t off = 0, gt = 0, lt = 0;
+  bool has_lt = false;
+  float mv = 0.f, z = 0.f;
+};
+// Sq / T: the attention's query and key extents (axes 2 and 3 of the operand)
+bool match_mask_form(const Graph& g, int mask, int64_t Sq, int64_t T, MaskForm& f);
 std::vector<AttnMatch> match_attention(const Graph& g, const std::vector<char>& live,
                                        const std::vector<std::vector<int>>& users);
 

@@ -227,6 +227,25 @@ __device__ void merge_if_last(const AttnParams& P, const uint64_t* __restrict__ 
   if (threadIdx.x == 0) *ctr = 0u;  // ready for the next launch
 }
 
+
+// The additive mask of query row offset `moff` at position j.  mask_mode 0
+// reads it through the mask view; mask_mode 1 computes the causal /
+// sliding-window form the planner proved the printed mask to be, where the
+// view's strides {0, 0, 1, 0} make `moff` the query index and qpos0 is the
+// position of query 0 (mask_qpos0: the graph's position parameter plus the
+// form's offset).  The position parameter is never written by a plan kernel,
+// so it may be read before a kernel's dependency wait.
+__device__ __forceinline__ int mask_qpos0(const AttnParams& P, const uint64_t* __restrict__ argtab) {
+  if (!P.mask_mode) return 0;
+  return P.mask_off + (P.has_mask_pos ? *(const int*)dres(P.mask_pos, argtab) : 0);
+}
+__device__ __forceinline__ float mask_at(const AttnParams& P, const char* mb, int64_t moff, int64_t j, int qpos0) {
+  if (P.mask_mode) {
+    const int d = (int)j - (qpos0 + (int)moff);
+    return (d > P.mask_gt || d < P.mask_lt) ? P.mask_mv : P.mask_z;
+  }
+  return ld_any(mb, moff + j * P.mask.stride[3], P.mask.dt);
+}
 template <typename KT, int HPL, int NQV>
 __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ AttnParams P,
                                                       const uint64_t* __restrict__ argtab) {
@@ -248,6 +267,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
   const KT* kb = (const KT*)dres(P.k.p, argtab);
   const KT* vb = (const KT*)dres(P.v.p, argtab);
   const char* mb = dres(P.mask.p, argtab);
+  const int qp0 = mask_qpos0(P, argtab);
 
   // query vectors of this CTA -> shared (f32)
   for (int e = threadIdx.x; e < NQV * HD; e += NW * 32) {
@@ -289,7 +309,7 @@ __global__ void __launch_bounds__(NW * 32) attn_kernel(const __grid_constant__ A
     for (int r = 0; r < NQV; ++r) {
       mk[r] = -INFINITY;
       if (r < nqv && j < t1) {
-        mk[r] = ld_any(mb, mrow[r] + j * P.mask.stride[3], P.mask.dt);
+        mk[r] = mask_at(P, mb, mrow[r], j, qp0);
         any |= mk[r] > P.mask_skip;
       }
     }
@@ -435,6 +455,7 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
   const char* mb = dres(P.mask.p, argtab);
+  const int qp0 = mask_qpos0(P, argtab);
 
   for (int e = threadIdx.x; e < NQV * HD; e += NW * 32) {
     int r = e / HD, d = e % HD;
@@ -469,7 +490,7 @@ __global__ void __launch_bounds__(NW * 32) attn_smem_kernel(const __grid_constan
     for (int r = 0; r < NQV; ++r) {
       mk[r] = -INFINITY;
       if (r < nqv && j < c1) {
-        mk[r] = ld_any(mb, mrow[r] + j * P.mask.stride[3], P.mask.dt);
+        mk[r] = mask_at(P, mb, mrow[r], j, qp0);
         any |= mk[r] > P.mask_skip;
       }
     }
@@ -726,6 +747,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
   const char* mb = dres(P.mask.p, argtab);
+  const int qp0 = mask_qpos0(P, argtab);
   auto qrow = [&](int r, int& qi, int& h) {
     qi = r / P.group;
     h = kh * P.group + r % P.group;
@@ -776,7 +798,6 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
   }
   const uint32_t qsa = (uint32_t)__cvta_generic_to_shared(&qsm[0][g][2 * t]);
   constexpr uint32_t QPART = 8 * (HD + 8) * 2;  // bytes between Q parts
-  const int64_t ms3 = P.mask.stride[3];
   // stage chunk c0 into buffer buf: mask values, active steps, K/V rows of active steps
   // staging of a chunk, in two halves around a barrier the caller places:
   // mask values first, then (once they are visible) the K/V rows of active steps
@@ -784,7 +805,7 @@ __global__ void __launch_bounds__(128) attn_tc_kernel(const __grid_constant__ At
     for (int e = threadIdx.x; e < nqv * TC_CH; e += 128) {
       const int r = e / TC_CH, j = e % TC_CH;
       float v = -INFINITY;
-      if (c0 + j < t1) v = ld_any(mb, moff_s[r] + (c0 + j) * ms3, P.mask.dt);
+      if (c0 + j < t1) v = mask_at(P, mb, moff_s[r], c0 + j, qp0);
       msk[buf][r][j] = v;
     }
     if (threadIdx.x == 0) s_act[buf] = 0u;
@@ -1112,11 +1133,13 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
     s_m[threadIdx.x] = -INFINITY;
     s_l[threadIdx.x] = 0.f;
   }
+  // a computed mask needs only the position (a graph parameter, never written
+  // by a plan kernel): read it before the dependency wait
+  const int qp0 = mask_qpos0(P, argtab);
   __syncthreads();
   pdl_enter();
   unsigned* status = P.has_status ? (unsigned*)dres(P.status, argtab) : nullptr;
   const char* mb = dres(P.mask.p, argtab);
-  const int64_t ms3 = P.mask.stride[3];
   // queries: lane-owned dims of every query vector, f32
   float q[NQ][VPL];
   {
@@ -1148,7 +1171,7 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
     for (int e = threadIdx.x; e < NQ * DEC_CH; e += DEC_THREADS) {
       const int r = e / DEC_CH, j = e % DEC_CH;
       float v = -INFINITY;
-      if (r < nqv && j < n) v = ld_any(mb, s_moff[r] + (c0 + j) * ms3, P.mask.dt);
+      if (r < nqv && j < n) v = mask_at(P, mb, s_moff[r], c0 + j, qp0);
       msk[e] = v;
       if (v > P.mask_skip) {
         lo = min(lo, j);
@@ -1433,6 +1456,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
   const char* mb = dres(P.mask.p, argtab);
+  const int qp0 = mask_qpos0(P, argtab);
   const float* mf = (const float*)mb;
   if (threadIdx.x < PF_ROWS) {
     const int r = threadIdx.x < nrows ? threadIdx.x : 0;
@@ -1462,7 +1486,6 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
       else ((uint16_t*)Qs)[r * ROW + c] = (uint16_t)val[u];
     }
   }
-  const int64_t ms3 = P.mask.stride[3];
   const int nchunks = (P.T + PF_CH - 1) / PF_CH;
   // live chunks: one warp per chunk, stopping at the first position above mask_skip
   for (int ch = warp; ch < nchunks; ch += 8) {
@@ -1475,7 +1498,11 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
           const int e = e0 + 32 * u + lane;
           const int64_t pos = c0 + 4 * (e & 15);
           if (e < nrows * 16 && pos < P.T) {
-            const float4 m4 = *(const float4*)(mf + moff_s[e >> 4] + pos);
+            const float4 m4 = P.mask_mode ? make_float4(mask_at(P, mb, moff_s[e >> 4], pos, qp0),
+                                                        mask_at(P, mb, moff_s[e >> 4], pos + 1, qp0),
+                                                        mask_at(P, mb, moff_s[e >> 4], pos + 2, qp0),
+                                                        mask_at(P, mb, moff_s[e >> 4], pos + 3, qp0))
+                                          : *(const float4*)(mf + moff_s[e >> 4] + pos);
             any |= fmaxf(fmaxf(m4.x, m4.y), fmaxf(m4.z, m4.w)) > P.mask_skip;
           }
         }
@@ -1487,7 +1514,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         for (int u = 0; u < 4; ++u) {
           const int e = e0 + 32 * u + lane;
           const int64_t pos = c0 + (e % PF_CH);
-          if (e < nrows * PF_CH && pos < P.T && ld_any(mb, moff_s[e / PF_CH] + pos * ms3, P.mask.dt) > P.mask_skip)
+          if (e < nrows * PF_CH && pos < P.T && mask_at(P, mb, moff_s[e / PF_CH], pos, qp0) > P.mask_skip)
             any = true;
         }
         if (__any_sync(0xffffffffu, any)) break;
@@ -1530,7 +1557,10 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
         const int r = q >> 4, sg = q & 15;
         const int64_t pos = c0 + 4 * sg;
         float* md = Ms + ((size_t)buf * PF_ROWS + r) * PF_MROW + 4 * sg;
-        if (r < nrows && pos < P.T) cp_async16(md, mf + moff_s[r] + pos);
+        if (r < nrows && pos < P.T && P.mask_mode)
+          *(float4*)md = make_float4(mask_at(P, mb, moff_s[r], pos, qp0), mask_at(P, mb, moff_s[r], pos + 1, qp0),
+                                     mask_at(P, mb, moff_s[r], pos + 2, qp0), mask_at(P, mb, moff_s[r], pos + 3, qp0));
+        else if (r < nrows && pos < P.T) cp_async16(md, mf + moff_s[r] + pos);
         else *(float4*)md = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
       }
     }
@@ -1642,7 +1672,7 @@ __global__ void __launch_bounds__(256, 1) attn_tc_prefill_kernel(const __grid_co
             const int64_t j = c + 8 * tile + 2 * t + e;
             float v = -INFINITY;
             if (r < nrows && j < P.T) {
-              const float mk = ld_any(mb, moff_s[r] + j * ms3, P.mask.dt);
+              const float mk = mask_at(P, mb, moff_s[r], j, qp0);
               if (mk > skip) v = rnd_dt(apply_chain(P, rnd_dt(sc[n][2 * hr + e], P.dt_d1)) + mk, P.dt_m);
             }
             sc[n][2 * hr + e] = v;
@@ -1783,9 +1813,12 @@ constexpr int PF_SMEM_MAX = 227 * 1024 - 20 * 1024;  // the opt-in limit less th
 // the specialised form applies: f32 mask with 16-byte aligned rows, f32
 // softmax arithmetic, a closed-form chain, and the mask tiles fit
 bool prefill_fast(const AttnParams& p) {
-  if (p.mask.dt != KDT_F32 || p.mask.stride[3] != 1 || (p.mask.p.off % 16) || (p.T % 4)) return false;
-  for (int d = 0; d < 3; ++d)
-    if (p.mask.stride[d] % 4) return false;
+  if (p.T % 4) return false;
+  if (!p.mask_mode) {  // a computed mask has no rows to load
+    if (p.mask.dt != KDT_F32 || p.mask.stride[3] != 1 || (p.mask.p.off % 16)) return false;
+    for (int d = 0; d < 3; ++d)
+      if (p.mask.stride[d] % 4) return false;
+  }
   if (p.dt_m != KDT_F32 || p.dt_sub != KDT_F32 || p.dt_exp != KDT_F32) return false;
   if (!(p.dt_d1 == KDT_BF16 || p.dt_d1 == KDT_F32)) return false;
   if (!(p.chain_kind == 2 || (p.chain_kind == 1 && (p.chain_dt == KDT_BF16 || p.chain_dt == KDT_F32)))) return false;
@@ -1988,7 +2021,13 @@ void verify_attention(const Launch& l, const RegionFn& region) {
   vext(p.q, "q");
   vext(p.k, "k");
   vext(p.v, "v");
-  vext(p.mask, "mask");
+  if (p.mask_mode) {
+    if (p.has_mask_pos) region(p.mask_pos, 4, "mask position");
+    if (p.mask.stride[0] || p.mask.stride[1] || p.mask.stride[2] != 1 || p.mask.stride[3] || p.mask_mode != 1)
+      fail(E_INTERNAL, "computed attention mask with a bad view");
+  } else {
+    vext(p.mask, "mask");
+  }
   int64_t rows = (int64_t)p.B * p.nq * p.Sq;
   region(p.out, rows * p.hd * (int64_t)dt_size((DT)p.out_dt), "out");
   if (p.splits > 1) region(p.part, attention_part_bytes(p), "partials");

@@ -16,6 +16,10 @@
 // reshape(broadcast_in_dim(cache, [0,1,3,4])).  Every interior value must have
 // no other consumer, so replacing the block by one kernel is exact.
 #include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <set>
 
 #include "fast_kernels.h"
@@ -210,6 +214,308 @@ std::vector<AttnMatch> match_attention(const Graph& g, const std::vector<char>& 
     out.push_back(am);
   }
   return out;
+}
+
+// ---------------------------------------------------------------------------
+// Mask forms.  generate-causal-mask (attention.clj:189-224) prints either a
+// chain over iotas and the traced position,
+//   d = j - (i + p);  m = select(d > 0, -1e4, 0);  [m = select(d < -W, -1e4, m)]
+// viewed up to the attention's [B, nq, Sq, T] operand, or (numeric position,
+// static sizes) the same values as a dense [1, 1, Sq, T] literal.  Both are
+// recognised exactly: the chain by an affine analysis of d over the operand's
+// coordinates, the literal by checking every element.
+namespace {
+
+struct Aff {
+  std::vector<int64_t> coef;  // per axis of the node: value += coef[a] * coordinate a
+  int64_t cp = 0;             // times the position
+  int pparam = -1;            // graph parameter holding the position (element 0)
+  int64_t c0 = 0;
+  bool same(const Aff& o) const {
+    return coef == o.coef && cp == o.cp && c0 == o.c0 && (cp == 0 || pparam == o.pparam);
+  }
+};
+
+struct MaskAn {
+  const Graph& g;
+  const Node& N(int i) const { return g.nodes[i]; }
+  static bool is_view(const Graph& g, int i) {
+    const Node& n = g.nodes[i];
+    return n.op == Op::Reshape || n.op == Op::Broadcast || n.op == Op::Transpose ||
+           (n.op == Op::Convert && g.nodes[n.in[0]].dt == n.dt);
+  }
+  // a one-element constant (splat or dense), through views and exact converts
+  bool scalar(int x, double& v) const {
+    const Node& n = N(x);
+    if (n.op == Op::Constant) {
+      if (n.splat) { v = n.splat_val; return true; }
+      if (n.numel() != 1) return false;
+      switch (n.dt) {
+        case DT::F32: { float f; memcpy(&f, n.data.data(), 4); v = f; return true; }
+        case DT::I32: { int32_t i; memcpy(&i, n.data.data(), 4); v = i; return true; }
+        case DT::F64: { memcpy(&v, n.data.data(), 8); return true; }
+        default: return false;
+      }
+    }
+    if (is_view(g, x) || n.op == Op::Slice) return scalar(n.in[0], v);
+    if (n.op == Op::Convert && scalar(n.in[0], v)) {
+      if (n.dt == DT::F32) return (double)(float)v == v;
+      if (n.dt == DT::I32) return (double)(int32_t)v == v;
+      return false;
+    }
+    return false;
+  }
+  // maps per-axis coefficients of a view's operand onto the view's axes
+  bool view_map(int x, const std::vector<int64_t>& in, std::vector<int64_t>& out) const {
+    const Node& n = N(x);
+    const Node& src = N(n.in[0]);
+    out.assign(n.rank(), 0);
+    switch (n.op) {
+      case Op::Convert: out = in; return true;
+      case Op::Transpose:
+        for (int a = 0; a < n.rank(); ++a) out[a] = in[n.ia[a]];
+        return true;
+      case Op::Broadcast:
+        for (int a = 0; a < src.rank(); ++a) out[n.ia[a]] = src.shape[a] == 1 ? 0 : in[a];
+        return true;
+      case Op::Reshape: {
+        std::vector<int> ai, ao;
+        for (int a = 0; a < src.rank(); ++a) if (src.shape[a] != 1) ai.push_back(a);
+        for (int a = 0; a < n.rank(); ++a) if (n.shape[a] != 1) ao.push_back(a);
+        bool aligned = ai.size() == ao.size();
+        for (size_t k = 0; aligned && k < ai.size(); ++k) aligned = src.shape[ai[k]] == n.shape[ao[k]];
+        if (aligned) {
+          for (size_t k = 0; k < ai.size(); ++k) out[ao[k]] = in[ai[k]];
+          return true;
+        }
+        for (int a : ai) if (in[a] != 0) return false;  // merged / split axes of a varying value
+        return true;
+      }
+      default: return false;
+    }
+  }
+  bool aff(int x, Aff& a, int depth = 0) const {
+    if (depth > 64) return false;
+    const Node& n = N(x);
+    a = Aff{};
+    a.coef.assign(n.rank(), 0);
+    double v;
+    if (scalar(x, v)) {
+      if (v != std::floor(v) || std::fabs(v) > (double)(1 << 23)) return false;
+      a.c0 = (int64_t)v;
+      return true;
+    }
+    switch (n.op) {
+      case Op::Iota:
+        if (n.i0 < 0 || n.i0 >= n.rank() || n.shape[n.i0] > (1 << 23)) return false;
+        a.coef[n.i0] = 1;
+        return true;
+      case Op::Param:
+        if (n.numel() != 1 || n.dt != DT::I32) return false;
+        a.cp = 1;
+        a.pparam = x;
+        return true;
+      case Op::Slice: {
+        // element 0 of an i32 parameter (the first column of pos / pos_ids)
+        const Node& src = N(n.in[0]);
+        if (n.numel() != 1 || src.op != Op::Param || src.dt != DT::I32) return false;
+        for (int64_t s0 : n.ia) if (s0 != 0) return false;
+        a.cp = 1;
+        a.pparam = n.in[0];
+        return true;
+      }
+      case Op::Convert: {
+        // integer values stay exact through i32 / f32 / f64 (|value| < 2^24)
+        if (!(n.dt == DT::F32 || n.dt == DT::I32 || n.dt == DT::F64 || n.dt == DT::I64)) return false;
+        const DT s = N(n.in[0]).dt;
+        if (!(s == DT::F32 || s == DT::I32 || s == DT::F64 || s == DT::I64)) return false;
+        return aff(n.in[0], a, depth + 1);
+      }
+      case Op::Reshape: case Op::Broadcast: case Op::Transpose: {
+        Aff in;
+        if (!aff(n.in[0], in, depth + 1)) return false;
+        std::vector<int64_t> c;
+        if (!view_map(x, in.coef, c)) return false;
+        a = in;
+        a.coef = c;
+        return true;
+      }
+      case Op::Add: case Op::Sub: {
+        Aff l, r;
+        if (!aff(n.in[0], l, depth + 1) || !aff(n.in[1], r, depth + 1)) return false;
+        if (l.coef.size() != r.coef.size()) return false;
+        const int64_t sg = n.op == Op::Add ? 1 : -1;
+        if (l.cp && r.cp && l.pparam != r.pparam) return false;
+        a.coef = l.coef;
+        for (size_t k = 0; k < a.coef.size(); ++k) a.coef[k] += sg * r.coef[k];
+        a.cp = l.cp + sg * r.cp;
+        a.pparam = a.cp ? (l.cp ? l.pparam : r.pparam) : -1;
+        a.c0 = l.c0 + sg * r.c0;
+        return true;
+      }
+      case Op::Neg: {
+        if (!aff(n.in[0], a, depth + 1)) return false;
+        for (auto& c : a.coef) c = -c;
+        a.cp = -a.cp;
+        a.c0 = -a.c0;
+        return true;
+      }
+      default: return false;
+    }
+  }
+  // value = mv where d > gt or d < lt, else z (d affine over the node's axes)
+  struct Piece {
+    Aff d;
+    bool has_gt = false, has_lt = false, cst = false;
+    int64_t gt = 0, lt = 0;
+    double mv = 0, z = 0;
+  };
+  bool piece(int x, Piece& f, int depth = 0) const {
+    if (depth > 8) return false;
+    double v;
+    if (scalar(x, v)) {
+      f = Piece{};
+      f.cst = true;
+      f.z = v;
+      return true;
+    }
+    const Node& n = N(x);
+    if (n.op != Op::Select) return false;
+    const Node& c = N(n.in[0]);
+    double mv;
+    if (c.op != Op::Compare || !scalar(n.in[1], mv)) return false;
+    Piece inner;
+    if (!piece(n.in[2], inner, depth + 1)) return false;
+    int dir = (int)c.i0;
+    double k;
+    Aff d;
+    if (scalar(c.in[1], k)) {
+      if (!aff(c.in[0], d)) return false;
+    } else if (scalar(c.in[0], k)) {  // constant on the left: mirror the direction
+      if (!aff(c.in[1], d)) return false;
+      dir = dir == CMP_GT ? CMP_LT : dir == CMP_LT ? CMP_GT : dir == CMP_GE ? CMP_LE : dir == CMP_LE ? CMP_GE : dir;
+    } else {
+      return false;
+    }
+    if (k != std::floor(k) || std::fabs(k) > (double)(1 << 23)) return false;
+    if (d.coef.size() != (size_t)n.rank()) return false;
+    if (inner.cst) {
+      f = Piece{};
+      f.d = d;
+      f.z = inner.z;
+    } else {
+      if (!inner.d.same(d) || inner.mv != mv) return false;
+      f = inner;
+    }
+    f.mv = mv;
+    const int64_t ki = (int64_t)k;
+    if (dir == CMP_GT || dir == CMP_GE) {
+      if (f.has_gt) return false;
+      f.has_gt = true;
+      f.gt = dir == CMP_GT ? ki : ki - 1;
+    } else if (dir == CMP_LT || dir == CMP_LE) {
+      if (f.has_lt) return false;
+      f.has_lt = true;
+      f.lt = dir == CMP_LT ? ki : ki + 1;
+    } else {
+      return false;
+    }
+    return true;
+  }
+};
+
+}  // namespace
+
+bool match_mask_form(const Graph& g, int mask, int64_t Sq, int64_t T, MaskForm& f) {
+  MaskAn an{g};
+  const Node& M = g.nodes[mask];
+  if (M.rank() != 4 || M.shape[2] != Sq || M.shape[3] != T || M.dt != DT::F32) return false;
+  if (Sq >= (1 << 23) || T >= (1 << 23)) return false;
+  // views from the operand down to the value that defines the mask
+  std::vector<int> views;
+  int base = mask;
+  while (MaskAn::is_view(g, base)) {
+    views.push_back(base);
+    base = g.nodes[base].in[0];
+    if (views.size() > 16) return false;
+  }
+  auto lift = [&](std::vector<int64_t> c, std::vector<int64_t>& out) {
+    for (size_t k = views.size(); k-- > 0;) {
+      std::vector<int64_t> o;
+      if (!an.view_map(views[k], c, o)) return false;
+      c.swap(o);
+    }
+    out = c;
+    return true;
+  };
+  const Node& Bn = g.nodes[base];
+  if (Bn.op == Op::Constant && !Bn.splat && Bn.dt == DT::F32) {
+    // a literal (the printer emits it flat and reshapes it: the reshapes right
+    // above it only reinterpret its row-major data); its last two axes must
+    // become the operand's query and key axes
+    std::vector<int64_t> lshape = Bn.shape;
+    while (!views.empty() && g.nodes[views.back()].op == Op::Reshape) {
+      lshape = g.nodes[views.back()].shape;
+      views.pop_back();
+    }
+    const int r = (int)lshape.size();
+    if (r < 2) return false;
+    const int64_t ls = lshape[r - 2], lt = lshape[r - 1];
+    if (Bn.numel() != ls * lt || lt != T || !(ls == Sq || Sq == 1)) return false;
+    std::vector<int64_t> ei(r, 0), ej(r, 0), oi, oj;
+    ei[r - 2] = 1;
+    ej[r - 1] = 1;
+    if (!lift(ei, oi) || !lift(ej, oj)) return false;
+    if (oj != std::vector<int64_t>{0, 0, 0, 1}) return false;
+    if (Sq > 1 && oi != std::vector<int64_t>{0, 0, 1, 0}) return false;
+    if (ls != Sq) return false;
+    const float* v = (const float*)Bn.data.data();
+    float hi = -INFINITY, lo = INFINITY;
+    for (int64_t e = 0; e < ls * lt; ++e) {
+      if (!std::isfinite(v[e])) return false;
+      hi = std::max(hi, v[e]);
+      lo = std::min(lo, v[e]);
+    }
+    if (!(lo < hi)) return false;
+    // unmasked (the larger value) positions must be exactly d = j - i in [dlo, dhi]
+    int64_t dlo = INT64_MAX, dhi = INT64_MIN;
+    for (int64_t i = 0; i < ls; ++i)
+      for (int64_t j = 0; j < lt; ++j) {
+        const float x = v[i * lt + j];
+        if (x != hi && x != lo) return false;
+        if (x == hi) { dlo = std::min(dlo, j - i); dhi = std::max(dhi, j - i); }
+      }
+    for (int64_t i = 0; i < ls; ++i)
+      for (int64_t j = 0; j < lt; ++j)
+        if ((v[i * lt + j] == hi) != (j - i >= dlo && j - i <= dhi)) return false;
+    f = MaskForm{};
+    f.off = 0;
+    f.gt = dhi;
+    f.has_lt = dlo > -(ls - 1);
+    f.lt = f.has_lt ? dlo : 0;
+    f.mv = lo;
+    f.z = hi;
+    return true;
+  }
+  MaskAn::Piece p;
+  if (!an.piece(base, p) || p.cst || !p.has_gt) return false;
+  std::vector<int64_t> c;
+  if (!lift(p.d.coef, c)) return false;
+  // d must be j - qi - pos + c0 over the operand's axes
+  if (c[3] != 1 || c[0] != 0 || c[1] != 0) return false;
+  if (Sq > 1 && c[2] != -1) return false;
+  if (!(p.d.cp == -1 || p.d.cp == 0)) return false;
+  if (std::fabs(p.mv) > 3.0e38 || std::fabs(p.z) > 3.0e38 || (double)(float)p.mv != p.mv || (double)(float)p.z != p.z)
+    return false;
+  f = MaskForm{};
+  f.pos_param = p.d.cp ? p.d.pparam : -1;
+  f.off = -p.d.c0;
+  f.gt = p.gt;
+  f.has_lt = p.has_lt;
+  f.lt = p.lt;
+  f.mv = (float)p.mv;
+  f.z = (float)p.z;
+  return std::llabs(f.off) < (1 << 23) && std::llabs(f.gt) < (1 << 23) && std::llabs(f.lt) < (1 << 23);
 }
 
 }  // namespace cljxla

@@ -549,9 +549,10 @@ size_t cljxla_b200_profile_dump(char* out, size_t cap) {
 int cljxla_b200_plan_info(const PJRT_LoadedExecutable* ex, int64_t* info, int n) {
   if (!ex || !info) return -1;
   const Plan* pl = ex->inplace.plan ? ex->inplace.plan.get() : ex->copy.plan.get();  // the variant normally run
-  int64_t v[7] = {(int64_t)pl->launches.size(), pl->arena_bytes, pl->n_nodes,
-                  pl->n_live, pl->n_fused_groups, (int64_t)pl->const_blob.size(), pl->n_jit_missing};
-  for (int i = 0; i < n && i < 7; ++i) info[i] = v[i];
+  int64_t v[8] = {(int64_t)pl->launches.size(), pl->arena_bytes, pl->n_nodes,
+                  pl->n_live, pl->n_fused_groups, (int64_t)pl->const_blob.size(), pl->n_jit_missing,
+                  pl->n_mask_computed};
+  for (int i = 0; i < n && i < 8; ++i) info[i] = v[i];
   return 0;
 }
 
@@ -564,7 +565,7 @@ void* cljxla_b200_buffer_device_pointer(const PJRT_Buffer* b) { return b ? b->pt
 extern "C" {
 
 // Parses and plans MLIR text without touching a device (host-side checks).
-// info[0..6) as cljxla_b200_plan_info.  Returns 0, or the PJRT error code with
+// info[0..8) as cljxla_b200_plan_info (index 6, the kernels still to compile, is 0).  Returns 0, or the PJRT error code with
 // the message copied into err.
 CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, int64_t* info, int n, char* err,
                                         size_t errcap) {
@@ -574,9 +575,9 @@ CLJXLA_EXPORT int cljxla_b200_plan_text(const char* text, size_t len, int fuse, 
     po.fuse = (fuse & 1) != 0;        // bit 0: fusion
     po.kv_in_place = (fuse & 2) != 0;  // bit 1: in-place KV-cache updates
     auto p = build_plan(*g, po);
-    int64_t v[6] = {(int64_t)p->launches.size(), p->arena_bytes, p->n_nodes, p->n_live, p->n_fused_groups,
-                    (int64_t)p->const_blob.size()};
-    for (int i = 0; i < n && i < 6; ++i) info[i] = v[i];
+    int64_t v[8] = {(int64_t)p->launches.size(), p->arena_bytes, p->n_nodes, p->n_live, p->n_fused_groups,
+                    (int64_t)p->const_blob.size(), 0, p->n_mask_computed};
+    for (int i = 0; i < n && i < 8; ++i) info[i] = v[i];
     return 0;
   } catch (const Error& e) {
     if (err && errcap) snprintf(err, errcap, "%s", e.what());

@@ -19,6 +19,7 @@
 #include "fast_kernels.h"
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <functional>
 #include <map>
@@ -205,6 +206,7 @@ class Planner {
   std::vector<std::vector<int>> users_;
   std::vector<std::vector<int>> ins_;         // operands (fused kernels override the graph's)
   std::map<int, AttnMatch> attn_;             // probs.V dot -> matched attention block
+  std::map<int, MaskForm> mask_form_;         // probs.V dot -> its mask, proven a causal / window form
   std::map<int, int> argmax_;                 // final i32 reduce of a printed argmax -> the float logits it reads
   int match_argmax(int r) const;
   std::vector<RowRegion> regions_;
@@ -1473,7 +1475,35 @@ void Planner::emit_attention(int d2) {
   P.q = view_of(am.q);
   P.k = view_of(am.kc);
   P.v = view_of(am.vc);
-  P.mask = view_of(am.mask);
+  if (mask_form_.count(d2)) {
+    const MaskForm& f = mask_form_.at(d2);
+    P.mask_mode = 1;
+    P.mask_gt = (int32_t)f.gt;
+    P.mask_lt = f.has_lt ? (int32_t)f.lt : INT32_MIN;
+    P.mask_off = (int32_t)f.off;
+    P.mask_mv = f.mv;
+    P.mask_z = f.z;
+    if (f.pos_param >= 0) {
+      P.mask_pos = view_of(f.pos_param).p;
+      P.has_mask_pos = 1;
+    }
+    // a view whose row offset is the query index (never dereferenced)
+    P.mask = P.q;
+    P.mask.dt = kdt(DT::F32);
+    P.mask.rank = 4;
+    const int64_t shp[4] = {D2.shape[0], D2.shape[1], D2.shape[2], K.shape[2]}, str[4] = {0, 0, 1, 0};
+    for (int i = 0; i < 4; ++i) {
+      P.mask.shape[i] = shp[i];
+      P.mask.stride[i] = str[i];
+    }
+    plan_.n_mask_computed++;
+    if (getenv("CLJXLA_B200_DEBUG_ATTN"))
+      fprintf(stderr, "attention %s: computed mask gt %lld lt %s%lld off %lld mv %g z %g pos %s\n", D2.name.c_str(),
+              (long long)f.gt, f.has_lt ? "" : "none ", (long long)f.lt, (long long)f.off, (double)f.mv, (double)f.z,
+              f.pos_param >= 0 ? g_.nodes[f.pos_param].name.c_str() : "-");
+  } else {
+    P.mask = view_of(am.mask);
+  }
   P.B = (int32_t)D2.shape[0];
   P.nq = (int32_t)D2.shape[1];
   P.Sq = (int32_t)D2.shape[2];
@@ -2283,7 +2313,17 @@ void Planner::run() {
     // fused attention: the matched block's interior disappears, the probs.V
     // dot becomes one kernel reading q, the K/V caches and the mask
     for (AttnMatch& am : match_attention(g_, live_, users_)) {
-      ins_[am.d2] = {am.q, am.kc, am.vc, am.mask};
+      // a mask of the printed causal / sliding-window form is computed in the
+      // kernel from the position: its chain (or literal) leaves the plan
+      MaskForm mf;
+      if (!getenv_off("CLJXLA_B200_MASK_FORM") &&
+          match_mask_form(g_, am.mask, g_.nodes[am.d2].shape[2], g_.nodes[am.kc].shape[2], mf)) {
+        mask_form_[am.d2] = mf;
+        ins_[am.d2] = {am.q, am.kc, am.vc};
+        if (mf.pos_param >= 0) ins_[am.d2].push_back(mf.pos_param);
+      } else {
+        ins_[am.d2] = {am.q, am.kc, am.vc, am.mask};
+      }
       attn_[am.d2] = am;
     }
     if (!attn_.empty()) liveness();

@@ -114,6 +114,7 @@ struct Plan {
   // outs[i] may alias param alias_param[i] (in-place dynamic_update_slice), else -1
   std::vector<int> out_alias_param;
   int n_nodes = 0, n_live = 0, n_fused_groups = 0;
+  int n_mask_computed = 0;  // attention launches whose mask is computed in the kernel, not read
   int n_jit_missing = 0;  // launches with a compiled form that did not compile (interpreting fallback runs)
   std::vector<int64_t> tmp_offsets;  // arena offset of each scratch buffer
   std::vector<int64_t> tmp_bytes;    // size of each scratch buffer

@@ -190,7 +190,11 @@ bool accesses(const Plan& p, const Launch& l, std::vector<Access>& out) {
         c.view(a.q, false);
         c.view(a.k, false);
         c.view(a.v, false);
-        c.view(a.mask, false);
+        if (a.mask_mode) {
+          if (a.has_mask_pos) c.add(a.mask_pos, 4, false);
+        } else {
+          c.view(a.mask, false);
+        }
         if (a.splits > 1) c.add(a.part, part, true);
         if (a.splits == 1 || a.use_counters) c.add(a.out, rows * a.hd * (int64_t)dt_size((DT)a.out_dt), true);
         if (a.splits > 1 && a.use_counters)

@@ -150,9 +150,10 @@ def kernel_launches(ctx: Context) -> int:
 def plan_info(ctx: Context, exe: dict) -> dict:
     f = _lib(ctx).cljxla_b200_plan_info
     f.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
-    info = (ctypes.c_int64 * 7)()
-    f(ctypes.c_void_p(exe["handle"]), info, 7)
-    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes", "jit_missing"]
+    info = (ctypes.c_int64 * 8)()
+    f(ctypes.c_void_p(exe["handle"]), info, 8)
+    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes", "jit_missing",
+            "computed_masks"]
     return dict(zip(keys, list(info)))
 
 
@@ -236,11 +237,12 @@ def plan_text(lib_path: str, text: str, fuse: bool = True) -> dict:
                   ctypes.c_char_p, ctypes.c_size_t]
     f.restype = ctypes.c_int
     b = text.encode()
-    info = (ctypes.c_int64 * 6)()
+    info = (ctypes.c_int64 * 8)()
     err = ctypes.create_string_buffer(4096)
     flags = int(fuse) if not isinstance(fuse, bool) else (1 if fuse else 0)  # bit 0 fusion, bit 1 in-place KV
-    rc = f(b, len(b), flags, info, 6, err, 4096)
+    rc = f(b, len(b), flags, info, 8, err, 4096)
     if rc != 0:
         raise RuntimeError(f"plan failed ({rc}): {err.value.decode()}")
-    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes"]
+    keys = ["launches", "arena_bytes", "nodes", "live_nodes", "fused_groups", "const_bytes", "jit_missing",
+            "computed_masks"]
     return dict(zip(keys, list(info)))

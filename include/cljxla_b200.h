@@ -52,7 +52,9 @@ CLJXLA_EXPORT size_t cljxla_b200_profile_dump(char* out, size_t cap);
 
 /* info[0..n): launches, scratch bytes, graph nodes, live nodes, fused
  * elementwise groups, constant bytes, launches whose compiled (NVRTC) form
- * failed so that an interpreting kernel runs instead.  Returns 0 on success. */
+ * failed so that an interpreting kernel runs instead, attention launches whose
+ * causal / sliding-window mask is computed in the kernel instead of read.
+ * Returns 0 on success. */
 CLJXLA_EXPORT int cljxla_b200_plan_info(const PJRT_LoadedExecutable* exec, int64_t* info, int n);
 
 /* Parses and plans MLIR text on the host only (no device needed).  `fuse`
