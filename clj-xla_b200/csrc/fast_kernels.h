@@ -140,7 +140,11 @@ struct AttnParams {
   int32_t mask_mode, mask_gt, mask_lt, mask_off;
   float mask_mv, mask_z;
   DPtr mask_pos;
-  int32_t has_mask_pos, pad_m;
+  int32_t has_mask_pos;
+  // staged decode with a computed mask whose masked positions are skipped: the
+  // splits share the live positions [qpos + mask_lt, qpos + mask_gt] evenly
+  // instead of covering [0, T) in dec_per_split blocks
+  int32_t dec_live_splits;
   EwInstr chain[12];
   // the chain in closed form where it is one (kernels skip the interpreter):
   // 0 general, 1 a multiply by chain_c rounded to chain_dt, 2 identity

@@ -1086,7 +1086,19 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bk = blockIdx.y, b = bk / P.nkv, kh = bk % P.nkv;
   const int nqv = P.group;  // Sq == 1: one query vector per head of the group
-  const int64_t t0 = (int64_t)blockIdx.x * P.dec_per_split, t1 = min((int64_t)P.T, t0 + P.dec_per_split);
+  // a computed mask needs only the position (a graph parameter, never written
+  // by a plan kernel): read it before the dependency wait
+  const int qp0 = mask_qpos0(P, argtab);
+  int64_t t0 = (int64_t)blockIdx.x * P.dec_per_split, t1 = min((int64_t)P.T, t0 + P.dec_per_split);
+  if (P.dec_live_splits) {
+    // the live positions [lo, hi] spread evenly over the splits
+    const int64_t lo = max((int64_t)0, (int64_t)qp0 + P.mask_lt);
+    const int64_t hi = min((int64_t)P.T - 1, (int64_t)qp0 + P.mask_gt);
+    const int64_t n = max((int64_t)0, hi - lo + 1), per = (n + P.splits - 1) / P.splits;
+    t0 = min(hi + 1, lo + (int64_t)blockIdx.x * per);
+    t1 = min(hi + 1, t0 + per);
+    if (n == 0) t0 = t1 = 0;
+  }
   const uint16_t* kbase = (const uint16_t*)dres(P.k.p, argtab) + b * P.k.stride[0] + kh * P.k.stride[1];
   const uint16_t* vbase = (const uint16_t*)dres(P.v.p, argtab) + b * P.v.stride[0] + kh * P.v.stride[1];
   const int64_t ks = P.k.stride[2], vs = P.v.stride[2];
@@ -1133,9 +1145,6 @@ __global__ void __launch_bounds__(DEC_THREADS) attn_dec_kernel(const __grid_cons
     s_m[threadIdx.x] = -INFINITY;
     s_l[threadIdx.x] = 0.f;
   }
-  // a computed mask needs only the position (a graph parameter, never written
-  // by a plan kernel): read it before the dependency wait
-  const int qp0 = mask_qpos0(P, argtab);
   __syncthreads();
   pdl_enter();
   unsigned* status = P.has_status ? (unsigned*)dres(P.status, argtab) : nullptr;
@@ -2051,6 +2060,8 @@ void verify_attention(const Launch& l, const RegionFn& region) {
       region(p.hint[h], p.hint_bytes[h], "prefetched weights");
     }
   }
+  if (p.dec_live_splits && (p.use_tc != 3 || p.mask_mode != 1))
+    fail(E_INTERNAL, "live-position splits without a computed mask");
   if (p.use_tc == 2 && (!attention_tc_prefill_ok(p) || p.splits != 1))
     fail(E_INTERNAL, "tensor-core prefill attention on unsupported views");
   if (p.q.shape[0] != p.B || p.q.shape[1] != p.nq || p.q.shape[2] != p.Sq || p.q.shape[3] != p.hd ||

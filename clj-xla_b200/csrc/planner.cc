@@ -1622,6 +1622,8 @@ void Planner::emit_attention(int d2) {
   if (P.Sq == 1 && attention_dec_ok(P) && !getenv_off("CLJXLA_B200_ATTN_DEC")) {
     P.use_tc = 3;
     plan_attention_dec(P, 148);
+    P.dec_live_splits = P.mask_mode && P.mask_mv <= P.mask_skip && P.mask_z > P.mask_skip &&
+                        !getenv_off("CLJXLA_B200_ATTN_LIVE_SPLITS");
     splits = P.splits;
     if (getenv("CLJXLA_B200_DEBUG_ATTN"))
       fprintf(stderr, "attention %s: staged decode, %d splits of %d positions, chunk %d\n", D2.name.c_str(), P.splits,

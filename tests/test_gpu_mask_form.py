@@ -90,6 +90,10 @@ def test_computed_mask_is_bit_exact(ctx, monkeypatch, case):
     cfg = TINY[family]
     for k, v in env.items():
         monkeypatch.setenv(k, v)
+    # the staged decode kernel spreads the live positions of a computed mask over
+    # its splits (another summation grouping, checked against the oracle in the
+    # model tests); here both plans split [0, T) alike
+    monkeypatch.setenv("CLJXLA_B200_ATTN_LIVE_SPLITS", "0")
     n = P if kind == "prefill" else 1
     graph = d.build_graph(cfg, kind, B, P, T, dynamic_prefill=dynamic)
     text = shlo.graph_to_mlir_text(graph)
@@ -106,3 +110,27 @@ def test_computed_mask_is_bit_exact(ctx, monkeypatch, case):
         assert a.dtype == b.dtype and a.shape == b.shape
         ok = np.array_equal(np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(b).view(np.uint8))
         assert ok, f"output {i}: computed and read masks differ ({np.sum(a != b)} elements)"
+
+
+@pytest.mark.parametrize("family,pos", [("gemma3", 300), ("gemma3", 511), ("gemma2", 200)])
+def test_live_splits_match_oracle(ctx, monkeypatch, family, pos):
+    """Staged decode over a 512-position cache (8 splits of 64 positions):
+    with a computed mask the splits share only the live positions (the
+    window on local layers, [0, pos] on global ones), and the decode step
+    still equals the oracle's."""
+    from oracle import interp
+    from test_gpu_models import _compare_all
+    cfg = TINY[family]
+    B, T = 1, 512
+    monkeypatch.delenv("CLJXLA_B200_ATTN_LIVE_SPLITS", raising=False)
+    monkeypatch.delenv("CLJXLA_B200_MASK_FORM", raising=False)
+    graph = d.build_graph(cfg, "decode", B, pos, T)
+    text = shlo.graph_to_mlir_text(graph)
+    toks = d.make_prompt(cfg, B, 1, seed=9)
+    inputs = [toks, d.pos_inputs(cfg, "decode", B, pos, 1)] + d.make_weights(cfg) + \
+        [_cache(cfg, B, T, 200 + i) for i in range(2 * cfg.layers)]
+    info, got = _run(ctx, graph, text, inputs)
+    assert info["computed_masks"] == cfg.layers
+    want = interp.run_mlir(text, inputs)
+    _compare_all(got, want, runner.out_specs(graph), f"{family} decode at {pos}, live splits", cfg.dtype,
+                 lambda sd: interp.run_mlir(text, inputs, ulp_noise_seed=sd))
