@@ -203,8 +203,9 @@ void run_launch(const Launch& l, const uint64_t* argtab, cudaStream_t s) {
                           std::to_string(g_coll.ranks));
     const char* src = (const char*)(uintptr_t)(g_coll.host_argtab[a.src.slot] + (uint64_t)a.src.off);
     char* dst = (char*)(uintptr_t)(g_coll.host_argtab[a.dst.slot] + (uint64_t)a.dst.off);
-    if (g_coll.p2p && g_coll.p2p->fits(a.count, a.dt)) g_coll.p2p->run(src, dst, a.count, a.dt, s);
-    else nccl_all_reduce_sum(src, dst, (size_t)a.count, a.dt, g_coll.comm, s);
+    // the one-shot peer kernel sums; maxima (the vocab-split greedy token) go to NCCL
+    if (a.reduce == RED_ADD && g_coll.p2p && g_coll.p2p->fits(a.count, a.dt)) g_coll.p2p->run(src, dst, a.count, a.dt, s);
+    else nccl_all_reduce(src, dst, (size_t)a.count, a.dt, a.reduce, g_coll.comm, s);
     return;
   }
   if (l.jit_fn) {

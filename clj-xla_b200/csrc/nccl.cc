@@ -3,6 +3,7 @@
 // client; the all_reduce(sum) of a plan is issued on the client's stream and
 // is captured into the executable's CUDA graph like any kernel.
 #include "nccl_rt.h"
+#include "ir.h"
 
 #include <dlfcn.h>
 #include <nccl.h>
@@ -81,15 +82,18 @@ void* nccl_comm_init(int nranks, int rank, const std::string& id_hex) {
   return (void*)comm;
 }
 
-void nccl_all_reduce_sum(const void* src, void* dst, size_t count, int kdt, void* comm, cudaStream_t s) {
+void nccl_all_reduce(const void* src, void* dst, size_t count, int kdt, int reduce, void* comm, cudaStream_t s) {
   ncclDataType_t t;
   switch (kdt) {
     case KDT_F32: t = ncclFloat32; break;
     case KDT_BF16: t = ncclBfloat16; break;
     case KDT_F16: t = ncclFloat16; break;
+    case KDT_I32: t = ncclInt32; break;
     default: fail(E_UNIMPLEMENTED, "all_reduce element type");
   }
-  check(lib().all_reduce(src, dst, count, t, ncclSum, (ncclComm_t)comm, s), "ncclAllReduce");
+  if (reduce != RED_ADD && reduce != RED_MAX) fail(E_UNIMPLEMENTED, "all_reduce reduction");
+  check(lib().all_reduce(src, dst, count, t, reduce == RED_MAX ? ncclMax : ncclSum, (ncclComm_t)comm, s),
+        "ncclAllReduce");
 }
 
 void nccl_comm_destroy(void* comm) {

@@ -11,7 +11,8 @@ namespace cljxla {
 
 std::string nccl_unique_id_hex();                                  // 256 hex characters
 void* nccl_comm_init(int nranks, int rank, const std::string& id_hex);  // a collective over all ranks
-void nccl_all_reduce_sum(const void* src, void* dst, size_t count, int kdt, void* comm, cudaStream_t s);
+// reduce: RED_ADD (sum) or RED_MAX (elementwise maximum; also for i32)
+void nccl_all_reduce(const void* src, void* dst, size_t count, int kdt, int reduce, void* comm, cudaStream_t s);
 void nccl_comm_destroy(void* comm);
 
 // One-shot all-reduce over NVLink peer memory (p2p_allreduce.cu) for messages

@@ -584,7 +584,8 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
       continue;
     }
     if (starts(rhs, "\"stablehlo.all_reduce\"(")) {
-      // tensor-parallel sum: region of one stablehlo.add, replica_groups = dense<[[0, .., n-1]]>
+      // tensor-parallel sum or maximum: region of one stablehlo.add / stablehlo.maximum,
+      // replica_groups = dense<[[0, .., n-1]]>
       sv args = rhs.substr(23);
       size_t close = args.find(')');
       auto ops = parse_operands(args.substr(0, close), line);
@@ -604,7 +605,9 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
         tail_line = trim(sv(p, (size_t)(nl2 - p)));
         p = nl2 + 1;
       }
-      if (body_line.find("stablehlo.add ") == sv::npos)
+      int64_t red = RED_ADD;
+      if (body_line.find("stablehlo.maximum ") != sv::npos) red = RED_MAX;
+      else if (body_line.find("stablehlo.add ") == sv::npos)
         fail(E_UNIMPLEMENTED, "all_reduce body not supported: " + std::string(body_line));
       if (!starts(tail_line, "})")) perr("bad all_reduce tail", tail_line);
       size_t g = tail_line.find("replica_groups = dense<[[");
@@ -618,6 +621,7 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
       Type t = parse_type(tail_line.substr(arrow + 4), tail_line);
       n.op = Op::AllReduce;
       n.i0 = count;
+      n.ia = {red};
       n.in = {lookup(ops[0], line)};
       n.shape = t.shape;
       n.dt = t.dt;

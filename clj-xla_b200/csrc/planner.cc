@@ -1835,7 +1835,9 @@ void Planner::emit_node_kernel(int id) {
       // NCCL reads and writes plain device addresses: a dense arena copy of the
       // operand in, the arena result slot out (both fixed for the executable)
       const Node& in = g_.nodes[n.in[0]];
-      if (!(n.dt == DT::F32 || n.dt == DT::BF16 || n.dt == DT::F16) || in.dt != n.dt)
+      const int red = n.ia.empty() ? RED_ADD : (int)n.ia[0];
+      if (!(n.dt == DT::F32 || n.dt == DT::BF16 || n.dt == DT::F16 || (red == RED_MAX && n.dt == DT::I32)) ||
+          in.dt != n.dt)
         fail(E_UNIMPLEMENTED, "all_reduce of element type " + std::string(dt_name(n.dt)));
       TView v = view_of(n.in[0]);
       bool dense = v.p.slot >= tmp_slot(0) && v.p.off % 16 == 0;
@@ -1851,6 +1853,7 @@ void Planner::emit_node_kernel(int id) {
       A.count = n.numel();
       A.dt = kdt(n.dt);
       A.ranks = (int32_t)n.i0;
+      A.reduce = red;
       push(K_ALLREDUCE, blob_of(A), n.name, 2 * n.numel() * (int64_t)dt_size(n.dt));
       break;
     }

@@ -23,13 +23,14 @@ enum KernelKind : int {
 };
 const char* kernel_kind_name(int k);
 
-// all_reduce(sum) of `count` elements of type dt from src into dst; both in
-// the scratch arena, whose addresses are fixed for the executable's life, so
-// the collective can be captured into the CUDA graph.
+// all_reduce (sum, or elementwise max) of `count` elements of type dt from src
+// into dst; both in the scratch arena, whose addresses are fixed for the
+// executable's life, so the collective can be captured into the CUDA graph.
 struct AllReduceParams {
   DPtr src, dst;
   int64_t count;
   int32_t dt, ranks;
+  int32_t reduce, pad_;  // RED_ADD or RED_MAX
 };
 
 // Buffers of a compiled fused kernel, passed by value at launch: buffer k is

@@ -46,6 +46,9 @@ class ModelConfig:
     window: Optional[int] = None          # local attention window
     n_positions: int = 1024               # GPT-2 learned position table
     tp: int = 1                           # tensor-parallel ranks this (per-rank) config is a shard of
+    # vocab-split LM head (greedy graphs of a tensor-parallel Gemma): this rank's
+    # index; its logits cover vocabulary rows [rank * V / tp, (rank + 1) * V / tp)
+    vocab_rank: Optional[int] = None
 
     def is_local(self, i: int) -> bool:
         if self.window is None:
@@ -80,18 +83,25 @@ def round_up(n: int, m: int) -> int:
 
 
 # ------------------------------------------------------- tensor parallelism
-def shard_config(cfg: ModelConfig, tp: int) -> ModelConfig:
+def shard_config(cfg: ModelConfig, tp: int, vocab_rank: Optional[int] = None) -> ModelConfig:
     """Per-rank config of a tensor-parallel Gemma: query / KV heads and the MLP
     width split over ``tp`` ranks (Megatron column split of q/k/v and gate/up,
-    row split of o and down), embedding, norms and LM head replicated.  An
-    addition of this repository; the reference runs on one device."""
+    row split of o and down), embedding and norms replicated.  The LM head is
+    replicated too, unless ``vocab_rank`` names this rank: then a greedy graph
+    computes the logits of its vocabulary shard only (rows of the tied
+    embedding, read in place) and the ranks agree on the token through two
+    max all-reduces (``vocab_split_greedy``).  An addition of this repository;
+    the reference runs on one device."""
     if tp == 1:
         return cfg
     if cfg.family == "gpt2":
         raise ValueError("tensor parallelism is provided for the Gemma families")
     if cfg.n_heads % tp or cfg.n_kv_heads % tp or cfg.mlp % tp:
         raise ValueError(f"heads {cfg.n_heads}/{cfg.n_kv_heads} and MLP {cfg.mlp} must divide by tp={tp}")
-    return replace(cfg, n_heads=cfg.n_heads // tp, n_kv_heads=cfg.n_kv_heads // tp, mlp=cfg.mlp // tp, tp=tp)
+    if vocab_rank is not None and (cfg.vocab % tp or not 0 <= vocab_rank < tp):
+        raise ValueError(f"vocabulary {cfg.vocab} must divide by tp={tp} (rank {vocab_rank})")
+    return replace(cfg, n_heads=cfg.n_heads // tp, n_kv_heads=cfg.n_kv_heads // tp, mlp=cfg.mlp // tp, tp=tp,
+                   vocab_rank=vocab_rank)
 
 
 def shard_weights(cfg: ModelConfig, weights: List[np.ndarray], rank: int, tp: int) -> List[np.ndarray]:
@@ -222,9 +232,15 @@ def trace_fn(cfg: ModelConfig, kind: str, prompt_len: int, dynamic_prefill: bool
             pos_ids, pos = pos_tr, t.slice(pos_tr, [0], [1], [1])
         else:
             pos_ids, pos = pos_tr, pos_tr
+        split = greedy and cfg.vocab_rank is not None
+        if split:
+            opts["lm-head-rows"] = _vocab_rows(cfg)
         logits, new_kv = full_gemma_forward(x, emb, maps, fnorm, pos_ids, cfg.n_heads, cfg.n_kv_heads,
                                             kv_seq, pos, opts)
-        out = [_greedy_token(t.convert(logits, "f32")) if greedy else t.convert(logits, "f32")]
+        if split:
+            out = [vocab_split_greedy(t.convert(logits, "f32"), _vocab_rows(cfg)[0], cfg.tp)]
+        else:
+            out = [_greedy_token(t.convert(logits, "f32")) if greedy else t.convert(logits, "f32")]
         for k, v in new_kv:
             out += [k, v]
         return out
@@ -238,6 +254,27 @@ def _greedy_token(logits):
     output, so a decode step returns 4 bytes per sequence instead of V * 4.
     Ties take the highest index (the in-graph rule), not argmax-host's lowest."""
     return t.argmax(logits, axis=-1)
+
+
+def _vocab_rows(cfg: ModelConfig):
+    """[first, last) vocabulary rows of this rank's LM-head shard."""
+    n = cfg.vocab // cfg.tp
+    return cfg.vocab_rank * n, (cfg.vocab_rank + 1) * n
+
+
+def vocab_split_greedy(logits, first_row: int, tp: int):
+    """The greedy token of a vocabulary-sharded LM head: each rank holds the
+    logits of rows [first_row, first_row + V / tp).  Its local argmax (highest
+    index on ties, tensor.clj:519-532) and local maximum go through two max
+    all-reduces: the group's maximum, then the largest global index among the
+    ranks that reach it, which is the unsharded argmax's highest-index tie
+    rule.  Replaces the replicated LM head's V x d weight read per rank by
+    V / tp x d, and the logits never leave their rank."""
+    local_max = t.reduce_max(logits, axes=[-1], keep_dims=False)
+    local_idx = t.add(t.argmax(logits, axis=-1), first_row)
+    top = t.all_reduce(local_max, tp, "max")
+    cand = t.select(t.eq(local_max, top), local_idx, -1)
+    return t.all_reduce(cand, tp, "max")
 
 
 def build_graph(cfg: ModelConfig, kind: str, batch: int, prompt_len: int, max_seq: int,

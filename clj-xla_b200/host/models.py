@@ -188,6 +188,11 @@ def full_gemma_forward(x, embed, layers, final_norm_w, pos_ids, num_heads, num_k
         for lw in layers:
             h = gemma_block(h, lw, num_heads, num_kv_heads, pos_ids)
     normed = gemma_rms_norm(h, final_norm_w, 1e-6)
+    rows = opts.get("lm-head-rows")
+    if rows is not None:
+        # vocabulary-sharded LM head (tensor parallelism, an addition of this
+        # repository): this rank's rows of the tied embedding, a view in place
+        embed = t.slice(embed, [rows[0], 0], [rows[1], hidden], [1, 1])
     embed_t = t.transpose(embed, [1, 0])
     raw = gemma_linear(normed, embed_t, None)
     fs = opts.get("final-logit-softcap", 30.0)

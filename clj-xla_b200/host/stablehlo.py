@@ -408,9 +408,10 @@ def format_equation(eqn: dict, var_types: Dict[str, str]) -> str:
         _, dt = parse_tensor_dims(it)
         n = int(attrs["replica_count"])
         ranks = ", ".join(str(i) for i in range(n))
+        body = "stablehlo.maximum" if attrs.get("reduce") == "max" else "stablehlo.add"
         return (f'    %{out} = "stablehlo.all_reduce"(%{iv}) ({{\n'
                 f"    ^bb0(%arg_a: tensor<{dt}>, %arg_b: tensor<{dt}>):\n"
-                f"      %arg_res = stablehlo.add %arg_a, %arg_b : tensor<{dt}>\n"
+                f"      %arg_res = {body} %arg_a, %arg_b : tensor<{dt}>\n"
                 f'      "stablehlo.return"(%arg_res) : (tensor<{dt}>) -> ()\n'
                 f"    }}) {{replica_groups = dense<[[{ranks}]]> : tensor<1x{n}xi64>}} : ({it}) -> {it}")
     if op == "stablehlo/dot_general":

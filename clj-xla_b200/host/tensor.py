@@ -439,15 +439,20 @@ def argmax(x, axis=-1):
     return reduce_max(masked, axes=[ax], keep_dims=False)
 
 
-def all_reduce(x, replica_count: int):
-    """Sum of ``x`` over the ``replica_count`` ranks of a tensor-parallel group.
+def all_reduce(x, replica_count: int, reduce: str = "sum"):
+    """Sum (``reduce="sum"``) or elementwise maximum (``"max"``) of ``x`` over
+    the ``replica_count`` ranks of a tensor-parallel group.
 
     An addition of this repository for tensor parallelism: the reference
     (clj-xla) has no multi-device code and its tensor API no collectives."""
+    if reduce not in ("sum", "max"):
+        raise ValueError(f"all_reduce: unsupported reduction {reduce!r}")
     tx = emit_constant(x, None)
     out_id = gen_var_id("t_allreduce")
-    _emit({"op": "stablehlo/all_reduce", "invars": [tx.id], "outvars": [out_id],
-           "attrs": {"replica_count": int(replica_count)}})
+    attrs = {"replica_count": int(replica_count)}
+    if reduce == "max":
+        attrs["reduce"] = "max"
+    _emit({"op": "stablehlo/all_reduce", "invars": [tx.id], "outvars": [out_id], "attrs": attrs})
     return Tracer(out_id, tx.type)
 
 

@@ -471,7 +471,9 @@ class Interpreter:
         if name == "all_reduce":
             if self._collective is None:
                 raise ValueError("all_reduce needs the ranks of its group (run_mlir_tp)")
-            return to_dtype(self._collective(np.asarray(args[0], np.float32)), dt)
+            kind = "max" if op.body == "stablehlo.maximum" else "sum"
+            x = np.asarray(args[0], np.int64 if dt in _INT else np.float32)
+            return to_dtype(self._collective(x, kind), dt)
         if name == "gather":
             return self._gather(op, args, shape, dt)
         if name == "reduce":
@@ -559,7 +561,8 @@ def run_mlir(text: str, inputs, keep_all=False, ulp_noise_seed=None):
 def run_mlir_tp(texts, inputs_per_rank, ulp_noise_seed=None):
     """Runs the per-rank graphs of a tensor-parallel group together, one thread
     per rank.  Each all_reduce is the sum, in f64 and in rank order, of the
-    ranks' f32 values, rounded to the result type by the caller's op."""
+    ranks' f32 values, rounded to the result type by the caller's op, or (a
+    ``stablehlo.maximum`` region) their elementwise maximum."""
     import threading
     n = len(texts)
     barrier = threading.Barrier(n)
@@ -569,14 +572,17 @@ def run_mlir_tp(texts, inputs_per_rank, ulp_noise_seed=None):
     errors = []
 
     def worker(r):
-        def collective(x):
+        def collective(x, kind="sum"):
             slots[r] = x
             barrier.wait()
             if r == 0:
-                acc = np.zeros(x.shape, np.float64)
-                for v in slots:
-                    acc += v
-                result[0] = acc
+                if kind == "max":
+                    result[0] = np.maximum.reduce([np.asarray(v) for v in slots])
+                else:
+                    acc = np.zeros(x.shape, np.float64)
+                    for v in slots:
+                        acc += v
+                    result[0] = acc
             barrier.wait()
             y = result[0]
             barrier.wait()

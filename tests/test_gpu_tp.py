@@ -105,6 +105,57 @@ def test_tp2_greedy_decode_matches_oracle(dtype, p2p):
         assert ok, f"step {i}: {bad:.2%} out of bound, rel rms {rr:.3g} (floor {fb:.2%}, {fr:.3g})"
 
 
+def _rank_vocab(rank, world, nid, cfg_full, shape, ins, q):
+    try:
+        from cljxla_b200.host import runner
+        ctx = core.init_tp_backend(world, rank, nid, device=rank)
+        B, S, T = shape
+        g = d.build_graph(d.shard_config(cfg_full, world, vocab_rank=rank), "decode", B, S, T, greedy=True)
+        out = runner.run_graph(ctx, g, ins)
+        core.close_backend(ctx)
+        q.put((rank, np.asarray(out[0]), None))
+    except Exception as e:  # noqa: BLE001 - reported by the parent
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("tie", [False, True], ids=["random", "all-tied"])
+def test_tp2_vocab_split_greedy_token(tie):
+    """A greedy decode step whose LM head is split by vocabulary rows over 2
+    ranks: the token the two max all-reduces (NCCL, f32 values and i32
+    indices) agree on equals the sharded oracle's, on both ranks, and the
+    all-tied step gives the last index."""
+    from test_tp import _split_decode_inputs
+    cfg = dataclasses.replace(TINY3, dtype="f32")
+    B, S, T, world = 2, 6, 16, 2
+    ins = _split_decode_inputs(cfg, B, S, T, world, tie=tie)
+    from cljxla_b200.host import stablehlo as shlo
+    texts = [shlo.graph_to_mlir_text(d.build_graph(d.shard_config(cfg, world, vocab_rank=r), "decode", B, S, T,
+                                                   greedy=True)) for r in range(world)]
+    want = np.asarray(interp.run_mlir_tp(texts, ins)[0][0])
+    nid = core.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_vocab, args=(r, world, nid, cfg, (B, S, T), ins[r], q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(world):
+            r, tok, err = q.get(timeout=300)
+            assert err is None, f"rank {r}: {err}"
+            got[r] = tok
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert np.array_equal(got[r], want), (r, got[r].ravel(), want.ravel())
+    if tie:
+        assert np.all(want == cfg.vocab - 1)
+
+
 def _rank_skip(rank, world, nid, q, hq, hin, go, ready, start):
     """Rank of a 2-rank group whose rank 1 leaves after the first step."""
     import os

@@ -103,6 +103,48 @@ def test_tp_oracle_matches_unsharded_oracle(dtype):
             assert rr < 0.05, rr
 
 
+def _split_decode_inputs(cfg, B, S, T, tp_n, seed=3, tie=False):
+    w = d.make_weights(cfg)
+    if tie:   # final (1 + w) norm weight -1: every logit is 0, the argmax is the last index
+        i = [n for n, _, _ in d.weight_specs(cfg)].index("final_norm_w")
+        w[i] = np.full_like(w[i], 0xBF80 if cfg.dtype == "bf16" else -1.0)
+    rng = np.random.default_rng(seed)
+    kv = [rng.standard_normal(d.cache_shape(cfg, B, T)).astype(np.float32) for _ in range(2 * cfg.layers)]
+    if cfg.dtype == "bf16":
+        kv = [d._to_bf16_bits(a) for a in kv]
+    toks = d.make_prompt(cfg, B, 1, seed=seed)
+    pos = d.pos_inputs(cfg, "decode", B, S, 1)
+    nk = cfg.n_kv_heads // tp_n
+    return [[toks, pos] + d.shard_weights(cfg, w, r, tp_n) + [a[:, r * nk:(r + 1) * nk].copy() for a in kv]
+            for r in range(tp_n)]
+
+
+@pytest.mark.parametrize("cfg,tie", [(dataclasses.replace(TINY3, dtype="f32"), False), (TINY3, False),
+                                     (TINY2, False), (TINY3, True)],
+                         ids=["gemma3-f32", "gemma3-bf16", "gemma2-softcap", "all-tied"])
+def test_vocab_split_greedy_matches_replicated_head(cfg, tie, lib_path):
+    """Greedy decode graphs with the LM head split by vocabulary rows pick the
+    same token on every rank as the replicated head, which every rank
+    computes in full: each logit is the same dot either way, and the two max
+    all-reduces keep the in-graph argmax's highest-index tie rule (the
+    all-tied case must give V - 1).  The library plans the split graphs."""
+    B, S, T, n = 2, 6, 16, 2
+    ins = _split_decode_inputs(cfg, B, S, T, n, tie=tie)
+    rep = shlo.graph_to_mlir_text(d.build_graph(d.shard_config(cfg, n), "decode", B, S, T, greedy=True))
+    want = interp.run_mlir_tp([rep] * n, ins)
+    texts = [shlo.graph_to_mlir_text(d.build_graph(d.shard_config(cfg, n, vocab_rank=r), "decode", B, S, T,
+                                                   greedy=True)) for r in range(n)]
+    assert texts[0] != texts[1]                       # the ranks slice different vocabulary rows
+    assert len(re.findall(r"%arg_res = stablehlo.maximum %arg_a, %arg_b : tensor<(f32|i32)>", texts[0])) >= 2
+    got = interp.run_mlir_tp(texts, ins)
+    for r in range(n):
+        assert np.array_equal(got[r][0], want[0][0]), (r, got[r][0].ravel(), want[0][0].ravel())
+    if tie:
+        assert np.all(np.asarray(got[0][0]) == cfg.vocab - 1)
+    for r in range(n):
+        assert core.plan_text(lib_path, texts[r])["launches"] > 0
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
