@@ -89,6 +89,58 @@ def test_switch_keeps_read_masks(lib_path):
     assert on["launches"] < info["launches"] and on["live_nodes"] < info["live_nodes"]
 
 
+def _decode_text():
+    return shlo.graph_to_mlir_text(d.build_graph(FAMILIES["gemma3"], "decode", 1, 12, 32))
+
+
+def _first(text, old, new):
+    assert old in text, old
+    return text.replace(old, new, 1)
+
+
+@pytest.mark.parametrize("mutation,layer0", [
+    # an equivalent window test: d <= -7 is d < -6
+    ("le", (0, -6)),
+    # another window: the proof reads the threshold, it does not assume it
+    ("window5", (0, -5)),
+    # d >= 0 also masks the query's own position: gt -1
+    ("ge", (-1, -6)),
+], ids=["le-is-lt", "other-window", "ge-masks-diagonal"])
+def test_mask_chain_variants_are_read_exactly(lib_path, mutation, layer0):
+    """Edits of layer 0's printed mask chain that keep it of the closed form are
+    proven with the thresholds they mean (the other layers keep theirs)."""
+    text = _decode_text()
+    if mutation == "le":
+        text = _first(text, "dense<[-6.000000e+00]>", "dense<[-7.000000e+00]>")
+        text = _first(text, "comparison_direction LT>", "comparison_direction LE>")
+    elif mutation == "window5":
+        text = _first(text, "dense<[-6.000000e+00]>", "dense<[-5.000000e+00]>")
+    else:
+        text = _first(text, "comparison_direction GT>", "comparison_direction GE>")
+    info, forms = _plan_forms(lib_path, text)
+    assert info["computed_masks"] == FAMILIES["gemma3"].layers == len(forms)
+    assert (forms[0][0], forms[0][1]) == layer0
+    assert all((f[0], f[1]) == (0, -6) for f in forms[1:5]) and forms[5][:2] == (0, None)
+
+
+def test_mask_chain_not_of_the_form_stays_read(lib_path):
+    """Layer 0's compared value turned around (i + p - j: an anti-causal mask)
+    and layer 1's position taken twice (j - i - 2p) are not the closed form:
+    those layers read their masks, the others stay computed."""
+    text = _decode_text()
+    m = re.search(r"stablehlo\.subtract %(\S+), %(\S+) : tensor<1x1x1x32xf32>", text)
+    text = text[:m.start()] + f"stablehlo.subtract %{m.group(2)}, %{m.group(1)} : tensor<1x1x1x32xf32>" + \
+        text[m.end():]
+    # layer 1: its i + p add becomes i + p + p (the position reshaped once more)
+    adds = list(re.finditer(r"%(t_add_\d+) = stablehlo\.add %(\S+), %(\S+) : tensor<1x1x1x1xf32>", text))
+    a = adds[1]
+    text = text[:a.start()] + (f"%{a.group(1)}_p = stablehlo.add %{a.group(2)}, %{a.group(3)} : tensor<1x1x1x1xf32>\n"
+                               f"    %{a.group(1)} = stablehlo.add %{a.group(1)}_p, %{a.group(3)} : "
+                               f"tensor<1x1x1x1xf32>") + text[a.end():]
+    info, forms = _plan_forms(lib_path, text)
+    assert info["computed_masks"] == FAMILIES["gemma3"].layers - 2 == len(forms)
+
+
 def test_literal_not_of_the_form_stays_read(lib_path):
     cfg = FAMILIES["gemma3"]
     text = shlo.graph_to_mlir_text(d.build_graph(cfg, "prefill", 1, 12, 32))
