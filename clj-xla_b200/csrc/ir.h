@@ -22,6 +22,11 @@ enum class Op : uint8_t {
   Reduce, Dot,
   // collectives (tensor parallelism)
   AllReduce,
+  // the NaN / Inf assertions of clj-xla's debug module (debug.clj:24-60), printed
+  // as custom_call "check_non_nan" / "check_non_inf" (stablehlo.clj:562-570); i0:
+  // 0 NaN, 1 Inf.  Their tensor<i1> result is never used by the printed graphs,
+  // so they are dropped with the rest of the dead code.
+  NanCheck,
 };
 const char* op_name(Op o);
 inline bool op_is_elementwise(Op o) { return o >= Op::Add && o <= Op::Iota; }

@@ -39,7 +39,8 @@ const char* op_name(Op o) {
                                 "minimum", "exponential", "tanh", "sqrt", "rsqrt", "sine", "cosine",
                                 "logistic", "negate", "abs", "convert", "compare", "select", "iota",
                                 "reshape", "transpose", "broadcast_in_dim", "slice", "concatenate",
-                                "dynamic_update_slice", "gather", "reduce", "dot_general", "all_reduce"};
+                                "dynamic_update_slice", "gather", "reduce", "dot_general", "all_reduce",
+                                "custom_call"};
   return names[(int)o];
 }
 
@@ -730,6 +731,16 @@ std::unique_ptr<Graph> parse_mlir(const char* text, size_t len) {
       } else if (opn == "concatenate") {
         n.op = Op::Concat;
         n.i0 = attr_int(attrs, "dimension", line);
+      } else if (opn == "custom_call") {
+        // only the debug module's assertions (stablehlo.clj:562-570)
+        size_t tp = attrs.find("call_target_name = \"");
+        sv target = tp == sv::npos ? sv() : attrs.substr(tp + 20);
+        target = target.substr(0, target.find('"'));
+        if (target == "check_non_nan") n.i0 = 0;
+        else if (target == "check_non_inf") n.i0 = 1;
+        else fail(E_UNIMPLEMENTED, "custom_call target not supported: " + std::string(target));
+        if (n.in.size() != 1 || n.dt != DT::I1 || !n.shape.empty()) perr("bad check custom_call", line);
+        n.op = Op::NanCheck;
       } else if (opn == "dot_general") {
         n.op = Op::Dot;
         n.ia = attr_list(attrs, "lhs_batching_dimensions", line, false);

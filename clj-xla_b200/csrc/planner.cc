@@ -2314,6 +2314,10 @@ void Planner::run() {
     }
   };
   liveness();
+  for (int i = 0; i < N; ++i)
+    if (live_[i] && g_.nodes[i].op == Op::NanCheck)
+      fail(E_UNIMPLEMENTED, "custom_call " + std::string(g_.nodes[i].i0 ? "check_non_inf" : "check_non_nan") +
+                                ": its result is used by the graph; the assertion is not executed on the device");
   if (opt_.fast_kernels) {
     // fused attention: the matched block's interior disappears, the probs.V
     // dot becomes one kernel reading q, the K/V caches and the mask

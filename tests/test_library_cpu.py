@@ -95,6 +95,43 @@ def test_loc_suffix_is_ignored(lib_path):
     assert core.plan_text(lib_path, txt)["launches"] >= 1
 
 
+def test_debug_checks_are_dropped_with_dead_code(lib_path):
+    """debug.clj's check-non-nan / check-non-inf print as custom_call ops
+    whose tensor<i1> result nothing uses (stablehlo.clj:562-570): a model graph
+    carrying them (with their loc suffix) plans to the same launches as without
+    them.  A check whose result the graph returns, or any other custom_call
+    target, is UNIMPLEMENTED."""
+    cfg = dataclasses.replace(d.GEMMA3_4B, vocab=64, d_model=64, layers=2, n_heads=4, n_kv_heads=2,
+                              head_dim=64, mlp=64, window=6)
+    txt = shlo.graph_to_mlir_text(d.build_graph(cfg, "decode", 1, 12, 32))
+    base = core.plan_text(lib_path, txt)
+    m = re.search(r"\n(\s*)%(t_\w+) = stablehlo\.multiply %\S+, %\S+ : (tensor<[^>]*xf32>)\n", txt)
+    ind, v, ty = m.group(1), m.group(2), m.group(3)
+    checks = (f'{ind}%chk_nan_1 = "stablehlo.custom_call"(%{v}) {{call_target_name = "check_non_nan"}} : '
+              f'({ty}) -> tensor<i1> loc("gemma/layer_0/check")\n'
+              f'{ind}%chk_inf_2 = "stablehlo.custom_call"(%{v}) {{call_target_name = "check_non_inf"}} : '
+              f'({ty}) -> tensor<i1>\n')
+    with_checks = txt[:m.end()] + checks + txt[m.end():]
+    got = core.plan_text(lib_path, with_checks)
+    assert got["launches"] == base["launches"] and got["live_nodes"] == base["live_nodes"]
+    # the oracle evaluates the checks and computes the same results
+    import numpy as np
+    from oracle import interp
+    ins = [d.make_prompt(cfg, 1, 1), d.pos_inputs(cfg, "decode", 1, 12, 1)] + d.make_weights(cfg) + \
+        [d.zero_cache(cfg, 1, 32) for _ in range(2 * cfg.layers)]
+    a, b = interp.run_mlir(txt, ins), interp.run_mlir(with_checks, ins)
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))
+    # the first result (the logits) replaced by the check
+    returned = re.sub(r"return %\w+, (.*) : tensor<[^>]*>, ", r"return %chk_nan_1, \1 : tensor<i1>, ", with_checks, 1)
+    returned = re.sub(r"\) -> \(tensor<[^>]*>, ", ") -> (tensor<i1>, ", returned, 1)
+    assert returned.count("tensor<i1>, ") >= 2
+    with pytest.raises(RuntimeError, match=r"\(12\).*check_non_nan"):
+        core.plan_text(lib_path, returned)
+    other = with_checks.replace('"check_non_inf"', '"embed_lookup"')
+    with pytest.raises(RuntimeError, match=r"\(12\).*embed_lookup"):
+        core.plan_text(lib_path, other)
+
+
 def test_generated_fused_kernels_compile(lib_path):
     """Every fused elementwise / row kernel the planner generates for the
     model graphs compiles with NVRTC for sm_100a (host only)."""
