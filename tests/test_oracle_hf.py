@@ -35,7 +35,8 @@ from oracle import interp
 torch = pytest.importorskip("torch")
 transformers = pytest.importorskip("transformers")
 
-B, S, T, DECODE = 1, 10, 16, 3
+S, T, DECODE = 10, 16, 3
+BATCHES = [1, 2]   # batch 2: the batched gather, attention and cache layout of the graphs
 
 
 def approx_equal(a, b, atol=1e-4, rtol=1e-4):
@@ -48,6 +49,7 @@ def approx_equal(a, b, atol=1e-4, rtol=1e-4):
 def oracle_logits(cfg, w, toks):
     """Prefill of the first S tokens, then DECODE single-token steps on the
     returned caches: logits of every position, [B, S + DECODE, V]."""
+    B = toks.shape[0]
     g = d.build_graph(cfg, "prefill", B, S, T, dynamic_prefill=True)
     inputs = [toks[:, :S], d.pos_inputs(cfg, "prefill", B, 0, S)] + w + \
         [d.zero_cache(cfg, B, T) for _ in range(2 * cfg.layers)]
@@ -73,7 +75,8 @@ def hf_logits(model, sd, toks):
         return model(torch.from_numpy(toks).long()).logits.numpy()
 
 
-def test_gpt2_matches_hf():
+@pytest.mark.parametrize("B", BATCHES)
+def test_gpt2_matches_hf(B):
     from transformers import GPT2Config, GPT2LMHeadModel
     # gpt2.clj's block passes 12 heads
     cfg = dataclasses.replace(d.GPT2_SMALL, vocab=96, d_model=96, layers=2, n_heads=12, n_kv_heads=12,
@@ -129,7 +132,8 @@ def _gemma_common(cfg):
                 hidden_activation="gelu_pytorch_tanh")
 
 
-def test_gemma2_matches_hf():
+@pytest.mark.parametrize("B", BATCHES)
+def test_gemma2_matches_hf(B):
     from transformers import Gemma2Config, Gemma2ForCausalLM
     # window 4 < prompt 10: local layers (even indices) mask, the global one does not
     cfg = dataclasses.replace(d.GEMMA2_2B, vocab=128, d_model=64, layers=2, n_heads=4, n_kv_heads=2,
@@ -144,7 +148,8 @@ def test_gemma2_matches_hf():
     assert approx_equal(got, ref), float(np.abs(got - ref).max())
 
 
-def test_gemma3_matches_hf():
+@pytest.mark.parametrize("B", BATCHES)
+def test_gemma3_matches_hf(B):
     from transformers import Gemma3ForCausalLM, Gemma3TextConfig
     # 6 layers: five local (window 4, RoPE 1e4) and one global (RoPE 1e6)
     cfg = dataclasses.replace(d.GEMMA3_4B, vocab=128, d_model=64, layers=6, n_heads=4, n_kv_heads=2,
