@@ -145,6 +145,33 @@ def test_vocab_split_greedy_matches_replicated_head(cfg, tie, lib_path):
         assert core.plan_text(lib_path, texts[r])["launches"] > 0
 
 
+def test_vocab_split_head_reads_its_rows_only(lib_path, tmp_path):
+    """The planned LM-head launch of a vocab-split rank reads V / tp rows of
+    the tied embedding in place: its algorithmic bytes are half the
+    replicated head's at tp = 2 (the embedding dominates both), with no copy
+    of the slice."""
+    cfg = dataclasses.replace(TINY3, vocab=8192)
+    biggest = {}
+    for name, vr in (("replicated", None), ("split", 1)):
+        dump = tmp_path / f"{name}.txt"
+        txt = shlo.graph_to_mlir_text(d.build_graph(d.shard_config(cfg, 2, vocab_rank=vr), "decode", 1, 6, 16,
+                                                    greedy=True))
+        code = ("import sys; sys.path.insert(0, %r); import __graft_entry__ as g; g._pkg();"
+                "from cljxla_b200.host import core; core.plan_text(%r, sys.stdin.read())"
+                % (os.path.dirname(os.path.dirname(os.path.abspath(__file__))), lib_path))
+        import subprocess
+        import sys
+        r = subprocess.run([sys.executable, "-c", code], input=txt, capture_output=True, text=True, timeout=300,
+                           env=dict(os.environ, CLJXLA_B200_DUMP_PLAN=str(dump)))
+        assert r.returncode == 0, r.stderr[-2000:]
+        rows = [ln.split("\t") for ln in dump.read_text().splitlines() if not ln.startswith("#")]
+        assert not any(k == "copy" and int(b) >= cfg.vocab * cfg.d_model for k, b, _ in rows)
+        biggest[name] = max(int(b) for _, b, _ in rows)
+    table = cfg.vocab * cfg.d_model * 2
+    assert biggest["replicated"] >= table
+    assert table // 2 <= biggest["split"] < table // 2 + table // 16
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
